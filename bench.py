@@ -1,0 +1,482 @@
+"""bench.py — throughput of the offloaded ops on B200, one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload attn|q8gemm|w8a8]
+                    [--impl b200|reference]
+
+Workloads (synthetic seeded data of the named shapes):
+  attn    config #2: GQA attention, 3633 tokens, 16 q / 8 kv heads x 128, fp16,
+          RoPE (theta 1e6) pre-applied; one step = one causal + one
+          bidirectional call. Metric: attention TFLOP/s (algorithmic FLOPs:
+          4*S*S*D*H bidirectional, 4*D*H*S(S+1)/2 causal).
+  q8gemm  config #1: f32 [512, 1024] x Q8_0 [3072, 1024]^T -> f32 [512, 3072].
+  w8a8    config #4's four projection GEMMs (qkv 3456, o 1152, fc1 4304,
+          fc2 1152 <- 4304) over one 16 x 2394-patch batch, W8A8.
+
+Timing: W untimed warm-up steps, then exactly K steps timed with CUDA events on
+the launching stream, an L2 flush (a 256 MiB write) between timed steps, a
+barrier + synchronize on both sides, max over ranks. With N > 1 each rank runs
+an independent replica (the single ops do not shard: replicas only) and
+`value` is the aggregate over ranks. The `e2e` figure goes through the public
+C-ABI host entry points (rb_*_host) with pinned host buffers, so host<->device
+copies are inside its timed region.
+
+`--impl reference` times the reference algorithm on the host cores instead:
+the CPU restatement of the reference's `--device cpu` path (oracle/, all
+OpenMP threads), on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+def profile_traffic(name):
+    """DRAM bytes per launch of the dominant kernel, from the committed ncu summary."""
+    p = ROOT / "profiles" / f"{name}.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[3:7]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- workloads
+def rope_inplace(x, n_heads, d, theta=1e6):
+    """Rotate-half RoPE (util/rope.rs:15-75) on a [S, H*D] tensor, positions 0..S-1."""
+    import torch
+    s = x.shape[0]
+    half = d // 2
+    inv = torch.tensor([1.0 / theta ** (2.0 * i / d) for i in range(half)], dtype=torch.float64).float()
+    pos = torch.arange(s, dtype=torch.float32)
+    ang = pos[:, None] * inv[None, :]
+    cos, sin = ang.cos().to(x.device), ang.sin().to(x.device)
+    xv = x.float().view(s, n_heads, d)
+    x1, x2 = xv[..., :half], xv[..., half:]
+    o1 = x1 * cos[:, None, :] - x2 * sin[:, None, :]
+    o2 = x2 * cos[:, None, :] + x1 * sin[:, None, :]
+    return torch.cat([o1, o2], -1).reshape(s, n_heads * d).to(x.dtype)
+
+
+class AttnWorkload:
+    name = "attn"
+    metric = "GQA attention TFLOP/s (config #2: S=3633, 16q/8kv x 128, causal + bidirectional)"
+    unit = "TFLOP/s"
+    S, H, KV, D = 3633, 16, 8, 128
+
+    def __init__(self, dev, seed):
+        import torch
+        import burn_rocket_b200 as rb
+        self.rb = rb
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        S, H, KV, D = self.S, self.H, self.KV, self.D
+        q = torch.randn(S, H * D, generator=g)
+        k = torch.randn(S, KV * D, generator=g)
+        v = torch.randn(S, KV * D, generator=g)
+        self.q = rope_inplace(q, H, D).half().to(dev)
+        self.k = rope_inplace(k, KV, D).half().to(dev)
+        self.v = v.half().to(dev)
+        self.out_c = torch.empty_like(self.q)
+        self.out_b = torch.empty_like(self.q)
+        self.scale = 1.0 / math.sqrt(D)
+        self.flops_b = 4.0 * S * S * D * H
+        self.flops_c = 4.0 * D * H * S * (S + 1) / 2
+        self.flops = self.flops_b + self.flops_c
+        # pinned host copies for the end-to-end leg
+        self.hq = self.q.cpu().pin_memory()
+        self.hk = self.k.cpu().pin_memory()
+        self.hv = self.v.cpu().pin_memory()
+        self.hout = torch.empty_like(self.hq).pin_memory()
+
+    def step(self, stream):
+        rb = self.rb
+        rb.attention(self.q, self.k, self.v, self.H, self.KV, self.D, self.scale, None, True, out=self.out_c,
+                     stream=stream)
+        rb.attention(self.q, self.k, self.v, self.H, self.KV, self.D, self.scale, None, False, out=self.out_b,
+                     stream=stream)
+
+    def kernel_launches(self):
+        return [("attn_kernel causal", self.flops_c), ("attn_kernel bidirectional", self.flops_b)]
+
+    def e2e_step(self):
+        import burn_rocket_b200._lib as L
+        lib = L.load()
+        for mode in (L.MASK_CAUSAL, L.MASK_NONE):
+            rc = lib.rb_attention_host(self.hq.data_ptr(), self.hk.data_ptr(), self.hv.data_ptr(),
+                                       self.hout.data_ptr(), L.DTYPE_F16, self.S, self.S, self.H, self.KV, self.D,
+                                       self.scale, 0.0, mode, -1, 0, 0)
+            if rc != 0:
+                raise RuntimeError(L.last_error())
+        return (2 * (self.hq.numel() + self.hk.numel() + self.hv.numel()) * 2, 2 * self.hout.numel() * 2)
+
+    @staticmethod
+    def cpu_sample(orc, seed, timed_repeats=1):
+        """Reference CPU algorithm on 1 of the 8 KV groups (2 of 16 heads), causal + bidirectional."""
+        S, D = AttnWorkload.S, AttnWorkload.D
+        rng = np.random.default_rng(seed)
+        q = rng.standard_normal((S, 2 * D)).astype(np.float32)
+        k = rng.standard_normal((S, D)).astype(np.float32)
+        v = rng.standard_normal((S, D)).astype(np.float32)
+        flops = 4.0 * S * S * D * 2 + 4.0 * D * 2 * S * (S + 1) / 2
+        t0 = time.perf_counter()
+        for _ in range(timed_repeats):
+            orc.attention_cpu(q, k, v, 2, 1, D, 1.0 / math.sqrt(D), True)
+            orc.attention_cpu(q, k, v, 2, 1, D, 1.0 / math.sqrt(D), False)
+        dt = (time.perf_counter() - t0) / timed_repeats
+        return flops / dt / 1e12, "1 of 8 KV groups (2 of 16 q heads), full 3633 tokens, causal + bidirectional"
+
+
+class Q8GemmWorkload:
+    name = "q8gemm"
+    metric = "Q8_0 GEMM TFLOP/s (config #1: f32 [512,1024] x Q8_0 [3072,1024]^T)"
+    unit = "TFLOP/s"
+    M, K, N = 512, 1024, 3072
+
+    def __init__(self, dev, seed):
+        import torch
+        import burn_rocket_b200 as rb
+        from oracle import oracle as orc  # only to build the synthetic Q8_0 blocks
+        self.rb = rb
+        rng = np.random.default_rng(seed)
+        a = rng.standard_normal((self.M, self.K)).astype(np.float32)
+        w = (rng.standard_normal((self.N, self.K)) * 0.02).astype(np.float32)
+        self.wid = rb.pack(w)  # device Q8_0 encoder
+        self.x = torch.from_numpy(a).to(dev)
+        self.y = torch.empty(self.M, self.N, dtype=torch.float32, device=dev)
+        self.flops = 2.0 * self.M * self.N * self.K
+        self.hx = torch.from_numpy(a).pin_memory()
+        self.hy = torch.empty(self.M, self.N, dtype=torch.float32).pin_memory()
+        del orc
+
+    def step(self, stream):
+        self.rb.matmul(self.x, self.wid, out=self.y, stream=stream)
+
+    def kernel_launches(self):
+        return [("q8_0 gemm (+ f32->f16 cast)", self.flops)]
+
+    def e2e_step(self):
+        import burn_rocket_b200._lib as L
+        rc = L.load().rb_matmul_host(self.wid.id, self.hx.data_ptr(), L.DTYPE_F32, self.M, self.K,
+                                     self.hy.data_ptr(), L.DTYPE_F32)
+        if rc != 0:
+            raise RuntimeError(L.last_error())
+        return (self.hx.numel() * 4, self.hy.numel() * 4)
+
+    @staticmethod
+    def cpu_sample(orc, seed, timed_repeats=3):
+        M, K, N = Q8GemmWorkload.M, Q8GemmWorkload.K, Q8GemmWorkload.N
+        rng = np.random.default_rng(seed)
+        a = rng.standard_normal((M, K)).astype(np.float32)
+        codes, scales = orc.q8_0_quantize((rng.standard_normal((N, K)) * 0.02).astype(np.float32))
+        scratch = np.empty((N, K), np.float32)
+        orc.q8_0_matmul_cpu(a, codes, scales, scratch)
+        t0 = time.perf_counter()
+        for _ in range(timed_repeats):
+            orc.q8_0_matmul_cpu(a, codes, scales, scratch)
+        dt = (time.perf_counter() - t0) / timed_repeats
+        return 2.0 * M * N * K / dt / 1e12, "full config #1 call (dequantise + f32 GEMM)"
+
+
+class W8A8Workload:
+    name = "w8a8"
+    metric = "W8A8 GEMM TOP/s (config #4 projections, 16 x 2394 patches)"
+    unit = "TOP/s"
+    M = 16 * 2394
+    SHAPES = [(3456, 1152), (1152, 1152), (4304, 1152), (1152, 4304)]  # (N, K)
+
+    def __init__(self, dev, seed):
+        import torch
+        import burn_rocket_b200 as rb
+        self.rb = rb
+        rng = np.random.default_rng(seed)
+        self.ws, self.xs, self.ys = [], [], []
+        for n, k in self.SHAPES:
+            codes = rng.integers(-127, 128, size=(n, k), dtype=np.int8)
+            scale = (rng.random(n).astype(np.float32) * 1e-3 + 1e-4)
+            self.ws.append(rb.pack_qat(codes, scale, n, k))
+            self.xs.append(torch.randn(self.M, k, device=dev))
+            self.ys.append(torch.empty(self.M, n, dtype=torch.float32, device=dev))
+        self.flops = sum(2.0 * self.M * n * k for n, k in self.SHAPES)
+        self.hx = [x.cpu().pin_memory() for x in self.xs]
+        self.hy = [y.cpu().pin_memory() for y in self.ys]
+
+    def step(self, stream):
+        for w, x, y in zip(self.ws, self.xs, self.ys):
+            self.rb.matmul(x, w, out=y, stream=stream)
+
+    def kernel_launches(self):
+        return [(f"w8a8 gemm N={n} K={k} (+ row quantiser)", 2.0 * self.M * n * k) for n, k in self.SHAPES]
+
+    def e2e_step(self):
+        import burn_rocket_b200._lib as L
+        h2d = d2h = 0
+        for (n, k), w, hx, hy in zip(self.SHAPES, self.ws, self.hx, self.hy):
+            rc = L.load().rb_matmul_host(w.id, hx.data_ptr(), L.DTYPE_F32, self.M, k, hy.data_ptr(), L.DTYPE_F32)
+            if rc != 0:
+                raise RuntimeError(L.last_error())
+            h2d += hx.numel() * 4
+            d2h += hy.numel() * 4
+        return (h2d, d2h)
+
+    @staticmethod
+    def cpu_sample(orc, seed, timed_repeats=1):
+        rng = np.random.default_rng(seed)
+        rows = 512
+        flops = 0.0
+        t = 0.0
+        for n, k in W8A8Workload.SHAPES:
+            x = rng.standard_normal((rows, k)).astype(np.float32)
+            codes = rng.integers(-127, 128, size=(n, k), dtype=np.int8)
+            s = np.full(n, 1e-3, np.float32)
+            t0 = time.perf_counter()
+            orc.w8a8_matmul(x, codes, s)
+            t += time.perf_counter() - t0
+            flops += 2.0 * rows * n * k
+        return flops / t / 1e12, f"{rows} of {W8A8Workload.M} rows of each projection (quantise + int GEMM + epilogue)"
+
+
+WORKLOADS = {w.name: w for w in (AttnWorkload, Q8GemmWorkload, W8A8Workload)}
+
+
+# ----------------------------------------------------------------------------- driver
+def dist_setup(n_gpus):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    return rank, world, local
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+    rank, world, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    import burn_rocket_b200 as rb
+    rb.init(local)
+    W = WORKLOADS[args.workload]
+    wl = W(dev, seed=0x5EED + rank)
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+
+    for _ in range(args.warmup):
+        wl.step(stream)
+    torch.cuda.synchronize()
+    rb.check_device_errors()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    rb.launch_count(reset=True)
+    barrier()
+    with ClockSampler(local) as clocks:
+        for i in range(args.steps):
+            flush.zero_()  # L2 flush between timed steps (outside the events)
+            starts[i].record(stream)
+            wl.step(stream)
+            ends[i].record(stream)
+        barrier()
+    launches = rb.launch_count()
+    ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    rb.check_device_errors()
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    ms_per_step = ms_max / args.steps
+    value = wl.flops * world * args.steps / (ms_max / 1e3) / 1e12
+
+    # End-to-end through the host entry points (copies inside the timed region).
+    for _ in range(2):
+        wl.e2e_step()
+    barrier()
+    t0 = time.perf_counter()
+    e2e_steps = max(3, min(args.steps, 10))
+    for _ in range(e2e_steps):
+        h2d, d2h = wl.e2e_step()
+    e2e_s = time.perf_counter() - t0
+    te = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = wl.flops * world * e2e_steps / float(te.item()) / 1e12
+
+    peaks, peak_kind = load_peaks()
+    achieved = wl.flops / (ms_per_step / 1e3) / 1e12  # per launch group, per GPU
+    peak = float(peaks["bf16_tflops"])
+    if wl.name == "w8a8":
+        peak = 2.0 * peak  # dense int8 is twice the dense bf16 rate
+    traffic = profile_traffic(f"{wl.name}_ncu")
+    line = {
+        "metric": wl.metric, "value": round(value, 3), "unit": wl.unit, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": {"attn": "f16", "q8gemm": "f16xq8_0->f32", "w8a8": "s8"}[wl.name],
+        "data": "synthetic (seeded, BASELINE.json shapes)",
+        "config": {"workload": {"attn": "configs[1] GQA attention", "q8gemm": "configs[0] Q8_0 GEMM",
+                                "w8a8": "configs[3] W8A8 projections"}[wl.name],
+                   "l2": "flushed between timed steps (256 MiB write)",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
+                     "unit": "TFLOP/s" if wl.name != "w8a8" else "TOP/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "peak_source": f"{peak_kind} MEASURED_PEAKS bf16_tflops (burst)" + (" x2 for int8" if wl.name == "w8a8" else "")},
+        "e2e": {"value": round(e2e_value, 3), "unit": wl.unit, "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h)},
+        "gpu_launches": int(launches),
+        "clocks": clocks.summary(),
+    }
+    if world > 1:
+        dist.barrier()
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as orc
+        v, sample = W.cpu_sample(orc, seed=1)
+        line["cpu_baseline"] = {"value": round(v, 5), "unit": wl.unit, "cores": orc.num_threads(),
+                                "kind": "port", "sample": sample}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return  # rank 0 alone runs the host-core reference
+    from oracle import oracle as orc
+    W = WORKLOADS[args.workload]
+    for _ in range(args.warmup):
+        W.cpu_sample(orc, seed=1)
+    vals = []
+    sample = ""
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        v, sample = W.cpu_sample(orc, seed=1)
+        vals.append(v)
+    wall = time.perf_counter() - t0
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": W.metric, "value": round(value, 5), "unit": W.unit,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(wall / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE.json shapes)",
+        "config": {"workload": W.name},
+        "cpu_baseline": {"value": round(value, 5), "unit": W.unit, "cores": orc.num_threads(), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 5), "unit": W.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "CPU restatement of the reference's --device cpu algorithm (oracle/, OpenMP); the Rust "
+                "reference cannot be built here (no cargo/rustc, no crate registry)",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="attn", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

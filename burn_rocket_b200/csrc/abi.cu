@@ -1,0 +1,648 @@
+// abi.cu — the extern "C" surface of librocket_b200.so (include/rocket_b200.h).
+//
+// Mirrors the engine of crates/burn-rocket/src/ext.rs: one global engine per
+// process behind a mutex (ext.rs:537-556), a registry of resident weights with
+// monotonically increasing ids (ext.rs:39-50, 829-840), and op entry points
+// that validate shapes and report the reference's status codes. The device
+// work itself lives in gemm.cu, quant.cu and attention.cu.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "kernels.h"
+#include "sm100.cuh"
+
+namespace rb {
+
+// ------------------------------------------------------------------ errors
+static thread_local std::string g_last_error;
+
+static int fail(int rc, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return rc;
+}
+
+#define RB_CUDA(call, what)                                                                  \
+  do {                                                                                       \
+    cudaError_t e_ = (call);                                                                 \
+    if (e_ != cudaSuccess)                                                                   \
+      return fail(RB_E_DEVICE, "%s: %s (%s)", what, cudaGetErrorName(e_), cudaGetErrorString(e_)); \
+  } while (0)
+
+// ------------------------------------------------------------------ tensor maps
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+static bool load_encode_fn() {
+  if (g_encode) return true;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault,
+                                       &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || fn == nullptr)
+    return false;
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return true;
+}
+
+int make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t rows,
+                 uint64_t cols, uint64_t row_stride_elems, uint32_t box_cols, uint32_t box_rows,
+                 bool swizzle128) {
+  if (!load_encode_fn()) return fail(RB_E_DEVICE, "cuTensorMapEncodeTiled unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0)
+    return fail(RB_E_SHAPE, "tensor base %p is not 16-byte aligned", base);
+  if ((row_stride_elems * elem_bytes) % 16 != 0)
+    return fail(RB_E_SHAPE, "row stride %llu elements is not a multiple of 16 bytes",
+                (unsigned long long)row_stride_elems);
+  CUtensorMapDataType dt = elem_bytes == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                           : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {row_stride_elems * elem_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(RB_E_DEVICE, "cuTensorMapEncodeTiled failed (%d) rows=%llu cols=%llu box=%ux%u",
+                (int)r, (unsigned long long)rows, (unsigned long long)cols, box_cols, box_rows);
+  return RB_OK;
+}
+
+// ------------------------------------------------------------------ engine
+struct Weight {
+  int kind = 0;
+  int64_t n = 0, k = 0;
+  int8_t* codes = nullptr;   // [n, k]
+  void* scales = nullptr;    // Q8_0: f16 [n, k/32]; W8A8: f32 [n]
+  float in_scale = 0.0f, out_scale = 0.0f;
+  CUtensorMap tmap_b[2]{};   // W8A8: TMA maps of the codes, box rows 256 / 128
+  size_t bytes = 0;
+};
+
+struct Scratch {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  int grow(size_t need, const char* what) {
+    if (need <= bytes) return RB_OK;
+    if (ptr) cudaFree(ptr);
+    ptr = nullptr;
+    bytes = 0;
+    size_t want = need + need / 4 + 256;
+    if (cudaMalloc(&ptr, want) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(RB_E_NOMEM, "%s: cudaMalloc(%zu) failed", what, want);
+    }
+    bytes = want;
+    return RB_OK;
+  }
+};
+
+struct Engine {
+  int device = -1;
+  int num_sms = 0;
+  uint32_t* err = nullptr;  // device error word
+  std::unordered_map<int64_t, Weight> weights;
+  int64_t next_id = 1;
+  Scratch act;       // activation staging (f16 or int8 codes)
+  Scratch rowscale;  // per-row scales
+  Scratch io_in, io_out, io_k, io_v;  // host-entry staging
+  cudaStream_t host_stream = nullptr;
+};
+
+static std::mutex g_mu;
+static Engine* g_engine = nullptr;
+static std::atomic<int64_t> g_launches{0};
+
+static int ensure_engine(Engine** out) {
+  if (!g_engine) return fail(RB_E_IO, "rb_init() has not been called");
+  int cur = -1;
+  cudaGetDevice(&cur);
+  if (cur != g_engine->device) RB_CUDA(cudaSetDevice(g_engine->device), "cudaSetDevice");
+  *out = g_engine;
+  return RB_OK;
+}
+
+static size_t dtype_bytes(int dt) {
+  switch (dt) {
+    case RB_DTYPE_F32: return 4;
+    case RB_DTYPE_F16: return 2;
+    case RB_DTYPE_BF16: return 2;
+    default: return 0;
+  }
+}
+
+// ------------------------------------------------------------------ ops
+static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int64_t m,
+                         int64_t k, void* y, int y_dtype, cudaStream_t st) {
+  auto it = e->weights.find(id);
+  if (it == e->weights.end()) return fail(RB_E_SHAPE, "weight id %lld is not packed", (long long)id);
+  const Weight& w = it->second;
+  if (k != w.k) return fail(RB_E_SHAPE, "activation K=%lld mismatch for weight id %lld (K=%lld)",
+                            (long long)k, (long long)id, (long long)w.k);
+  if (m <= 0) return fail(RB_E_SHAPE, "matmul needs M > 0 (M=%lld)", (long long)m);
+  if (m > (int64_t(1) << 31) - 1) return fail(RB_E_SHAPE, "M=%lld too large", (long long)m);
+  if (!dtype_bytes(x_dtype) || !dtype_bytes(y_dtype)) return fail(RB_E_SHAPE, "bad dtype");
+  if ((w.n * static_cast<int64_t>(dtype_bytes(y_dtype))) % 16 != 0 &&
+      (reinterpret_cast<uintptr_t>(y) & 15) != 0)
+    return fail(RB_E_SHAPE, "output buffer must be 16-byte aligned");
+
+  GemmLaunch L{};
+  L.M = static_cast<int>(m);
+  L.N = static_cast<int>(w.n);
+  L.K = static_cast<int>(w.k);
+  L.out = y;
+  L.ldo = static_cast<int>(w.n);
+  L.out_dtype = y_dtype;
+  L.err = e->err;
+  L.num_sms = e->num_sms;
+  int rc;
+  if (w.kind == RB_WEIGHT_Q8_0) {
+    const void* a = x;
+    if (x_dtype != RB_DTYPE_F16 || (reinterpret_cast<uintptr_t>(x) & 15) != 0) {
+      if ((rc = e->act.grow(static_cast<size_t>(m) * k * 2, "matmul activations")) != RB_OK) return rc;
+      if ((rc = launch_cast(x, x_dtype, e->act.ptr, RB_DTYPE_F16, m * k, st)) != RB_OK)
+        return fail(rc, "activation cast launch failed");
+      g_launches++;
+      a = e->act.ptr;
+    }
+    CUtensorMap tmA;
+    if ((rc = make_tmap_2d(&tmA, a, 2, m, k, k, 64, 128, true)) != RB_OK) return rc;
+    L.w_codes = w.codes;
+    L.w_scales = w.scales;
+    if ((rc = launch_q8_gemm(tmA, L, st)) != RB_OK) return fail(rc, "q8_0 gemm launch failed");
+    g_launches++;
+    return RB_OK;
+  }
+  if (w.kind == RB_WEIGHT_W8A8) {
+    const size_t codes_bytes = (static_cast<size_t>(m) * k + 255) & ~size_t(255);
+    if ((rc = e->act.grow(codes_bytes, "w8a8 activation codes")) != RB_OK) return rc;
+    if ((rc = e->rowscale.grow(static_cast<size_t>(m) * 4, "w8a8 row scales")) != RB_OK) return rc;
+    int8_t* codes = reinterpret_cast<int8_t*>(e->act.ptr);
+    float* rs = reinterpret_cast<float*>(e->rowscale.ptr);
+    if ((rc = launch_quantize_rows_i8(x, x_dtype, m, k, w.in_scale, codes, rs, st)) != RB_OK)
+      return fail(rc, "row quantiser launch failed");
+    g_launches++;
+    CUtensorMap tmA;
+    if ((rc = make_tmap_2d(&tmA, codes, 1, m, k, k, 128, 128, true)) != RB_OK) return rc;
+    L.s_row = rs;
+    L.s_col = reinterpret_cast<const float*>(w.scales);
+    L.out_scale = w.out_scale;
+    if ((rc = launch_w8a8_gemm(tmA, w.tmap_b[0], w.tmap_b[1], L, st)) != RB_OK)
+      return fail(rc, "w8a8 gemm launch failed");
+    g_launches++;
+    return RB_OK;
+  }
+  return fail(RB_E_UNSUPPORTED, "weight kind %d", w.kind);
+}
+
+static int attention_locked(Engine* e, const void* q, const void* k, const void* v, void* out,
+                            int dtype, int64_t n_q, int64_t n_kv, int n_head, int n_kv_heads,
+                            int head_dim, float scale, float softcap, int mask_mode,
+                            int64_t window, int64_t q_start, int64_t kv_start, cudaStream_t st) {
+  // Contract of check_flash (attn/mod.rs:1424-1460) and attention_impl
+  // (ext.rs:1680-1712).
+  if (n_q <= 0 || n_kv <= 0 || head_dim <= 0)
+    return fail(RB_E_SHAPE, "flash_attn/dims: n_q=%lld n_kv=%lld head_dim=%d", (long long)n_q,
+                (long long)n_kv, head_dim);
+  if (n_head <= 0 || n_kv_heads <= 0 || n_head % n_kv_heads != 0)
+    return fail(RB_E_SHAPE, "flash_attn/heads: n_head=%d n_kv_heads=%d", n_head, n_kv_heads);
+  if (head_dim != 64 && head_dim != 128)
+    return fail(RB_E_UNSUPPORTED, "flash_attn/dims: head_dim %d (supported: 64, 128)", head_dim);
+  if (mask_mode < RB_MASK_NONE || mask_mode > RB_MASK_CAUSAL_BLOCK)
+    return fail(RB_E_SHAPE, "unknown mask mode %d", mask_mode);
+  const bool block = mask_mode == RB_MASK_NONE_BLOCK || mask_mode == RB_MASK_WINDOW_BLOCK ||
+                     mask_mode == RB_MASK_CAUSAL_BLOCK;
+  if (!block && n_q != n_kv)
+    return fail(RB_E_SHAPE, "the full-sequence mask modes need equal query/key lengths (%lld vs %lld)",
+                (long long)n_q, (long long)n_kv);
+  if (n_q > (1 << 29) || n_kv > (1 << 29)) return fail(RB_E_SHAPE, "sequence too long");
+  // Windowed modes with window < 0 fall back to their unwindowed form
+  // (ext.rs:672-677, 693-698, 717-727).
+  if (mask_mode == RB_MASK_WINDOW && window < 0) mask_mode = RB_MASK_NONE;
+  if (mask_mode == RB_MASK_CAUSAL_WINDOW && window < 0) mask_mode = RB_MASK_CAUSAL;
+  if (mask_mode == RB_MASK_WINDOW_BLOCK && window < 0) mask_mode = RB_MASK_NONE_BLOCK;
+  if (q_start < 0) q_start = 0;
+  if (kv_start < 0) kv_start = 0;
+
+  int rc;
+  const void* qh = q;
+  const void* kh = k;
+  const void* vh = v;
+  void* oh = out;
+  int kdt = dtype;
+  if (dtype == RB_DTYPE_F32) {
+    // f32 tensors (the Burn boundary) are rounded to f16 like fill_heads
+    // (ext.rs:2174-2190), and the f16 result widened on the way out.
+    const size_t nq = static_cast<size_t>(n_q) * n_head * head_dim;
+    const size_t nk = static_cast<size_t>(n_kv) * n_kv_heads * head_dim;
+    const size_t a16 = (nq * 2 + 255) & ~size_t(255), k16 = (nk * 2 + 255) & ~size_t(255);
+    if ((rc = e->act.grow(2 * a16 + 2 * k16, "attention f16 staging")) != RB_OK) return rc;
+    uint8_t* base = reinterpret_cast<uint8_t*>(e->act.ptr);
+    void* q16 = base;
+    void* o16 = base + a16;
+    void* k16p = base + 2 * a16;
+    void* v16 = base + 2 * a16 + k16;
+    if ((rc = launch_cast(q, RB_DTYPE_F32, q16, RB_DTYPE_F16, nq, st)) != RB_OK) return fail(rc, "cast q");
+    if ((rc = launch_cast(k, RB_DTYPE_F32, k16p, RB_DTYPE_F16, nk, st)) != RB_OK) return fail(rc, "cast k");
+    if ((rc = launch_cast(v, RB_DTYPE_F32, v16, RB_DTYPE_F16, nk, st)) != RB_OK) return fail(rc, "cast v");
+    g_launches += 3;
+    qh = q16; kh = k16p; vh = v16; oh = o16;
+    kdt = RB_DTYPE_F16;
+  } else if (dtype != RB_DTYPE_F16 && dtype != RB_DTYPE_BF16) {
+    return fail(RB_E_SHAPE, "attention dtype %d", dtype);
+  }
+  CUtensorMap tq, tk, tv;
+  const uint64_t ldq = static_cast<uint64_t>(n_head) * head_dim;
+  const uint64_t ldk = static_cast<uint64_t>(n_kv_heads) * head_dim;
+  if ((rc = make_tmap_2d(&tq, qh, 2, n_q, ldq, ldq, 64, 128, true)) != RB_OK) return rc;
+  if ((rc = make_tmap_2d(&tk, kh, 2, n_kv, ldk, ldk, 64, 128, true)) != RB_OK) return rc;
+  if ((rc = make_tmap_2d(&tv, vh, 2, n_kv, ldk, ldk, 64, 128, true)) != RB_OK) return rc;
+  if ((reinterpret_cast<uintptr_t>(oh) & 15) != 0)
+    return fail(RB_E_SHAPE, "attention output must be 16-byte aligned");
+  AttnLaunch L{};
+  L.q = qh; L.k = kh; L.v = vh; L.out = oh;
+  L.dtype = kdt;
+  L.n_q = static_cast<int>(n_q);
+  L.n_kv = static_cast<int>(n_kv);
+  L.n_head = n_head;
+  L.n_kv_heads = n_kv_heads;
+  L.head_dim = head_dim;
+  L.ldq = static_cast<int>(ldq);
+  L.ldk = L.ldv = static_cast<int>(ldk);
+  L.ldo = static_cast<int>(ldq);
+  L.scale = scale;
+  L.softcap = softcap;
+  L.mask_mode = mask_mode;
+  L.window = window;
+  L.q_start = q_start;
+  L.kv_start = kv_start;
+  L.err = e->err;
+  L.num_sms = e->num_sms;
+  if ((rc = launch_attention(tq, tk, tv, L, st)) != RB_OK) return fail(rc, "attention launch failed");
+  g_launches++;
+  if (dtype == RB_DTYPE_F32) {
+    if ((rc = launch_cast(oh, RB_DTYPE_F16, out, RB_DTYPE_F32, static_cast<int64_t>(n_q) * ldq, st)) != RB_OK)
+      return fail(rc, "cast out");
+    g_launches++;
+  }
+  return RB_OK;
+}
+
+}  // namespace rb
+
+using namespace rb;
+
+extern "C" {
+
+int rb_init(int device_ordinal) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_engine) return RB_OK;
+  int count = 0;
+  RB_CUDA(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
+  if (device_ordinal < 0 || device_ordinal >= count)
+    return fail(RB_E_DEVICE, "device %d out of range (%d devices)", device_ordinal, count);
+  RB_CUDA(cudaSetDevice(device_ordinal), "cudaSetDevice");
+  cudaDeviceProp prop;
+  RB_CUDA(cudaGetDeviceProperties(&prop, device_ordinal), "cudaGetDeviceProperties");
+  if (prop.major != 10)
+    return fail(RB_E_UNSUPPORTED, "device %d is sm_%d%d; librocket_b200 needs sm_100a", device_ordinal,
+                prop.major, prop.minor);
+  if (!load_encode_fn()) return fail(RB_E_DEVICE, "cuTensorMapEncodeTiled unavailable");
+  Engine* e = new Engine();
+  e->device = device_ordinal;
+  e->num_sms = prop.multiProcessorCount;
+  if (cudaMalloc(&e->err, sizeof(uint32_t)) != cudaSuccess) {
+    delete e;
+    return fail(RB_E_NOMEM, "cudaMalloc(error word) failed");
+  }
+  cudaMemset(e->err, 0, sizeof(uint32_t));
+  cudaStreamCreateWithFlags(&e->host_stream, cudaStreamNonBlocking);
+  g_engine = e;
+  return RB_OK;
+}
+
+int rb_last_error(char* buf, size_t len) {
+  if (buf && len) {
+    std::strncpy(buf, g_last_error.c_str(), len - 1);
+    buf[len - 1] = '\0';
+  }
+  return static_cast<int>(g_last_error.size());
+}
+
+int rb_check_device_errors(void) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Engine* e;
+  int rc = ensure_engine(&e);
+  if (rc) return rc;
+  RB_CUDA(cudaDeviceSynchronize(), "device synchronize");
+  uint32_t word = 0;
+  RB_CUDA(cudaMemcpy(&word, e->err, sizeof(word), cudaMemcpyDeviceToHost), "read error word");
+  if (word) {
+    cudaMemset(e->err, 0, sizeof(uint32_t));
+    return fail(RB_E_DEVICE, "kernel error word 0x%x (%s%s%s)", word,
+                (word & kErrWaitTimeout) ? "wait-timeout " : "",
+                (word & kErrTmemAlloc) ? "tmem-alloc " : "",
+                (word & kErrBadShape) ? "bad-shape" : "");
+  }
+  return RB_OK;
+}
+
+int64_t rb_pack_q8_0(const void* blocks_host, int64_t n, int64_t k) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Engine* e;
+  int rc = ensure_engine(&e);
+  if (rc) return rc;
+  if (!blocks_host) return fail(RB_E_SHAPE, "null Q8_0 blocks");
+  if (n <= 0 || k <= 0 || k % 32 != 0)
+    return fail(RB_E_SHAPE, "Q8_0 weight [%lld, %lld]: K must be a positive multiple of 32",
+                (long long)n, (long long)k);
+  if (n > (1 << 30) || k > (1 << 30)) return fail(RB_E_SHAPE, "Q8_0 weight too large");
+  const size_t nblk = static_cast<size_t>(n) * (k / 32);
+  Weight w;
+  w.kind = RB_WEIGHT_Q8_0;
+  w.n = n;
+  w.k = k;
+  uint8_t* dblk = nullptr;
+  if (cudaMalloc(&dblk, nblk * 34) != cudaSuccess ||
+      cudaMalloc(&w.codes, static_cast<size_t>(n) * k) != cudaSuccess ||
+      cudaMalloc(&w.scales, nblk * 2) != cudaSuccess) {
+    cudaGetLastError();
+    if (dblk) cudaFree(dblk);
+    if (w.codes) cudaFree(w.codes);
+    return fail(RB_E_NOMEM, "Q8_0 pack: device allocation failed");
+  }
+  RB_CUDA(cudaMemcpy(dblk, blocks_host, nblk * 34, cudaMemcpyHostToDevice), "Q8_0 upload");
+  if ((rc = launch_q8_0_unpack_blocks(dblk, n, k, w.codes, reinterpret_cast<uint16_t*>(w.scales),
+                                      nullptr)) != RB_OK)
+    return fail(rc, "Q8_0 unpack launch failed");
+  g_launches++;
+  RB_CUDA(cudaDeviceSynchronize(), "Q8_0 unpack");
+  cudaFree(dblk);
+  w.bytes = static_cast<size_t>(n) * k + nblk * 2;
+  const int64_t id = e->next_id++;
+  e->weights[id] = w;
+  return id;
+}
+
+int64_t rb_pack_f32_q8_0(const float* const* parts_host, const int64_t* n_parts, int num_parts,
+                         int64_t k) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Engine* e;
+  int rc = ensure_engine(&e);
+  if (rc) return rc;
+  if (num_parts < 1 || !parts_host || !n_parts) return fail(RB_E_SHAPE, "no weight parts");
+  if (k <= 0 || k % 32 != 0) return fail(RB_E_SHAPE, "Q8_0 pack: K=%lld must be a positive multiple of 32", (long long)k);
+  int64_t n = 0;
+  for (int i = 0; i < num_parts; ++i) {
+    if (n_parts[i] <= 0 || !parts_host[i]) return fail(RB_E_SHAPE, "weight part %d is empty", i);
+    n += n_parts[i];
+  }
+  if (n > (1 << 30)) return fail(RB_E_SHAPE, "Q8_0 weight too large");
+  Weight w;
+  w.kind = RB_WEIGHT_Q8_0;
+  w.n = n;
+  w.k = k;
+  float* dw = nullptr;
+  if (cudaMalloc(&dw, static_cast<size_t>(n) * k * 4) != cudaSuccess ||
+      cudaMalloc(&w.codes, static_cast<size_t>(n) * k) != cudaSuccess ||
+      cudaMalloc(&w.scales, static_cast<size_t>(n) * (k / 32) * 2) != cudaSuccess) {
+    cudaGetLastError();
+    if (dw) cudaFree(dw);
+    if (w.codes) cudaFree(w.codes);
+    return fail(RB_E_NOMEM, "Q8_0 pack: device allocation failed");
+  }
+  int64_t off = 0;
+  for (int i = 0; i < num_parts; ++i) {
+    RB_CUDA(cudaMemcpy(dw + off * k, parts_host[i], static_cast<size_t>(n_parts[i]) * k * 4,
+                       cudaMemcpyHostToDevice), "weight upload");
+    off += n_parts[i];
+  }
+  if ((rc = launch_q8_0_encode(dw, n, k, w.codes, reinterpret_cast<uint16_t*>(w.scales), nullptr)) != RB_OK)
+    return fail(rc, "Q8_0 encode launch failed");
+  g_launches++;
+  RB_CUDA(cudaDeviceSynchronize(), "Q8_0 encode");
+  cudaFree(dw);
+  w.bytes = static_cast<size_t>(n) * k + static_cast<size_t>(n) * (k / 32) * 2;
+  const int64_t id = e->next_id++;
+  e->weights[id] = w;
+  return id;
+}
+
+int64_t rb_pack_w8a8(const int8_t* codes_host, const float* w_scale_host, int64_t n, int64_t k,
+                     float in_scale, float out_scale) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Engine* e;
+  int rc = ensure_engine(&e);
+  if (rc) return rc;
+  // pack_qat asserts (ext.rs:1390-1394); this build tiles any K % 16 == 0
+  // (TMA row pitch) and any N.
+  if (!codes_host || !w_scale_host) return fail(RB_E_SHAPE, "null W8A8 codes/scales");
+  if (n <= 0 || k <= 0 || k % 16 != 0)
+    return fail(RB_E_SHAPE, "W8A8 weight [%lld, %lld]: K must be a positive multiple of 16",
+                (long long)n, (long long)k);
+  if (!(in_scale >= 0.0f)) return fail(RB_E_SHAPE, "QAT input scale must not be negative");
+  if (n > (1 << 30) || k > (1 << 30)) return fail(RB_E_SHAPE, "W8A8 weight too large");
+  Weight w;
+  w.kind = RB_WEIGHT_W8A8;
+  w.n = n;
+  w.k = k;
+  w.in_scale = in_scale;
+  w.out_scale = out_scale;
+  if (cudaMalloc(&w.codes, static_cast<size_t>(n) * k) != cudaSuccess ||
+      cudaMalloc(&w.scales, static_cast<size_t>(n) * 4) != cudaSuccess) {
+    cudaGetLastError();
+    if (w.codes) cudaFree(w.codes);
+    return fail(RB_E_NOMEM, "W8A8 pack: device allocation failed");
+  }
+  RB_CUDA(cudaMemcpy(w.codes, codes_host, static_cast<size_t>(n) * k, cudaMemcpyHostToDevice), "codes upload");
+  RB_CUDA(cudaMemcpy(w.scales, w_scale_host, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice), "scale upload");
+  // TMA maps of the codes for the two N tile heights the int8 GEMM uses.
+  if ((rc = make_tmap_2d(&w.tmap_b[0], w.codes, 1, n, k, k, 128, 256, true)) != RB_OK) return rc;
+  if ((rc = make_tmap_2d(&w.tmap_b[1], w.codes, 1, n, k, k, 128, 128, true)) != RB_OK) return rc;
+  w.bytes = static_cast<size_t>(n) * k + static_cast<size_t>(n) * 4;
+  const int64_t id = e->next_id++;
+  e->weights[id] = w;
+  return id;
+}
+
+int rb_weight_info(int64_t id, int* kind, int64_t* n, int64_t* k) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Engine* e;
+  int rc = ensure_engine(&e);
+  if (rc) return rc;
+  auto it = e->weights.find(id);
+  if (it == e->weights.end()) return fail(RB_E_SHAPE, "weight id %lld is not packed", (long long)id);
+  if (kind) *kind = it->second.kind;
+  if (n) *n = it->second.n;
+  if (k) *k = it->second.k;
+  return RB_OK;
+}
+
+int rb_matmul(int64_t id, const void* x, int x_dtype, int64_t m, int64_t k, void* y, int y_dtype,
+              void* stream) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Engine* e;
+  int rc = ensure_engine(&e);
+  if (rc) return rc;
+  if (!x || !y) return fail(RB_E_SHAPE, "null matmul buffer");
+  return matmul_locked(e, id, x, x_dtype, m, k, y, y_dtype, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int rb_matmul_host(int64_t id, const void* x_host, int x_dtype, int64_t m, int64_t k, void* y_host,
+                   int y_dtype) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Engine* e;
+  int rc = ensure_engine(&e);
+  if (rc) return rc;
+  if (!x_host || !y_host) return fail(RB_E_SHAPE, "null matmul buffer");
+  auto it = e->weights.find(id);
+  if (it == e->weights.end()) return fail(RB_E_SHAPE, "weight id %lld is not packed", (long long)id);
+  const int64_t n = it->second.n;
+  const size_t xb = static_cast<size_t>(m) * k * dtype_bytes(x_dtype);
+  const size_t yb = static_cast<size_t>(m) * n * dtype_bytes(y_dtype);
+  if (!xb || !yb) return fail(RB_E_SHAPE, "bad dtype or empty matmul");
+  if ((rc = e->io_in.grow(xb, "matmul input staging")) != RB_OK) return rc;
+  if ((rc = e->io_out.grow(yb, "matmul output staging")) != RB_OK) return rc;
+  cudaStream_t st = e->host_stream;
+  RB_CUDA(cudaMemcpyAsync(e->io_in.ptr, x_host, xb, cudaMemcpyHostToDevice, st), "H2D");
+  if ((rc = matmul_locked(e, id, e->io_in.ptr, x_dtype, m, k, e->io_out.ptr, y_dtype, st)) != RB_OK)
+    return rc;
+  RB_CUDA(cudaMemcpyAsync(y_host, e->io_out.ptr, yb, cudaMemcpyDeviceToHost, st), "D2H");
+  RB_CUDA(cudaStreamSynchronize(st), "matmul sync");
+  return RB_OK;
+}
+
+int rb_attention(const void* q, const void* k, const void* v, void* out, int dtype, int64_t n_q,
+                 int64_t n_kv, int n_head, int n_kv_heads, int head_dim, float scale, float softcap,
+                 int mask_mode, int64_t window, int64_t q_start, int64_t kv_start, void* stream) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Engine* e;
+  int rc = ensure_engine(&e);
+  if (rc) return rc;
+  if (!q || !k || !v || !out) return fail(RB_E_SHAPE, "null attention buffer");
+  return attention_locked(e, q, k, v, out, dtype, n_q, n_kv, n_head, n_kv_heads, head_dim, scale,
+                          softcap, mask_mode, window, q_start, kv_start,
+                          reinterpret_cast<cudaStream_t>(stream));
+}
+
+int rb_attention_host(const void* q, const void* k, const void* v, void* out, int dtype,
+                      int64_t n_q, int64_t n_kv, int n_head, int n_kv_heads, int head_dim,
+                      float scale, float softcap, int mask_mode, int64_t window, int64_t q_start,
+                      int64_t kv_start) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Engine* e;
+  int rc = ensure_engine(&e);
+  if (rc) return rc;
+  if (!q || !k || !v || !out) return fail(RB_E_SHAPE, "null attention buffer");
+  const size_t eb = dtype_bytes(dtype);
+  if (!eb || n_q <= 0 || n_kv <= 0 || head_dim <= 0 || n_head <= 0 || n_kv_heads <= 0)
+    return fail(RB_E_SHAPE, "bad attention arguments");
+  const size_t qb = static_cast<size_t>(n_q) * n_head * head_dim * eb;
+  const size_t kb = static_cast<size_t>(n_kv) * n_kv_heads * head_dim * eb;
+  if ((rc = e->io_in.grow(qb, "q staging")) || (rc = e->io_out.grow(qb, "out staging")) ||
+      (rc = e->io_k.grow(kb, "k staging")) || (rc = e->io_v.grow(kb, "v staging")))
+    return rc;
+  cudaStream_t st = e->host_stream;
+  RB_CUDA(cudaMemcpyAsync(e->io_in.ptr, q, qb, cudaMemcpyHostToDevice, st), "H2D q");
+  RB_CUDA(cudaMemcpyAsync(e->io_k.ptr, k, kb, cudaMemcpyHostToDevice, st), "H2D k");
+  RB_CUDA(cudaMemcpyAsync(e->io_v.ptr, v, kb, cudaMemcpyHostToDevice, st), "H2D v");
+  if ((rc = attention_locked(e, e->io_in.ptr, e->io_k.ptr, e->io_v.ptr, e->io_out.ptr, dtype, n_q,
+                             n_kv, n_head, n_kv_heads, head_dim, scale, softcap, mask_mode, window,
+                             q_start, kv_start, st)) != RB_OK)
+    return rc;
+  RB_CUDA(cudaMemcpyAsync(out, e->io_out.ptr, qb, cudaMemcpyDeviceToHost, st), "D2H out");
+  RB_CUDA(cudaStreamSynchronize(st), "attention sync");
+  return RB_OK;
+}
+
+int rb_q8_0_dequant(int64_t id, void* out, int out_dtype, void* stream) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Engine* e;
+  int rc = ensure_engine(&e);
+  if (rc) return rc;
+  auto it = e->weights.find(id);
+  if (it == e->weights.end() || it->second.kind != RB_WEIGHT_Q8_0)
+    return fail(RB_E_SHAPE, "weight id %lld is not a Q8_0 weight", (long long)id);
+  if (out_dtype != RB_DTYPE_F32 && out_dtype != RB_DTYPE_F16) return fail(RB_E_SHAPE, "dequant dtype");
+  const Weight& w = it->second;
+  rc = launch_q8_dequant(w.codes, w.scales, static_cast<int>(w.n), static_cast<int>(w.k), out,
+                         out_dtype == RB_DTYPE_F16, reinterpret_cast<cudaStream_t>(stream));
+  g_launches++;
+  return rc == RB_OK ? RB_OK : fail(rc, "dequant launch failed");
+}
+
+int rb_quantize_rows_i8(const void* x, int x_dtype, int64_t m, int64_t k, int8_t* codes,
+                        float* row_scale, void* stream) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Engine* e;
+  int rc = ensure_engine(&e);
+  if (rc) return rc;
+  if (m <= 0 || k <= 0 || !x || !codes || !row_scale) return fail(RB_E_SHAPE, "bad quantiser arguments");
+  rc = launch_quantize_rows_i8(x, x_dtype, m, k, 0.0f, codes, row_scale,
+                               reinterpret_cast<cudaStream_t>(stream));
+  g_launches++;
+  return rc == RB_OK ? RB_OK : fail(rc, "quantiser launch failed");
+}
+
+int rb_matmul_i8_acc(int64_t id, const int8_t* codes, int64_t m, int32_t* acc, void* stream) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Engine* e;
+  int rc = ensure_engine(&e);
+  if (rc) return rc;
+  auto it = e->weights.find(id);
+  if (it == e->weights.end() || it->second.kind != RB_WEIGHT_W8A8)
+    return fail(RB_E_SHAPE, "weight id %lld is not a W8A8 weight", (long long)id);
+  const Weight& w = it->second;
+  if (m <= 0 || !codes || !acc) return fail(RB_E_SHAPE, "bad int8 matmul arguments");
+  CUtensorMap tmA;
+  if ((rc = make_tmap_2d(&tmA, codes, 1, m, w.k, w.k, 128, 128, true)) != RB_OK) return rc;
+  GemmLaunch L{};
+  L.M = static_cast<int>(m);
+  L.N = static_cast<int>(w.n);
+  L.K = static_cast<int>(w.k);
+  L.out = acc;
+  L.ldo = static_cast<int>(w.n);
+  L.out_dtype = RB_DTYPE_I32;
+  L.err = e->err;
+  L.num_sms = e->num_sms;
+  L.s_col = reinterpret_cast<const float*>(w.scales);
+  rc = launch_w8a8_gemm(tmA, w.tmap_b[0], w.tmap_b[1], L, reinterpret_cast<cudaStream_t>(stream));
+  g_launches++;
+  return rc == RB_OK ? RB_OK : fail(rc, "int8 gemm launch failed");
+}
+
+int rb_mem_stats(int64_t* weights_bytes, int64_t* scratch_bytes, int64_t* num_weights) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Engine* e;
+  int rc = ensure_engine(&e);
+  if (rc) return rc;
+  int64_t wb = 0;
+  for (auto& kv : e->weights) wb += static_cast<int64_t>(kv.second.bytes);
+  if (weights_bytes) *weights_bytes = wb;
+  if (scratch_bytes)
+    *scratch_bytes = static_cast<int64_t>(e->act.bytes + e->rowscale.bytes + e->io_in.bytes +
+                                          e->io_out.bytes + e->io_k.bytes + e->io_v.bytes);
+  if (num_weights) *num_weights = static_cast<int64_t>(e->weights.size());
+  return RB_OK;
+}
+
+int64_t rb_launch_count(int reset) {
+  return reset ? g_launches.exchange(0) : g_launches.load();
+}
+
+}  // extern "C"

@@ -1,0 +1,492 @@
+// attention.cu — fused masked grouped-query flash attention for sm_100a.
+//
+// Semantics: crates/rocket-npu/src/attn/oneshot.rs:130-199 (flash_attn_ref +
+// fa_score) with the mask predicates of crates/burn-rocket/src/masks.rs:11-114
+// evaluated in-kernel instead of an [n_q, n_kv] additive mask:
+//   s   = qk * scale;  s = softcap * tanh(s / softcap) when softcap != 0
+//   s   = max(s + mask, -30000)     (mask = 0 visible, -inf hidden)
+//   out = sum_j exp(s_j - max) v_j / sum_j exp(s_j - max)   over the real keys
+// so a fully masked row averages the values of every key it iterates, as the
+// reference does.
+//
+// Design (one CTA = two 128-row query "slots" of the same KV head):
+//   * GQA: the two slots are two query heads of one KV group (or two query
+//     tiles of one head when the group has a single head), so every K/V tile
+//     is loaded by TMA once and consumed by both slots.
+//   * warp 0: TMA (Q once, then a 2-stage K and V ring; 128-B swizzled tiles);
+//     warp 1: UMMA issuer; warps 4-7 / 8-11: softmax for slot 0 / slot 1, one
+//     query row per thread (TMEM lane = row).
+//   * TMEM per slot: S = Q·K^T in 128 f32 columns; P = exp(S - m) is written
+//     back as packed f16/bf16 over the first 64 of those columns and consumed
+//     by a TS-form UMMA (A from TMEM) O += P·V into D more f32 columns.
+//   * Online softmax in the log2 domain with a lazy rescale: the running max
+//     used for the exponent only moves (and O/l are rescaled) when a new row
+//     max exceeds it by more than 8 (a factor 256), so P stays within f16 range
+//     and O is rarely touched by the softmax warps.
+//   * Causal / window / block masks: tiles wholly outside a slot's visible key
+//     band are skipped; tiles wholly inside skip the predicate; a slot that
+//     may contain a fully masked row iterates every key tile (reference
+//     semantics above).
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+
+#include "sm100.cuh"
+#include "kernels.h"
+
+namespace rb {
+
+namespace attn {
+
+constexpr int BM = 128;      // query rows per slot
+constexpr int BN = 128;      // keys per tile
+constexpr int KV_STAGES = 2;
+constexpr int kSoftWarp0 = 4;
+constexpr int kThreads = 12 * 32;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kClamp = -30000.0f;   // fa_score clamp (oneshot.rs PAD_KEY_SCORE)
+constexpr float kRescaleThresh = 8.0f;  // log2 units
+constexpr int kNoBound = 1 << 30;
+
+struct Params {
+  void* out;
+  int n_q, n_kv, n_head, n_kv_heads, group;
+  int ldo;
+  int q_tiles;
+  int pairs_per_group;
+  float scale_log2;    // scale * log2(e)
+  float scale;
+  float softcap;
+  int dlo, dhi;        // visible iff dlo <= (k_off + j) - (q_off + i) <= dhi
+  int q_off, k_off;
+  uint32_t* err;
+};
+
+template <int D>
+struct Smem {
+  static constexpr int ATOMS = D / 64;              // 64-element (128-B) column atoms
+  static constexpr int TILE = 128 * 128 * ATOMS;    // bytes of one 128-row tile
+  static constexpr int Q_OFF = 0;                   // 2 slots
+  static constexpr int K_OFF = 2 * TILE;            // KV_STAGES
+  static constexpr int V_OFF = K_OFF + KV_STAGES * TILE;
+  static constexpr int BAR_OFF = V_OFF + KV_STAGES * TILE;
+  static constexpr int BYTES = BAR_OFF + 256 + 1024;
+};
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  if (BF16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+
+struct SlotInfo {
+  int head;   // query head
+  int qt;     // query tile
+  int lo, hi; // key tile range (inclusive); empty when lo > hi
+};
+
+__device__ __forceinline__ SlotInfo slot_info(const Params& p, int g, int item) {
+  SlotInfo s;
+  const int total = p.group * p.q_tiles;
+  if (item >= total) { s.head = 0; s.qt = 0; s.lo = 1; s.hi = 0; return s; }
+  s.qt = item / p.group;
+  s.head = g * p.group + item % p.group;
+  const int n_kv_tiles = (p.n_kv + BN - 1) / BN;
+  const int qa0 = p.q_off + s.qt * BM;
+  const int qa1 = p.q_off + min(s.qt * BM + BM, p.n_q) - 1;
+  // Visible absolute keys of row qa: [qa + dlo, qa + dhi] ∩ [k_off, k_off + n_kv).
+  const int klast = p.k_off + p.n_kv - 1;
+  auto row_empty = [&](int qa) {
+    const long lo = (p.dlo <= -kNoBound) ? p.k_off : max(static_cast<long>(p.k_off), static_cast<long>(qa) + p.dlo);
+    const long hi = (p.dhi >= kNoBound) ? klast : min(static_cast<long>(klast), static_cast<long>(qa) + p.dhi);
+    return lo > hi;
+  };
+  if (row_empty(qa0) || row_empty(qa1)) {
+    s.lo = 0; s.hi = n_kv_tiles - 1;  // reference semantics: iterate every key
+    return s;
+  }
+  long jlo = (p.dlo <= -kNoBound) ? 0 : static_cast<long>(qa0) + p.dlo - p.k_off;
+  long jhi = (p.dhi >= kNoBound) ? p.n_kv - 1 : static_cast<long>(qa1) + p.dhi - p.k_off;
+  jlo = max(jlo, 0L);
+  jhi = min(jhi, static_cast<long>(p.n_kv - 1));
+  s.lo = static_cast<int>(jlo / BN);
+  s.hi = static_cast<int>(jhi / BN);
+  return s;
+}
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+            const __grid_constant__ CUtensorMap tmV, Params p) {
+  using L = Smem<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* k_empty = bars + 3;  // [2]
+  uint64_t* v_full = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;  // [2]
+  uint64_t* s_full = bars + 9;   // [2 slots]
+  uint64_t* p_full = bars + 11;  // [2 slots]
+  uint64_t* o_done = bars + 13;  // [2 slots]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // Work item: heavy (late) query tiles first so causal runs finish together.
+  const int g = blockIdx.x % p.n_kv_heads;
+  const int pair = p.pairs_per_group - 1 - blockIdx.x / p.n_kv_heads;
+  SlotInfo sl[2];
+  sl[0] = slot_info(p, g, 2 * pair);
+  sl[1] = slot_info(p, g, 2 * pair + 1);
+  const bool act0 = sl[0].lo <= sl[0].hi, act1 = sl[1].lo <= sl[1].hi;
+  const int J0 = act1 ? min(sl[0].lo, sl[1].lo) : sl[0].lo;
+  const int J1 = act1 ? max(sl[0].hi, sl[1].hi) : sl[0].hi;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_done[i], 1);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA
+    if (elect_one_sync()) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      const int nslots = act1 ? 2 : 1;
+      mbar_arrive_expect_tx(q_full, nslots * L::TILE);
+      for (int s = 0; s < nslots; ++s)
+        for (int a = 0; a < L::ATOMS; ++a)
+          tma_load_2d(smem + L::Q_OFF + s * L::TILE + a * 16384, &tmQ, q_full,
+                      sl[s].head * D + a * 64, sl[s].qt * BM);
+      for (int j = J0; j <= J1; ++j) {
+        const int jl = j - J0, st = jl & 1;
+        const uint32_t ph = ((jl >> 1) & 1) ^ 1;
+        if (!mbar_wait(&k_empty[st], ph, p.err, abort_flag)) break;
+        mbar_arrive_expect_tx(&k_full[st], L::TILE);
+        for (int a = 0; a < L::ATOMS; ++a)
+          tma_load_2d(smem + L::K_OFF + st * L::TILE + a * 16384, &tmK, &k_full[st],
+                      g * D + a * 64, j * BN);
+        if (!mbar_wait(&v_empty[st], ph, p.err, abort_flag)) break;
+        mbar_arrive_expect_tx(&v_full[st], L::TILE);
+        for (int a = 0; a < L::ATOMS; ++a)
+          tma_load_2d(smem + L::V_OFF + st * L::TILE + a * 16384, &tmV, &v_full[st],
+                      g * D + a * 64, j * BN);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ UMMA issuer
+    if (elect_one_sync()) {
+      constexpr uint32_t idesc_s = idesc_f16(BM, BN, BF16, false, false);
+      constexpr uint32_t idesc_o = idesc_f16(BM, D, BF16, false, true);
+      const uint32_t q_addr = smem_u32(smem + L::Q_OFF);
+      const uint32_t k_addr = smem_u32(smem + L::K_OFF);
+      const uint32_t v_addr = smem_u32(smem + L::V_OFF);
+      int n_pv[2] = {0, 0};
+      int n_s[2] = {0, 0};
+      if (!mbar_wait(q_full, 0, p.err, abort_flag)) goto mma_done;
+      for (int j = J0; j <= J1; ++j) {
+        const int jl = j - J0, st = jl & 1;
+        const uint32_t ph = (jl >> 1) & 1;
+        if (!mbar_wait(&k_full[st], ph, p.err, abort_flag)) goto mma_done;
+        tc_fence_after();
+        for (int s = 0; s < 2; ++s) {
+          if (!(sl[s].lo <= j && j <= sl[s].hi)) continue;
+          // S/P region of this slot is free once its previous P·V retired.
+          if (n_pv[s] > 0) {
+            if (!mbar_wait(&o_done[s], (n_pv[s] - 1) & 1, p.err, abort_flag)) goto mma_done;
+            tc_fence_after();
+          }
+          const uint32_t d_tmem = tmem_base + s * 256;
+#pragma unroll
+          for (int ks = 0; ks < D / 16; ++ks) {
+            const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
+            umma_f16_ss(d_tmem, desc_kmajor_sw128(q_addr + s * L::TILE + off),
+                        desc_kmajor_sw128(k_addr + st * L::TILE + off), idesc_s, ks > 0);
+          }
+          umma_commit(&s_full[s]);
+          ++n_s[s];
+        }
+        umma_commit(&k_empty[st]);
+        if (!mbar_wait(&v_full[st], ph, p.err, abort_flag)) goto mma_done;
+        tc_fence_after();
+        for (int s = 0; s < 2; ++s) {
+          if (!(sl[s].lo <= j && j <= sl[s].hi)) continue;
+          if (!mbar_wait(&p_full[s], (n_s[s] - 1) & 1, p.err, abort_flag)) goto mma_done;
+          tc_fence_after();
+          const uint32_t o_tmem = tmem_base + s * 256 + 128;
+          const uint32_t p_tmem = tmem_base + s * 256;
+#pragma unroll
+          for (int ks = 0; ks < BN / 16; ++ks) {
+            const uint64_t vd = desc_mnmajor_sw128(v_addr + st * L::TILE + ks * 2048, 16384, 1024);
+            umma_f16_ts(o_tmem, p_tmem + ks * 8, vd, idesc_o, (n_pv[s] > 0 || ks > 0) ? 1u : 0u);
+          }
+          umma_commit(&o_done[s]);
+          ++n_pv[s];
+        }
+        umma_commit(&v_empty[st]);
+      }
+    mma_done:;
+    }
+  } else if (warp >= kSoftWarp0) {
+    // ------------------------------------------------------------ softmax
+    const int s = (warp - kSoftWarp0) >> 2;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const SlotInfo me = sl[s];
+    if (me.lo <= me.hi) {
+      const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+      const uint32_t s_col = s * 256, o_col = s * 256 + 128;
+      const int qa = p.q_off + me.qt * BM + row;  // absolute query position
+      float m_used = -INFINITY, l = 0.0f;
+      int it = 0;
+      bool ok = true;
+      for (int j = me.lo; j <= me.hi; ++j, ++it) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[s], it & 1, p.err, abort_flag))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        float x[BN];
+        {
+          uint32_t r[32];
+#pragma unroll
+          for (int c = 0; c < BN; c += 32) {
+            tmem_ld32(lane_base + s_col + c, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) x[c + i] = __uint_as_float(r[i]);
+          }
+        }
+        // Scores in the log2 domain, with the reference's clamp and masks.
+        const int ka0 = p.k_off + j * BN;          // absolute key of column 0
+        const int kvalid = p.n_kv - j * BN;        // real keys in this tile
+        const bool interior = (kvalid >= BN) &&
+            (p.dlo <= -kNoBound || ka0 - (p.q_off + me.qt * BM + BM - 1) >= p.dlo) &&
+            (p.dhi >= kNoBound || ka0 + BN - 1 - (p.q_off + me.qt * BM) <= p.dhi);
+        const float clamp2 = kClamp * kLog2e;
+        float mt = -INFINITY;
+        if (p.softcap != 0.0f) {
+#pragma unroll
+          for (int i = 0; i < BN; ++i) {
+            float v = __fmul_rn(x[i], p.scale);
+            v = p.softcap * tanhf(v / p.softcap);
+            x[i] = fmaxf(v, kClamp) * kLog2e;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < BN; ++i) x[i] = fmaxf(x[i] * p.scale_log2, clamp2);
+        }
+        if (!interior) {
+#pragma unroll
+          for (int i = 0; i < BN; ++i) {
+            const int d = ka0 + i - qa;
+            const bool vis = (p.dlo <= -kNoBound || d >= p.dlo) && (p.dhi >= kNoBound || d <= p.dhi);
+            x[i] = (i >= kvalid) ? -INFINITY : (vis ? x[i] : clamp2);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < BN; ++i) mt = fmaxf(mt, x[i]);
+        // Lazy rescale: move the exponent base only when the new max exceeds
+        // it by more than the threshold (P then stays <= 2^8).
+        float alpha = 1.0f;
+        bool need = false;
+        if (it == 0) {
+          m_used = mt;
+        } else if (mt > m_used + kRescaleThresh) {
+          alpha = fast_exp2(m_used - mt);
+          m_used = mt;
+          need = true;
+        }
+        if (__any_sync(0xffffffffu, need)) {
+          // P·V of the previous tile has retired (the S MMA of this tile was
+          // issued after it), so O is stable here.
+          uint32_t r[32];
+#pragma unroll
+          for (int c = 0; c < D; c += 32) {
+            tmem_ld32(lane_base + o_col + c, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            uint32_t lo16[16], hi16[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) { lo16[i] = r[i]; hi16[i] = r[16 + i]; }
+            tmem_st16(lane_base + o_col + c, lo16);
+            tmem_st16(lane_base + o_col + c + 16, hi16);
+          }
+          l *= alpha;
+        }
+        float rowsum = 0.0f;
+#pragma unroll
+        for (int c = 0; c < BN; c += 32) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float p0 = fast_exp2(x[c + 2 * i] - m_used);
+            const float p1 = fast_exp2(x[c + 2 * i + 1] - m_used);
+            rowsum += p0 + p1;
+            pk[i] = pack2<BF16>(p0, p1);
+          }
+          tmem_st16(lane_base + s_col + c / 2, pk);
+        }
+        l += rowsum;
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[s]);
+      }
+      // Epilogue: wait for the last P·V, normalise, store.
+      if (ok && __all_sync(0xffffffffu, mbar_wait(&o_done[s], (it - 1) & 1, p.err, abort_flag))) {
+        tc_fence_after();
+        const float inv_l = 1.0f / l;
+        const int qrow = me.qt * BM + row;
+        uint32_t r[32];
+#pragma unroll
+        for (int c = 0; c < D; c += 32) {
+          tmem_ld32(lane_base + o_col + c, r);
+          tmem_wait_ld();
+          if (qrow < p.n_q) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              pk[i] = pack2<BF16>(__uint_as_float(r[2 * i]) * inv_l,
+                                  __uint_as_float(r[2 * i + 1]) * inv_l);
+            uint4* dst = reinterpret_cast<uint4*>(
+                reinterpret_cast<uint16_t*>(p.out) + static_cast<int64_t>(qrow) * p.ldo +
+                me.head * D + c);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) drain_after_abort();  // let in-flight TMA / UMMA work retire
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+template <int D, bool BF16>
+static int launch_impl(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
+                       const Params& p, int grid, cudaStream_t stream) {
+  static uint64_t configured = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured & (1ull << (dev & 63)))) {
+    if (cudaFuncSetAttribute(attn_kernel<D, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Smem<D>::BYTES) != cudaSuccess)
+      return RB_E_DEVICE;
+    configured |= 1ull << (dev & 63);
+  }
+  attn_kernel<D, BF16><<<grid, kThreads, Smem<D>::BYTES, stream>>>(tmQ, tmK, tmV, p);
+  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
+}
+
+}  // namespace attn
+
+int launch_attention(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
+                     const AttnLaunch& L, cudaStream_t stream) {
+  using namespace attn;
+  Params p{};
+  p.out = L.out;
+  p.n_q = L.n_q;
+  p.n_kv = L.n_kv;
+  p.n_head = L.n_head;
+  p.n_kv_heads = L.n_kv_heads;
+  p.group = L.n_head / L.n_kv_heads;
+  p.ldo = L.ldo;
+  p.q_tiles = (L.n_q + BM - 1) / BM;
+  p.pairs_per_group = (p.group * p.q_tiles + 1) / 2;
+  p.scale = L.scale;
+  p.scale_log2 = L.scale * kLog2e;
+  p.softcap = L.softcap;
+  p.err = L.err;
+  // Mask band in relative coordinates (key - query).
+  auto clampw = [](int64_t w) { return static_cast<int>(w > (kNoBound / 2) ? (kNoBound / 2) : w); };
+  p.dlo = -kNoBound;
+  p.dhi = kNoBound;
+  p.q_off = 0;
+  p.k_off = 0;
+  switch (L.mask_mode) {
+    case RB_MASK_NONE:
+    case RB_MASK_NONE_BLOCK:
+      break;
+    case RB_MASK_CAUSAL:
+      p.dhi = 0;
+      break;
+    case RB_MASK_WINDOW:
+      p.dlo = -clampw(L.window);
+      p.dhi = clampw(L.window);
+      break;
+    case RB_MASK_CAUSAL_WINDOW:
+      p.dlo = 1 - clampw(L.window);
+      p.dhi = 0;
+      break;
+    case RB_MASK_WINDOW_BLOCK:
+      p.dlo = -clampw(L.window);
+      p.dhi = clampw(L.window);
+      p.q_off = static_cast<int>(L.q_start);
+      p.k_off = static_cast<int>(L.kv_start);
+      break;
+    case RB_MASK_CAUSAL_BLOCK:
+      if (L.window >= 0) p.dlo = 1 - clampw(L.window);
+      p.dhi = 0;
+      p.q_off = static_cast<int>(L.q_start);
+      p.k_off = static_cast<int>(L.kv_start);
+      break;
+    default:
+      return RB_E_SHAPE;
+  }
+  const int grid = p.pairs_per_group * L.n_kv_heads;
+  const bool bf16 = L.dtype == RB_DTYPE_BF16;
+  if (L.head_dim == 128)
+    return bf16 ? launch_impl<128, true>(tmQ, tmK, tmV, p, grid, stream)
+                : launch_impl<128, false>(tmQ, tmK, tmV, p, grid, stream);
+  if (L.head_dim == 64)
+    return bf16 ? launch_impl<64, true>(tmQ, tmK, tmV, p, grid, stream)
+                : launch_impl<64, false>(tmQ, tmK, tmV, p, grid, stream);
+  return RB_E_UNSUPPORTED;
+}
+
+}  // namespace rb

@@ -1,0 +1,73 @@
+// kernels.h — internal launch interface between the C ABI (abi.cu) and the
+// kernel translation units. Not part of the public ABI.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "../../include/rocket_b200.h"
+
+// Internal-only output type: raw int32 accumulators of the int8 GEMM.
+#define RB_DTYPE_I32 3
+
+namespace rb {
+
+struct GemmLaunch {
+  int M, N, K;
+  const int8_t* w_codes;  // Q8_0 codes [N, K]
+  const void* w_scales;   // Q8_0 f16 scales [N, K/32]
+  const float* s_row;     // W8A8 per-row activation scale [M]
+  const float* s_col;     // W8A8 per-channel weight scale [N]
+  void* out;
+  int ldo;
+  int out_dtype;
+  float out_scale;        // W8A8: 0 = unrounded output
+  uint32_t* err;
+  int num_sms;
+  int force_bn;           // 0 = heuristic
+};
+
+int launch_q8_gemm(const CUtensorMap& tmA, const GemmLaunch& L, cudaStream_t stream);
+// tmB256 / tmB128: TMA maps of the weight codes with box heights 256 / 128.
+int launch_w8a8_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB256,
+                     const CUtensorMap& tmB128, const GemmLaunch& L, cudaStream_t stream);
+int launch_q8_dequant(const int8_t* codes, const void* scales, int N, int K, void* out,
+                      bool f16_out, cudaStream_t stream);
+
+// Elementwise / codec kernels (quant.cu).
+int launch_cast(const void* x, int x_dtype, void* y, int y_dtype, int64_t count,
+                cudaStream_t stream);
+int launch_quantize_rows_i8(const void* x, int x_dtype, int64_t m, int64_t k, float in_scale,
+                            int8_t* codes, float* row_scale, cudaStream_t stream);
+int launch_q8_0_encode(const float* w, int64_t n, int64_t k, int8_t* codes, uint16_t* scales,
+                       cudaStream_t stream);
+int launch_q8_0_unpack_blocks(const uint8_t* blocks, int64_t n, int64_t k, int8_t* codes,
+                              uint16_t* scales, cudaStream_t stream);
+
+// Attention (attention.cu).
+struct AttnLaunch {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* out;
+  int dtype;  // RB_DTYPE_F16 or RB_DTYPE_BF16
+  int n_q, n_kv;
+  int n_head, n_kv_heads, head_dim;
+  int ldq, ldk, ldv, ldo;  // row strides in elements
+  float scale, softcap;
+  int mask_mode;
+  int64_t window, q_start, kv_start;
+  uint32_t* err;
+  int num_sms;
+};
+int launch_attention(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
+                     const AttnLaunch& L, cudaStream_t stream);
+
+// Tensor-map helper (abi.cu): 2D row-major [rows, cols] tile map with a
+// 128-byte swizzle; box = {box_cols, box_rows}.
+int make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t rows,
+                 uint64_t cols, uint64_t row_stride_elems, uint32_t box_cols, uint32_t box_rows,
+                 bool swizzle128);
+
+}  // namespace rb

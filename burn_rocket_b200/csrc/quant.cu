@@ -1,0 +1,211 @@
+// quant.cu — codec and quantiser kernels around the GEMMs:
+//   * Q8_0 encode (f32 -> codes + f16 block scale), the reference encoder of
+//     crates/rocket-npu/src/bin/q8_bench.rs:199-219, bit for bit;
+//   * GGUF Q8_0 block unpack (34-byte AoS blocks -> codes / scales planes),
+//     src/util/gguf.rs:197-215;
+//   * per-row int8 activation quantiser of the W8A8 path,
+//     crates/burn-rocket/src/ext.rs:1236-1238 and 1263-1279;
+//   * dtype casts (f32/bf16 -> f16 with round-to-nearest-even, like
+//     f32_to_f16_par, ext.rs:2144-2156).
+// All arithmetic uses explicitly rounded IEEE intrinsics (__fdiv_rn,
+// __fmul_rn) so results match the CPU oracle exactly.
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+
+#include "kernels.h"
+
+namespace rb {
+
+__device__ __forceinline__ float load_as_f32(const void* p, int dtype, int64_t i) {
+  if (dtype == RB_DTYPE_F32) return reinterpret_cast<const float*>(p)[i];
+  if (dtype == RB_DTYPE_F16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
+  return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+}
+
+// ---------------------------------------------------------------- Q8_0 encode
+// One thread per 32-value block. d = f16(amax / 127); codes are rounded half
+// away from zero against the *stored* f16 scale and clamped to [-127, 127].
+__global__ void q8_0_encode_kernel(const float* __restrict__ w, int64_t n, int64_t k,
+                                   int8_t* __restrict__ codes, uint16_t* __restrict__ scales) {
+  const int64_t nblk = k / 32;
+  const int64_t total = n * nblk;
+  for (int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; b < total;
+       b += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = b / nblk, g = b % nblk;
+    const float* seg = w + row * k + g * 32;
+    float amax = 0.0f;
+    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(seg[i]));
+    const __half d = __float2half_rn(__fdiv_rn(amax, 127.0f));
+    const float scale = __half2float(d);
+    const float inv = scale > 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
+    int8_t* q = codes + row * k + g * 32;
+    for (int i = 0; i < 32; ++i) {
+      const float r = roundf(__fmul_rn(seg[i], inv));  // half away from zero
+      q[i] = static_cast<int8_t>(fminf(fmaxf(r, -127.0f), 127.0f));
+    }
+    scales[row * nblk + g] = __half_as_ushort(d);
+  }
+}
+
+int launch_q8_0_encode(const float* w, int64_t n, int64_t k, int8_t* codes, uint16_t* scales,
+                       cudaStream_t stream) {
+  const int64_t total = n * (k / 32);
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 65535) blocks = 65535;
+  if (blocks < 1) blocks = 1;
+  q8_0_encode_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(w, n, k, codes, scales);
+  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
+}
+
+// ---------------------------------------------------------------- GGUF unpack
+// Block b of row r holds bytes [0,2) = f16 scale (little endian), [2,34) = codes.
+__global__ void q8_0_unpack_kernel(const uint8_t* __restrict__ blocks, int64_t n, int64_t k,
+                                   int8_t* __restrict__ codes, uint16_t* __restrict__ scales) {
+  const int64_t nblk = k / 32;
+  const int64_t total = n * nblk;
+  for (int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; b < total;
+       b += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint8_t* src = blocks + b * 34;
+    scales[b] = static_cast<uint16_t>(src[0] | (src[1] << 8));
+    int8_t* dst = codes + b * 32;  // rows are contiguous runs of blocks
+    for (int i = 0; i < 32; ++i) dst[i] = static_cast<int8_t>(src[2 + i]);
+  }
+}
+
+int launch_q8_0_unpack_blocks(const uint8_t* blocks, int64_t n, int64_t k, int8_t* codes,
+                              uint16_t* scales, cudaStream_t stream) {
+  const int64_t total = n * (k / 32);
+  int64_t grid = (total + 255) / 256;
+  if (grid > 65535) grid = 65535;
+  if (grid < 1) grid = 1;
+  q8_0_unpack_kernel<<<static_cast<int>(grid), 256, 0, stream>>>(blocks, n, k, codes, scales);
+  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
+}
+
+// ---------------------------------------------------------------- row quantiser
+// One warp per row. Dynamic mode (in_scale == 0): s = max(max|x| / 127, 1e-12).
+// Static mode: s = in_scale. code = clamp(rint(x * (1/s)), -128, 127).
+template <int DT>
+__global__ void quantize_rows_kernel(const void* __restrict__ x, int64_t m, int64_t k,
+                                     float in_scale, int8_t* __restrict__ codes,
+                                     float* __restrict__ row_scale) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
+       row < m; row += warps_total) {
+    const int64_t base = row * k;
+    float s = in_scale;
+    if (in_scale == 0.0f) {
+      float amax = 0.0f;
+      for (int64_t i = lane; i < k; i += 32) amax = fmaxf(amax, fabsf(load_as_f32(x, DT, base + i)));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-12f);
+    }
+    const float inv = __fdiv_rn(1.0f, s);
+    int8_t* q = codes + base;
+    if ((k & 3) == 0) {
+      for (int64_t i = lane * 4; i < k; i += 128) {
+        char4 c;
+        c.x = static_cast<signed char>(fminf(fmaxf(rintf(__fmul_rn(load_as_f32(x, DT, base + i), inv)), -128.f), 127.f));
+        c.y = static_cast<signed char>(fminf(fmaxf(rintf(__fmul_rn(load_as_f32(x, DT, base + i + 1), inv)), -128.f), 127.f));
+        c.z = static_cast<signed char>(fminf(fmaxf(rintf(__fmul_rn(load_as_f32(x, DT, base + i + 2), inv)), -128.f), 127.f));
+        c.w = static_cast<signed char>(fminf(fmaxf(rintf(__fmul_rn(load_as_f32(x, DT, base + i + 3), inv)), -128.f), 127.f));
+        *reinterpret_cast<char4*>(q + i) = c;
+      }
+    } else {
+      for (int64_t i = lane; i < k; i += 32)
+        q[i] = static_cast<int8_t>(
+            fminf(fmaxf(rintf(__fmul_rn(load_as_f32(x, DT, base + i), inv)), -128.f), 127.f));
+    }
+    if (lane == 0) row_scale[row] = s;
+  }
+}
+
+int launch_quantize_rows_i8(const void* x, int x_dtype, int64_t m, int64_t k, float in_scale,
+                            int8_t* codes, float* row_scale, cudaStream_t stream) {
+  const int threads = 256;
+  int64_t blocks = (m + 7) / 8;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  if (blocks < 1) blocks = 1;
+  switch (x_dtype) {
+    case RB_DTYPE_F32:
+      quantize_rows_kernel<RB_DTYPE_F32><<<static_cast<int>(blocks), threads, 0, stream>>>(
+          x, m, k, in_scale, codes, row_scale);
+      break;
+    case RB_DTYPE_F16:
+      quantize_rows_kernel<RB_DTYPE_F16><<<static_cast<int>(blocks), threads, 0, stream>>>(
+          x, m, k, in_scale, codes, row_scale);
+      break;
+    case RB_DTYPE_BF16:
+      quantize_rows_kernel<RB_DTYPE_BF16><<<static_cast<int>(blocks), threads, 0, stream>>>(
+          x, m, k, in_scale, codes, row_scale);
+      break;
+    default:
+      return RB_E_SHAPE;
+  }
+  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
+}
+
+// ---------------------------------------------------------------- casts
+template <int SRC, int DST>
+__global__ void cast_kernel(const void* __restrict__ x, void* __restrict__ y, int64_t count) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < count;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float v = load_as_f32(x, SRC, i);
+    if (DST == RB_DTYPE_F32) reinterpret_cast<float*>(y)[i] = v;
+    else if (DST == RB_DTYPE_F16) reinterpret_cast<__half*>(y)[i] = __float2half_rn(v);
+    else reinterpret_cast<__nv_bfloat16*>(y)[i] = __float2bfloat16_rn(v);
+  }
+}
+
+// f32 -> f16, 8 elements per thread (the hot cast on the Q8_0 matmul path).
+__global__ void cast_f32_f16_vec_kernel(const float4* __restrict__ x, uint4* __restrict__ y,
+                                        int64_t count8) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < count8;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float4 a = x[2 * i], b = x[2 * i + 1];
+    uint4 o;
+    __half2* h = reinterpret_cast<__half2*>(&o);
+    h[0] = __floats2half2_rn(a.x, a.y);
+    h[1] = __floats2half2_rn(a.z, a.w);
+    h[2] = __floats2half2_rn(b.x, b.y);
+    h[3] = __floats2half2_rn(b.z, b.w);
+    y[i] = o;
+  }
+}
+
+int launch_cast(const void* x, int x_dtype, void* y, int y_dtype, int64_t count,
+                cudaStream_t stream) {
+  const int threads = 256;
+  if (x_dtype == RB_DTYPE_F32 && y_dtype == RB_DTYPE_F16 && (count & 7) == 0 &&
+      (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
+    const int64_t c8 = count / 8;
+    int64_t blocks = (c8 + threads - 1) / threads;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    if (blocks < 1) blocks = 1;
+    cast_f32_f16_vec_kernel<<<static_cast<int>(blocks), threads, 0, stream>>>(
+        reinterpret_cast<const float4*>(x), reinterpret_cast<uint4*>(y), c8);
+    return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
+  }
+  int64_t blocks = (count + threads - 1) / threads;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  if (blocks < 1) blocks = 1;
+  const int g = static_cast<int>(blocks);
+#define RB_CAST_CASE(S, D)                                                   \
+  if (x_dtype == S && y_dtype == D) {                                        \
+    cast_kernel<S, D><<<g, threads, 0, stream>>>(x, y, count);               \
+    return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;          \
+  }
+  RB_CAST_CASE(RB_DTYPE_F32, RB_DTYPE_F16)
+  RB_CAST_CASE(RB_DTYPE_F32, RB_DTYPE_BF16)
+  RB_CAST_CASE(RB_DTYPE_F16, RB_DTYPE_F32)
+  RB_CAST_CASE(RB_DTYPE_BF16, RB_DTYPE_F32)
+  RB_CAST_CASE(RB_DTYPE_BF16, RB_DTYPE_F16)
+  RB_CAST_CASE(RB_DTYPE_F16, RB_DTYPE_BF16)
+#undef RB_CAST_CASE
+  return RB_E_SHAPE;
+}
+
+}  // namespace rb

@@ -1,0 +1,171 @@
+/*
+ * rocket_b200.h — C ABI of librocket_b200.so, the B200 (sm_100a) replacement
+ * for the operations burn-rocket offloads through its Burn backend extension
+ * (crates/burn-rocket/src/ext.rs:57-164, trait RocketOps).
+ *
+ * Conventions
+ *   - Every entry point returns RB_OK (0) or a negative status code; the codes
+ *     are burn-rocket's (crates/burn-rocket/src/lib.rs:116-146) extended with
+ *     rocket-npu's RANGE/IO (crates/rocket-npu/src/error.rs:28-55). Pack entry
+ *     points return a positive weight id or a negative status code.
+ *   - Tensor arguments are DEVICE pointers unless the name ends in _host.
+ *     Device entry points are asynchronous on the given stream (a cudaStream_t
+ *     passed as void*, NULL = legacy default stream); host entry points copy
+ *     in and out themselves and return after the result is on the host.
+ *   - Layouts follow burn-rocket's boundary: weights [N, K] row-major
+ *     (ext.rs:758-779), activations [M, K] row-major, attention tensors
+ *     token-major [S, heads * head_dim] (ext.rs:1680-1701).
+ *   - One engine per process and device (rb_init). Calls are serialised by an
+ *     internal mutex, as the reference serialises through its global ENGINE
+ *     mutex (ext.rs:537-556). Resident weights live until process exit
+ *     ("pack-and-drop", ext.rs:39-50).
+ */
+#ifndef ROCKET_B200_H
+#define ROCKET_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define RB_API __attribute__((visibility("default")))
+#else
+#define RB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes (lib.rs:116-146 and rocket-npu error.rs:28-55). */
+#define RB_OK 0
+#define RB_E_SHAPE (-1)       /* unsupported shape / bad argument */
+#define RB_E_TILING (-2)      /* shape not tileable (caller may fall back) */
+#define RB_E_NOMEM (-3)       /* allocation failed */
+#define RB_E_DEVICE (-4)      /* CUDA runtime / device failure */
+#define RB_E_UNSUPPORTED (-5) /* feature not implemented */
+#define RB_E_RANGE (-6)       /* value left the output type's range */
+#define RB_E_IO (-7)          /* argument / state failure outside the above */
+
+/* Element types of activation / output buffers. */
+#define RB_DTYPE_F32 0
+#define RB_DTYPE_F16 1
+#define RB_DTYPE_BF16 2
+
+/* Attention mask modes: ext.rs:1643-1667 (enum MaskMode). */
+#define RB_MASK_NONE 0          /* full bidirectional, n_q == n_kv            */
+#define RB_MASK_NONE_BLOCK 1    /* bidirectional over a query chunk           */
+#define RB_MASK_CAUSAL 2        /* j <= t                                     */
+#define RB_MASK_WINDOW 3        /* |t - j| <= window                          */
+#define RB_MASK_CAUSAL_WINDOW 4 /* t - window < j <= t                        */
+#define RB_MASK_WINDOW_BLOCK 5  /* |(q0+i) - (k0+j)| <= window                */
+#define RB_MASK_CAUSAL_BLOCK 6  /* k0+j <= q0+i (and q0+i-window < k0+j if w>=0) */
+
+/* Weight kinds held by the registry. */
+#define RB_WEIGHT_Q8_0 1 /* int8 codes + f16 scale per 32-wide K block           */
+#define RB_WEIGHT_W8A8 2 /* per-output-channel int8 codes + f32 scale (QAT form) */
+
+/* Replaces burn_rocket::init(threads) (ext.rs:561-580): binds the calling
+ * process to CUDA device `device_ordinal` and creates the engine. Later calls
+ * are no-ops returning RB_OK. */
+RB_API int rb_init(int device_ordinal);
+
+/* Copies the last error message of this thread into buf (NUL-terminated).
+ * Returns the message length. The reference logs its failures on stderr
+ * before panicking with OpFailure (ext.rs:344-352). */
+RB_API int rb_last_error(char* buf, size_t len);
+
+/* Synchronises the engine's device and reports kernel-side failures recorded
+ * in the device error word (a bounded wait that timed out, a shape guard):
+ * RB_OK, or RB_E_DEVICE with the detail in rb_last_error. Clears the word. */
+RB_API int rb_check_device_errors(void);
+
+/* ---- packing (weights become resident; the caller's buffer can be freed) */
+
+/* GGUF Q8_0 blocks (34 bytes: f16 scale + 32 int8 codes, util/gguf.rs:197-215)
+ * of an [n, k] weight in HOST memory, blocks running along K. Replaces
+ * rocket_pack for Q8_0 checkpoints (ext.rs:586-597, 829-872). */
+RB_API int64_t rb_pack_q8_0(const void* blocks_host, int64_t n, int64_t k);
+
+/* f32 [n_i, k] weights in HOST memory, quantised to Q8_0 with the reference
+ * encoder (q8_bench.rs:199-219) and concatenated along N. num_parts = 1, 2, 3
+ * replace rocket_pack / rocket_pack2 / rocket_pack3 (ext.rs:59-64, 829-934). */
+RB_API int64_t rb_pack_f32_q8_0(const float* const* parts_host, const int64_t* n_parts,
+                         int num_parts, int64_t k);
+
+/* Per-output-channel int8 weight of a QAT checkpoint: codes [n, k] and
+ * w_scale [n] in HOST memory. in_scale == 0 selects the dynamic per-row
+ * activation scale max|x|/127; out_scale == 0 leaves the output unrounded.
+ * Replaces burn_rocket::pack_qat (ext.rs:1382-1425). */
+RB_API int64_t rb_pack_w8a8(const int8_t* codes_host, const float* w_scale_host, int64_t n, int64_t k,
+                     float in_scale, float out_scale);
+
+/* Weight geometry of a packed id: kind (RB_WEIGHT_*), n, k. */
+RB_API int rb_weight_info(int64_t id, int* kind, int64_t* n, int64_t* k);
+
+/* ---- matmul */
+
+/* y[m, n] = x[m, k] · W[n, k]^T with resident weight `id`. x and y are device
+ * buffers of x_dtype / y_dtype (RB_DTYPE_*). Replaces rocket_matmul /
+ * matmul_impl (ext.rs:85, 1208-1232): Q8_0 weights run the tcgen05 f16 GEMM
+ * (activations rounded to f16 like f32_to_f16_par, ext.rs:2144-2156); W8A8
+ * weights quantise each activation row to int8 (ext.rs:1263-1279) and run the
+ * tcgen05 int8 GEMM with the f32 epilogue of ext.rs:1350-1363. */
+RB_API int rb_matmul(int64_t id, const void* x, int x_dtype, int64_t m, int64_t k, void* y,
+              int y_dtype, void* stream);
+
+/* Same as rb_matmul with HOST x (x_dtype) and HOST y (y_dtype): the
+ * host<->device copies happen inside the call, as in the reference whose
+ * Burn tensors live in host memory. */
+RB_API int rb_matmul_host(int64_t id, const void* x_host, int x_dtype, int64_t m, int64_t k,
+                   void* y_host, int y_dtype);
+
+/* ---- attention */
+
+/* Masked grouped-query attention (ext.rs:1669-1858, attention_impl):
+ * out = softmax(scale·QK^T (softcapped when softcap != 0) + mask) · V per head,
+ * head h reading KV head h / (n_head / n_kv_heads). q/out are [n_q, n_head*d],
+ * k/v are [n_kv, n_kv_heads*d], all of `dtype`. mask_mode is RB_MASK_*;
+ * window < 0 means "no window" for the windowed modes; q_start / kv_start are
+ * the absolute offsets of the block modes (clamped at 0 like ext.rs:736-741).
+ * Scores follow fa_score (attn/oneshot.rs:193-199): masked keys score -30000,
+ * so a fully masked row averages the values of the keys it iterates. */
+RB_API int rb_attention(const void* q, const void* k, const void* v, void* out, int dtype, int64_t n_q,
+                 int64_t n_kv, int n_head, int n_kv_heads, int head_dim, float scale,
+                 float softcap, int mask_mode, int64_t window, int64_t q_start, int64_t kv_start,
+                 void* stream);
+
+/* rb_attention with HOST q/k/v/out buffers (copies inside the call). */
+RB_API int rb_attention_host(const void* q, const void* k, const void* v, void* out, int dtype,
+                      int64_t n_q, int64_t n_kv, int n_head, int n_kv_heads, int head_dim,
+                      float scale, float softcap, int mask_mode, int64_t window, int64_t q_start,
+                      int64_t kv_start);
+
+/* ---- codec and quantiser surfaces (parity / debugging) */
+
+/* Dequantise a packed Q8_0 weight into a device buffer: f32 (exact d·q, the
+ * GGUF decode of util/gguf.rs:197-215) or f16 (RNE(d·q), the values the GEMM
+ * stages in shared memory). */
+RB_API int rb_q8_0_dequant(int64_t id, void* out, int out_dtype, void* stream);
+
+/* Per-row dynamic int8 quantisation of an [m, k] device activation
+ * (ext.rs:1263-1279): scale = max(max|x|/127, 1e-12), code =
+ * clamp(round_ties_even(x · (1/scale)), -128, 127). */
+RB_API int rb_quantize_rows_i8(const void* x, int x_dtype, int64_t m, int64_t k, int8_t* codes,
+                        float* row_scale, void* stream);
+
+/* Raw int32 accumulators acc[m, n] = codes[m, k] · W[n, k]^T of a W8A8 weight
+ * (the exact integer product the reference checks under ROCKET_QAT_CHECK,
+ * ext.rs:1309-1334). */
+RB_API int rb_matmul_i8_acc(int64_t id, const int8_t* codes, int64_t m, int32_t* acc, void* stream);
+
+/* ---- statistics (MemStats, lib.rs:44-96) */
+RB_API int rb_mem_stats(int64_t* weights_bytes, int64_t* scratch_bytes, int64_t* num_weights);
+
+/* Number of rocket-b200 kernel launches issued since the last reset. */
+RB_API int64_t rb_launch_count(int reset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ROCKET_B200_H */

@@ -1,0 +1,165 @@
+"""Device parity of the fused GQA flash-attention kernel, through the C ABI.
+
+Small and ragged cases compare against the CPU oracle (flash_attn_ref of
+attn/oneshot.rs:130-185 with the masks.rs predicates); the full BASELINE
+config #2 size compares against a plain torch fp32 reference of the same op.
+Tolerance (north star): cosine >= 0.9999 and max |err| <= 1e-2 * max |ref|.
+"""
+import math
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+COS_MIN = 0.9999
+MAX_REL = 1e-2
+
+
+def cosine(a, b):
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b) + 1e-300))
+
+
+def max_rel(got, want):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    return float(np.abs(got - want).max() / (np.abs(want).max() + 1e-30))
+
+
+def run_case(rb, orc, n_q, n_kv, h, hkv, d, mode, window=-1, q0=0, k0=0, softcap=0.0, seed=0,
+             dtype="f16"):
+    import torch
+    rng = np.random.default_rng(seed)
+    q = orc.f32_to_f16_bits(rng.standard_normal((n_q, h * d)).astype(np.float32))
+    k = orc.f32_to_f16_bits(rng.standard_normal((n_kv, hkv * d)).astype(np.float32))
+    v = orc.f32_to_f16_bits(rng.standard_normal((n_kv, hkv * d)).astype(np.float32))
+    scale = 1.0 / math.sqrt(d)
+    ref = orc.f16_bits_to_f32(orc.flash_attn_ref(q, k, v, h, hkv, d, scale, softcap, mode, window, q0, k0))
+    tq, tk, tv = (torch.from_numpy(a.view(np.float16)).cuda() for a in (q, k, v))
+    if dtype == "f32":
+        tq, tk, tv = tq.float(), tk.float(), tv.float()
+    out = rb.attention_raw(tq, tk, tv, h, hkv, d, scale, softcap, mode, window, q0, k0)
+    torch.cuda.synchronize()
+    rb.check_device_errors()
+    return out.float().cpu().numpy(), ref
+
+
+M = None  # filled lazily from the oracle module
+
+
+CASES = [
+    # n_q, n_kv, h, hkv, d, mode, window, q0, k0
+    (1, 1, 2, 1, 128, 0, -1, 0, 0),
+    (77, 77, 2, 1, 128, 0, -1, 0, 0),
+    (128, 128, 4, 2, 128, 2, -1, 0, 0),
+    (300, 300, 16, 8, 128, 2, -1, 0, 0),
+    (300, 300, 16, 8, 128, 0, -1, 0, 0),
+    (257, 257, 8, 8, 64, 2, -1, 0, 0),
+    (200, 200, 32, 4, 128, 2, -1, 0, 0),
+    (333, 333, 4, 2, 64, 3, 37, 0, 0),
+    (333, 333, 4, 2, 128, 4, 50, 0, 0),
+    (150, 400, 4, 2, 128, 5, 60, 200, 150),
+    (150, 500, 4, 2, 128, 6, -1, 300, 0),
+    (150, 400, 4, 2, 64, 6, 90, 300, 100),
+    (64, 300, 2, 1, 128, 1, -1, 0, 0),
+]
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_attention_matches_oracle(rb, orc, case):
+    n_q, n_kv, h, hkv, d, mode, window, q0, k0 = case
+    got, ref = run_case(rb, orc, n_q, n_kv, h, hkv, d, mode, window, q0, k0, seed=sum(case[:5]))
+    assert cosine(got, ref) >= COS_MIN, cosine(got, ref)
+    assert max_rel(got, ref) <= MAX_REL, max_rel(got, ref)
+
+
+def test_attention_softcap(rb, orc):
+    got, ref = run_case(rb, orc, 200, 200, 4, 2, 128, 2, softcap=5.0, seed=3)
+    assert cosine(got, ref) >= COS_MIN
+    assert max_rel(got, ref) <= MAX_REL
+
+
+def test_attention_fully_masked_rows_average_every_key(rb, orc):
+    """A causal block whose keys lie above some queries: those rows see no key
+    and average every real key (attn/oneshot.rs:910-950)."""
+    got, ref = run_case(rb, orc, 130, 200, 2, 1, 128, 6, -1, q0=0, k0=60, seed=4)
+    assert cosine(got, ref) >= COS_MIN
+    assert max_rel(got, ref) <= MAX_REL
+
+
+def test_attention_f32_boundary(rb, orc):
+    got, ref = run_case(rb, orc, 160, 160, 4, 2, 128, 2, seed=5, dtype="f32")
+    assert cosine(got, ref) >= COS_MIN
+    assert max_rel(got, ref) <= MAX_REL
+
+
+def torch_ref(q, k, v, h, hkv, d, causal):
+    import torch
+    n = q.shape[0]
+    g = h // hkv
+    qf = q.float().view(n, h, d).transpose(0, 1)
+    kf = k.float().view(-1, hkv, d).transpose(0, 1).repeat_interleave(g, 0)
+    vf = v.float().view(-1, hkv, d).transpose(0, 1).repeat_interleave(g, 0)
+    s = (qf @ kf.transpose(1, 2)) / math.sqrt(d)
+    if causal:
+        mask = torch.ones(n, n, dtype=torch.bool, device=q.device).tril()
+        s = s.masked_fill(~mask, float("-inf"))
+    return (torch.softmax(s, -1) @ vf).transpose(0, 1).reshape(n, h * d)
+
+
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+def test_attention_config2_full_size(rb, causal, dtype):
+    """BASELINE config #2: 3633 tokens, 16/8 heads x 128, causal and bidirectional."""
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(7)
+    tdt = torch.float16 if dtype == "f16" else torch.bfloat16
+    n, h, hkv, d = 3633, 16, 8, 128
+    q = torch.randn(n, h * d, device="cuda", generator=g).to(tdt)
+    k = torch.randn(n, hkv * d, device="cuda", generator=g).to(tdt)
+    v = torch.randn(n, hkv * d, device="cuda", generator=g).to(tdt)
+    out = rb.attention(q, k, v, h, hkv, d, 1.0 / math.sqrt(d), None, causal)
+    torch.cuda.synchronize()
+    rb.check_device_errors()
+    ref = torch_ref(q, k, v, h, hkv, d, causal)
+    got = out.float()
+    cos = torch.nn.functional.cosine_similarity(got.flatten().double(), ref.flatten().double(), dim=0).item()
+    mr = ((got - ref).abs().max() / ref.abs().max()).item()
+    assert cos >= COS_MIN, cos
+    assert mr <= MAX_REL, mr
+
+
+def test_attention_host_entry(rb, orc):
+    import burn_rocket_b200._lib as L
+    rng = np.random.default_rng(8)
+    n, h, hkv, d = 100, 4, 2, 128
+    q = orc.f32_to_f16_bits(rng.standard_normal((n, h * d)).astype(np.float32))
+    k = orc.f32_to_f16_bits(rng.standard_normal((n, hkv * d)).astype(np.float32))
+    v = orc.f32_to_f16_bits(rng.standard_normal((n, hkv * d)).astype(np.float32))
+    out = np.empty_like(q)
+    rc = L.load().rb_attention_host(q.ctypes.data, k.ctypes.data, v.ctypes.data, out.ctypes.data, L.DTYPE_F16,
+                                    n, n, h, hkv, d, 1.0 / math.sqrt(d), 0.0, L.MASK_CAUSAL, -1, 0, 0)
+    assert rc == 0, L.last_error()
+    ref = orc.f16_bits_to_f32(orc.flash_attn_ref(q, k, v, h, hkv, d, 1.0 / math.sqrt(d), 0.0, 2))
+    got = orc.f16_bits_to_f32(out)
+    assert cosine(got, ref) >= COS_MIN and max_rel(got, ref) <= MAX_REL
+
+
+def test_attention_contract_errors(rb):
+    import torch
+    q = torch.zeros(8, 4 * 96, dtype=torch.float16, device="cuda")
+    with pytest.raises(rb.OpFailure) as ei:
+        rb.attention(q, q[:, :2 * 96].contiguous(), q[:, :2 * 96].contiguous(), 4, 2, 96, 0.1)
+    assert ei.value.error.rc == -5  # head_dim not supported by this build
+    q = torch.zeros(8, 3 * 128, dtype=torch.float16, device="cuda")
+    kv = torch.zeros(8, 2 * 128, dtype=torch.float16, device="cuda")
+    with pytest.raises(rb.OpFailure) as ei:
+        rb.attention(q, kv, kv, 3, 2, 128, 0.1)
+    assert ei.value.error.rc == -1  # n_head % n_kv_heads
+    q = torch.zeros(8, 2 * 128, dtype=torch.float16, device="cuda")
+    kv = torch.zeros(9, 128, dtype=torch.float16, device="cuda")
+    with pytest.raises(rb.OpFailure) as ei:
+        rb.attention(q, kv, kv, 2, 1, 128, 0.1, None, True)
+    assert ei.value.error.rc == -1  # full-sequence modes need n_q == n_kv

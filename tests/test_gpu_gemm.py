@@ -1,0 +1,168 @@
+"""Device parity of the quantised matmuls against the CPU oracle, through the
+C ABI (librocket_b200.so).
+
+Bars (north star): the Q8_0 dequantisation and the W8A8 int32 accumulators are
+bit-exact; W8A8 outputs are bit-exact too (the epilogue is a fixed sequence of
+f32 roundings); Q8_0 GEMM outputs reach cosine >= 0.9999 and a max error of at
+most 1e-2 of the output's max magnitude against the reference f32 path
+(f64-accumulated product with the exactly dequantised weight).
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+COS_MIN = 0.9999
+MAX_REL = 1e-2
+
+
+def cosine(a, b):
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b) + 1e-300))
+
+
+def max_rel(got, want):
+    return float(np.abs(np.asarray(got, np.float64) - want).max() / (np.abs(want).max() + 1e-30))
+
+
+def q8_weight(orc, n, k, seed, std=0.02):
+    rng = np.random.default_rng(seed)
+    w = (rng.standard_normal((n, k)) * std).astype(np.float32)
+    codes, scales = orc.q8_0_quantize(w)
+    return w, codes, scales
+
+
+# ------------------------------------------------------------------ Q8_0 codec on device
+@pytest.mark.parametrize("n,k", [(64, 32), (3072, 1024), (130, 96)])
+def test_q8_0_device_encode_and_dequant_bit_exact(rb, orc, n, k):
+    import torch
+    w, codes, scales = q8_weight(orc, n, k, seed=n * 7 + k)
+    deq = orc.q8_0_dequant(codes, scales)
+    # GGUF block ingest
+    wid = rb.pack_q8_0_blocks(orc.q8_0_to_blocks(codes, scales), n, k)
+    got = rb.q8_0_dequant(wid, "f32").cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), deq.view(np.uint32))
+    # the f16 values the GEMM stages in shared memory: RNE(d*q)
+    got16 = rb.q8_0_dequant(wid, "f16").cpu().numpy()
+    assert np.array_equal(got16.view(np.uint16), orc.f32_to_f16_bits(deq))
+    # device encoder (rb_pack_f32_q8_0) == reference encoder, bit for bit
+    wid2 = rb.pack(w)
+    got2 = rb.q8_0_dequant(wid2, "f32").cpu().numpy()
+    assert np.array_equal(got2.view(np.uint32), deq.view(np.uint32))
+    torch.cuda.synchronize()
+    rb.check_device_errors()
+
+
+# ------------------------------------------------------------------ Q8_0 GEMM
+def _q8_gemm_case(rb, orc, m, n, k, seed, x_dtype="f32"):
+    import torch
+    rng = np.random.default_rng(seed)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    w, codes, scales = q8_weight(orc, n, k, seed + 1)
+    wid = rb.pack_q8_0_blocks(orc.q8_0_to_blocks(codes, scales), n, k)
+    tdt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[x_dtype]
+    x = torch.from_numpy(a).to("cuda", tdt)
+    y = rb.matmul(x, wid, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    rb.check_device_errors()
+    got = y.cpu().numpy()
+    deq = orc.q8_0_dequant(codes, scales)
+    ref = orc.gemm_f64acc(a, deq)  # the reference f32 path
+    return got, ref, a, deq
+
+
+def test_q8_0_gemm_config1_parity(rb, orc):
+    """BASELINE config #1: [512, 1024] x Q8_0 [3072, 1024]^T -> f32 [512, 3072]."""
+    got, ref, a, deq = _q8_gemm_case(rb, orc, 512, 3072, 1024, seed=11)
+    assert cosine(got, ref) >= COS_MIN
+    assert max_rel(got, ref) <= MAX_REL
+    # tighter: same f16-rounded operands, only the accumulation order differs
+    a16 = orc.f16_bits_to_f32(orc.f32_to_f16_bits(a))
+    w16 = orc.f16_bits_to_f32(orc.f32_to_f16_bits(deq))
+    ref16 = orc.gemm_f64acc(a16, w16)
+    assert max_rel(got, ref16) <= 1e-5
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 32, 32), (3, 96, 96), (129, 200, 1024), (300, 3072, 64),
+                                   (77, 136, 160), (1000, 1024, 1024), (128, 6144, 1024)])
+def test_q8_0_gemm_ragged_shapes(rb, orc, m, n, k):
+    got, ref, _, _ = _q8_gemm_case(rb, orc, m, n, k, seed=m + n + k)
+    assert cosine(got, ref) >= COS_MIN
+    assert max_rel(got, ref) <= MAX_REL
+
+
+@pytest.mark.parametrize("x_dtype", ["f16", "bf16"])
+def test_q8_0_gemm_half_inputs(rb, orc, x_dtype):
+    got, ref, _, _ = _q8_gemm_case(rb, orc, 256, 512, 512, seed=5, x_dtype=x_dtype)
+    assert cosine(got, ref) >= COS_MIN
+    assert max_rel(got, ref) <= MAX_REL
+
+
+def test_q8_0_gemm_host_entry_matches_device(rb, orc):
+    import torch
+    rng = np.random.default_rng(21)
+    a = rng.standard_normal((64, 256)).astype(np.float32)
+    w, codes, scales = q8_weight(orc, 128, 256, 22)
+    wid = rb.pack_q8_0_blocks(orc.q8_0_to_blocks(codes, scales), 128, 256)
+    y_host = rb.matmul_host(a, wid)
+    y_dev = rb.matmul(torch.from_numpy(a).cuda(), wid).cpu().numpy()
+    assert np.array_equal(y_host, y_dev)
+
+
+def test_q8_0_gemm_rejects_bad_k(rb, orc):
+    import torch
+    w, codes, scales = q8_weight(orc, 32, 64, 1)
+    wid = rb.pack_q8_0_blocks(orc.q8_0_to_blocks(codes, scales), 32, 64)
+    with pytest.raises(rb.OpFailure) as ei:
+        rb.matmul(torch.zeros(4, 96, device="cuda"), wid)
+    assert ei.value.error.rc == -1
+
+
+# ------------------------------------------------------------------ W8A8
+def _w8a8_case(rb, orc, m, n, k, seed, in_scale=0.0, out_scale=0.0):
+    import torch
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    codes, ws = orc.quantize_weight_per_channel(w)
+    wid = rb.pack_qat(codes, ws, n, k, in_scale, out_scale)
+    xd = torch.from_numpy(x).cuda()
+    return x, codes, ws, wid, xd
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 32, 32), (7, 100, 64), (300, 3456, 1152), (2394, 1152, 1152),
+                                   (257, 1152, 4304), (129, 4304, 1152)])
+def test_w8a8_bit_exact(rb, orc, m, n, k):
+    import torch
+    x, codes, ws, wid, xd = _w8a8_case(rb, orc, m, n, k, seed=m * 3 + n + k)
+    # per-row activation quantiser (ext.rs:1263-1279)
+    qd, sd = rb.quantize_rows_i8(xd)
+    q, s = orc.quantize_rows_i8(x)
+    assert np.array_equal(qd.cpu().numpy(), q)
+    assert np.array_equal(sd.cpu().numpy().view(np.uint32), s.view(np.uint32))
+    # exact int32 accumulators
+    acc = rb.matmul_i8_acc(qd, wid).cpu().numpy()
+    assert np.array_equal(acc, orc.gemm_i8(q, codes))
+    # full op, f32 epilogue bit for bit
+    y = rb.matmul(xd, wid).cpu().numpy()
+    want = orc.w8a8_matmul(x, codes, ws)
+    assert np.array_equal(y.view(np.uint32), want.view(np.uint32))
+    torch.cuda.synchronize()
+    rb.check_device_errors()
+
+
+def test_w8a8_static_scales(rb, orc):
+    """pack_qat with calibrated in/out scales (ext.rs:1256-1262, 1356-1360)."""
+    x, codes, ws, wid, xd = _w8a8_case(rb, orc, 64, 96, 128, seed=9, in_scale=0.03, out_scale=0.05)
+    y = rb.matmul(xd, wid).cpu().numpy()
+    want = orc.w8a8_matmul(x, codes, ws, 0.03, 0.05)
+    assert np.array_equal(y.view(np.uint32), want.view(np.uint32))
+
+
+def test_w8a8_f16_output(rb, orc):
+    import torch
+    x, codes, ws, wid, xd = _w8a8_case(rb, orc, 50, 160, 256, seed=10)
+    y = rb.matmul(xd, wid, out_dtype=torch.float16).cpu().numpy()
+    want = orc.w8a8_matmul(x, codes, ws)
+    assert np.array_equal(y.view(np.uint16), orc.f32_to_f16_bits(want))
