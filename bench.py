@@ -31,7 +31,6 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -69,59 +68,66 @@ def profile_traffic(name):
 
 # ----------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+    """Samples SM clocks and throttle reasons (NVML, the counters nvidia-smi
+    reports) every few milliseconds while the timed region runs."""
 
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4}
 
-    def __init__(self, gpu_index):
-        self.gpu = gpu_index
-        self.proc = None
-        self.lines = []
+    def __init__(self, torch_device_index, period_s=0.005):
+        self.idx = torch_device_index
+        self.period = period_s
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self.handle = None
+
+    def _open(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        try:
+            p = torch.cuda.get_device_properties(self.idx)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            return pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+        except Exception:
+            return pynvml.nvmlDeviceGetHandleByIndex(self.idx)
+
+    def _run(self):
+        import pynvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(pynvml.nvmlDeviceGetClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+                r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                for name, bit in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+            self.handle = self._open()
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            self.t = threading.Thread(target=self._run, daemon=True)
             self.t.start()
-        except (OSError, FileNotFoundError):
-            self.proc = None
+        except Exception:
+            self.handle = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *a):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        self._stop.set()
+        if self.handle is not None:
+            self.t.join(timeout=2)
 
     def summary(self):
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [x.strip() for x in ln.split(",")]
-            if len(parts) < 7:
-                continue
-            try:
-                sm.append(float(parts[0]))
-                mx.append(float(parts[1]))
-            except ValueError:
-                continue
-            for nm, val in zip(names, parts[3:7]):
-                if val.lower() == "active":
-                    reasons.add(nm)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
 # ----------------------------------------------------------------------------- workloads
@@ -171,12 +177,10 @@ class AttnWorkload:
         self.hv = self.v.cpu().pin_memory()
         self.hout = torch.empty_like(self.hq).pin_memory()
 
-    def step(self, stream):
+    def step(self):
         rb = self.rb
-        rb.attention(self.q, self.k, self.v, self.H, self.KV, self.D, self.scale, None, True, out=self.out_c,
-                     stream=stream)
-        rb.attention(self.q, self.k, self.v, self.H, self.KV, self.D, self.scale, None, False, out=self.out_b,
-                     stream=stream)
+        rb.attention(self.q, self.k, self.v, self.H, self.KV, self.D, self.scale, None, True, out=self.out_c)
+        rb.attention(self.q, self.k, self.v, self.H, self.KV, self.D, self.scale, None, False, out=self.out_b)
 
     def kernel_launches(self):
         return [("attn_kernel causal", self.flops_c), ("attn_kernel bidirectional", self.flops_b)]
@@ -231,8 +235,8 @@ class Q8GemmWorkload:
         self.hy = torch.empty(self.M, self.N, dtype=torch.float32).pin_memory()
         del orc
 
-    def step(self, stream):
-        self.rb.matmul(self.x, self.wid, out=self.y, stream=stream)
+    def step(self):
+        self.rb.matmul(self.x, self.wid, out=self.y)
 
     def kernel_launches(self):
         return [("q8_0 gemm (+ f32->f16 cast)", self.flops)]
@@ -283,9 +287,9 @@ class W8A8Workload:
         self.hx = [x.cpu().pin_memory() for x in self.xs]
         self.hy = [y.cpu().pin_memory() for y in self.ys]
 
-    def step(self, stream):
+    def step(self):
         for w, x, y in zip(self.ws, self.xs, self.ys):
-            self.rb.matmul(x, w, out=y, stream=stream)
+            self.rb.matmul(x, w, out=y)
 
     def kernel_launches(self):
         return [(f"w8a8 gemm N={n} K={k} (+ row quantiser)", 2.0 * self.M * n * k) for n, k in self.SHAPES]
@@ -348,7 +352,7 @@ def run_b200(args):
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
 
     for _ in range(args.warmup):
-        wl.step(stream)
+        wl.step()
     torch.cuda.synchronize()
     rb.check_device_errors()
 
@@ -357,18 +361,32 @@ def run_b200(args):
             dist.barrier()
         torch.cuda.synchronize()
 
+    # One step = the workload's C-ABI calls, captured once into a CUDA graph so
+    # host-side Python/ctypes overhead stays out of the device timing.
+    graph = None
+    rb.launch_count(reset=True)
+    if not args.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+            wl.step()
+        per_step = rb.launch_count(reset=True)
+        graph.replay()
+        torch.cuda.synchronize()
+        rb.check_device_errors()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    rb.launch_count(reset=True)
     barrier()
     with ClockSampler(local) as clocks:
         for i in range(args.steps):
             flush.zero_()  # L2 flush between timed steps (outside the events)
             starts[i].record(stream)
-            wl.step(stream)
+            if graph is not None:
+                graph.replay()
+            else:
+                wl.step()
             ends[i].record(stream)
         barrier()
-    launches = rb.launch_count()
+    launches = per_step * args.steps if graph is not None else rb.launch_count()
     ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
     rb.check_device_errors()
     t = torch.tensor([ms], dtype=torch.float64, device=dev)
@@ -415,6 +433,7 @@ def run_b200(args):
         "e2e": {"value": round(e2e_value, 3), "unit": wl.unit, "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h)},
         "gpu_launches": int(launches),
+        "timing": "CUDA-graph replay of the step's C-ABI calls" if graph is not None else "eager launches",
         "clocks": clocks.summary(),
     }
     if world > 1:
@@ -464,14 +483,17 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (default: per workload, ~0.1-1 s)")
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="attn", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying a CUDA graph")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.steps is None:
+        args.steps = {"attn": 200, "q8gemm": 2000, "w8a8": 60}.get(args.workload, 20)
     if args.impl == "reference":
         run_reference(args)
     else:

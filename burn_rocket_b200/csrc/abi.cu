@@ -67,8 +67,9 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t ro
   if ((row_stride_elems * elem_bytes) % 16 != 0)
     return fail(RB_E_SHAPE, "row stride %llu elements is not a multiple of 16 bytes",
                 (unsigned long long)row_stride_elems);
-  CUtensorMapDataType dt = elem_bytes == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
-                                           : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+  CUtensorMapDataType dt = elem_bytes == 1   ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                           : elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16
+                                             : CU_TENSOR_MAP_DATA_TYPE_UINT32;
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {row_stride_elems * elem_bytes};
   cuuint32_t box[2] = {box_cols, box_rows};
@@ -83,16 +84,59 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t ro
   return RB_OK;
 }
 
+int bn_index(int bn) {
+  switch (bn) {
+    case 256: return 0;
+    case 128: return 1;
+    case 96: return 2;
+    case 64: return 3;
+    default: return -1;
+  }
+}
+
 // ------------------------------------------------------------------ engine
 struct Weight {
   int kind = 0;
   int64_t n = 0, k = 0;
   int8_t* codes = nullptr;   // [n, k]
-  void* scales = nullptr;    // Q8_0: f16 [n, k/32]; W8A8: f32 [n]
+  void* scales = nullptr;    // Q8_0: f16 [k/32, pitch]; W8A8: f32 [n]
+  int64_t pitch = 0;         // Q8_0 scale row pitch: round_up(n, 8)
   float in_scale = 0.0f, out_scale = 0.0f;
-  CUtensorMap tmap_b[2]{};   // W8A8: TMA maps of the codes, box rows 256 / 128
+  // TMA maps per N tile ({256, 128, 96, 64}, see bn_index): the codes
+  // (Q8_0: box 64 x bn; W8A8: box 128 x bn, 128-B swizzle) and the Q8_0
+  // scales (box bn x 2).
+  CUtensorMap tm_codes[4]{};
+  CUtensorMap tm_scales[4]{};
   size_t bytes = 0;
 };
+
+// Builds the per-N-tile TMA maps of a packed weight.
+static int weight_maps(Weight& w) {
+  static const int bns[4] = {256, 128, 96, 64};
+  for (int i = 0; i < 4; ++i) {
+    const int bn = bns[i];
+    int rc;
+    if (w.kind == RB_WEIGHT_Q8_0) {
+      if ((rc = make_tmap_2d(&w.tm_codes[i], w.codes, 1, w.n, w.k, w.k, 64, bn, false)) != RB_OK) return rc;
+      if ((rc = make_tmap_2d(&w.tm_scales[i], w.scales, 2, w.k / 32, w.n, w.pitch, bn, 2, false)) != RB_OK)
+        return rc;
+    } else if (i < 2) {
+      if ((rc = make_tmap_2d(&w.tm_codes[i], w.codes, 1, w.n, w.k, w.k, 128, bn, true)) != RB_OK) return rc;
+    }
+  }
+  return RB_OK;
+}
+
+// Output map for the TMA-store epilogue, or false when the output pitch or
+// base alignment rules it out (the kernel then stores directly).
+static bool output_map(CUtensorMap* map, void* y, int y_dtype, int64_t m, int64_t n) {
+  const int eb = (y_dtype == RB_DTYPE_F16 || y_dtype == RB_DTYPE_BF16) ? 2 : 4;
+  if ((reinterpret_cast<uintptr_t>(y) & 15) != 0 || (n * eb) % 16 != 0) return false;
+  const std::string saved = g_last_error;
+  const bool ok = make_tmap_2d(map, y, eb, m, n, n, 128 / eb, 32, true) == RB_OK;
+  g_last_error = saved;
+  return ok;
+}
 
 struct Scratch {
   void* ptr = nullptr;
@@ -180,11 +224,14 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
       g_launches++;
       a = e->act.ptr;
     }
-    CUtensorMap tmA;
+    CUtensorMap tmA, tmC;
     if ((rc = make_tmap_2d(&tmA, a, 2, m, k, k, 64, 128, true)) != RB_OK) return rc;
-    L.w_codes = w.codes;
-    L.w_scales = w.scales;
-    if ((rc = launch_q8_gemm(tmA, L, st)) != RB_OK) return fail(rc, "q8_0 gemm launch failed");
+    const bool tstore = output_map(&tmC, y, y_dtype, m, w.n);
+    const int bn = gemm_pick_bn(false, L.M, L.N, e->num_sms);
+    const int bi = bn_index(bn);
+    if ((rc = launch_q8_gemm(L, bn, tmA, w.tm_codes[bi], w.tm_scales[bi], tstore ? &tmC : nullptr,
+                             st)) != RB_OK)
+      return fail(rc, "q8_0 gemm launch failed");
     g_launches++;
     return RB_OK;
   }
@@ -197,12 +244,14 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
     if ((rc = launch_quantize_rows_i8(x, x_dtype, m, k, w.in_scale, codes, rs, st)) != RB_OK)
       return fail(rc, "row quantiser launch failed");
     g_launches++;
-    CUtensorMap tmA;
+    CUtensorMap tmA, tmC;
     if ((rc = make_tmap_2d(&tmA, codes, 1, m, k, k, 128, 128, true)) != RB_OK) return rc;
     L.s_row = rs;
     L.s_col = reinterpret_cast<const float*>(w.scales);
     L.out_scale = w.out_scale;
-    if ((rc = launch_w8a8_gemm(tmA, w.tmap_b[0], w.tmap_b[1], L, st)) != RB_OK)
+    const bool tstore = output_map(&tmC, y, y_dtype, m, w.n);
+    const int bn = gemm_pick_bn(true, L.M, L.N, e->num_sms);
+    if ((rc = launch_w8a8_gemm(L, bn, tmA, w.tm_codes[bn_index(bn)], tstore ? &tmC : nullptr, st)) != RB_OK)
       return fail(rc, "w8a8 gemm launch failed");
     g_launches++;
     return RB_OK;
@@ -270,8 +319,9 @@ static int attention_locked(Engine* e, const void* q, const void* k, const void*
   const uint64_t ldq = static_cast<uint64_t>(n_head) * head_dim;
   const uint64_t ldk = static_cast<uint64_t>(n_kv_heads) * head_dim;
   if ((rc = make_tmap_2d(&tq, qh, 2, n_q, ldq, ldq, 64, 128, true)) != RB_OK) return rc;
-  if ((rc = make_tmap_2d(&tk, kh, 2, n_kv, ldk, ldk, 64, 128, true)) != RB_OK) return rc;
-  if ((rc = make_tmap_2d(&tv, vh, 2, n_kv, ldk, ldk, 64, 128, true)) != RB_OK) return rc;
+  // Q tiles are 128 query rows, K/V tiles 64 keys; 64-element (128-B) columns.
+  if ((rc = make_tmap_2d(&tk, kh, 2, n_kv, ldk, ldk, 64, 64, true)) != RB_OK) return rc;
+  if ((rc = make_tmap_2d(&tv, vh, 2, n_kv, ldk, ldk, 64, 64, true)) != RB_OK) return rc;
   if ((reinterpret_cast<uintptr_t>(oh) & 15) != 0)
     return fail(RB_E_SHAPE, "attention output must be 16-byte aligned");
   AttnLaunch L{};
@@ -377,23 +427,27 @@ int64_t rb_pack_q8_0(const void* blocks_host, int64_t n, int64_t k) {
   w.kind = RB_WEIGHT_Q8_0;
   w.n = n;
   w.k = k;
+  w.pitch = (n + 7) & ~int64_t(7);
+  const size_t sbytes = static_cast<size_t>(w.pitch) * (k / 32) * 2;
   uint8_t* dblk = nullptr;
   if (cudaMalloc(&dblk, nblk * 34) != cudaSuccess ||
       cudaMalloc(&w.codes, static_cast<size_t>(n) * k) != cudaSuccess ||
-      cudaMalloc(&w.scales, nblk * 2) != cudaSuccess) {
+      cudaMalloc(&w.scales, sbytes) != cudaSuccess) {
     cudaGetLastError();
     if (dblk) cudaFree(dblk);
     if (w.codes) cudaFree(w.codes);
     return fail(RB_E_NOMEM, "Q8_0 pack: device allocation failed");
   }
   RB_CUDA(cudaMemcpy(dblk, blocks_host, nblk * 34, cudaMemcpyHostToDevice), "Q8_0 upload");
-  if ((rc = launch_q8_0_unpack_blocks(dblk, n, k, w.codes, reinterpret_cast<uint16_t*>(w.scales),
+  cudaMemset(w.scales, 0, sbytes);
+  if ((rc = launch_q8_0_unpack_blocks(dblk, n, k, w.pitch, w.codes, reinterpret_cast<uint16_t*>(w.scales),
                                       nullptr)) != RB_OK)
     return fail(rc, "Q8_0 unpack launch failed");
   g_launches++;
   RB_CUDA(cudaDeviceSynchronize(), "Q8_0 unpack");
   cudaFree(dblk);
-  w.bytes = static_cast<size_t>(n) * k + nblk * 2;
+  w.bytes = static_cast<size_t>(n) * k + sbytes;
+  if ((rc = weight_maps(w)) != RB_OK) return rc;
   const int64_t id = e->next_id++;
   e->weights[id] = w;
   return id;
@@ -417,10 +471,12 @@ int64_t rb_pack_f32_q8_0(const float* const* parts_host, const int64_t* n_parts,
   w.kind = RB_WEIGHT_Q8_0;
   w.n = n;
   w.k = k;
+  w.pitch = (n + 7) & ~int64_t(7);
+  const size_t sbytes = static_cast<size_t>(w.pitch) * (k / 32) * 2;
   float* dw = nullptr;
   if (cudaMalloc(&dw, static_cast<size_t>(n) * k * 4) != cudaSuccess ||
       cudaMalloc(&w.codes, static_cast<size_t>(n) * k) != cudaSuccess ||
-      cudaMalloc(&w.scales, static_cast<size_t>(n) * (k / 32) * 2) != cudaSuccess) {
+      cudaMalloc(&w.scales, sbytes) != cudaSuccess) {
     cudaGetLastError();
     if (dw) cudaFree(dw);
     if (w.codes) cudaFree(w.codes);
@@ -432,12 +488,14 @@ int64_t rb_pack_f32_q8_0(const float* const* parts_host, const int64_t* n_parts,
                        cudaMemcpyHostToDevice), "weight upload");
     off += n_parts[i];
   }
-  if ((rc = launch_q8_0_encode(dw, n, k, w.codes, reinterpret_cast<uint16_t*>(w.scales), nullptr)) != RB_OK)
+  cudaMemset(w.scales, 0, sbytes);
+  if ((rc = launch_q8_0_encode(dw, n, k, w.pitch, w.codes, reinterpret_cast<uint16_t*>(w.scales), nullptr)) != RB_OK)
     return fail(rc, "Q8_0 encode launch failed");
   g_launches++;
   RB_CUDA(cudaDeviceSynchronize(), "Q8_0 encode");
   cudaFree(dw);
-  w.bytes = static_cast<size_t>(n) * k + static_cast<size_t>(n) * (k / 32) * 2;
+  w.bytes = static_cast<size_t>(n) * k + sbytes;
+  if ((rc = weight_maps(w)) != RB_OK) return rc;
   const int64_t id = e->next_id++;
   e->weights[id] = w;
   return id;
@@ -471,9 +529,7 @@ int64_t rb_pack_w8a8(const int8_t* codes_host, const float* w_scale_host, int64_
   }
   RB_CUDA(cudaMemcpy(w.codes, codes_host, static_cast<size_t>(n) * k, cudaMemcpyHostToDevice), "codes upload");
   RB_CUDA(cudaMemcpy(w.scales, w_scale_host, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice), "scale upload");
-  // TMA maps of the codes for the two N tile heights the int8 GEMM uses.
-  if ((rc = make_tmap_2d(&w.tmap_b[0], w.codes, 1, n, k, k, 128, 256, true)) != RB_OK) return rc;
-  if ((rc = make_tmap_2d(&w.tmap_b[1], w.codes, 1, n, k, k, 128, 128, true)) != RB_OK) return rc;
+  if ((rc = weight_maps(w)) != RB_OK) return rc;
   w.bytes = static_cast<size_t>(n) * k + static_cast<size_t>(n) * 4;
   const int64_t id = e->next_id++;
   e->weights[id] = w;
@@ -580,7 +636,8 @@ int rb_q8_0_dequant(int64_t id, void* out, int out_dtype, void* stream) {
     return fail(RB_E_SHAPE, "weight id %lld is not a Q8_0 weight", (long long)id);
   if (out_dtype != RB_DTYPE_F32 && out_dtype != RB_DTYPE_F16) return fail(RB_E_SHAPE, "dequant dtype");
   const Weight& w = it->second;
-  rc = launch_q8_dequant(w.codes, w.scales, static_cast<int>(w.n), static_cast<int>(w.k), out,
+  rc = launch_q8_dequant(w.codes, w.scales, static_cast<int>(w.n), static_cast<int>(w.k),
+                         static_cast<int>(w.pitch), out,
                          out_dtype == RB_DTYPE_F16, reinterpret_cast<cudaStream_t>(stream));
   g_launches++;
   return rc == RB_OK ? RB_OK : fail(rc, "dequant launch failed");
@@ -609,7 +666,7 @@ int rb_matmul_i8_acc(int64_t id, const int8_t* codes, int64_t m, int32_t* acc, v
     return fail(RB_E_SHAPE, "weight id %lld is not a W8A8 weight", (long long)id);
   const Weight& w = it->second;
   if (m <= 0 || !codes || !acc) return fail(RB_E_SHAPE, "bad int8 matmul arguments");
-  CUtensorMap tmA;
+  CUtensorMap tmA, tmC;
   if ((rc = make_tmap_2d(&tmA, codes, 1, m, w.k, w.k, 128, 128, true)) != RB_OK) return rc;
   GemmLaunch L{};
   L.M = static_cast<int>(m);
@@ -621,7 +678,10 @@ int rb_matmul_i8_acc(int64_t id, const int8_t* codes, int64_t m, int32_t* acc, v
   L.err = e->err;
   L.num_sms = e->num_sms;
   L.s_col = reinterpret_cast<const float*>(w.scales);
-  rc = launch_w8a8_gemm(tmA, w.tmap_b[0], w.tmap_b[1], L, reinterpret_cast<cudaStream_t>(stream));
+  const bool tstore = output_map(&tmC, acc, RB_DTYPE_I32, m, w.n);
+  const int bn = gemm_pick_bn(true, L.M, L.N, e->num_sms);
+  rc = launch_w8a8_gemm(L, bn, tmA, w.tm_codes[bn_index(bn)], tstore ? &tmC : nullptr,
+                        reinterpret_cast<cudaStream_t>(stream));
   g_launches++;
   return rc == RB_OK ? RB_OK : fail(rc, "int8 gemm launch failed");
 }

@@ -9,24 +9,29 @@
 // so a fully masked row averages the values of every key it iterates, as the
 // reference does.
 //
-// Design (one CTA = two 128-row query "slots" of the same KV head):
+// Design (one CTA = two 128-row query "slots" sharing one KV head):
 //   * GQA: the two slots are two query heads of one KV group (or two query
 //     tiles of one head when the group has a single head), so every K/V tile
 //     is loaded by TMA once and consumed by both slots.
-//   * warp 0: TMA (Q once, then a 2-stage K and V ring; 128-B swizzled tiles);
-//     warp 1: UMMA issuer; warps 4-7 / 8-11: softmax for slot 0 / slot 1, one
-//     query row per thread (TMEM lane = row).
-//   * TMEM per slot: S = Q·K^T in 128 f32 columns; P = exp(S - m) is written
-//     back as packed f16/bf16 over the first 64 of those columns and consumed
-//     by a TS-form UMMA (A from TMEM) O += P·V into D more f32 columns.
-//   * Online softmax in the log2 domain with a lazy rescale: the running max
-//     used for the exponent only moves (and O/l are rescaled) when a new row
-//     max exceeds it by more than 8 (a factor 256), so P stays within f16 range
-//     and O is rarely touched by the softmax warps.
-//   * Causal / window / block masks: tiles wholly outside a slot's visible key
+//   * warp 0: TMA (Q once, then 4-stage K and V rings of 64-key tiles, 128-B
+//     swizzled); warp 1: UMMA issuer; warps 4-7 / 8-11: softmax of slot 0 /
+//     slot 1, one query row per thread (TMEM lane = row).
+//   * TMEM per slot (256 columns): two S buffers of 64 f32 columns and O in D
+//     columns. S(j+1) is computed into the other buffer while the softmax of
+//     tile j runs; P = exp2(S - m) is written back as packed f16/bf16 over the
+//     first 32 columns of its own S buffer and consumed by a TS-form UMMA
+//     (A from TMEM) O += P·V. The UMMA warp issues S(j+1) before P·V(j).
+//   * Online softmax in the log2 domain with a lazy rescale: the exponent base
+//     only moves (and O, l are rescaled) when a new row max exceeds it by more
+//     than 8 (a factor 256), so P stays within f16 range and O is rarely
+//     touched by the softmax warps.
+//   * The -30000 clamp is exact: once a row's exponent base lies 160 above the
+//     clamp (any row with a visible key scoring above ~-29900), every clamped
+//     or masked key underflows to 0 either way, and the warp takes the fast
+//     path (one FFMA + one MUFU ex2 per score).
+//   * Causal / window / block masks: key tiles wholly outside a slot's visible
 //     band are skipped; tiles wholly inside skip the predicate; a slot that
-//     may contain a fully masked row iterates every key tile (reference
-//     semantics above).
+//     may contain a fully masked row iterates every key tile.
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -40,13 +45,15 @@ namespace rb {
 namespace attn {
 
 constexpr int BM = 128;      // query rows per slot
-constexpr int BN = 128;      // keys per tile
-constexpr int KV_STAGES = 2;
+constexpr int BN = 64;       // keys per tile
+constexpr int KV_STAGES = 4;
 constexpr int kSoftWarp0 = 4;
 constexpr int kThreads = 12 * 32;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kClamp = -30000.0f;   // fa_score clamp (oneshot.rs PAD_KEY_SCORE)
+constexpr float kClamp2 = kClamp * kLog2e;
 constexpr float kRescaleThresh = 8.0f;  // log2 units
+constexpr float kFastMargin = 160.0f;   // exp2(-160) underflows f32 to 0
 constexpr int kNoBound = 1 << 30;
 
 struct Params {
@@ -66,18 +73,27 @@ struct Params {
 template <int D>
 struct Smem {
   static constexpr int ATOMS = D / 64;              // 64-element (128-B) column atoms
-  static constexpr int TILE = 128 * 128 * ATOMS;    // bytes of one 128-row tile
+  static constexpr int Q_ATOM = BM * 128;           // 16 KB
+  static constexpr int KV_ATOM = BN * 128;          // 8 KB
+  static constexpr int Q_TILE = ATOMS * Q_ATOM;
+  static constexpr int KV_TILE = ATOMS * KV_ATOM;
   static constexpr int Q_OFF = 0;                   // 2 slots
-  static constexpr int K_OFF = 2 * TILE;            // KV_STAGES
-  static constexpr int V_OFF = K_OFF + KV_STAGES * TILE;
-  static constexpr int BAR_OFF = V_OFF + KV_STAGES * TILE;
-  static constexpr int BYTES = BAR_OFF + 256 + 1024;
+  static constexpr int K_OFF = 2 * Q_TILE;
+  static constexpr int V_OFF = K_OFF + KV_STAGES * KV_TILE;
+  static constexpr int BAR_OFF = V_OFF + KV_STAGES * KV_TILE;
+  static constexpr int BYTES = BAR_OFF + 512 + 1024;
 };
 
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 template <bool BF16>
@@ -107,10 +123,10 @@ __device__ __forceinline__ SlotInfo slot_info(const Params& p, int g, int item) 
   const int qa0 = p.q_off + s.qt * BM;
   const int qa1 = p.q_off + min(s.qt * BM + BM, p.n_q) - 1;
   // Visible absolute keys of row qa: [qa + dlo, qa + dhi] ∩ [k_off, k_off + n_kv).
-  const int klast = p.k_off + p.n_kv - 1;
+  const long klast = static_cast<long>(p.k_off) + p.n_kv - 1;
   auto row_empty = [&](int qa) {
     const long lo = (p.dlo <= -kNoBound) ? p.k_off : max(static_cast<long>(p.k_off), static_cast<long>(qa) + p.dlo);
-    const long hi = (p.dhi >= kNoBound) ? klast : min(static_cast<long>(klast), static_cast<long>(qa) + p.dhi);
+    const long hi = (p.dhi >= kNoBound) ? klast : min(klast, static_cast<long>(qa) + p.dhi);
     return lo > hi;
   };
   if (row_empty(qa0) || row_empty(qa1)) {
@@ -126,7 +142,7 @@ __device__ __forceinline__ SlotInfo slot_info(const Params& p, int g, int item) 
   return s;
 }
 
-template <int D, bool BF16>
+template <int D, bool BF16, bool SOFTCAP>
 __global__ void __launch_bounds__(kThreads, 1)
 attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
             const __grid_constant__ CUtensorMap tmV, Params p) {
@@ -135,15 +151,16 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
-  uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;   // [2]
-  uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // [2 slots]
-  uint64_t* p_full = bars + 11;  // [2 slots]
-  uint64_t* o_done = bars + 13;  // [2 slots]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+  uint64_t* q_full = bars;                      // [1]
+  uint64_t* k_full = bars + 1;                  // [KV_STAGES]
+  uint64_t* k_empty = k_full + KV_STAGES;       // [KV_STAGES]
+  uint64_t* v_full = k_empty + KV_STAGES;       // [KV_STAGES]
+  uint64_t* v_empty = v_full + KV_STAGES;       // [KV_STAGES]
+  uint64_t* s_full = v_empty + KV_STAGES;       // [slot][buf]
+  uint64_t* s_free = s_full + 4;                // [slot][buf]
+  uint64_t* p_full = s_free + 4;                // [slot][buf]
+  uint64_t* o_done = p_full + 4;                // [slot]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -155,21 +172,25 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   SlotInfo sl[2];
   sl[0] = slot_info(p, g, 2 * pair);
   sl[1] = slot_info(p, g, 2 * pair + 1);
-  const bool act0 = sl[0].lo <= sl[0].hi, act1 = sl[1].lo <= sl[1].hi;
+  const bool act1 = sl[1].lo <= sl[1].hi;
   const int J0 = act1 ? min(sl[0].lo, sl[1].lo) : sl[0].lo;
   const int J1 = act1 ? max(sl[0].hi, sl[1].hi) : sl[0].hi;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < KV_STAGES; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 4);
-      mbar_init(&o_done[i], 1);
     }
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 1);
+      mbar_init(&p_full[i], 4);
+    }
+    mbar_init(&o_done[0], 1);
+    mbar_init(&o_done[1], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -189,23 +210,23 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
       const int nslots = act1 ? 2 : 1;
-      mbar_arrive_expect_tx(q_full, nslots * L::TILE);
+      mbar_arrive_expect_tx(q_full, nslots * L::Q_TILE);
       for (int s = 0; s < nslots; ++s)
         for (int a = 0; a < L::ATOMS; ++a)
-          tma_load_2d(smem + L::Q_OFF + s * L::TILE + a * 16384, &tmQ, q_full,
+          tma_load_2d(smem + L::Q_OFF + s * L::Q_TILE + a * L::Q_ATOM, &tmQ, q_full,
                       sl[s].head * D + a * 64, sl[s].qt * BM);
       for (int j = J0; j <= J1; ++j) {
-        const int jl = j - J0, st = jl & 1;
-        const uint32_t ph = ((jl >> 1) & 1) ^ 1;
+        const int jl = j - J0, st = jl % KV_STAGES;
+        const uint32_t ph = ((jl / KV_STAGES) & 1) ^ 1;
         if (!mbar_wait(&k_empty[st], ph, p.err, abort_flag)) break;
-        mbar_arrive_expect_tx(&k_full[st], L::TILE);
+        mbar_arrive_expect_tx(&k_full[st], L::KV_TILE);
         for (int a = 0; a < L::ATOMS; ++a)
-          tma_load_2d(smem + L::K_OFF + st * L::TILE + a * 16384, &tmK, &k_full[st],
+          tma_load_2d(smem + L::K_OFF + st * L::KV_TILE + a * L::KV_ATOM, &tmK, &k_full[st],
                       g * D + a * 64, j * BN);
         if (!mbar_wait(&v_empty[st], ph, p.err, abort_flag)) break;
-        mbar_arrive_expect_tx(&v_full[st], L::TILE);
+        mbar_arrive_expect_tx(&v_full[st], L::KV_TILE);
         for (int a = 0; a < L::ATOMS; ++a)
-          tma_load_2d(smem + L::V_OFF + st * L::TILE + a * 16384, &tmV, &v_full[st],
+          tma_load_2d(smem + L::V_OFF + st * L::KV_TILE + a * L::KV_ATOM, &tmV, &v_full[st],
                       g * D + a * 64, j * BN);
       }
     }
@@ -217,51 +238,64 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       const uint32_t q_addr = smem_u32(smem + L::Q_OFF);
       const uint32_t k_addr = smem_u32(smem + L::K_OFF);
       const uint32_t v_addr = smem_u32(smem + L::V_OFF);
-      int n_pv[2] = {0, 0};
-      int n_s[2] = {0, 0};
-      if (!mbar_wait(q_full, 0, p.err, abort_flag)) goto mma_done;
-      for (int j = J0; j <= J1; ++j) {
-        const int jl = j - J0, st = jl & 1;
-        const uint32_t ph = (jl >> 1) & 1;
-        if (!mbar_wait(&k_full[st], ph, p.err, abort_flag)) goto mma_done;
+      int n_s[2] = {0, 0};   // S tiles issued per slot
+      int n_pv[2] = {0, 0};  // P·V issued per slot
+      bool ok = mbar_wait(q_full, 0, p.err, abort_flag);
+      // S = Q K_j^T for every slot that sees tile j, into its next S buffer.
+      auto issue_s = [&](int j) -> bool {
+        const int jl = j - J0, st = jl % KV_STAGES;
+        if (!mbar_wait(&k_full[st], (jl / KV_STAGES) & 1, p.err, abort_flag)) return false;
         tc_fence_after();
         for (int s = 0; s < 2; ++s) {
           if (!(sl[s].lo <= j && j <= sl[s].hi)) continue;
-          // S/P region of this slot is free once its previous P·V retired.
-          if (n_pv[s] > 0) {
-            if (!mbar_wait(&o_done[s], (n_pv[s] - 1) & 1, p.err, abort_flag)) goto mma_done;
+          const int b = n_s[s] & 1;
+          if (n_s[s] >= 2) {  // the P·V that read this buffer two tiles ago has retired
+            if (!mbar_wait(&s_free[2 * s + b], ((n_s[s] >> 1) - 1) & 1, p.err, abort_flag)) return false;
             tc_fence_after();
           }
-          const uint32_t d_tmem = tmem_base + s * 256;
+          const uint32_t d_tmem = tmem_base + s * 256 + b * 64;
 #pragma unroll
           for (int ks = 0; ks < D / 16; ++ks) {
-            const uint32_t off = (ks >> 2) * 16384 + (ks & 3) * 32;
-            umma_f16_ss(d_tmem, desc_kmajor_sw128(q_addr + s * L::TILE + off),
-                        desc_kmajor_sw128(k_addr + st * L::TILE + off), idesc_s, ks > 0);
+            const uint32_t qo = (ks >> 2) * L::Q_ATOM + (ks & 3) * 32;
+            const uint32_t ko = (ks >> 2) * L::KV_ATOM + (ks & 3) * 32;
+            umma_f16_ss(d_tmem, desc_kmajor_sw128(q_addr + s * L::Q_TILE + qo),
+                        desc_kmajor_sw128(k_addr + st * L::KV_TILE + ko), idesc_s, ks > 0);
           }
-          umma_commit(&s_full[s]);
+          umma_commit(&s_full[2 * s + b]);
           ++n_s[s];
         }
         umma_commit(&k_empty[st]);
-        if (!mbar_wait(&v_full[st], ph, p.err, abort_flag)) goto mma_done;
+        return true;
+      };
+      // O += P_j V_j for every slot that sees tile j.
+      auto issue_pv = [&](int j) -> bool {
+        const int jl = j - J0, st = jl % KV_STAGES;
+        if (!mbar_wait(&v_full[st], (jl / KV_STAGES) & 1, p.err, abort_flag)) return false;
         tc_fence_after();
         for (int s = 0; s < 2; ++s) {
           if (!(sl[s].lo <= j && j <= sl[s].hi)) continue;
-          if (!mbar_wait(&p_full[s], (n_s[s] - 1) & 1, p.err, abort_flag)) goto mma_done;
+          const int b = n_pv[s] & 1;
+          if (!mbar_wait(&p_full[2 * s + b], (n_pv[s] >> 1) & 1, p.err, abort_flag)) return false;
           tc_fence_after();
           const uint32_t o_tmem = tmem_base + s * 256 + 128;
-          const uint32_t p_tmem = tmem_base + s * 256;
+          const uint32_t p_tmem = tmem_base + s * 256 + b * 64;
 #pragma unroll
           for (int ks = 0; ks < BN / 16; ++ks) {
-            const uint64_t vd = desc_mnmajor_sw128(v_addr + st * L::TILE + ks * 2048, 16384, 1024);
+            const uint64_t vd = desc_mnmajor_sw128(v_addr + st * L::KV_TILE + ks * 2048, L::KV_ATOM, 1024);
             umma_f16_ts(o_tmem, p_tmem + ks * 8, vd, idesc_o, (n_pv[s] > 0 || ks > 0) ? 1u : 0u);
           }
+          umma_commit(&s_free[2 * s + b]);
           umma_commit(&o_done[s]);
           ++n_pv[s];
         }
         umma_commit(&v_empty[st]);
+        return true;
+      };
+      if (ok) ok = issue_s(J0);
+      for (int j = J0; ok && j <= J1; ++j) {
+        if (j < J1) ok = issue_s(j + 1);
+        if (ok) ok = issue_pv(j);
       }
-    mma_done:;
     }
   } else if (warp >= kSoftWarp0) {
     // ------------------------------------------------------------ softmax
@@ -271,13 +305,16 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     const SlotInfo me = sl[s];
     if (me.lo <= me.hi) {
       const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
-      const uint32_t s_col = s * 256, o_col = s * 256 + 128;
+      const uint32_t o_col = s * 256 + 128;
       const int qa = p.q_off + me.qt * BM + row;  // absolute query position
+      const int qa_min = p.q_off + me.qt * BM, qa_max = qa_min + BM - 1;
       float m_used = -INFINITY, l = 0.0f;
       int it = 0;
       bool ok = true;
       for (int j = me.lo; j <= me.hi; ++j, ++it) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[s], it & 1, p.err, abort_flag))) {
+        const int b = it & 1;
+        const uint32_t s_col = s * 256 + b * 64;
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[2 * s + b], (it >> 1) & 1, p.err, abort_flag))) {
           ok = false;
           break;
         }
@@ -285,45 +322,56 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         float x[BN];
         {
           uint32_t r[32];
+          tmem_ld32(lane_base + s_col, r);
+          tmem_wait_ld();
 #pragma unroll
-          for (int c = 0; c < BN; c += 32) {
-            tmem_ld32(lane_base + s_col + c, r);
-            tmem_wait_ld();
+          for (int i = 0; i < 32; ++i) x[i] = __uint_as_float(r[i]);
+          tmem_ld32(lane_base + s_col + 32, r);
+          tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) x[c + i] = __uint_as_float(r[i]);
-          }
+          for (int i = 0; i < 32; ++i) x[32 + i] = __uint_as_float(r[i]);
         }
-        // Scores in the log2 domain, with the reference's clamp and masks.
-        const int ka0 = p.k_off + j * BN;          // absolute key of column 0
-        const int kvalid = p.n_kv - j * BN;        // real keys in this tile
-        const bool interior = (kvalid >= BN) &&
-            (p.dlo <= -kNoBound || ka0 - (p.q_off + me.qt * BM + BM - 1) >= p.dlo) &&
-            (p.dhi >= kNoBound || ka0 + BN - 1 - (p.q_off + me.qt * BM) <= p.dhi);
-        const float clamp2 = kClamp * kLog2e;
-        float mt = -INFINITY;
-        if (p.softcap != 0.0f) {
+        if (SOFTCAP) {
+          // s = softcap * tanh(s*scale / softcap), then back to "raw" units so
+          // the common scaling below applies.
 #pragma unroll
           for (int i = 0; i < BN; ++i) {
-            float v = __fmul_rn(x[i], p.scale);
-            v = p.softcap * tanhf(v / p.softcap);
-            x[i] = fmaxf(v, kClamp) * kLog2e;
+            const float v = __fmul_rn(x[i], p.scale);
+            x[i] = p.softcap * tanhf(v / p.softcap) / p.scale;
           }
-        } else {
-#pragma unroll
-          for (int i = 0; i < BN; ++i) x[i] = fmaxf(x[i] * p.scale_log2, clamp2);
         }
+        const int ka0 = p.k_off + j * BN;  // absolute key of column 0
+        const int kvalid = p.n_kv - j * BN;
+        const bool interior = (kvalid >= BN) &&
+            (p.dlo <= -kNoBound || ka0 - qa_max >= p.dlo) &&
+            (p.dhi >= kNoBound || ka0 + BN - 1 - qa_min <= p.dhi);
+        // Visibility bitmask of this row's 64 keys (all ones on interior tiles).
+        uint64_t vis = ~0ull, real = ~0ull;
         if (!interior) {
+          vis = 0;
+          real = 0;
 #pragma unroll
           for (int i = 0; i < BN; ++i) {
             const int d = ka0 + i - qa;
-            const bool vis = (p.dlo <= -kNoBound || d >= p.dlo) && (p.dhi >= kNoBound || d <= p.dhi);
-            x[i] = (i >= kvalid) ? -INFINITY : (vis ? x[i] : clamp2);
+            const bool r_ = i < kvalid;
+            const bool v_ = r_ && (p.dlo <= -kNoBound || d >= p.dlo) && (p.dhi >= kNoBound || d <= p.dhi);
+            vis |= static_cast<uint64_t>(v_) << i;
+            real |= static_cast<uint64_t>(r_) << i;
           }
         }
+        // Tile max in log2 units: max over visible of s*c, floored at the clamp
+        // (masked real keys score exactly the clamp).
+        float mraw = -INFINITY;
+        if (interior) {
 #pragma unroll
-        for (int i = 0; i < BN; ++i) mt = fmaxf(mt, x[i]);
-        // Lazy rescale: move the exponent base only when the new max exceeds
-        // it by more than the threshold (P then stays <= 2^8).
+          for (int i = 0; i < BN; i += 2) mraw = max3(mraw, x[i], x[i + 1]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < BN; ++i) mraw = fmaxf(mraw, ((vis >> i) & 1) ? x[i] : -INFINITY);
+        }
+        float mt = mraw * p.scale_log2;
+        if (real != vis || mt < kClamp2) mt = fmaxf(mt, kClamp2);
+        // Lazy rescale of the exponent base.
         float alpha = 1.0f;
         bool need = false;
         if (it == 0) {
@@ -333,42 +381,72 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
           m_used = mt;
           need = true;
         }
+        const bool fast = __all_sync(0xffffffffu, m_used >= kClamp2 + kFastMargin);
+        const float c = p.scale_log2, nm = -m_used;
+        float rowsum = 0.0f;
+        uint32_t pk[BN / 2];
+        if (fast) {
+#pragma unroll
+          for (int i = 0; i < BN; i += 2) {
+            float p0 = fast_exp2(fmaf(x[i], c, nm));
+            float p1 = fast_exp2(fmaf(x[i + 1], c, nm));
+            if (!interior) {
+              p0 = ((vis >> i) & 1) ? p0 : 0.0f;
+              p1 = ((vis >> (i + 1)) & 1) ? p1 : 0.0f;
+            }
+            rowsum += p0 + p1;
+            pk[i / 2] = pack2<BF16>(p0, p1);
+          }
+        } else {
+          // Exact path near the clamp: y = visible ? max(s*c, clamp) :
+          // (real key ? clamp : -inf).
+#pragma unroll
+          for (int i = 0; i < BN; i += 2) {
+            float y0 = fmaxf(x[i] * c, kClamp2), y1 = fmaxf(x[i + 1] * c, kClamp2);
+            if (!((vis >> i) & 1)) y0 = ((real >> i) & 1) ? kClamp2 : -INFINITY;
+            if (!((vis >> (i + 1)) & 1)) y1 = ((real >> (i + 1)) & 1) ? kClamp2 : -INFINITY;
+            const float p0 = fast_exp2(y0 + nm), p1 = fast_exp2(y1 + nm);
+            rowsum += p0 + p1;
+            pk[i / 2] = pack2<BF16>(p0, p1);
+          }
+        }
+        l = l * alpha + rowsum;
+        // The previous P·V of this slot must have retired before O is touched
+        // (and before this tile's P·V is released). Waited every tile.
+        if (it > 0) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&o_done[s], (it - 1) & 1, p.err, abort_flag))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
         if (__any_sync(0xffffffffu, need)) {
-          // P·V of the previous tile has retired (the S MMA of this tile was
-          // issued after it), so O is stable here.
           uint32_t r[32];
 #pragma unroll
-          for (int c = 0; c < D; c += 32) {
-            tmem_ld32(lane_base + o_col + c, r);
+          for (int c0 = 0; c0 < D; c0 += 32) {
+            tmem_ld32(lane_base + o_col + c0, r);
             tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
             uint32_t lo16[16], hi16[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) { lo16[i] = r[i]; hi16[i] = r[16 + i]; }
-            tmem_st16(lane_base + o_col + c, lo16);
-            tmem_st16(lane_base + o_col + c + 16, hi16);
+            for (int i = 0; i < 16; ++i) {
+              lo16[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+              hi16[i] = __float_as_uint(__uint_as_float(r[16 + i]) * alpha);
+            }
+            tmem_st16(lane_base + o_col + c0, lo16);
+            tmem_st16(lane_base + o_col + c0 + 16, hi16);
           }
-          l *= alpha;
         }
-        float rowsum = 0.0f;
+        {
+          uint32_t a16[16], b16[16];
 #pragma unroll
-        for (int c = 0; c < BN; c += 32) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float p0 = fast_exp2(x[c + 2 * i] - m_used);
-            const float p1 = fast_exp2(x[c + 2 * i + 1] - m_used);
-            rowsum += p0 + p1;
-            pk[i] = pack2<BF16>(p0, p1);
-          }
-          tmem_st16(lane_base + s_col + c / 2, pk);
+          for (int i = 0; i < 16; ++i) { a16[i] = pk[i]; b16[i] = pk[16 + i]; }
+          tmem_st16(lane_base + s_col, a16);
+          tmem_st16(lane_base + s_col + 16, b16);
         }
-        l += rowsum;
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[s]);
+        if (lane == 0) mbar_arrive(&p_full[2 * s + b]);
       }
       // Epilogue: wait for the last P·V, normalise, store.
       if (ok && __all_sync(0xffffffffu, mbar_wait(&o_done[s], (it - 1) & 1, p.err, abort_flag))) {
@@ -377,8 +455,8 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         const int qrow = me.qt * BM + row;
         uint32_t r[32];
 #pragma unroll
-        for (int c = 0; c < D; c += 32) {
-          tmem_ld32(lane_base + o_col + c, r);
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          tmem_ld32(lane_base + o_col + c0, r);
           tmem_wait_ld();
           if (qrow < p.n_q) {
             uint32_t pk[16];
@@ -388,7 +466,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
                                   __uint_as_float(r[2 * i + 1]) * inv_l);
             uint4* dst = reinterpret_cast<uint4*>(
                 reinterpret_cast<uint16_t*>(p.out) + static_cast<int64_t>(qrow) * p.ldo +
-                me.head * D + c);
+                me.head * D + c0);
 #pragma unroll
             for (int i = 0; i < 4; ++i)
               dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
@@ -407,20 +485,30 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   }
 }
 
-template <int D, bool BF16>
+template <int D, bool BF16, bool SOFTCAP>
 static int launch_impl(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
                        const Params& p, int grid, cudaStream_t stream) {
   static uint64_t configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(configured & (1ull << (dev & 63)))) {
-    if (cudaFuncSetAttribute(attn_kernel<D, BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             Smem<D>::BYTES) != cudaSuccess)
+    if (cudaFuncSetAttribute(attn_kernel<D, BF16, SOFTCAP>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, Smem<D>::BYTES) != cudaSuccess)
       return RB_E_DEVICE;
     configured |= 1ull << (dev & 63);
   }
-  attn_kernel<D, BF16><<<grid, kThreads, Smem<D>::BYTES, stream>>>(tmQ, tmK, tmV, p);
+  attn_kernel<D, BF16, SOFTCAP><<<grid, kThreads, Smem<D>::BYTES, stream>>>(tmQ, tmK, tmV, p);
   return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
+}
+
+template <int D>
+static int launch_d(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
+                    const Params& p, int grid, bool bf16, cudaStream_t stream) {
+  if (p.softcap != 0.0f)
+    return bf16 ? launch_impl<D, true, true>(tmQ, tmK, tmV, p, grid, stream)
+                : launch_impl<D, false, true>(tmQ, tmK, tmV, p, grid, stream);
+  return bf16 ? launch_impl<D, true, false>(tmQ, tmK, tmV, p, grid, stream)
+              : launch_impl<D, false, false>(tmQ, tmK, tmV, p, grid, stream);
 }
 
 }  // namespace attn
@@ -480,12 +568,8 @@ int launch_attention(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUten
   }
   const int grid = p.pairs_per_group * L.n_kv_heads;
   const bool bf16 = L.dtype == RB_DTYPE_BF16;
-  if (L.head_dim == 128)
-    return bf16 ? launch_impl<128, true>(tmQ, tmK, tmV, p, grid, stream)
-                : launch_impl<128, false>(tmQ, tmK, tmV, p, grid, stream);
-  if (L.head_dim == 64)
-    return bf16 ? launch_impl<64, true>(tmQ, tmK, tmV, p, grid, stream)
-                : launch_impl<64, false>(tmQ, tmK, tmV, p, grid, stream);
+  if (L.head_dim == 128) return launch_d<128>(tmQ, tmK, tmV, p, grid, bf16, stream);
+  if (L.head_dim == 64) return launch_d<64>(tmQ, tmK, tmV, p, grid, bf16, stream);
   return RB_E_UNSUPPORTED;
 }
 

@@ -1,23 +1,31 @@
 // gemm.cu — persistent tcgen05 GEMMs for the two resident-weight matmul kinds
 // burn-rocket offloads:
 //
-//   * Q8_0:  C[M,N] = A[M,K] (f16) · deq(W)[N,K]^T, deq(W) = f16(d · q) built
-//            in shared memory from int8 codes + f16 block scales (blocks of 32
-//            along K) by producer warps, feeding kind::f16 UMMA with an f32
-//            TMEM accumulator. (Reference semantics: the NPU route packs
-//            dequantised Q8_0 as fp16, ext.rs:1437-1499; the Q8_0 codec is
-//            util/gguf.rs:197-215.)
+//   * Q8_0:  C[M,N] = A[M,K] (f16) · deq(W)[N,K]^T with deq(W) = f16(d · q).
+//            The int8 codes and the f16 block scales (one per 32 K values) are
+//            staged into shared memory by TMA and dequantised there, by
+//            producer warps, into the 128-byte-swizzled K-major layout that
+//            kind::f16 UMMA reads; accumulation is f32 in TMEM. (Reference
+//            semantics: the NPU route packs dequantised Q8_0 as fp16,
+//            crates/burn-rocket/src/ext.rs:1437-1499; the codec is
+//            src/util/gguf.rs:197-215.)
 //   * W8A8:  acc[M,N] = Aq[M,K] (s8) · Wq[N,K]^T (s8) on kind::i8 UMMA with an
 //            s32 TMEM accumulator; epilogue y = f32(acc) · (s_row[m] · s_col[n])
 //            in exactly that order (ext.rs:1350-1363).
 //
+// Q8_0 weight planes in HBM (written at pack time):
+//   codes  int8 [N, K] row-major
+//   scales f16  [K/32, pitch], pitch = round_up(N, 8) (k-block-major: one TMA
+//                           box carries the two scales of a 64-wide K stage
+//                           for BN weight rows)
+//
 // Warp roles (one CTA per SM, persistent over output tiles):
-//   warp 0      TMA producer (A always; B too for W8A8)
-//   warp 1      UMMA issuer (single elected lane) + TMEM owner
-//   warps 2..5  epilogue: TMEM -> registers -> global (one accumulator row per thread)
-//   warps 6..13 Q8_0 only: dequantise weight codes into the swizzled B stage
-// The accumulator is double-buffered in TMEM so the epilogue of tile i overlaps
-// the main loop of tile i+1.
+//   warp 0      TMA producer (A and B, or A + codes + scales)
+//   warp 1      UMMA issuer (one elected lane) and TMEM owner
+//   warps 2..5  epilogue: TMEM -> registers -> swizzled smem -> TMA store
+//   warps 6..13 Q8_0 only: dequantise staged codes into the f16 B ring
+// The accumulator is double-buffered in TMEM so the epilogue of tile i
+// overlaps the main loop of tile i+1.
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -29,57 +37,67 @@
 namespace rb {
 
 constexpr int kBM = 128;          // UMMA M (one TMEM lane per output row)
-constexpr int kStageBytesK = 128; // bytes of K per stage (one 128-B swizzle atom)
 constexpr int kEpiWarp0 = 2;      // first epilogue warp
 constexpr int kNumEpiWarps = 4;
 constexpr int kDqWarp0 = 6;       // first dequant warp (Q8_0 only)
 constexpr int kNumDqWarps = 8;
+constexpr int kEpiBufBytes = 4096;  // 32 rows x 128 B, one per warp and buffer
 
 enum class BSrc { Tma, Q8Dequant };
 
-template <int BN_, int STAGES_, bool I8_, BSrc BSRC_>
+constexpr int round1k(int x) { return (x + 1023) & ~1023; }
+
+template <int BN_, int LSTAGES_, bool I8_>
 struct GemmCfg {
   static constexpr int BN = BN_;
-  static constexpr int STAGES = STAGES_;
+  static constexpr int LSTAGES = LSTAGES_;          // TMA load ring depth
   static constexpr bool I8 = I8_;
-  static constexpr BSrc B_SRC = BSRC_;
-  static constexpr int ELEM = I8 ? 1 : 2;                   // operand bytes
-  static constexpr int BK = kStageBytesK / ELEM;             // K elements per stage
-  static constexpr int UMMA_K = I8 ? 32 : 16;                // K per instruction
-  static constexpr int KSTEPS = BK / UMMA_K;                 // 4
-  static constexpr int A_BYTES = kBM * kStageBytesK;         // 16 KB
-  static constexpr int B_BYTES = BN * kStageBytesK;
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int NUM_WARPS = (B_SRC == BSrc::Q8Dequant) ? (kDqWarp0 + kNumDqWarps) : 6;
+  static constexpr bool Q8 = !I8;
+  static constexpr int BSTAGES = 2;                 // dequantised B ring (Q8_0)
+  static constexpr int ELEM = I8 ? 1 : 2;
+  static constexpr int BK = 128 / ELEM;             // K elements per stage (one 128-B atom)
+  static constexpr int UMMA_K = I8 ? 32 : 16;
+  static constexpr int KSTEPS = BK / UMMA_K;        // 4
+  static constexpr int A_BYTES = kBM * 128;         // 16 KB
+  static constexpr int B_BYTES = BN * 128;          // one B tile (f16 or s8)
+  static constexpr int CODE_BYTES = Q8 ? BN * 64 : 0;
+  static constexpr int SC_BYTES = Q8 ? 2 * BN * 2 : 0;
+  static constexpr int LOAD_TX = Q8 ? (A_BYTES + CODE_BYTES + SC_BYTES) : (A_BYTES + B_BYTES);
+  static constexpr int LSTAGE = round1k(LOAD_TX);
+  static constexpr int BRING_OFF = LSTAGES * LSTAGE;
+  static constexpr int BRING = Q8 ? BSTAGES * B_BYTES : 0;
+  static constexpr int EPI_OFF = BRING_OFF + BRING;
+  static constexpr int EPI_BYTES = kNumEpiWarps * 2 * kEpiBufBytes;
+  static constexpr int BAR_OFF = EPI_OFF + EPI_BYTES;
+  static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
+  static constexpr int NUM_WARPS = Q8 ? (kDqWarp0 + kNumDqWarps) : 6;
   static constexpr int THREADS = NUM_WARPS * 32;
   static constexpr uint32_t TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64
                                         : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
   static_assert(2 * BN <= 512, "two accumulators must fit in TMEM");
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N constraint for M=128");
+  static_assert(B_BYTES % 1024 == 0, "B tiles must keep 1024-byte alignment");
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
 
 struct GemmArgs {
   int M, N, K;
-  // Q8_0 weight planes (unused for W8A8)
-  const int8_t* w_codes;   // [N, K]
-  const __half* w_scales;  // [N, K/32]
-  // W8A8 scales (unused for Q8_0)
-  const float* s_row;      // [M]
-  const float* s_col;      // [N]
-  void* out;               // [M, ldo]
+  const float* s_row;  // W8A8 [M]
+  const float* s_col;  // W8A8 [N]
+  void* out;           // [M, ldo]
   int ldo;
-  int out_dtype;           // RB_DTYPE_* (RB_DTYPE_I32: raw int8-GEMM accumulators)
-  float out_scale;         // W8A8: calibrated output grid (0 = unrounded)
-  float out_inv;           // 1 / out_scale in f32
+  int out_dtype;       // RB_DTYPE_* (RB_DTYPE_I32: raw int8-GEMM accumulators)
+  float out_scale;     // W8A8: calibrated output grid (0 = unrounded)
+  float out_inv;       // 1 / out_scale in f32
+  int tma_store;       // epilogue through smem + TMA store (else direct stores)
   uint32_t* err;
 };
 
 // --------------------------------------------------------------------------
 // Q8_0 dequantisation of 8 consecutive codes of one weight row:
-// f16 value = RNE(d * q), computed as (biased-exponent trick: 0x6400|u is the
-// f16 number 1024+u) q = h - 1152 exactly, then one correctly rounded f16
-// multiply by the block scale d.
+// f16 value = RNE(d * q). 0x6400|u is the f16 number 1024+u, so q = h - 1152
+// exactly; one correctly rounded f16 multiply by d then gives RNE(d * q)
+// (d * q is exact in f32, so this equals rounding the exact product once).
 __device__ __forceinline__ uint4 q8_dequant8_f16(uint2 codes, __half d) {
   const uint32_t lo = codes.x ^ 0x80808080u;
   const uint32_t hi = codes.y ^ 0x80808080u;
@@ -114,43 +132,46 @@ __device__ __forceinline__ void store_out8(void* out, int dtype, int64_t idx, co
     }
   } else if (dtype == RB_DTYPE_F16) {
     __half* p = reinterpret_cast<__half*>(out) + idx;
-    if (count == 8 && (idx & 7) == 0) {
-      uint4 u;
-      __half2* h = reinterpret_cast<__half2*>(&u);
-      for (int i = 0; i < 4; ++i) h[i] = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
-      *reinterpret_cast<uint4*>(p) = u;
-    } else {
-      for (int i = 0; i < count; ++i) p[i] = __float2half_rn(v[i]);
-    }
+    for (int i = 0; i < count; ++i) p[i] = __float2half_rn(v[i]);
   } else {
     __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(out) + idx;
-    if (count == 8 && (idx & 7) == 0) {
-      uint4 u;
-      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
-      for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-      *reinterpret_cast<uint4*>(p) = u;
-    } else {
-      for (int i = 0; i < count; ++i) p[i] = __float2bfloat16_rn(v[i]);
-    }
+    for (int i = 0; i < count; ++i) p[i] = __float2bfloat16_rn(v[i]);
   }
+}
+
+// Epilogue value for accumulator bits r at column n (row scale rs).
+template <bool I8>
+__device__ __forceinline__ float epi_value(const GemmArgs& a, uint32_t r, float rs, int n) {
+  if (!I8) return __uint_as_float(r);
+  if (a.out_dtype == RB_DTYPE_I32) return __uint_as_float(r);
+  // Order matters for bit parity: f32(acc) * (s_row * s_col).
+  float y = __fmul_rn(__int2float_rn(static_cast<int32_t>(r)), __fmul_rn(rs, a.s_col[n]));
+  if (a.out_scale != 0.0f) {
+    // static_code(y, 1/out_scale) * out_scale (ext.rs:1236-1238, 1356-1360),
+    // through an integer code like the reference (`as i8`), so zero is +0.0.
+    const int code = max(-128, min(127, __float2int_rn(__fmul_rn(y, a.out_inv))));
+    y = __fmul_rn(__int2float_rn(code), a.out_scale);
+  }
+  return y;
 }
 
 template <class Cfg>
 __global__ void __launch_bounds__(Cfg::THREADS, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+            const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmC,
             GemmArgs args) {
   constexpr int BN = Cfg::BN;
-  constexpr int STAGES = Cfg::STAGES;
+  constexpr int LSTAGES = Cfg::LSTAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  // 1024-byte alignment for the 128-B swizzle atoms.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
-  uint64_t* full_a = bars;                 // [STAGES] TMA bytes (A, and B for W8A8)
-  uint64_t* full_b = bars + STAGES;        // [STAGES] dequant warps (Q8_0)
-  uint64_t* empty = bars + 2 * STAGES;     // [STAGES] UMMA commit
-  uint64_t* acc_full = bars + 3 * STAGES;  // [2]
-  uint64_t* acc_empty = acc_full + 2;      // [2]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::BAR_OFF);
+  uint64_t* load_full = bars;                       // [LSTAGES] TMA bytes
+  uint64_t* load_empty = bars + LSTAGES;            // [LSTAGES] UMMA (+ dequant warps)
+  uint64_t* b_full = bars + 2 * LSTAGES;            // [2] dequant warps (Q8_0)
+  uint64_t* b_empty = b_full + 2;                   // [2] UMMA (Q8_0)
+  uint64_t* acc_full = b_empty + 2;                 // [2]
+  uint64_t* acc_empty = acc_full + 2;               // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -163,12 +184,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   const int num_kb = (K + Cfg::BK - 1) / Cfg::BK;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full_a[s], 1);
-      mbar_init(&full_b[s], kNumDqWarps);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < LSTAGES; ++s) {
+      mbar_init(&load_full[s], 1);
+      mbar_init(&load_empty[s], Cfg::Q8 ? 1 + kNumDqWarps : 1);
     }
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&b_full[i], kNumDqWarps);
+      mbar_init(&b_empty[i], 1);
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], kNumEpiWarps);
     }
@@ -181,7 +203,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
-    if (Cfg::B_SRC == BSrc::Tma) tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmB);
+    if (Cfg::Q8) tma_prefetch_desc(&tmS);
+    if (args.tma_store) tma_prefetch_desc(&tmC);
   }
   tc_fence_before();
   __syncthreads();
@@ -191,23 +215,23 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (elect_one_sync()) {
-      int stage = 0;
-      uint32_t phase = 0;
+      int ls = 0;
+      uint32_t lph = 0;
       for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
         const int m0 = (t / tiles_n) * kBM;
         const int n0 = (t % tiles_n) * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, args.err, abort_flag)) goto producer_done;
-          uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
-          if (Cfg::B_SRC == BSrc::Tma) {
-            mbar_arrive_expect_tx(&full_a[stage], Cfg::A_BYTES + Cfg::B_BYTES);
-            tma_load_2d(sa, &tmA, &full_a[stage], kb * Cfg::BK, m0);
-            tma_load_2d(sa + Cfg::A_BYTES, &tmB, &full_a[stage], kb * Cfg::BK, n0);
+          if (!mbar_wait(&load_empty[ls], lph ^ 1, args.err, abort_flag)) goto producer_done;
+          uint8_t* st = smem + ls * Cfg::LSTAGE;
+          mbar_arrive_expect_tx(&load_full[ls], Cfg::LOAD_TX);
+          tma_load_2d(st, &tmA, &load_full[ls], kb * Cfg::BK, m0);
+          if (Cfg::I8) {
+            tma_load_2d(st + Cfg::A_BYTES, &tmB, &load_full[ls], kb * Cfg::BK, n0);
           } else {
-            mbar_arrive_expect_tx(&full_a[stage], Cfg::A_BYTES);
-            tma_load_2d(sa, &tmA, &full_a[stage], kb * Cfg::BK, m0);
+            tma_load_2d(st + Cfg::A_BYTES, &tmB, &load_full[ls], kb * 64, n0);
+            tma_load_2d(st + Cfg::A_BYTES + Cfg::CODE_BYTES, &tmS, &load_full[ls], n0, kb * 2);
           }
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          if (++ls == LSTAGES) { ls = 0; lph ^= 1; }
         }
       }
     producer_done:;
@@ -217,8 +241,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     if (elect_one_sync()) {
       constexpr uint32_t idesc =
           Cfg::I8 ? idesc_i8(kBM, BN) : idesc_f16(kBM, BN, false, false, false);
-      int stage = 0;
-      uint32_t phase = 0;
+      int ls = 0, bs = 0;
+      uint32_t lph = 0, bph = 0;
       int local = 0;
       for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
         const int acc = local & 1;
@@ -227,13 +251,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&full_a[stage], phase, args.err, abort_flag)) goto mma_done;
-          if (Cfg::B_SRC == BSrc::Q8Dequant) {
-            if (!mbar_wait(&full_b[stage], phase, args.err, abort_flag)) goto mma_done;
+          if (!mbar_wait(&load_full[ls], lph, args.err, abort_flag)) goto mma_done;
+          if (Cfg::Q8) {
+            if (!mbar_wait(&b_full[bs], bph, args.err, abort_flag)) goto mma_done;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + stage * Cfg::STAGE_BYTES);
-          const uint32_t b_addr = a_addr + Cfg::A_BYTES;
+          const uint32_t a_addr = smem_u32(smem + ls * Cfg::LSTAGE);
+          const uint32_t b_addr = Cfg::Q8 ? smem_u32(smem + Cfg::BRING_OFF + bs * Cfg::B_BYTES)
+                                          : a_addr + Cfg::A_BYTES;
 #pragma unroll
           for (int ks = 0; ks < Cfg::KSTEPS; ++ks) {
             const uint64_t da = desc_kmajor_sw128(a_addr + ks * 32);
@@ -242,8 +267,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             if (Cfg::I8) umma_i8_ss(d_tmem, da, db, idesc, accum);
             else umma_f16_ss(d_tmem, da, db, idesc, accum);
           }
-          umma_commit(&empty[stage]);  // frees the stage once these MMAs retire
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          umma_commit(&load_empty[ls]);  // frees the load stage once these MMAs retire
+          if (++ls == LSTAGES) { ls = 0; lph ^= 1; }
+          if (Cfg::Q8) {
+            umma_commit(&b_empty[bs]);
+            if (++bs == Cfg::BSTAGES) { bs = 0; bph ^= 1; }
+          }
         }
         umma_commit(&acc_full[acc]);
       }
@@ -253,6 +282,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;
+    uint8_t* ebuf = smem + Cfg::EPI_OFF + (warp - kEpiWarp0) * 2 * kEpiBufBytes;
+    const int out_bytes = (args.out_dtype == RB_DTYPE_F16 || args.out_dtype == RB_DTYPE_BF16) ? 2 : 4;
+    const int CW = 128 / out_bytes;  // columns per 128-byte store row
+    int buf = 0;
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       const int m0 = (t / tiles_n) * kBM;
@@ -265,103 +298,124 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       float rs = 1.0f;
       // Raw int32 output (RB_DTYPE_I32) carries no scales.
       if (Cfg::I8 && m < M && args.out_dtype != RB_DTYPE_I32) rs = args.s_row[m];
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
-        uint32_t r[16];
-        tmem_ld16(tmem_addr(tmem_base, quarter * 32, acc * BN + c), r);
-        tmem_wait_ld();
-        if (m < M && n0 + c < N) {
-          float v[16];
+      const bool rows_live = m0 + quarter * 32 < M;  // warp-uniform
+      if (args.tma_store) {
+        if (rows_live) {
+          for (int c0 = 0; c0 < BN && n0 + c0 < N; c0 += CW) {
+            uint32_t r[64];
+            tmem_ld32(tmem_addr(tmem_base, quarter * 32, acc * BN + c0),
+                      *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+            if (CW == 64)
+              tmem_ld32(tmem_addr(tmem_base, quarter * 32, acc * BN + c0 + 32),
+                        *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+            tmem_wait_ld();
+            // The buffer about to be written must have been read by its
+            // previous TMA store (at most one store of this warp in flight).
+            if (lane == 0) bulk_wait_read<1>();
+            __syncwarp();
+            uint8_t* b = ebuf + buf * kEpiBufBytes + lane * 128;
+            if (out_bytes == 4) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            if (Cfg::I8) {
-              if (args.out_dtype == RB_DTYPE_I32) {
-                v[j] = __uint_as_float(r[j]);
-              } else {
-                const int n = min(n0 + c + j, N - 1);
-                // Order matters for bit parity: f32(acc) * (s_row * s_col).
-                float y = __fmul_rn(__int2float_rn(static_cast<int32_t>(r[j])),
-                                    __fmul_rn(rs, args.s_col[n]));
-                if (args.out_scale != 0.0f) {
-                  // static_code(y, 1/out_scale) * out_scale (ext.rs:1236-1238, 1356-1360)
-                  // Through an integer code like the reference (`as i8`), so a
-                  // code of zero is +0.0, never -0.0.
-                  const int code = max(-128, min(127, __float2int_rn(__fmul_rn(y, args.out_inv))));
-                  y = __fmul_rn(__int2float_rn(code), args.out_scale);
-                }
-                v[j] = y;
+              for (int j = 0; j < 8; ++j) {
+                float v[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  v[e] = epi_value<Cfg::I8>(args, r[4 * j + e], rs, min(n0 + c0 + 4 * j + e, N - 1));
+                *reinterpret_cast<float4*>(b + ((j ^ (lane & 7)) << 4)) =
+                    make_float4(v[0], v[1], v[2], v[3]);
               }
             } else {
-              v[j] = __uint_as_float(r[j]);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                uint32_t pk[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int c = 8 * j + 2 * e;
+                  const float v0 = epi_value<Cfg::I8>(args, r[c], rs, min(n0 + c0 + c, N - 1));
+                  const float v1 = epi_value<Cfg::I8>(args, r[c + 1], rs, min(n0 + c0 + c + 1, N - 1));
+                  if (args.out_dtype == RB_DTYPE_F16) {
+                    __half2 h = __floats2half2_rn(v0, v1);
+                    pk[e] = *reinterpret_cast<uint32_t*>(&h);
+                  } else {
+                    __nv_bfloat162 h = __floats2bfloat162_rn(v0, v1);
+                    pk[e] = *reinterpret_cast<uint32_t*>(&h);
+                  }
+                }
+                *reinterpret_cast<uint4*>(b + ((j ^ (lane & 7)) << 4)) =
+                    make_uint4(pk[0], pk[1], pk[2], pk[3]);
+              }
             }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmC, ebuf + buf * kEpiBufBytes, n0 + c0, m0 + quarter * 32);
+              bulk_commit();
+            }
+            buf ^= 1;
           }
-          const int64_t base = static_cast<int64_t>(m) * args.ldo + n0 + c;
-          const int left = N - (n0 + c);
-          store_out8(args.out, args.out_dtype, base, v, left >= 8 ? 8 : left);
-          if (left > 8) store_out8(args.out, args.out_dtype, base + 8, v + 8, left >= 16 ? 8 : left - 8);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          uint32_t r[16];
+          tmem_ld16(tmem_addr(tmem_base, quarter * 32, acc * BN + c), r);
+          tmem_wait_ld();
+          if (m < M && n0 + c < N) {
+            float v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = epi_value<Cfg::I8>(args, r[j], rs, min(n0 + c + j, N - 1));
+            const int64_t base = static_cast<int64_t>(m) * args.ldo + n0 + c;
+            const int left = N - (n0 + c);
+            store_out8(args.out, args.out_dtype, base, v, left >= 8 ? 8 : left);
+            if (left > 8) store_out8(args.out, args.out_dtype, base + 8, v + 8, left >= 16 ? 8 : left - 8);
+          }
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
     }
-  } else if (Cfg::B_SRC == BSrc::Q8Dequant && warp >= kDqWarp0) {
+    if (args.tma_store && lane == 0) bulk_wait_all<0>();  // stores complete before exit
+  } else if (Cfg::Q8 && warp >= kDqWarp0) {
     // ------------------------------------------------------------ Q8_0 dequant
-    // Each 16-byte chunk of the B stage holds 8 f16 weights of one row. Chunk
-    // (row, c) lands at row*128 + ((c ^ (row & 7)) * 16) — the 128-B swizzle
-    // TMA would have produced — so UMMA reads it with the same descriptor.
+    // Chunk (row, c) — 8 codes of one weight row — is read from the staged
+    // codes at row*64 + c*8 and written as 8 f16 at row*128 + ((c ^ (row&7))*16):
+    // the 128-byte swizzle TMA would produce, read by UMMA with the same
+    // descriptor as any other K-major operand.
     constexpr int kChunks = BN * 8;
     constexpr int kThreads = kNumDqWarps * 32;
     constexpr int kPer = (kChunks + kThreads - 1) / kThreads;
     const int tid = threadIdx.x - kDqWarp0 * 32;
-    const int kblocks32 = K / 32;
-    int stage = 0;
-    uint32_t phase = 0;
+    int ls = 0, bs = 0;
+    uint32_t lph = 0, bph = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-      const int n0 = (t % tiles_n) * BN;
-      // Prefetch registers for k-block 0.
-      uint2 codes[kPer];
-      __half sc[kPer];
-      auto load_kb = [&](int kb) {
-#pragma unroll
-        for (int j = 0; j < kPer; ++j) {
-          const int i = tid + j * kThreads;
-          const int rowi = i >> 3, c = i & 7;
-          const int n = n0 + rowi;
-          const int k = kb * 64 + c * 8;
-          if (i < kChunks && n < N && k < K) {
-            codes[j] = __ldg(reinterpret_cast<const uint2*>(args.w_codes +
-                                                            static_cast<int64_t>(n) * K + k));
-            sc[j] = args.w_scales[static_cast<int64_t>(n) * kblocks32 + (k >> 5)];
-          } else {
-            codes[j] = make_uint2(0u, 0u);
-            sc[j] = __ushort_as_half(0);
-          }
-        }
-      };
-      load_kb(0);
       for (int kb = 0; kb < num_kb; ++kb) {
-        uint2 cur[kPer];
-        __half cur_sc[kPer];
-#pragma unroll
-        for (int j = 0; j < kPer; ++j) { cur[j] = codes[j]; cur_sc[j] = sc[j]; }
-        if (kb + 1 < num_kb) load_kb(kb + 1);
-        if (!__all_sync(0xffffffffu, mbar_wait(&empty[stage], phase ^ 1, args.err, abort_flag)))
+        if (!__all_sync(0xffffffffu, mbar_wait(&load_full[ls], lph, args.err, abort_flag)))
           goto dq_done;
-        uint8_t* sb = smem + stage * Cfg::STAGE_BYTES + Cfg::A_BYTES;
+        if (!__all_sync(0xffffffffu, mbar_wait(&b_empty[bs], bph ^ 1, args.err, abort_flag)))
+          goto dq_done;
+        const uint8_t* codes = smem + ls * Cfg::LSTAGE + Cfg::A_BYTES;
+        const __half* sc = reinterpret_cast<const __half*>(codes + Cfg::CODE_BYTES);
+        uint8_t* sb = smem + Cfg::BRING_OFF + bs * Cfg::B_BYTES;
 #pragma unroll
         for (int j = 0; j < kPer; ++j) {
           const int i = tid + j * kThreads;
-          if (i < kChunks) {
+          if (kChunks % kThreads == 0 || i < kChunks) {
             const int rowi = i >> 3, c = i & 7;
-            const uint4 w = q8_dequant8_f16(cur[j], cur_sc[j]);
-            *reinterpret_cast<uint4*>(sb + rowi * 128 + ((c ^ (rowi & 7)) << 4)) = w;
+            const uint2 q = *reinterpret_cast<const uint2*>(codes + rowi * 64 + c * 8);
+            const __half d = sc[(c >> 2) * BN + rowi];
+            *reinterpret_cast<uint4*>(sb + rowi * 128 + ((c ^ (rowi & 7)) << 4)) =
+                q8_dequant8_f16(q, d);
           }
         }
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&full_b[stage]);
-        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        if (lane == 0) {
+          mbar_arrive(&b_full[bs]);
+          mbar_arrive(&load_empty[ls]);  // staged codes consumed
+        }
+        if (++ls == LSTAGES) { ls = 0; lph ^= 1; }
+        if (++bs == Cfg::BSTAGES) { bs = 0; bph ^= 1; }
       }
     }
   dq_done:;
@@ -377,11 +431,19 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 }
 
 // --------------------------------------------------------------------------
-// Host-side launch helpers.
+// Host-side launch.
+
+using CfgQ8_256 = GemmCfg<256, 3, false>;
+using CfgQ8_128 = GemmCfg<128, 6, false>;
+using CfgQ8_96 = GemmCfg<96, 6, false>;
+using CfgQ8_64 = GemmCfg<64, 7, false>;
+using CfgI8_256 = GemmCfg<256, 4, true>;
+using CfgI8_128 = GemmCfg<128, 6, true>;
 
 template <class Cfg>
-static int launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmArgs& a,
-                       int num_sms, cudaStream_t stream) {
+static int launch_cfg(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmS,
+                      const CUtensorMap* tmC, const GemmArgs& a, int num_sms,
+                      cudaStream_t stream) {
   const int tiles = ((a.M + kBM - 1) / kBM) * ((a.N + Cfg::BN - 1) / Cfg::BN);
   const int grid = tiles < num_sms ? tiles : num_sms;
   static uint64_t configured = 0;  // one bit per device ordinal
@@ -393,98 +455,98 @@ static int launch_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB, const Gem
       return RB_E_DEVICE;
     configured |= 1ull << (dev & 63);
   }
-  gemm_kernel<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(tmA, tmB, a);
+  GemmArgs args = a;
+  const int out_bytes = (a.out_dtype == RB_DTYPE_F16 || a.out_dtype == RB_DTYPE_BF16) ? 2 : 4;
+  // The TMA-store epilogue writes whole 128-byte rows of the N tile.
+  args.tma_store = tmC != nullptr && (Cfg::BN % (128 / out_bytes)) == 0;
+  gemm_kernel<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(tmA, tmB, tmS,
+                                                                     tmC ? *tmC : tmA, args);
   return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
 }
 
-using CfgQ8_256 = GemmCfg<256, 4, false, BSrc::Q8Dequant>;
-using CfgQ8_128 = GemmCfg<128, 6, false, BSrc::Q8Dequant>;
-using CfgQ8_96 = GemmCfg<96, 6, false, BSrc::Q8Dequant>;
-using CfgQ8_64 = GemmCfg<64, 8, false, BSrc::Q8Dequant>;
-using CfgI8_256 = GemmCfg<256, 4, true, BSrc::Tma>;
-using CfgI8_128 = GemmCfg<128, 6, true, BSrc::Tma>;
-
-// Pick the N tile minimising the makespan of the persistent grid: rounds of
-// tiles per SM times the per-tile cost (proportional to BN plus a fixed
-// pipeline fill / epilogue overhead expressed in BN units).
-static int pick_bn(int M, int N, int num_sms, const int* cands, int ncands) {
+// N tile minimising the makespan of the persistent grid: rounds of tiles per
+// SM times the per-tile cost (proportional to BN plus a fixed pipeline fill /
+// epilogue overhead expressed in BN units).
+int gemm_pick_bn(bool i8, int M, int N, int num_sms) {
+  static const int q8c[] = {256, 128, 96, 64};
+  static const int i8c[] = {256, 128};
+  const int* c = i8 ? i8c : q8c;
+  const int nc = i8 ? 2 : 4;
   const long tm = (M + kBM - 1) / kBM;
-  int best = cands[0];
+  int best = c[0];
   long best_cost = -1;
-  for (int i = 0; i < ncands; ++i) {
-    const int bn = cands[i];
-    const long tiles = tm * ((N + bn - 1) / bn);
+  for (int i = 0; i < nc; ++i) {
+    const long tiles = tm * ((N + c[i] - 1) / c[i]);
     const long rounds = (tiles + num_sms - 1) / num_sms;
-    const long cost = rounds * (bn + 32);
-    if (best_cost < 0 || cost < best_cost) { best_cost = cost; best = bn; }
+    const long cost = rounds * (c[i] + 32);
+    if (best_cost < 0 || cost < best_cost) { best_cost = cost; best = c[i]; }
   }
   return best;
 }
 
-int launch_q8_gemm(const CUtensorMap& tmA, const GemmLaunch& L, cudaStream_t stream) {
+static GemmArgs make_args(const GemmLaunch& L) {
   GemmArgs a{};
   a.M = L.M; a.N = L.N; a.K = L.K;
-  a.w_codes = L.w_codes; a.w_scales = reinterpret_cast<const __half*>(L.w_scales);
-  a.out = L.out; a.ldo = L.ldo; a.out_dtype = L.out_dtype; a.err = L.err;
-  static const int cands[] = {256, 128, 96, 64};
-  int bn = L.force_bn ? L.force_bn : pick_bn(L.M, L.N, L.num_sms, cands, 4);
-  CUtensorMap dummy = tmA;
+  a.s_row = L.s_row; a.s_col = L.s_col;
+  a.out = L.out; a.ldo = L.ldo; a.out_dtype = L.out_dtype;
+  a.out_scale = L.out_scale;
+  a.out_inv = L.out_scale != 0.0f ? 1.0f / L.out_scale : 0.0f;
+  a.err = L.err;
+  return a;
+}
+
+int launch_q8_gemm(const GemmLaunch& L, int bn, const CUtensorMap& tmA, const CUtensorMap& tmCodes,
+                   const CUtensorMap& tmScales, const CUtensorMap* tmC, cudaStream_t stream) {
+  const GemmArgs a = make_args(L);
   switch (bn) {
-    case 256: return launch_gemm<CfgQ8_256>(tmA, dummy, a, L.num_sms, stream);
-    case 128: return launch_gemm<CfgQ8_128>(tmA, dummy, a, L.num_sms, stream);
-    case 96: return launch_gemm<CfgQ8_96>(tmA, dummy, a, L.num_sms, stream);
-    case 64: return launch_gemm<CfgQ8_64>(tmA, dummy, a, L.num_sms, stream);
+    case 256: return launch_cfg<CfgQ8_256>(tmA, tmCodes, tmScales, tmC, a, L.num_sms, stream);
+    case 128: return launch_cfg<CfgQ8_128>(tmA, tmCodes, tmScales, tmC, a, L.num_sms, stream);
+    case 96: return launch_cfg<CfgQ8_96>(tmA, tmCodes, tmScales, tmC, a, L.num_sms, stream);
+    case 64: return launch_cfg<CfgQ8_64>(tmA, tmCodes, tmScales, tmC, a, L.num_sms, stream);
     default: return RB_E_SHAPE;
   }
 }
 
-int launch_w8a8_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB256,
-                     const CUtensorMap& tmB128, const GemmLaunch& L, cudaStream_t stream) {
-  GemmArgs a{};
-  a.M = L.M; a.N = L.N; a.K = L.K;
-  a.s_row = L.s_row; a.s_col = L.s_col;
-  a.out_scale = L.out_scale;
-  a.out_inv = L.out_scale != 0.0f ? 1.0f / L.out_scale : 0.0f;
-  a.out = L.out; a.ldo = L.ldo; a.out_dtype = L.out_dtype; a.err = L.err;
-  static const int cands[] = {256, 128};
-  int bn = L.force_bn ? L.force_bn : pick_bn(L.M, L.N, L.num_sms, cands, 2);
+int launch_w8a8_gemm(const GemmLaunch& L, int bn, const CUtensorMap& tmA, const CUtensorMap& tmB,
+                     const CUtensorMap* tmC, cudaStream_t stream) {
+  const GemmArgs a = make_args(L);
   switch (bn) {
-    case 256: return launch_gemm<CfgI8_256>(tmA, tmB256, a, L.num_sms, stream);
-    case 128: return launch_gemm<CfgI8_128>(tmA, tmB128, a, L.num_sms, stream);
+    case 256: return launch_cfg<CfgI8_256>(tmA, tmB, tmA, tmC, a, L.num_sms, stream);
+    case 128: return launch_cfg<CfgI8_128>(tmA, tmB, tmA, tmC, a, L.num_sms, stream);
     default: return RB_E_SHAPE;
   }
 }
 
 // --------------------------------------------------------------------------
-// Standalone dequantisation kernels (debug / parity surface of the codec).
+// Standalone dequantisation kernels (the codec's parity surface).
 
-// f32 = f32(d) * f32(q), exact (gguf.rs:197-215).
+// f32 = f32(d) * f32(q), exact (gguf.rs:197-215). scales are [K/32, N].
 __global__ void q8_dequant_f32_kernel(const int8_t* codes, const __half* scales, int N, int K,
-                                      float* out) {
+                                      int pitch, float* out) {
   const int64_t total = static_cast<int64_t>(N) * K;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t n = i / K, k = i % K;
-    const float d = __half2float(scales[n * (K / 32) + k / 32]);
+    const float d = __half2float(scales[(k / 32) * pitch + n]);
     out[i] = __fmul_rn(d, static_cast<float>(codes[i]));
   }
 }
 
 // f16 = RNE(d * q): the exact values the GEMM's producer warps stage.
 __global__ void q8_dequant_f16_kernel(const int8_t* codes, const __half* scales, int N, int K,
-                                      __half* out) {
+                                      int pitch, __half* out) {
   const int64_t total8 = static_cast<int64_t>(N) * K / 8;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total8;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t e = i * 8;
     const int64_t n = e / K, k = e % K;
     const uint2 c = *reinterpret_cast<const uint2*>(codes + e);
-    const uint4 w = q8_dequant8_f16(c, scales[n * (K / 32) + k / 32]);
+    const uint4 w = q8_dequant8_f16(c, scales[(k / 32) * pitch + n]);
     *reinterpret_cast<uint4*>(out + e) = w;
   }
 }
 
-int launch_q8_dequant(const int8_t* codes, const void* scales, int N, int K, void* out,
+int launch_q8_dequant(const int8_t* codes, const void* scales, int N, int K, int pitch, void* out,
                       bool f16_out, cudaStream_t stream) {
   const int64_t total = static_cast<int64_t>(N) * K;
   const int threads = 256;
@@ -492,10 +554,10 @@ int launch_q8_dequant(const int8_t* codes, const void* scales, int N, int K, voi
   if (blocks > 148 * 32) blocks = 148 * 32;
   if (f16_out)
     q8_dequant_f16_kernel<<<static_cast<int>(blocks), threads, 0, stream>>>(
-        codes, reinterpret_cast<const __half*>(scales), N, K, reinterpret_cast<__half*>(out));
+        codes, reinterpret_cast<const __half*>(scales), N, K, pitch, reinterpret_cast<__half*>(out));
   else
     q8_dequant_f32_kernel<<<static_cast<int>(blocks), threads, 0, stream>>>(
-        codes, reinterpret_cast<const __half*>(scales), N, K, reinterpret_cast<float*>(out));
+        codes, reinterpret_cast<const __half*>(scales), N, K, pitch, reinterpret_cast<float*>(out));
   return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
 }
 

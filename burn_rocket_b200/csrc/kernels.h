@@ -16,7 +16,7 @@ namespace rb {
 struct GemmLaunch {
   int M, N, K;
   const int8_t* w_codes;  // Q8_0 codes [N, K]
-  const void* w_scales;   // Q8_0 f16 scales [N, K/32]
+  const void* w_scales;   // Q8_0 f16 scales [K/32, N]
   const float* s_row;     // W8A8 per-row activation scale [M]
   const float* s_col;     // W8A8 per-channel weight scale [N]
   void* out;
@@ -28,11 +28,20 @@ struct GemmLaunch {
   int force_bn;           // 0 = heuristic
 };
 
-int launch_q8_gemm(const CUtensorMap& tmA, const GemmLaunch& L, cudaStream_t stream);
-// tmB256 / tmB128: TMA maps of the weight codes with box heights 256 / 128.
-int launch_w8a8_gemm(const CUtensorMap& tmA, const CUtensorMap& tmB256,
-                     const CUtensorMap& tmB128, const GemmLaunch& L, cudaStream_t stream);
-int launch_q8_dequant(const int8_t* codes, const void* scales, int N, int K, void* out,
+// N tile the persistent GEMM will use for an [M, N] output (weight tensor
+// maps are built per N tile).
+int gemm_pick_bn(bool i8, int M, int N, int num_sms);
+// Q8_0: tmA = f16 activations [M, K] (box 64 x 128, 128-B swizzle); tmCodes =
+// codes [N, K] (box 64 x bn); tmScales = f16 scales [K/32, N] (box bn x 2);
+// tmC = output map (box 32 rows x 128 B, 128-B swizzle) or nullptr for direct
+// stores.
+int launch_q8_gemm(const GemmLaunch& L, int bn, const CUtensorMap& tmA, const CUtensorMap& tmCodes,
+                   const CUtensorMap& tmScales, const CUtensorMap* tmC, cudaStream_t stream);
+// W8A8: tmA = s8 activation codes [M, K] (box 128 x 128), tmB = s8 weight
+// codes [N, K] (box 128 x bn), both 128-B swizzled.
+int launch_w8a8_gemm(const GemmLaunch& L, int bn, const CUtensorMap& tmA, const CUtensorMap& tmB,
+                     const CUtensorMap* tmC, cudaStream_t stream);
+int launch_q8_dequant(const int8_t* codes, const void* scales, int N, int K, int pitch, void* out,
                       bool f16_out, cudaStream_t stream);
 
 // Elementwise / codec kernels (quant.cu).
@@ -40,10 +49,12 @@ int launch_cast(const void* x, int x_dtype, void* y, int y_dtype, int64_t count,
                 cudaStream_t stream);
 int launch_quantize_rows_i8(const void* x, int x_dtype, int64_t m, int64_t k, float in_scale,
                             int8_t* codes, float* row_scale, cudaStream_t stream);
-int launch_q8_0_encode(const float* w, int64_t n, int64_t k, int8_t* codes, uint16_t* scales,
-                       cudaStream_t stream);
-int launch_q8_0_unpack_blocks(const uint8_t* blocks, int64_t n, int64_t k, int8_t* codes,
-                              uint16_t* scales, cudaStream_t stream);
+// Q8_0 planes: codes [n, k]; scales [k/32, pitch] with pitch = round_up(n, 8)
+// so every scale row starts on a 16-byte boundary (TMA).
+int launch_q8_0_encode(const float* w, int64_t n, int64_t k, int64_t pitch, int8_t* codes,
+                       uint16_t* scales, cudaStream_t stream);
+int launch_q8_0_unpack_blocks(const uint8_t* blocks, int64_t n, int64_t k, int64_t pitch,
+                              int8_t* codes, uint16_t* scales, cudaStream_t stream);
 
 // Attention (attention.cu).
 struct AttnLaunch {
@@ -69,5 +80,7 @@ int launch_attention(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUten
 int make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t rows,
                  uint64_t cols, uint64_t row_stride_elems, uint32_t box_cols, uint32_t box_rows,
                  bool swizzle128);
+// Index of an N tile in the per-weight tensor-map caches ({256,128,96,64}).
+int bn_index(int bn);
 
 }  // namespace rb

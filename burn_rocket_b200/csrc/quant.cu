@@ -27,7 +27,8 @@ __device__ __forceinline__ float load_as_f32(const void* p, int dtype, int64_t i
 // One thread per 32-value block. d = f16(amax / 127); codes are rounded half
 // away from zero against the *stored* f16 scale and clamped to [-127, 127].
 __global__ void q8_0_encode_kernel(const float* __restrict__ w, int64_t n, int64_t k,
-                                   int8_t* __restrict__ codes, uint16_t* __restrict__ scales) {
+                                   int64_t pitch, int8_t* __restrict__ codes,
+                                   uint16_t* __restrict__ scales) {
   const int64_t nblk = k / 32;
   const int64_t total = n * nblk;
   for (int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; b < total;
@@ -44,42 +45,44 @@ __global__ void q8_0_encode_kernel(const float* __restrict__ w, int64_t n, int64
       const float r = roundf(__fmul_rn(seg[i], inv));  // half away from zero
       q[i] = static_cast<int8_t>(fminf(fmaxf(r, -127.0f), 127.0f));
     }
-    scales[row * nblk + g] = __half_as_ushort(d);
+    scales[g * pitch + row] = __half_as_ushort(d);  // k-block-major [K/32, pitch]
   }
 }
 
-int launch_q8_0_encode(const float* w, int64_t n, int64_t k, int8_t* codes, uint16_t* scales,
-                       cudaStream_t stream) {
+int launch_q8_0_encode(const float* w, int64_t n, int64_t k, int64_t pitch, int8_t* codes,
+                       uint16_t* scales, cudaStream_t stream) {
   const int64_t total = n * (k / 32);
   int64_t blocks = (total + 255) / 256;
   if (blocks > 65535) blocks = 65535;
   if (blocks < 1) blocks = 1;
-  q8_0_encode_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(w, n, k, codes, scales);
+  q8_0_encode_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(w, n, k, pitch, codes, scales);
   return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
 }
 
 // ---------------------------------------------------------------- GGUF unpack
 // Block b of row r holds bytes [0,2) = f16 scale (little endian), [2,34) = codes.
 __global__ void q8_0_unpack_kernel(const uint8_t* __restrict__ blocks, int64_t n, int64_t k,
-                                   int8_t* __restrict__ codes, uint16_t* __restrict__ scales) {
+                                   int64_t pitch, int8_t* __restrict__ codes,
+                                   uint16_t* __restrict__ scales) {
   const int64_t nblk = k / 32;
   const int64_t total = n * nblk;
   for (int64_t b = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; b < total;
        b += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const uint8_t* src = blocks + b * 34;
-    scales[b] = static_cast<uint16_t>(src[0] | (src[1] << 8));
+    const int64_t row = b / nblk, g = b % nblk;
+    scales[g * pitch + row] = static_cast<uint16_t>(src[0] | (src[1] << 8));  // [K/32, pitch]
     int8_t* dst = codes + b * 32;  // rows are contiguous runs of blocks
     for (int i = 0; i < 32; ++i) dst[i] = static_cast<int8_t>(src[2 + i]);
   }
 }
 
-int launch_q8_0_unpack_blocks(const uint8_t* blocks, int64_t n, int64_t k, int8_t* codes,
-                              uint16_t* scales, cudaStream_t stream) {
+int launch_q8_0_unpack_blocks(const uint8_t* blocks, int64_t n, int64_t k, int64_t pitch,
+                              int8_t* codes, uint16_t* scales, cudaStream_t stream) {
   const int64_t total = n * (k / 32);
   int64_t grid = (total + 255) / 256;
   if (grid > 65535) grid = 65535;
   if (grid < 1) grid = 1;
-  q8_0_unpack_kernel<<<static_cast<int>(grid), 256, 0, stream>>>(blocks, n, k, codes, scales);
+  q8_0_unpack_kernel<<<static_cast<int>(grid), 256, 0, stream>>>(blocks, n, k, pitch, codes, scales);
   return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
 }
 
