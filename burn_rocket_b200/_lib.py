@@ -61,6 +61,7 @@ SIGNATURES = {
     "rb_weight_info": (_i, [_i64, C.POINTER(_i), C.POINTER(_i64), C.POINTER(_i64)]),
     "rb_matmul": (_i, [_i64, _p, _i, _i64, _i64, _p, _i, _p]),
     "rb_matmul_host": (_i, [_i64, _p, _i, _i64, _i64, _p, _i]),
+    "rb_matmul_w8a8_noalloc": (_i, [_i64, _p, _i, _i64, _i64, _p, _i, _p]),
     "rb_attention": (_i, [_p, _p, _p, _p, _i, _i64, _i64, _i, _i, _i, _f, _f, _i, _i64, _i64, _i64, _p]),
     "rb_attention_host": (_i, [_p, _p, _p, _p, _i, _i64, _i64, _i, _i, _i, _f, _f, _i, _i64, _i64, _i64]),
     "rb_q8_0_dequant": (_i, [_i64, _p, _i, _p]),

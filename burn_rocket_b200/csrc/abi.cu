@@ -181,6 +181,39 @@ static int ensure_engine(Engine** out) {
   return RB_OK;
 }
 
+// ------------------------------------------------------------------ internal accessors
+// Used by entry points that live in other translation units (noalloc.cu).
+int report_error(int rc, const char* msg) { return fail(rc, "%s", msg); }
+
+void count_launches(int n) { g_launches += n; }
+
+bool make_output_map(CUtensorMap* map, void* y, int y_dtype, int64_t m, int64_t n) {
+  return output_map(map, y, y_dtype, m, n);
+}
+
+int w8a8_view(int64_t id, W8A8View* v) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Engine* e;
+  int rc = ensure_engine(&e);
+  if (rc) return rc;
+  auto it = e->weights.find(id);
+  if (it == e->weights.end() || it->second.kind != RB_WEIGHT_W8A8)
+    return fail(RB_E_SHAPE, "weight id %lld is not a W8A8 weight", (long long)id);
+  const Weight& w = it->second;
+  v->codes = w.codes;
+  v->w_scale = reinterpret_cast<const float*>(w.scales);
+  v->n = w.n;
+  v->k = w.k;
+  v->in_scale = w.in_scale;
+  v->out_scale = w.out_scale;
+  v->tm_codes[0] = w.tm_codes[0];
+  v->tm_codes[1] = w.tm_codes[1];
+  v->err = e->err;
+  v->num_sms = e->num_sms;
+  v->device = e->device;
+  return RB_OK;
+}
+
 static size_t dtype_bytes(int dt) {
   switch (dt) {
     case RB_DTYPE_F32: return 4;

@@ -83,4 +83,22 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t ro
 // Index of an N tile in the per-weight tensor-map caches ({256,128,96,64}).
 int bn_index(int bn);
 
+// Engine accessors for entry points in other translation units (abi.cu).
+int report_error(int rc, const char* msg);  // records rb_last_error, returns rc
+void count_launches(int n);
+bool make_output_map(CUtensorMap* map, void* y, int y_dtype, int64_t m, int64_t n);
+struct W8A8View {
+  const int8_t* codes;     // [n, k]
+  const float* w_scale;    // [n]
+  int64_t n, k;
+  float in_scale, out_scale;
+  CUtensorMap tm_codes[2];  // box heights 256 / 128
+  uint32_t* err;
+  int num_sms;
+  int device;
+};
+// Copies out what a W8A8 matmul needs of packed weight `id` (engine lock held
+// for the copy only; weights are never freed).
+int w8a8_view(int64_t id, W8A8View* v);
+
 }  // namespace rb

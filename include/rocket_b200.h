@@ -119,6 +119,21 @@ RB_API int rb_matmul(int64_t id, const void* x, int x_dtype, int64_t m, int64_t 
 RB_API int rb_matmul_host(int64_t id, const void* x_host, int x_dtype, int64_t m, int64_t k,
                    void* y_host, int y_dtype);
 
+/* rb_matmul for a W8A8 weight that allocates nothing. No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory in the
+ * middle of their work, such as code running while a CUDA graph is being
+ * captured, code under a fixed device-memory budget or custom allocator, or
+ * latency-critical paths that cannot take a synchronising cudaMalloc. The
+ * int8 activation codes and row scales that rb_matmul stages in growable
+ * engine scratch go instead to one file-scope device array of 32 MiB per GPU
+ * (held until process exit); calls needing more than round_up(m*k, 256) +
+ * 4*m <= 32 MiB are rejected with RB_E_SHAPE. The first call on a device
+ * resolves that array's address, so make it before any stream capture. All
+ * calls share the array: calls whose work overlaps on the GPU race and must
+ * be serialised by the caller. Results equal rb_matmul's bit for bit. */
+RB_API int rb_matmul_w8a8_noalloc(int64_t id, const void* x, int x_dtype, int64_t m, int64_t k,
+                                  void* y, int y_dtype, void* stream);
+
 /* ---- attention */
 
 /* Masked grouped-query attention (ext.rs:1669-1858, attention_impl):
