@@ -64,6 +64,18 @@ SIGNATURES = {
     "rb_matmul_w8a8_noalloc": (_i, [_i64, _p, _i, _i64, _i64, _p, _i, _p]),
     "rb_attention": (_i, [_p, _p, _p, _p, _i, _i64, _i64, _i, _i, _i, _f, _f, _i, _i64, _i64, _i64, _p]),
     "rb_attention_host": (_i, [_p, _p, _p, _p, _i, _i64, _i64, _i, _i, _i, _f, _f, _i, _i64, _i64, _i64]),
+    "rb_pack_f32_q8_0_device": (_i64, [C.POINTER(_p), C.POINTER(_i64), _i, _i64]),
+    "rb_attention_batched": (_i, [_p, _i64, _p, _i64, _p, _i64, _p, _i64, _i, _i64, _i64, _i64, _i, _i, _i, _f, _f,
+                                  _i, _i64, _i64, _i64, _p]),
+    "rb_rms_norm": (_i, [_p, _i, _p, _f, _p, _i, _i64, _i64, _p]),
+    "rb_silu_mul": (_i, [_p, _p, _i, _p, _i64, _p]),
+    "rb_gelu_mul": (_i, [_p, _p, _i, _p, _i64, _p]),
+    "rb_rope": (_i, [_p, _i, _p, _p, _p, _i64, _i64, _i, _i, _p]),
+    "rb_embed_gather": (_i, [_p, _i64, _p, _i64, _i64, _p, _p]),
+    "rb_add_rms_norm": (_i, [_p, _p, _p, _f, _p, _i64, _i64, _p]),
+    "rb_qk_norm_rope": (_i, [_p, _i64, _i64, _i, _i, _i, _p, _p, _f, _p, _p, _i64, _p]),
+    "rb_silu_mul_halves": (_i, [_p, _i64, _i64, _p, _p]),
+    "rb_last_token_l2": (_i, [_p, _i64, _i64, _i64, _p, _f, _p, _p]),
     "rb_q8_0_dequant": (_i, [_i64, _p, _i, _p]),
     "rb_quantize_rows_i8": (_i, [_p, _i, _i64, _i64, _p, _p, _p]),
     "rb_matmul_i8_acc": (_i, [_i64, _p, _i64, _p, _p]),

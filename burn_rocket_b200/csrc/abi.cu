@@ -292,15 +292,16 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
   return fail(RB_E_UNSUPPORTED, "weight kind %d", w.kind);
 }
 
-static int attention_locked(Engine* e, const void* q, const void* k, const void* v, void* out,
-                            int dtype, int64_t n_q, int64_t n_kv, int n_head, int n_kv_heads,
-                            int head_dim, float scale, float softcap, int mask_mode,
-                            int64_t window, int64_t q_start, int64_t kv_start, cudaStream_t st) {
+static int attention_locked(Engine* e, const void* q, int64_t ldq, const void* k, int64_t ldk,
+                            const void* v, int64_t ldv, void* out, int64_t ldo, int dtype,
+                            int64_t batch, int64_t n_q, int64_t n_kv, int n_head, int n_kv_heads,
+                            int head_dim, float scale, float softcap, int mask_mode, int64_t window,
+                            int64_t q_start, int64_t kv_start, cudaStream_t st) {
   // Contract of check_flash (attn/mod.rs:1424-1460) and attention_impl
   // (ext.rs:1680-1712).
-  if (n_q <= 0 || n_kv <= 0 || head_dim <= 0)
-    return fail(RB_E_SHAPE, "flash_attn/dims: n_q=%lld n_kv=%lld head_dim=%d", (long long)n_q,
-                (long long)n_kv, head_dim);
+  if (n_q <= 0 || n_kv <= 0 || head_dim <= 0 || batch <= 0)
+    return fail(RB_E_SHAPE, "flash_attn/dims: n_q=%lld n_kv=%lld head_dim=%d batch=%lld",
+                (long long)n_q, (long long)n_kv, head_dim, (long long)batch);
   if (n_head <= 0 || n_kv_heads <= 0 || n_head % n_kv_heads != 0)
     return fail(RB_E_SHAPE, "flash_attn/heads: n_head=%d n_kv_heads=%d", n_head, n_kv_heads);
   if (head_dim != 64 && head_dim != 128)
@@ -312,7 +313,10 @@ static int attention_locked(Engine* e, const void* q, const void* k, const void*
   if (!block && n_q != n_kv)
     return fail(RB_E_SHAPE, "the full-sequence mask modes need equal query/key lengths (%lld vs %lld)",
                 (long long)n_q, (long long)n_kv);
-  if (n_q > (1 << 29) || n_kv > (1 << 29)) return fail(RB_E_SHAPE, "sequence too long");
+  if (batch * n_q > (1 << 30) || batch * n_kv > (1 << 30)) return fail(RB_E_SHAPE, "sequence too long");
+  if (ldq < (int64_t)n_head * head_dim || ldo < (int64_t)n_head * head_dim ||
+      ldk < (int64_t)n_kv_heads * head_dim || ldv < (int64_t)n_kv_heads * head_dim)
+    return fail(RB_E_SHAPE, "flash_attn/buffers: row strides shorter than heads * head_dim");
   // Windowed modes with window < 0 fall back to their unwindowed form
   // (ext.rs:672-677, 693-698, 717-727).
   if (mask_mode == RB_MASK_WINDOW && window < 0) mask_mode = RB_MASK_NONE;
@@ -327,11 +331,14 @@ static int attention_locked(Engine* e, const void* q, const void* k, const void*
   const void* vh = v;
   void* oh = out;
   int kdt = dtype;
+  const int64_t wq = (int64_t)n_head * head_dim, wk = (int64_t)n_kv_heads * head_dim;
   if (dtype == RB_DTYPE_F32) {
     // f32 tensors (the Burn boundary) are rounded to f16 like fill_heads
     // (ext.rs:2174-2190), and the f16 result widened on the way out.
-    const size_t nq = static_cast<size_t>(n_q) * n_head * head_dim;
-    const size_t nk = static_cast<size_t>(n_kv) * n_kv_heads * head_dim;
+    if (ldq != wq || ldk != wk || ldv != wk || ldo != wq)
+      return fail(RB_E_UNSUPPORTED, "f32 attention needs contiguous [S, heads*d] tensors");
+    const size_t nq = static_cast<size_t>(batch * n_q) * wq;
+    const size_t nk = static_cast<size_t>(batch * n_kv) * wk;
     const size_t a16 = (nq * 2 + 255) & ~size_t(255), k16 = (nk * 2 + 255) & ~size_t(255);
     if ((rc = e->act.grow(2 * a16 + 2 * k16, "attention f16 staging")) != RB_OK) return rc;
     uint8_t* base = reinterpret_cast<uint8_t*>(e->act.ptr);
@@ -349,25 +356,25 @@ static int attention_locked(Engine* e, const void* q, const void* k, const void*
     return fail(RB_E_SHAPE, "attention dtype %d", dtype);
   }
   CUtensorMap tq, tk, tv;
-  const uint64_t ldq = static_cast<uint64_t>(n_head) * head_dim;
-  const uint64_t ldk = static_cast<uint64_t>(n_kv_heads) * head_dim;
-  if ((rc = make_tmap_2d(&tq, qh, 2, n_q, ldq, ldq, 64, 128, true)) != RB_OK) return rc;
   // Q tiles are 128 query rows, K/V tiles 64 keys; 64-element (128-B) columns.
-  if ((rc = make_tmap_2d(&tk, kh, 2, n_kv, ldk, ldk, 64, 64, true)) != RB_OK) return rc;
-  if ((rc = make_tmap_2d(&tv, vh, 2, n_kv, ldk, ldk, 64, 64, true)) != RB_OK) return rc;
-  if ((reinterpret_cast<uintptr_t>(oh) & 15) != 0)
+  if ((rc = make_tmap_2d(&tq, qh, 2, batch * n_q, wq, ldq, 64, 128, true)) != RB_OK) return rc;
+  if ((rc = make_tmap_2d(&tk, kh, 2, batch * n_kv, wk, ldk, 64, 64, true)) != RB_OK) return rc;
+  if ((rc = make_tmap_2d(&tv, vh, 2, batch * n_kv, wk, ldv, 64, 64, true)) != RB_OK) return rc;
+  if ((reinterpret_cast<uintptr_t>(oh) & 15) != 0 || (ldo * 2) % 16 != 0)
     return fail(RB_E_SHAPE, "attention output must be 16-byte aligned");
   AttnLaunch L{};
   L.q = qh; L.k = kh; L.v = vh; L.out = oh;
   L.dtype = kdt;
+  L.batch = static_cast<int>(batch);
   L.n_q = static_cast<int>(n_q);
   L.n_kv = static_cast<int>(n_kv);
   L.n_head = n_head;
   L.n_kv_heads = n_kv_heads;
   L.head_dim = head_dim;
   L.ldq = static_cast<int>(ldq);
-  L.ldk = L.ldv = static_cast<int>(ldk);
-  L.ldo = static_cast<int>(ldq);
+  L.ldk = static_cast<int>(ldk);
+  L.ldv = static_cast<int>(ldv);
+  L.ldo = static_cast<int>(ldo);
   L.scale = scale;
   L.softcap = softcap;
   L.mask_mode = mask_mode;
@@ -379,7 +386,7 @@ static int attention_locked(Engine* e, const void* q, const void* k, const void*
   if ((rc = launch_attention(tq, tk, tv, L, st)) != RB_OK) return fail(rc, "attention launch failed");
   g_launches++;
   if (dtype == RB_DTYPE_F32) {
-    if ((rc = launch_cast(oh, RB_DTYPE_F16, out, RB_DTYPE_F32, static_cast<int64_t>(n_q) * ldq, st)) != RB_OK)
+    if ((rc = launch_cast(oh, RB_DTYPE_F16, out, RB_DTYPE_F32, batch * n_q * wq, st)) != RB_OK)
       return fail(rc, "cast out");
     g_launches++;
   }
@@ -486,8 +493,8 @@ int64_t rb_pack_q8_0(const void* blocks_host, int64_t n, int64_t k) {
   return id;
 }
 
-int64_t rb_pack_f32_q8_0(const float* const* parts_host, const int64_t* n_parts, int num_parts,
-                         int64_t k) {
+static int64_t pack_f32_q8_0_impl(const float* const* parts_host, const int64_t* n_parts, int num_parts,
+                                  int64_t k, cudaMemcpyKind kind) {
   std::lock_guard<std::mutex> lk(g_mu);
   Engine* e;
   int rc = ensure_engine(&e);
@@ -517,8 +524,8 @@ int64_t rb_pack_f32_q8_0(const float* const* parts_host, const int64_t* n_parts,
   }
   int64_t off = 0;
   for (int i = 0; i < num_parts; ++i) {
-    RB_CUDA(cudaMemcpy(dw + off * k, parts_host[i], static_cast<size_t>(n_parts[i]) * k * 4,
-                       cudaMemcpyHostToDevice), "weight upload");
+    RB_CUDA(cudaMemcpy(dw + off * k, parts_host[i], static_cast<size_t>(n_parts[i]) * k * 4, kind),
+            "weight upload");
     off += n_parts[i];
   }
   cudaMemset(w.scales, 0, sbytes);
@@ -532,6 +539,16 @@ int64_t rb_pack_f32_q8_0(const float* const* parts_host, const int64_t* n_parts,
   const int64_t id = e->next_id++;
   e->weights[id] = w;
   return id;
+}
+
+int64_t rb_pack_f32_q8_0(const float* const* parts_host, const int64_t* n_parts, int num_parts,
+                         int64_t k) {
+  return pack_f32_q8_0_impl(parts_host, n_parts, num_parts, k, cudaMemcpyHostToDevice);
+}
+
+int64_t rb_pack_f32_q8_0_device(const float* const* parts_dev, const int64_t* n_parts, int num_parts,
+                                int64_t k) {
+  return pack_f32_q8_0_impl(parts_dev, n_parts, num_parts, k, cudaMemcpyDeviceToDevice);
 }
 
 int64_t rb_pack_w8a8(const int8_t* codes_host, const float* w_scale_host, int64_t n, int64_t k,
@@ -624,8 +641,9 @@ int rb_attention(const void* q, const void* k, const void* v, void* out, int dty
   int rc = ensure_engine(&e);
   if (rc) return rc;
   if (!q || !k || !v || !out) return fail(RB_E_SHAPE, "null attention buffer");
-  return attention_locked(e, q, k, v, out, dtype, n_q, n_kv, n_head, n_kv_heads, head_dim, scale,
-                          softcap, mask_mode, window, q_start, kv_start,
+  const int64_t wq = (int64_t)n_head * head_dim, wk = (int64_t)n_kv_heads * head_dim;
+  return attention_locked(e, q, wq, k, wk, v, wk, out, wq, dtype, 1, n_q, n_kv, n_head, n_kv_heads,
+                          head_dim, scale, softcap, mask_mode, window, q_start, kv_start,
                           reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -650,13 +668,123 @@ int rb_attention_host(const void* q, const void* k, const void* v, void* out, in
   RB_CUDA(cudaMemcpyAsync(e->io_in.ptr, q, qb, cudaMemcpyHostToDevice, st), "H2D q");
   RB_CUDA(cudaMemcpyAsync(e->io_k.ptr, k, kb, cudaMemcpyHostToDevice, st), "H2D k");
   RB_CUDA(cudaMemcpyAsync(e->io_v.ptr, v, kb, cudaMemcpyHostToDevice, st), "H2D v");
-  if ((rc = attention_locked(e, e->io_in.ptr, e->io_k.ptr, e->io_v.ptr, e->io_out.ptr, dtype, n_q,
-                             n_kv, n_head, n_kv_heads, head_dim, scale, softcap, mask_mode, window,
-                             q_start, kv_start, st)) != RB_OK)
+  const int64_t wq = (int64_t)n_head * head_dim, wk = (int64_t)n_kv_heads * head_dim;
+  if ((rc = attention_locked(e, e->io_in.ptr, wq, e->io_k.ptr, wk, e->io_v.ptr, wk, e->io_out.ptr, wq,
+                             dtype, 1, n_q, n_kv, n_head, n_kv_heads, head_dim, scale, softcap,
+                             mask_mode, window, q_start, kv_start, st)) != RB_OK)
     return rc;
   RB_CUDA(cudaMemcpyAsync(out, e->io_out.ptr, qb, cudaMemcpyDeviceToHost, st), "D2H out");
   RB_CUDA(cudaStreamSynchronize(st), "attention sync");
   return RB_OK;
+}
+
+int rb_attention_batched(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
+                         int64_t ldv, void* out, int64_t ldo, int dtype, int64_t batch, int64_t n_q,
+                         int64_t n_kv, int n_head, int n_kv_heads, int head_dim, float scale,
+                         float softcap, int mask_mode, int64_t window, int64_t q_start,
+                         int64_t kv_start, void* stream) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Engine* e;
+  int rc = ensure_engine(&e);
+  if (rc) return rc;
+  if (!q || !k || !v || !out) return fail(RB_E_SHAPE, "null attention buffer");
+  return attention_locked(e, q, ldq, k, ldk, v, ldv, out, ldo, dtype, batch, n_q, n_kv, n_head,
+                          n_kv_heads, head_dim, scale, softcap, mask_mode, window, q_start, kv_start,
+                          reinterpret_cast<cudaStream_t>(stream));
+}
+
+// ---- glue
+static bool valid_dtype(int dt) { return dt >= RB_DTYPE_F32 && dt <= RB_DTYPE_BF16; }
+
+int rb_rms_norm(const void* x, int x_dtype, const float* w, float eps, void* y, int y_dtype,
+                int64_t rows, int64_t d, void* stream) {
+  if (!x || !y || rows <= 0 || d <= 0 || !valid_dtype(x_dtype) || !valid_dtype(y_dtype))
+    return fail(RB_E_SHAPE, "rms_norm: bad arguments");
+  const int rc = launch_rms_norm(x, x_dtype, w, eps, y, y_dtype, rows, static_cast<int>(d),
+                                 reinterpret_cast<cudaStream_t>(stream));
+  g_launches++;
+  return rc == RB_OK ? RB_OK : fail(rc, "rms_norm launch failed");
+}
+
+static int gated_entry(int act, const void* gate, const void* up, int dtype, void* out, int64_t count,
+                       void* stream) {
+  if (!gate || !up || !out || count <= 0 || !valid_dtype(dtype))
+    return fail(RB_E_SHAPE, "gated activation: bad arguments");
+  const int rc = launch_gated(act, gate, up, dtype, count, count, out, dtype, count, 1, count,
+                              reinterpret_cast<cudaStream_t>(stream));
+  g_launches++;
+  return rc == RB_OK ? RB_OK : fail(rc, "gated activation launch failed");
+}
+
+int rb_silu_mul(const void* gate, const void* up, int dtype, void* out, int64_t count, void* stream) {
+  return gated_entry(0, gate, up, dtype, out, count, stream);
+}
+
+int rb_gelu_mul(const void* gate, const void* up, int dtype, void* out, int64_t count, void* stream) {
+  return gated_entry(1, gate, up, dtype, out, count, stream);
+}
+
+int rb_rope(const void* x, int dtype, const float* cos_t, const float* sin_t, void* y, int64_t batch,
+            int64_t seq, int heads, int head_dim, void* stream) {
+  if (!x || !y || !cos_t || !sin_t || batch <= 0 || seq <= 0 || heads <= 0 || head_dim <= 0 ||
+      head_dim % 2 || !valid_dtype(dtype))
+    return fail(RB_E_SHAPE, "rope: bad arguments (x must be [B, S, H, D], D even)");
+  const int rc = launch_rope(x, dtype, cos_t, sin_t, y, batch * seq, heads, head_dim,
+                             static_cast<int>(seq), reinterpret_cast<cudaStream_t>(stream));
+  g_launches++;
+  return rc == RB_OK ? RB_OK : fail(rc, "rope launch failed");
+}
+
+int rb_embed_gather(const int32_t* ids, int64_t tokens, const void* table_f16, int64_t vocab, int64_t d,
+                    float* x, void* stream) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Engine* e;
+  int rc = ensure_engine(&e);
+  if (rc) return rc;
+  if (!ids || !table_f16 || !x || tokens <= 0 || vocab <= 0 || d <= 0 || d % 8)
+    return fail(RB_E_SHAPE, "embed_gather: bad arguments");
+  rc = launch_embed_gather(ids, table_f16, vocab, static_cast<int>(d), x, tokens, e->err,
+                           reinterpret_cast<cudaStream_t>(stream));
+  g_launches++;
+  return rc == RB_OK ? RB_OK : fail(rc, "embed_gather launch failed");
+}
+
+int rb_add_rms_norm(float* x, const void* delta_f16, const float* w, float eps, void* h_f16,
+                    int64_t rows, int64_t d, void* stream) {
+  if (!x || !w || !h_f16 || rows <= 0) return fail(RB_E_SHAPE, "add_rms_norm: bad arguments");
+  const int rc = launch_add_rms_norm(x, delta_f16, w, eps, h_f16, rows, static_cast<int>(d),
+                                     reinterpret_cast<cudaStream_t>(stream));
+  g_launches++;
+  return rc == RB_OK ? RB_OK : fail(rc, "add_rms_norm: unsupported width %lld", (long long)d);
+}
+
+int rb_qk_norm_rope(void* qkv_f16, int64_t ld, int64_t tokens, int n_q_heads, int n_kv_heads,
+                    int head_dim, const float* q_norm_w, const float* k_norm_w, float eps,
+                    const float* cos_t, const float* sin_t, int64_t seq, void* stream) {
+  if (!qkv_f16 || !q_norm_w || !k_norm_w || !cos_t || !sin_t || tokens <= 0 || seq <= 0)
+    return fail(RB_E_SHAPE, "qk_norm_rope: bad arguments");
+  if (head_dim != 128) return fail(RB_E_UNSUPPORTED, "qk_norm_rope: head_dim %d (supported: 128)", head_dim);
+  const int rc = launch_qk_norm_rope(qkv_f16, ld, tokens, n_q_heads, n_kv_heads, q_norm_w, k_norm_w, eps,
+                                     cos_t, sin_t, static_cast<int>(seq),
+                                     reinterpret_cast<cudaStream_t>(stream));
+  g_launches++;
+  return rc == RB_OK ? RB_OK : fail(rc, "qk_norm_rope launch failed");
+}
+
+int rb_silu_mul_halves(const void* gu_f16, int64_t rows, int64_t n, void* out_f16, void* stream) {
+  if (!gu_f16 || !out_f16 || rows <= 0 || n <= 0) return fail(RB_E_SHAPE, "silu_mul_halves: bad arguments");
+  const int rc = launch_silu_mul_halves_f16(gu_f16, rows, n, out_f16, reinterpret_cast<cudaStream_t>(stream));
+  g_launches++;
+  return rc == RB_OK ? RB_OK : fail(rc, "silu_mul_halves: n must be a multiple of 8");
+}
+
+int rb_last_token_l2(const float* x, int64_t batch, int64_t seq, int64_t d, const float* w, float eps,
+                     float* out, void* stream) {
+  if (!x || !w || !out || batch <= 0 || seq <= 0 || d <= 0) return fail(RB_E_SHAPE, "last_token_l2: bad arguments");
+  const int rc = launch_last_token_l2(x, static_cast<int>(d), static_cast<int>(seq), static_cast<int>(batch), w,
+                                      eps, out, reinterpret_cast<cudaStream_t>(stream));
+  g_launches++;
+  return rc == RB_OK ? RB_OK : fail(rc, "last_token_l2 launch failed");
 }
 
 int rb_q8_0_dequant(int64_t id, void* out, int out_dtype, void* stream) {

@@ -67,6 +67,8 @@ struct Params {
   float softcap;
   int dlo, dhi;        // visible iff dlo <= (k_off + j) - (q_off + i) <= dhi
   int q_off, k_off;
+  // Sequences lie back to back: sequence b (blockIdx.y) owns query rows
+  // [b*n_q, (b+1)*n_q) and key rows [b*n_kv, (b+1)*n_kv) of the tensors.
   uint32_t* err;
 };
 
@@ -165,6 +167,8 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int q_row0 = blockIdx.y * p.n_q;    // this sequence's first query row
+  const int kv_row0 = blockIdx.y * p.n_kv;  // and first key row
 
   // Work item: heavy (late) query tiles first so causal runs finish together.
   const int g = blockIdx.x % p.n_kv_heads;
@@ -214,7 +218,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       for (int s = 0; s < nslots; ++s)
         for (int a = 0; a < L::ATOMS; ++a)
           tma_load_2d(smem + L::Q_OFF + s * L::Q_TILE + a * L::Q_ATOM, &tmQ, q_full,
-                      sl[s].head * D + a * 64, sl[s].qt * BM);
+                      sl[s].head * D + a * 64, q_row0 + sl[s].qt * BM);
       for (int j = J0; j <= J1; ++j) {
         const int jl = j - J0, st = jl % KV_STAGES;
         const uint32_t ph = ((jl / KV_STAGES) & 1) ^ 1;
@@ -222,12 +226,12 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         mbar_arrive_expect_tx(&k_full[st], L::KV_TILE);
         for (int a = 0; a < L::ATOMS; ++a)
           tma_load_2d(smem + L::K_OFF + st * L::KV_TILE + a * L::KV_ATOM, &tmK, &k_full[st],
-                      g * D + a * 64, j * BN);
+                      g * D + a * 64, kv_row0 + j * BN);
         if (!mbar_wait(&v_empty[st], ph, p.err, abort_flag)) break;
         mbar_arrive_expect_tx(&v_full[st], L::KV_TILE);
         for (int a = 0; a < L::ATOMS; ++a)
           tma_load_2d(smem + L::V_OFF + st * L::KV_TILE + a * L::KV_ATOM, &tmV, &v_full[st],
-                      g * D + a * 64, j * BN);
+                      g * D + a * 64, kv_row0 + j * BN);
       }
     }
   } else if (warp == 1) {
@@ -465,7 +469,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
               pk[i] = pack2<BF16>(__uint_as_float(r[2 * i]) * inv_l,
                                   __uint_as_float(r[2 * i + 1]) * inv_l);
             uint4* dst = reinterpret_cast<uint4*>(
-                reinterpret_cast<uint16_t*>(p.out) + static_cast<int64_t>(qrow) * p.ldo +
+                reinterpret_cast<uint16_t*>(p.out) + static_cast<int64_t>(q_row0 + qrow) * p.ldo +
                 me.head * D + c0);
 #pragma unroll
             for (int i = 0; i < 4; ++i)
@@ -487,7 +491,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
 
 template <int D, bool BF16, bool SOFTCAP>
 static int launch_impl(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
-                       const Params& p, int grid, cudaStream_t stream) {
+                       const Params& p, dim3 grid, cudaStream_t stream) {
   static uint64_t configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -503,7 +507,7 @@ static int launch_impl(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUt
 
 template <int D>
 static int launch_d(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
-                    const Params& p, int grid, bool bf16, cudaStream_t stream) {
+                    const Params& p, dim3 grid, bool bf16, cudaStream_t stream) {
   if (p.softcap != 0.0f)
     return bf16 ? launch_impl<D, true, true>(tmQ, tmK, tmV, p, grid, stream)
                 : launch_impl<D, false, true>(tmQ, tmK, tmV, p, grid, stream);
@@ -566,7 +570,7 @@ int launch_attention(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUten
     default:
       return RB_E_SHAPE;
   }
-  const int grid = p.pairs_per_group * L.n_kv_heads;
+  const dim3 grid(p.pairs_per_group * L.n_kv_heads, L.batch > 0 ? L.batch : 1);
   const bool bf16 = L.dtype == RB_DTYPE_BF16;
   if (L.head_dim == 128) return launch_d<128>(tmQ, tmK, tmV, p, grid, bf16, stream);
   if (L.head_dim == 64) return launch_d<64>(tmQ, tmK, tmV, p, grid, bf16, stream);

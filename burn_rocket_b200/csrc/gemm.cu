@@ -47,13 +47,13 @@ enum class BSrc { Tma, Q8Dequant };
 
 constexpr int round1k(int x) { return (x + 1023) & ~1023; }
 
-template <int BN_, int LSTAGES_, bool I8_>
+template <int BN_, int LSTAGES_, bool I8_, int BSTAGES_ = 2>
 struct GemmCfg {
   static constexpr int BN = BN_;
   static constexpr int LSTAGES = LSTAGES_;          // TMA load ring depth
   static constexpr bool I8 = I8_;
   static constexpr bool Q8 = !I8;
-  static constexpr int BSTAGES = 2;                 // dequantised B ring (Q8_0)
+  static constexpr int BSTAGES = BSTAGES_;          // dequantised B ring (Q8_0)
   static constexpr int ELEM = I8 ? 1 : 2;
   static constexpr int BK = 128 / ELEM;             // K elements per stage (one 128-B atom)
   static constexpr int UMMA_K = I8 ? 32 : 16;
@@ -69,7 +69,7 @@ struct GemmCfg {
   static constexpr int EPI_OFF = BRING_OFF + BRING;
   static constexpr int EPI_BYTES = kNumEpiWarps * 2 * kEpiBufBytes;
   static constexpr int BAR_OFF = EPI_OFF + EPI_BYTES;
-  static constexpr int SMEM_BYTES = BAR_OFF + 256 + 1024;
+  static constexpr int SMEM_BYTES = BAR_OFF + 384 + 1024;
   static constexpr int NUM_WARPS = Q8 ? (kDqWarp0 + kNumDqWarps) : 6;
   static constexpr int THREADS = NUM_WARPS * 32;
   static constexpr uint32_t TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64
@@ -168,9 +168,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::BAR_OFF);
   uint64_t* load_full = bars;                       // [LSTAGES] TMA bytes
   uint64_t* load_empty = bars + LSTAGES;            // [LSTAGES] UMMA (+ dequant warps)
-  uint64_t* b_full = bars + 2 * LSTAGES;            // [2] dequant warps (Q8_0)
-  uint64_t* b_empty = b_full + 2;                   // [2] UMMA (Q8_0)
-  uint64_t* acc_full = b_empty + 2;                 // [2]
+  uint64_t* b_full = bars + 2 * LSTAGES;            // [BSTAGES] dequant warps (Q8_0)
+  uint64_t* b_empty = b_full + Cfg::BSTAGES;        // [BSTAGES] UMMA (Q8_0)
+  uint64_t* acc_full = b_empty + Cfg::BSTAGES;      // [2]
   uint64_t* acc_empty = acc_full + 2;               // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -188,9 +188,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       mbar_init(&load_full[s], 1);
       mbar_init(&load_empty[s], Cfg::Q8 ? 1 + kNumDqWarps : 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < Cfg::BSTAGES; ++i) {
       mbar_init(&b_full[i], kNumDqWarps);
       mbar_init(&b_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], kNumEpiWarps);
     }
@@ -433,10 +435,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 // --------------------------------------------------------------------------
 // Host-side launch.
 
-using CfgQ8_256 = GemmCfg<256, 3, false>;
-using CfgQ8_128 = GemmCfg<128, 6, false>;
-using CfgQ8_96 = GemmCfg<96, 6, false>;
-using CfgQ8_64 = GemmCfg<64, 7, false>;
+// Q8_0: (BN, load-ring depth, dequantised-B-ring depth) sized to the smem budget.
+using CfgQ8_256 = GemmCfg<256, 3, false, 2>;
+using CfgQ8_128 = GemmCfg<128, 4, false, 4>;
+using CfgQ8_96 = GemmCfg<96, 4, false, 6>;
+using CfgQ8_64 = GemmCfg<64, 6, false, 6>;
 using CfgI8_256 = GemmCfg<256, 4, true>;
 using CfgI8_128 = GemmCfg<128, 6, true>;
 

@@ -1,0 +1,338 @@
+// glue.cu — the elementwise / normalisation ops around the matmuls.
+//
+// RocketOps glue surface (crates/burn-rocket/src/ext.rs:70-83, host formulas
+// in crates/burn-rocket/src/host.rs:15-72):
+//   rms_norm        x * (mean(x^2) + eps)^-0.5 * w          (host.rs:42-56)
+//   silu_mul        g * sigmoid(g) * u, sigmoid = 1/(1+exp(-g))  (host.rs:31-38)
+//   gelu_mul        0.5 g (1 + tanh(sqrt(2/pi)(g + 0.044715 g^3))) * u  (host.rs:15-27)
+//   rope            rotate-half with [S, D/2] cos/sin tables  (host.rs:61-72)
+// and the fused steps of the embedding-model forward:
+//   embed_gather    token ids -> f32 rows of an f16 table
+//   add_rms_norm    x += delta (f16); h = rms_norm(x) as f16  (residual + norm in one pass)
+//   qk_norm_rope    per-head RMSNorm then RoPE, in place on the q and k columns of a fused
+//                   q|k|v projection (src/qwen3_embedding/model.rs:355-381)
+//   last_token_l2   final RMSNorm of each sequence's last token, L2-normalised
+// One warp per row; f32 arithmetic; reductions are warp trees (the reference
+// sums sequentially, so sums agree to f32 rounding, not bit for bit).
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+
+#include "kernels.h"
+
+namespace rb {
+
+__device__ __forceinline__ float ld_f(const void* p, int dt, int64_t i) {
+  if (dt == RB_DTYPE_F32) return reinterpret_cast<const float*>(p)[i];
+  if (dt == RB_DTYPE_F16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
+  return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+}
+__device__ __forceinline__ void st_f(void* p, int dt, int64_t i, float v) {
+  if (dt == RB_DTYPE_F32) reinterpret_cast<float*>(p)[i] = v;
+  else if (dt == RB_DTYPE_F16) reinterpret_cast<__half*>(p)[i] = __float2half_rn(v);
+  else reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+static int grid_for_rows(int64_t rows, int warps_per_block) {
+  int64_t g = (rows + warps_per_block - 1) / warps_per_block;
+  if (g > 148 * 64) g = 148 * 64;
+  return static_cast<int>(g < 1 ? 1 : g);
+}
+
+// ---------------------------------------------------------------- rms_norm
+// Generic: one warp per row of length d; w may be null (scale-free form).
+__global__ void rms_norm_kernel(const void* x, int xdt, const float* w, float eps, void* y, int ydt,
+                                int64_t rows, int d) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += nw) {
+    const int64_t base = r * d;
+    float ss = 0.0f;
+    for (int i = lane; i < d; i += 32) {
+      const float v = ld_f(x, xdt, base + i);
+      ss = fmaf(v, v, ss);
+    }
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / static_cast<float>(d) + eps);
+    for (int i = lane; i < d; i += 32) {
+      const float v = ld_f(x, xdt, base + i) * inv;
+      st_f(y, ydt, base + i, w ? v * w[i] : v);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- gated activations
+__device__ __forceinline__ float silu_f(float g) { return g * (1.0f / (1.0f + expf(-g))); }
+__device__ __forceinline__ float gelu_tanh_f(float g) {
+  // sqrt(2/pi) as the f32 rounding of the f64 constant (host.rs:10-18).
+  const float k = 0.7978845608028654f;
+  const float inner = (g + g * g * g * 0.044715f) * k;
+  return (g * (tanhf(inner) + 1.0f)) * 0.5f;
+}
+
+// out[r, c] = act(a[r, c]) * b[r, c]; a and b may be two halves of one row
+// (lda / ldb strides), out has stride ldo.
+template <int ACT>
+__global__ void gated_kernel(const void* a, const void* b, int dt, int64_t lda, int64_t ldb,
+                             void* out, int odt, int64_t ldo, int64_t rows, int64_t cols) {
+  const int64_t total = rows * cols;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / cols, c = i % cols;
+    const float g = ld_f(a, dt, r * lda + c);
+    const float u = ld_f(b, dt, r * ldb + c);
+    const float v = ACT == 0 ? silu_f(g) * u : gelu_tanh_f(g) * u;
+    st_f(out, odt, r * ldo + c, v);
+  }
+}
+
+// f16 fast path for silu(gate) * up over the two halves of a gate|up row:
+// 8 elements per thread, 16-byte loads and stores.
+__global__ void silu_mul_halves_f16_kernel(const __half* gu, int64_t rows, int64_t n, __half* out) {
+  const int64_t n8 = n / 8;
+  const int64_t total = rows * n8;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / n8, c = (i % n8) * 8;
+    const uint4 g4 = *reinterpret_cast<const uint4*>(gu + r * 2 * n + c);
+    const uint4 u4 = *reinterpret_cast<const uint4*>(gu + r * 2 * n + n + c);
+    const __half2* g2 = reinterpret_cast<const __half2*>(&g4);
+    const __half2* u2 = reinterpret_cast<const __half2*>(&u4);
+    uint4 o4;
+    __half2* o2 = reinterpret_cast<__half2*>(&o4);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 g = __half22float2(g2[j]);
+      const float2 u = __half22float2(u2[j]);
+      o2[j] = __floats2half2_rn(silu_f(g.x) * u.x, silu_f(g.y) * u.y);
+    }
+    *reinterpret_cast<uint4*>(out + r * n + c) = o4;
+  }
+}
+
+// ---------------------------------------------------------------- rope
+// x [rows, heads, d] (any float dtype, in place allowed); row r uses table row
+// pos = (r / heads) % seq. out[j] = x[j] c - x[j+h] s ; out[j+h] = x[j+h] c + x[j] s.
+__global__ void rope_kernel(const void* x, int dt, const float* cos_t, const float* sin_t, void* y,
+                            int64_t rows, int heads, int d, int seq) {
+  const int half = d / 2;
+  const int64_t total = rows * heads * half;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t rh = i / half;
+    const int j = static_cast<int>(i % half);
+    const int64_t r = rh / heads;
+    const int pos = static_cast<int>(r % seq);
+    const int64_t base = rh * d;
+    const float x1 = ld_f(x, dt, base + j), x2 = ld_f(x, dt, base + half + j);
+    const float c = cos_t[pos * half + j], s = sin_t[pos * half + j];
+    st_f(y, dt, base + j, x1 * c - x2 * s);
+    st_f(y, dt, base + half + j, x2 * c + x1 * s);
+  }
+}
+
+// ---------------------------------------------------------------- fused forward steps
+// ids [T] -> x [T, d] f32 from an f16 table [vocab, d].
+__global__ void embed_gather_kernel(const int32_t* ids, const __half* table, int64_t vocab, int d,
+                                    float* x, int64_t rows, uint32_t* err) {
+  const int64_t total = rows * (d / 8);
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / (d / 8), c = (i % (d / 8)) * 8;
+    int64_t id = ids[r];
+    if (id < 0 || id >= vocab) {
+      atomicOr(err, 4u);  // kErrBadShape: token id outside the vocabulary
+      id = 0;
+    }
+    const uint4 h4 = *reinterpret_cast<const uint4*>(table + id * d + c);
+    const __half2* h2 = reinterpret_cast<const __half2*>(&h4);
+    float4 a, b;
+    float2 t;
+    t = __half22float2(h2[0]); a.x = t.x; a.y = t.y;
+    t = __half22float2(h2[1]); a.z = t.x; a.w = t.y;
+    t = __half22float2(h2[2]); b.x = t.x; b.y = t.y;
+    t = __half22float2(h2[3]); b.z = t.x; b.w = t.y;
+    float4* dst = reinterpret_cast<float4*>(x + r * d + c);
+    dst[0] = a;
+    dst[1] = b;
+  }
+}
+
+// x [rows, D] f32 (+= delta f16 when non-null), then h = rms_norm(x, w) f16.
+// One warp per row; D = 32 * 4 * NV (D % 128 == 0), values kept in registers.
+template <int NV>
+__global__ void add_rms_norm_kernel(float* x, const __half* delta, const float* w, float eps,
+                                    __half* h, int64_t rows) {
+  constexpr int D = 128 * NV;
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += nw) {
+    float v[4 * NV];
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = j * 128 + lane * 4;
+      float4 xv = *reinterpret_cast<const float4*>(x + r * D + c);
+      if (delta) {
+        const uint2 d2 = *reinterpret_cast<const uint2*>(delta + r * D + c);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&d2.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&d2.y));
+        xv.x += a.x; xv.y += a.y; xv.z += b.x; xv.w += b.y;
+        *reinterpret_cast<float4*>(x + r * D + c) = xv;
+      }
+      v[4 * j] = xv.x; v[4 * j + 1] = xv.y; v[4 * j + 2] = xv.z; v[4 * j + 3] = xv.w;
+      ss = fmaf(xv.x, xv.x, fmaf(xv.y, xv.y, fmaf(xv.z, xv.z, fmaf(xv.w, xv.w, ss))));
+    }
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = j * 128 + lane * 4;
+      const float4 wv = *reinterpret_cast<const float4*>(w + c);
+      const __half2 a = __floats2half2_rn(v[4 * j] * inv * wv.x, v[4 * j + 1] * inv * wv.y);
+      const __half2 b = __floats2half2_rn(v[4 * j + 2] * inv * wv.z, v[4 * j + 3] * inv * wv.w);
+      uint2 o;
+      o.x = *reinterpret_cast<const uint32_t*>(&a);
+      o.y = *reinterpret_cast<const uint32_t*>(&b);
+      *reinterpret_cast<uint2*>(h + r * D + c) = o;
+    }
+  }
+}
+
+// In place on qkv [T, ld] f16: heads [0, hq) of width 128 at column 0 (q) use
+// wq, heads [hq, hq+hk) (k) use wk. One warp per (token, head); lane l owns
+// elements 2l, 2l+1 and 64+2l, 64+2l+1 (the rotate-half pairs).
+__global__ void qk_norm_rope_kernel(__half* qkv, int64_t ld, int64_t tokens, int hq, int hk,
+                                    const float* wq, const float* wk, float eps,
+                                    const float* cos_t, const float* sin_t, int seq) {
+  const int lane = threadIdx.x & 31;
+  const int heads = hq + hk;
+  const int64_t items = tokens * heads;
+  const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t it = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); it < items; it += nw) {
+    const int64_t t = it / heads;
+    const int hd = static_cast<int>(it % heads);
+    __half* p = qkv + t * ld + static_cast<int64_t>(hd) * 128;
+    const float* w = hd < hq ? wq : wk;
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(p + 2 * lane));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(p + 64 + 2 * lane));
+    float ss = a.x * a.x + a.y * a.y + b.x * b.x + b.y * b.y;
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / 128.0f + eps);
+    const float a0 = a.x * inv * w[2 * lane], a1 = a.y * inv * w[2 * lane + 1];
+    const float b0 = b.x * inv * w[64 + 2 * lane], b1 = b.y * inv * w[64 + 2 * lane + 1];
+    const int pos = static_cast<int>(t % seq);
+    const float c0 = cos_t[pos * 64 + 2 * lane], c1 = cos_t[pos * 64 + 2 * lane + 1];
+    const float s0 = sin_t[pos * 64 + 2 * lane], s1 = sin_t[pos * 64 + 2 * lane + 1];
+    *reinterpret_cast<__half2*>(p + 2 * lane) = __floats2half2_rn(a0 * c0 - b0 * s0, a1 * c1 - b1 * s1);
+    *reinterpret_cast<__half2*>(p + 64 + 2 * lane) = __floats2half2_rn(b0 * c0 + a0 * s0, b1 * c1 + a1 * s1);
+  }
+}
+
+// out[b] = l2_normalise(rms_norm(x[b * seq + seq - 1], w)), one warp per sequence.
+__global__ void last_token_l2_kernel(const float* x, int d, int seq, int batch, const float* w,
+                                     float eps, float* out) {
+  const int lane = threadIdx.x & 31;
+  const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (b >= batch) return;
+  const float* row = x + (static_cast<int64_t>(b) * seq + seq - 1) * d;
+  float ss = 0.0f;
+  for (int i = lane; i < d; i += 32) ss = fmaf(row[i], row[i], ss);
+  ss = warp_sum(ss);
+  const float inv = 1.0f / sqrtf(ss / static_cast<float>(d) + eps);
+  float nn = 0.0f;
+  for (int i = lane; i < d; i += 32) {
+    const float v = row[i] * inv * w[i];
+    nn = fmaf(v, v, nn);
+  }
+  nn = warp_sum(nn);
+  const float inv2 = 1.0f / fmaxf(sqrtf(nn), 1e-12f);
+  for (int i = lane; i < d; i += 32) out[static_cast<int64_t>(b) * d + i] = row[i] * inv * w[i] * inv2;
+}
+
+// ---------------------------------------------------------------- launchers
+#define RB_LAUNCH_OK() (cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE)
+
+int launch_rms_norm(const void* x, int xdt, const float* w, float eps, void* y, int ydt, int64_t rows,
+                    int d, cudaStream_t st) {
+  rms_norm_kernel<<<grid_for_rows(rows, 8), 256, 0, st>>>(x, xdt, w, eps, y, ydt, rows, d);
+  return RB_LAUNCH_OK();
+}
+
+int launch_gated(int act, const void* a, const void* b, int dt, int64_t lda, int64_t ldb, void* out,
+                 int odt, int64_t ldo, int64_t rows, int64_t cols, cudaStream_t st) {
+  int64_t g = (rows * cols + 255) / 256;
+  if (g > 148 * 32) g = 148 * 32;
+  if (g < 1) g = 1;
+  if (act == 0)
+    gated_kernel<0><<<static_cast<int>(g), 256, 0, st>>>(a, b, dt, lda, ldb, out, odt, ldo, rows, cols);
+  else
+    gated_kernel<1><<<static_cast<int>(g), 256, 0, st>>>(a, b, dt, lda, ldb, out, odt, ldo, rows, cols);
+  return RB_LAUNCH_OK();
+}
+
+int launch_silu_mul_halves_f16(const void* gu, int64_t rows, int64_t n, void* out, cudaStream_t st) {
+  if (n % 8) return RB_E_SHAPE;
+  int64_t g = (rows * (n / 8) + 255) / 256;
+  if (g > 148 * 32) g = 148 * 32;
+  if (g < 1) g = 1;
+  silu_mul_halves_f16_kernel<<<static_cast<int>(g), 256, 0, st>>>(
+      reinterpret_cast<const __half*>(gu), rows, n, reinterpret_cast<__half*>(out));
+  return RB_LAUNCH_OK();
+}
+
+int launch_rope(const void* x, int dt, const float* cos_t, const float* sin_t, void* y, int64_t rows,
+                int heads, int d, int seq, cudaStream_t st) {
+  int64_t g = (rows * heads * (d / 2) + 255) / 256;
+  if (g > 148 * 32) g = 148 * 32;
+  if (g < 1) g = 1;
+  rope_kernel<<<static_cast<int>(g), 256, 0, st>>>(x, dt, cos_t, sin_t, y, rows, heads, d, seq);
+  return RB_LAUNCH_OK();
+}
+
+int launch_embed_gather(const int32_t* ids, const void* table, int64_t vocab, int d, float* x,
+                        int64_t rows, uint32_t* err, cudaStream_t st) {
+  if (d % 8) return RB_E_SHAPE;
+  int64_t g = (rows * (d / 8) + 255) / 256;
+  if (g > 148 * 32) g = 148 * 32;
+  if (g < 1) g = 1;
+  embed_gather_kernel<<<static_cast<int>(g), 256, 0, st>>>(
+      ids, reinterpret_cast<const __half*>(table), vocab, d, x, rows, err);
+  return RB_LAUNCH_OK();
+}
+
+int launch_add_rms_norm(float* x, const void* delta, const float* w, float eps, void* h, int64_t rows,
+                        int d, cudaStream_t st) {
+  const int grid = grid_for_rows(rows, 8);
+  const __half* dl = reinterpret_cast<const __half*>(delta);
+  __half* hh = reinterpret_cast<__half*>(h);
+  switch (d) {
+    case 1024: add_rms_norm_kernel<8><<<grid, 256, 0, st>>>(x, dl, w, eps, hh, rows); break;
+    case 2048: add_rms_norm_kernel<16><<<grid, 256, 0, st>>>(x, dl, w, eps, hh, rows); break;
+    case 1152: add_rms_norm_kernel<9><<<grid, 256, 0, st>>>(x, dl, w, eps, hh, rows); break;
+    default: return RB_E_UNSUPPORTED;
+  }
+  return RB_LAUNCH_OK();
+}
+
+int launch_qk_norm_rope(void* qkv, int64_t ld, int64_t tokens, int hq, int hk, const float* wq,
+                        const float* wk, float eps, const float* cos_t, const float* sin_t, int seq,
+                        cudaStream_t st) {
+  const int64_t items = tokens * (hq + hk);
+  qk_norm_rope_kernel<<<grid_for_rows(items, 8), 256, 0, st>>>(
+      reinterpret_cast<__half*>(qkv), ld, tokens, hq, hk, wq, wk, eps, cos_t, sin_t, seq);
+  return RB_LAUNCH_OK();
+}
+
+int launch_last_token_l2(const float* x, int d, int seq, int batch, const float* w, float eps,
+                         float* out, cudaStream_t st) {
+  last_token_l2_kernel<<<(batch + 7) / 8, 256, 0, st>>>(x, d, seq, batch, w, eps, out);
+  return RB_LAUNCH_OK();
+}
+
+}  // namespace rb

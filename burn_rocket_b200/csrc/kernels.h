@@ -63,7 +63,8 @@ struct AttnLaunch {
   const void* v;
   void* out;
   int dtype;  // RB_DTYPE_F16 or RB_DTYPE_BF16
-  int n_q, n_kv;
+  int batch;     // sequences laid back to back (>= 1)
+  int n_q, n_kv;  // per sequence
   int n_head, n_kv_heads, head_dim;
   int ldq, ldk, ldv, ldo;  // row strides in elements
   float scale, softcap;
@@ -74,6 +75,24 @@ struct AttnLaunch {
 };
 int launch_attention(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
                      const AttnLaunch& L, cudaStream_t stream);
+
+// Glue (glue.cu).
+int launch_rms_norm(const void* x, int xdt, const float* w, float eps, void* y, int ydt, int64_t rows,
+                    int d, cudaStream_t st);
+int launch_gated(int act, const void* a, const void* b, int dt, int64_t lda, int64_t ldb, void* out,
+                 int odt, int64_t ldo, int64_t rows, int64_t cols, cudaStream_t st);
+int launch_silu_mul_halves_f16(const void* gu, int64_t rows, int64_t n, void* out, cudaStream_t st);
+int launch_rope(const void* x, int dt, const float* cos_t, const float* sin_t, void* y, int64_t rows,
+                int heads, int d, int seq, cudaStream_t st);
+int launch_embed_gather(const int32_t* ids, const void* table, int64_t vocab, int d, float* x,
+                        int64_t rows, uint32_t* err, cudaStream_t st);
+int launch_add_rms_norm(float* x, const void* delta, const float* w, float eps, void* h, int64_t rows,
+                        int d, cudaStream_t st);
+int launch_qk_norm_rope(void* qkv, int64_t ld, int64_t tokens, int hq, int hk, const float* wq,
+                        const float* wk, float eps, const float* cos_t, const float* sin_t, int seq,
+                        cudaStream_t st);
+int launch_last_token_l2(const float* x, int d, int seq, int batch, const float* w, float eps,
+                         float* out, cudaStream_t st);
 
 // Tensor-map helper (abi.cu): 2D row-major [rows, cols] tile map with a
 // 128-byte swizzle; box = {box_cols, box_rows}.

@@ -92,6 +92,10 @@ RB_API int64_t rb_pack_q8_0(const void* blocks_host, int64_t n, int64_t k);
 RB_API int64_t rb_pack_f32_q8_0(const float* const* parts_host, const int64_t* n_parts,
                          int num_parts, int64_t k);
 
+/* rb_pack_f32_q8_0 with the f32 parts in DEVICE memory (same encoder). */
+RB_API int64_t rb_pack_f32_q8_0_device(const float* const* parts_dev, const int64_t* n_parts,
+                                       int num_parts, int64_t k);
+
 /* Per-output-channel int8 weight of a QAT checkpoint: codes [n, k] and
  * w_scale [n] in HOST memory. in_scale == 0 selects the dynamic per-row
  * activation scale max|x|/127; out_scale == 0 leaves the output unrounded.
@@ -154,6 +158,59 @@ RB_API int rb_attention_host(const void* q, const void* k, const void* v, void* 
                       int64_t n_q, int64_t n_kv, int n_head, int n_kv_heads, int head_dim,
                       float scale, float softcap, int mask_mode, int64_t window, int64_t q_start,
                       int64_t kv_start);
+
+/* Batched, strided form of rb_attention: `batch` sequences lie back to back
+ * (sequence b owns query rows [b*n_q, (b+1)*n_q) and key rows
+ * [b*n_kv, (b+1)*n_kv)); ldq/ldk/ldv/ldo are row strides in elements, so q, k
+ * and v can be column slices of one fused q|k|v projection (the NPU route's
+ * split of the fused matmul output, src/qwen3_embedding/model.rs:355-368).
+ * f16/bf16 only when strided. */
+RB_API int rb_attention_batched(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v,
+                                int64_t ldv, void* out, int64_t ldo, int dtype, int64_t batch,
+                                int64_t n_q, int64_t n_kv, int n_head, int n_kv_heads, int head_dim,
+                                float scale, float softcap, int mask_mode, int64_t window,
+                                int64_t q_start, int64_t kv_start, void* stream);
+
+/* ---- glue ops of the RocketOps surface (ext.rs:70-83, 1054-1152; formulas
+ * host.rs:15-72). Device buffers, any float dtype, asynchronous on `stream`. */
+
+/* rocket_rms_norm / rocket_rms_norm_noscale: y = x * (mean(x^2) + eps)^-0.5 * w
+ * over rows of length d; w == NULL is the scale-free form. */
+RB_API int rb_rms_norm(const void* x, int x_dtype, const float* w, float eps, void* y, int y_dtype,
+                       int64_t rows, int64_t d, void* stream);
+/* rocket_silu_mul: out = gate * sigmoid(gate) * up (host.rs:31-38). */
+RB_API int rb_silu_mul(const void* gate, const void* up, int dtype, void* out, int64_t count,
+                       void* stream);
+/* rocket_gelu_mul: out = gelu_tanh(gate) * up (host.rs:15-27). */
+RB_API int rb_gelu_mul(const void* gate, const void* up, int dtype, void* out, int64_t count,
+                       void* stream);
+/* rocket_rope: x [batch, seq, heads, head_dim], cos/sin f32 [seq, head_dim/2];
+ * rotate-half (host.rs:61-72). In place when y == x. */
+RB_API int rb_rope(const void* x, int dtype, const float* cos, const float* sin, void* y,
+                   int64_t batch, int64_t seq, int heads, int head_dim, void* stream);
+
+/* ---- fused steps of the embedding-model forward (src/qwen3_embedding/model.rs) */
+
+/* x[t, :] = f32(table[ids[t], :]) for an f16 table [vocab, d]; an id outside
+ * the vocabulary reads row 0 and flags the device error word. */
+RB_API int rb_embed_gather(const int32_t* ids, int64_t tokens, const void* table_f16, int64_t vocab,
+                           int64_t d, float* x, void* stream);
+/* x += delta (f16, NULL = none); h = rms_norm(x, w, eps) as f16. d in {1024, 1152, 2048}. */
+RB_API int rb_add_rms_norm(float* x, const void* delta_f16, const float* w, float eps, void* h_f16,
+                           int64_t rows, int64_t d, void* stream);
+/* In place on a fused q|k|v f16 buffer [tokens, ld]: per-head RMSNorm of the
+ * q heads (q_norm_w) and k heads (k_norm_w), then RoPE at position t % seq
+ * (model.rs:369-376). head_dim 128. */
+RB_API int rb_qk_norm_rope(void* qkv_f16, int64_t ld, int64_t tokens, int n_q_heads, int n_kv_heads,
+                           int head_dim, const float* q_norm_w, const float* k_norm_w, float eps,
+                           const float* cos, const float* sin, int64_t seq, void* stream);
+/* out[r, :] = silu(gu[r, :n]) * gu[r, n:2n] for a fused gate|up f16 output
+ * (model.rs:593-606). */
+RB_API int rb_silu_mul_halves(const void* gu_f16, int64_t rows, int64_t n, void* out_f16, void* stream);
+/* out[b, :] = l2_normalise(rms_norm(x[b*seq + seq-1, :], w, eps)): the final
+ * norm of each sequence's last token (model.rs:230-235), L2-normalised. */
+RB_API int rb_last_token_l2(const float* x, int64_t batch, int64_t seq, int64_t d, const float* w,
+                            float eps, float* out, void* stream);
 
 /* ---- codec and quantiser surfaces (parity / debugging) */
 
