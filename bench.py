@@ -218,22 +218,24 @@ class Q8GemmWorkload:
     metric = "Q8_0 GEMM TFLOP/s (config #1: f32 [512,1024] x Q8_0 [3072,1024]^T)"
     unit = "TFLOP/s"
     M, K, N = 512, 1024, 3072
+    X_DTYPE = "f32"
 
     def __init__(self, dev, seed):
         import torch
         import burn_rocket_b200 as rb
-        from oracle import oracle as orc  # only to build the synthetic Q8_0 blocks
         self.rb = rb
+        if (self.M, self.N, self.K) != (512, 3072, 1024):
+            self.metric = f"Q8_0 GEMM TFLOP/s ([{self.M},{self.K}] {self.X_DTYPE} x Q8_0 [{self.N},{self.K}]^T)"
         rng = np.random.default_rng(seed)
         a = rng.standard_normal((self.M, self.K)).astype(np.float32)
         w = (rng.standard_normal((self.N, self.K)) * 0.02).astype(np.float32)
         self.wid = rb.pack(w)  # device Q8_0 encoder
-        self.x = torch.from_numpy(a).to(dev)
-        self.y = torch.empty(self.M, self.N, dtype=torch.float32, device=dev)
+        xdt = torch.float32 if self.X_DTYPE == "f32" else torch.float16
+        self.x = torch.from_numpy(a).to(dev).to(xdt)
+        self.y = torch.empty(self.M, self.N, dtype=xdt, device=dev)
         self.flops = 2.0 * self.M * self.N * self.K
-        self.hx = torch.from_numpy(a).pin_memory()
-        self.hy = torch.empty(self.M, self.N, dtype=torch.float32).pin_memory()
-        del orc
+        self.hx = self.x.cpu().pin_memory()
+        self.hy = torch.empty(self.M, self.N, dtype=xdt).pin_memory()
 
     def step(self):
         self.rb.matmul(self.x, self.wid, out=self.y)
@@ -243,11 +245,12 @@ class Q8GemmWorkload:
 
     def e2e_step(self):
         import burn_rocket_b200._lib as L
-        rc = L.load().rb_matmul_host(self.wid.id, self.hx.data_ptr(), L.DTYPE_F32, self.M, self.K,
-                                     self.hy.data_ptr(), L.DTYPE_F32)
+        dt = L.DTYPE_F32 if self.X_DTYPE == "f32" else L.DTYPE_F16
+        rc = L.load().rb_matmul_host(self.wid.id, self.hx.data_ptr(), dt, self.M, self.K,
+                                     self.hy.data_ptr(), dt)
         if rc != 0:
             raise RuntimeError(L.last_error())
-        return (self.hx.numel() * 4, self.hy.numel() * 4)
+        return (self.hx.numel() * self.hx.element_size(), self.hy.numel() * self.hy.element_size())
 
     @staticmethod
     def cpu_sample(orc, seed, timed_repeats=3):
@@ -586,11 +589,17 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying a CUDA graph")
+    ap.add_argument("--gemm-shape", default=None,
+                    help="q8gemm only: M,N,K with f16 activations/outputs (profiling the model's shapes)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.steps is None:
         args.steps = {"attn": 200, "q8gemm": 2000, "w8a8": 60, "qwen3": 10}.get(args.workload, 20)
+    if args.gemm_shape:
+        m, n, k = (int(v) for v in args.gemm_shape.split(","))
+        Q8GemmWorkload.M, Q8GemmWorkload.N, Q8GemmWorkload.K = m, n, k
+        Q8GemmWorkload.X_DTYPE = "f16"
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -257,12 +257,13 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
       g_launches++;
       a = e->act.ptr;
     }
+    int bn = 0, mh = 1;
+    gemm_pick(false, L.M, L.N, e->num_sms, &bn, &mh);
     CUtensorMap tmA, tmC;
-    if ((rc = make_tmap_2d(&tmA, a, 2, m, k, k, 64, 128, true)) != RB_OK) return rc;
+    if ((rc = make_tmap_2d(&tmA, a, 2, m, k, k, 64, 128 * mh, true)) != RB_OK) return rc;
     const bool tstore = output_map(&tmC, y, y_dtype, m, w.n);
-    const int bn = gemm_pick_bn(false, L.M, L.N, e->num_sms);
     const int bi = bn_index(bn);
-    if ((rc = launch_q8_gemm(L, bn, tmA, w.tm_codes[bi], w.tm_scales[bi], tstore ? &tmC : nullptr,
+    if ((rc = launch_q8_gemm(L, bn, mh, tmA, w.tm_codes[bi], w.tm_scales[bi], tstore ? &tmC : nullptr,
                              st)) != RB_OK)
       return fail(rc, "q8_0 gemm launch failed");
     g_launches++;
@@ -283,7 +284,8 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
     L.s_col = reinterpret_cast<const float*>(w.scales);
     L.out_scale = w.out_scale;
     const bool tstore = output_map(&tmC, y, y_dtype, m, w.n);
-    const int bn = gemm_pick_bn(true, L.M, L.N, e->num_sms);
+    int bn = 0, mh = 1;
+    gemm_pick(true, L.M, L.N, e->num_sms, &bn, &mh);
     if ((rc = launch_w8a8_gemm(L, bn, tmA, w.tm_codes[bn_index(bn)], tstore ? &tmC : nullptr, st)) != RB_OK)
       return fail(rc, "w8a8 gemm launch failed");
     g_launches++;
@@ -840,7 +842,8 @@ int rb_matmul_i8_acc(int64_t id, const int8_t* codes, int64_t m, int32_t* acc, v
   L.num_sms = e->num_sms;
   L.s_col = reinterpret_cast<const float*>(w.scales);
   const bool tstore = output_map(&tmC, acc, RB_DTYPE_I32, m, w.n);
-  const int bn = gemm_pick_bn(true, L.M, L.N, e->num_sms);
+  int bn = 0, mh = 1;
+  gemm_pick(true, L.M, L.N, e->num_sms, &bn, &mh);
   rc = launch_w8a8_gemm(L, bn, tmA, w.tm_codes[bn_index(bn)], tstore ? &tmC : nullptr,
                         reinterpret_cast<cudaStream_t>(stream));
   g_launches++;

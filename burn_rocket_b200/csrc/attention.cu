@@ -306,7 +306,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     const int s = (warp - kSoftWarp0) >> 2;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
-    const SlotInfo me = sl[s];
+    const SlotInfo me = s == 0 ? sl[0] : sl[1];  // no runtime index into sl[]
     if (me.lo <= me.hi) {
       const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
       const uint32_t o_col = s * 256 + 128;

@@ -36,7 +36,6 @@
 
 namespace rb {
 
-constexpr int kBM = 128;          // UMMA M (one TMEM lane per output row)
 constexpr int kEpiWarp0 = 2;      // first epilogue warp
 constexpr int kNumEpiWarps = 4;
 constexpr int kDqWarp0 = 6;       // first dequant warp (Q8_0 only)
@@ -47,9 +46,13 @@ enum class BSrc { Tma, Q8Dequant };
 
 constexpr int round1k(int x) { return (x + 1023) & ~1023; }
 
-template <int BN_, int LSTAGES_, bool I8_, int BSTAGES_ = 2>
+template <int BN_, int LSTAGES_, bool I8_, int BSTAGES_ = 2, int MH_ = 1>
 struct GemmCfg {
   static constexpr int BN = BN_;
+  // 128-row M halves per tile: MH = 2 issues two M=128 UMMAs per K step that
+  // share one (dequantised) B tile, halving the dequant work per FLOP.
+  static constexpr int MH = MH_;
+  static constexpr int BM = 128 * MH;
   static constexpr int LSTAGES = LSTAGES_;          // TMA load ring depth
   static constexpr bool I8 = I8_;
   static constexpr bool Q8 = !I8;
@@ -58,7 +61,7 @@ struct GemmCfg {
   static constexpr int BK = 128 / ELEM;             // K elements per stage (one 128-B atom)
   static constexpr int UMMA_K = I8 ? 32 : 16;
   static constexpr int KSTEPS = BK / UMMA_K;        // 4
-  static constexpr int A_BYTES = kBM * 128;         // 16 KB
+  static constexpr int A_BYTES = BM * 128;          // 16 KB per M half
   static constexpr int B_BYTES = BN * 128;          // one B tile (f16 or s8)
   static constexpr int CODE_BYTES = Q8 ? BN * 64 : 0;
   static constexpr int SC_BYTES = Q8 ? 2 * BN * 2 : 0;
@@ -72,9 +75,10 @@ struct GemmCfg {
   static constexpr int SMEM_BYTES = BAR_OFF + 384 + 1024;
   static constexpr int NUM_WARPS = Q8 ? (kDqWarp0 + kNumDqWarps) : 6;
   static constexpr int THREADS = NUM_WARPS * 32;
-  static constexpr uint32_t TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64
-                                        : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
-  static_assert(2 * BN <= 512, "two accumulators must fit in TMEM");
+  static constexpr int ACC_COLS = MH * BN;          // one accumulator (all M halves)
+  static constexpr uint32_t TMEM_COLS = (2 * ACC_COLS <= 32) ? 32 : (2 * ACC_COLS <= 64) ? 64
+                                        : (2 * ACC_COLS <= 128) ? 128 : (2 * ACC_COLS <= 256) ? 256 : 512;
+  static_assert(2 * ACC_COLS <= 512, "two accumulators must fit in TMEM");
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N constraint for M=128");
   static_assert(B_BYTES % 1024 == 0, "B tiles must keep 1024-byte alignment");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
@@ -120,37 +124,43 @@ __device__ __forceinline__ uint4 q8_dequant8_f16(uint2 codes, __half d) {
   return out;
 }
 
-__device__ __forceinline__ void store_out8(void* out, int dtype, int64_t idx, const float* v,
-                                           int count) {
-  if (dtype == RB_DTYPE_F32 || dtype == RB_DTYPE_I32) {  // I32: raw bits in v
-    float* p = reinterpret_cast<float*>(out) + idx;
-    if (count == 8 && (idx & 3) == 0) {
-      reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
-      reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
-    } else {
-      for (int i = 0; i < count; ++i) p[i] = v[i];
+// Direct-store fallback: element j of v goes to idx + j when j < count
+// (compile-time unrolled so v stays in registers).
+__device__ __forceinline__ void store_out16(void* out, int dtype, int64_t idx, const float (&v)[16],
+                                            int count) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    if (j < count) {
+      if (dtype == RB_DTYPE_F32 || dtype == RB_DTYPE_I32)  // I32: raw bits in v
+        reinterpret_cast<float*>(out)[idx + j] = v[j];
+      else if (dtype == RB_DTYPE_F16)
+        reinterpret_cast<__half*>(out)[idx + j] = __float2half_rn(v[j]);
+      else
+        reinterpret_cast<__nv_bfloat16*>(out)[idx + j] = __float2bfloat16_rn(v[j]);
     }
-  } else if (dtype == RB_DTYPE_F16) {
-    __half* p = reinterpret_cast<__half*>(out) + idx;
-    for (int i = 0; i < count; ++i) p[i] = __float2half_rn(v[i]);
-  } else {
-    __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(out) + idx;
-    for (int i = 0; i < count; ++i) p[i] = __float2bfloat16_rn(v[i]);
   }
 }
 
+// Epilogue parameters held in registers (never through a reference to the
+// kernel-parameter struct, which would force a local-memory copy).
+struct EpiParams {
+  const float* s_col;
+  int out_dtype;
+  float out_scale, out_inv;
+};
+
 // Epilogue value for accumulator bits r at column n (row scale rs).
 template <bool I8>
-__device__ __forceinline__ float epi_value(const GemmArgs& a, uint32_t r, float rs, int n) {
+__device__ __forceinline__ float epi_value(const EpiParams e, uint32_t r, float rs, int n) {
   if (!I8) return __uint_as_float(r);
-  if (a.out_dtype == RB_DTYPE_I32) return __uint_as_float(r);
+  if (e.out_dtype == RB_DTYPE_I32) return __uint_as_float(r);
   // Order matters for bit parity: f32(acc) * (s_row * s_col).
-  float y = __fmul_rn(__int2float_rn(static_cast<int32_t>(r)), __fmul_rn(rs, a.s_col[n]));
-  if (a.out_scale != 0.0f) {
+  float y = __fmul_rn(__int2float_rn(static_cast<int32_t>(r)), __fmul_rn(rs, __ldg(e.s_col + n)));
+  if (e.out_scale != 0.0f) {
     // static_code(y, 1/out_scale) * out_scale (ext.rs:1236-1238, 1356-1360),
     // through an integer code like the reference (`as i8`), so zero is +0.0.
-    const int code = max(-128, min(127, __float2int_rn(__fmul_rn(y, a.out_inv))));
-    y = __fmul_rn(__int2float_rn(code), a.out_scale);
+    const int code = max(-128, min(127, __float2int_rn(__fmul_rn(y, e.out_inv))));
+    y = __fmul_rn(__int2float_rn(code), e.out_scale);
   }
   return y;
 }
@@ -179,7 +189,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   const int lane = threadIdx.x & 31;
   const int M = args.M, N = args.N, K = args.K;
   const int tiles_n = (N + BN - 1) / BN;
-  const int tiles_m = (M + kBM - 1) / kBM;
+  const int tiles_m = (M + Cfg::BM - 1) / Cfg::BM;
   const int num_tiles = tiles_m * tiles_n;
   const int num_kb = (K + Cfg::BK - 1) / Cfg::BK;
 
@@ -220,7 +230,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       int ls = 0;
       uint32_t lph = 0;
       for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
-        const int m0 = (t / tiles_n) * kBM;
+        const int m0 = (t / tiles_n) * Cfg::BM;
         const int n0 = (t % tiles_n) * BN;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&load_empty[ls], lph ^ 1, args.err, abort_flag)) goto producer_done;
@@ -242,7 +252,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     // ------------------------------------------------------------ UMMA issuer
     if (elect_one_sync()) {
       constexpr uint32_t idesc =
-          Cfg::I8 ? idesc_i8(kBM, BN) : idesc_f16(kBM, BN, false, false, false);
+          Cfg::I8 ? idesc_i8(128, BN) : idesc_f16(128, BN, false, false, false);
       int ls = 0, bs = 0;
       uint32_t lph = 0, bph = 0;
       int local = 0;
@@ -251,7 +261,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, args.err, abort_flag)) goto mma_done;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * BN;
+        const uint32_t d_tmem = tmem_base + acc * Cfg::ACC_COLS;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&load_full[ls], lph, args.err, abort_flag)) goto mma_done;
           if (Cfg::Q8) {
@@ -263,11 +273,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                                           : a_addr + Cfg::A_BYTES;
 #pragma unroll
           for (int ks = 0; ks < Cfg::KSTEPS; ++ks) {
-            const uint64_t da = desc_kmajor_sw128(a_addr + ks * 32);
             const uint64_t db = desc_kmajor_sw128(b_addr + ks * 32);
             const uint32_t accum = (kb > 0 || ks > 0) ? 1u : 0u;
-            if (Cfg::I8) umma_i8_ss(d_tmem, da, db, idesc, accum);
-            else umma_f16_ss(d_tmem, da, db, idesc, accum);
+#pragma unroll
+            for (int h = 0; h < Cfg::MH; ++h) {  // M halves share the B tile
+              const uint64_t da = desc_kmajor_sw128(a_addr + h * 16384 + ks * 32);
+              if (Cfg::I8) umma_i8_ss(d_tmem + h * BN, da, db, idesc, accum);
+              else umma_f16_ss(d_tmem + h * BN, da, db, idesc, accum);
+            }
           }
           umma_commit(&load_empty[ls]);  // frees the load stage once these MMAs retire
           if (++ls == LSTAGES) { ls = 0; lph ^= 1; }
@@ -284,18 +297,21 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;
+    const EpiParams ep{args.s_col, args.out_dtype, args.out_scale, args.out_inv};
     uint8_t* ebuf = smem + Cfg::EPI_OFF + (warp - kEpiWarp0) * 2 * kEpiBufBytes;
     const int out_bytes = (args.out_dtype == RB_DTYPE_F16 || args.out_dtype == RB_DTYPE_BF16) ? 2 : 4;
     const int CW = 128 / out_bytes;  // columns per 128-byte store row
     int buf = 0;
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
-      const int m0 = (t / tiles_n) * kBM;
       const int n0 = (t % tiles_n) * BN;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[acc], acc_phase, args.err, abort_flag))) break;
+      if (!warp_wait(&acc_full[acc], acc_phase, args.err, abort_flag)) break;
       tc_fence_after();
+      for (int h = 0; h < Cfg::MH; ++h) {
+      const int m0 = (t / tiles_n) * Cfg::BM + h * 128;
+      const uint32_t acc_col = acc * Cfg::ACC_COLS + h * BN;
       const int m = m0 + row;
       float rs = 1.0f;
       // Raw int32 output (RB_DTYPE_I32) carries no scales.
@@ -304,12 +320,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       if (args.tma_store) {
         if (rows_live) {
           for (int c0 = 0; c0 < BN && n0 + c0 < N; c0 += CW) {
-            uint32_t r[64];
-            tmem_ld32(tmem_addr(tmem_base, quarter * 32, acc * BN + c0),
-                      *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
-            if (CW == 64)
-              tmem_ld32(tmem_addr(tmem_base, quarter * 32, acc * BN + c0 + 32),
-                        *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+            uint32_t ra[32], rb[32];  // columns c0..c0+31 and (2-byte outputs) c0+32..c0+63
+            tmem_ld32(tmem_addr(tmem_base, quarter * 32, acc_col + c0), ra);
+            if (CW == 64) tmem_ld32(tmem_addr(tmem_base, quarter * 32, acc_col + c0 + 32), rb);
             tmem_wait_ld();
             // The buffer about to be written must have been read by its
             // previous TMA store (at most one store of this warp in flight).
@@ -322,7 +335,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
                 float v[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e)
-                  v[e] = epi_value<Cfg::I8>(args, r[4 * j + e], rs, min(n0 + c0 + 4 * j + e, N - 1));
+                  v[e] = epi_value<Cfg::I8>(ep, ra[4 * j + e], rs, min(n0 + c0 + 4 * j + e, N - 1));
                 *reinterpret_cast<float4*>(b + ((j ^ (lane & 7)) << 4)) =
                     make_float4(v[0], v[1], v[2], v[3]);
               }
@@ -333,8 +346,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                   const int c = 8 * j + 2 * e;
-                  const float v0 = epi_value<Cfg::I8>(args, r[c], rs, min(n0 + c0 + c, N - 1));
-                  const float v1 = epi_value<Cfg::I8>(args, r[c + 1], rs, min(n0 + c0 + c + 1, N - 1));
+                  const uint32_t r0 = c < 32 ? ra[c] : rb[c - 32];
+                  const uint32_t r1 = c + 1 < 32 ? ra[c + 1] : rb[c + 1 - 32];
+                  const float v0 = epi_value<Cfg::I8>(ep, r0, rs, min(n0 + c0 + c, N - 1));
+                  const float v1 = epi_value<Cfg::I8>(ep, r1, rs, min(n0 + c0 + c + 1, N - 1));
                   if (args.out_dtype == RB_DTYPE_F16) {
                     __half2 h = __floats2half2_rn(v0, v1);
                     pk[e] = *reinterpret_cast<uint32_t*>(&h);
@@ -360,19 +375,18 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 #pragma unroll 1
         for (int c = 0; c < BN; c += 16) {
           uint32_t r[16];
-          tmem_ld16(tmem_addr(tmem_base, quarter * 32, acc * BN + c), r);
+          tmem_ld16(tmem_addr(tmem_base, quarter * 32, acc_col + c), r);
           tmem_wait_ld();
           if (m < M && n0 + c < N) {
             float v[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = epi_value<Cfg::I8>(args, r[j], rs, min(n0 + c + j, N - 1));
+            for (int j = 0; j < 16; ++j) v[j] = epi_value<Cfg::I8>(ep, r[j], rs, min(n0 + c + j, N - 1));
             const int64_t base = static_cast<int64_t>(m) * args.ldo + n0 + c;
-            const int left = N - (n0 + c);
-            store_out8(args.out, args.out_dtype, base, v, left >= 8 ? 8 : left);
-            if (left > 8) store_out8(args.out, args.out_dtype, base + 8, v + 8, left >= 16 ? 8 : left - 8);
+            store_out16(args.out, ep.out_dtype, base, v, N - (n0 + c));
           }
         }
       }
+      }  // M halves
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
@@ -392,10 +406,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     uint32_t lph = 0, bph = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
       for (int kb = 0; kb < num_kb; ++kb) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&load_full[ls], lph, args.err, abort_flag)))
-          goto dq_done;
-        if (!__all_sync(0xffffffffu, mbar_wait(&b_empty[bs], bph ^ 1, args.err, abort_flag)))
-          goto dq_done;
+        if (!warp_wait(&load_full[ls], lph, args.err, abort_flag)) goto dq_done;
+        if (!warp_wait(&b_empty[bs], bph ^ 1, args.err, abort_flag)) goto dq_done;
         const uint8_t* codes = smem + ls * Cfg::LSTAGE + Cfg::A_BYTES;
         const __half* sc = reinterpret_cast<const __half*>(codes + Cfg::CODE_BYTES);
         uint8_t* sb = smem + Cfg::BRING_OFF + bs * Cfg::B_BYTES;
@@ -440,6 +452,7 @@ using CfgQ8_256 = GemmCfg<256, 3, false, 2>;
 using CfgQ8_128 = GemmCfg<128, 4, false, 4>;
 using CfgQ8_96 = GemmCfg<96, 4, false, 6>;
 using CfgQ8_64 = GemmCfg<64, 6, false, 6>;
+using CfgQ8_128x2 = GemmCfg<128, 3, false, 3, 2>;  // 256-row M tile
 using CfgI8_256 = GemmCfg<256, 4, true>;
 using CfgI8_128 = GemmCfg<128, 6, true>;
 
@@ -447,7 +460,7 @@ template <class Cfg>
 static int launch_cfg(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmS,
                       const CUtensorMap* tmC, const GemmArgs& a, int num_sms,
                       cudaStream_t stream) {
-  const int tiles = ((a.M + kBM - 1) / kBM) * ((a.N + Cfg::BN - 1) / Cfg::BN);
+  const int tiles = ((a.M + Cfg::BM - 1) / Cfg::BM) * ((a.N + Cfg::BN - 1) / Cfg::BN);
   const int grid = tiles < num_sms ? tiles : num_sms;
   static uint64_t configured = 0;  // one bit per device ordinal
   int dev = 0;
@@ -467,24 +480,28 @@ static int launch_cfg(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUte
   return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
 }
 
-// N tile minimising the makespan of the persistent grid: rounds of tiles per
-// SM times the per-tile cost (proportional to BN plus a fixed pipeline fill /
-// epilogue overhead expressed in BN units).
-int gemm_pick_bn(bool i8, int M, int N, int num_sms) {
-  static const int q8c[] = {256, 128, 96, 64};
-  static const int i8c[] = {256, 128};
-  const int* c = i8 ? i8c : q8c;
-  const int nc = i8 ? 2 : 4;
-  const long tm = (M + kBM - 1) / kBM;
-  int best = c[0];
-  long best_cost = -1;
+// Tile shape (BN, M halves) minimising the makespan of the persistent grid:
+// rounds of tiles per SM times the per-tile cost. A tile's cost is its MMA
+// work (MH * BN columns of 128 rows) scaled by how well the shape feeds the
+// tensor core — a Q8_0 tile with one M half spends twice the dequant work per
+// FLOP — plus a fixed pipeline fill / epilogue overhead.
+void gemm_pick(bool i8, int M, int N, int num_sms, int* bn_out, int* mh_out) {
+  struct Shape { int bn, mh; double eff; };
+  static const Shape q8c[] = {{256, 1, 1.4}, {128, 1, 1.4}, {96, 1, 1.4}, {64, 1, 1.4}, {128, 2, 1.0}};
+  static const Shape i8c[] = {{256, 1, 1.0}, {128, 1, 1.0}};
+  const Shape* c = i8 ? i8c : q8c;
+  const int nc = i8 ? 2 : 5;
+  double best_cost = -1.0;
   for (int i = 0; i < nc; ++i) {
-    const long tiles = tm * ((N + c[i] - 1) / c[i]);
+    const long tiles = ((M + 128L * c[i].mh - 1) / (128L * c[i].mh)) * ((N + c[i].bn - 1) / c[i].bn);
     const long rounds = (tiles + num_sms - 1) / num_sms;
-    const long cost = rounds * (c[i] + 32);
-    if (best_cost < 0 || cost < best_cost) { best_cost = cost; best = c[i]; }
+    const double cost = rounds * (c[i].mh * c[i].bn * c[i].eff + 32.0);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      *bn_out = c[i].bn;
+      *mh_out = c[i].mh;
+    }
   }
-  return best;
 }
 
 static GemmArgs make_args(const GemmLaunch& L) {
@@ -498,9 +515,14 @@ static GemmArgs make_args(const GemmLaunch& L) {
   return a;
 }
 
-int launch_q8_gemm(const GemmLaunch& L, int bn, const CUtensorMap& tmA, const CUtensorMap& tmCodes,
-                   const CUtensorMap& tmScales, const CUtensorMap* tmC, cudaStream_t stream) {
+int launch_q8_gemm(const GemmLaunch& L, int bn, int mh, const CUtensorMap& tmA,
+                   const CUtensorMap& tmCodes, const CUtensorMap& tmScales, const CUtensorMap* tmC,
+                   cudaStream_t stream) {
   const GemmArgs a = make_args(L);
+  if (mh == 2) {
+    if (bn != 128) return RB_E_SHAPE;
+    return launch_cfg<CfgQ8_128x2>(tmA, tmCodes, tmScales, tmC, a, L.num_sms, stream);
+  }
   switch (bn) {
     case 256: return launch_cfg<CfgQ8_256>(tmA, tmCodes, tmScales, tmC, a, L.num_sms, stream);
     case 128: return launch_cfg<CfgQ8_128>(tmA, tmCodes, tmScales, tmC, a, L.num_sms, stream);

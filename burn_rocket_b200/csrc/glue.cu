@@ -205,32 +205,41 @@ __global__ void add_rms_norm_kernel(float* x, const __half* delta, const float* 
 }
 
 // In place on qkv [T, ld] f16: heads [0, hq) of width 128 at column 0 (q) use
-// wq, heads [hq, hq+hk) (k) use wk. One warp per (token, head); lane l owns
-// elements 2l, 2l+1 and 64+2l, 64+2l+1 (the rotate-half pairs).
+// wq, heads [hq, hq+hk) (k) use wk. One warp per token: the RoPE row of the
+// token's position and both norm weights are loaded once, then every head is
+// normalised and rotated; lane l owns elements 2l, 2l+1 and 64+2l, 64+2l+1
+// (the rotate-half pairs).
 __global__ void qk_norm_rope_kernel(__half* qkv, int64_t ld, int64_t tokens, int hq, int hk,
                                     const float* wq, const float* wk, float eps,
                                     const float* cos_t, const float* sin_t, int seq) {
   const int lane = threadIdx.x & 31;
-  const int heads = hq + hk;
-  const int64_t items = tokens * heads;
+  const float2 wq_a = *reinterpret_cast<const float2*>(wq + 2 * lane);
+  const float2 wq_b = *reinterpret_cast<const float2*>(wq + 64 + 2 * lane);
+  const float2 wk_a = *reinterpret_cast<const float2*>(wk + 2 * lane);
+  const float2 wk_b = *reinterpret_cast<const float2*>(wk + 64 + 2 * lane);
   const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  for (int64_t it = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); it < items; it += nw) {
-    const int64_t t = it / heads;
-    const int hd = static_cast<int>(it % heads);
-    __half* p = qkv + t * ld + static_cast<int64_t>(hd) * 128;
-    const float* w = hd < hq ? wq : wk;
-    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(p + 2 * lane));
-    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(p + 64 + 2 * lane));
-    float ss = a.x * a.x + a.y * a.y + b.x * b.x + b.y * b.y;
-    ss = warp_sum(ss);
-    const float inv = 1.0f / sqrtf(ss / 128.0f + eps);
-    const float a0 = a.x * inv * w[2 * lane], a1 = a.y * inv * w[2 * lane + 1];
-    const float b0 = b.x * inv * w[64 + 2 * lane], b1 = b.y * inv * w[64 + 2 * lane + 1];
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); t < tokens; t += nw) {
     const int pos = static_cast<int>(t % seq);
-    const float c0 = cos_t[pos * 64 + 2 * lane], c1 = cos_t[pos * 64 + 2 * lane + 1];
-    const float s0 = sin_t[pos * 64 + 2 * lane], s1 = sin_t[pos * 64 + 2 * lane + 1];
-    *reinterpret_cast<__half2*>(p + 2 * lane) = __floats2half2_rn(a0 * c0 - b0 * s0, a1 * c1 - b1 * s1);
-    *reinterpret_cast<__half2*>(p + 64 + 2 * lane) = __floats2half2_rn(b0 * c0 + a0 * s0, b1 * c1 + a1 * s1);
+    const float2 cs = *reinterpret_cast<const float2*>(cos_t + pos * 64 + 2 * lane);
+    const float2 sn = *reinterpret_cast<const float2*>(sin_t + pos * 64 + 2 * lane);
+    __half* row = qkv + t * ld;
+#pragma unroll 4
+    for (int hd = 0; hd < hq + hk; ++hd) {
+      __half* p = row + static_cast<int64_t>(hd) * 128;
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(p + 2 * lane));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(p + 64 + 2 * lane));
+      float ss = a.x * a.x + a.y * a.y + b.x * b.x + b.y * b.y;
+      ss = warp_sum(ss);
+      const float inv = 1.0f / sqrtf(ss / 128.0f + eps);
+      const float2 wa = hd < hq ? wq_a : wk_a;
+      const float2 wb = hd < hq ? wq_b : wk_b;
+      const float a0 = a.x * inv * wa.x, a1 = a.y * inv * wa.y;
+      const float b0 = b.x * inv * wb.x, b1 = b.y * inv * wb.y;
+      *reinterpret_cast<__half2*>(p + 2 * lane) =
+          __floats2half2_rn(a0 * cs.x - b0 * sn.x, a1 * cs.y - b1 * sn.y);
+      *reinterpret_cast<__half2*>(p + 64 + 2 * lane) =
+          __floats2half2_rn(b0 * cs.x + a0 * sn.x, b1 * cs.y + a1 * sn.y);
+    }
   }
 }
 
@@ -323,8 +332,7 @@ int launch_add_rms_norm(float* x, const void* delta, const float* w, float eps, 
 int launch_qk_norm_rope(void* qkv, int64_t ld, int64_t tokens, int hq, int hk, const float* wq,
                         const float* wk, float eps, const float* cos_t, const float* sin_t, int seq,
                         cudaStream_t st) {
-  const int64_t items = tokens * (hq + hk);
-  qk_norm_rope_kernel<<<grid_for_rows(items, 8), 256, 0, st>>>(
+  qk_norm_rope_kernel<<<grid_for_rows(tokens, 8), 256, 0, st>>>(
       reinterpret_cast<__half*>(qkv), ld, tokens, hq, hk, wq, wk, eps, cos_t, sin_t, seq);
   return RB_LAUNCH_OK();
 }

@@ -28,15 +28,16 @@ struct GemmLaunch {
   int force_bn;           // 0 = heuristic
 };
 
-// N tile the persistent GEMM will use for an [M, N] output (weight tensor
-// maps are built per N tile).
-int gemm_pick_bn(bool i8, int M, int N, int num_sms);
-// Q8_0: tmA = f16 activations [M, K] (box 64 x 128, 128-B swizzle); tmCodes =
+// Tile shape the persistent GEMM will use for an [M, N] output: N tile (the
+// weight tensor maps are built per N tile) and 128-row M halves per tile.
+void gemm_pick(bool i8, int M, int N, int num_sms, int* bn, int* mh);
+// Q8_0: tmA = f16 activations [M, K] (box 64 x 128*mh, 128-B swizzle); tmCodes =
 // codes [N, K] (box 64 x bn); tmScales = f16 scales [K/32, N] (box bn x 2);
 // tmC = output map (box 32 rows x 128 B, 128-B swizzle) or nullptr for direct
 // stores.
-int launch_q8_gemm(const GemmLaunch& L, int bn, const CUtensorMap& tmA, const CUtensorMap& tmCodes,
-                   const CUtensorMap& tmScales, const CUtensorMap* tmC, cudaStream_t stream);
+int launch_q8_gemm(const GemmLaunch& L, int bn, int mh, const CUtensorMap& tmA,
+                   const CUtensorMap& tmCodes, const CUtensorMap& tmScales, const CUtensorMap* tmC,
+                   cudaStream_t stream);
 // W8A8: tmA = s8 activation codes [M, K] (box 128 x 128), tmB = s8 weight
 // codes [N, K] (box 128 x bn), both 128-B swizzled.
 int launch_w8a8_gemm(const GemmLaunch& L, int bn, const CUtensorMap& tmA, const CUtensorMap& tmB,

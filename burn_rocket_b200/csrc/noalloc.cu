@@ -109,7 +109,8 @@ extern "C" int rb_matmul_w8a8_noalloc(int64_t id, const void* x, int x_dtype, in
   L.err = v.err;
   L.num_sms = v.num_sms;
   const bool tstore = make_output_map(&tmC, y, y_dtype, m, v.n);
-  const int bn = gemm_pick_bn(true, L.M, L.N, v.num_sms);
+  int bn = 0, mh = 1;
+  gemm_pick(true, L.M, L.N, v.num_sms, &bn, &mh);
   if ((rc = launch_w8a8_gemm(L, bn, tmA, v.tm_codes[bn_index(bn)], tstore ? &tmC : nullptr, st)) !=
       RB_OK)
     return report_error(rc, "w8a8 gemm launch failed");

@@ -101,6 +101,41 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   return false;
 }
 
+// Same bounded wait, but backing off with nanosleep between polls: for waits
+// expected to be long (an epilogue waiting for a whole main loop) so the
+// polling does not compete with the pipeline for shared-memory bandwidth.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t* err,
+                                                volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  uint32_t ns = 32;
+  for (uint32_t i = 1;; ++i) {
+    __nanosleep(ns);
+    if (ns < 256) ns <<= 1;
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 15u) == 0) {
+      if (*abort_flag) return false;
+      if (global_timer_ns() - t0 > kWaitLimitNs) break;
+    }
+  }
+  *abort_flag = 1;
+  if (err) atomicOr(err, kErrWaitTimeout);
+  return false;
+}
+
+// Warp-wide wait: lane 0 polls the barrier (one shared-memory request per
+// poll instead of 32) and the outcome is broadcast; __syncwarp orders the
+// other lanes' subsequent reads after lane 0's acquire.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint32_t* err,
+                                          volatile int* abort_flag, bool sleep = false) {
+  bool ok = true;
+  if ((threadIdx.x & 31) == 0)
+    ok = sleep ? mbar_wait_sleep(bar, parity, err, abort_flag) : mbar_wait(bar, parity, err, abort_flag);
+  ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+  __syncwarp();
+  return ok;
+}
+
 // After an aborted pipeline: give asynchronous copies and MMAs already issued
 // by this CTA time to retire (bounded, ~1 ms) before TMEM and shared memory
 // are released. Called by every thread after the final __syncthreads.
