@@ -1,6 +1,6 @@
 """bench.py — throughput of the offloaded ops on B200, one JSON line on rank 0.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload attn|q8gemm|w8a8]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload attn|q8gemm|w8a8|qwen3|siglip]
                     [--impl b200|reference]
 
 Workloads (synthetic seeded data of the named shapes):
@@ -409,7 +409,96 @@ class Qwen3Workload:
         return T / (t_layer * cfg.layers), "one layer (4 Q8_0 projections + attention) at 512 tokens, x28 layers"
 
 
-WORKLOADS = {w.name: w for w in (AttnWorkload, Q8GemmWorkload, W8A8Workload, Qwen3Workload)}
+class SiglipWorkload:
+    """Config #4: SigLIP-style W8A8 vision tower, 16 images x 2394 patches,
+    data-parallel over images (16/N per GPU)."""
+    name = "siglip"
+    metric = "SigLIP-style W8A8 tower patches/s (config #4: 16 images x 2394 patches, 27 layers)"
+    unit = "patch/s"
+    IMAGES = 16
+
+    def __init__(self, dev, seed, world=1, rank=0):
+        import torch
+        import burn_rocket_b200 as rb
+        from burn_rocket_b200.siglip import SiglipConfig, SiglipTower
+        self.rb = rb
+        self.cfg = SiglipConfig()
+        if self.IMAGES % world:
+            raise SystemExit(f"--gpus {world} must divide the {self.IMAGES}-image batch")
+        self.local = self.IMAGES // world
+        # identical random-init weights on every rank (seed 0); rank r encodes
+        # images [r*local, (r+1)*local) of the global batch.
+        self.model = SiglipTower(self.cfg, self.local, seed=0)
+        S, h = self.cfg.patches, self.cfg.hidden
+        g = torch.Generator(device="cpu").manual_seed(seed + rank)
+        mine = torch.randn(self.local * S, h, generator=g)
+        self.model.patches.copy_(mine.to(dev))
+        self.hpatches = mine.pin_memory()
+        self.hout = torch.empty(self.local * S, h, dtype=torch.float16).pin_memory()
+        self.units = self.local * S  # patches per step on this rank
+        lin, att = self.cfg.ops_per_patch()
+        self.flops = (lin + att) * self.units
+
+    def step(self):
+        self.model.forward_device()
+
+    def e2e_step(self):
+        self.model.encode_host(self.hpatches, self.hout)
+        return (self.hpatches.numel() * 4, self.hout.numel() * 2)
+
+    def kernel_roofline(self):
+        """Device time of the four W8A8 projections of one layer (row quantiser + int8 GEMM)."""
+        import torch
+        m, L = self.model, self.model.layers[0]
+        calls = [(m.h, L["qkv"], m.qkv), (m.attn, L["o"], m.o), (m.h, L["fc1"], m.f), (m.f, L["fc2"], m.d)]
+        ops = 0.0
+        for x, w, y in calls:
+            _, n, k = self.rb.weight_info(w)
+            ops += 2.0 * x.shape[0] * n * k
+        for _ in range(2):
+            for x, w, y in calls:
+                self.rb.matmul(x, w, out=y)
+        reps = 5
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        torch.cuda.synchronize()
+        ev[0].record()
+        for _ in range(reps):
+            for x, w, y in calls:
+                self.rb.matmul(x, w, out=y)
+        ev[1].record()
+        torch.cuda.synchronize()
+        ms = ev[0].elapsed_time(ev[1]) / reps
+        return "w8a8 gemm_kernel + row quantiser (qkv, o, fc1, fc2 of one layer)", ops / (ms / 1e3) / 1e12, ms
+
+    @staticmethod
+    def cpu_sample(orc, seed, timed_repeats=1):
+        """The reference CPU algorithm for one layer: the four W8A8 projections
+        on 256 patch rows and the attention of 2 of 16 heads over one 2394-patch
+        image, scaled to 27 layers x all rows / heads."""
+        from burn_rocket_b200.siglip import SiglipConfig
+        cfg = SiglipConfig()
+        rng = np.random.default_rng(seed)
+        rows, h, S, D = 256, cfg.hidden, cfg.patches, cfg.head_dim
+        shapes = [(3 * h, h), (h, h), (cfg.inter, h), (h, cfg.inter)]
+        ws = [orc.quantize_weight_per_channel((rng.standard_normal(sh) * 0.02).astype(np.float32)) for sh in shapes]
+        xs = [rng.standard_normal((rows, sh[1])).astype(np.float32) for sh in shapes]
+        q = rng.standard_normal((S, 2 * D)).astype(np.float32)
+        kv = rng.standard_normal((S, 2 * D)).astype(np.float32)
+        t0 = time.perf_counter()
+        for _ in range(timed_repeats):
+            for (codes, ws_), x in zip(ws, xs):
+                orc.w8a8_matmul(x, codes, ws_)
+        t_proj = (time.perf_counter() - t0) / timed_repeats / rows
+        t0 = time.perf_counter()
+        for _ in range(timed_repeats):
+            orc.attention_cpu(q, kv, kv, 2, 2, D, 1 / math.sqrt(D), False)
+        t_att = (time.perf_counter() - t0) / timed_repeats / S * (cfg.heads / 2)
+        return 1.0 / ((t_proj + t_att) * cfg.layers), (
+            "one layer: 4 W8A8 projections on 256 rows + attention of 2 of 16 heads over one image, x27 layers")
+
+
+WORKLOADS = {w.name: w for w in (AttnWorkload, Q8GemmWorkload, W8A8Workload, Qwen3Workload, SiglipWorkload)}
+DP_WORKLOADS = ("qwen3", "siglip")
 
 
 # ----------------------------------------------------------------------------- driver
@@ -434,7 +523,7 @@ def run_b200(args):
     import burn_rocket_b200 as rb
     rb.init(local)
     W = WORKLOADS[args.workload]
-    wl = W(dev, seed=0x5EED, world=world, rank=rank) if W is Qwen3Workload else W(dev, seed=0x5EED + rank)
+    wl = W(dev, seed=0x5EED, world=world, rank=rank) if W.name in DP_WORKLOADS else W(dev, seed=0x5EED + rank)
     stream = torch.cuda.current_stream()
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
 
@@ -506,6 +595,9 @@ def run_b200(args):
         kname, achieved, kms = wl.kernel_roofline()
         peak = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
         peak_src = f"{peak_kind} MEASURED_PEAKS bf16_tflops_sustained"
+        if wl.name == "siglip":
+            peak = 2.0 * peak  # dense int8 is twice the dense bf16 rate
+            peak_src += " x2 for int8"
     else:
         kname = "whole step"
         achieved = wl.flops / (ms_per_step / 1e3) / 1e12  # per launch group, per GPU
@@ -518,17 +610,20 @@ def run_b200(args):
     line = {
         "metric": wl.metric, "value": round(value, 3), "unit": wl.unit, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
-        "higher_is_better": True, "scaling": "strong" if wl.name == "qwen3" else "weak", "vs_baseline": None,
-        "dtype": {"attn": "f16", "q8gemm": "f16xq8_0->f32", "w8a8": "s8", "qwen3": "f16xq8_0 (f32 residual)"}[wl.name],
+        "higher_is_better": True, "scaling": "strong" if wl.name in DP_WORKLOADS else "weak", "vs_baseline": None,
+        "dtype": {"attn": "f16", "q8gemm": "f16xq8_0->f32", "w8a8": "s8", "qwen3": "f16xq8_0 (f32 residual)",
+                  "siglip": "s8 linears, f16 attention (f32 residual)"}[wl.name],
         "data": "synthetic (seeded, BASELINE.json shapes)",
         "config": {"workload": {"attn": "configs[1] GQA attention", "q8gemm": "configs[0] Q8_0 GEMM",
                                 "w8a8": "configs[3] W8A8 projections",
-                                "qwen3": "configs[2] Qwen3-Embedding-0.6B arch, 28 layers, 64x512 tokens"}[wl.name],
+                                "qwen3": "configs[2] Qwen3-Embedding-0.6B arch, 28 layers, 64x512 tokens",
+                                "siglip": "configs[3] SigLIP-style W8A8 tower, 27 layers, 16x2394 patches"}[wl.name],
                    "l2": "flushed between timed steps (256 MiB write)",
                    "parallelism": (f"dp{world} over sequences" if wl.name == "qwen3"
+                                   else f"dp{world} over images" if wl.name == "siglip"
                                    else (f"replicas x{world}" if world > 1 else "single GPU"))},
         "roofline": {"bound": "tensor", "kernel": kname, "achieved": round(achieved, 2), "peak": peak,
-                     "unit": "TFLOP/s" if wl.name != "w8a8" else "TOP/s",
+                     "unit": "TOP/s" if wl.name in ("w8a8", "siglip") else "TFLOP/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": peak_src},
         "e2e": {"value": round(e2e_value, 3), "unit": wl.unit, "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h)},
@@ -595,7 +690,7 @@ def main():
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.steps is None:
-        args.steps = {"attn": 200, "q8gemm": 2000, "w8a8": 60, "qwen3": 10}.get(args.workload, 20)
+        args.steps = {"attn": 200, "q8gemm": 2000, "w8a8": 60, "qwen3": 10, "siglip": 5}.get(args.workload, 20)
     if args.gemm_shape:
         m, n, k = (int(v) for v in args.gemm_shape.split(","))
         Q8GemmWorkload.M, Q8GemmWorkload.N, Q8GemmWorkload.K = m, n, k

@@ -26,7 +26,7 @@ from ._lib import (DTYPE_BF16, DTYPE_F16, DTYPE_F32, MASK_CAUSAL, MASK_CAUSAL_BL
                    MASK_WINDOW_BLOCK, WEIGHT_Q8_0, WEIGHT_W8A8)
 
 __all__ = [
-    "Error", "OpFailure", "WeightId", "init", "pack", "pack2", "pack3", "pack_q8_0_blocks",
+    "Error", "OpFailure", "WeightId", "init", "pack", "pack2", "pack3", "pack_q8_0_blocks", "pack_w8a8_float",
     "pack_qat", "matmul", "matmul_host", "attention", "attention_window",
     "attention_causal_window", "attention_window_block", "attention_causal_block",
     "attention_raw", "q8_0_dequant", "quantize_rows_i8", "matmul_i8_acc", "check_device_errors",
@@ -153,6 +153,19 @@ def pack_qat(codes, w_scale, n: int, k: int, in_scale: float = 0.0, out_scale: f
     if w_scale.size != n:
         raise OpFailure(Error("rocket_pack_qat", _lib.RB_E_SHAPE), 0, k, n, "one weight scale per output channel")
     wid = _lib.load().rb_pack_w8a8(codes.ctypes.data, w_scale.ctypes.data, n, k, float(in_scale), float(out_scale))
+    _check(wid, "rocket_pack_qat", 0, k, n)
+    return WeightId(int(wid))
+
+
+def pack_w8a8_float(w, in_scale: float = 0.0, out_scale: float = 0.0) -> WeightId:
+    """Quantise a float [N, K] CUDA weight to per-output-channel int8 on the
+    device (rb_pack_f32_w8a8_device) and pack it like pack_qat."""
+    import torch
+    if not (isinstance(w, torch.Tensor) and w.is_cuda and w.dim() == 2):
+        raise OpFailure(Error("rocket_pack_qat", _lib.RB_E_SHAPE), detail="weight must be a 2-D CUDA tensor")
+    w = w.detach().float().contiguous()
+    n, k = w.shape
+    wid = _lib.load().rb_pack_f32_w8a8_device(C.c_void_p(w.data_ptr()), n, k, float(in_scale), float(out_scale))
     _check(wid, "rocket_pack_qat", 0, k, n)
     return WeightId(int(wid))
 

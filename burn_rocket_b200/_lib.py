@@ -68,6 +68,9 @@ SIGNATURES = {
     "rb_attention_batched": (_i, [_p, _i64, _p, _i64, _p, _i64, _p, _i64, _i, _i64, _i64, _i64, _i, _i, _i, _f, _f,
                                   _i, _i64, _i64, _i64, _p]),
     "rb_rms_norm": (_i, [_p, _i, _p, _f, _p, _i, _i64, _i64, _p]),
+    "rb_pack_f32_w8a8_device": (_i64, [_p, _i64, _i64, _f, _f]),
+    "rb_add_layer_norm": (_i, [_p, _p, _p, _p, _f, _p, _i64, _i64, _p]),
+    "rb_gelu": (_i, [_p, _i64, _p]),
     "rb_silu_mul": (_i, [_p, _p, _i, _p, _i64, _p]),
     "rb_gelu_mul": (_i, [_p, _p, _i, _p, _i64, _p]),
     "rb_rope": (_i, [_p, _i, _p, _p, _p, _i64, _i64, _i, _i, _p]),

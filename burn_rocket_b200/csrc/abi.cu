@@ -60,7 +60,7 @@ static bool load_encode_fn() {
 
 int make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t rows,
                  uint64_t cols, uint64_t row_stride_elems, uint32_t box_cols, uint32_t box_rows,
-                 bool swizzle128) {
+                 int swizzle_bytes) {
   if (!load_encode_fn()) return fail(RB_E_DEVICE, "cuTensorMapEncodeTiled unavailable");
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0)
     return fail(RB_E_SHAPE, "tensor base %p is not 16-byte aligned", base);
@@ -76,7 +76,10 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t ro
   cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                        : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                        : swizzle_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                              : CU_TENSOR_MAP_SWIZZLE_NONE,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(RB_E_DEVICE, "cuTensorMapEncodeTiled failed (%d) rows=%llu cols=%llu box=%ux%u",
@@ -117,11 +120,11 @@ static int weight_maps(Weight& w) {
     const int bn = bns[i];
     int rc;
     if (w.kind == RB_WEIGHT_Q8_0) {
-      if ((rc = make_tmap_2d(&w.tm_codes[i], w.codes, 1, w.n, w.k, w.k, 64, bn, false)) != RB_OK) return rc;
-      if ((rc = make_tmap_2d(&w.tm_scales[i], w.scales, 2, w.k / 32, w.n, w.pitch, bn, 2, false)) != RB_OK)
+      if ((rc = make_tmap_2d(&w.tm_codes[i], w.codes, 1, w.n, w.k, w.k, 64, bn, 0)) != RB_OK) return rc;
+      if ((rc = make_tmap_2d(&w.tm_scales[i], w.scales, 2, w.k / 32, w.n, w.pitch, bn, 2, 0)) != RB_OK)
         return rc;
     } else if (i < 2) {
-      if ((rc = make_tmap_2d(&w.tm_codes[i], w.codes, 1, w.n, w.k, w.k, 128, bn, true)) != RB_OK) return rc;
+      if ((rc = make_tmap_2d(&w.tm_codes[i], w.codes, 1, w.n, w.k, w.k, 128, bn, 128)) != RB_OK) return rc;
     }
   }
   return RB_OK;
@@ -133,7 +136,7 @@ static bool output_map(CUtensorMap* map, void* y, int y_dtype, int64_t m, int64_
   const int eb = (y_dtype == RB_DTYPE_F16 || y_dtype == RB_DTYPE_BF16) ? 2 : 4;
   if ((reinterpret_cast<uintptr_t>(y) & 15) != 0 || (n * eb) % 16 != 0) return false;
   const std::string saved = g_last_error;
-  const bool ok = make_tmap_2d(map, y, eb, m, n, n, 128 / eb, 32, true) == RB_OK;
+  const bool ok = make_tmap_2d(map, y, eb, m, n, n, 128 / eb, 32, 128) == RB_OK;
   g_last_error = saved;
   return ok;
 }
@@ -163,6 +166,7 @@ struct Engine {
   std::unordered_map<int64_t, Weight> weights;
   int64_t next_id = 1;
   Scratch act;       // activation staging (f16 or int8 codes)
+  Scratch pad;       // zero-padded attention heads (head_dim 72 -> 80)
   Scratch rowscale;  // per-row scales
   Scratch io_in, io_out, io_k, io_v;  // host-entry staging
   cudaStream_t host_stream = nullptr;
@@ -260,7 +264,7 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
     int bn = 0, mh = 1;
     gemm_pick(false, L.M, L.N, e->num_sms, &bn, &mh);
     CUtensorMap tmA, tmC;
-    if ((rc = make_tmap_2d(&tmA, a, 2, m, k, k, 64, 128 * mh, true)) != RB_OK) return rc;
+    if ((rc = make_tmap_2d(&tmA, a, 2, m, k, k, 64, 128 * mh, 128)) != RB_OK) return rc;
     const bool tstore = output_map(&tmC, y, y_dtype, m, w.n);
     const int bi = bn_index(bn);
     if ((rc = launch_q8_gemm(L, bn, mh, tmA, w.tm_codes[bi], w.tm_scales[bi], tstore ? &tmC : nullptr,
@@ -279,7 +283,7 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
       return fail(rc, "row quantiser launch failed");
     g_launches++;
     CUtensorMap tmA, tmC;
-    if ((rc = make_tmap_2d(&tmA, codes, 1, m, k, k, 128, 128, true)) != RB_OK) return rc;
+    if ((rc = make_tmap_2d(&tmA, codes, 1, m, k, k, 128, 128, 128)) != RB_OK) return rc;
     L.s_row = rs;
     L.s_col = reinterpret_cast<const float*>(w.scales);
     L.out_scale = w.out_scale;
@@ -306,8 +310,8 @@ static int attention_locked(Engine* e, const void* q, int64_t ldq, const void* k
                 (long long)n_q, (long long)n_kv, head_dim, (long long)batch);
   if (n_head <= 0 || n_kv_heads <= 0 || n_head % n_kv_heads != 0)
     return fail(RB_E_SHAPE, "flash_attn/heads: n_head=%d n_kv_heads=%d", n_head, n_kv_heads);
-  if (head_dim != 64 && head_dim != 128)
-    return fail(RB_E_UNSUPPORTED, "flash_attn/dims: head_dim %d (supported: 64, 128)", head_dim);
+  if (head_dim != 64 && head_dim != 128 && head_dim != 72)
+    return fail(RB_E_UNSUPPORTED, "flash_attn/dims: head_dim %d (supported: 64, 72, 128)", head_dim);
   if (mask_mode < RB_MASK_NONE || mask_mode > RB_MASK_CAUSAL_BLOCK)
     return fail(RB_E_SHAPE, "unknown mask mode %d", mask_mode);
   const bool block = mask_mode == RB_MASK_NONE_BLOCK || mask_mode == RB_MASK_WINDOW_BLOCK ||
@@ -357,11 +361,44 @@ static int attention_locked(Engine* e, const void* q, int64_t ldq, const void* k
   } else if (dtype != RB_DTYPE_F16 && dtype != RB_DTYPE_BF16) {
     return fail(RB_E_SHAPE, "attention dtype %d", dtype);
   }
-  CUtensorMap tq, tk, tv;
-  // Q tiles are 128 query rows, K/V tiles 64 keys; 64-element (128-B) columns.
-  if ((rc = make_tmap_2d(&tq, qh, 2, batch * n_q, wq, ldq, 64, 128, true)) != RB_OK) return rc;
-  if ((rc = make_tmap_2d(&tk, kh, 2, batch * n_kv, wk, ldk, 64, 64, true)) != RB_OK) return rc;
-  if ((rc = make_tmap_2d(&tv, vh, 2, batch * n_kv, wk, ldv, 64, 64, true)) != RB_OK) return rc;
+  // head_dim 72 is staged as 80 (the UMMA K granularity): q/k/v are copied
+  // into zero-padded [rows, heads, 80] scratch and the output keeps 72 columns.
+  int d_stage = head_dim;
+  int64_t sq = ldq, sk = ldk, sv = ldv, cq = wq, ck = wk;
+  if (head_dim == 72) {
+    d_stage = 80;
+    const size_t pq = static_cast<size_t>(batch * n_q) * n_head * 80 * 2;
+    const size_t pk = static_cast<size_t>(batch * n_kv) * n_kv_heads * 80 * 2;
+    const size_t aq = (pq + 255) & ~size_t(255), ak = (pk + 255) & ~size_t(255);
+    if ((rc = e->pad.grow(aq + 2 * ak, "attention head padding")) != RB_OK) return rc;
+    uint8_t* base = reinterpret_cast<uint8_t*>(e->pad.ptr);
+    void* qp = base;
+    void* kp = base + aq;
+    void* vp = base + aq + ak;
+    if ((rc = launch_pad_heads(qh, ldq, batch * n_q, n_head, 72, qp, 80, st)) != RB_OK ||
+        (rc = launch_pad_heads(kh, ldk, batch * n_kv, n_kv_heads, 72, kp, 80, st)) != RB_OK ||
+        (rc = launch_pad_heads(vh, ldv, batch * n_kv, n_kv_heads, 72, vp, 80, st)) != RB_OK)
+      return fail(rc, "head_dim 72 staging: q/k/v need 16-byte-aligned rows (rc from the pad launch)");
+    g_launches += 3;
+    qh = qp; kh = kp; vh = vp;
+    cq = sq = static_cast<int64_t>(n_head) * 80;
+    ck = sk = sv = static_cast<int64_t>(n_kv_heads) * 80;
+  }
+  CUtensorMap tm[6];
+  // Q tiles are 128 query rows, K/V tiles 64 keys; 64-element (128-B) column
+  // atoms, plus 16-element (32-B) tail atoms for the padded 80-wide heads.
+  if ((rc = make_tmap_2d(&tm[0], qh, 2, batch * n_q, cq, sq, 64, 128, 128)) != RB_OK) return rc;
+  if ((rc = make_tmap_2d(&tm[1], kh, 2, batch * n_kv, ck, sk, 64, 64, 128)) != RB_OK) return rc;
+  if ((rc = make_tmap_2d(&tm[2], vh, 2, batch * n_kv, ck, sv, 64, 64, 128)) != RB_OK) return rc;
+  if (d_stage == 80) {
+    if ((rc = make_tmap_2d(&tm[3], qh, 2, batch * n_q, cq, sq, 16, 128, 32)) != RB_OK) return rc;
+    if ((rc = make_tmap_2d(&tm[4], kh, 2, batch * n_kv, ck, sk, 16, 64, 32)) != RB_OK) return rc;
+    if ((rc = make_tmap_2d(&tm[5], vh, 2, batch * n_kv, ck, sv, 16, 64, 32)) != RB_OK) return rc;
+  } else {
+    tm[3] = tm[0];
+    tm[4] = tm[1];
+    tm[5] = tm[2];
+  }
   if ((reinterpret_cast<uintptr_t>(oh) & 15) != 0 || (ldo * 2) % 16 != 0)
     return fail(RB_E_SHAPE, "attention output must be 16-byte aligned");
   AttnLaunch L{};
@@ -372,10 +409,11 @@ static int attention_locked(Engine* e, const void* q, int64_t ldq, const void* k
   L.n_kv = static_cast<int>(n_kv);
   L.n_head = n_head;
   L.n_kv_heads = n_kv_heads;
-  L.head_dim = head_dim;
-  L.ldq = static_cast<int>(ldq);
-  L.ldk = static_cast<int>(ldk);
-  L.ldv = static_cast<int>(ldv);
+  L.head_dim = d_stage;
+  L.d_out = head_dim;
+  L.ldq = static_cast<int>(sq);
+  L.ldk = static_cast<int>(sk);
+  L.ldv = static_cast<int>(sv);
   L.ldo = static_cast<int>(ldo);
   L.scale = scale;
   L.softcap = softcap;
@@ -385,7 +423,7 @@ static int attention_locked(Engine* e, const void* q, int64_t ldq, const void* k
   L.kv_start = kv_start;
   L.err = e->err;
   L.num_sms = e->num_sms;
-  if ((rc = launch_attention(tq, tk, tv, L, st)) != RB_OK) return fail(rc, "attention launch failed");
+  if ((rc = launch_attention(tm, L, st)) != RB_OK) return fail(rc, "attention launch failed");
   g_launches++;
   if (dtype == RB_DTYPE_F32) {
     if ((rc = launch_cast(oh, RB_DTYPE_F16, out, RB_DTYPE_F32, batch * n_q * wq, st)) != RB_OK)
@@ -588,6 +626,40 @@ int64_t rb_pack_w8a8(const int8_t* codes_host, const float* w_scale_host, int64_
   return id;
 }
 
+int64_t rb_pack_f32_w8a8_device(const float* w_dev, int64_t n, int64_t k, float in_scale,
+                                float out_scale) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Engine* e;
+  int rc = ensure_engine(&e);
+  if (rc) return rc;
+  if (!w_dev) return fail(RB_E_SHAPE, "null weight");
+  if (n <= 0 || k <= 0 || k % 16 != 0)
+    return fail(RB_E_SHAPE, "W8A8 weight [%lld, %lld]: K must be a positive multiple of 16",
+                (long long)n, (long long)k);
+  if (!(in_scale >= 0.0f)) return fail(RB_E_SHAPE, "QAT input scale must not be negative");
+  Weight w;
+  w.kind = RB_WEIGHT_W8A8;
+  w.n = n;
+  w.k = k;
+  w.in_scale = in_scale;
+  w.out_scale = out_scale;
+  if (cudaMalloc(&w.codes, static_cast<size_t>(n) * k) != cudaSuccess ||
+      cudaMalloc(&w.scales, static_cast<size_t>(n) * 4) != cudaSuccess) {
+    cudaGetLastError();
+    if (w.codes) cudaFree(w.codes);
+    return fail(RB_E_NOMEM, "W8A8 pack: device allocation failed");
+  }
+  if ((rc = launch_w8a8_weight_quant(w_dev, n, k, w.codes, reinterpret_cast<float*>(w.scales), nullptr)) != RB_OK)
+    return fail(rc, "W8A8 weight quantiser launch failed");
+  g_launches++;
+  RB_CUDA(cudaDeviceSynchronize(), "W8A8 weight quantiser");
+  if ((rc = weight_maps(w)) != RB_OK) return rc;
+  w.bytes = static_cast<size_t>(n) * k + static_cast<size_t>(n) * 4;
+  const int64_t id = e->next_id++;
+  e->weights[id] = w;
+  return id;
+}
+
 int rb_weight_info(int64_t id, int* kind, int64_t* n, int64_t* k) {
   std::lock_guard<std::mutex> lk(g_mu);
   Engine* e;
@@ -760,6 +832,22 @@ int rb_add_rms_norm(float* x, const void* delta_f16, const float* w, float eps, 
   return rc == RB_OK ? RB_OK : fail(rc, "add_rms_norm: unsupported width %lld", (long long)d);
 }
 
+int rb_add_layer_norm(float* x, const void* delta_f16, const float* g, const float* b, float eps,
+                      void* h_f16, int64_t rows, int64_t d, void* stream) {
+  if (!x || !g || !b || !h_f16 || rows <= 0) return fail(RB_E_SHAPE, "add_layer_norm: bad arguments");
+  const int rc = launch_add_layer_norm(x, delta_f16, g, b, eps, h_f16, rows, static_cast<int>(d),
+                                       reinterpret_cast<cudaStream_t>(stream));
+  g_launches++;
+  return rc == RB_OK ? RB_OK : fail(rc, "add_layer_norm: unsupported width %lld", (long long)d);
+}
+
+int rb_gelu(void* y_f16, int64_t count, void* stream) {
+  if (!y_f16 || count <= 0) return fail(RB_E_SHAPE, "gelu: bad arguments");
+  const int rc = launch_gelu_f16(y_f16, count, reinterpret_cast<cudaStream_t>(stream));
+  g_launches++;
+  return rc == RB_OK ? RB_OK : fail(rc, "gelu: count must be a multiple of 8");
+}
+
 int rb_qk_norm_rope(void* qkv_f16, int64_t ld, int64_t tokens, int n_q_heads, int n_kv_heads,
                     int head_dim, const float* q_norm_w, const float* k_norm_w, float eps,
                     const float* cos_t, const float* sin_t, int64_t seq, void* stream) {
@@ -830,7 +918,7 @@ int rb_matmul_i8_acc(int64_t id, const int8_t* codes, int64_t m, int32_t* acc, v
   const Weight& w = it->second;
   if (m <= 0 || !codes || !acc) return fail(RB_E_SHAPE, "bad int8 matmul arguments");
   CUtensorMap tmA, tmC;
-  if ((rc = make_tmap_2d(&tmA, codes, 1, m, w.k, w.k, 128, 128, true)) != RB_OK) return rc;
+  if ((rc = make_tmap_2d(&tmA, codes, 1, m, w.k, w.k, 128, 128, 128)) != RB_OK) return rc;
   GemmLaunch L{};
   L.M = static_cast<int>(m);
   L.N = static_cast<int>(w.n);
@@ -859,7 +947,7 @@ int rb_mem_stats(int64_t* weights_bytes, int64_t* scratch_bytes, int64_t* num_we
   for (auto& kv : e->weights) wb += static_cast<int64_t>(kv.second.bytes);
   if (weights_bytes) *weights_bytes = wb;
   if (scratch_bytes)
-    *scratch_bytes = static_cast<int64_t>(e->act.bytes + e->rowscale.bytes + e->io_in.bytes +
+    *scratch_bytes = static_cast<int64_t>(e->act.bytes + e->pad.bytes + e->rowscale.bytes + e->io_in.bytes +
                                           e->io_out.bytes + e->io_k.bytes + e->io_v.bytes);
   if (num_weights) *num_weights = static_cast<int64_t>(e->weights.size());
   return RB_OK;

@@ -67,18 +67,27 @@ struct Params {
   float softcap;
   int dlo, dhi;        // visible iff dlo <= (k_off + j) - (q_off + i) <= dhi
   int q_off, k_off;
+  int d_out;           // output columns per head (<= D: the real head_dim)
   // Sequences lie back to back: sequence b (blockIdx.y) owns query rows
   // [b*n_q, (b+1)*n_q) and key rows [b*n_kv, (b+1)*n_kv) of the tensors.
   uint32_t* err;
 };
 
+// A head row of D elements is staged as D/64 128-byte-swizzled atoms of 64
+// columns plus, when D % 64 == 16 (D = 80: head_dim 72 zero-padded to the
+// UMMA K granularity), one 32-byte-swizzled tail atom of 16 columns.
 template <int D>
 struct Smem {
   static constexpr int ATOMS = D / 64;              // 64-element (128-B) column atoms
+  static constexpr int TAIL = D % 64;               // 0 or 16 columns (32-B rows)
+  static_assert(TAIL == 0 || TAIL == 16, "head width must be 64k or 64k+16");
   static constexpr int Q_ATOM = BM * 128;           // 16 KB
   static constexpr int KV_ATOM = BN * 128;          // 8 KB
-  static constexpr int Q_TILE = ATOMS * Q_ATOM;
-  static constexpr int KV_TILE = ATOMS * KV_ATOM;
+  static constexpr int Q_TAIL_OFF = ATOMS * Q_ATOM;
+  static constexpr int KV_TAIL_OFF = ATOMS * KV_ATOM;
+  static constexpr int Q_TILE = ATOMS * Q_ATOM + BM * TAIL * 2;
+  static constexpr int KV_TILE = ATOMS * KV_ATOM + BN * TAIL * 2;
+  static_assert(Q_TILE % 1024 == 0 && KV_TILE % 1024 == 0, "tiles keep 1024-B alignment");
   static constexpr int Q_OFF = 0;                   // 2 slots
   static constexpr int K_OFF = 2 * Q_TILE;
   static constexpr int V_OFF = K_OFF + KV_STAGES * KV_TILE;
@@ -147,7 +156,9 @@ __device__ __forceinline__ SlotInfo slot_info(const Params& p, int g, int item) 
 template <int D, bool BF16, bool SOFTCAP>
 __global__ void __launch_bounds__(kThreads, 1)
 attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-            const __grid_constant__ CUtensorMap tmV, Params p) {
+            const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmQt,
+            const __grid_constant__ CUtensorMap tmKt, const __grid_constant__ CUtensorMap tmVt,
+            Params p) {
   using L = Smem<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -215,10 +226,14 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       tma_prefetch_desc(&tmV);
       const int nslots = act1 ? 2 : 1;
       mbar_arrive_expect_tx(q_full, nslots * L::Q_TILE);
-      for (int s = 0; s < nslots; ++s)
+      for (int s = 0; s < nslots; ++s) {
         for (int a = 0; a < L::ATOMS; ++a)
           tma_load_2d(smem + L::Q_OFF + s * L::Q_TILE + a * L::Q_ATOM, &tmQ, q_full,
                       sl[s].head * D + a * 64, q_row0 + sl[s].qt * BM);
+        if (L::TAIL)
+          tma_load_2d(smem + L::Q_OFF + s * L::Q_TILE + L::Q_TAIL_OFF, &tmQt, q_full,
+                      sl[s].head * D + L::ATOMS * 64, q_row0 + sl[s].qt * BM);
+      }
       for (int j = J0; j <= J1; ++j) {
         const int jl = j - J0, st = jl % KV_STAGES;
         const uint32_t ph = ((jl / KV_STAGES) & 1) ^ 1;
@@ -227,18 +242,25 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         for (int a = 0; a < L::ATOMS; ++a)
           tma_load_2d(smem + L::K_OFF + st * L::KV_TILE + a * L::KV_ATOM, &tmK, &k_full[st],
                       g * D + a * 64, kv_row0 + j * BN);
+        if (L::TAIL)
+          tma_load_2d(smem + L::K_OFF + st * L::KV_TILE + L::KV_TAIL_OFF, &tmKt, &k_full[st],
+                      g * D + L::ATOMS * 64, kv_row0 + j * BN);
         if (!mbar_wait(&v_empty[st], ph, p.err, abort_flag)) break;
         mbar_arrive_expect_tx(&v_full[st], L::KV_TILE);
         for (int a = 0; a < L::ATOMS; ++a)
           tma_load_2d(smem + L::V_OFF + st * L::KV_TILE + a * L::KV_ATOM, &tmV, &v_full[st],
                       g * D + a * 64, kv_row0 + j * BN);
+        if (L::TAIL)
+          tma_load_2d(smem + L::V_OFF + st * L::KV_TILE + L::KV_TAIL_OFF, &tmVt, &v_full[st],
+                      g * D + L::ATOMS * 64, kv_row0 + j * BN);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ UMMA issuer
     if (elect_one_sync()) {
       constexpr uint32_t idesc_s = idesc_f16(BM, BN, BF16, false, false);
-      constexpr uint32_t idesc_o = idesc_f16(BM, D, BF16, false, true);
+      constexpr uint32_t idesc_o = idesc_f16(BM, L::ATOMS * 64, BF16, false, true);
+      constexpr uint32_t idesc_ot = idesc_f16(BM, L::TAIL ? L::TAIL : 16, BF16, false, true);
       const uint32_t q_addr = smem_u32(smem + L::Q_OFF);
       const uint32_t k_addr = smem_u32(smem + L::K_OFF);
       const uint32_t v_addr = smem_u32(smem + L::V_OFF);
@@ -259,11 +281,15 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
           }
           const uint32_t d_tmem = tmem_base + s * 256 + b * 64;
 #pragma unroll
-          for (int ks = 0; ks < D / 16; ++ks) {
+          for (int ks = 0; ks < L::ATOMS * 4; ++ks) {
             const uint32_t qo = (ks >> 2) * L::Q_ATOM + (ks & 3) * 32;
             const uint32_t ko = (ks >> 2) * L::KV_ATOM + (ks & 3) * 32;
             umma_f16_ss(d_tmem, desc_kmajor_sw128(q_addr + s * L::Q_TILE + qo),
                         desc_kmajor_sw128(k_addr + st * L::KV_TILE + ko), idesc_s, ks > 0);
+          }
+          if (L::TAIL) {  // the 16-column tail: one K step on 32-B-swizzled rows
+            umma_f16_ss(d_tmem, desc_kmajor_sw32(q_addr + s * L::Q_TILE + L::Q_TAIL_OFF),
+                        desc_kmajor_sw32(k_addr + st * L::KV_TILE + L::KV_TAIL_OFF), idesc_s, 1u);
           }
           umma_commit(&s_full[2 * s + b]);
           ++n_s[s];
@@ -285,8 +311,13 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
           const uint32_t p_tmem = tmem_base + s * 256 + b * 64;
 #pragma unroll
           for (int ks = 0; ks < BN / 16; ++ks) {
+            const uint32_t acc = (n_pv[s] > 0 || ks > 0) ? 1u : 0u;
             const uint64_t vd = desc_mnmajor_sw128(v_addr + st * L::KV_TILE + ks * 2048, L::KV_ATOM, 1024);
-            umma_f16_ts(o_tmem, p_tmem + ks * 8, vd, idesc_o, (n_pv[s] > 0 || ks > 0) ? 1u : 0u);
+            umma_f16_ts(o_tmem, p_tmem + ks * 8, vd, idesc_o, acc);
+            if (L::TAIL) {  // O columns [64*ATOMS, D) from the tail atom (16 key rows = 512 B)
+              const uint64_t vt = desc_mnmajor_sw32(v_addr + st * L::KV_TILE + L::KV_TAIL_OFF + ks * 512);
+              umma_f16_ts(o_tmem + L::ATOMS * 64, p_tmem + ks * 8, vt, idesc_ot, acc);
+            }
           }
           umma_commit(&s_free[2 * s + b]);
           umma_commit(&o_done[s]);
@@ -470,10 +501,11 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
                                   __uint_as_float(r[2 * i + 1]) * inv_l);
             uint4* dst = reinterpret_cast<uint4*>(
                 reinterpret_cast<uint16_t*>(p.out) + static_cast<int64_t>(q_row0 + qrow) * p.ldo +
-                me.head * D + c0);
+                me.head * p.d_out + c0);
 #pragma unroll
             for (int i = 0; i < 4; ++i)
-              dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+              if (c0 + 8 * i + 8 <= p.d_out)  // 8-column groups of the real head width
+                dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
           }
         }
       }
@@ -490,8 +522,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
 }
 
 template <int D, bool BF16, bool SOFTCAP>
-static int launch_impl(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
-                       const Params& p, dim3 grid, cudaStream_t stream) {
+static int launch_impl(const CUtensorMap* tm, const Params& p, dim3 grid, cudaStream_t stream) {
   static uint64_t configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -501,24 +532,23 @@ static int launch_impl(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUt
       return RB_E_DEVICE;
     configured |= 1ull << (dev & 63);
   }
-  attn_kernel<D, BF16, SOFTCAP><<<grid, kThreads, Smem<D>::BYTES, stream>>>(tmQ, tmK, tmV, p);
+  attn_kernel<D, BF16, SOFTCAP><<<grid, kThreads, Smem<D>::BYTES, stream>>>(tm[0], tm[1], tm[2], tm[3],
+                                                                          tm[4], tm[5], p);
   return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
 }
 
 template <int D>
-static int launch_d(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
-                    const Params& p, dim3 grid, bool bf16, cudaStream_t stream) {
+static int launch_d(const CUtensorMap* tm, const Params& p, dim3 grid, bool bf16, cudaStream_t stream) {
   if (p.softcap != 0.0f)
-    return bf16 ? launch_impl<D, true, true>(tmQ, tmK, tmV, p, grid, stream)
-                : launch_impl<D, false, true>(tmQ, tmK, tmV, p, grid, stream);
-  return bf16 ? launch_impl<D, true, false>(tmQ, tmK, tmV, p, grid, stream)
-              : launch_impl<D, false, false>(tmQ, tmK, tmV, p, grid, stream);
+    return bf16 ? launch_impl<D, true, true>(tm, p, grid, stream)
+                : launch_impl<D, false, true>(tm, p, grid, stream);
+  return bf16 ? launch_impl<D, true, false>(tm, p, grid, stream)
+              : launch_impl<D, false, false>(tm, p, grid, stream);
 }
 
 }  // namespace attn
 
-int launch_attention(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
-                     const AttnLaunch& L, cudaStream_t stream) {
+int launch_attention(const CUtensorMap* tm, const AttnLaunch& L, cudaStream_t stream) {
   using namespace attn;
   Params p{};
   p.out = L.out;
@@ -534,6 +564,7 @@ int launch_attention(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUten
   p.scale_log2 = L.scale * kLog2e;
   p.softcap = L.softcap;
   p.err = L.err;
+  p.d_out = L.d_out;
   // Mask band in relative coordinates (key - query).
   auto clampw = [](int64_t w) { return static_cast<int>(w > (kNoBound / 2) ? (kNoBound / 2) : w); };
   p.dlo = -kNoBound;
@@ -572,8 +603,9 @@ int launch_attention(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUten
   }
   const dim3 grid(p.pairs_per_group * L.n_kv_heads, L.batch > 0 ? L.batch : 1);
   const bool bf16 = L.dtype == RB_DTYPE_BF16;
-  if (L.head_dim == 128) return launch_d<128>(tmQ, tmK, tmV, p, grid, bf16, stream);
-  if (L.head_dim == 64) return launch_d<64>(tmQ, tmK, tmV, p, grid, bf16, stream);
+  if (L.head_dim == 128) return launch_d<128>(tm, p, grid, bf16, stream);
+  if (L.head_dim == 64) return launch_d<64>(tm, p, grid, bf16, stream);
+  if (L.head_dim == 80) return launch_d<80>(tm, p, grid, bf16, stream);
   return RB_E_UNSUPPORTED;
 }
 

@@ -204,6 +204,73 @@ __global__ void add_rms_norm_kernel(float* x, const __half* delta, const float* 
   }
 }
 
+// x [rows, D] f32 (+= delta f16 when non-null), then
+// h = (x - mean) / sqrt(var + eps) * g + b as f16 (pre-LayerNorm of the
+// SigLIP-style tower; var is the biased mean of squared deviations).
+template <int NV>
+__global__ void add_layer_norm_kernel(float* x, const __half* delta, const float* g, const float* b,
+                                      float eps, __half* h, int64_t rows) {
+  constexpr int D = 128 * NV;
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += nw) {
+    float v[4 * NV];
+    float sum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = j * 128 + lane * 4;
+      float4 xv = *reinterpret_cast<const float4*>(x + r * D + c);
+      if (delta) {
+        const uint2 d2 = *reinterpret_cast<const uint2*>(delta + r * D + c);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&d2.x));
+        const float2 bb = __half22float2(*reinterpret_cast<const __half2*>(&d2.y));
+        xv.x += a.x; xv.y += a.y; xv.z += bb.x; xv.w += bb.y;
+        *reinterpret_cast<float4*>(x + r * D + c) = xv;
+      }
+      v[4 * j] = xv.x; v[4 * j + 1] = xv.y; v[4 * j + 2] = xv.z; v[4 * j + 3] = xv.w;
+      sum += (xv.x + xv.y) + (xv.z + xv.w);
+    }
+    const float mean = warp_sum(sum) / static_cast<float>(D);
+    float var = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4 * NV; ++i) {
+      const float dv = v[i] - mean;
+      var = fmaf(dv, dv, var);
+    }
+    var = warp_sum(var) / static_cast<float>(D);
+    const float inv = 1.0f / sqrtf(var + eps);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = j * 128 + lane * 4;
+      const float4 gv = *reinterpret_cast<const float4*>(g + c);
+      const float4 bv = *reinterpret_cast<const float4*>(b + c);
+      const __half2 a = __floats2half2_rn((v[4 * j] - mean) * inv * gv.x + bv.x,
+                                          (v[4 * j + 1] - mean) * inv * gv.y + bv.y);
+      const __half2 bb = __floats2half2_rn((v[4 * j + 2] - mean) * inv * gv.z + bv.z,
+                                           (v[4 * j + 3] - mean) * inv * gv.w + bv.w);
+      uint2 o;
+      o.x = *reinterpret_cast<const uint32_t*>(&a);
+      o.y = *reinterpret_cast<const uint32_t*>(&bb);
+      *reinterpret_cast<uint2*>(h + r * D + c) = o;
+    }
+  }
+}
+
+// In place on f16 [count]: y = gelu_tanh(y) (host.rs:15-18), 8 elements per thread.
+__global__ void gelu_f16_kernel(__half* y, int64_t count8) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < count8;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    uint4 u = *reinterpret_cast<const uint4*>(y + i * 8);
+    __half2* h = reinterpret_cast<__half2*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __half22float2(h[j]);
+      h[j] = __floats2half2_rn(gelu_tanh_f(f.x), gelu_tanh_f(f.y));
+    }
+    *reinterpret_cast<uint4*>(y + i * 8) = u;
+  }
+}
+
 // In place on qkv [T, ld] f16: heads [0, hq) of width 128 at column 0 (q) use
 // wq, heads [hq, hq+hk) (k) use wk. One warp per token: the RoPE row of the
 // token's position and both norm weights are loaded once, then every head is
@@ -264,7 +331,37 @@ __global__ void last_token_l2_kernel(const float* x, int d, int seq, int batch, 
   for (int i = lane; i < d; i += 32) out[static_cast<int64_t>(b) * d + i] = row[i] * inv * w[i] * inv2;
 }
 
+// ---------------------------------------------------------------- head padding
+// One thread per 16-byte group (8 elements) of the padded output.
+__global__ void pad_heads_kernel(const uint16_t* __restrict__ src, int64_t ld_src, int64_t rows, int heads,
+                                 int d, uint16_t* __restrict__ dst, int dp) {
+  const int g_per_head = dp / 8, g_real = d / 8;
+  const int64_t total = rows * heads * g_per_head;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int gi = static_cast<int>(i % g_per_head);
+    const int64_t rh = i / g_per_head;
+    const int h = static_cast<int>(rh % heads);
+    const int64_t r = rh / heads;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (gi < g_real) v = *reinterpret_cast<const uint4*>(src + r * ld_src + static_cast<int64_t>(h) * d + gi * 8);
+    *reinterpret_cast<uint4*>(dst + i * 8) = v;
+  }
+}
+
 // ---------------------------------------------------------------- launchers
+int launch_pad_heads(const void* src, int64_t ld_src, int64_t rows, int heads, int d, void* dst,
+                     int dp, cudaStream_t st) {
+  if (d % 8 || dp % 8 || dp < d || ld_src % 8) return RB_E_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) return RB_E_SHAPE;
+  int64_t g = (rows * heads * (dp / 8) + 255) / 256;
+  if (g > 148 * 32) g = 148 * 32;
+  if (g < 1) g = 1;
+  pad_heads_kernel<<<static_cast<int>(g), 256, 0, st>>>(reinterpret_cast<const uint16_t*>(src), ld_src, rows,
+                                                        heads, d, reinterpret_cast<uint16_t*>(dst), dp);
+  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
+}
+
 #define RB_LAUNCH_OK() (cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE)
 
 int launch_rms_norm(const void* x, int xdt, const float* w, float eps, void* y, int ydt, int64_t rows,
@@ -326,6 +423,29 @@ int launch_add_rms_norm(float* x, const void* delta, const float* w, float eps, 
     case 1152: add_rms_norm_kernel<9><<<grid, 256, 0, st>>>(x, dl, w, eps, hh, rows); break;
     default: return RB_E_UNSUPPORTED;
   }
+  return RB_LAUNCH_OK();
+}
+
+int launch_add_layer_norm(float* x, const void* delta, const float* g, const float* b, float eps,
+                          void* h, int64_t rows, int d, cudaStream_t st) {
+  const int grid = grid_for_rows(rows, 8);
+  const __half* dl = reinterpret_cast<const __half*>(delta);
+  __half* hh = reinterpret_cast<__half*>(h);
+  switch (d) {
+    case 1152: add_layer_norm_kernel<9><<<grid, 256, 0, st>>>(x, dl, g, b, eps, hh, rows); break;
+    case 1024: add_layer_norm_kernel<8><<<grid, 256, 0, st>>>(x, dl, g, b, eps, hh, rows); break;
+    case 768: add_layer_norm_kernel<6><<<grid, 256, 0, st>>>(x, dl, g, b, eps, hh, rows); break;
+    default: return RB_E_UNSUPPORTED;
+  }
+  return RB_LAUNCH_OK();
+}
+
+int launch_gelu_f16(void* y, int64_t count, cudaStream_t st) {
+  if (count % 8) return RB_E_SHAPE;
+  int64_t g = (count / 8 + 255) / 256;
+  if (g > 148 * 32) g = 148 * 32;
+  if (g < 1) g = 1;
+  gelu_f16_kernel<<<static_cast<int>(g), 256, 0, st>>>(reinterpret_cast<__half*>(y), count / 8);
   return RB_LAUNCH_OK();
 }
 

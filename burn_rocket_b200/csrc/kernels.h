@@ -54,6 +54,8 @@ int launch_quantize_rows_i8(const void* x, int x_dtype, int64_t m, int64_t k, fl
 // so every scale row starts on a 16-byte boundary (TMA).
 int launch_q8_0_encode(const float* w, int64_t n, int64_t k, int64_t pitch, int8_t* codes,
                        uint16_t* scales, cudaStream_t stream);
+int launch_w8a8_weight_quant(const float* w, int64_t n, int64_t k, int8_t* codes, float* scale,
+                             cudaStream_t stream);
 int launch_q8_0_unpack_blocks(const uint8_t* blocks, int64_t n, int64_t k, int64_t pitch,
                               int8_t* codes, uint16_t* scales, cudaStream_t stream);
 
@@ -66,7 +68,8 @@ struct AttnLaunch {
   int dtype;  // RB_DTYPE_F16 or RB_DTYPE_BF16
   int batch;     // sequences laid back to back (>= 1)
   int n_q, n_kv;  // per sequence
-  int n_head, n_kv_heads, head_dim;
+  int n_head, n_kv_heads, head_dim;  // head_dim: staged width (64, 80 or 128)
+  int d_out;                          // output columns per head (real head_dim)
   int ldq, ldk, ldv, ldo;  // row strides in elements
   float scale, softcap;
   int mask_mode;
@@ -74,8 +77,9 @@ struct AttnLaunch {
   uint32_t* err;
   int num_sms;
 };
-int launch_attention(const CUtensorMap& tmQ, const CUtensorMap& tmK, const CUtensorMap& tmV,
-                     const AttnLaunch& L, cudaStream_t stream);
+// tm[0..2]: Q, K, V maps of the 64-column atoms (128-B swizzle); tm[3..5]: the
+// 16-column tail maps (32-B swizzle) used when head_dim == 80.
+int launch_attention(const CUtensorMap* tm, const AttnLaunch& L, cudaStream_t stream);
 
 // Glue (glue.cu).
 int launch_rms_norm(const void* x, int xdt, const float* w, float eps, void* y, int ydt, int64_t rows,
@@ -92,6 +96,13 @@ int launch_add_rms_norm(float* x, const void* delta, const float* w, float eps, 
 int launch_qk_norm_rope(void* qkv, int64_t ld, int64_t tokens, int hq, int hk, const float* wq,
                         const float* wk, float eps, const float* cos_t, const float* sin_t, int seq,
                         cudaStream_t st);
+// dst[r, h, 0:d] = src[r, h*d : h*d+d], dst[r, h, d:dp] = 0 (2-byte elements;
+// d and dp multiples of 8).
+int launch_add_layer_norm(float* x, const void* delta, const float* g, const float* b, float eps,
+                          void* h, int64_t rows, int d, cudaStream_t st);
+int launch_gelu_f16(void* y, int64_t count, cudaStream_t st);
+int launch_pad_heads(const void* src, int64_t ld_src, int64_t rows, int heads, int d, void* dst,
+                     int dp, cudaStream_t st);
 int launch_last_token_l2(const float* x, int d, int seq, int batch, const float* w, float eps,
                          float* out, cudaStream_t st);
 
@@ -99,7 +110,7 @@ int launch_last_token_l2(const float* x, int d, int seq, int batch, const float*
 // 128-byte swizzle; box = {box_cols, box_rows}.
 int make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t rows,
                  uint64_t cols, uint64_t row_stride_elems, uint32_t box_cols, uint32_t box_rows,
-                 bool swizzle128);
+                 int swizzle_bytes);  // 0 (none), 32, 64 or 128
 // Index of an N tile in the per-weight tensor-map caches ({256,128,96,64}).
 int bn_index(int bn);
 

@@ -95,7 +95,7 @@ extern "C" int rb_matmul_w8a8_noalloc(int64_t id, const void* x, int x_dtype, in
     return report_error(rc, "row quantiser launch failed");
   count_launches(1);
   CUtensorMap tmA, tmC;
-  if ((rc = make_tmap_2d(&tmA, codes, 1, m, k, k, 128, 128, true)) != RB_OK) return rc;
+  if ((rc = make_tmap_2d(&tmA, codes, 1, m, k, k, 128, 128, 128)) != RB_OK) return rc;
   GemmLaunch L{};
   L.M = static_cast<int>(m);
   L.N = static_cast<int>(v.n);

@@ -151,6 +151,38 @@ int launch_quantize_rows_i8(const void* x, int x_dtype, int64_t m, int64_t k, fl
   return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
 }
 
+// ---------------------------------------------------------------- W8A8 weight codes
+// Per output channel (row) of an f32 [n, k] weight: s = max(max|w| / 127, 1e-12),
+// code = clamp(rint(w * (1/s)), -127, 127) — symmetric per-channel int8, the
+// form of a QAT checkpoint's codes + w_scale that pack_qat takes
+// (ext.rs:1382-1425). One warp per row.
+__global__ void w8a8_weight_quant_kernel(const float* __restrict__ w, int64_t n, int64_t k,
+                                         int8_t* __restrict__ codes, float* __restrict__ scale) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); r < n; r += nw) {
+    const float* row = w + r * k;
+    float amax = 0.0f;
+    for (int64_t i = lane; i < k; i += 32) amax = fmaxf(amax, fabsf(row[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-12f);
+    const float inv = __fdiv_rn(1.0f, s);
+    for (int64_t i = lane; i < k; i += 32)
+      codes[r * k + i] = static_cast<int8_t>(fminf(fmaxf(rintf(__fmul_rn(row[i], inv)), -127.f), 127.f));
+    if (lane == 0) scale[r] = s;
+  }
+}
+
+int launch_w8a8_weight_quant(const float* w, int64_t n, int64_t k, int8_t* codes, float* scale,
+                             cudaStream_t stream) {
+  int64_t blocks = (n + 7) / 8;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  if (blocks < 1) blocks = 1;
+  w8a8_weight_quant_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(w, n, k, codes, scale);
+  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
+}
+
 // ---------------------------------------------------------------- casts
 template <int SRC, int DST>
 __global__ void cast_kernel(const void* __restrict__ x, void* __restrict__ y, int64_t count) {

@@ -338,6 +338,18 @@ __device__ __forceinline__ uint64_t desc_mnmajor_sw128(uint32_t saddr, uint32_t 
   return smem_desc(saddr, lbo, sbo, Swz::B128);
 }
 
+// K-major operand staged as 32-byte swizzled rows (TMA SWIZZLE_32B, a 16-column
+// f16 box): rows 32 B apart, 8-row groups 256 B apart; one K step per row.
+__device__ __forceinline__ uint64_t desc_kmajor_sw32(uint32_t saddr) {
+  return smem_desc(saddr, 16, 256, Swz::B32);
+}
+
+// MN-major operand with 16 MN elements (32 B) per K row, 32-byte swizzled:
+// K rows 32 B apart, 8-K-row groups 256 B apart.
+__device__ __forceinline__ uint64_t desc_mnmajor_sw32(uint32_t saddr) {
+  return smem_desc(saddr, 16, 256, Swz::B32);
+}
+
 // Instruction descriptor for kind::f16 with f32 accumulation.
 //   bits 4-5 D format (1 = f32), 7-9 A format, 10-12 B format (0 f16, 1 bf16),
 //   15/16 A/B major (0 K-major, 1 MN-major), 17-22 N>>3, 24-28 M>>4.

@@ -1,0 +1,178 @@
+"""SigLIP-style W8A8 vision tower on librocket_b200 (BASELINE config #4).
+
+A synthetic pre-LayerNorm encoder: per layer
+    h = layer_norm_1(x)
+    q|k|v = h · Wqkv^T            (one fused W8A8 matmul, matmul_qat ext.rs:1245-1373)
+    x += attention(q, k, v) · Wo^T  (bidirectional, 16 heads x 72, attention_window(-1)
+                                   as the reference's vision tower calls it, ext.rs:1907-1950)
+    h = layer_norm_2(x)
+    x += gelu_tanh(h · W1^T) · W2^T  (gelu_tanh of host.rs:15-18)
+then the final (post) LayerNorm of every patch. Every projection is W8A8:
+int8 per-output-channel weight codes (the fp16 weights quantised on the device
+by rb_pack_f32_w8a8_device, the form pack_qat takes, ext.rs:1382-1425) and
+dynamic per-token int8 activation codes with the f32 epilogue of
+matmul_qat. Linear layers carry no bias (the reference's W8A8 op has none).
+
+Every op is a librocket_b200 kernel launched through the C ABI; torch only
+allocates device buffers, generates the synthetic weights and captures the
+call sequence into a CUDA graph. The residual stream is f32; matmul
+inputs/outputs are f16. Images are independent, so data parallelism shards
+them over GPUs with no collective.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+from . import _lib
+from . import _check, _dev_ptr, _stream_ptr, matmul, pack_w8a8_float
+from ._lib import DTYPE_F16, MASK_NONE
+
+
+@dataclass(frozen=True)
+class SiglipConfig:
+    layers: int = 27
+    hidden: int = 1152
+    heads: int = 16
+    head_dim: int = 72
+    inter: int = 4304
+    eps: float = 1e-6
+    patches: int = 2394
+
+    @property
+    def linear_params_per_layer(self) -> int:
+        h = self.hidden
+        return 3 * h * self.heads * self.head_dim + self.heads * self.head_dim * h + 2 * h * self.inter
+
+    def ops_per_patch(self) -> tuple[float, float]:
+        """(int8 linear ops, attention FLOPs) per patch: 2·params and 4·S·D·H, per layer."""
+        lin = self.layers * 2.0 * self.linear_params_per_layer
+        att = self.layers * 4.0 * self.patches * self.head_dim * self.heads
+        return lin, att
+
+
+class SiglipTower:
+    """Resident random-init tower (W8A8 linears) + preallocated activations for
+    `images` images of cfg.patches patch embeddings on the current CUDA device."""
+
+    def __init__(self, cfg: SiglipConfig, images: int, seed: int = 0, host_weights: dict | None = None):
+        import torch
+        self.cfg, self.images = cfg, images
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.dev = dev
+        T = images * cfg.patches
+        self.T = T
+        g = torch.Generator(device=dev).manual_seed(seed)
+        h, inter = cfg.hidden, cfg.inter
+        hq = cfg.heads * cfg.head_dim
+
+        def randn16(*shape):
+            # fp16 weights ~ N(0, 0.02), widened for the device quantiser
+            return (torch.randn(*shape, generator=g, device=dev, dtype=torch.float32) * 0.02).half().float()
+
+        def pack(w):
+            return pack_w8a8_float(w)
+
+        def ln_pair(n):
+            return (torch.ones(n, device=dev), torch.zeros(n, device=dev))
+
+        self.layers = []
+        for li in range(cfg.layers):
+            if host_weights is not None:
+                W = {k: torch.from_numpy(v).to(dev) for k, v in host_weights["layers"][li].items()}
+            else:
+                g1, b1 = ln_pair(h)
+                g2, b2 = ln_pair(h)
+                W = {"wq": randn16(hq, h), "wk": randn16(hq, h), "wv": randn16(hq, h), "wo": randn16(h, hq),
+                     "w1": randn16(inter, h), "w2": randn16(h, inter),
+                     "ln1_g": g1, "ln1_b": b1, "ln2_g": g2, "ln2_b": b2}
+            self.layers.append({
+                "qkv": pack(torch.cat([W["wq"], W["wk"], W["wv"]], 0)),
+                "o": pack(W["wo"]), "fc1": pack(W["w1"]), "fc2": pack(W["w2"]),
+                "ln1_g": W["ln1_g"].float().contiguous(), "ln1_b": W["ln1_b"].float().contiguous(),
+                "ln2_g": W["ln2_g"].float().contiguous(), "ln2_b": W["ln2_b"].float().contiguous(),
+            })
+            del W
+        if host_weights is not None:
+            self.post_g = torch.from_numpy(host_weights["post_g"]).to(dev).float().contiguous()
+            self.post_b = torch.from_numpy(host_weights["post_b"]).to(dev).float().contiguous()
+        else:
+            self.post_g, self.post_b = ln_pair(h)
+        torch.cuda.synchronize()
+        f16 = torch.float16
+        self.patches = torch.empty(T, h, dtype=torch.float32, device=dev)  # input patch embeddings
+        self.x = torch.empty(T, h, dtype=torch.float32, device=dev)
+        self.h = torch.empty(T, h, dtype=f16, device=dev)
+        self.qkv = torch.empty(T, 3 * hq, dtype=f16, device=dev)
+        self.attn = torch.empty(T, hq, dtype=f16, device=dev)
+        self.o = torch.empty(T, h, dtype=f16, device=dev)
+        self.f = torch.empty(T, inter, dtype=f16, device=dev)
+        self.d = torch.empty(T, h, dtype=f16, device=dev)
+        self.out = torch.empty(T, h, dtype=f16, device=dev)
+        self.graph = None
+
+    # ------------------------------------------------------------------ forward
+    def forward_device(self, stream=None):
+        """One forward over self.patches (f32 [T, hidden]) into self.out (f16 [T, hidden])."""
+        import torch
+        cfg, lib, T = self.cfg, _lib.load(), self.T
+        st = _stream_ptr(stream)
+        h, hq, S = cfg.hidden, cfg.heads * cfg.head_dim, cfg.patches
+        ld = 3 * hq
+        # the residual stream starts as the input (x is rewritten in place each layer)
+        if stream is None:
+            self.x.copy_(self.patches)
+        else:
+            with torch.cuda.stream(stream):
+                self.x.copy_(self.patches)
+        qkv_p = _dev_ptr(self.qkv)
+        delta = None
+        for L in self.layers:
+            _check(lib.rb_add_layer_norm(_dev_ptr(self.x), delta, _dev_ptr(L["ln1_g"]), _dev_ptr(L["ln1_b"]), cfg.eps,
+                                         _dev_ptr(self.h), T, h, st), "add_layer_norm")
+            matmul(self.h, L["qkv"], out=self.qkv, stream=stream)
+            _check(lib.rb_attention_batched(qkv_p, ld, qkv_p + hq * 2, ld, qkv_p + 2 * hq * 2, ld,
+                                            _dev_ptr(self.attn), hq, DTYPE_F16, self.images, S, S,
+                                            cfg.heads, cfg.heads, cfg.head_dim, 1.0 / math.sqrt(cfg.head_dim),
+                                            0.0, MASK_NONE, -1, 0, 0, st),
+                   "rocket_flash_attn", S, S, cfg.head_dim)
+            matmul(self.attn, L["o"], out=self.o, stream=stream)
+            _check(lib.rb_add_layer_norm(_dev_ptr(self.x), _dev_ptr(self.o), _dev_ptr(L["ln2_g"]), _dev_ptr(L["ln2_b"]),
+                                         cfg.eps, _dev_ptr(self.h), T, h, st), "add_layer_norm")
+            matmul(self.h, L["fc1"], out=self.f, stream=stream)
+            _check(lib.rb_gelu(_dev_ptr(self.f), T * cfg.inter, st), "gelu")
+            matmul(self.f, L["fc2"], out=self.d, stream=stream)
+            delta = _dev_ptr(self.d)
+        _check(lib.rb_add_layer_norm(_dev_ptr(self.x), delta, _dev_ptr(self.post_g), _dev_ptr(self.post_b), cfg.eps,
+                                     _dev_ptr(self.out), T, h, st), "add_layer_norm")
+        return self.out
+
+    def capture(self):
+        """Capture forward_device into a CUDA graph (after one eager warm-up)."""
+        import torch
+        self.forward_device()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, capture_error_mode="thread_local"):
+            self.forward_device()
+        self.graph = g
+        return g
+
+    def run(self):
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self.forward_device()
+        return self.out
+
+    def encode_host(self, patches_host, out_host=None):
+        """End-to-end call: host patch embeddings [images*patches, hidden] f32 in,
+        host f16 patch states out."""
+        import torch
+        self.patches.copy_(patches_host, non_blocking=True)
+        self.run()
+        if out_host is None:
+            out_host = torch.empty(self.T, self.cfg.hidden, dtype=torch.float16, pin_memory=True)
+        out_host.copy_(self.out, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        return out_host

@@ -103,6 +103,14 @@ RB_API int64_t rb_pack_f32_q8_0_device(const float* const* parts_dev, const int6
 RB_API int64_t rb_pack_w8a8(const int8_t* codes_host, const float* w_scale_host, int64_t n, int64_t k,
                      float in_scale, float out_scale);
 
+/* Per-output-channel int8 weight from an f32 [n, k] DEVICE weight: codes
+ * clamp(round_ties_even(w / s), -127, 127) with s = max(max|w_row|/127, 1e-12)
+ * per row, packed like rb_pack_w8a8 (for float checkpoints such as the
+ * SigLIP-style tower's f16 weights; the reference takes pre-quantised QAT
+ * codes only). */
+RB_API int64_t rb_pack_f32_w8a8_device(const float* w_dev, int64_t n, int64_t k, float in_scale,
+                                       float out_scale);
+
 /* Weight geometry of a packed id: kind (RB_WEIGHT_*), n, k. */
 RB_API int rb_weight_info(int64_t id, int* kind, int64_t* n, int64_t* k);
 
@@ -171,6 +179,10 @@ RB_API int rb_attention_batched(const void* q, int64_t ldq, const void* k, int64
                                 float scale, float softcap, int mask_mode, int64_t window,
                                 int64_t q_start, int64_t kv_start, void* stream);
 
+/* head_dim 72 (the SigLIP-style config) is supported by every attention entry:
+ * heads are staged zero-padded to 80 columns (the UMMA K granularity) in
+ * engine scratch and the output keeps 72 columns. */
+
 /* ---- glue ops of the RocketOps surface (ext.rs:70-83, 1054-1152; formulas
  * host.rs:15-72). Device buffers, any float dtype, asynchronous on `stream`. */
 
@@ -198,6 +210,12 @@ RB_API int rb_embed_gather(const int32_t* ids, int64_t tokens, const void* table
 /* x += delta (f16, NULL = none); h = rms_norm(x, w, eps) as f16. d in {1024, 1152, 2048}. */
 RB_API int rb_add_rms_norm(float* x, const void* delta_f16, const float* w, float eps, void* h_f16,
                            int64_t rows, int64_t d, void* stream);
+/* x += delta (f16, NULL = none); h = layer_norm(x) * g + b as f16 (biased
+ * variance, eps inside the sqrt). d in {768, 1024, 1152}. */
+RB_API int rb_add_layer_norm(float* x, const void* delta_f16, const float* g, const float* b, float eps,
+                             void* h_f16, int64_t rows, int64_t d, void* stream);
+/* In place: y = gelu_tanh(y) for f16 y (host.rs:15-18); count % 8 == 0. */
+RB_API int rb_gelu(void* y_f16, int64_t count, void* stream);
 /* In place on a fused q|k|v f16 buffer [tokens, ld]: per-head RMSNorm of the
  * q heads (q_norm_w) and k heads (k_norm_w), then RoPE at position t % seq
  * (model.rs:369-376). head_dim 128. */

@@ -64,6 +64,11 @@ CASES = [
     (150, 500, 4, 2, 128, 6, -1, 300, 0),
     (150, 400, 4, 2, 64, 6, 90, 300, 100),
     (64, 300, 2, 1, 128, 1, -1, 0, 0),
+    # head_dim 72 (staged as 80 = 64-column atom + 16-column tail)
+    (1, 1, 2, 2, 72, 0, -1, 0, 0),
+    (300, 300, 16, 16, 72, 0, -1, 0, 0),
+    (257, 257, 4, 2, 72, 2, -1, 0, 0),
+    (150, 400, 4, 2, 72, 5, 60, 200, 150),
 ]
 
 
