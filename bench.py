@@ -273,19 +273,24 @@ class W8A8Workload:
     unit = "TOP/s"
     M = 16 * 2394
     SHAPES = [(3456, 1152), (1152, 1152), (4304, 1152), (1152, 4304)]  # (N, K)
+    X_DTYPE = "f32"
 
     def __init__(self, dev, seed):
         import torch
         import burn_rocket_b200 as rb
         self.rb = rb
         rng = np.random.default_rng(seed)
+        if self.X_DTYPE != "f32":
+            self.metric = "W8A8 GEMM TOP/s (" + ", ".join(f"[{self.M},{k}] f16 x s8 [{n},{k}]^T"
+                                                          for n, k in self.SHAPES) + ")"
+        xdt = torch.float32 if self.X_DTYPE == "f32" else torch.float16
         self.ws, self.xs, self.ys = [], [], []
         for n, k in self.SHAPES:
             codes = rng.integers(-127, 128, size=(n, k), dtype=np.int8)
             scale = (rng.random(n).astype(np.float32) * 1e-3 + 1e-4)
             self.ws.append(rb.pack_qat(codes, scale, n, k))
-            self.xs.append(torch.randn(self.M, k, device=dev))
-            self.ys.append(torch.empty(self.M, n, dtype=torch.float32, device=dev))
+            self.xs.append(torch.randn(self.M, k, device=dev).to(xdt))
+            self.ys.append(torch.empty(self.M, n, dtype=xdt, device=dev))
         self.flops = sum(2.0 * self.M * n * k for n, k in self.SHAPES)
         self.hx = [x.cpu().pin_memory() for x in self.xs]
         self.hy = [y.cpu().pin_memory() for y in self.ys]
@@ -300,12 +305,13 @@ class W8A8Workload:
     def e2e_step(self):
         import burn_rocket_b200._lib as L
         h2d = d2h = 0
+        dt = L.DTYPE_F32 if self.X_DTYPE == "f32" else L.DTYPE_F16
         for (n, k), w, hx, hy in zip(self.SHAPES, self.ws, self.hx, self.hy):
-            rc = L.load().rb_matmul_host(w.id, hx.data_ptr(), L.DTYPE_F32, self.M, k, hy.data_ptr(), L.DTYPE_F32)
+            rc = L.load().rb_matmul_host(w.id, hx.data_ptr(), dt, self.M, k, hy.data_ptr(), dt)
             if rc != 0:
                 raise RuntimeError(L.last_error())
-            h2d += hx.numel() * 4
-            d2h += hy.numel() * 4
+            h2d += hx.numel() * hx.element_size()
+            d2h += hy.numel() * hy.element_size()
         return (h2d, d2h)
 
     @staticmethod
@@ -685,7 +691,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying a CUDA graph")
     ap.add_argument("--gemm-shape", default=None,
-                    help="q8gemm only: M,N,K with f16 activations/outputs (profiling the model's shapes)")
+                    help="q8gemm / w8a8: one M,N,K GEMM with f16 activations/outputs (profiling the model's shapes)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -693,8 +699,12 @@ def main():
         args.steps = {"attn": 200, "q8gemm": 2000, "w8a8": 60, "qwen3": 10, "siglip": 5}.get(args.workload, 20)
     if args.gemm_shape:
         m, n, k = (int(v) for v in args.gemm_shape.split(","))
-        Q8GemmWorkload.M, Q8GemmWorkload.N, Q8GemmWorkload.K = m, n, k
-        Q8GemmWorkload.X_DTYPE = "f16"
+        if args.workload == "w8a8":
+            W8A8Workload.M, W8A8Workload.SHAPES = m, [(n, k)]
+            W8A8Workload.X_DTYPE = "f16"
+        else:
+            Q8GemmWorkload.M, Q8GemmWorkload.N, Q8GemmWorkload.K = m, n, k
+            Q8GemmWorkload.X_DTYPE = "f16"
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -165,6 +165,85 @@ __device__ __forceinline__ float epi_value(const EpiParams e, uint32_t r, float 
   return y;
 }
 
+// Epilogue modes of the TMA-store path, fixed per launch: raw 4-byte
+// accumulators (f32 for Q8_0, s32 for RB_DTYPE_I32), f16 / bf16 casts, and the
+// W8A8 scaled forms (kEpiS8*; Q = onto the calibrated output grid).
+enum : int {
+  kEpiRaw4 = 0, kEpiF16, kEpiBF16,
+  kEpiS8F32, kEpiS8F16, kEpiS8BF16, kEpiS8F32Q, kEpiS8F16Q, kEpiS8BF16Q
+};
+
+__host__ __device__ __forceinline__ int epi_mode(bool i8, int out_dtype, float out_scale) {
+  const int cast = out_dtype == RB_DTYPE_F16 ? 1 : out_dtype == RB_DTYPE_BF16 ? 2 : 0;
+  if (!i8 || out_dtype == RB_DTYPE_I32) return out_dtype == RB_DTYPE_I32 ? kEpiRaw4 : cast;
+  return kEpiS8F32 + cast + (out_scale != 0.0f ? 3 : 0);
+}
+
+// One 32-row x 128-byte chunk of the output tile, written into the
+// 128-byte-swizzled staging row `b` of this lane: columns [0, CW) of the chunk
+// from accumulator registers ra (0..31) and rb (32..63, 2-byte outputs only).
+// SCALE applies the W8A8 epilogue f32(acc) * (rs * s_col[n]) — in that order,
+// for bit parity with ext.rs:1350-1363 — with the chunk's column scales read
+// as float4 vectors up front (scp = s_col + first column; nvalid columns are
+// in range, the rest clamp to the last valid one and are clipped by the TMA
+// store). OUT is the output element size in bytes' role: 4 (f32 / raw), 1 (f16),
+// 2 (bf16). QGRID rounds onto the static output grid (ext.rs:1236-1238).
+template <bool SCALE, int OUT, bool QGRID>
+__device__ __forceinline__ void epi_chunk(uint8_t* b, int lane, const uint32_t (&ra)[32],
+                                          const uint32_t (&rb)[32], float rs, const float* scp,
+                                          int nvalid, const EpiParams& ep) {
+  constexpr int CW = OUT == 4 ? 32 : 64;
+  float sc[SCALE ? CW : 1];
+  if constexpr (SCALE) {
+    if (nvalid >= CW) {
+#pragma unroll
+      for (int i = 0; i < CW / 4; ++i) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(scp) + i);
+        sc[4 * i] = v.x; sc[4 * i + 1] = v.y; sc[4 * i + 2] = v.z; sc[4 * i + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < CW; ++i) sc[i] = __ldg(scp + min(i, nvalid - 1));
+    }
+  }
+  auto value = [&](int i) -> float {
+    const uint32_t r = i < 32 ? ra[i] : rb[i - 32];
+    if constexpr (!SCALE) {
+      return __uint_as_float(r);
+    } else {
+      float y = __fmul_rn(__int2float_rn(static_cast<int32_t>(r)), __fmul_rn(rs, sc[i]));
+      if constexpr (QGRID) {
+        const int code = max(-128, min(127, __float2int_rn(__fmul_rn(y, ep.out_inv))));
+        y = __fmul_rn(__int2float_rn(code), ep.out_scale);
+      }
+      return y;
+    }
+  };
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    uint4 o;
+    if constexpr (OUT == 4) {
+      o = make_uint4(__float_as_uint(value(4 * j)), __float_as_uint(value(4 * j + 1)),
+                     __float_as_uint(value(4 * j + 2)), __float_as_uint(value(4 * j + 3)));
+    } else {
+      uint32_t pk[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float v0 = value(8 * j + 2 * e), v1 = value(8 * j + 2 * e + 1);
+        if constexpr (OUT == 1) {
+          __half2 h = __floats2half2_rn(v0, v1);
+          pk[e] = *reinterpret_cast<uint32_t*>(&h);
+        } else {
+          __nv_bfloat162 h = __floats2bfloat162_rn(v0, v1);
+          pk[e] = *reinterpret_cast<uint32_t*>(&h);
+        }
+      }
+      o = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    }
+    *reinterpret_cast<uint4*>(b + ((j ^ (lane & 7)) << 4)) = o;
+  }
+}
+
 template <class Cfg>
 __global__ void __launch_bounds__(Cfg::THREADS, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -301,6 +380,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     uint8_t* ebuf = smem + Cfg::EPI_OFF + (warp - kEpiWarp0) * 2 * kEpiBufBytes;
     const int out_bytes = (args.out_dtype == RB_DTYPE_F16 || args.out_dtype == RB_DTYPE_BF16) ? 2 : 4;
     const int CW = 128 / out_bytes;  // columns per 128-byte store row
+    const int mode = epi_mode(Cfg::I8, args.out_dtype, args.out_scale);
     int buf = 0;
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
@@ -329,38 +409,24 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             if (lane == 0) bulk_wait_read<1>();
             __syncwarp();
             uint8_t* b = ebuf + buf * kEpiBufBytes + lane * 128;
-            if (out_bytes == 4) {
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                float v[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e)
-                  v[e] = epi_value<Cfg::I8>(ep, ra[4 * j + e], rs, min(n0 + c0 + 4 * j + e, N - 1));
-                *reinterpret_cast<float4*>(b + ((j ^ (lane & 7)) << 4)) =
-                    make_float4(v[0], v[1], v[2], v[3]);
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                uint32_t pk[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const int c = 8 * j + 2 * e;
-                  const uint32_t r0 = c < 32 ? ra[c] : rb[c - 32];
-                  const uint32_t r1 = c + 1 < 32 ? ra[c + 1] : rb[c + 1 - 32];
-                  const float v0 = epi_value<Cfg::I8>(ep, r0, rs, min(n0 + c0 + c, N - 1));
-                  const float v1 = epi_value<Cfg::I8>(ep, r1, rs, min(n0 + c0 + c + 1, N - 1));
-                  if (args.out_dtype == RB_DTYPE_F16) {
-                    __half2 h = __floats2half2_rn(v0, v1);
-                    pk[e] = *reinterpret_cast<uint32_t*>(&h);
-                  } else {
-                    __nv_bfloat162 h = __floats2bfloat162_rn(v0, v1);
-                    pk[e] = *reinterpret_cast<uint32_t*>(&h);
+            const float* scp = Cfg::I8 ? ep.s_col + n0 + c0 : nullptr;
+            const int nvalid = N - (n0 + c0);
+            switch (mode) {
+              case kEpiRaw4: epi_chunk<false, 4, false>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
+              case kEpiF16: epi_chunk<false, 1, false>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
+              case kEpiBF16: epi_chunk<false, 2, false>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
+              default:
+                if constexpr (Cfg::I8) {
+                  switch (mode) {
+                    case kEpiS8F32: epi_chunk<true, 4, false>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
+                    case kEpiS8F16: epi_chunk<true, 1, false>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
+                    case kEpiS8BF16: epi_chunk<true, 2, false>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
+                    case kEpiS8F32Q: epi_chunk<true, 4, true>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
+                    case kEpiS8F16Q: epi_chunk<true, 1, true>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
+                    default: epi_chunk<true, 2, true>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
                   }
                 }
-                *reinterpret_cast<uint4*>(b + ((j ^ (lane & 7)) << 4)) =
-                    make_uint4(pk[0], pk[1], pk[2], pk[3]);
-              }
+                break;
             }
             fence_proxy_async_smem();
             __syncwarp();
