@@ -52,9 +52,21 @@ def load_peaks():
     return PEAKS_FALLBACK, "fallback"
 
 
-def profile_traffic(name):
+# Committed ncu summary of each workload's dominant kernel (profiles/).
+PROFILES = {
+    "attn": "attn_kernel_gqa_s3633_ncu.md",
+    "q8gemm": "gemm_kernel_q8_0_ncu.md",
+    "w8a8": "gemm_kernel_w8a8_ncu.md",
+    "qwen3": "gemm_kernel_q8_0_ncu.md",
+    "siglip": "gemm_kernel_w8a8_ncu.md",
+}
+
+
+def profile_traffic(workload):
     """DRAM bytes per launch of the dominant kernel, from the committed ncu summary."""
-    p = ROOT / "profiles" / f"{name}.md"
+    if workload not in PROFILES:
+        return None
+    p = ROOT / "profiles" / PROFILES[workload]
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
@@ -612,7 +624,7 @@ def run_b200(args):
         if wl.name == "w8a8":
             peak = 2.0 * peak  # dense int8 is twice the dense bf16 rate
             peak_src += " x2 for int8"
-    traffic = profile_traffic(f"{wl.name}_ncu")
+    traffic = profile_traffic(wl.name)
     line = {
         "metric": wl.metric, "value": round(value, 3), "unit": wl.unit, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),

@@ -300,5 +300,16 @@ def mem_stats():
     return {"weights_bytes": wb.value, "scratch_bytes": sb.value, "num_weights": nw.value}
 
 
+def set_tile_policy(policy: str) -> str:
+    """GEMM tile policy for later matmuls: "auto", "single" (single-CTA tiles
+    only) or "pair" (prefer 256-row CTA-pair tiles). Returns the previous one."""
+    names = ["auto", "single", "pair"]
+    if policy not in names:
+        raise ValueError(f"tile policy must be one of {names}")
+    old = _lib.load().rb_set_tile_policy(names.index(policy))
+    _check(old, "rb_set_tile_policy")
+    return names[old]
+
+
 def launch_count(reset: bool = False) -> int:
     return int(_lib.load().rb_launch_count(1 if reset else 0))

@@ -51,6 +51,8 @@ _p = C.c_void_p
 _f = C.c_float
 
 # name -> (restype, argtypes)
+TILES_AUTO, TILES_SINGLE, TILES_PAIR = 0, 1, 2
+
 SIGNATURES = {
     "rb_init": (_i, [_i]),
     "rb_last_error": (_i, [C.c_char_p, C.c_size_t]),
@@ -84,6 +86,7 @@ SIGNATURES = {
     "rb_matmul_i8_acc": (_i, [_i64, _p, _i64, _p, _p]),
     "rb_mem_stats": (_i, [C.POINTER(_i64), C.POINTER(_i64), C.POINTER(_i64)]),
     "rb_launch_count": (_i64, [_i]),
+    "rb_set_tile_policy": (_i, [_i]),
 }
 
 _lib = None

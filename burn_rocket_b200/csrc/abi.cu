@@ -105,7 +105,8 @@ struct Weight {
   void* scales = nullptr;    // Q8_0: f16 [k/32, pitch]; W8A8: f32 [n]
   int64_t pitch = 0;         // Q8_0 scale row pitch: round_up(n, 8)
   float in_scale = 0.0f, out_scale = 0.0f;
-  // TMA maps per N tile ({256, 128, 96, 64}, see bn_index): the codes
+  // TMA maps per staged weight-tile height ({256, 128, 96, 64}, see
+  // bn_index; a CTA-pair tile stages half its N per CTA): the codes
   // (Q8_0: box 64 x bn; W8A8: box 128 x bn, 128-B swizzle) and the Q8_0
   // scales (box bn x 2).
   CUtensorMap tm_codes[4]{};
@@ -123,7 +124,7 @@ static int weight_maps(Weight& w) {
       if ((rc = make_tmap_2d(&w.tm_codes[i], w.codes, 1, w.n, w.k, w.k, 64, bn, 0)) != RB_OK) return rc;
       if ((rc = make_tmap_2d(&w.tm_scales[i], w.scales, 2, w.k / 32, w.n, w.pitch, bn, 2, 0)) != RB_OK)
         return rc;
-    } else if (i < 2) {
+    } else {
       if ((rc = make_tmap_2d(&w.tm_codes[i], w.codes, 1, w.n, w.k, w.k, 128, bn, 128)) != RB_OK) return rc;
     }
   }
@@ -210,8 +211,7 @@ int w8a8_view(int64_t id, W8A8View* v) {
   v->k = w.k;
   v->in_scale = w.in_scale;
   v->out_scale = w.out_scale;
-  v->tm_codes[0] = w.tm_codes[0];
-  v->tm_codes[1] = w.tm_codes[1];
+  for (int i = 0; i < 4; ++i) v->tm_codes[i] = w.tm_codes[i];
   v->err = e->err;
   v->num_sms = e->num_sms;
   v->device = e->device;
@@ -261,13 +261,12 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
       g_launches++;
       a = e->act.ptr;
     }
-    int bn = 0, mh = 1;
-    gemm_pick(false, L.M, L.N, e->num_sms, &bn, &mh);
+    const GemmPlan plan = gemm_plan(false, L.M, L.N, L.K, e->num_sms);
     CUtensorMap tmA, tmC;
-    if ((rc = make_tmap_2d(&tmA, a, 2, m, k, k, 64, 128 * mh, 128)) != RB_OK) return rc;
+    if ((rc = make_tmap_2d(&tmA, a, 2, m, k, k, 64, plan.a_rows(), 128)) != RB_OK) return rc;
     const bool tstore = output_map(&tmC, y, y_dtype, m, w.n);
-    const int bi = bn_index(bn);
-    if ((rc = launch_q8_gemm(L, bn, mh, tmA, w.tm_codes[bi], w.tm_scales[bi], tstore ? &tmC : nullptr,
+    const int bi = bn_index(plan.weight_rows());
+    if ((rc = launch_q8_gemm(L, plan, tmA, w.tm_codes[bi], w.tm_scales[bi], tstore ? &tmC : nullptr,
                              st)) != RB_OK)
       return fail(rc, "q8_0 gemm launch failed");
     g_launches++;
@@ -288,9 +287,9 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
     L.s_col = reinterpret_cast<const float*>(w.scales);
     L.out_scale = w.out_scale;
     const bool tstore = output_map(&tmC, y, y_dtype, m, w.n);
-    int bn = 0, mh = 1;
-    gemm_pick(true, L.M, L.N, e->num_sms, &bn, &mh);
-    if ((rc = launch_w8a8_gemm(L, bn, tmA, w.tm_codes[bn_index(bn)], tstore ? &tmC : nullptr, st)) != RB_OK)
+    const GemmPlan plan = gemm_plan(true, L.M, L.N, L.K, e->num_sms);
+    if ((rc = launch_w8a8_gemm(L, plan, tmA, w.tm_codes[bn_index(plan.weight_rows())], tstore ? &tmC : nullptr,
+                               st)) != RB_OK)
       return fail(rc, "w8a8 gemm launch failed");
     g_launches++;
     return RB_OK;
@@ -930,9 +929,8 @@ int rb_matmul_i8_acc(int64_t id, const int8_t* codes, int64_t m, int32_t* acc, v
   L.num_sms = e->num_sms;
   L.s_col = reinterpret_cast<const float*>(w.scales);
   const bool tstore = output_map(&tmC, acc, RB_DTYPE_I32, m, w.n);
-  int bn = 0, mh = 1;
-  gemm_pick(true, L.M, L.N, e->num_sms, &bn, &mh);
-  rc = launch_w8a8_gemm(L, bn, tmA, w.tm_codes[bn_index(bn)], tstore ? &tmC : nullptr,
+  const GemmPlan plan = gemm_plan(true, L.M, L.N, L.K, e->num_sms);
+  rc = launch_w8a8_gemm(L, plan, tmA, w.tm_codes[bn_index(plan.weight_rows())], tstore ? &tmC : nullptr,
                         reinterpret_cast<cudaStream_t>(stream));
   g_launches++;
   return rc == RB_OK ? RB_OK : fail(rc, "int8 gemm launch failed");
@@ -951,6 +949,11 @@ int rb_mem_stats(int64_t* weights_bytes, int64_t* scratch_bytes, int64_t* num_we
                                           e->io_out.bytes + e->io_k.bytes + e->io_v.bytes);
   if (num_weights) *num_weights = static_cast<int64_t>(e->weights.size());
   return RB_OK;
+}
+
+int rb_set_tile_policy(int policy) {
+  if (policy < RB_TILES_AUTO || policy > RB_TILES_PAIR) return fail(RB_E_SHAPE, "unknown tile policy %d", policy);
+  return set_gemm_policy(policy);
 }
 
 int64_t rb_launch_count(int reset) {

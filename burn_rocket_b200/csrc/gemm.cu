@@ -31,20 +31,11 @@
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 
-#include "sm100.cuh"
-#include "kernels.h"
+#include <atomic>
+
+#include "gemm_common.cuh"
 
 namespace rb {
-
-constexpr int kEpiWarp0 = 2;      // first epilogue warp
-constexpr int kNumEpiWarps = 4;
-constexpr int kDqWarp0 = 6;       // first dequant warp (Q8_0 only)
-constexpr int kNumDqWarps = 8;
-constexpr int kEpiBufBytes = 4096;  // 32 rows x 128 B, one per warp and buffer
-
-enum class BSrc { Tma, Q8Dequant };
-
-constexpr int round1k(int x) { return (x + 1023) & ~1023; }
 
 template <int BN_, int LSTAGES_, bool I8_, int BSTAGES_ = 2, int MH_ = 1>
 struct GemmCfg {
@@ -83,166 +74,6 @@ struct GemmCfg {
   static_assert(B_BYTES % 1024 == 0, "B tiles must keep 1024-byte alignment");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
-
-struct GemmArgs {
-  int M, N, K;
-  const float* s_row;  // W8A8 [M]
-  const float* s_col;  // W8A8 [N]
-  void* out;           // [M, ldo]
-  int ldo;
-  int out_dtype;       // RB_DTYPE_* (RB_DTYPE_I32: raw int8-GEMM accumulators)
-  float out_scale;     // W8A8: calibrated output grid (0 = unrounded)
-  float out_inv;       // 1 / out_scale in f32
-  int tma_store;       // epilogue through smem + TMA store (else direct stores)
-  uint32_t* err;
-};
-
-// --------------------------------------------------------------------------
-// Q8_0 dequantisation of 8 consecutive codes of one weight row:
-// f16 value = RNE(d * q). 0x6400|u is the f16 number 1024+u, so q = h - 1152
-// exactly; one correctly rounded f16 multiply by d then gives RNE(d * q)
-// (d * q is exact in f32, so this equals rounding the exact product once).
-__device__ __forceinline__ uint4 q8_dequant8_f16(uint2 codes, __half d) {
-  const uint32_t lo = codes.x ^ 0x80808080u;
-  const uint32_t hi = codes.y ^ 0x80808080u;
-  const uint32_t magic = 0x64646464u;
-  uint32_t h[4];
-  asm("prmt.b32 %0, %1, %2, 0x5140;" : "=r"(h[0]) : "r"(lo), "r"(magic));
-  asm("prmt.b32 %0, %1, %2, 0x7362;" : "=r"(h[1]) : "r"(lo), "r"(magic));
-  asm("prmt.b32 %0, %1, %2, 0x5140;" : "=r"(h[2]) : "r"(hi), "r"(magic));
-  asm("prmt.b32 %0, %1, %2, 0x7362;" : "=r"(h[3]) : "r"(hi), "r"(magic));
-  const __half2 bias = __half2half2(__ushort_as_half(0x6480));  // 1152.0
-  const __half2 d2 = __half2half2(d);
-  uint4 out;
-  uint32_t* o = reinterpret_cast<uint32_t*>(&out);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    __half2 v = *reinterpret_cast<__half2*>(&h[i]);
-    v = __hmul2_rn(__hsub2(v, bias), d2);
-    o[i] = *reinterpret_cast<uint32_t*>(&v);
-  }
-  return out;
-}
-
-// Direct-store fallback: element j of v goes to idx + j when j < count
-// (compile-time unrolled so v stays in registers).
-__device__ __forceinline__ void store_out16(void* out, int dtype, int64_t idx, const float (&v)[16],
-                                            int count) {
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    if (j < count) {
-      if (dtype == RB_DTYPE_F32 || dtype == RB_DTYPE_I32)  // I32: raw bits in v
-        reinterpret_cast<float*>(out)[idx + j] = v[j];
-      else if (dtype == RB_DTYPE_F16)
-        reinterpret_cast<__half*>(out)[idx + j] = __float2half_rn(v[j]);
-      else
-        reinterpret_cast<__nv_bfloat16*>(out)[idx + j] = __float2bfloat16_rn(v[j]);
-    }
-  }
-}
-
-// Epilogue parameters held in registers (never through a reference to the
-// kernel-parameter struct, which would force a local-memory copy).
-struct EpiParams {
-  const float* s_col;
-  int out_dtype;
-  float out_scale, out_inv;
-};
-
-// Epilogue value for accumulator bits r at column n (row scale rs).
-template <bool I8>
-__device__ __forceinline__ float epi_value(const EpiParams e, uint32_t r, float rs, int n) {
-  if (!I8) return __uint_as_float(r);
-  if (e.out_dtype == RB_DTYPE_I32) return __uint_as_float(r);
-  // Order matters for bit parity: f32(acc) * (s_row * s_col).
-  float y = __fmul_rn(__int2float_rn(static_cast<int32_t>(r)), __fmul_rn(rs, __ldg(e.s_col + n)));
-  if (e.out_scale != 0.0f) {
-    // static_code(y, 1/out_scale) * out_scale (ext.rs:1236-1238, 1356-1360),
-    // through an integer code like the reference (`as i8`), so zero is +0.0.
-    const int code = max(-128, min(127, __float2int_rn(__fmul_rn(y, e.out_inv))));
-    y = __fmul_rn(__int2float_rn(code), e.out_scale);
-  }
-  return y;
-}
-
-// Epilogue modes of the TMA-store path, fixed per launch: raw 4-byte
-// accumulators (f32 for Q8_0, s32 for RB_DTYPE_I32), f16 / bf16 casts, and the
-// W8A8 scaled forms (kEpiS8*; Q = onto the calibrated output grid).
-enum : int {
-  kEpiRaw4 = 0, kEpiF16, kEpiBF16,
-  kEpiS8F32, kEpiS8F16, kEpiS8BF16, kEpiS8F32Q, kEpiS8F16Q, kEpiS8BF16Q
-};
-
-__host__ __device__ __forceinline__ int epi_mode(bool i8, int out_dtype, float out_scale) {
-  const int cast = out_dtype == RB_DTYPE_F16 ? 1 : out_dtype == RB_DTYPE_BF16 ? 2 : 0;
-  if (!i8 || out_dtype == RB_DTYPE_I32) return out_dtype == RB_DTYPE_I32 ? kEpiRaw4 : cast;
-  return kEpiS8F32 + cast + (out_scale != 0.0f ? 3 : 0);
-}
-
-// One 32-row x 128-byte chunk of the output tile, written into the
-// 128-byte-swizzled staging row `b` of this lane: columns [0, CW) of the chunk
-// from accumulator registers ra (0..31) and rb (32..63, 2-byte outputs only).
-// SCALE applies the W8A8 epilogue f32(acc) * (rs * s_col[n]) — in that order,
-// for bit parity with ext.rs:1350-1363 — with the chunk's column scales read
-// as float4 vectors up front (scp = s_col + first column; nvalid columns are
-// in range, the rest clamp to the last valid one and are clipped by the TMA
-// store). OUT is the output element size in bytes' role: 4 (f32 / raw), 1 (f16),
-// 2 (bf16). QGRID rounds onto the static output grid (ext.rs:1236-1238).
-template <bool SCALE, int OUT, bool QGRID>
-__device__ __forceinline__ void epi_chunk(uint8_t* b, int lane, const uint32_t (&ra)[32],
-                                          const uint32_t (&rb)[32], float rs, const float* scp,
-                                          int nvalid, const EpiParams& ep) {
-  constexpr int CW = OUT == 4 ? 32 : 64;
-  float sc[SCALE ? CW : 1];
-  if constexpr (SCALE) {
-    if (nvalid >= CW) {
-#pragma unroll
-      for (int i = 0; i < CW / 4; ++i) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(scp) + i);
-        sc[4 * i] = v.x; sc[4 * i + 1] = v.y; sc[4 * i + 2] = v.z; sc[4 * i + 3] = v.w;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < CW; ++i) sc[i] = __ldg(scp + min(i, nvalid - 1));
-    }
-  }
-  auto value = [&](int i) -> float {
-    const uint32_t r = i < 32 ? ra[i] : rb[i - 32];
-    if constexpr (!SCALE) {
-      return __uint_as_float(r);
-    } else {
-      float y = __fmul_rn(__int2float_rn(static_cast<int32_t>(r)), __fmul_rn(rs, sc[i]));
-      if constexpr (QGRID) {
-        const int code = max(-128, min(127, __float2int_rn(__fmul_rn(y, ep.out_inv))));
-        y = __fmul_rn(__int2float_rn(code), ep.out_scale);
-      }
-      return y;
-    }
-  };
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    uint4 o;
-    if constexpr (OUT == 4) {
-      o = make_uint4(__float_as_uint(value(4 * j)), __float_as_uint(value(4 * j + 1)),
-                     __float_as_uint(value(4 * j + 2)), __float_as_uint(value(4 * j + 3)));
-    } else {
-      uint32_t pk[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float v0 = value(8 * j + 2 * e), v1 = value(8 * j + 2 * e + 1);
-        if constexpr (OUT == 1) {
-          __half2 h = __floats2half2_rn(v0, v1);
-          pk[e] = *reinterpret_cast<uint32_t*>(&h);
-        } else {
-          __nv_bfloat162 h = __floats2bfloat162_rn(v0, v1);
-          pk[e] = *reinterpret_cast<uint32_t*>(&h);
-        }
-      }
-      o = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-    }
-    *reinterpret_cast<uint4*>(b + ((j ^ (lane & 7)) << 4)) = o;
-  }
-}
 
 template <class Cfg>
 __global__ void __launch_bounds__(Cfg::THREADS, 1)
@@ -375,11 +206,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + kNumEpiWarps) {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    const int row = quarter * 32 + lane;
     const EpiParams ep{args.s_col, args.out_dtype, args.out_scale, args.out_inv};
     uint8_t* ebuf = smem + Cfg::EPI_OFF + (warp - kEpiWarp0) * 2 * kEpiBufBytes;
-    const int out_bytes = (args.out_dtype == RB_DTYPE_F16 || args.out_dtype == RB_DTYPE_BF16) ? 2 : 4;
-    const int CW = 128 / out_bytes;  // columns per 128-byte store row
     const int mode = epi_mode(Cfg::I8, args.out_dtype, args.out_scale);
     int buf = 0;
     int local = 0;
@@ -392,66 +220,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       for (int h = 0; h < Cfg::MH; ++h) {
       const int m0 = (t / tiles_n) * Cfg::BM + h * 128;
       const uint32_t acc_col = acc * Cfg::ACC_COLS + h * BN;
-      const int m = m0 + row;
-      float rs = 1.0f;
-      // Raw int32 output (RB_DTYPE_I32) carries no scales.
-      if (Cfg::I8 && m < M && args.out_dtype != RB_DTYPE_I32) rs = args.s_row[m];
-      const bool rows_live = m0 + quarter * 32 < M;  // warp-uniform
-      if (args.tma_store) {
-        if (rows_live) {
-          for (int c0 = 0; c0 < BN && n0 + c0 < N; c0 += CW) {
-            uint32_t ra[32], rb[32];  // columns c0..c0+31 and (2-byte outputs) c0+32..c0+63
-            tmem_ld32(tmem_addr(tmem_base, quarter * 32, acc_col + c0), ra);
-            if (CW == 64) tmem_ld32(tmem_addr(tmem_base, quarter * 32, acc_col + c0 + 32), rb);
-            tmem_wait_ld();
-            // The buffer about to be written must have been read by its
-            // previous TMA store (at most one store of this warp in flight).
-            if (lane == 0) bulk_wait_read<1>();
-            __syncwarp();
-            uint8_t* b = ebuf + buf * kEpiBufBytes + lane * 128;
-            const float* scp = Cfg::I8 ? ep.s_col + n0 + c0 : nullptr;
-            const int nvalid = N - (n0 + c0);
-            switch (mode) {
-              case kEpiRaw4: epi_chunk<false, 4, false>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
-              case kEpiF16: epi_chunk<false, 1, false>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
-              case kEpiBF16: epi_chunk<false, 2, false>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
-              default:
-                if constexpr (Cfg::I8) {
-                  switch (mode) {
-                    case kEpiS8F32: epi_chunk<true, 4, false>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
-                    case kEpiS8F16: epi_chunk<true, 1, false>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
-                    case kEpiS8BF16: epi_chunk<true, 2, false>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
-                    case kEpiS8F32Q: epi_chunk<true, 4, true>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
-                    case kEpiS8F16Q: epi_chunk<true, 1, true>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
-                    default: epi_chunk<true, 2, true>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
-                  }
-                }
-                break;
-            }
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-              tma_store_2d(&tmC, ebuf + buf * kEpiBufBytes, n0 + c0, m0 + quarter * 32);
-              bulk_commit();
-            }
-            buf ^= 1;
-          }
-        }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
-          uint32_t r[16];
-          tmem_ld16(tmem_addr(tmem_base, quarter * 32, acc_col + c), r);
-          tmem_wait_ld();
-          if (m < M && n0 + c < N) {
-            float v[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = epi_value<Cfg::I8>(ep, r[j], rs, min(n0 + c + j, N - 1));
-            const int64_t base = static_cast<int64_t>(m) * args.ldo + n0 + c;
-            store_out16(args.out, ep.out_dtype, base, v, N - (n0 + c));
-          }
-        }
-      }
+      epi_block<BN, Cfg::I8>(tmem_base, acc_col, quarter, lane, m0, n0, M, N, args.s_row, args.out,
+                             args.ldo, mode, ep, args.tma_store != 0, &tmC, ebuf, buf);
       }  // M halves
       tc_fence_before();
       __syncwarp();
@@ -546,28 +316,46 @@ static int launch_cfg(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUte
   return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
 }
 
-// Tile shape (BN, M halves) minimising the makespan of the persistent grid:
-// rounds of tiles per SM times the per-tile cost. A tile's cost is its MMA
-// work (MH * BN columns of 128 rows) scaled by how well the shape feeds the
-// tensor core — a Q8_0 tile with one M half spends twice the dequant work per
-// FLOP — plus a fixed pipeline fill / epilogue overhead.
-void gemm_pick(bool i8, int M, int N, int num_sms, int* bn_out, int* mh_out) {
-  struct Shape { int bn, mh; double eff; };
-  static const Shape q8c[] = {{256, 1, 1.4}, {128, 1, 1.4}, {96, 1, 1.4}, {64, 1, 1.4}, {128, 2, 1.0}};
-  static const Shape i8c[] = {{256, 1, 1.0}, {128, 1, 1.0}};
+// Tile plan minimising the makespan of the persistent grid: rounds of tiles
+// per SM (per SM pair for the pair kernel) times the per-tile cost. A tile's
+// cost is its MMA columns per SM (128-row halves x BN) scaled by a measured
+// per-SM efficiency factor of the shape, plus a fixed pipeline fill /
+// epilogue overhead. Measured on B200 (rb_matmul, f16 in / out):
+//   * W8A8, K <= 2048: single-CTA 128 x 256 tiles run ~7% faster than pair
+//     tiles (the epilogue, not the operand traffic, bounds them);
+//   * W8A8, K > 2048: pair tiles run ~20% faster (L2 -> SM operand traffic
+//     bounds the single-CTA tile);
+//   * Q8_0, large M: 256 x 128 single-CTA tiles (two M halves sharing one
+//     dequantised B tile) beat pair tiles by ~35%; at small M the pair tile,
+//     which dequantises only half its weight rows per SM, fills the GPU with
+//     fewer, cheaper tiles.
+GemmPlan gemm_plan(bool i8, int M, int N, int K, int num_sms) {
+  const int policy = g_policy.load();
+  struct Shape { int bn, mh; bool pair; double eff; };
+  const bool long_k = K > 2048;
+  const Shape q8c[] = {{256, 1, false, 2.0}, {128, 1, false, 2.0}, {96, 1, false, 2.0},
+                       {64, 1, false, 2.0},  {128, 2, false, 1.5}, {256, 1, true, 1.6},
+                       {128, 1, true, 1.2}};
+  const Shape i8c[] = {{256, 1, false, long_k ? 1.25 : 1.0}, {128, 1, false, long_k ? 1.35 : 1.1},
+                       {256, 1, true, long_k ? 1.0 : 1.07}, {128, 1, true, long_k ? 1.15 : 1.2}};
   const Shape* c = i8 ? i8c : q8c;
-  const int nc = i8 ? 2 : 5;
+  const int nc = i8 ? 4 : 7;
+  GemmPlan best{c[0].bn, c[0].mh, false};
   double best_cost = -1.0;
   for (int i = 0; i < nc; ++i) {
-    const long tiles = ((M + 128L * c[i].mh - 1) / (128L * c[i].mh)) * ((N + c[i].bn - 1) / c[i].bn);
-    const long rounds = (tiles + num_sms - 1) / num_sms;
+    if (policy == RB_TILES_SINGLE && c[i].pair) continue;
+    if (policy == RB_TILES_PAIR && !c[i].pair) continue;
+    const long rows = c[i].pair ? 256L : 128L * c[i].mh;
+    const long tiles = ((M + rows - 1) / rows) * ((N + c[i].bn - 1) / c[i].bn);
+    const long units = c[i].pair ? num_sms / 2 : num_sms;
+    const long rounds = (tiles + units - 1) / units;
     const double cost = rounds * (c[i].mh * c[i].bn * c[i].eff + 32.0);
     if (best_cost < 0 || cost < best_cost) {
       best_cost = cost;
-      *bn_out = c[i].bn;
-      *mh_out = c[i].mh;
+      best = GemmPlan{c[i].bn, c[i].mh, c[i].pair};
     }
   }
+  return best;
 }
 
 static GemmArgs make_args(const GemmLaunch& L) {
@@ -581,15 +369,22 @@ static GemmArgs make_args(const GemmLaunch& L) {
   return a;
 }
 
-int launch_q8_gemm(const GemmLaunch& L, int bn, int mh, const CUtensorMap& tmA,
+int launch_q8_gemm_pair(const GemmArgs& a, int bn, int num_sms, const CUtensorMap& tmA,
+                        const CUtensorMap& tmCodes, const CUtensorMap& tmScales,
+                        const CUtensorMap* tmC, cudaStream_t stream);
+int launch_w8a8_gemm_pair(const GemmArgs& a, int bn, int num_sms, const CUtensorMap& tmA,
+                          const CUtensorMap& tmB, const CUtensorMap* tmC, cudaStream_t stream);
+
+int launch_q8_gemm(const GemmLaunch& L, const GemmPlan& plan, const CUtensorMap& tmA,
                    const CUtensorMap& tmCodes, const CUtensorMap& tmScales, const CUtensorMap* tmC,
                    cudaStream_t stream) {
   const GemmArgs a = make_args(L);
-  if (mh == 2) {
-    if (bn != 128) return RB_E_SHAPE;
+  if (plan.pair) return launch_q8_gemm_pair(a, plan.bn, L.num_sms, tmA, tmCodes, tmScales, tmC, stream);
+  if (plan.mh == 2) {
+    if (plan.bn != 128) return RB_E_SHAPE;
     return launch_cfg<CfgQ8_128x2>(tmA, tmCodes, tmScales, tmC, a, L.num_sms, stream);
   }
-  switch (bn) {
+  switch (plan.bn) {
     case 256: return launch_cfg<CfgQ8_256>(tmA, tmCodes, tmScales, tmC, a, L.num_sms, stream);
     case 128: return launch_cfg<CfgQ8_128>(tmA, tmCodes, tmScales, tmC, a, L.num_sms, stream);
     case 96: return launch_cfg<CfgQ8_96>(tmA, tmCodes, tmScales, tmC, a, L.num_sms, stream);
@@ -598,10 +393,11 @@ int launch_q8_gemm(const GemmLaunch& L, int bn, int mh, const CUtensorMap& tmA,
   }
 }
 
-int launch_w8a8_gemm(const GemmLaunch& L, int bn, const CUtensorMap& tmA, const CUtensorMap& tmB,
-                     const CUtensorMap* tmC, cudaStream_t stream) {
+int launch_w8a8_gemm(const GemmLaunch& L, const GemmPlan& plan, const CUtensorMap& tmA,
+                     const CUtensorMap& tmB, const CUtensorMap* tmC, cudaStream_t stream) {
   const GemmArgs a = make_args(L);
-  switch (bn) {
+  if (plan.pair) return launch_w8a8_gemm_pair(a, plan.bn, L.num_sms, tmA, tmB, tmC, stream);
+  switch (plan.bn) {
     case 256: return launch_cfg<CfgI8_256>(tmA, tmB, tmA, tmC, a, L.num_sms, stream);
     case 128: return launch_cfg<CfgI8_128>(tmA, tmB, tmA, tmC, a, L.num_sms, stream);
     default: return RB_E_SHAPE;

@@ -1,0 +1,345 @@
+// gemm_pair.cu — CTA-pair (cta_group::2) tcgen05 GEMMs for large M.
+//
+// Same two matmul kinds and epilogues as gemm.cu (Q8_0 block-dequant on
+// kind::f16, W8A8 on kind::i8), but one output tile of 256 rows x BN columns
+// is computed by a pair of CTAs on neighbouring SMs (a (2,1,1) cluster):
+//
+//   * each CTA stages its own 128 rows of A and its own BN/2 rows of B
+//     (int8 codes, or for Q8_0 the codes it dequantises itself);
+//   * the leader (cluster rank 0) issues M=256 UMMAs that read A and B from
+//     both CTAs' shared memory and write rows 0..127 of the accumulator into
+//     the leader's TMEM and rows 128..255 into the peer's;
+//   * each CTA's epilogue stores its own 128 rows.
+//
+// Per SM this halves the B bytes loaded from L2 and read from shared memory
+// per FLOP compared with a 128 x BN tile on one SM, which is what bounds the
+// single-CTA kernel at large M (L2 -> SM traffic and shared-memory bandwidth),
+// and for Q8_0 it halves the dequantisation work per FLOP.
+//
+// Synchronisation (all waits bounded, see sm100.cuh):
+//   ld_full[s]   leader only: A (and W8A8 B) bytes of both CTAs' TMA loads
+//                (cta_group::2 loads complete on the leader's barrier); the
+//                leader's producer arms it with both CTAs' byte count.
+//   cd_full[s]   Q8_0, each CTA: its own codes + scales bytes.
+//   ld_empty[s]  each CTA: the leader's UMMA commit (multicast to both CTAs)
+//                + (Q8_0) this CTA's dequant warps.
+//   b_full[b]    leader: dequant warps of both CTAs (remote arrive).
+//   b_empty[b]   each CTA: the leader's UMMA commit (multicast).
+//   acc_full[a]  each CTA: the leader's UMMA commit (multicast).
+//   acc_empty[a] leader: epilogue warps of both CTAs (remote arrive).
+#include "gemm_common.cuh"
+
+namespace rb {
+
+template <int BN_, int LSTAGES_, bool I8_, int BSTAGES_>
+struct PairCfg {
+  static constexpr int BN = BN_;                    // UMMA N of the pair tile
+  static constexpr int HB = BN / 2;                 // weight rows staged per CTA
+  static constexpr int LSTAGES = LSTAGES_;
+  static constexpr bool I8 = I8_;
+  static constexpr bool Q8 = !I8_;
+  static constexpr int BSTAGES = Q8 ? BSTAGES_ : 1;
+  static constexpr int ELEM = I8 ? 1 : 2;
+  static constexpr int BK = 128 / ELEM;             // K elements per stage (one 128-B atom)
+  static constexpr int UMMA_K = I8 ? 32 : 16;
+  static constexpr int KSTEPS = BK / UMMA_K;        // 4
+  static constexpr int A_BYTES = 128 * 128;         // this CTA's 128 rows of A
+  static constexpr int B_BYTES = HB * 128;          // this CTA's half of B (s8, or dequantised f16)
+  static constexpr int CODE_BYTES = Q8 ? HB * 64 : 0;
+  static constexpr int SC_BYTES = Q8 ? 2 * HB * 2 : 0;
+  static constexpr uint32_t PAIR_TX = I8 ? 2 * (A_BYTES + B_BYTES) : 2 * A_BYTES;
+  static constexpr uint32_t CODE_TX = CODE_BYTES + SC_BYTES;
+  static constexpr int LSTAGE = round1k(A_BYTES + (I8 ? B_BYTES : CODE_BYTES + SC_BYTES));
+  static constexpr int BRING_OFF = LSTAGES * LSTAGE;
+  static constexpr int BRING = Q8 ? BSTAGES * B_BYTES : 0;
+  static constexpr int EPI_OFF = BRING_OFF + BRING;
+  static constexpr int EPI_BYTES = kNumEpiWarps * 2 * kEpiBufBytes;
+  static constexpr int BAR_OFF = EPI_OFF + EPI_BYTES;
+  static constexpr int SMEM_BYTES = BAR_OFF + 512 + 1024;
+  static constexpr int NUM_WARPS = Q8 ? (kDqWarp0 + kNumDqWarps) : 6;
+  static constexpr int THREADS = NUM_WARPS * 32;
+  static constexpr uint32_t TMEM_COLS = 2 * BN <= 256 ? 256 : 512;  // two accumulators
+  static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "pair UMMA N");
+  static_assert(B_BYTES % 1024 == 0, "B halves keep 1024-byte alignment");
+  static_assert(BAR_OFF % 1024 == 0, "stage alignment");
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+};
+
+template <class Cfg>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
+gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmC,
+                 GemmArgs args) {
+  constexpr int BN = Cfg::BN;
+  constexpr int HB = Cfg::HB;
+  constexpr int LSTAGES = Cfg::LSTAGES;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::BAR_OFF);
+  uint64_t* ld_full = bars;                          // [LSTAGES]
+  uint64_t* cd_full = ld_full + LSTAGES;             // [LSTAGES]
+  uint64_t* ld_empty = cd_full + LSTAGES;            // [LSTAGES]
+  uint64_t* b_full = ld_empty + LSTAGES;             // [BSTAGES]
+  uint64_t* b_empty = b_full + Cfg::BSTAGES;         // [BSTAGES]
+  uint64_t* acc_full = b_empty + Cfg::BSTAGES;       // [2]
+  uint64_t* acc_empty = acc_full + 2;                // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int M = args.M, N = args.N, K = args.K;
+  const int tiles_n = (N + BN - 1) / BN;
+  const int tiles_m = (M + 255) / 256;
+  const int num_tiles = tiles_m * tiles_n;
+  const int num_kb = (K + Cfg::BK - 1) / Cfg::BK;
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < LSTAGES; ++s) {
+      mbar_init(&ld_full[s], 1);
+      mbar_init(&cd_full[s], 1);
+      mbar_init(&ld_empty[s], Cfg::Q8 ? 1 + kNumDqWarps : 1);
+    }
+    for (int i = 0; i < Cfg::BSTAGES; ++i) {
+      mbar_init(&b_full[i], 2 * kNumDqWarps);
+      mbar_init(&b_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 2 * kNumEpiWarps);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (Cfg::Q8) tma_prefetch_desc(&tmS);
+    if (args.tma_store) tma_prefetch_desc(&tmC);
+  }
+  // Both CTAs' barriers are initialised (and visible cluster-wide) before any
+  // TMA completion or remote arrive can target them.
+  tc_fence_before();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (elect_one_sync()) {
+      int ls = 0;
+      uint32_t lph = 0;
+      for (int t = pair; t < num_tiles; t += npairs) {
+        const int m0 = (t / tiles_n) * 256 + static_cast<int>(rank) * 128;
+        const int nb = (t % tiles_n) * BN + static_cast<int>(rank) * HB;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&ld_empty[ls], lph ^ 1, args.err, abort_flag)) goto producer_done;
+          uint8_t* st = smem + ls * Cfg::LSTAGE;
+          const uint32_t lf = mapa_shared(&ld_full[ls], 0);
+          if (rank == 0) mbar_arrive_expect_tx(&ld_full[ls], Cfg::PAIR_TX);
+          tma_load_2d_pair(st, &tmA, lf, kb * Cfg::BK, m0);
+          if constexpr (Cfg::I8) {
+            tma_load_2d_pair(st + Cfg::A_BYTES, &tmB, lf, kb * Cfg::BK, nb);
+          } else {
+            mbar_arrive_expect_tx(&cd_full[ls], Cfg::CODE_TX);
+            tma_load_2d(st + Cfg::A_BYTES, &tmB, &cd_full[ls], kb * 64, nb);
+            tma_load_2d(st + Cfg::A_BYTES + Cfg::CODE_BYTES, &tmS, &cd_full[ls], nb, kb * 2);
+          }
+          if (++ls == LSTAGES) { ls = 0; lph ^= 1; }
+        }
+      }
+    producer_done:;
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ UMMA issuer (leader)
+    if (rank == 0 && elect_one_sync()) {
+      constexpr uint32_t idesc =
+          Cfg::I8 ? idesc_i8(256, BN) : idesc_f16(256, BN, false, false, false);
+      constexpr uint16_t kBoth = 0x3;
+      int ls = 0, bs = 0;
+      uint32_t lph = 0, bph = 0;
+      int local = 0;
+      for (int t = pair; t < num_tiles; t += npairs, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait_cluster(&acc_empty[acc], acc_phase ^ 1, args.err, abort_flag)) goto mma_done;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_cluster(&ld_full[ls], lph, args.err, abort_flag)) goto mma_done;
+          if constexpr (Cfg::Q8) {
+            if (!mbar_wait_cluster(&b_full[bs], bph, args.err, abort_flag)) goto mma_done;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + ls * Cfg::LSTAGE);
+          const uint32_t b_addr = Cfg::Q8 ? smem_u32(smem + Cfg::BRING_OFF + bs * Cfg::B_BYTES)
+                                          : a_addr + Cfg::A_BYTES;
+#pragma unroll
+          for (int ks = 0; ks < Cfg::KSTEPS; ++ks) {
+            const uint64_t da = desc_kmajor_sw128(a_addr + ks * 32);
+            const uint64_t db = desc_kmajor_sw128(b_addr + ks * 32);
+            const uint32_t accum = (kb > 0 || ks > 0) ? 1u : 0u;
+            if constexpr (Cfg::I8) umma_i8_pair(d_tmem, da, db, idesc, accum);
+            else umma_f16_pair(d_tmem, da, db, idesc, accum);
+          }
+          umma_commit_pair(&ld_empty[ls], kBoth);  // both CTAs' stage s is free once these retire
+          if (++ls == LSTAGES) { ls = 0; lph ^= 1; }
+          if constexpr (Cfg::Q8) {
+            umma_commit_pair(&b_empty[bs], kBoth);
+            if (++bs == Cfg::BSTAGES) { bs = 0; bph ^= 1; }
+          }
+        }
+        umma_commit_pair(&acc_full[acc], kBoth);
+      }
+    mma_done:;
+    }
+  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + kNumEpiWarps) {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const EpiParams ep{args.s_col, args.out_dtype, args.out_scale, args.out_inv};
+    uint8_t* ebuf = smem + Cfg::EPI_OFF + (warp - kEpiWarp0) * 2 * kEpiBufBytes;
+    const int mode = epi_mode(Cfg::I8, args.out_dtype, args.out_scale);
+    int buf = 0;
+    int local = 0;
+    for (int t = pair; t < num_tiles; t += npairs, ++local) {
+      const int n0 = (t % tiles_n) * BN;
+      const int m0 = (t / tiles_n) * 256 + static_cast<int>(rank) * 128;
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!warp_wait(&acc_full[acc], acc_phase, args.err, abort_flag)) break;
+      tc_fence_after();
+      epi_block<BN, Cfg::I8>(tmem_base, acc * BN, quarter, lane, m0, n0, M, N, args.s_row, args.out,
+                             args.ldo, mode, ep, args.tma_store != 0, &tmC, ebuf, buf);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(&acc_empty[acc], 0));
+    }
+    if (args.tma_store && lane == 0) bulk_wait_all<0>();  // stores complete before exit
+  } else if (Cfg::Q8 && warp >= kDqWarp0) {
+    // ------------------------------------------------------------ Q8_0 dequant (both CTAs)
+    // This CTA's HB weight rows: chunk (row, c) — 8 codes — is read from the
+    // staged codes at row*64 + c*8 and written as 8 f16 in the 128-byte
+    // swizzled K-major layout the UMMA descriptor reads.
+    constexpr int kChunks = HB * 8;
+    constexpr int kThreads = kNumDqWarps * 32;
+    constexpr int kPer = (kChunks + kThreads - 1) / kThreads;
+    const int tid = threadIdx.x - kDqWarp0 * 32;
+    int ls = 0, bs = 0;
+    uint32_t lph = 0, bph = 0;
+    for (int t = pair; t < num_tiles; t += npairs) {
+      for (int kb = 0; kb < num_kb; ++kb) {
+        if (!warp_wait(&cd_full[ls], lph, args.err, abort_flag)) goto dq_done;
+        if (!warp_wait(&b_empty[bs], bph ^ 1, args.err, abort_flag)) goto dq_done;
+        const uint8_t* codes = smem + ls * Cfg::LSTAGE + Cfg::A_BYTES;
+        const __half* sc = reinterpret_cast<const __half*>(codes + Cfg::CODE_BYTES);
+        uint8_t* sb = smem + Cfg::BRING_OFF + bs * Cfg::B_BYTES;
+#pragma unroll
+        for (int j = 0; j < kPer; ++j) {
+          const int i = tid + j * kThreads;
+          if (kChunks % kThreads == 0 || i < kChunks) {
+            const int rowi = i >> 3, c = i & 7;
+            const uint2 q = *reinterpret_cast<const uint2*>(codes + rowi * 64 + c * 8);
+            const __half d = sc[(c >> 2) * HB + rowi];
+            *reinterpret_cast<uint4*>(sb + rowi * 128 + ((c ^ (rowi & 7)) << 4)) =
+                q8_dequant8_f16(q, d);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive_cluster(mapa_shared(&b_full[bs], 0));  // the leader's UMMA reads this half
+          mbar_arrive(&ld_empty[ls]);                         // staged codes consumed
+        }
+        if (++ls == LSTAGES) { ls = 0; lph ^= 1; }
+        if (++bs == Cfg::BSTAGES) { bs = 0; bph ^= 1; }
+      }
+    }
+  dq_done:;
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) drain_after_abort();  // let in-flight TMA / UMMA work retire
+  // Neither CTA leaves (or frees TMEM) while the pair's UMMAs may still read
+  // its shared memory or write its TMEM.
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// --------------------------------------------------------------------------
+// Host-side launch.
+
+using PairQ8_256 = PairCfg<256, 5, false, 4>;
+using PairQ8_128 = PairCfg<128, 6, false, 6>;
+using PairI8_256 = PairCfg<256, 6, true, 1>;
+using PairI8_128 = PairCfg<128, 8, true, 1>;
+
+template <class Cfg>
+static int launch_pair_cfg(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmS,
+                           const CUtensorMap* tmC, const GemmArgs& a, int num_sms,
+                           cudaStream_t stream) {
+  const int tiles = ((a.M + 255) / 256) * ((a.N + Cfg::BN - 1) / Cfg::BN);
+  static uint64_t configured = 0;  // one bit per device ordinal
+  static int max_pairs[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(configured & (1ull << (dev & 63)))) {
+    if (cudaFuncSetAttribute(gemm_pair_kernel<Cfg>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Cfg::SMEM_BYTES) != cudaSuccess)
+      return RB_E_DEVICE;
+    // Co-resident pairs: one CTA per SM, two SMs of a cluster-capable pair.
+    // (The kernel's compile-time cluster shape applies; none is passed here.)
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2 * (num_sms / 2));
+    cfg.blockDim = dim3(Cfg::THREADS);
+    cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, gemm_pair_kernel<Cfg>, &cfg) != cudaSuccess ||
+        clusters < 1) {
+      cudaGetLastError();
+      clusters = num_sms / 2;
+    }
+    max_pairs[dev & 63] = clusters;
+    configured |= 1ull << (dev & 63);
+  }
+  int pairs = max_pairs[dev & 63];
+  if (pairs > tiles) pairs = tiles;
+  GemmArgs args = a;
+  const int out_bytes = (a.out_dtype == RB_DTYPE_F16 || a.out_dtype == RB_DTYPE_BF16) ? 2 : 4;
+  args.tma_store = tmC != nullptr && (Cfg::BN % (128 / out_bytes)) == 0;
+  gemm_pair_kernel<Cfg><<<2 * pairs, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(
+      tmA, tmB, tmS, tmC ? *tmC : tmA, args);
+  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
+}
+
+int launch_q8_gemm_pair(const GemmArgs& a, int bn, int num_sms, const CUtensorMap& tmA,
+                        const CUtensorMap& tmCodes, const CUtensorMap& tmScales,
+                        const CUtensorMap* tmC, cudaStream_t stream) {
+  switch (bn) {
+    case 256: return launch_pair_cfg<PairQ8_256>(tmA, tmCodes, tmScales, tmC, a, num_sms, stream);
+    case 128: return launch_pair_cfg<PairQ8_128>(tmA, tmCodes, tmScales, tmC, a, num_sms, stream);
+    default: return RB_E_SHAPE;
+  }
+}
+
+int launch_w8a8_gemm_pair(const GemmArgs& a, int bn, int num_sms, const CUtensorMap& tmA,
+                          const CUtensorMap& tmB, const CUtensorMap* tmC, cudaStream_t stream) {
+  switch (bn) {
+    case 256: return launch_pair_cfg<PairI8_256>(tmA, tmB, tmA, tmC, a, num_sms, stream);
+    case 128: return launch_pair_cfg<PairI8_128>(tmA, tmB, tmA, tmC, a, num_sms, stream);
+    default: return RB_E_SHAPE;
+  }
+}
+
+}  // namespace rb

@@ -25,23 +25,32 @@ struct GemmLaunch {
   float out_scale;        // W8A8: 0 = unrounded output
   uint32_t* err;
   int num_sms;
-  int force_bn;           // 0 = heuristic
 };
 
-// Tile shape the persistent GEMM will use for an [M, N] output: N tile (the
-// weight tensor maps are built per N tile) and 128-row M halves per tile.
-void gemm_pick(bool i8, int M, int N, int num_sms, int* bn, int* mh);
-// Q8_0: tmA = f16 activations [M, K] (box 64 x 128*mh, 128-B swizzle); tmCodes =
-// codes [N, K] (box 64 x bn); tmScales = f16 scales [K/32, N] (box bn x 2);
-// tmC = output map (box 32 rows x 128 B, 128-B swizzle) or nullptr for direct
-// stores.
-int launch_q8_gemm(const GemmLaunch& L, int bn, int mh, const CUtensorMap& tmA,
+// Tile plan of one matmul. Single CTA: a (128*mh) x bn output tile per CTA.
+// Pair: a 256 x bn tile per (2,1,1) cluster of CTAs running cta_group::2 UMMA,
+// each CTA staging 128 rows of A and bn/2 rows of the weight.
+struct GemmPlan {
+  int bn;
+  int mh;
+  bool pair;
+  int weight_rows() const { return pair ? bn / 2 : bn; }  // weight map box height
+  int a_rows() const { return pair ? 128 : 128 * mh; }     // activation map box height
+};
+GemmPlan gemm_plan(bool i8, int M, int N, int K, int num_sms);
+// Restricts gemm_plan to single-CTA or (preferably) pair tiles; returns the old policy.
+int set_gemm_policy(int policy);
+// Q8_0: tmA = f16 activations [M, K] (box 64 x a_rows(), 128-B swizzle);
+// tmCodes = codes [N, K] (box 64 x weight_rows()); tmScales = f16 scales
+// [K/32, N] (box weight_rows() x 2); tmC = output map (box 32 rows x 128 B,
+// 128-B swizzle) or nullptr for direct stores.
+int launch_q8_gemm(const GemmLaunch& L, const GemmPlan& plan, const CUtensorMap& tmA,
                    const CUtensorMap& tmCodes, const CUtensorMap& tmScales, const CUtensorMap* tmC,
                    cudaStream_t stream);
 // W8A8: tmA = s8 activation codes [M, K] (box 128 x 128), tmB = s8 weight
-// codes [N, K] (box 128 x bn), both 128-B swizzled.
-int launch_w8a8_gemm(const GemmLaunch& L, int bn, const CUtensorMap& tmA, const CUtensorMap& tmB,
-                     const CUtensorMap* tmC, cudaStream_t stream);
+// codes [N, K] (box 128 x weight_rows()), both 128-B swizzled.
+int launch_w8a8_gemm(const GemmLaunch& L, const GemmPlan& plan, const CUtensorMap& tmA,
+                     const CUtensorMap& tmB, const CUtensorMap* tmC, cudaStream_t stream);
 int launch_q8_dequant(const int8_t* codes, const void* scales, int N, int K, int pitch, void* out,
                       bool f16_out, cudaStream_t stream);
 
@@ -123,7 +132,7 @@ struct W8A8View {
   const float* w_scale;    // [n]
   int64_t n, k;
   float in_scale, out_scale;
-  CUtensorMap tm_codes[2];  // box heights 256 / 128
+  CUtensorMap tm_codes[4];  // box heights 256 / 128 / 96 / 64 (bn_index)
   uint32_t* err;
   int num_sms;
   int device;

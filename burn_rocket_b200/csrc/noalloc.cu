@@ -109,10 +109,9 @@ extern "C" int rb_matmul_w8a8_noalloc(int64_t id, const void* x, int x_dtype, in
   L.err = v.err;
   L.num_sms = v.num_sms;
   const bool tstore = make_output_map(&tmC, y, y_dtype, m, v.n);
-  int bn = 0, mh = 1;
-  gemm_pick(true, L.M, L.N, v.num_sms, &bn, &mh);
-  if ((rc = launch_w8a8_gemm(L, bn, tmA, v.tm_codes[bn_index(bn)], tstore ? &tmC : nullptr, st)) !=
-      RB_OK)
+  const GemmPlan plan = gemm_plan(true, L.M, L.N, L.K, v.num_sms);
+  if ((rc = launch_w8a8_gemm(L, plan, tmA, v.tm_codes[bn_index(plan.weight_rows())],
+                             tstore ? &tmC : nullptr, st)) != RB_OK)
     return report_error(rc, "w8a8 gemm launch failed");
   count_launches(1);
   return RB_OK;

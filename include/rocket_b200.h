@@ -254,6 +254,17 @@ RB_API int rb_mem_stats(int64_t* weights_bytes, int64_t* scratch_bytes, int64_t*
 /* Number of rocket-b200 kernel launches issued since the last reset. */
 RB_API int64_t rb_launch_count(int reset);
 
+/* GEMM tile policy for later matmul calls (process-wide; no counterpart in the
+ * reference): RB_TILES_AUTO picks single-CTA or CTA-pair tiles by a cost model,
+ * RB_TILES_SINGLE uses only single-CTA tiles, RB_TILES_PAIR prefers CTA-pair
+ * (256-row, cta_group::2) tiles. Results are bit-identical across policies for
+ * W8A8 and identical up to f32 summation order for Q8_0. Returns the previous
+ * policy, or RB_E_SHAPE for an unknown one. */
+#define RB_TILES_AUTO 0
+#define RB_TILES_SINGLE 1
+#define RB_TILES_PAIR 2
+RB_API int rb_set_tile_policy(int policy);
+
 #ifdef __cplusplus
 }
 #endif

@@ -166,3 +166,47 @@ def test_w8a8_f16_output(rb, orc):
     y = rb.matmul(xd, wid, out_dtype=torch.float16).cpu().numpy()
     want = orc.w8a8_matmul(x, codes, ws)
     assert np.array_equal(y.view(np.uint16), orc.f32_to_f16_bits(want))
+
+
+# ------------------------------------------------------------------ tile policies
+@pytest.fixture
+def tile_policy(rb):
+    """Restores the automatic GEMM tile policy after the test."""
+    yield rb.set_tile_policy
+    rb.set_tile_policy("auto")
+
+
+@pytest.mark.parametrize("policy", ["single", "pair"])
+@pytest.mark.parametrize("m,n,k", [(1, 32, 32), (300, 3456, 1152), (257, 1152, 4304), (600, 1000, 256),
+                                   (1100, 4304, 1152)])
+def test_w8a8_bit_exact_each_tile_policy(rb, orc, tile_policy, policy, m, n, k):
+    """Single-CTA and CTA-pair (cta_group::2, 256-row) tiles both reproduce
+    matmul_qat bit for bit, including M and N tails of the 256-row pair tile."""
+    tile_policy(policy)
+    x, codes, ws, wid, xd = _w8a8_case(rb, orc, m, n, k, seed=m + 2 * n + k)
+    qd, _ = rb.quantize_rows_i8(xd)
+    acc = rb.matmul_i8_acc(qd, wid).cpu().numpy()
+    assert np.array_equal(acc, orc.gemm_i8(qd.cpu().numpy(), codes))
+    y = rb.matmul(xd, wid).cpu().numpy()
+    want = orc.w8a8_matmul(x, codes, ws)
+    assert np.array_equal(y.view(np.uint32), want.view(np.uint32))
+    rb.check_device_errors()
+
+
+@pytest.mark.parametrize("policy", ["single", "pair"])
+@pytest.mark.parametrize("m,n,k", [(1, 32, 32), (300, 3072, 64), (1000, 1024, 1024), (600, 6144, 1024),
+                                   (513, 136, 160)])
+def test_q8_0_gemm_each_tile_policy(rb, orc, tile_policy, policy, m, n, k):
+    tile_policy(policy)
+    got, ref, a, deq = _q8_gemm_case(rb, orc, m, n, k, seed=3 * m + n + k)
+    assert cosine(got, ref) >= COS_MIN
+    assert max_rel(got, ref) <= MAX_REL
+    a16 = orc.f16_bits_to_f32(orc.f32_to_f16_bits(a))
+    w16 = orc.f16_bits_to_f32(orc.f32_to_f16_bits(deq))
+    assert max_rel(got, orc.gemm_f64acc(a16, w16)) <= 1e-5
+
+
+def test_tile_policy_rejects_unknown(rb):
+    import burn_rocket_b200._lib as L
+    assert L.load().rb_set_tile_policy(7) != 0
+    assert rb.set_tile_policy("auto") == "auto"
