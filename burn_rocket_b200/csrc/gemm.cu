@@ -316,6 +316,10 @@ static int launch_cfg(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUte
   return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
 }
 
+static std::atomic<int> g_policy{RB_TILES_AUTO};
+
+int set_gemm_policy(int policy) { return g_policy.exchange(policy); }
+
 // Tile plan minimising the makespan of the persistent grid: rounds of tiles
 // per SM (per SM pair for the pair kernel) times the per-tile cost. A tile's
 // cost is its MMA columns per SM (128-row halves x BN) scaled by a measured
