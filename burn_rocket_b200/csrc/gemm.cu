@@ -329,17 +329,17 @@ int set_gemm_policy(int policy) { return g_policy.exchange(policy); }
 //     tiles (the epilogue, not the operand traffic, bounds them);
 //   * W8A8, K > 2048: pair tiles run ~20% faster (L2 -> SM operand traffic
 //     bounds the single-CTA tile);
-//   * Q8_0, large M: 256 x 128 single-CTA tiles (two M halves sharing one
-//     dequantised B tile) beat pair tiles by ~35%; at small M the pair tile,
-//     which dequantises only half its weight rows per SM, fills the GPU with
-//     fewer, cheaper tiles.
+//   * Q8_0: 256 x 128 single-CTA tiles (two M halves sharing one dequantised
+//     B tile) beat pair tiles by ~35% at large M, and single-CTA tiles also
+//     win at small M (the pair's codes and A share one load ring, which
+//     caps how far the dequant warps can run ahead of the MMA).
 GemmPlan gemm_plan(bool i8, int M, int N, int K, int num_sms) {
   const int policy = g_policy.load();
   struct Shape { int bn, mh; bool pair; double eff; };
   const bool long_k = K > 2048;
   const Shape q8c[] = {{256, 1, false, 2.0}, {128, 1, false, 2.0}, {96, 1, false, 2.0},
-                       {64, 1, false, 2.0},  {128, 2, false, 1.5}, {256, 1, true, 1.6},
-                       {128, 1, true, 1.2}};
+                       {64, 1, false, 2.0},  {128, 2, false, 1.5}, {256, 1, true, 2.2},
+                       {128, 1, true, 2.6}};
   const Shape i8c[] = {{256, 1, false, long_k ? 1.25 : 1.0}, {128, 1, false, long_k ? 1.35 : 1.1},
                        {256, 1, true, long_k ? 1.0 : 1.07}, {128, 1, true, long_k ? 1.15 : 1.2}};
   const Shape* c = i8 ? i8c : q8c;
