@@ -446,16 +446,21 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
           }
         }
         l = l * alpha + rowsum;
-        // The previous P·V of this slot must have retired before O is touched
-        // (and before this tile's P·V is released). Waited every tile.
-        if (it > 0) {
+        // O may only be rescaled once the previous P·V of this slot has
+        // retired. The wait is unambiguous whenever it is taken: S(j) was
+        // committed after P·V(j-2) was issued, so at this point P·V(j-2) has
+        // completed and P·V(j) is not yet issued, i.e. o_done has completed
+        // exactly j-1 or j phases. On the slot's last tile the wait is always
+        // taken so that the epilogue's wait for the final P·V is unambiguous too.
+        const bool need_any = __any_sync(0xffffffffu, need);
+        if (it > 0 && (need_any || j == me.hi)) {
           if (!__all_sync(0xffffffffu, mbar_wait(&o_done[s], (it - 1) & 1, p.err, abort_flag))) {
             ok = false;
             break;
           }
           tc_fence_after();
         }
-        if (__any_sync(0xffffffffu, need)) {
+        if (need_any) {
           uint32_t r[32];
 #pragma unroll
           for (int c0 = 0; c0 < D; c0 += 32) {
