@@ -32,6 +32,8 @@
 #include <cuda_bf16.h>
 
 #include <atomic>
+#include <cstdlib>
+#include <cstring>
 
 #include "gemm_common.cuh"
 
@@ -61,10 +63,12 @@ struct GemmCfg {
   static constexpr int BRING_OFF = LSTAGES * LSTAGE;
   static constexpr int BRING = Q8 ? BSTAGES * B_BYTES : 0;
   static constexpr int EPI_OFF = BRING_OFF + BRING;
-  static constexpr int EPI_BYTES = kNumEpiWarps * 2 * kEpiBufBytes;
+  static constexpr int EPI_WARPS = I8 ? kNumEpiWarpsI8 : kNumEpiWarps;
+  static constexpr int EPI_BUFS = I8 ? 1 : 2;       // staging buffers per epilogue warp
+  static constexpr int EPI_BYTES = EPI_WARPS * EPI_BUFS * kEpiBufBytes;
   static constexpr int BAR_OFF = EPI_OFF + EPI_BYTES;
   static constexpr int SMEM_BYTES = BAR_OFF + 384 + 1024;
-  static constexpr int NUM_WARPS = Q8 ? (kDqWarp0 + kNumDqWarps) : 6;
+  static constexpr int NUM_WARPS = Q8 ? (kDqWarp0 + kNumDqWarps) : kEpiWarp0 + EPI_WARPS;
   static constexpr int THREADS = NUM_WARPS * 32;
   static constexpr int ACC_COLS = MH * BN;          // one accumulator (all M halves)
   static constexpr uint32_t TMEM_COLS = (2 * ACC_COLS <= 32) ? 32 : (2 * ACC_COLS <= 64) ? 64
@@ -114,7 +118,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], kNumEpiWarps);
+      mbar_init(&acc_empty[i], Cfg::EPI_WARPS);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -127,7 +131,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     if (Cfg::Q8) tma_prefetch_desc(&tmS);
-    if (args.tma_store) tma_prefetch_desc(&tmC);
+    if (args.epi_path == kEpiPathTma) tma_prefetch_desc(&tmC);
   }
   tc_fence_before();
   __syncthreads();
@@ -203,11 +207,15 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       }
     mma_done:;
     }
-  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + kNumEpiWarps) {
+  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + Cfg::EPI_WARPS) {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const EpiParams ep{args.s_col, args.out_dtype, args.out_scale, args.out_inv};
-    uint8_t* ebuf = smem + Cfg::EPI_OFF + (warp - kEpiWarp0) * 2 * kEpiBufBytes;
+    uint8_t* ebuf = smem + Cfg::EPI_OFF + (warp - kEpiWarp0) * Cfg::EPI_BUFS * kEpiBufBytes;
+    // With eight epilogue warps, warps 2..5 take the first half of the tile's
+    // columns and warps 6..9 the second (each quarter of TMEM lanes has two).
+    constexpr int kColSplit = Cfg::EPI_WARPS / 4;
+    const int cbeg = ((warp - kEpiWarp0) >> 2) * (BN / kColSplit), cend = cbeg + BN / kColSplit;
     const int mode = epi_mode(Cfg::I8, args.out_dtype, args.out_scale);
     int buf = 0;
     int local = 0;
@@ -220,14 +228,15 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       for (int h = 0; h < Cfg::MH; ++h) {
       const int m0 = (t / tiles_n) * Cfg::BM + h * 128;
       const uint32_t acc_col = acc * Cfg::ACC_COLS + h * BN;
-      epi_block<BN, Cfg::I8>(tmem_base, acc_col, quarter, lane, m0, n0, M, N, args.s_row, args.out,
-                             args.ldo, mode, ep, args.tma_store != 0, &tmC, ebuf, buf);
+      epi_block<BN, Cfg::I8, Cfg::EPI_BUFS>(tmem_base, acc_col, quarter, lane, m0, n0, cbeg, cend, M, N,
+                                            args.s_row, args.out, args.ldo, mode, ep, args.epi_path,
+                                            &tmC, ebuf, buf);
       }  // M halves
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
     }
-    if (args.tma_store && lane == 0) bulk_wait_all<0>();  // stores complete before exit
+    if (args.epi_path == kEpiPathTma && lane == 0) bulk_wait_all<0>();  // stores complete before exit
   } else if (Cfg::Q8 && warp >= kDqWarp0) {
     // ------------------------------------------------------------ Q8_0 dequant
     // Chunk (row, c) — 8 codes of one weight row — is read from the staged
@@ -310,10 +319,23 @@ static int launch_cfg(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUte
   GemmArgs args = a;
   const int out_bytes = (a.out_dtype == RB_DTYPE_F16 || a.out_dtype == RB_DTYPE_BF16) ? 2 : 4;
   // The TMA-store epilogue writes whole 128-byte rows of the N tile.
-  args.tma_store = tmC != nullptr && (Cfg::BN % (128 / out_bytes)) == 0;
+  // Both fast paths write whole 128-byte rows of the N tile; tmC != nullptr
+  // means the output rows are 16-byte aligned.
+  args.epi_path = (tmC == nullptr || (Cfg::BN % (128 / out_bytes)) != 0) ? kEpiPathScalar
+                  : epi_path_default();
   gemm_kernel<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(tmA, tmB, tmS,
                                                                      tmC ? *tmC : tmA, args);
   return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
+}
+
+int epi_path_default() {
+  static const int path = [] {
+    const char* v = getenv("ROCKET_B200_EPILOGUE");
+    if (v && strcmp(v, "tma") == 0) return static_cast<int>(kEpiPathTma);
+    if (v && strcmp(v, "vector") == 0) return static_cast<int>(kEpiPathVector);
+    return static_cast<int>(kEpiPathTma);  // measured faster on B200 for every GEMM shape
+  }();
+  return path;
 }
 
 static std::atomic<int> g_policy{RB_TILES_AUTO};

@@ -13,7 +13,8 @@
 namespace rb {
 
 constexpr int kEpiWarp0 = 2;      // first epilogue warp
-constexpr int kNumEpiWarps = 4;
+constexpr int kNumEpiWarps = 4;   // Q8_0 kernels: one warp per TMEM lane quarter
+constexpr int kNumEpiWarpsI8 = 8; // W8A8 kernels: two warps per lane quarter (column halves)
 constexpr int kDqWarp0 = 6;       // first dequant warp (Q8_0 only)
 constexpr int kNumDqWarps = 8;
 constexpr int kEpiBufBytes = 4096;  // 32 rows x 128 B, one per warp and buffer
@@ -31,7 +32,7 @@ struct GemmArgs {
   int out_dtype;       // RB_DTYPE_* (RB_DTYPE_I32: raw int8-GEMM accumulators)
   float out_scale;     // W8A8: calibrated output grid (0 = unrounded)
   float out_inv;       // 1 / out_scale in f32
-  int tma_store;       // epilogue through smem + TMA store (else direct stores)
+  int epi_path;        // kEpiPath*: how the epilogue writes the output tile
   uint32_t* err;
 };
 
@@ -103,6 +104,15 @@ __device__ __forceinline__ float epi_value(const EpiParams e, uint32_t r, float 
   return y;
 }
 
+// Epilogue output paths: element-wise bounds-checked stores (any layout),
+// swizzled shared-memory staging + TMA store, or 16-byte vector stores from
+// registers (no shared-memory traffic; needs 16-byte aligned rows).
+enum : int { kEpiPathScalar = 0, kEpiPathTma = 1, kEpiPathVector = 2 };
+
+// Fast path used when the output allows both (host side; the environment
+// variable ROCKET_B200_EPILOGUE=tma|vector overrides the built-in choice).
+int epi_path_default();
+
 // Epilogue modes of the TMA-store path, fixed per launch: raw 4-byte
 // accumulators (f32 for Q8_0, s32 for RB_DTYPE_I32), f16 / bf16 casts, and the
 // W8A8 scaled forms (kEpiS8*; Q = onto the calibrated output grid).
@@ -117,8 +127,11 @@ __host__ __device__ __forceinline__ int epi_mode(bool i8, int out_dtype, float o
   return kEpiS8F32 + cast + (out_scale != 0.0f ? 3 : 0);
 }
 
-// One 32-row x 128-byte chunk of the output tile, written into the
-// 128-byte-swizzled staging row `b` of this lane: columns [0, CW) of the chunk
+// One 32-row x 128-byte chunk of the output tile: this lane's 128 bytes of
+// its row go either into the 128-byte-swizzled staging row `b` (for a TMA
+// store) or, when `g` is non-null, straight to global memory at `g` as
+// 16-byte stores of the groups that lie below column nvalid (`live` = the row
+// exists). Columns [0, CW) of the chunk
 // from accumulator registers ra (0..31) and rb (32..63, 2-byte outputs only).
 // SCALE applies the W8A8 epilogue f32(acc) * (rs * s_col[n]) — in that order,
 // for bit parity with ext.rs:1350-1363 — with the chunk's column scales read
@@ -127,9 +140,9 @@ __host__ __device__ __forceinline__ int epi_mode(bool i8, int out_dtype, float o
 // store). OUT is the output element size in bytes' role: 4 (f32 / raw), 1 (f16),
 // 2 (bf16). QGRID rounds onto the static output grid (ext.rs:1236-1238).
 template <bool SCALE, int OUT, bool QGRID>
-__device__ __forceinline__ void epi_chunk(uint8_t* b, int lane, const uint32_t (&ra)[32],
-                                          const uint32_t (&rb)[32], float rs, const float* scp,
-                                          int nvalid, const EpiParams& ep) {
+__device__ __forceinline__ void epi_chunk(uint8_t* b, uint4* g, bool live, int lane,
+                                          const uint32_t (&ra)[32], const uint32_t (&rb)[32], float rs,
+                                          const float* scp, int nvalid, const EpiParams& ep) {
   constexpr int CW = OUT == 4 ? 32 : 64;
   float sc[SCALE ? CW : 1];
   if constexpr (SCALE) {
@@ -178,22 +191,31 @@ __device__ __forceinline__ void epi_chunk(uint8_t* b, int lane, const uint32_t (
       }
       o = make_uint4(pk[0], pk[1], pk[2], pk[3]);
     }
-    *reinterpret_cast<uint4*>(b + ((j ^ (lane & 7)) << 4)) = o;
+    if (g == nullptr) {
+      *reinterpret_cast<uint4*>(b + ((j ^ (lane & 7)) << 4)) = o;
+    } else if (live && (j + 1) * (CW / 8) <= nvalid) {
+      __stcg(g + j, o);  // 16 bytes = CW/8 columns; L2 only (no reuse in L1)
+    }
   }
 }
 
 
 // One 128-row block of a finished accumulator (TMEM columns acc_col ..
-// acc_col + BN) -> output rows m0 .. m0+127, columns n0 .. n0+BN: each of the
-// four epilogue warps owns the TMEM lane quarter `quarter` (32 rows). With
-// tma_store the rows go through this warp's two 4 KB swizzled staging buffers
-// (ebuf, alternating by `buf`) and TMA stores clip at the tensor edge;
-// otherwise direct (bounds-checked) stores.
-template <int BN, bool I8>
+// acc_col + BN) -> output rows m0 .. m0+127, columns n0 .. n0+BN: each
+// epilogue warp owns the TMEM lane quarter `quarter` (32 rows) and the tile
+// columns [cbeg, cend). NBUF staging buffers of 4 KB per warp. With
+// the TMA path the rows go through this warp's two 4 KB swizzled staging
+// buffers (ebuf, alternating by `buf`) and TMA stores clip at the tensor
+// edge; the vector path stores each lane's row straight from registers; the
+// scalar path stores element by element with bounds checks.
+template <int BN, bool I8, int NBUF>
 __device__ __forceinline__ void epi_block(uint32_t tmem_base, uint32_t acc_col, int quarter, int lane,
-                                          int m0, int n0, int M, int N, const float* s_row, void* out,
-                                          int ldo, int mode, const EpiParams ep, bool tma_store,
-                                          const CUtensorMap* tmC, uint8_t* ebuf, int& buf) {
+                                          int m0, int n0, int cbeg, int cend, int M, int N,
+                                          const float* s_row, void* out, int ldo, int mode,
+                                          const EpiParams ep, int path, const CUtensorMap* tmC,
+                                          uint8_t* ebuf, int& buf) {
+  const bool tma_store = path == kEpiPathTma;
+  const bool vec_store = path == kEpiPathVector;
   const int row = quarter * 32 + lane;
   const int CW = (mode == kEpiRaw4 || mode == kEpiS8F32 || mode == kEpiS8F32Q) ? 32 : 64;
   const int m = m0 + row;
@@ -201,49 +223,58 @@ __device__ __forceinline__ void epi_block(uint32_t tmem_base, uint32_t acc_col, 
   // Raw int32 output (RB_DTYPE_I32) carries no scales.
   if (I8 && m < M && ep.out_dtype != RB_DTYPE_I32) rs = s_row[m];
   const bool rows_live = m0 + quarter * 32 < M;  // warp-uniform
-  if (tma_store) {
+  if (tma_store || vec_store) {
     if (rows_live) {
-      for (int c0 = 0; c0 < BN && n0 + c0 < N; c0 += CW) {
+      for (int c0 = cbeg; c0 < cend && n0 + c0 < N; c0 += CW) {
         uint32_t ra[32], rb[32];  // columns c0..c0+31 and (2-byte outputs) c0+32..c0+63
         tmem_ld32(tmem_addr(tmem_base, quarter * 32, acc_col + c0), ra);
         if (CW == 64) tmem_ld32(tmem_addr(tmem_base, quarter * 32, acc_col + c0 + 32), rb);
         tmem_wait_ld();
         // The buffer about to be written must have been read by its
         // previous TMA store (at most one store of this warp in flight).
-        if (lane == 0) bulk_wait_read<1>();
-        __syncwarp();
+        if (tma_store) {
+          if (lane == 0) bulk_wait_read<NBUF - 1>();
+          __syncwarp();
+        }
         uint8_t* b = ebuf + buf * kEpiBufBytes + lane * 128;
+        uint4* g = nullptr;
+        if (vec_store)
+          g = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(out) +
+                                       (static_cast<int64_t>(min(m, M - 1)) * ldo + n0 + c0) *
+                                           (CW == 64 ? 2 : 4));
         const float* scp = I8 ? ep.s_col + n0 + c0 : nullptr;
         const int nvalid = N - (n0 + c0);
         switch (mode) {
-          case kEpiRaw4: epi_chunk<false, 4, false>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
-          case kEpiF16: epi_chunk<false, 1, false>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
-          case kEpiBF16: epi_chunk<false, 2, false>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
+          case kEpiRaw4: epi_chunk<false, 4, false>(b, g, m < M, lane, ra, rb, rs, scp, nvalid, ep); break;
+          case kEpiF16: epi_chunk<false, 1, false>(b, g, m < M, lane, ra, rb, rs, scp, nvalid, ep); break;
+          case kEpiBF16: epi_chunk<false, 2, false>(b, g, m < M, lane, ra, rb, rs, scp, nvalid, ep); break;
           default:
             if constexpr (I8) {
               switch (mode) {
-                case kEpiS8F32: epi_chunk<true, 4, false>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
-                case kEpiS8F16: epi_chunk<true, 1, false>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
-                case kEpiS8BF16: epi_chunk<true, 2, false>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
-                case kEpiS8F32Q: epi_chunk<true, 4, true>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
-                case kEpiS8F16Q: epi_chunk<true, 1, true>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
-                default: epi_chunk<true, 2, true>(b, lane, ra, rb, rs, scp, nvalid, ep); break;
+                case kEpiS8F32: epi_chunk<true, 4, false>(b, g, m < M, lane, ra, rb, rs, scp, nvalid, ep); break;
+                case kEpiS8F16: epi_chunk<true, 1, false>(b, g, m < M, lane, ra, rb, rs, scp, nvalid, ep); break;
+                case kEpiS8BF16: epi_chunk<true, 2, false>(b, g, m < M, lane, ra, rb, rs, scp, nvalid, ep); break;
+                case kEpiS8F32Q: epi_chunk<true, 4, true>(b, g, m < M, lane, ra, rb, rs, scp, nvalid, ep); break;
+                case kEpiS8F16Q: epi_chunk<true, 1, true>(b, g, m < M, lane, ra, rb, rs, scp, nvalid, ep); break;
+                default: epi_chunk<true, 2, true>(b, g, m < M, lane, ra, rb, rs, scp, nvalid, ep); break;
               }
             }
             break;
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(tmC, ebuf + buf * kEpiBufBytes, n0 + c0, m0 + quarter * 32);
-          bulk_commit();
+        if (tma_store) {
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(tmC, ebuf + buf * kEpiBufBytes, n0 + c0, m0 + quarter * 32);
+            bulk_commit();
+          }
+          if (NBUF == 2) buf ^= 1;
         }
-        buf ^= 1;
       }
     }
   } else {
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 16) {
+    for (int c = cbeg; c < cend; c += 16) {
       uint32_t r[16];
       tmem_ld16(tmem_addr(tmem_base, quarter * 32, acc_col + c), r);
       tmem_wait_ld();

@@ -53,10 +53,12 @@ struct PairCfg {
   static constexpr int BRING_OFF = LSTAGES * LSTAGE;
   static constexpr int BRING = Q8 ? BSTAGES * B_BYTES : 0;
   static constexpr int EPI_OFF = BRING_OFF + BRING;
-  static constexpr int EPI_BYTES = kNumEpiWarps * 2 * kEpiBufBytes;
+  static constexpr int EPI_WARPS = I8 ? kNumEpiWarpsI8 : kNumEpiWarps;
+  static constexpr int EPI_BUFS = I8 ? 1 : 2;       // staging buffers per epilogue warp
+  static constexpr int EPI_BYTES = EPI_WARPS * EPI_BUFS * kEpiBufBytes;
   static constexpr int BAR_OFF = EPI_OFF + EPI_BYTES;
   static constexpr int SMEM_BYTES = BAR_OFF + 512 + 1024;
-  static constexpr int NUM_WARPS = Q8 ? (kDqWarp0 + kNumDqWarps) : 6;
+  static constexpr int NUM_WARPS = Q8 ? (kDqWarp0 + kNumDqWarps) : kEpiWarp0 + EPI_WARPS;
   static constexpr int THREADS = NUM_WARPS * 32;
   static constexpr uint32_t TMEM_COLS = 2 * BN <= 256 ? 256 : 512;  // two accumulators
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "pair UMMA N");
@@ -110,7 +112,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 2 * kNumEpiWarps);
+      mbar_init(&acc_empty[i], 2 * Cfg::EPI_WARPS);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -123,7 +125,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     if (Cfg::Q8) tma_prefetch_desc(&tmS);
-    if (args.tma_store) tma_prefetch_desc(&tmC);
+    if (args.epi_path == kEpiPathTma) tma_prefetch_desc(&tmC);
   }
   // Both CTAs' barriers are initialised (and visible cluster-wide) before any
   // TMA completion or remote arrive can target them.
@@ -201,11 +203,13 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       }
     mma_done:;
     }
-  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + kNumEpiWarps) {
+  } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + Cfg::EPI_WARPS) {
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const EpiParams ep{args.s_col, args.out_dtype, args.out_scale, args.out_inv};
-    uint8_t* ebuf = smem + Cfg::EPI_OFF + (warp - kEpiWarp0) * 2 * kEpiBufBytes;
+    uint8_t* ebuf = smem + Cfg::EPI_OFF + (warp - kEpiWarp0) * Cfg::EPI_BUFS * kEpiBufBytes;
+    constexpr int kColSplit = Cfg::EPI_WARPS / 4;  // warps sharing a TMEM lane quarter
+    const int cbeg = ((warp - kEpiWarp0) >> 2) * (BN / kColSplit), cend = cbeg + BN / kColSplit;
     const int mode = epi_mode(Cfg::I8, args.out_dtype, args.out_scale);
     int buf = 0;
     int local = 0;
@@ -216,13 +220,14 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!warp_wait(&acc_full[acc], acc_phase, args.err, abort_flag)) break;
       tc_fence_after();
-      epi_block<BN, Cfg::I8>(tmem_base, acc * BN, quarter, lane, m0, n0, M, N, args.s_row, args.out,
-                             args.ldo, mode, ep, args.tma_store != 0, &tmC, ebuf, buf);
+      epi_block<BN, Cfg::I8, Cfg::EPI_BUFS>(tmem_base, acc * BN, quarter, lane, m0, n0, cbeg, cend, M, N,
+                                            args.s_row, args.out, args.ldo, mode, ep, args.epi_path,
+                                            &tmC, ebuf, buf);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(&acc_empty[acc], 0));
     }
-    if (args.tma_store && lane == 0) bulk_wait_all<0>();  // stores complete before exit
+    if (args.epi_path == kEpiPathTma && lane == 0) bulk_wait_all<0>();  // stores complete before exit
   } else if (Cfg::Q8 && warp >= kDqWarp0) {
     // ------------------------------------------------------------ Q8_0 dequant (both CTAs)
     // This CTA's HB weight rows: chunk (row, c) — 8 codes — is read from the
@@ -317,7 +322,10 @@ static int launch_pair_cfg(const CUtensorMap& tmA, const CUtensorMap& tmB, const
   if (pairs > tiles) pairs = tiles;
   GemmArgs args = a;
   const int out_bytes = (a.out_dtype == RB_DTYPE_F16 || a.out_dtype == RB_DTYPE_BF16) ? 2 : 4;
-  args.tma_store = tmC != nullptr && (Cfg::BN % (128 / out_bytes)) == 0;
+  // Both fast paths write whole 128-byte rows of the N tile; tmC != nullptr
+  // means the output rows are 16-byte aligned.
+  args.epi_path = (tmC == nullptr || (Cfg::BN % (128 / out_bytes)) != 0) ? kEpiPathScalar
+                  : epi_path_default();
   gemm_pair_kernel<Cfg><<<2 * pairs, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(
       tmA, tmB, tmS, tmC ? *tmC : tmA, args);
   return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
