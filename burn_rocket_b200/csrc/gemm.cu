@@ -347,10 +347,9 @@ int set_gemm_policy(int policy) { return g_policy.exchange(policy); }
 // cost is its MMA columns per SM (128-row halves x BN) scaled by a measured
 // per-SM efficiency factor of the shape, plus a fixed pipeline fill /
 // epilogue overhead. Measured on B200 (rb_matmul, f16 in / out):
-//   * W8A8, K <= 2048: single-CTA 128 x 256 tiles run ~7% faster than pair
-//     tiles (the epilogue, not the operand traffic, bounds them);
-//   * W8A8, K > 2048: pair tiles run ~20% faster (L2 -> SM operand traffic
-//     bounds the single-CTA tile);
+//   * W8A8: pair tiles run ~3% faster than single-CTA 128 x 256 tiles at
+//     K ~ 1k and ~13% faster at K ~ 4k (per SM they stage and read half the
+//     weight bytes; shared-memory bandwidth bounds the single-CTA tile);
 //   * Q8_0: 256 x 128 single-CTA tiles (two M halves sharing one dequantised
 //     B tile) beat pair tiles by ~35% at large M, and single-CTA tiles also
 //     win at small M (the pair's codes and A share one load ring, which
@@ -362,8 +361,8 @@ GemmPlan gemm_plan(bool i8, int M, int N, int K, int num_sms) {
   const Shape q8c[] = {{256, 1, false, 2.0}, {128, 1, false, 2.0}, {96, 1, false, 2.0},
                        {64, 1, false, 2.0},  {128, 2, false, 1.5}, {256, 1, true, 2.2},
                        {128, 1, true, 2.6}};
-  const Shape i8c[] = {{256, 1, false, long_k ? 1.25 : 1.0}, {128, 1, false, long_k ? 1.35 : 1.1},
-                       {256, 1, true, long_k ? 1.0 : 1.07}, {128, 1, true, long_k ? 1.15 : 1.2}};
+  const Shape i8c[] = {{256, 1, false, long_k ? 1.13 : 1.04}, {128, 1, false, long_k ? 1.25 : 1.15},
+                       {256, 1, true, 1.0}, {128, 1, true, 1.12}};
   const Shape* c = i8 ? i8c : q8c;
   const int nc = i8 ? 4 : 7;
   GemmPlan best{c[0].bn, c[0].mh, false};

@@ -23,10 +23,16 @@
 //   cd_full[s]   Q8_0, each CTA: its own codes + scales bytes.
 //   ld_empty[s]  each CTA: the leader's UMMA commit (multicast to both CTAs)
 //                + (Q8_0) this CTA's dequant warps.
-//   b_full[b]    leader: dequant warps of both CTAs (remote arrive).
+//   b_local[b]   each CTA: its own dequant warps (local arrive).
+//   b_full[b]    leader: the peer's half is dequantised — one remote arrive
+//                per stage by the peer's forwarding thread (warp 1), which
+//                waits on the peer's b_local. (Cluster-scope arrives are
+//                costly; one per stage instead of one per dequant warp.)
 //   b_empty[b]   each CTA: the leader's UMMA commit (multicast).
 //   acc_full[a]  each CTA: the leader's UMMA commit (multicast).
-//   acc_empty[a] leader: epilogue warps of both CTAs (remote arrive).
+//   acc_local[a] peer: its own epilogue warps (local arrive).
+//   acc_empty[a] leader: its own epilogue warps (local arrive) + one remote
+//                arrive per tile from the peer's forwarding thread.
 #include "gemm_common.cuh"
 
 namespace rb {
@@ -58,7 +64,9 @@ struct PairCfg {
   static constexpr int EPI_BYTES = EPI_WARPS * EPI_BUFS * kEpiBufBytes;
   static constexpr int BAR_OFF = EPI_OFF + EPI_BYTES;
   static constexpr int SMEM_BYTES = BAR_OFF + 512 + 1024;
-  static constexpr int NUM_WARPS = Q8 ? (kDqWarp0 + kNumDqWarps) : kEpiWarp0 + EPI_WARPS;
+  // Last warp: the peer's accumulator-release forwarder (idle in the leader).
+  static constexpr int FWD_WARP = Q8 ? (kDqWarp0 + kNumDqWarps) : kEpiWarp0 + EPI_WARPS;
+  static constexpr int NUM_WARPS = FWD_WARP + 1;
   static constexpr int THREADS = NUM_WARPS * 32;
   static constexpr uint32_t TMEM_COLS = 2 * BN <= 256 ? 256 : 512;  // two accumulators
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "pair UMMA N");
@@ -84,9 +92,11 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   uint64_t* ld_empty = cd_full + LSTAGES;            // [LSTAGES]
   uint64_t* b_full = ld_empty + LSTAGES;             // [BSTAGES]
   uint64_t* b_empty = b_full + Cfg::BSTAGES;         // [BSTAGES]
-  uint64_t* acc_full = b_empty + Cfg::BSTAGES;       // [2]
+  uint64_t* b_local = b_empty + Cfg::BSTAGES;        // [BSTAGES]
+  uint64_t* acc_full = b_local + Cfg::BSTAGES;       // [2]
   uint64_t* acc_empty = acc_full + 2;                // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* acc_local = acc_empty + 2;               // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_local + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -107,12 +117,14 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       mbar_init(&ld_empty[s], Cfg::Q8 ? 1 + kNumDqWarps : 1);
     }
     for (int i = 0; i < Cfg::BSTAGES; ++i) {
-      mbar_init(&b_full[i], 2 * kNumDqWarps);
+      mbar_init(&b_full[i], 1);
       mbar_init(&b_empty[i], 1);
+      mbar_init(&b_local[i], kNumDqWarps);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 2 * Cfg::EPI_WARPS);
+      mbar_init(&acc_empty[i], Cfg::EPI_WARPS + 1);
+      mbar_init(&acc_local[i], Cfg::EPI_WARPS);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -178,6 +190,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait_cluster(&ld_full[ls], lph, args.err, abort_flag)) goto mma_done;
           if constexpr (Cfg::Q8) {
+            if (!mbar_wait(&b_local[bs], bph, args.err, abort_flag)) goto mma_done;
             if (!mbar_wait_cluster(&b_full[bs], bph, args.err, abort_flag)) goto mma_done;
           }
           tc_fence_after();
@@ -202,6 +215,18 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         umma_commit_pair(&acc_full[acc], kBoth);
       }
     mma_done:;
+    } else if (rank == 1 && Cfg::Q8 && elect_one_sync()) {
+      // Peer: forward "my half of B stage bs is ready" to the leader, once.
+      int bs = 0;
+      uint32_t bph = 0;
+      for (int t = pair; t < num_tiles; t += npairs) {
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&b_local[bs], bph, args.err, abort_flag)) goto fwd_b_done;
+          mbar_arrive_cluster(mapa_shared(&b_full[bs], 0));
+          if (++bs == Cfg::BSTAGES) { bs = 0; bph ^= 1; }
+        }
+      }
+    fwd_b_done:;
     }
   } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + Cfg::EPI_WARPS) {
     // ------------------------------------------------------------ epilogue (both CTAs)
@@ -225,9 +250,20 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                                             &tmC, ebuf, buf);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(mapa_shared(&acc_empty[acc], 0));
+      if (lane == 0) mbar_arrive(rank == 0 ? &acc_empty[acc] : &acc_local[acc]);
     }
     if (args.epi_path == kEpiPathTma && lane == 0) bulk_wait_all<0>();  // stores complete before exit
+  } else if (warp == Cfg::FWD_WARP) {
+    // ------------------------------------------------------------ peer: accumulator release
+    // Forward "my accumulator rows are drained" to the leader, once per tile.
+    if (rank == 1 && elect_one_sync()) {
+      int local = 0;
+      for (int t = pair; t < num_tiles; t += npairs, ++local) {
+        const int acc = local & 1;
+        if (!mbar_wait(&acc_local[acc], (local >> 1) & 1, args.err, abort_flag)) break;
+        mbar_arrive_cluster(mapa_shared(&acc_empty[acc], 0));
+      }
+    }
   } else if (Cfg::Q8 && warp >= kDqWarp0) {
     // ------------------------------------------------------------ Q8_0 dequant (both CTAs)
     // This CTA's HB weight rows: chunk (row, c) — 8 codes — is read from the
@@ -260,8 +296,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive_cluster(mapa_shared(&b_full[bs], 0));  // the leader's UMMA reads this half
-          mbar_arrive(&ld_empty[ls]);                         // staged codes consumed
+          mbar_arrive(&b_local[bs]);    // this CTA's half of B stage bs is written
+          mbar_arrive(&ld_empty[ls]);   // staged codes consumed
         }
         if (++ls == LSTAGES) { ls = 0; lph ^= 1; }
         if (++bs == Cfg::BSTAGES) { bs = 0; bph ^= 1; }
