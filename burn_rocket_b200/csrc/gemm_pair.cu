@@ -20,9 +20,9 @@
 //   ld_full[s]   leader only: A (and W8A8 B) bytes of both CTAs' TMA loads
 //                (cta_group::2 loads complete on the leader's barrier); the
 //                leader's producer arms it with both CTAs' byte count.
-//   cd_full[s]   Q8_0, each CTA: its own codes + scales bytes.
-//   ld_empty[s]  each CTA: the leader's UMMA commit (multicast to both CTAs)
-//                + (Q8_0) this CTA's dequant warps.
+//   ld_empty[s]  each CTA: the leader's UMMA commit (multicast to both CTAs).
+//   cd_full[c]   Q8_0, each CTA: its own codes + scales bytes (codes producer).
+//   cd_empty[c]  Q8_0, each CTA: its own dequant warps have read the stage.
 //   b_local[b]   each CTA: its own dequant warps (local arrive).
 //   b_full[b]    leader: the peer's half is dequantised — one remote arrive
 //                per stage by the peer's forwarding thread (warp 1), which
@@ -37,13 +37,18 @@
 
 namespace rb {
 
-template <int BN_, int LSTAGES_, bool I8_, int BSTAGES_>
+// LSTAGES: A stages (W8A8: A + this CTA's B half). Q8_0 also has a separate
+// ring of CSTAGES staged code/scale stages, refilled by its own producer warp
+// as soon as the dequant warps have read a stage (so dequantisation can run
+// ahead of the MMA by up to CSTAGES stages), and BSTAGES dequantised B stages.
+template <int BN_, int LSTAGES_, bool I8_, int CSTAGES_ = 1, int BSTAGES_ = 1>
 struct PairCfg {
   static constexpr int BN = BN_;                    // UMMA N of the pair tile
   static constexpr int HB = BN / 2;                 // weight rows staged per CTA
   static constexpr int LSTAGES = LSTAGES_;
   static constexpr bool I8 = I8_;
   static constexpr bool Q8 = !I8_;
+  static constexpr int CSTAGES = Q8 ? CSTAGES_ : 1;
   static constexpr int BSTAGES = Q8 ? BSTAGES_ : 1;
   static constexpr int ELEM = I8 ? 1 : 2;
   static constexpr int BK = 128 / ELEM;             // K elements per stage (one 128-B atom)
@@ -55,23 +60,27 @@ struct PairCfg {
   static constexpr int SC_BYTES = Q8 ? 2 * HB * 2 : 0;
   static constexpr uint32_t PAIR_TX = I8 ? 2 * (A_BYTES + B_BYTES) : 2 * A_BYTES;
   static constexpr uint32_t CODE_TX = CODE_BYTES + SC_BYTES;
-  static constexpr int LSTAGE = round1k(A_BYTES + (I8 ? B_BYTES : CODE_BYTES + SC_BYTES));
-  static constexpr int BRING_OFF = LSTAGES * LSTAGE;
+  static constexpr int LSTAGE = round1k(A_BYTES + (I8 ? B_BYTES : 0));
+  static constexpr int CSTAGE = Q8 ? round1k(CODE_BYTES + SC_BYTES) : 0;
+  static constexpr int CODE_OFF = LSTAGES * LSTAGE;
+  static constexpr int BRING_OFF = CODE_OFF + CSTAGES * CSTAGE;
   static constexpr int BRING = Q8 ? BSTAGES * B_BYTES : 0;
   static constexpr int EPI_OFF = BRING_OFF + BRING;
   static constexpr int EPI_WARPS = I8 ? kNumEpiWarpsI8 : kNumEpiWarps;
-  static constexpr int EPI_BUFS = I8 ? 1 : 2;       // staging buffers per epilogue warp
+  static constexpr int EPI_BUFS = 1;                // staging buffers per epilogue warp
   static constexpr int EPI_BYTES = EPI_WARPS * EPI_BUFS * kEpiBufBytes;
   static constexpr int BAR_OFF = EPI_OFF + EPI_BYTES;
   static constexpr int SMEM_BYTES = BAR_OFF + 512 + 1024;
-  // Last warp: the peer's accumulator-release forwarder (idle in the leader).
+  // After the role warps: the peer's accumulator-release forwarder (idle in
+  // the leader) and, for Q8_0, the codes producer.
   static constexpr int FWD_WARP = Q8 ? (kDqWarp0 + kNumDqWarps) : kEpiWarp0 + EPI_WARPS;
-  static constexpr int NUM_WARPS = FWD_WARP + 1;
+  static constexpr int CP_WARP = FWD_WARP + 1;
+  static constexpr int NUM_WARPS = Q8 ? CP_WARP + 1 : FWD_WARP + 1;
   static constexpr int THREADS = NUM_WARPS * 32;
   static constexpr uint32_t TMEM_COLS = 2 * BN <= 256 ? 256 : 512;  // two accumulators
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "pair UMMA N");
   static_assert(B_BYTES % 1024 == 0, "B halves keep 1024-byte alignment");
-  static_assert(BAR_OFF % 1024 == 0, "stage alignment");
+  static_assert(BAR_OFF % 1024 == 0 && BRING_OFF % 1024 == 0, "stage alignment");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
 
@@ -88,9 +97,10 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                                              ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::BAR_OFF);
   uint64_t* ld_full = bars;                          // [LSTAGES]
-  uint64_t* cd_full = ld_full + LSTAGES;             // [LSTAGES]
-  uint64_t* ld_empty = cd_full + LSTAGES;            // [LSTAGES]
-  uint64_t* b_full = ld_empty + LSTAGES;             // [BSTAGES]
+  uint64_t* ld_empty = ld_full + LSTAGES;            // [LSTAGES]
+  uint64_t* cd_full = ld_empty + LSTAGES;            // [CSTAGES]
+  uint64_t* cd_empty = cd_full + Cfg::CSTAGES;       // [CSTAGES]
+  uint64_t* b_full = cd_empty + Cfg::CSTAGES;        // [BSTAGES]
   uint64_t* b_empty = b_full + Cfg::BSTAGES;         // [BSTAGES]
   uint64_t* b_local = b_empty + Cfg::BSTAGES;        // [BSTAGES]
   uint64_t* acc_full = b_local + Cfg::BSTAGES;       // [2]
@@ -113,8 +123,11 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   if (threadIdx.x == 0) {
     for (int s = 0; s < LSTAGES; ++s) {
       mbar_init(&ld_full[s], 1);
+      mbar_init(&ld_empty[s], 1);
+    }
+    for (int s = 0; s < Cfg::CSTAGES; ++s) {
       mbar_init(&cd_full[s], 1);
-      mbar_init(&ld_empty[s], Cfg::Q8 ? 1 + kNumDqWarps : 1);
+      mbar_init(&cd_empty[s], kNumDqWarps);
     }
     for (int i = 0; i < Cfg::BSTAGES; ++i) {
       mbar_init(&b_full[i], 1);
@@ -160,13 +173,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           const uint32_t lf = mapa_shared(&ld_full[ls], 0);
           if (rank == 0) mbar_arrive_expect_tx(&ld_full[ls], Cfg::PAIR_TX);
           tma_load_2d_pair(st, &tmA, lf, kb * Cfg::BK, m0);
-          if constexpr (Cfg::I8) {
-            tma_load_2d_pair(st + Cfg::A_BYTES, &tmB, lf, kb * Cfg::BK, nb);
-          } else {
-            mbar_arrive_expect_tx(&cd_full[ls], Cfg::CODE_TX);
-            tma_load_2d(st + Cfg::A_BYTES, &tmB, &cd_full[ls], kb * 64, nb);
-            tma_load_2d(st + Cfg::A_BYTES + Cfg::CODE_BYTES, &tmS, &cd_full[ls], nb, kb * 2);
-          }
+          if constexpr (Cfg::I8) tma_load_2d_pair(st + Cfg::A_BYTES, &tmB, lf, kb * Cfg::BK, nb);
           if (++ls == LSTAGES) { ls = 0; lph ^= 1; }
         }
       }
@@ -253,6 +260,24 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       if (lane == 0) mbar_arrive(rank == 0 ? &acc_empty[acc] : &acc_local[acc]);
     }
     if (args.epi_path == kEpiPathTma && lane == 0) bulk_wait_all<0>();  // stores complete before exit
+  } else if (Cfg::Q8 && warp == Cfg::CP_WARP) {
+    // ------------------------------------------------------------ codes producer (Q8_0, both CTAs)
+    if (elect_one_sync()) {
+      int cs = 0;
+      uint32_t cph = 0;
+      for (int t = pair; t < num_tiles; t += npairs) {
+        const int nb = (t % tiles_n) * BN + static_cast<int>(rank) * HB;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&cd_empty[cs], cph ^ 1, args.err, abort_flag)) goto codes_done;
+          uint8_t* st = smem + Cfg::CODE_OFF + cs * Cfg::CSTAGE;
+          mbar_arrive_expect_tx(&cd_full[cs], Cfg::CODE_TX);
+          tma_load_2d(st, &tmB, &cd_full[cs], kb * 64, nb);
+          tma_load_2d(st + Cfg::CODE_BYTES, &tmS, &cd_full[cs], nb, kb * 2);
+          if (++cs == Cfg::CSTAGES) { cs = 0; cph ^= 1; }
+        }
+      }
+    codes_done:;
+    }
   } else if (warp == Cfg::FWD_WARP) {
     // ------------------------------------------------------------ peer: accumulator release
     // Forward "my accumulator rows are drained" to the leader, once per tile.
@@ -273,13 +298,13 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     constexpr int kThreads = kNumDqWarps * 32;
     constexpr int kPer = (kChunks + kThreads - 1) / kThreads;
     const int tid = threadIdx.x - kDqWarp0 * 32;
-    int ls = 0, bs = 0;
-    uint32_t lph = 0, bph = 0;
+    int cs = 0, bs = 0;
+    uint32_t cph = 0, bph = 0;
     for (int t = pair; t < num_tiles; t += npairs) {
       for (int kb = 0; kb < num_kb; ++kb) {
-        if (!warp_wait(&cd_full[ls], lph, args.err, abort_flag)) goto dq_done;
+        if (!warp_wait(&cd_full[cs], cph, args.err, abort_flag)) goto dq_done;
         if (!warp_wait(&b_empty[bs], bph ^ 1, args.err, abort_flag)) goto dq_done;
-        const uint8_t* codes = smem + ls * Cfg::LSTAGE + Cfg::A_BYTES;
+        const uint8_t* codes = smem + Cfg::CODE_OFF + cs * Cfg::CSTAGE;
         const __half* sc = reinterpret_cast<const __half*>(codes + Cfg::CODE_BYTES);
         uint8_t* sb = smem + Cfg::BRING_OFF + bs * Cfg::B_BYTES;
 #pragma unroll
@@ -297,9 +322,9 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(&b_local[bs]);    // this CTA's half of B stage bs is written
-          mbar_arrive(&ld_empty[ls]);   // staged codes consumed
+          mbar_arrive(&cd_empty[cs]);   // staged codes consumed
         }
-        if (++ls == LSTAGES) { ls = 0; lph ^= 1; }
+        if (++cs == Cfg::CSTAGES) { cs = 0; cph ^= 1; }
         if (++bs == Cfg::BSTAGES) { bs = 0; bph ^= 1; }
       }
     }
@@ -321,10 +346,10 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 // --------------------------------------------------------------------------
 // Host-side launch.
 
-using PairQ8_256 = PairCfg<256, 5, false, 4>;
-using PairQ8_128 = PairCfg<128, 6, false, 6>;
-using PairI8_256 = PairCfg<256, 6, true, 1>;
-using PairI8_128 = PairCfg<128, 8, true, 1>;
+using PairQ8_256 = PairCfg<256, 6, false, 6, 3>;
+using PairQ8_128 = PairCfg<128, 8, false, 8, 4>;
+using PairI8_256 = PairCfg<256, 6, true>;
+using PairI8_128 = PairCfg<128, 8, true>;
 
 template <class Cfg>
 static int launch_pair_cfg(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmS,
