@@ -540,6 +540,7 @@ def run_b200(args):
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     import burn_rocket_b200 as rb
     rb.init(local)
+    rb.set_tile_policy(args.tile_policy)
     W = WORKLOADS[args.workload]
     wl = W(dev, seed=0x5EED, world=world, rank=rank) if W.name in DP_WORKLOADS else W(dev, seed=0x5EED + rank)
     stream = torch.cuda.current_stream()
@@ -702,6 +703,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying a CUDA graph")
+    ap.add_argument("--tile-policy", default="auto", choices=["auto", "single", "pair"],
+                    help="GEMM tile policy (rb_set_tile_policy)")
     ap.add_argument("--gemm-shape", default=None,
                     help="q8gemm / w8a8: one M,N,K GEMM with f16 activations/outputs (profiling the model's shapes)")
     args = ap.parse_args()

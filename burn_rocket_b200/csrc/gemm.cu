@@ -350,17 +350,16 @@ int set_gemm_policy(int policy) { return g_policy.exchange(policy); }
 //   * W8A8: pair tiles run ~3% faster than single-CTA 128 x 256 tiles at
 //     K ~ 1k and ~13% faster at K ~ 4k (per SM they stage and read half the
 //     weight bytes; shared-memory bandwidth bounds the single-CTA tile);
-//   * Q8_0: 256 x 128 single-CTA tiles (two M halves sharing one dequantised
-//     B tile) beat pair tiles by ~35% at large M, and single-CTA tiles also
-//     win at small M (the pair's codes and A share one load ring, which
-//     caps how far the dequant warps can run ahead of the MMA).
+//   * Q8_0: pair tiles run ~40% faster than the best single-CTA tile (256 x
+//     128, two M halves sharing one dequantised B tile) at large M; at small
+//     M (a single round of tiles) the two are even.
 GemmPlan gemm_plan(bool i8, int M, int N, int K, int num_sms) {
   const int policy = g_policy.load();
   struct Shape { int bn, mh; bool pair; double eff; };
   const bool long_k = K > 2048;
   const Shape q8c[] = {{256, 1, false, 2.0}, {128, 1, false, 2.0}, {96, 1, false, 2.0},
-                       {64, 1, false, 2.0},  {128, 2, false, 1.5}, {256, 1, true, 2.2},
-                       {128, 1, true, 2.6}};
+                       {64, 1, false, 2.0},  {128, 2, false, 1.5}, {256, 1, true, 1.03},
+                       {128, 1, true, 1.2}};
   const Shape i8c[] = {{256, 1, false, long_k ? 1.13 : 1.04}, {128, 1, false, long_k ? 1.25 : 1.15},
                        {256, 1, true, 1.0}, {128, 1, true, 1.12}};
   const Shape* c = i8 ? i8c : q8c;

@@ -41,8 +41,12 @@ namespace rb {
 // ring of CSTAGES staged code/scale stages, refilled by its own producer warp
 // as soon as the dequant warps have read a stage (so dequantisation can run
 // ahead of the MMA by up to CSTAGES stages), and BSTAGES dequantised B stages.
-template <int BN_, int LSTAGES_, bool I8_, int CSTAGES_ = 1, int BSTAGES_ = 1>
+template <int BN_, int LSTAGES_, bool I8_, int CSTAGES_ = 1, int BSTAGES_ = 1, int DQ_WARPS_ = 8,
+          int DQ_GROUPS_ = 1>
 struct PairCfg {
+  static constexpr int DQ_WARPS = DQ_WARPS_;         // Q8_0 dequant warps
+  static constexpr int DQ_GROUPS = DQ_GROUPS_;       // stages dequantised concurrently
+  static_assert(DQ_WARPS % DQ_GROUPS == 0, "equal dequant groups");
   static constexpr int BN = BN_;                    // UMMA N of the pair tile
   static constexpr int HB = BN / 2;                 // weight rows staged per CTA
   static constexpr int LSTAGES = LSTAGES_;
@@ -73,7 +77,7 @@ struct PairCfg {
   static constexpr int SMEM_BYTES = BAR_OFF + 512 + 1024;
   // After the role warps: the peer's accumulator-release forwarder (idle in
   // the leader) and, for Q8_0, the codes producer.
-  static constexpr int FWD_WARP = Q8 ? (kDqWarp0 + kNumDqWarps) : kEpiWarp0 + EPI_WARPS;
+  static constexpr int FWD_WARP = Q8 ? (kDqWarp0 + DQ_WARPS) : kEpiWarp0 + EPI_WARPS;
   static constexpr int CP_WARP = FWD_WARP + 1;
   static constexpr int NUM_WARPS = Q8 ? CP_WARP + 1 : FWD_WARP + 1;
   static constexpr int THREADS = NUM_WARPS * 32;
@@ -127,12 +131,12 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     }
     for (int s = 0; s < Cfg::CSTAGES; ++s) {
       mbar_init(&cd_full[s], 1);
-      mbar_init(&cd_empty[s], kNumDqWarps);
+      mbar_init(&cd_empty[s], Cfg::DQ_WARPS / Cfg::DQ_GROUPS);
     }
     for (int i = 0; i < Cfg::BSTAGES; ++i) {
       mbar_init(&b_full[i], 1);
       mbar_init(&b_empty[i], 1);
-      mbar_init(&b_local[i], kNumDqWarps);
+      mbar_init(&b_local[i], Cfg::DQ_WARPS / Cfg::DQ_GROUPS);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
@@ -291,17 +295,25 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     }
   } else if (Cfg::Q8 && warp >= kDqWarp0) {
     // ------------------------------------------------------------ Q8_0 dequant (both CTAs)
-    // This CTA's HB weight rows: chunk (row, c) — 8 codes — is read from the
-    // staged codes at row*64 + c*8 and written as 8 f16 in the 128-byte
-    // swizzled K-major layout the UMMA descriptor reads.
+    // The dequant warps form DQ_GROUPS groups; group g dequantises stages
+    // q = g, g + DQ_GROUPS, ... of the (tile, k-block) sequence, so several
+    // stages are in flight at once and each stage's fixed wait / fence /
+    // arrive latency overlaps the others'. Within a stage, chunk (row, c) —
+    // 8 codes of one of this CTA's HB weight rows — is read from the staged
+    // codes at row*64 + c*8 and written as 8 f16 in the 128-byte swizzled
+    // K-major layout the UMMA descriptor reads.
+    constexpr int kGroupWarps = Cfg::DQ_WARPS / Cfg::DQ_GROUPS;
     constexpr int kChunks = HB * 8;
-    constexpr int kThreads = kNumDqWarps * 32;
+    constexpr int kThreads = kGroupWarps * 32;
     constexpr int kPer = (kChunks + kThreads - 1) / kThreads;
-    const int tid = threadIdx.x - kDqWarp0 * 32;
-    int cs = 0, bs = 0;
-    uint32_t cph = 0, bph = 0;
+    const int grp = (warp - kDqWarp0) / kGroupWarps;
+    const int tid = threadIdx.x - (kDqWarp0 + grp * kGroupWarps) * 32;
+    int q = 0;
     for (int t = pair; t < num_tiles; t += npairs) {
-      for (int kb = 0; kb < num_kb; ++kb) {
+      for (int kb = 0; kb < num_kb; ++kb, ++q) {
+        if (q % Cfg::DQ_GROUPS != grp) continue;
+        const int cs = q % Cfg::CSTAGES, bs = q % Cfg::BSTAGES;
+        const uint32_t cph = (q / Cfg::CSTAGES) & 1, bph = (q / Cfg::BSTAGES) & 1;
         if (!warp_wait(&cd_full[cs], cph, args.err, abort_flag)) goto dq_done;
         if (!warp_wait(&b_empty[bs], bph ^ 1, args.err, abort_flag)) goto dq_done;
         const uint8_t* codes = smem + Cfg::CODE_OFF + cs * Cfg::CSTAGE;
@@ -312,10 +324,10 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           const int i = tid + j * kThreads;
           if (kChunks % kThreads == 0 || i < kChunks) {
             const int rowi = i >> 3, c = i & 7;
-            const uint2 q = *reinterpret_cast<const uint2*>(codes + rowi * 64 + c * 8);
+            const uint2 qc = *reinterpret_cast<const uint2*>(codes + rowi * 64 + c * 8);
             const __half d = sc[(c >> 2) * HB + rowi];
             *reinterpret_cast<uint4*>(sb + rowi * 128 + ((c ^ (rowi & 7)) << 4)) =
-                q8_dequant8_f16(q, d);
+                q8_dequant8_f16(qc, d);
           }
         }
         fence_proxy_async_smem();
@@ -324,8 +336,6 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           mbar_arrive(&b_local[bs]);    // this CTA's half of B stage bs is written
           mbar_arrive(&cd_empty[cs]);   // staged codes consumed
         }
-        if (++cs == Cfg::CSTAGES) { cs = 0; cph ^= 1; }
-        if (++bs == Cfg::BSTAGES) { bs = 0; bph ^= 1; }
       }
     }
   dq_done:;
@@ -346,8 +356,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 // --------------------------------------------------------------------------
 // Host-side launch.
 
-using PairQ8_256 = PairCfg<256, 6, false, 6, 3>;
-using PairQ8_128 = PairCfg<128, 8, false, 8, 4>;
+using PairQ8_256 = PairCfg<256, 5, false, 5, 5, 12, 3>;
+using PairQ8_128 = PairCfg<128, 7, false, 8, 6, 12, 3>;
 using PairI8_256 = PairCfg<256, 6, true>;
 using PairI8_128 = PairCfg<128, 8, true>;
 
