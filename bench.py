@@ -55,10 +55,10 @@ def load_peaks():
 # Committed ncu summary of each workload's dominant kernel (profiles/).
 PROFILES = {
     "attn": "attn_kernel_gqa_s3633_ncu.md",
-    "q8gemm": "gemm_kernel_q8_0_ncu.md",
-    "w8a8": "gemm_kernel_w8a8_ncu.md",
-    "qwen3": "gemm_kernel_q8_0_ncu.md",
-    "siglip": "gemm_kernel_w8a8_ncu.md",
+    "q8gemm": "gemm_pair_kernel_q8_0_config1_ncu.md",
+    "w8a8": "gemm_pair_kernel_w8a8_8192x4304x1152_ncu.md",
+    "qwen3": "gemm_pair_kernel_q8_0_8192x6144x1024_ncu.md",
+    "siglip": "gemm_pair_kernel_w8a8_8192x4304x1152_ncu.md",
 }
 
 
