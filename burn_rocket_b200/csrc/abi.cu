@@ -951,6 +951,92 @@ int rb_mem_stats(int64_t* weights_bytes, int64_t* scratch_bytes, int64_t* num_we
   return RB_OK;
 }
 
+int64_t rb_moe_workspace_bytes(int64_t tokens, int top_k, int experts) {
+  if (tokens <= 0 || top_k <= 0 || experts <= 0) return fail(RB_E_SHAPE, "moe workspace: bad sizes");
+  return moe_layout(tokens, top_k, experts).words * 4;
+}
+
+int64_t rb_moe_max_rows(int64_t tokens, int top_k, int experts) {
+  if (tokens <= 0 || top_k <= 0 || experts <= 0) return fail(RB_E_SHAPE, "moe rows: bad sizes");
+  return moe_layout(tokens, top_k, experts).max_rows;
+}
+
+int rb_moe_route(const float* logits, int64_t tokens, int experts, int top_k, int normalize, int32_t* ids,
+                 float* weights, void* stream) {
+  if (!logits || !ids || !weights || tokens <= 0) return fail(RB_E_SHAPE, "moe_route: bad arguments");
+  const int rc = launch_moe_route(logits, tokens, experts, top_k, normalize, ids, weights,
+                                  reinterpret_cast<cudaStream_t>(stream));
+  g_launches++;
+  return rc == RB_OK ? RB_OK : fail(rc, "moe_route: %d experts, top-%d (supported: experts <= 256, k <= 32)",
+                                    experts, top_k);
+}
+
+int rb_moe_dispatch(const int32_t* ids, int64_t tokens, int top_k, int experts, const void* x_f16,
+                    int64_t hidden, void* workspace, void* x_perm_f16, void* stream) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Engine* e;
+  int rc = ensure_engine(&e);
+  if (rc) return rc;
+  if (!ids || !x_f16 || !workspace || !x_perm_f16 || tokens <= 0 || top_k <= 0)
+    return fail(RB_E_SHAPE, "moe_dispatch: bad arguments");
+  if ((reinterpret_cast<uintptr_t>(x_f16) | reinterpret_cast<uintptr_t>(x_perm_f16)) & 15)
+    return fail(RB_E_SHAPE, "moe_dispatch: rows must be 16-byte aligned");
+  rc = launch_moe_dispatch(ids, tokens, top_k, experts, x_f16, hidden, reinterpret_cast<int32_t*>(workspace),
+                           x_perm_f16, e->err, reinterpret_cast<cudaStream_t>(stream));
+  g_launches += 4;
+  return rc == RB_OK ? RB_OK : fail(rc, "moe_dispatch: experts %d (<= 1024), hidden %lld (multiple of 8)",
+                                    experts, (long long)hidden);
+}
+
+int rb_matmul_grouped(int64_t id, int experts, const void* x_perm_f16, int64_t max_rows, const void* workspace,
+                      int64_t tokens, int top_k, void* y, int y_dtype, void* stream) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Engine* e;
+  int rc = ensure_engine(&e);
+  if (rc) return rc;
+  auto it = e->weights.find(id);
+  if (it == e->weights.end()) return fail(RB_E_SHAPE, "weight id %lld is not packed", (long long)id);
+  const Weight& w = it->second;
+  if (w.kind != RB_WEIGHT_Q8_0) return fail(RB_E_UNSUPPORTED, "grouped matmul: Q8_0 weights only");
+  if (experts <= 0 || w.n % experts) return fail(RB_E_SHAPE, "grouped matmul: weight rows not a multiple of experts");
+  const MoeLayout ml = moe_layout(tokens, top_k, experts);
+  if (max_rows != ml.max_rows) return fail(RB_E_SHAPE, "grouped matmul: max_rows must be rb_moe_max_rows()");
+  if (!x_perm_f16 || !workspace || !y || (y_dtype != RB_DTYPE_F16 && y_dtype != RB_DTYPE_F32))
+    return fail(RB_E_SHAPE, "grouped matmul: bad arguments");
+  const int64_t n = w.n / experts;
+  GemmLaunch L{};
+  L.M = static_cast<int>(max_rows);
+  L.N = static_cast<int>(n);
+  L.K = static_cast<int>(w.k);
+  L.out = y;
+  L.ldo = static_cast<int>(n);
+  L.out_dtype = y_dtype;
+  L.err = e->err;
+  L.num_sms = e->num_sms;
+  L.tile_expert = reinterpret_cast<const int32_t*>(workspace) + ml.tile_expert;
+  // Grouped tiles are single-CTA with one 128-row M half (segments are 128-aligned).
+  const GemmPlan plan{n % 256 == 0 ? 256 : 128, 1, false};
+  CUtensorMap tmA, tmC;
+  if ((rc = make_tmap_2d(&tmA, x_perm_f16, 2, max_rows, w.k, w.k, 64, 128, 128)) != RB_OK) return rc;
+  const bool tstore = output_map(&tmC, y, y_dtype, max_rows, n);
+  const int bi = bn_index(plan.weight_rows());
+  if ((rc = launch_q8_gemm(L, plan, tmA, w.tm_codes[bi], w.tm_scales[bi], tstore ? &tmC : nullptr,
+                           reinterpret_cast<cudaStream_t>(stream))) != RB_OK)
+    return fail(rc, "grouped q8_0 gemm launch failed");
+  g_launches++;
+  return RB_OK;
+}
+
+int rb_moe_combine(float* x, const void* y_perm_f16, int64_t hidden, const int32_t* ids, const float* weights,
+                   const void* workspace, int64_t tokens, int top_k, int experts, void* stream) {
+  if (!x || !y_perm_f16 || !ids || !weights || !workspace || tokens <= 0)
+    return fail(RB_E_SHAPE, "moe_combine: bad arguments");
+  const int rc = launch_moe_combine(x, y_perm_f16, hidden, ids, weights, reinterpret_cast<const int32_t*>(workspace),
+                                    tokens, top_k, experts, reinterpret_cast<cudaStream_t>(stream));
+  g_launches++;
+  return rc == RB_OK ? RB_OK : fail(rc, "moe_combine: hidden must be a multiple of 8, top_k <= 32");
+}
+
 int rb_set_tile_policy(int policy) {
   if (policy < RB_TILES_AUTO || policy > RB_TILES_PAIR) return fail(RB_E_SHAPE, "unknown tile policy %d", policy);
   return set_gemm_policy(policy);

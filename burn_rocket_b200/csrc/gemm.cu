@@ -145,7 +145,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       uint32_t lph = 0;
       for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
         const int m0 = (t / tiles_n) * Cfg::BM;
-        const int n0 = (t % tiles_n) * BN;
+        int n0 = (t % tiles_n) * BN;
+        if (args.tile_expert) {  // grouped: this M tile's weight block starts at expert * N
+          const int e = __ldg(args.tile_expert + t / tiles_n);
+          if (e < 0) continue;
+          n0 += e * N;
+        }
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&load_empty[ls], lph ^ 1, args.err, abort_flag)) goto producer_done;
           uint8_t* st = smem + ls * Cfg::LSTAGE;
@@ -170,9 +175,11 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       int ls = 0, bs = 0;
       uint32_t lph = 0, bph = 0;
       int local = 0;
-      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+        if (args.tile_expert && __ldg(args.tile_expert + t / tiles_n) < 0) continue;
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
+        ++local;  // counts processed tiles only (accumulator ring phases)
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, args.err, abort_flag)) goto mma_done;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * Cfg::ACC_COLS;
@@ -219,10 +226,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     const int mode = epi_mode(Cfg::I8, args.out_dtype, args.out_scale);
     int buf = 0;
     int local = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      if (args.tile_expert && __ldg(args.tile_expert + t / tiles_n) < 0) continue;
       const int n0 = (t % tiles_n) * BN;
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
+      ++local;
       if (!warp_wait(&acc_full[acc], acc_phase, args.err, abort_flag)) break;
       tc_fence_after();
       for (int h = 0; h < Cfg::MH; ++h) {
@@ -250,6 +259,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     int ls = 0, bs = 0;
     uint32_t lph = 0, bph = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      if (args.tile_expert && __ldg(args.tile_expert + t / tiles_n) < 0) continue;
       for (int kb = 0; kb < num_kb; ++kb) {
         if (!warp_wait(&load_full[ls], lph, args.err, abort_flag)) goto dq_done;
         if (!warp_wait(&b_empty[bs], bph ^ 1, args.err, abort_flag)) goto dq_done;
@@ -390,6 +400,7 @@ static GemmArgs make_args(const GemmLaunch& L) {
   a.out_scale = L.out_scale;
   a.out_inv = L.out_scale != 0.0f ? 1.0f / L.out_scale : 0.0f;
   a.err = L.err;
+  a.tile_expert = L.tile_expert;
   return a;
 }
 

@@ -33,6 +33,9 @@ struct GemmArgs {
   float out_scale;     // W8A8: calibrated output grid (0 = unrounded)
   float out_inv;       // 1 / out_scale in f32
   int epi_path;        // kEpiPath*: how the epilogue writes the output tile
+  // Grouped GEMM (MoE experts): per 128-row M tile, the expert whose weight
+  // rows [e*N, (e+1)*N) it multiplies, or -1 to skip the tile; nullptr = plain.
+  const int* tile_expert;
   uint32_t* err;
 };
 

@@ -23,6 +23,7 @@ struct GemmLaunch {
   int ldo;
   int out_dtype;
   float out_scale;        // W8A8: 0 = unrounded output
+  const int* tile_expert; // grouped GEMM table (single-CTA 128-row tiles), or nullptr
   uint32_t* err;
   int num_sms;
 };
@@ -53,6 +54,20 @@ int launch_w8a8_gemm(const GemmLaunch& L, const GemmPlan& plan, const CUtensorMa
                      const CUtensorMap& tmB, const CUtensorMap* tmC, cudaStream_t stream);
 int launch_q8_dequant(const int8_t* codes, const void* scales, int N, int K, int pitch, void* out,
                       bool f16_out, cudaStream_t stream);
+
+// Mixture-of-experts routing / dispatch / combine (moe.cu). Workspace offsets
+// in int32 words.
+struct MoeLayout {
+  int64_t max_rows, max_tiles;
+  int64_t counts, seg_start, cursor, tile_expert, row_of_slot, token_of_row, words;
+};
+MoeLayout moe_layout(int64_t tokens, int top_k, int experts);
+int launch_moe_route(const float* logits, int64_t tokens, int experts, int top_k, int norm, int32_t* ids,
+                     float* wts, cudaStream_t st);
+int launch_moe_dispatch(const int32_t* ids, int64_t tokens, int top_k, int experts, const void* x, int64_t hidden,
+                        int32_t* ws, void* x_perm, uint32_t* err, cudaStream_t st);
+int launch_moe_combine(float* x, const void* y, int64_t hidden, const int32_t* ids, const float* wts,
+                       const int32_t* ws, int64_t tokens, int top_k, int experts, cudaStream_t st);
 
 // Elementwise / codec kernels (quant.cu).
 int launch_cast(const void* x, int x_dtype, void* y, int y_dtype, int64_t count,

@@ -1,0 +1,311 @@
+// moe.cu — mixture-of-experts routing, token dispatch and combine.
+//
+// The device form of the reference's MoE layer around the expert GEMMs
+// (`route`, src/clef/model.rs:462-489; `Buckets::build` / `combine`,
+// src/clef/engine.rs:284-340):
+//
+//   route     softmax over the E router logits of a token, top-k by
+//             probability (ties to the lower expert id), weights renormalised
+//             over the selected k (in selection order, f32);
+//   dispatch  per-expert row counts, 128-row-aligned expert segments in a
+//             permuted activation buffer, the M-tile -> expert table the
+//             grouped GEMM reads, and the gather of each routed token row;
+//   combine   x[t] += w_j * y[row_j] over the token's k experts in ascending
+//             expert id (f32, product then sum, as the reference).
+//
+// Rows inside an expert's segment are placed by atomics, so their order
+// varies between calls; every row's result is independent of its position
+// and the combine reads rows through the slot -> row map, so outputs do not.
+//
+// Workspace (int32 words, laid out by moe_layout):
+//   counts[E]  seg_start[E+1]  cursor[E]  tile_expert[max_tiles]
+//   row_of_slot[T*k]  token_of_row[max_rows]
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "kernels.h"
+#include "sm100.cuh"
+
+namespace rb {
+
+constexpr int kMoeSeg = 128;  // segment alignment = grouped-GEMM M tile
+
+MoeLayout moe_layout(int64_t tokens, int top_k, int experts) {
+  MoeLayout L{};
+  L.max_rows = ((tokens * top_k + static_cast<int64_t>(experts) * (kMoeSeg - 1)) + kMoeSeg - 1) / kMoeSeg *
+               kMoeSeg;
+  L.max_tiles = L.max_rows / kMoeSeg;
+  int64_t off = 0;
+  L.counts = off; off += experts;
+  L.seg_start = off; off += experts + 1;
+  L.cursor = off; off += experts;
+  L.tile_expert = off; off += L.max_tiles;
+  L.row_of_slot = off; off += tokens * top_k;
+  L.token_of_row = off; off += L.max_rows;
+  L.words = off;
+  return L;
+}
+
+// ---------------------------------------------------------------- route
+// One warp per token; lane l holds logits l, l+32, ... (EPL per lane).
+template <int EPL>
+__global__ void moe_route_kernel(const float* __restrict__ logits, int64_t tokens, int E, int k, int norm,
+                                 int32_t* __restrict__ ids, float* __restrict__ wts) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); t < tokens; t += nw) {
+    float p[EPL];
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      const int e = lane + 32 * i;
+      p[i] = e < E ? logits[t * E + e] : -INFINITY;
+      m = fmaxf(m, p[i]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      p[i] = (lane + 32 * i) < E ? expf(p[i] - m) : 0.0f;
+      s += p[i];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) p[i] = (lane + 32 * i) < E ? __fdiv_rn(p[i], s) : -1.0f;
+    // k rounds of a warp arg-max; ties go to the lower expert id.
+    float sel[32];
+    int sel_id[32];
+#pragma unroll
+    for (int r = 0; r < 32; ++r) {
+      if (r >= k) break;
+      float bv = -2.0f;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) {
+        const int e = lane + 32 * i;
+        if (p[i] > bv || (p[i] == bv && e < bi)) { bv = p[i]; bi = e; }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+      }
+      sel[r] = bv;
+      sel_id[r] = bi;
+#pragma unroll
+      for (int i = 0; i < EPL; ++i)
+        if (lane + 32 * i == bi) p[i] = -1.0f;
+    }
+    if (lane == 0) {
+      float sum = 0.0f;
+#pragma unroll
+      for (int r = 0; r < 32; ++r)
+        if (r < k) sum = __fadd_rn(sum, sel[r]);
+#pragma unroll
+      for (int r = 0; r < 32; ++r) {
+        if (r < k) {
+          ids[t * k + r] = sel_id[r];
+          wts[t * k + r] = norm ? __fdiv_rn(sel[r], sum) : sel[r];
+        }
+      }
+    }
+  }
+}
+
+int launch_moe_route(const float* logits, int64_t tokens, int experts, int top_k, int norm, int32_t* ids,
+                     float* wts, cudaStream_t st) {
+  if (experts < 1 || experts > 256 || top_k < 1 || top_k > 32 || top_k > experts) return RB_E_SHAPE;
+  int64_t g = (tokens + 7) / 8;
+  if (g > 148 * 16) g = 148 * 16;
+  if (g < 1) g = 1;
+  const int blocks = static_cast<int>(g);
+  if (experts <= 32) moe_route_kernel<1><<<blocks, 256, 0, st>>>(logits, tokens, experts, top_k, norm, ids, wts);
+  else if (experts <= 64) moe_route_kernel<2><<<blocks, 256, 0, st>>>(logits, tokens, experts, top_k, norm, ids, wts);
+  else if (experts <= 128) moe_route_kernel<4><<<blocks, 256, 0, st>>>(logits, tokens, experts, top_k, norm, ids, wts);
+  else moe_route_kernel<8><<<blocks, 256, 0, st>>>(logits, tokens, experts, top_k, norm, ids, wts);
+  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
+}
+
+// ---------------------------------------------------------------- dispatch
+__global__ void moe_count_kernel(const int32_t* __restrict__ ids, int64_t slots, int E, int32_t* counts,
+                                 uint32_t* err) {
+  for (int64_t s = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; s < slots;
+       s += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int e = ids[s];
+    if (e < 0 || e >= E) {
+      atomicOr(err, kErrBadShape);
+      continue;
+    }
+    atomicAdd(&counts[e], 1);
+  }
+}
+
+// One block: exclusive scan of the 128-aligned segment sizes, the segment
+// starts, the insertion cursors and the M-tile -> expert table.
+__global__ void moe_offsets_kernel(const int32_t* __restrict__ counts, int E, int64_t max_tiles,
+                                   int32_t* seg_start, int32_t* cursor, int32_t* tile_expert) {
+  __shared__ int32_t s_start[1025];
+  if (threadIdx.x == 0) {
+    int32_t acc = 0;
+    for (int e = 0; e < E; ++e) {
+      s_start[e] = acc;
+      acc += (counts[e] + kMoeSeg - 1) / kMoeSeg * kMoeSeg;
+    }
+    s_start[E] = acc;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e <= E; e += blockDim.x) {
+    seg_start[e] = s_start[e];
+    if (e < E) cursor[e] = s_start[e];
+  }
+  const int64_t used = s_start[E] / kMoeSeg;
+  for (int64_t mt = threadIdx.x; mt < max_tiles; mt += blockDim.x) {
+    int32_t ex = -1;
+    if (mt < used) {
+      // expert whose segment holds tile mt (binary search over the starts)
+      int lo = 0, hi = E - 1;
+      const int32_t row = static_cast<int32_t>(mt * kMoeSeg);
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (s_start[mid] <= row) lo = mid; else hi = mid - 1;
+      }
+      // skip empty segments that start at the same row
+      while (lo + 1 < E && s_start[lo + 1] <= row) ++lo;
+      ex = lo;
+    }
+    tile_expert[mt] = ex;
+  }
+}
+
+__global__ void moe_scatter_kernel(const int32_t* __restrict__ ids, int64_t slots, int k, int E, int32_t* cursor,
+                                   int32_t* row_of_slot, int32_t* token_of_row) {
+  for (int64_t s = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; s < slots;
+       s += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int e = ids[s];
+    if (e < 0 || e >= E) continue;
+    const int32_t row = atomicAdd(&cursor[e], 1);
+    row_of_slot[s] = row;
+    token_of_row[row] = static_cast<int32_t>(s / k);
+  }
+}
+
+// One warp per permuted row: copy the routed token's f16 row, or zeros for
+// the padding rows of a segment. Rows of unused tiles are left alone (the
+// grouped GEMM skips those tiles).
+__global__ void moe_gather_kernel(const __half* __restrict__ x, int64_t hidden, int64_t max_rows,
+                                  const int32_t* __restrict__ counts, const int32_t* __restrict__ seg_start,
+                                  const int32_t* __restrict__ tile_expert, const int32_t* __restrict__ token_of_row,
+                                  __half* __restrict__ xp) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int64_t v8 = hidden / 8;
+  for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); r < max_rows; r += nw) {
+    const int e = tile_expert[r / kMoeSeg];
+    if (e < 0) continue;
+    const bool real = (r - seg_start[e]) < counts[e];
+    uint4* dst = reinterpret_cast<uint4*>(xp + r * hidden);
+    if (real) {
+      const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(token_of_row[r]) * hidden);
+      for (int64_t i = lane; i < v8; i += 32) dst[i] = src[i];
+    } else {
+      for (int64_t i = lane; i < v8; i += 32) dst[i] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+}
+
+int launch_moe_dispatch(const int32_t* ids, int64_t tokens, int top_k, int experts, const void* x, int64_t hidden,
+                        int32_t* ws, void* x_perm, uint32_t* err, cudaStream_t st) {
+  if (experts < 1 || experts > 1024 || hidden % 8) return RB_E_SHAPE;
+  const MoeLayout L = moe_layout(tokens, top_k, experts);
+  const int64_t slots = tokens * top_k;
+  if (cudaMemsetAsync(ws + L.counts, 0, sizeof(int32_t) * experts, st) != cudaSuccess) return RB_E_DEVICE;
+  int64_t g = (slots + 255) / 256;
+  if (g > 148 * 8) g = 148 * 8;
+  if (g < 1) g = 1;
+  moe_count_kernel<<<static_cast<int>(g), 256, 0, st>>>(ids, slots, experts, ws + L.counts, err);
+  moe_offsets_kernel<<<1, 256, 0, st>>>(ws + L.counts, experts, L.max_tiles, ws + L.seg_start, ws + L.cursor,
+                                        ws + L.tile_expert);
+  moe_scatter_kernel<<<static_cast<int>(g), 256, 0, st>>>(ids, slots, top_k, experts, ws + L.cursor,
+                                                          ws + L.row_of_slot, ws + L.token_of_row);
+  int64_t gr = (L.max_rows + 7) / 8;
+  if (gr > 148 * 16) gr = 148 * 16;
+  moe_gather_kernel<<<static_cast<int>(gr), 256, 0, st>>>(
+      reinterpret_cast<const __half*>(x), hidden, L.max_rows, ws + L.counts, ws + L.seg_start, ws + L.tile_expert,
+      ws + L.token_of_row, reinterpret_cast<__half*>(x_perm));
+  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
+}
+
+// ---------------------------------------------------------------- combine
+// One warp per token: x[t] (f32, in place) += w_j * y[row_j] over the
+// token's k slots in ascending expert id; each lane owns 8-column groups.
+__global__ void moe_combine_kernel(float* __restrict__ x, const __half* __restrict__ y, int64_t hidden,
+                                   const int32_t* __restrict__ ids, const float* __restrict__ wts,
+                                   const int32_t* __restrict__ row_of_slot, int64_t tokens, int k) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); t < tokens; t += nw) {
+    // slot j of this token lives in lane j; rank = position in ascending expert order
+    int my_e = 0x7fffffff, my_row = 0;
+    float my_w = 0.0f;
+    if (lane < k) {
+      my_e = ids[t * k + lane];
+      my_w = wts[t * k + lane];
+      my_row = row_of_slot[t * k + lane];
+    }
+    int rank = 0;
+    for (int j = 0; j < k; ++j) {
+      const int ej = __shfl_sync(0xffffffffu, my_e, j);
+      if (ej < my_e || (ej == my_e && j < lane)) ++rank;
+    }
+    // order[r] = lane holding rank r
+    int ord_row[32];
+    float ord_w[32];
+#pragma unroll
+    for (int r = 0; r < 32; ++r) {
+      if (r >= k) break;
+      const unsigned hit = __ballot_sync(0xffffffffu, lane < k && rank == r);
+      const int src = __ffs(hit) - 1;
+      ord_row[r] = __shfl_sync(0xffffffffu, my_row, src);
+      ord_w[r] = __shfl_sync(0xffffffffu, my_w, src);
+    }
+    float* xr = x + t * hidden;
+    for (int64_t c = lane * 8; c < hidden; c += 256) {
+      float4 a0 = *reinterpret_cast<const float4*>(xr + c);
+      float4 a1 = *reinterpret_cast<const float4*>(xr + c + 4);
+      float acc[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+      for (int r = 0; r < 32; ++r) {
+        if (r >= k) break;
+        const uint4 u = *reinterpret_cast<const uint4*>(y + static_cast<int64_t>(ord_row[r]) * hidden + c);
+        const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __half22float2(h[q]);
+          acc[2 * q] = __fadd_rn(acc[2 * q], __fmul_rn(f.x, ord_w[r]));
+          acc[2 * q + 1] = __fadd_rn(acc[2 * q + 1], __fmul_rn(f.y, ord_w[r]));
+        }
+      }
+      *reinterpret_cast<float4*>(xr + c) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      *reinterpret_cast<float4*>(xr + c + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    }
+  }
+}
+
+int launch_moe_combine(float* x, const void* y, int64_t hidden, const int32_t* ids, const float* wts,
+                       const int32_t* ws, int64_t tokens, int top_k, int experts, cudaStream_t st) {
+  if (hidden % 8 || top_k > 32) return RB_E_SHAPE;
+  const MoeLayout L = moe_layout(tokens, top_k, experts);
+  int64_t g = (tokens + 7) / 8;
+  if (g > 148 * 16) g = 148 * 16;
+  if (g < 1) g = 1;
+  moe_combine_kernel<<<static_cast<int>(g), 256, 0, st>>>(x, reinterpret_cast<const __half*>(y), hidden, ids, wts,
+                                                          ws + L.row_of_slot, tokens, top_k);
+  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
+}
+
+}  // namespace rb

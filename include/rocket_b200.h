@@ -248,6 +248,35 @@ RB_API int rb_quantize_rows_i8(const void* x, int x_dtype, int64_t m, int64_t k,
  * ext.rs:1309-1334). */
 RB_API int rb_matmul_i8_acc(int64_t id, const int8_t* codes, int64_t m, int32_t* acc, void* stream);
 
+/* ---- mixture of experts (the Clef MoE layer around its expert GEMMs:
+ * route src/clef/model.rs:462-489, Buckets::build / combine
+ * src/clef/engine.rs:284-340; device-side, so a layer stays graph-capturable). */
+/* Workspace bytes and permuted-row capacity for `tokens` x top_k routed slots
+ * over `experts` (segments are 128-row aligned). */
+RB_API int64_t rb_moe_workspace_bytes(int64_t tokens, int top_k, int experts);
+RB_API int64_t rb_moe_max_rows(int64_t tokens, int top_k, int experts);
+/* f32 logits [tokens, experts] -> ids int32 [tokens, top_k] (descending
+ * probability, ties to the lower id) and weights f32 (renormalised over the
+ * selected experts when normalize != 0). experts <= 256, top_k <= 32. */
+RB_API int rb_moe_route(const float* logits, int64_t tokens, int experts, int top_k, int normalize,
+                        int32_t* ids, float* weights, void* stream);
+/* Buckets the routed slots per expert in `workspace` and gathers each slot's
+ * f16 token row x[tokens, hidden] into x_perm[rb_moe_max_rows(), hidden]
+ * (expert segments, padding rows zeroed). */
+RB_API int rb_moe_dispatch(const int32_t* ids, int64_t tokens, int top_k, int experts, const void* x_f16,
+                           int64_t hidden, void* workspace, void* x_perm_f16, void* stream);
+/* y_perm[r, :] = x_perm[r, :] · W_e^T for the expert e owning row r, where the
+ * Q8_0 weight `id` stacks the experts' [N, K] blocks (experts * N rows). Output
+ * f16 or f32 [max_rows, N]. */
+RB_API int rb_matmul_grouped(int64_t id, int experts, const void* x_perm_f16, int64_t max_rows,
+                             const void* workspace, int64_t tokens, int top_k, void* y, int y_dtype,
+                             void* stream);
+/* x[t, :] (f32, in place) += sum over the token's slots in ascending expert id
+ * of weight * y_perm[row of slot, :] (f16). */
+RB_API int rb_moe_combine(float* x, const void* y_perm_f16, int64_t hidden, const int32_t* ids,
+                          const float* weights, const void* workspace, int64_t tokens, int top_k, int experts,
+                          void* stream);
+
 /* ---- statistics (MemStats, lib.rs:44-96) */
 RB_API int rb_mem_stats(int64_t* weights_bytes, int64_t* scratch_bytes, int64_t* num_weights);
 

@@ -143,3 +143,51 @@ def layer_forward(x, wts: dict, cfg: dict, lens=None):
     ids, w, margins = route(logits, cfg["top_k"], cfg.get("norm_topk", True))
     y = experts_combine(hid, n2, ids, w, wts["experts"])
     return y, ids, w, margins
+
+
+# ---------------------------------------------------------------- the device model's reference
+def make_host_weights(cfg, seed: int) -> dict:
+    """Seeded synthetic weights (numpy f32) in the layout MoeModel(host_weights=) takes:
+    linears ~ N(0, 0.02), norm weights 1 + N(0, 0.1), embedding ~ N(0, 0.02)."""
+    rng = np.random.default_rng(seed)
+    h, d, nh, nkv, e, i = cfg.hidden, cfg.head_dim, cfg.heads, cfg.kv_heads, cfg.experts, cfg.inter
+
+    def randn(*shape):
+        return (rng.standard_normal(shape) * 0.02).astype(np.float32)
+
+    def norm_w(n):
+        return (1.0 + 0.1 * rng.standard_normal(n)).astype(np.float32)
+
+    layers = []
+    for _ in range(cfg.layers):
+        layers.append({"wq": randn(nh * d, h), "wk": randn(nkv * d, h), "wv": randn(nkv * d, h),
+                       "wo": randn(h, nh * d), "router": randn(e, h),
+                       "experts": [(randn(i, h), randn(i, h), randn(h, i)) for _ in range(e)],
+                       "in_norm": norm_w(h), "post_norm": norm_w(h), "q_norm": norm_w(d), "k_norm": norm_w(d)})
+    return {"layers": layers, "embed": randn(cfg.vocab, h), "final_norm": norm_w(h)}
+
+
+def forward(hw: dict, cfg, ids: np.ndarray, batch: int, seq: int):
+    """Final-normed hidden states [batch*seq, hidden] (f64) and per-layer
+    (ids, weights, margins), with every linear weight taken through the Q8_0
+    codec (oracle.q8_0_quantize / q8_0_dequant) and the embedding rounded to
+    f16, as the device model stores them."""
+    from . import oracle as orc
+
+    def deq(w):
+        codes, scales = orc.q8_0_quantize(np.asarray(w, np.float32))
+        return orc.q8_0_dequant(codes, scales).astype(np.float64)
+
+    c = {"heads": cfg.heads, "kv_heads": cfg.kv_heads, "head_dim": cfg.head_dim, "eps": cfg.eps,
+         "theta": cfg.theta, "top_k": cfg.top_k, "norm_topk": True}
+    emb = orc.f16_bits_to_f32(orc.f32_to_f16_bits(hw["embed"]))
+    x = emb[np.asarray(ids).reshape(-1)].astype(np.float64)
+    routing = []
+    for L in hw["layers"]:
+        w = {"in_norm": L["in_norm"], "post_norm": L["post_norm"], "q_norm": L["q_norm"], "k_norm": L["k_norm"],
+             "wq": deq(L["wq"]), "wk": deq(L["wk"]), "wv": deq(L["wv"]), "wo": deq(L["wo"]),
+             "router": deq(L["router"]),
+             "experts": [(deq(g), deq(u), deq(dn)) for g, u, dn in L["experts"]]}
+        x, rid, rw, mg = layer_forward(x, w, c, lens=[seq] * batch)
+        routing.append((rid, rw, mg))
+    return rms(x, hw["final_norm"], cfg.eps), routing
