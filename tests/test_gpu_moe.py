@@ -118,7 +118,9 @@ def test_moe_forward_matches_oracle(rb):
         dev_ids = model.routing[li][0].cpu().numpy()
         stable = margin > 1e-3
         assert stable.mean() > 0.7, (li, stable.mean())
-        assert np.array_equal(dev_ids[stable], rid[stable]), li
+        # the selected set (its order can swap between near-equal selected experts;
+        # the combine sums in ascending expert id either way)
+        assert np.array_equal(np.sort(dev_ids[stable], 1), np.sort(rid[stable], 1)), li
         stable_all &= stable
     assert cosine(got[stable_all], want[stable_all]) >= 0.999, cosine(got[stable_all], want[stable_all])
     for b in range(batch):
