@@ -515,8 +515,107 @@ class SiglipWorkload:
             "one layer: 4 W8A8 projections on 256 rows + attention of 2 of 16 heads over one image, x27 layers")
 
 
-WORKLOADS = {w.name: w for w in (AttnWorkload, Q8GemmWorkload, W8A8Workload, Qwen3Workload, SiglipWorkload)}
-DP_WORKLOADS = ("qwen3", "siglip")
+class MoeWorkload:
+    """Config #5: Qwen3-30B-A3B-style MoE prefill, 4 sequences x 2048 tokens,
+    48 layers, 128 experts top-8, causal. One GPU holds the whole model
+    (~31 GB of Q8_0 weights)."""
+    name = "moe"
+    metric = "Qwen3-30B-A3B-style MoE prefill tok/s (config #5: 4 seq x 2048 tok, 48 layers, 128 experts top-8)"
+    unit = "tok/s"
+    BATCH, SEQ = 4, 2048
+
+    def __init__(self, dev, seed, world=1, rank=0):
+        import torch
+        import burn_rocket_b200 as rb
+        from burn_rocket_b200.moe import MoeConfig, MoeModel
+        self.rb = rb
+        self.cfg = MoeConfig()
+        if world != 1:
+            raise SystemExit("--workload moe runs on one GPU (expert parallelism: --workload moe_ep)")
+        self.model = MoeModel(self.cfg, self.BATCH, self.SEQ, seed=0)
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        ids = torch.randint(0, self.cfg.vocab, (self.BATCH * self.SEQ,), generator=g, dtype=torch.int32)
+        self.model.ids_in.copy_(ids.to(dev))
+        self.hids = ids.pin_memory()
+        self.hout = torch.empty(self.BATCH * self.SEQ, self.cfg.hidden, dtype=torch.float16).pin_memory()
+        self.units = self.BATCH * self.SEQ
+        self.flops = self.cfg.flops_per_token(self.SEQ) * self.units
+
+    def step(self):
+        self.model.forward_device()
+
+    def e2e_step(self):
+        self.model.prefill_host(self.hids, self.hout)
+        return (self.hids.numel() * 4, self.hout.numel() * 2)
+
+    def kernel_roofline(self):
+        """Device time of one layer's grouped expert GEMMs (gate|up and down)."""
+        import torch
+        import burn_rocket_b200._lib as L
+        m, lay, lib = self.model, self.model.layers[0], L.load()
+        cfg = self.cfg
+        # routing of the current inputs for layer 0 is in the model's buffers after a forward
+        ops = 2.0 * self.units * cfg.top_k * 3 * cfg.hidden * cfg.inter
+
+        def run():
+            lib.rb_matmul_grouped(lay["gu"].id, cfg.experts, m.xp.data_ptr(), m.max_rows, m.ws.data_ptr(), m.T,
+                                  cfg.top_k, m.gup.data_ptr(), L.DTYPE_F16, None)
+            lib.rb_matmul_grouped(lay["down"].id, cfg.experts, m.actp.data_ptr(), m.max_rows, m.ws.data_ptr(), m.T,
+                                  cfg.top_k, m.yp.data_ptr(), L.DTYPE_F16, None)
+        for _ in range(2):
+            run()
+        reps = 5
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        torch.cuda.synchronize()
+        ev[0].record()
+        for _ in range(reps):
+            run()
+        ev[1].record()
+        torch.cuda.synchronize()
+        ms = ev[0].elapsed_time(ev[1]) / reps
+        return "grouped q8_0 gemm_kernel (experts gate|up + down of one layer)", ops / (ms / 1e3) / 1e12, ms
+
+    @staticmethod
+    def cpu_sample(orc, seed, timed_repeats=1):
+        """The reference CPU algorithm for the routed experts of one layer on a
+        256-token sample (dequantise + f32 GEMMs of the 8 selected experts per
+        token, grouped per expert), scaled to 48 layers; the dense part is
+        timed like Qwen3's (q/k/v/o projections + attention over 2048 tokens)."""
+        from burn_rocket_b200.moe import MoeConfig
+        cfg = MoeConfig()
+        rng = np.random.default_rng(seed)
+        T, h, i = 256, cfg.hidden, cfg.inter
+        per_expert = T * cfg.top_k // cfg.experts  # 16 rows per expert on average
+        gate = orc.q8_0_quantize((rng.standard_normal((2 * i, h)) * 0.02).astype(np.float32))
+        down = orc.q8_0_quantize((rng.standard_normal((h, i)) * 0.02).astype(np.float32))
+        xe = rng.standard_normal((per_expert, h)).astype(np.float32)
+        ae = rng.standard_normal((per_expert, i)).astype(np.float32)
+        t0 = time.perf_counter()
+        for _ in range(cfg.experts // 8):  # 16 of the 128 experts, scaled
+            orc.q8_0_matmul_cpu(xe, *gate)
+            orc.q8_0_matmul_cpu(ae, *down)
+        t_exp = (time.perf_counter() - t0) * 8 / T
+        shapes = [((cfg.heads + 2 * cfg.kv_heads) * cfg.head_dim, h), (h, cfg.heads * cfg.head_dim)]
+        ws = [orc.q8_0_quantize((rng.standard_normal(sh) * 0.02).astype(np.float32)) for sh in shapes]
+        xs = [rng.standard_normal((T, sh[1])).astype(np.float32) for sh in shapes]
+        q = rng.standard_normal((512, 2 * cfg.head_dim)).astype(np.float32)
+        kv = rng.standard_normal((512, cfg.head_dim)).astype(np.float32)
+        t0 = time.perf_counter()
+        for (codes, scales), x in zip(ws, xs):
+            orc.q8_0_matmul_cpu(x, codes, scales)
+        t_dense = (time.perf_counter() - t0) / T
+        t0 = time.perf_counter()
+        orc.attention_cpu(q, kv, kv, 2, 1, cfg.head_dim, 1 / math.sqrt(cfg.head_dim), True)
+        # 2 of 32 heads over 512 of 2048 tokens (causal work grows with S^2)
+        t_att = (time.perf_counter() - t0) * 16 * 16 / 2048
+        return 1.0 / ((t_exp + t_dense + t_att) * cfg.layers), (
+            "one layer: 16 of 128 experts on 16 rows each, q|k|v + o on 256 tokens, 2 of 32 heads of causal "
+            "attention over 512 tokens; scaled to 48 layers and 2048-token sequences")
+
+
+WORKLOADS = {w.name: w for w in (AttnWorkload, Q8GemmWorkload, W8A8Workload, Qwen3Workload, SiglipWorkload,
+                                 MoeWorkload)}
+DP_WORKLOADS = ("qwen3", "siglip", "moe")
 
 
 # ----------------------------------------------------------------------------- driver
@@ -631,15 +730,18 @@ def run_b200(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": True, "scaling": "strong" if wl.name in DP_WORKLOADS else "weak", "vs_baseline": None,
         "dtype": {"attn": "f16", "q8gemm": "f16xq8_0->f32", "w8a8": "s8", "qwen3": "f16xq8_0 (f32 residual)",
-                  "siglip": "s8 linears, f16 attention (f32 residual)"}[wl.name],
+                  "siglip": "s8 linears, f16 attention (f32 residual)",
+                  "moe": "f16xq8_0 (f32 residual, f32 router)"}[wl.name],
         "data": "synthetic (seeded, BASELINE.json shapes)",
         "config": {"workload": {"attn": "configs[1] GQA attention", "q8gemm": "configs[0] Q8_0 GEMM",
                                 "w8a8": "configs[3] W8A8 projections",
                                 "qwen3": "configs[2] Qwen3-Embedding-0.6B arch, 28 layers, 64x512 tokens",
-                                "siglip": "configs[3] SigLIP-style W8A8 tower, 27 layers, 16x2394 patches"}[wl.name],
+                                "siglip": "configs[3] SigLIP-style W8A8 tower, 27 layers, 16x2394 patches",
+                                "moe": "configs[4] Qwen3-30B-A3B-style MoE, 48 layers, 4x2048 tokens"}[wl.name],
                    "l2": "flushed between timed steps (256 MiB write)",
                    "parallelism": (f"dp{world} over sequences" if wl.name == "qwen3"
                                    else f"dp{world} over images" if wl.name == "siglip"
+                                   else "single GPU, all 128 experts resident" if wl.name == "moe"
                                    else (f"replicas x{world}" if world > 1 else "single GPU"))},
         "roofline": {"bound": "tensor", "kernel": kname, "achieved": round(achieved, 2), "peak": peak,
                      "unit": "TOP/s" if wl.name in ("w8a8", "siglip") else "TFLOP/s",
@@ -711,7 +813,7 @@ def main():
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.steps is None:
-        args.steps = {"attn": 200, "q8gemm": 2000, "w8a8": 60, "qwen3": 10, "siglip": 5}.get(args.workload, 20)
+        args.steps = {"attn": 200, "q8gemm": 2000, "w8a8": 60, "qwen3": 10, "siglip": 5, "moe": 3}.get(args.workload, 20)
     if args.gemm_shape:
         m, n, k = (int(v) for v in args.gemm_shape.split(","))
         if args.workload == "w8a8":
