@@ -89,10 +89,14 @@ SIGNATURES = {
     "rb_set_tile_policy": (_i, [_i]),
     "rb_moe_workspace_bytes": (_i64, [_i64, _i, _i]),
     "rb_moe_max_rows": (_i64, [_i64, _i, _i]),
+    "rb_moe_slot_rows_offset": (_i64, [_i64, _i, _i]),
     "rb_moe_route": (_i, [_p, _i64, _i, _i, _i, _p, _p, _p]),
     "rb_moe_dispatch": (_i, [_p, _i64, _i, _i, _p, _i64, _p, _p, _p]),
     "rb_matmul_grouped": (_i, [_i64, _i, _p, _i64, _p, _i64, _i, _p, _i, _p]),
     "rb_moe_combine": (_i, [_p, _p, _i64, _p, _p, _p, _i64, _i, _i, _p]),
+    "rb_ep_build_send": (_i, [_p, _i64, _i, _i, _i, _p, _i64, _p, _p, _p, _p, _p, _p]),
+    "rb_gather_rows": (_i, [_p, _p, _i64, _i64, _p, _p]),
+    "rb_moe_combine_rows": (_i, [_p, _p, _i64, _p, _p, _p, _i64, _i, _p]),
 }
 
 _lib = None

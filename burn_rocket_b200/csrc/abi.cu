@@ -961,6 +961,11 @@ int64_t rb_moe_max_rows(int64_t tokens, int top_k, int experts) {
   return moe_layout(tokens, top_k, experts).max_rows;
 }
 
+int64_t rb_moe_slot_rows_offset(int64_t tokens, int top_k, int experts) {
+  if (tokens <= 0 || top_k <= 0 || experts <= 0) return fail(RB_E_SHAPE, "moe layout: bad sizes");
+  return moe_layout(tokens, top_k, experts).row_of_slot;
+}
+
 int rb_moe_route(const float* logits, int64_t tokens, int experts, int top_k, int normalize, int32_t* ids,
                  float* weights, void* stream) {
   if (!logits || !ids || !weights || tokens <= 0) return fail(RB_E_SHAPE, "moe_route: bad arguments");
@@ -1035,6 +1040,39 @@ int rb_moe_combine(float* x, const void* y_perm_f16, int64_t hidden, const int32
                                     tokens, top_k, experts, reinterpret_cast<cudaStream_t>(stream));
   g_launches++;
   return rc == RB_OK ? RB_OK : fail(rc, "moe_combine: hidden must be a multiple of 8, top_k <= 32");
+}
+
+int rb_ep_build_send(const int32_t* ids, int64_t tokens, int top_k, int experts, int ranks, const void* x_f16,
+                     int64_t hidden, int32_t* dest_counts, int32_t* dest_cursor, int32_t* send_meta,
+                     int32_t* slot_pos, void* send_rows_f16, void* stream) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Engine* e;
+  int rc = ensure_engine(&e);
+  if (rc) return rc;
+  if (!ids || !x_f16 || !dest_counts || !dest_cursor || !send_meta || !slot_pos || !send_rows_f16 || tokens <= 0)
+    return fail(RB_E_SHAPE, "ep_build_send: bad arguments");
+  rc = launch_ep_build_send(ids, tokens, top_k, experts, ranks, x_f16, hidden, dest_counts, dest_cursor, send_meta,
+                            slot_pos, send_rows_f16, e->err, reinterpret_cast<cudaStream_t>(stream));
+  g_launches += 4;
+  return rc == RB_OK ? RB_OK : fail(rc, "ep_build_send: experts must divide over ranks, hidden % 8 == 0");
+}
+
+int rb_gather_rows(const void* in_f16, const int32_t* idx, int64_t n, int64_t hidden, void* out_f16, void* stream) {
+  if (!in_f16 || !idx || !out_f16 || n < 0) return fail(RB_E_SHAPE, "gather_rows: bad arguments");
+  if (n == 0) return RB_OK;
+  const int rc = launch_gather_rows(in_f16, idx, n, hidden, out_f16, reinterpret_cast<cudaStream_t>(stream));
+  g_launches++;
+  return rc == RB_OK ? RB_OK : fail(rc, "gather_rows: hidden % 8 == 0");
+}
+
+int rb_moe_combine_rows(float* x, const void* y_f16, int64_t hidden, const int32_t* ids, const float* weights,
+                        const int32_t* row_of_slot, int64_t tokens, int top_k, void* stream) {
+  if (!x || !y_f16 || !ids || !weights || !row_of_slot || tokens <= 0)
+    return fail(RB_E_SHAPE, "moe_combine_rows: bad arguments");
+  const int rc = launch_moe_combine_rows(x, y_f16, hidden, ids, weights, row_of_slot, tokens, top_k,
+                                         reinterpret_cast<cudaStream_t>(stream));
+  g_launches++;
+  return rc == RB_OK ? RB_OK : fail(rc, "moe_combine_rows: hidden % 8 == 0, top_k <= 32");
 }
 
 int rb_set_tile_policy(int policy) {

@@ -69,6 +69,13 @@ int launch_moe_dispatch(const int32_t* ids, int64_t tokens, int top_k, int exper
 int launch_moe_combine(float* x, const void* y, int64_t hidden, const int32_t* ids, const float* wts,
                        const int32_t* ws, int64_t tokens, int top_k, int experts, cudaStream_t st);
 
+int launch_ep_build_send(const int32_t* ids, int64_t tokens, int top_k, int experts, int ranks, const void* x,
+                         int64_t hidden, int32_t* dest_counts, int32_t* dest_cursor, int32_t* send_meta,
+                         int32_t* slot_pos, void* send_rows, uint32_t* err, cudaStream_t st);
+int launch_gather_rows(const void* in, const int32_t* idx, int64_t n, int64_t hidden, void* out, cudaStream_t st);
+int launch_moe_combine_rows(float* x, const void* y, int64_t hidden, const int32_t* ids, const float* wts,
+                            const int32_t* row_of_slot, int64_t tokens, int top_k, cudaStream_t st);
+
 // Elementwise / codec kernels (quant.cu).
 int launch_cast(const void* x, int x_dtype, void* y, int y_dtype, int64_t count,
                 cudaStream_t stream);

@@ -308,4 +308,105 @@ int launch_moe_combine(float* x, const void* y, int64_t hidden, const int32_t* i
   return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
 }
 
+// ---------------------------------------------------------------- expert parallelism
+// Send-side bookkeeping for an all-to-all token exchange: the destination of
+// slot (t, j) is the rank owning expert ids[t, j] (experts_per_rank
+// consecutive ids per rank). Slots are grouped by destination in the send
+// buffer; for each: the token's f16 row, the expert id local to the
+// destination, and (kept here) the send position of every slot for the
+// combine after the outputs come back.
+__global__ void ep_count_kernel(const int32_t* __restrict__ ids, int64_t slots, int per_rank, int ranks,
+                                int32_t* dest_counts, uint32_t* err) {
+  for (int64_t s = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; s < slots;
+       s += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int q = ids[s] / per_rank;
+    if (ids[s] < 0 || q >= ranks) {
+      atomicOr(err, kErrBadShape);
+      continue;
+    }
+    atomicAdd(&dest_counts[q], 1);
+  }
+}
+
+__global__ void ep_offsets_kernel(const int32_t* __restrict__ dest_counts, int ranks, int32_t* dest_cursor) {
+  if (threadIdx.x == 0) {
+    int32_t acc = 0;
+    for (int q = 0; q < ranks; ++q) {
+      dest_cursor[q] = acc;
+      acc += dest_counts[q];
+    }
+  }
+}
+
+__global__ void ep_scatter_kernel(const int32_t* __restrict__ ids, int64_t slots, int k, int per_rank,
+                                  int32_t* dest_cursor, int32_t* send_meta, int32_t* slot_pos) {
+  for (int64_t s = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; s < slots;
+       s += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int e = ids[s];
+    const int q = e / per_rank;
+    const int32_t pos = atomicAdd(&dest_cursor[q], 1);
+    send_meta[pos] = e - q * per_rank;
+    slot_pos[s] = pos;
+  }
+}
+
+// rows_out[i] = rows_in[idx[i] / div] (f16 rows, one warp per output row).
+__global__ void gather_rows_kernel(const __half* __restrict__ in, const int32_t* __restrict__ idx, int div,
+                                   int64_t n, int64_t hidden, __half* __restrict__ out, int inverse) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  const int64_t v8 = hidden / 8;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); i < n; i += nw) {
+    // forward: out[idx[i]] = in[i / div] (scatter by slot position);
+    // inverse: out[i] = in[idx[i]] (gather).
+    const int64_t src = inverse ? idx[i] : i / div;
+    const int64_t dst = inverse ? i : idx[i];
+    const uint4* a = reinterpret_cast<const uint4*>(in + src * hidden);
+    uint4* b = reinterpret_cast<uint4*>(out + dst * hidden);
+    for (int64_t c = lane; c < v8; c += 32) b[c] = a[c];
+  }
+}
+
+int launch_ep_build_send(const int32_t* ids, int64_t tokens, int top_k, int experts, int ranks, const void* x,
+                         int64_t hidden, int32_t* dest_counts, int32_t* dest_cursor, int32_t* send_meta,
+                         int32_t* slot_pos, void* send_rows, uint32_t* err, cudaStream_t st) {
+  if (ranks < 1 || experts % ranks || hidden % 8) return RB_E_SHAPE;
+  const int per_rank = experts / ranks;
+  const int64_t slots = tokens * top_k;
+  if (cudaMemsetAsync(dest_counts, 0, sizeof(int32_t) * ranks, st) != cudaSuccess) return RB_E_DEVICE;
+  int64_t g = (slots + 255) / 256;
+  if (g > 148 * 8) g = 148 * 8;
+  if (g < 1) g = 1;
+  ep_count_kernel<<<static_cast<int>(g), 256, 0, st>>>(ids, slots, per_rank, ranks, dest_counts, err);
+  ep_offsets_kernel<<<1, 32, 0, st>>>(dest_counts, ranks, dest_cursor);
+  ep_scatter_kernel<<<static_cast<int>(g), 256, 0, st>>>(ids, slots, top_k, per_rank, dest_cursor, send_meta,
+                                                         slot_pos);
+  int64_t gr = (slots + 7) / 8;
+  if (gr > 148 * 16) gr = 148 * 16;
+  gather_rows_kernel<<<static_cast<int>(gr), 256, 0, st>>>(reinterpret_cast<const __half*>(x), slot_pos, top_k,
+                                                           slots, hidden, reinterpret_cast<__half*>(send_rows), 0);
+  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
+}
+
+int launch_gather_rows(const void* in, const int32_t* idx, int64_t n, int64_t hidden, void* out, cudaStream_t st) {
+  if (hidden % 8) return RB_E_SHAPE;
+  int64_t g = (n + 7) / 8;
+  if (g > 148 * 16) g = 148 * 16;
+  if (g < 1) g = 1;
+  gather_rows_kernel<<<static_cast<int>(g), 256, 0, st>>>(reinterpret_cast<const __half*>(in), idx, 1, n, hidden,
+                                                          reinterpret_cast<__half*>(out), 1);
+  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
+}
+
+int launch_moe_combine_rows(float* x, const void* y, int64_t hidden, const int32_t* ids, const float* wts,
+                            const int32_t* row_of_slot, int64_t tokens, int top_k, cudaStream_t st) {
+  if (hidden % 8 || top_k > 32) return RB_E_SHAPE;
+  int64_t g = (tokens + 7) / 8;
+  if (g > 148 * 16) g = 148 * 16;
+  if (g < 1) g = 1;
+  moe_combine_kernel<<<static_cast<int>(g), 256, 0, st>>>(x, reinterpret_cast<const __half*>(y), hidden, ids, wts,
+                                                          row_of_slot, tokens, top_k);
+  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
+}
+
 }  // namespace rb

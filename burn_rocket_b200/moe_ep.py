@@ -1,0 +1,262 @@
+"""Expert-parallel form of the MoE decoder (BASELINE config #5 on 2/4/8 GPUs).
+
+One process per GPU. The 128 experts are split into `world` consecutive
+blocks (rank r owns experts [r*E/world, (r+1)*E/world)); the dense part
+(attention, router) runs on the rank that owns the token:
+
+  * world <= batch: rank r owns whole sequences (data parallel);
+  * world == 2 * batch: rank r owns half a sequence. The second half's
+    attention needs the first half's K/V, so each pair of ranks all-gathers
+    its k|v columns and the second half runs a causal block mask with query
+    offset seq/2 (`attention_causal_block`).
+
+Per layer the routed slots travel to their experts' ranks and back with two
+NCCL all-to-alls of f16 token rows (plus one of the local expert ids and one
+of the per-destination counts, read on the host to size the exchange):
+
+    route -> rb_ep_build_send -> all_to_all(counts) -> all_to_all(rows, meta)
+      -> local grouped expert GEMMs -> all_to_all(outputs back)
+      -> rb_moe_combine_rows (ascending expert id per token, as
+         src/clef/engine.rs:317-340)
+
+The reference runs every expert on one board (experts streamed from NVMe,
+src/clef/engine.rs:7-19); expert parallelism is new here.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+
+import numpy as np
+
+from . import _lib
+from . import _check, _dev_ptr, WeightId, matmul
+from ._lib import DTYPE_F16, MASK_CAUSAL, MASK_CAUSAL_BLOCK
+from .moe import MoeConfig
+from .qwen3 import rope_tables
+
+
+def ep_plan(world: int, batch: int, seq: int):
+    """Per rank: (sequence index, first row within the sequence, rows) of the
+    token block it owns, as a list of blocks."""
+    if world <= batch:
+        if batch % world:
+            raise ValueError(f"world {world} must divide the batch of {batch} sequences")
+        per = batch // world
+        return [[(r * per + i, 0, seq) for i in range(per)] for r in range(world)]
+    if world == 2 * batch and seq % 2 == 0:
+        return [[(r // 2, (r % 2) * (seq // 2), seq // 2)] for r in range(world)]
+    raise ValueError(f"world {world} must divide the batch ({batch}) or be twice it")
+
+
+def exchange(out, inp, out_splits, in_splits, group=None):
+    """all_to_all_single with uneven splits along dim 0 (NCCL for CUDA
+    tensors, gloo for CPU tensors)."""
+    import torch.distributed as dist
+    dist.all_to_all_single(out, inp, list(map(int, out_splits)), list(map(int, in_splits)), group=group)
+    return out
+
+
+# ---------------------------------------------------------------- host restatement (tests)
+def build_send_np(ids: np.ndarray, experts: int, ranks: int):
+    """numpy restatement of rb_ep_build_send with a stable (slot-order) layout:
+    counts [ranks], meta [slots] (expert id local to the destination),
+    slot_pos [slots] (send position of every slot)."""
+    per = experts // ranks
+    flat = ids.reshape(-1)
+    dest = flat // per
+    counts = np.bincount(dest, minlength=ranks).astype(np.int64)
+    order = np.argsort(dest, kind="stable")
+    slot_pos = np.empty_like(order)
+    slot_pos[order] = np.arange(order.size)
+    meta = (flat - dest * per)[order]
+    return counts, meta, slot_pos
+
+
+class MoeEPModel:
+    """Expert-parallel MoE decoder: this rank's token blocks, all dense
+    weights, and its own block of experts (Q8_0)."""
+
+    def __init__(self, cfg: MoeConfig, batch: int, seq: int, rank: int, world: int, seed: int = 0,
+                 host_weights: dict | None = None, group=None, pair_groups=None):
+        import torch
+        self.cfg, self.batch, self.seq, self.rank, self.world = cfg, batch, seq, rank, world
+        self.group = group
+        self.blocks = ep_plan(world, batch, seq)[rank]
+        self.split = world > batch  # half sequences
+        self.pair_group = pair_groups[rank // 2] if self.split else None
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.dev = dev
+        self.T = sum(b[2] for b in self.blocks)
+        T = self.T
+        lib = _lib.load()
+        E, I, h, d, nh, nkv, k = cfg.experts, cfg.inter, cfg.hidden, cfg.head_dim, cfg.heads, cfg.kv_heads, cfg.top_k
+        if E % world:
+            raise ValueError("experts must divide over the ranks")
+        self.epr = E // world
+        e0 = rank * self.epr
+        g_dense = torch.Generator(device=dev).manual_seed(seed)
+        g_exp = torch.Generator(device=dev).manual_seed(seed * 1000 + 7 + rank)
+
+        def randn(gen, *shape):
+            return torch.randn(*shape, generator=gen, device=dev, dtype=torch.float32).mul_(0.02)
+
+        def pack_dev(parts):
+            parts = [p.float().contiguous() for p in parts]
+            ptrs = (C.c_void_p * len(parts))(*[p.data_ptr() for p in parts])
+            ns = (C.c_int64 * len(parts))(*[p.shape[0] for p in parts])
+            wid = lib.rb_pack_f32_q8_0_device(ptrs, ns, len(parts), parts[0].shape[1])
+            _check(wid, "rocket_pack", 0, parts[0].shape[1], sum(p.shape[0] for p in parts))
+            return WeightId(int(wid))
+
+        self.layers = []
+        for li in range(cfg.layers):
+            if host_weights is not None:
+                W = host_weights["layers"][li]
+                t = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dev)
+                layer = {"qkv": pack_dev([t(W["wq"]), t(W["wk"]), t(W["wv"])]), "o": pack_dev([t(W["wo"])]),
+                         "router": pack_dev([t(W["router"])]),
+                         "gu": pack_dev([t(m) for gate, up, _ in W["experts"][e0:e0 + self.epr] for m in (gate, up)]),
+                         "down": pack_dev([t(dn) for _, _, dn in W["experts"][e0:e0 + self.epr]])}
+                layer.update({kk: t(W[kk]) for kk in ("in_norm", "post_norm", "q_norm", "k_norm")})
+            else:
+                layer = {"qkv": pack_dev([randn(g_dense, nh * d, h), randn(g_dense, nkv * d, h),
+                                          randn(g_dense, nkv * d, h)]),
+                         "o": pack_dev([randn(g_dense, h, nh * d)]), "router": pack_dev([randn(g_dense, E, h)])}
+                big = randn(g_exp, self.epr * 2 * I, h)
+                layer["gu"] = pack_dev([big])
+                del big
+                big = randn(g_exp, self.epr * h, I)
+                layer["down"] = pack_dev([big])
+                del big
+                ones = lambda n: torch.ones(n, device=dev)
+                layer.update({"in_norm": ones(h), "post_norm": ones(h), "q_norm": ones(d), "k_norm": ones(d)})
+            self.layers.append(layer)
+        if host_weights is not None:
+            self.final_norm = torch.from_numpy(host_weights["final_norm"]).to(dev).float()
+            self.embed = torch.from_numpy(host_weights["embed"]).to(dev).half().contiguous()
+        else:
+            self.final_norm = torch.ones(h, device=dev)
+            self.embed = (torch.randn(cfg.vocab, h, generator=g_dense, device=dev) * 0.02).half().contiguous()
+        cos, sin = rope_tables(seq, d, cfg.theta)
+        self.cos = torch.from_numpy(cos).to(dev)
+        self.sin = torch.from_numpy(sin).to(dev)
+        torch.cuda.synchronize()
+        f16 = torch.float16
+        S = T * k                      # slots sent by this rank
+        R = batch * seq * k            # upper bound on rows received
+        self.R_cap = R
+        self.ids_in = torch.zeros(T, dtype=torch.int32, device=dev)
+        self.x = torch.empty(T, h, dtype=torch.float32, device=dev)
+        self.h = torch.empty(T, h, dtype=f16, device=dev)
+        self.qkv = torch.empty(T, (nh + 2 * nkv) * d, dtype=f16, device=dev)
+        self.kv_full = torch.empty(2 * T, 2 * nkv * d, dtype=f16, device=dev) if self.split else None
+        self.attn = torch.empty(T, nh * d, dtype=f16, device=dev)
+        self.o = torch.empty(T, h, dtype=f16, device=dev)
+        self.logits = torch.empty(T, E, dtype=torch.float32, device=dev)
+        self.ids = torch.empty(T, k, dtype=torch.int32, device=dev)
+        self.wts = torch.empty(T, k, dtype=torch.float32, device=dev)
+        self.dest_counts = torch.empty(world, dtype=torch.int32, device=dev)
+        self.recv_counts = torch.empty(world, dtype=torch.int32, device=dev)
+        self.dest_cursor = torch.empty(world, dtype=torch.int32, device=dev)
+        self.send_meta = torch.empty(S, dtype=torch.int32, device=dev)
+        self.slot_pos = torch.empty(S, dtype=torch.int32, device=dev)
+        self.send_rows = torch.empty(S, h, dtype=f16, device=dev)
+        self.recv_meta = torch.empty(R, dtype=torch.int32, device=dev)
+        self.recv_rows = torch.empty(R, h, dtype=f16, device=dev)
+        self.y_recv = torch.empty(R, h, dtype=f16, device=dev)
+        self.y_back = torch.empty(S, h, dtype=f16, device=dev)
+        self.max_rows = int(lib.rb_moe_max_rows(R, 1, self.epr))
+        self.ws = torch.empty(int(lib.rb_moe_workspace_bytes(R, 1, self.epr)) // 4 + 1, dtype=torch.int32,
+                              device=dev)
+        self.xp = torch.empty(self.max_rows, h, dtype=f16, device=dev)
+        self.gup = torch.empty(self.max_rows, 2 * I, dtype=f16, device=dev)
+        self.actp = torch.empty(self.max_rows, I, dtype=f16, device=dev)
+        self.yp = torch.empty(self.max_rows, h, dtype=f16, device=dev)
+        self.out = torch.empty(T, h, dtype=f16, device=dev)
+        self.exchanged_rows = 0
+
+    def _attention(self, L, lib, qkv_p, ld):
+        cfg, d, nh, nkv = self.cfg, self.cfg.head_dim, self.cfg.heads, self.cfg.kv_heads
+        scale = 1.0 / math.sqrt(d)
+        if not self.split:
+            b = len(self.blocks)
+            _check(lib.rb_attention_batched(qkv_p, ld, qkv_p + nh * d * 2, ld, qkv_p + (nh + nkv) * d * 2, ld,
+                                            _dev_ptr(self.attn), nh * d, DTYPE_F16, b, self.seq, self.seq,
+                                            nh, nkv, d, scale, 0.0, MASK_CAUSAL, -1, 0, 0, None),
+                   "rocket_flash_attn", self.seq, self.seq, d)
+            return
+        import torch.distributed as dist
+        half = self.seq // 2
+        # all-gather the pair's k|v column blocks: rows [0, half) then [half, seq)
+        kv_mine = self.qkv[:, nh * d:].contiguous()
+        dist.all_gather_into_tensor(self.kv_full, kv_mine, group=self.pair_group)
+        kvp = _dev_ptr(self.kv_full)
+        ldkv = 2 * nkv * d
+        q_start = self.blocks[0][1]
+        n_kv = q_start + half
+        _check(lib.rb_attention_batched(qkv_p, ld, kvp, ldkv, kvp + nkv * d * 2, ldkv, _dev_ptr(self.attn), nh * d,
+                                        DTYPE_F16, 1, half, n_kv, nh, nkv, d, scale, 0.0, MASK_CAUSAL_BLOCK, -1,
+                                        q_start, 0, None),
+               "rocket_flash_attn", half, n_kv, d)
+
+    def forward_device(self):
+        """One forward over self.ids_in (this rank's tokens) into self.out."""
+        import torch
+        cfg, lib, T = self.cfg, _lib.load(), self.T
+        h, d, nh, nkv, E, I, k = cfg.hidden, cfg.head_dim, cfg.heads, cfg.kv_heads, cfg.experts, cfg.inter, cfg.top_k
+        W = self.world
+        ld = (nh + 2 * nkv) * d
+        qkv_p, xp = _dev_ptr(self.qkv), _dev_ptr(self.x)
+        # rope positions of this rank's first row (tables offset by the row within the sequence)
+        pos0 = self.blocks[0][1]
+        cos_p = _dev_ptr(self.cos) + pos0 * (d // 2) * 4
+        sin_p = _dev_ptr(self.sin) + pos0 * (d // 2) * 4
+        rope_seq = self.blocks[0][2]
+        _check(lib.rb_embed_gather(_dev_ptr(self.ids_in), T, _dev_ptr(self.embed), cfg.vocab, h, xp, None),
+               "embed_gather")
+        self.exchanged_rows = 0
+        for L in self.layers:
+            _check(lib.rb_add_rms_norm(xp, None, _dev_ptr(L["in_norm"]), cfg.eps, _dev_ptr(self.h), T, h, None),
+                   "add_rms_norm")
+            matmul(self.h, L["qkv"], out=self.qkv)
+            _check(lib.rb_qk_norm_rope(qkv_p, ld, T, nh, nkv, d, _dev_ptr(L["q_norm"]), _dev_ptr(L["k_norm"]),
+                                       cfg.eps, cos_p, sin_p, rope_seq, None), "qk_norm_rope")
+            self._attention(L, lib, qkv_p, ld)
+            matmul(self.attn, L["o"], out=self.o)
+            _check(lib.rb_add_rms_norm(xp, _dev_ptr(self.o), _dev_ptr(L["post_norm"]), cfg.eps, _dev_ptr(self.h),
+                                       T, h, None), "add_rms_norm")
+            matmul(self.h, L["router"], out=self.logits)
+            _check(lib.rb_moe_route(_dev_ptr(self.logits), T, E, k, 1, _dev_ptr(self.ids), _dev_ptr(self.wts), None),
+                   "moe_route")
+            _check(lib.rb_ep_build_send(_dev_ptr(self.ids), T, k, E, W, _dev_ptr(self.h), h,
+                                        _dev_ptr(self.dest_counts), _dev_ptr(self.dest_cursor),
+                                        _dev_ptr(self.send_meta), _dev_ptr(self.slot_pos),
+                                        _dev_ptr(self.send_rows), None), "ep_build_send")
+            exchange(self.recv_counts, self.dest_counts, [1] * W, [1] * W, self.group)
+            send_splits = self.dest_counts.cpu().tolist()
+            recv_splits = self.recv_counts.cpu().tolist()
+            R = int(sum(recv_splits))
+            self.exchanged_rows += int(sum(send_splits))
+            exchange(self.recv_rows[:R], self.send_rows, recv_splits, send_splits, self.group)
+            exchange(self.recv_meta[:R], self.send_meta, recv_splits, send_splits, self.group)
+            if R > 0:
+                rows = int(lib.rb_moe_max_rows(R, 1, self.epr))
+                ws = _dev_ptr(self.ws)
+                _check(lib.rb_moe_dispatch(_dev_ptr(self.recv_meta), R, 1, self.epr, _dev_ptr(self.recv_rows), h,
+                                           ws, _dev_ptr(self.xp), None), "moe_dispatch")
+                _check(lib.rb_matmul_grouped(L["gu"].id, self.epr, _dev_ptr(self.xp), rows, ws, R, 1,
+                                             _dev_ptr(self.gup), DTYPE_F16, None), "matmul_grouped")
+                _check(lib.rb_silu_mul_halves(_dev_ptr(self.gup), rows, I, _dev_ptr(self.actp), None), "silu_mul")
+                _check(lib.rb_matmul_grouped(L["down"].id, self.epr, _dev_ptr(self.actp), rows, ws, R, 1,
+                                             _dev_ptr(self.yp), DTYPE_F16, None), "matmul_grouped")
+                # back to receive order: y_recv[i] = yp[row of received slot i]
+                off = int(lib.rb_moe_slot_rows_offset(R, 1, self.epr))
+                _check(lib.rb_gather_rows(_dev_ptr(self.yp), ws + 4 * off, R, h, _dev_ptr(self.y_recv), None),
+                       "gather_rows")
+            exchange(self.y_back, self.y_recv[:R], send_splits, recv_splits, self.group)
+            _check(lib.rb_moe_combine_rows(xp, _dev_ptr(self.y_back), h, _dev_ptr(self.ids), _dev_ptr(self.wts),
+                                           _dev_ptr(self.slot_pos), T, k, None), "moe_combine")
+        _check(lib.rb_add_rms_norm(xp, None, _dev_ptr(self.final_norm), cfg.eps, _dev_ptr(self.out), T, h, None),
+               "add_rms_norm")
+        return self.out

@@ -255,6 +255,9 @@ RB_API int rb_matmul_i8_acc(int64_t id, const int8_t* codes, int64_t m, int32_t*
  * over `experts` (segments are 128-row aligned). */
 RB_API int64_t rb_moe_workspace_bytes(int64_t tokens, int top_k, int experts);
 RB_API int64_t rb_moe_max_rows(int64_t tokens, int top_k, int experts);
+/* int32-word offset, inside the workspace, of the slot -> permuted-row map
+ * [tokens * top_k] that rb_moe_dispatch writes. */
+RB_API int64_t rb_moe_slot_rows_offset(int64_t tokens, int top_k, int experts);
 /* f32 logits [tokens, experts] -> ids int32 [tokens, top_k] (descending
  * probability, ties to the lower id) and weights f32 (renormalised over the
  * selected experts when normalize != 0). experts <= 256, top_k <= 32. */
@@ -276,6 +279,25 @@ RB_API int rb_matmul_grouped(int64_t id, int experts, const void* x_perm_f16, in
 RB_API int rb_moe_combine(float* x, const void* y_perm_f16, int64_t hidden, const int32_t* ids,
                           const float* weights, const void* workspace, int64_t tokens, int top_k, int experts,
                           void* stream);
+
+/* ---- expert parallelism (no counterpart in the reference: its experts run
+ * on one board). Experts are split over `ranks` in consecutive blocks of
+ * experts/ranks ids. rb_ep_build_send groups the routed slots by destination
+ * rank: dest_counts[ranks] (rows per destination), send_rows[tokens*top_k,
+ * hidden] f16 (the token rows in destination order), send_meta[tokens*top_k]
+ * (expert id local to the destination) and slot_pos[tokens*top_k] (send
+ * position of each slot). dest_cursor[ranks] is scratch. */
+RB_API int rb_ep_build_send(const int32_t* ids, int64_t tokens, int top_k, int experts, int ranks,
+                            const void* x_f16, int64_t hidden, int32_t* dest_counts, int32_t* dest_cursor,
+                            int32_t* send_meta, int32_t* slot_pos, void* send_rows_f16, void* stream);
+/* out[i, :] = in[idx[i], :] for f16 rows. */
+RB_API int rb_gather_rows(const void* in_f16, const int32_t* idx, int64_t n, int64_t hidden, void* out_f16,
+                          void* stream);
+/* rb_moe_combine with an explicit slot -> row map (e.g. slot_pos after the
+ * outputs came back from the expert ranks). */
+RB_API int rb_moe_combine_rows(float* x, const void* y_f16, int64_t hidden, const int32_t* ids,
+                               const float* weights, const int32_t* row_of_slot, int64_t tokens, int top_k,
+                               void* stream);
 
 /* ---- statistics (MemStats, lib.rs:44-96) */
 RB_API int rb_mem_stats(int64_t* weights_bytes, int64_t* scratch_bytes, int64_t* num_weights);
