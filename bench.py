@@ -530,26 +530,48 @@ class MoeWorkload:
         from burn_rocket_b200.moe import MoeConfig, MoeModel
         self.rb = rb
         self.cfg = MoeConfig()
-        if world != 1:
-            raise SystemExit("--workload moe runs on one GPU (expert parallelism: --workload moe_ep)")
-        self.model = MoeModel(self.cfg, self.BATCH, self.SEQ, seed=0)
+        self.world = world
         g = torch.Generator(device="cpu").manual_seed(seed)
         ids = torch.randint(0, self.cfg.vocab, (self.BATCH * self.SEQ,), generator=g, dtype=torch.int32)
-        self.model.ids_in.copy_(ids.to(dev))
-        self.hids = ids.pin_memory()
-        self.hout = torch.empty(self.BATCH * self.SEQ, self.cfg.hidden, dtype=torch.float16).pin_memory()
-        self.units = self.BATCH * self.SEQ
+        if world == 1:
+            self.model = MoeModel(self.cfg, self.BATCH, self.SEQ, seed=0)
+            mine = ids
+        else:
+            # expert parallelism: experts split over the ranks, tokens by sequence
+            # (world <= 4) or by half sequence (world 8)
+            import torch.distributed as dist
+            from burn_rocket_b200.moe_ep import MoeEPModel, ep_plan
+            pairs = ([dist.new_group([2 * i, 2 * i + 1]) for i in range(world // 2)]
+                     if world > self.BATCH else None)
+            self.model = MoeEPModel(self.cfg, self.BATCH, self.SEQ, rank, world, seed=0, pair_groups=pairs)
+            mine = torch.cat([ids[s * self.SEQ + r0: s * self.SEQ + r0 + n]
+                              for s, r0, n in ep_plan(world, self.BATCH, self.SEQ)[rank]])
+            self.graphable = False  # the all-to-all splits are read on the host every layer
+        self.model.ids_in.copy_(mine.to(dev))
+        self.hids = mine.pin_memory()
+        self.hout = torch.empty(self.model.T, self.cfg.hidden, dtype=torch.float16).pin_memory()
+        self.units = self.model.T  # tokens per step on this rank
         self.flops = self.cfg.flops_per_token(self.SEQ) * self.units
 
     def step(self):
         self.model.forward_device()
 
     def e2e_step(self):
-        self.model.prefill_host(self.hids, self.hout)
+        import torch
+        if self.world == 1:
+            self.model.prefill_host(self.hids, self.hout)
+        else:
+            self.model.ids_in.copy_(self.hids, non_blocking=True)
+            self.model.forward_device()
+            self.hout.copy_(self.model.out, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
         return (self.hids.numel() * 4, self.hout.numel() * 2)
 
     def kernel_roofline(self):
-        """Device time of one layer's grouped expert GEMMs (gate|up and down)."""
+        """Device time of one layer's grouped expert GEMMs (gate|up and down);
+        None under expert parallelism (the whole step is reported)."""
+        if self.world != 1:
+            return None
         import torch
         import burn_rocket_b200._lib as L
         m, lay, lib = self.model, self.model.layers[0], L.load()
@@ -659,7 +681,7 @@ def run_b200(args):
     # host-side Python/ctypes overhead stays out of the device timing.
     graph = None
     rb.launch_count(reset=True)
-    if not args.no_graph:
+    if not args.no_graph and getattr(wl, "graphable", True):
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, capture_error_mode="thread_local"):
             wl.step()
@@ -707,10 +729,11 @@ def run_b200(args):
     e2e_value = per_step * world * e2e_steps / float(te.item())
 
     peaks, peak_kind = load_peaks()
-    if hasattr(wl, "kernel_roofline"):
+    kr = wl.kernel_roofline() if hasattr(wl, "kernel_roofline") else None
+    if kr is not None:
         # the dominant kernel measured on its own (inside a long step it runs
         # at the sustained clock: compare with the sustained peak)
-        kname, achieved, kms = wl.kernel_roofline()
+        kname, achieved, kms = kr
         peak = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
         peak_src = f"{peak_kind} MEASURED_PEAKS bf16_tflops_sustained"
         if wl.name == "siglip":
@@ -741,7 +764,10 @@ def run_b200(args):
                    "l2": "flushed between timed steps (256 MiB write)",
                    "parallelism": (f"dp{world} over sequences" if wl.name == "qwen3"
                                    else f"dp{world} over images" if wl.name == "siglip"
-                                   else "single GPU, all 128 experts resident" if wl.name == "moe"
+                                   else ("single GPU, all 128 experts resident" if world == 1
+                                         else f"ep{world} (experts {128 // world}/rank, NCCL all-to-all), "
+                                              f"{'dp over sequences' if world <= 4 else 'half sequences'}")
+                                   if wl.name == "moe"
                                    else (f"replicas x{world}" if world > 1 else "single GPU"))},
         "roofline": {"bound": "tensor", "kernel": kname, "achieved": round(achieved, 2), "peak": peak,
                      "unit": "TOP/s" if wl.name in ("w8a8", "siglip") else "TFLOP/s",
@@ -749,7 +775,9 @@ def run_b200(args):
         "e2e": {"value": round(e2e_value, 3), "unit": wl.unit, "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h)},
         "gpu_launches": int(launches),
-        "timing": "CUDA-graph replay of the step's C-ABI calls" if graph is not None else "eager launches",
+        "timing": ("CUDA-graph replay of the step's C-ABI calls" if graph is not None
+                   else "eager launches (per-layer host-sized all-to-all)" if wl.name == "moe" and world > 1
+                   else "eager launches"),
         "clocks": clocks.summary(),
     }
     if world > 1:
