@@ -27,6 +27,7 @@ from ._lib import (DTYPE_BF16, DTYPE_F16, DTYPE_F32, MASK_CAUSAL, MASK_CAUSAL_BL
 
 __all__ = [
     "Error", "OpFailure", "WeightId", "init", "pack", "pack2", "pack3", "pack_q8_0_blocks", "pack_w8a8_float",
+    "pack_i8", "quantize_row_groups",
     "pack_qat", "matmul", "matmul_host", "attention", "attention_window",
     "attention_causal_window", "attention_window_block", "attention_causal_block",
     "attention_raw", "q8_0_dequant", "quantize_rows_i8", "matmul_i8_acc", "check_device_errors",
@@ -155,6 +156,30 @@ def pack_qat(codes, w_scale, n: int, k: int, in_scale: float = 0.0, out_scale: f
     wid = _lib.load().rb_pack_w8a8(codes.ctypes.data, w_scale.ctypes.data, n, k, float(in_scale), float(out_scale))
     _check(wid, "rocket_pack_qat", 0, k, n)
     return WeightId(int(wid))
+
+
+def pack_i8(w, group: int) -> WeightId:
+    """Pack an [N, K] float weight as a group-wise int8 weight (rocket_pack_i8,
+    ext.rs:939-1029); rb_matmul then quantises the activations per group too."""
+    a = _as_f32_host(w)
+    if a.ndim != 2:
+        raise OpFailure(Error("rocket_pack_i8", _lib.RB_E_SHAPE), detail="weight must be [N, K]")
+    n, k = a.shape
+    wid = _lib.load().rb_pack_i8(a.ctypes.data, n, k, int(group))
+    _check(wid, "rocket_pack_i8", 0, k, n)
+    return WeightId(int(wid))
+
+
+def quantize_row_groups(x, group: int):
+    """Device group-wise row quantiser (host.rs:77-90): (codes int8 [M, K], scales f32 [M, K/group])."""
+    import torch
+    x = x.contiguous()
+    m, k = x.reshape(-1, x.shape[-1]).shape
+    codes = torch.empty(m, k, dtype=torch.int8, device=x.device)
+    scales = torch.empty(m, k // group, dtype=torch.float32, device=x.device)
+    _check(_lib.load().rb_quantize_row_groups(_dev_ptr(x), _dtype_code(x), m, k, int(group), _dev_ptr(codes),
+                                              _dev_ptr(scales), None), "quantize_row_groups")
+    return codes, scales
 
 
 def pack_w8a8_float(w, in_scale: float = 0.0, out_scale: float = 0.0) -> WeightId:

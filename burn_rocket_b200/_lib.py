@@ -53,6 +53,8 @@ _f = C.c_float
 # name -> (restype, argtypes)
 TILES_AUTO, TILES_SINGLE, TILES_PAIR = 0, 1, 2
 
+WEIGHT_I8G = 3
+
 SIGNATURES = {
     "rb_init": (_i, [_i]),
     "rb_last_error": (_i, [C.c_char_p, C.c_size_t]),
@@ -71,6 +73,8 @@ SIGNATURES = {
                                   _i, _i64, _i64, _i64, _p]),
     "rb_rms_norm": (_i, [_p, _i, _p, _f, _p, _i, _i64, _i64, _p]),
     "rb_pack_f32_w8a8_device": (_i64, [_p, _i64, _i64, _f, _f]),
+    "rb_pack_i8": (_i64, [_p, _i64, _i64, _i64]),
+    "rb_quantize_row_groups": (_i, [_p, _i, _i64, _i64, _i64, _p, _p, _p]),
     "rb_add_layer_norm": (_i, [_p, _p, _p, _p, _f, _p, _i64, _i64, _p]),
     "rb_gelu": (_i, [_p, _i64, _p]),
     "rb_silu_mul": (_i, [_p, _p, _i, _p, _i64, _p]),

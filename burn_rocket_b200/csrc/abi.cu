@@ -105,6 +105,7 @@ struct Weight {
   void* scales = nullptr;    // Q8_0: f16 [k/32, pitch]; W8A8: f32 [n]
   int64_t pitch = 0;         // Q8_0 scale row pitch: round_up(n, 8)
   float in_scale = 0.0f, out_scale = 0.0f;
+  int64_t group = 0;         // RB_WEIGHT_I8G: K group width (scales f32 [n, k/group])
   // TMA maps per staged weight-tile height ({256, 128, 96, 64}, see
   // bn_index; a CTA-pair tile stages half its N per CTA): the codes
   // (Q8_0: box 64 x bn; W8A8: box 128 x bn, 128-B swizzle) and the Q8_0
@@ -270,6 +271,49 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
                              st)) != RB_OK)
       return fail(rc, "q8_0 gemm launch failed");
     g_launches++;
+    return RB_OK;
+  }
+  if (w.kind == RB_WEIGHT_I8G) {
+    // Group-wise int8: per group, the int8 GEMM of the K slice gives exact
+    // int32 partials, folded into the f32 result in group order.
+    const int64_t G = w.group, ng = k / G;
+    const size_t codes_bytes = (static_cast<size_t>(m) * k + 255) & ~size_t(255);
+    const size_t part_bytes = (static_cast<size_t>(m) * w.n * 4 + 255) & ~size_t(255);
+    const size_t acc_bytes = y_dtype == RB_DTYPE_F32 ? 0 : static_cast<size_t>(m) * w.n * 4;
+    if ((rc = e->act.grow(codes_bytes + part_bytes + acc_bytes, "int8 group staging")) != RB_OK) return rc;
+    if ((rc = e->rowscale.grow(static_cast<size_t>(m) * ng * 4, "int8 group scales")) != RB_OK) return rc;
+    int8_t* codes = reinterpret_cast<int8_t*>(e->act.ptr);
+    int32_t* part = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(e->act.ptr) + codes_bytes);
+    float* acc = y_dtype == RB_DTYPE_F32
+                     ? reinterpret_cast<float*>(y)
+                     : reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(e->act.ptr) + codes_bytes + part_bytes);
+    float* a_s = reinterpret_cast<float*>(e->rowscale.ptr);
+    if ((rc = launch_quantize_groups(x, x_dtype, m, k, static_cast<int>(G), codes, a_s, st)) != RB_OK)
+      return fail(rc, "group quantiser launch failed");
+    g_launches++;
+    L.K = static_cast<int>(G);
+    L.out = part;
+    L.out_dtype = RB_DTYPE_I32;
+    L.ldo = static_cast<int>(w.n);
+    const GemmPlan plan{w.n % 256 == 0 ? 256 : 128, 1, false};
+    CUtensorMap tmC;
+    const bool tstore = output_map(&tmC, part, RB_DTYPE_I32, m, w.n);
+    for (int64_t g = 0; g < ng; ++g) {
+      CUtensorMap tmA, tmB;  // the group's K slice of both operands
+      if ((rc = make_tmap_2d(&tmA, codes + g * G, 1, m, G, k, 128, 128, 128)) != RB_OK) return rc;
+      if ((rc = make_tmap_2d(&tmB, w.codes + g * G, 1, w.n, G, k, 128, plan.weight_rows(), 128)) != RB_OK)
+        return rc;
+      if ((rc = launch_w8a8_gemm(L, plan, tmA, tmB, tstore ? &tmC : nullptr, st)) != RB_OK)
+        return fail(rc, "int8 group gemm launch failed");
+      if ((rc = launch_group_fold(part, m, w.n, a_s, reinterpret_cast<const float*>(w.scales), ng, g, g == 0, acc,
+                                  st)) != RB_OK)
+        return fail(rc, "group fold launch failed");
+      g_launches += 2;
+    }
+    if (y_dtype != RB_DTYPE_F32) {
+      if ((rc = launch_cast(acc, RB_DTYPE_F32, y, y_dtype, m * w.n, st)) != RB_OK) return fail(rc, "output cast");
+      g_launches++;
+    }
     return RB_OK;
   }
   if (w.kind == RB_WEIGHT_W8A8) {
@@ -623,6 +667,56 @@ int64_t rb_pack_w8a8(const int8_t* codes_host, const float* w_scale_host, int64_
   const int64_t id = e->next_id++;
   e->weights[id] = w;
   return id;
+}
+
+int64_t rb_pack_i8(const float* w_host, int64_t n, int64_t k, int64_t group) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Engine* e;
+  int rc = ensure_engine(&e);
+  if (rc) return rc;
+  if (!w_host) return fail(RB_E_SHAPE, "null weight");
+  // pack_i8_one asserts (ext.rs:948-953): group a positive multiple of 32
+  // dividing K; this build takes any N.
+  if (n <= 0 || k <= 0 || group <= 0 || group % 32 || k % group)
+    return fail(RB_E_SHAPE, "int8 group %lld must be a positive multiple of 32 dividing K=%lld", (long long)group,
+                (long long)k);
+  if (n > (1 << 30) || k > (1 << 30)) return fail(RB_E_SHAPE, "int8 weight too large");
+  Weight w;
+  w.kind = RB_WEIGHT_I8G;
+  w.n = n;
+  w.k = k;
+  w.group = group;
+  const size_t ng = static_cast<size_t>(k / group);
+  float* tmp = nullptr;
+  if (cudaMalloc(&w.codes, static_cast<size_t>(n) * k) != cudaSuccess ||
+      cudaMalloc(&w.scales, static_cast<size_t>(n) * ng * 4) != cudaSuccess ||
+      cudaMalloc(&tmp, static_cast<size_t>(n) * k * 4) != cudaSuccess) {
+    cudaGetLastError();
+    if (w.codes) cudaFree(w.codes);
+    if (w.scales) cudaFree(w.scales);
+    return fail(RB_E_NOMEM, "int8 pack: device allocation failed");
+  }
+  RB_CUDA(cudaMemcpy(tmp, w_host, static_cast<size_t>(n) * k * 4, cudaMemcpyHostToDevice), "weight upload");
+  rc = launch_quantize_groups(tmp, RB_DTYPE_F32, n, k, static_cast<int>(group), w.codes,
+                              reinterpret_cast<float*>(w.scales), nullptr);
+  g_launches++;
+  const cudaError_t ce = cudaDeviceSynchronize();
+  cudaFree(tmp);
+  if (rc != RB_OK || ce != cudaSuccess) return fail(RB_E_DEVICE, "int8 group quantiser failed");
+  w.bytes = static_cast<size_t>(n) * k + static_cast<size_t>(n) * ng * 4;
+  const int64_t id = e->next_id++;
+  e->weights[id] = w;
+  return id;
+}
+
+int rb_quantize_row_groups(const void* x, int x_dtype, int64_t m, int64_t k, int64_t group, int8_t* codes,
+                           float* scales, void* stream) {
+  if (!x || !codes || !scales || m <= 0 || k <= 0 || group <= 0 || k % group)
+    return fail(RB_E_SHAPE, "quantize_row_groups: group must divide K");
+  const int rc = launch_quantize_groups(x, x_dtype, m, k, static_cast<int>(group), codes, scales,
+                                        reinterpret_cast<cudaStream_t>(stream));
+  g_launches++;
+  return rc == RB_OK ? RB_OK : fail(rc, "quantize_row_groups: bad dtype");
 }
 
 int64_t rb_pack_f32_w8a8_device(const float* w_dev, int64_t n, int64_t k, float in_scale,

@@ -77,6 +77,10 @@ int launch_moe_combine_rows(float* x, const void* y, int64_t hidden, const int32
                             const int32_t* row_of_slot, int64_t tokens, int top_k, cudaStream_t st);
 
 // Elementwise / codec kernels (quant.cu).
+int launch_quantize_groups(const void* x, int x_dtype, int64_t m, int64_t k, int group, int8_t* codes,
+                           float* scales, cudaStream_t st);
+int launch_group_fold(const int32_t* part, int64_t m, int64_t n, const float* a_s, const float* b_s, int64_t ng,
+                      int64_t g, int first, float* y, cudaStream_t st);
 int launch_cast(const void* x, int x_dtype, void* y, int y_dtype, int64_t count,
                 cudaStream_t stream);
 int launch_quantize_rows_i8(const void* x, int x_dtype, int64_t m, int64_t k, float in_scale,

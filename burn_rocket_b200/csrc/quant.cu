@@ -183,6 +183,83 @@ int launch_w8a8_weight_quant(const float* w, int64_t n, int64_t k, int8_t* codes
   return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
 }
 
+// ---------------------------------------------------------------- group-wise int8
+// Per row and per `group`-wide K block: scale = max(max|x| / 127, 1e-12),
+// code = clamp(round_half_away(x * (1/scale)), -127, 127)
+// (quantize_row_groups, crates/burn-rocket/src/host.rs:77-90). One warp per
+// row; scales [m, k/group].
+template <int DT>
+__global__ void quantize_groups_kernel(const void* __restrict__ x, int64_t m, int64_t k, int group,
+                                       int8_t* __restrict__ codes, float* __restrict__ scales) {
+  const int lane = threadIdx.x & 31;
+  const int64_t ng = k / group;
+  const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); row < m;
+       row += nw) {
+    const int64_t base = row * k;
+    for (int64_t g = 0; g < ng; ++g) {
+      const int64_t g0 = base + g * group;
+      float amax = 0.0f;
+      for (int i = lane; i < group; i += 32) amax = fmaxf(amax, fabsf(load_as_f32(x, DT, g0 + i)));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const float s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-12f);
+      const float inv = __fdiv_rn(1.0f, s);
+      for (int i = lane; i < group; i += 32)
+        codes[g0 + i] = static_cast<int8_t>(
+            fminf(fmaxf(roundf(__fmul_rn(load_as_f32(x, DT, g0 + i), inv)), -127.f), 127.f));
+      if (lane == 0) scales[row * ng + g] = s;
+    }
+  }
+}
+
+int launch_quantize_groups(const void* x, int x_dtype, int64_t m, int64_t k, int group, int8_t* codes,
+                           float* scales, cudaStream_t st) {
+  if (group <= 0 || k % group) return RB_E_SHAPE;
+  int64_t blocks = (m + 7) / 8;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  if (blocks < 1) blocks = 1;
+  switch (x_dtype) {
+    case RB_DTYPE_F32:
+      quantize_groups_kernel<RB_DTYPE_F32><<<static_cast<int>(blocks), 256, 0, st>>>(x, m, k, group, codes, scales);
+      break;
+    case RB_DTYPE_F16:
+      quantize_groups_kernel<RB_DTYPE_F16><<<static_cast<int>(blocks), 256, 0, st>>>(x, m, k, group, codes, scales);
+      break;
+    case RB_DTYPE_BF16:
+      quantize_groups_kernel<RB_DTYPE_BF16><<<static_cast<int>(blocks), 256, 0, st>>>(x, m, k, group, codes, scales);
+      break;
+    default:
+      return RB_E_SHAPE;
+  }
+  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
+}
+
+// y[m, n] (f32) = (first ? 0 : y) + f32(a_s[m, g] * b_s[n, g]) * f32(partial[m, n]):
+// one group's int32 partial promoted as the reference's readback does
+// (layout::detile_accum_i8_scaled, crates/rocket-npu/src/matmul/layout.rs:504-529).
+__global__ void group_fold_kernel(const int32_t* __restrict__ part, int64_t m, int64_t n,
+                                  const float* __restrict__ a_s, const float* __restrict__ b_s, int64_t ng,
+                                  int64_t g, int first, float* __restrict__ y) {
+  const int64_t total = m * n;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / n, c = i % n;
+    const float scale = __fmul_rn(a_s[r * ng + g], b_s[c * ng + g]);
+    const float t = __fmul_rn(scale, __int2float_rn(part[i]));
+    y[i] = first ? __fadd_rn(0.0f, t) : __fadd_rn(y[i], t);
+  }
+}
+
+int launch_group_fold(const int32_t* part, int64_t m, int64_t n, const float* a_s, const float* b_s, int64_t ng,
+                      int64_t g, int first, float* y, cudaStream_t st) {
+  int64_t blocks = (m * n + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  if (blocks < 1) blocks = 1;
+  group_fold_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(part, m, n, a_s, b_s, ng, g, first, y);
+  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
+}
+
 // ---------------------------------------------------------------- casts
 template <int SRC, int DST>
 __global__ void cast_kernel(const void* __restrict__ x, void* __restrict__ y, int64_t count) {

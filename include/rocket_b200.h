@@ -63,6 +63,7 @@ extern "C" {
 /* Weight kinds held by the registry. */
 #define RB_WEIGHT_Q8_0 1 /* int8 codes + f16 scale per 32-wide K block           */
 #define RB_WEIGHT_W8A8 2 /* per-output-channel int8 codes + f32 scale (QAT form) */
+#define RB_WEIGHT_I8G 3  /* group-wise int8 codes + f32 scale per (row, K group)  */
 
 /* Replaces burn_rocket::init(threads) (ext.rs:561-580): binds the calling
  * process to CUDA device `device_ordinal` and creates the engine. Later calls
@@ -110,6 +111,19 @@ RB_API int64_t rb_pack_w8a8(const int8_t* codes_host, const float* w_scale_host,
  * codes only). */
 RB_API int64_t rb_pack_f32_w8a8_device(const float* w_dev, int64_t n, int64_t k, float in_scale,
                                        float out_scale);
+
+/* Group-wise int8 weight from a host f32 [n, k] weight (rocket_pack_i8,
+ * ext.rs:939-1029): per row and per `group`-wide K block, scale = max(max|w|/127,
+ * 1e-12) and code = clamp(round_half_away(w / scale), -127, 127)
+ * (host.rs:77-90). group must be a positive multiple of 32 dividing K.
+ * rb_matmul with such an id quantises the activation rows the same way and
+ * returns sum over groups g (in order) of f32(a_s[m,g]*b_s[n,g]) * f32(int32
+ * partial of group g) (matmul_i8 / matmul_gw, ext.rs:1505-1554,
+ * matmul/int8.rs:641-672). */
+RB_API int64_t rb_pack_i8(const float* w_host, int64_t n, int64_t k, int64_t group);
+/* Device group-wise row quantiser: codes int8 [m, k], scales f32 [m, k/group]. */
+RB_API int rb_quantize_row_groups(const void* x, int x_dtype, int64_t m, int64_t k, int64_t group,
+                                  int8_t* codes, float* scales, void* stream);
 
 /* Weight geometry of a packed id: kind (RB_WEIGHT_*), n, k. */
 RB_API int rb_weight_info(int64_t id, int* kind, int64_t* n, int64_t* k);

@@ -214,6 +214,33 @@ def quantize_row_groups(x, group: int):
     return q, s
 
 
+def matmul_gw(aq, a_s, bq, b_s, group: int) -> np.ndarray:
+    """Group-wise int8 matmul (matmul_gw, crates/rocket-npu/src/matmul/int8.rs:641-672;
+    promotion order of layout.rs:504-529): acc = 0; for g in order:
+    acc += f32(a_s[m,g] * b_s[n,g]) * f32(exact int32 partial of group g), all f32."""
+    aq, bq = np.asarray(aq, np.int8), np.asarray(bq, np.int8)
+    m, k = aq.shape
+    n = bq.shape[0]
+    ng = k // group
+    acc = np.zeros((m, n), np.float32)
+    for g in range(ng):
+        part = gemm_i8(aq[:, g * group:(g + 1) * group], bq[:, g * group:(g + 1) * group])
+        scale = (np.asarray(a_s, np.float32)[:, g:g + 1] * np.asarray(b_s, np.float32)[None, :, g]).astype(np.float32)
+        acc = (acc + (scale * part.astype(np.float32)).astype(np.float32)).astype(np.float32)
+    return acc
+
+
+def quantize_rows_groups(x, group: int):
+    """quantize_row_groups over every row of x [m, k] -> (codes [m, k], scales [m, k/group])."""
+    x = np.asarray(x, np.float32)
+    m, k = x.shape
+    q = np.empty((m, k), np.int8)
+    s = np.empty((m, k // group), np.float32)
+    for r in range(m):
+        q[r], s[r] = quantize_row_groups(x[r], group)
+    return q, s
+
+
 # ---------------------------------------------------------------- attention
 MASK_NONE, MASK_NONE_BLOCK, MASK_CAUSAL, MASK_WINDOW = 0, 1, 2, 3
 MASK_CAUSAL_WINDOW, MASK_WINDOW_BLOCK, MASK_CAUSAL_BLOCK = 4, 5, 6

@@ -168,3 +168,27 @@ def test_attention_contract_errors(rb):
     with pytest.raises(rb.OpFailure) as ei:
         rb.attention(q, kv, kv, 2, 1, 128, 0.1, None, True)
     assert ei.value.error.rc == -1  # full-sequence modes need n_q == n_kv
+
+
+# ------------------------------------------------------------------ chunked causal helper (a12)
+@pytest.mark.parametrize("window", [None, 300])
+def test_chunked_causal_attention_matches_dense(rb, orc, window):
+    """causal_attention (src/util/causal.rs:103-163) with 512-row chunks equals
+    the dense causal(-window) op: bit for bit for pure causal (same key tiles),
+    within tolerance with a window (the band start shifts the key tiling)."""
+    import torch
+    from burn_rocket_b200.causal import causal_attention
+    S, H, KV, D = 1500, 8, 2, 128
+    g = torch.Generator(device="cuda").manual_seed(11)
+    q = torch.randn(S, H * D, device="cuda", generator=g).half()
+    k = torch.randn(S, KV * D, device="cuda", generator=g).half()
+    v = torch.randn(S, KV * D, device="cuda", generator=g).half()
+    scale = 1 / math.sqrt(D)
+    dense = causal_attention(q, k, v, H, KV, D, scale, window=window, chunk=0)
+    chunked = causal_attention(q, k, v, H, KV, D, scale, window=window, chunk=512)
+    torch.cuda.synchronize()
+    if window is None:
+        assert torch.equal(dense, chunked)
+    else:
+        assert cosine(dense.float().cpu().numpy(), chunked.float().cpu().numpy()) >= 0.99999
+    rb.check_device_errors()

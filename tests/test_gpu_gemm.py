@@ -210,3 +210,40 @@ def test_tile_policy_rejects_unknown(rb):
     import burn_rocket_b200._lib as L
     assert L.load().rb_set_tile_policy(7) != 0
     assert rb.set_tile_policy("auto") == "auto"
+
+
+# ------------------------------------------------------------------ group-wise int8 (a7)
+@pytest.mark.parametrize("m,n,k,group", [(1, 32, 32, 32), (50, 96, 256, 32), (300, 1024, 1024, 128),
+                                         (129, 3072, 1024, 64), (257, 200, 384, 128)])
+def test_group_int8_matmul_bit_exact(rb, orc, m, n, k, group):
+    """rocket_pack_i8 + matmul_i8 (ext.rs:939-1029, 1505-1554): codes and group
+    scales of both operands, and the f32 sum of promoted int32 group partials,
+    bit for bit against the oracle (host.rs:77-90, int8.rs:641-672)."""
+    import torch
+    rng = np.random.default_rng(m + n + k + group)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    wid = rb.pack_i8(w, group)
+    xd = torch.from_numpy(x).cuda()
+    qd, sd = rb.quantize_row_groups(xd, group)
+    q, s = orc.quantize_rows_groups(x, group)
+    assert np.array_equal(qd.cpu().numpy(), q)
+    assert np.array_equal(sd.cpu().numpy().view(np.uint32), s.view(np.uint32))
+    y = rb.matmul(xd, wid).cpu().numpy()
+    wq, ws = orc.quantize_rows_groups(w, group)
+    want = orc.matmul_gw(q, s, wq, ws, group)
+    assert np.array_equal(y.view(np.uint32), want.view(np.uint32))
+    # and close to the float product (the reference's host.rs:224-275 bound)
+    ref = x.astype(np.float64) @ w.T.astype(np.float64)
+    assert np.abs(y - ref).max() <= 0.1 * max(np.abs(ref).max(), 1.0)
+    y16 = rb.matmul(xd.half(), wid, out_dtype=torch.float16).float().cpu().numpy()
+    assert np.allclose(y16, want, rtol=2e-3, atol=2e-3)
+    rb.check_device_errors()
+
+
+def test_group_int8_rejects_bad_group(rb):
+    import burn_rocket_b200 as rbm
+    with pytest.raises(rbm.OpFailure):
+        rb.pack_i8(np.zeros((32, 96), np.float32), 64)   # 64 does not divide 96
+    with pytest.raises(rbm.OpFailure):
+        rb.pack_i8(np.zeros((32, 96), np.float32), 48)   # not a multiple of 32
