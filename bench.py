@@ -241,7 +241,7 @@ class Q8GemmWorkload:
         rng = np.random.default_rng(seed)
         a = rng.standard_normal((self.M, self.K)).astype(np.float32)
         w = (rng.standard_normal((self.N, self.K)) * 0.02).astype(np.float32)
-        self.wid = rb.pack(w)  # device Q8_0 encoder
+        self.wid = rb.pack_q8_0(w)  # device Q8_0 encoder
         xdt = torch.float32 if self.X_DTYPE == "f32" else torch.float16
         self.x = torch.from_numpy(a).to(dev).to(xdt)
         self.y = torch.empty(self.M, self.N, dtype=xdt, device=dev)

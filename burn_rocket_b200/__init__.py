@@ -26,7 +26,8 @@ from ._lib import (DTYPE_BF16, DTYPE_F16, DTYPE_F32, MASK_CAUSAL, MASK_CAUSAL_BL
                    MASK_WINDOW_BLOCK, WEIGHT_Q8_0, WEIGHT_W8A8)
 
 __all__ = [
-    "Error", "OpFailure", "WeightId", "init", "pack", "pack2", "pack3", "pack_q8_0_blocks", "pack_w8a8_float",
+    "Error", "OpFailure", "WeightId", "init", "pack", "pack2", "pack3", "pack_q8_0", "pack2_q8_0", "pack3_q8_0",
+    "pack_q8_0_blocks", "pack_w8a8_float",
     "pack_i8", "quantize_row_groups",
     "pack_qat", "matmul", "matmul_host", "attention", "attention_window",
     "attention_causal_window", "attention_window_block", "attention_causal_block",
@@ -107,7 +108,7 @@ def _as_f32_host(w) -> np.ndarray:
     return np.ascontiguousarray(np.asarray(w, dtype=np.float32))
 
 
-def _pack_parts(parts: Sequence) -> WeightId:
+def _pack_parts_q8_0(parts: Sequence) -> WeightId:
     arrs = [_as_f32_host(p) for p in parts]
     k = arrs[0].shape[1]
     for a in arrs:
@@ -120,19 +121,56 @@ def _pack_parts(parts: Sequence) -> WeightId:
     return WeightId(int(wid))
 
 
+def _pack_parts_f16(parts: Sequence) -> WeightId:
+    """Host parts (numpy / CPU torch tensors of f32, f16 or bf16) -> one fp16-resident weight."""
+    import torch
+    ts = []
+    for p in parts:
+        t = p.detach() if hasattr(p, "detach") else torch.from_numpy(np.ascontiguousarray(p))
+        t = t.cpu()
+        if t.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+            t = t.float()
+        ts.append(t.contiguous())
+    dt = ts[0].dtype
+    ts = [t.to(dt) for t in ts]
+    k = ts[0].shape[1]
+    for t in ts:
+        if t.dim() != 2 or t.shape[1] != k:
+            raise OpFailure(Error("rocket_pack", _lib.RB_E_SHAPE), detail="all parts must be [N_i, K] with a shared K")
+    ptrs = (C.c_void_p * len(ts))(*[t.data_ptr() for t in ts])
+    ns = (C.c_int64 * len(ts))(*[t.shape[0] for t in ts])
+    wid = _lib.load().rb_pack_f16(ptrs, ns, len(ts), k, _dtype_code(ts[0]))
+    _check(wid, "rocket_pack", 0, k, sum(t.shape[0] for t in ts))
+    return WeightId(int(wid))
+
+
 def pack(w) -> WeightId:
-    """Pack an [N, K] float weight as a resident Q8_0 weight (rocket_pack, ext.rs:59)."""
-    return _pack_parts([w])
+    """Pack an [N, K] float weight as a resident fp16 weight (rocket_pack, ext.rs:59, 829-850)."""
+    return _pack_parts_f16([w])
 
 
 def pack2(a, b) -> WeightId:
-    """Pack two weights sharing one input, concatenated along N (ext.rs:61)."""
-    return _pack_parts([a, b])
+    """Pack two fp16 weights sharing one input, concatenated along N (ext.rs:61)."""
+    return _pack_parts_f16([a, b])
 
 
 def pack3(a, b, c) -> WeightId:
-    """Pack three weights sharing one input, concatenated along N (ext.rs:63)."""
-    return _pack_parts([a, b, c])
+    """Pack three fp16 weights sharing one input, concatenated along N (ext.rs:63)."""
+    return _pack_parts_f16([a, b, c])
+
+
+def pack_q8_0(w) -> WeightId:
+    """Pack an [N, K] float weight as a resident Q8_0 weight (the GGUF Q8_0 route:
+    device encoder of q8_bench.rs:199-219; dequantised inside the GEMM)."""
+    return _pack_parts_q8_0([w])
+
+
+def pack2_q8_0(a, b) -> WeightId:
+    return _pack_parts_q8_0([a, b])
+
+
+def pack3_q8_0(a, b, c) -> WeightId:
+    return _pack_parts_q8_0([a, b, c])
 
 
 def pack_q8_0_blocks(blocks: np.ndarray, n: int, k: int) -> WeightId:

@@ -54,6 +54,7 @@ _f = C.c_float
 TILES_AUTO, TILES_SINGLE, TILES_PAIR = 0, 1, 2
 
 WEIGHT_I8G = 3
+WEIGHT_F16 = 4
 
 SIGNATURES = {
     "rb_init": (_i, [_i]),
@@ -74,6 +75,7 @@ SIGNATURES = {
     "rb_rms_norm": (_i, [_p, _i, _p, _f, _p, _i, _i64, _i64, _p]),
     "rb_pack_f32_w8a8_device": (_i64, [_p, _i64, _i64, _f, _f]),
     "rb_pack_i8": (_i64, [_p, _i64, _i64, _i64]),
+    "rb_pack_f16": (_i64, [_p, _p, _i, _i64, _i]),
     "rb_quantize_row_groups": (_i, [_p, _i, _i64, _i64, _i64, _p, _p, _p]),
     "rb_add_layer_norm": (_i, [_p, _p, _p, _p, _f, _p, _i64, _i64, _p]),
     "rb_gelu": (_i, [_p, _i64, _p]),

@@ -125,6 +125,8 @@ static int weight_maps(Weight& w) {
       if ((rc = make_tmap_2d(&w.tm_codes[i], w.codes, 1, w.n, w.k, w.k, 64, bn, 0)) != RB_OK) return rc;
       if ((rc = make_tmap_2d(&w.tm_scales[i], w.scales, 2, w.k / 32, w.n, w.pitch, bn, 2, 0)) != RB_OK)
         return rc;
+    } else if (w.kind == RB_WEIGHT_F16) {
+      if ((rc = make_tmap_2d(&w.tm_codes[i], w.codes, 2, w.n, w.k, w.k, 64, bn, 128)) != RB_OK) return rc;
     } else {
       if ((rc = make_tmap_2d(&w.tm_codes[i], w.codes, 1, w.n, w.k, w.k, 128, bn, 128)) != RB_OK) return rc;
     }
@@ -253,6 +255,27 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
   L.err = e->err;
   L.num_sms = e->num_sms;
   int rc;
+  if (w.kind == RB_WEIGHT_F16) {
+    // fp16-resident weight (the reference's default pack, ext.rs:829-934):
+    // f16 x f16 with f32 accumulation.
+    const void* a = x;
+    if (x_dtype != RB_DTYPE_F16 || (reinterpret_cast<uintptr_t>(x) & 15) != 0) {
+      if ((rc = e->act.grow(static_cast<size_t>(m) * k * 2, "matmul activations")) != RB_OK) return rc;
+      if ((rc = launch_cast(x, x_dtype, e->act.ptr, RB_DTYPE_F16, m * k, st)) != RB_OK)
+        return fail(rc, "activation cast launch failed");
+      g_launches++;
+      a = e->act.ptr;
+    }
+    const GemmPlan plan = gemm_plan(true, L.M, L.N, L.K, e->num_sms);
+    CUtensorMap tmA, tmC;
+    if ((rc = make_tmap_2d(&tmA, a, 2, m, k, k, 64, plan.a_rows(), 128)) != RB_OK) return rc;
+    const bool tstore = output_map(&tmC, y, y_dtype, m, w.n);
+    if ((rc = launch_f16_gemm(L, plan, tmA, w.tm_codes[bn_index(plan.weight_rows())], tstore ? &tmC : nullptr,
+                              st)) != RB_OK)
+      return fail(rc, "f16 gemm launch failed");
+    g_launches++;
+    return RB_OK;
+  }
   if (w.kind == RB_WEIGHT_Q8_0) {
     const void* a = x;
     if (x_dtype != RB_DTYPE_F16 || (reinterpret_cast<uintptr_t>(x) & 15) != 0) {
@@ -664,6 +687,57 @@ int64_t rb_pack_w8a8(const int8_t* codes_host, const float* w_scale_host, int64_
   RB_CUDA(cudaMemcpy(w.scales, w_scale_host, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice), "scale upload");
   if ((rc = weight_maps(w)) != RB_OK) return rc;
   w.bytes = static_cast<size_t>(n) * k + static_cast<size_t>(n) * 4;
+  const int64_t id = e->next_id++;
+  e->weights[id] = w;
+  return id;
+}
+
+int64_t rb_pack_f16(const void* const* parts_host, const int64_t* n_parts, int num_parts, int64_t k,
+                    int src_dtype) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Engine* e;
+  int rc = ensure_engine(&e);
+  if (rc) return rc;
+  if (!parts_host || !n_parts || num_parts <= 0) return fail(RB_E_SHAPE, "pack: no parts");
+  if (k <= 0 || k % 8 != 0) return fail(RB_E_SHAPE, "pack: K=%lld must be a positive multiple of 8", (long long)k);
+  const int eb = dtype_bytes(src_dtype);
+  if (!eb) return fail(RB_E_SHAPE, "pack: bad source dtype %d", src_dtype);
+  int64_t n = 0;
+  for (int i = 0; i < num_parts; ++i) {
+    if (!parts_host[i] || n_parts[i] <= 0) return fail(RB_E_SHAPE, "pack: empty part %d", i);
+    n += n_parts[i];
+  }
+  if (n > (1 << 30) || k > (1 << 30)) return fail(RB_E_SHAPE, "pack: weight too large");
+  Weight w;
+  w.kind = RB_WEIGHT_F16;
+  w.n = n;
+  w.k = k;
+  void* tmp = nullptr;
+  const size_t elems = static_cast<size_t>(n) * k;
+  if (cudaMalloc(&w.codes, elems * 2) != cudaSuccess ||
+      (src_dtype != RB_DTYPE_F16 && cudaMalloc(&tmp, elems * eb) != cudaSuccess)) {
+    cudaGetLastError();
+    if (w.codes) cudaFree(w.codes);
+    return fail(RB_E_NOMEM, "pack: device allocation failed");
+  }
+  // parts concatenated along N (pack2 / pack3 / pack_seg, ext.rs:852-934)
+  uint8_t* dst = src_dtype == RB_DTYPE_F16 ? reinterpret_cast<uint8_t*>(w.codes) : reinterpret_cast<uint8_t*>(tmp);
+  size_t off = 0;
+  for (int i = 0; i < num_parts; ++i) {
+    const size_t bytes = static_cast<size_t>(n_parts[i]) * k * eb;
+    RB_CUDA(cudaMemcpy(dst + off, parts_host[i], bytes, cudaMemcpyHostToDevice), "weight upload");
+    off += bytes;
+  }
+  if (src_dtype != RB_DTYPE_F16) {
+    // f32 / bf16 -> f16 RNE, as the reference's pack converts (f32_to_f16_par, ext.rs:2144-2156)
+    rc = launch_cast(tmp, src_dtype, w.codes, RB_DTYPE_F16, static_cast<int64_t>(elems), nullptr);
+    g_launches++;
+    const cudaError_t ce = cudaDeviceSynchronize();
+    cudaFree(tmp);
+    if (rc != RB_OK || ce != cudaSuccess) return fail(RB_E_DEVICE, "pack: f16 conversion failed");
+  }
+  if ((rc = weight_maps(w)) != RB_OK) return rc;
+  w.bytes = elems * 2;
   const int64_t id = e->next_id++;
   e->weights[id] = w;
   return id;

@@ -39,7 +39,7 @@
 
 namespace rb {
 
-template <int BN_, int LSTAGES_, bool I8_, int BSTAGES_ = 2, int MH_ = 1>
+template <int BN_, int LSTAGES_, int KIND_, int BSTAGES_ = 2, int MH_ = 1>
 struct GemmCfg {
   static constexpr int BN = BN_;
   // 128-row M halves per tile: MH = 2 issues two M=128 UMMAs per K step that
@@ -47,8 +47,9 @@ struct GemmCfg {
   static constexpr int MH = MH_;
   static constexpr int BM = 128 * MH;
   static constexpr int LSTAGES = LSTAGES_;          // TMA load ring depth
-  static constexpr bool I8 = I8_;
-  static constexpr bool Q8 = !I8;
+  static constexpr bool I8 = KIND_ == kKindI8;      // int8 UMMA + W8A8 epilogue
+  static constexpr bool Q8 = KIND_ == kKindQ8;      // B dequantised from staged codes
+  static constexpr bool TMAB = !Q8;                 // B tiles loaded by TMA
   static constexpr int BSTAGES = BSTAGES_;          // dequantised B ring (Q8_0)
   static constexpr int ELEM = I8 ? 1 : 2;
   static constexpr int BK = 128 / ELEM;             // K elements per stage (one 128-B atom)
@@ -156,7 +157,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           uint8_t* st = smem + ls * Cfg::LSTAGE;
           mbar_arrive_expect_tx(&load_full[ls], Cfg::LOAD_TX);
           tma_load_2d(st, &tmA, &load_full[ls], kb * Cfg::BK, m0);
-          if (Cfg::I8) {
+          if (Cfg::TMAB) {
             tma_load_2d(st + Cfg::A_BYTES, &tmB, &load_full[ls], kb * Cfg::BK, n0);
           } else {
             tma_load_2d(st + Cfg::A_BYTES, &tmB, &load_full[ls], kb * 64, n0);
@@ -303,13 +304,15 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 // Host-side launch.
 
 // Q8_0: (BN, load-ring depth, dequantised-B-ring depth) sized to the smem budget.
-using CfgQ8_256 = GemmCfg<256, 3, false, 2>;
-using CfgQ8_128 = GemmCfg<128, 4, false, 4>;
-using CfgQ8_96 = GemmCfg<96, 4, false, 6>;
-using CfgQ8_64 = GemmCfg<64, 6, false, 6>;
-using CfgQ8_128x2 = GemmCfg<128, 3, false, 3, 2>;  // 256-row M tile
-using CfgI8_256 = GemmCfg<256, 4, true>;
-using CfgI8_128 = GemmCfg<128, 6, true>;
+using CfgQ8_256 = GemmCfg<256, 3, kKindQ8, 2>;
+using CfgQ8_128 = GemmCfg<128, 4, kKindQ8, 4>;
+using CfgQ8_96 = GemmCfg<96, 4, kKindQ8, 6>;
+using CfgQ8_64 = GemmCfg<64, 6, kKindQ8, 6>;
+using CfgQ8_128x2 = GemmCfg<128, 3, kKindQ8, 3, 2>;  // 256-row M tile
+using CfgI8_256 = GemmCfg<256, 4, kKindI8>;
+using CfgI8_128 = GemmCfg<128, 6, kKindI8>;
+using CfgF16_256 = GemmCfg<256, 4, kKindF16>;
+using CfgF16_128 = GemmCfg<128, 6, kKindF16>;
 
 template <class Cfg>
 static int launch_cfg(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmS,
@@ -424,6 +427,20 @@ int launch_q8_gemm(const GemmLaunch& L, const GemmPlan& plan, const CUtensorMap&
     case 128: return launch_cfg<CfgQ8_128>(tmA, tmCodes, tmScales, tmC, a, L.num_sms, stream);
     case 96: return launch_cfg<CfgQ8_96>(tmA, tmCodes, tmScales, tmC, a, L.num_sms, stream);
     case 64: return launch_cfg<CfgQ8_64>(tmA, tmCodes, tmScales, tmC, a, L.num_sms, stream);
+    default: return RB_E_SHAPE;
+  }
+}
+
+int launch_f16_gemm_pair(const GemmArgs& a, int bn, int num_sms, const CUtensorMap& tmA,
+                         const CUtensorMap& tmB, const CUtensorMap* tmC, cudaStream_t stream);
+
+int launch_f16_gemm(const GemmLaunch& L, const GemmPlan& plan, const CUtensorMap& tmA,
+                    const CUtensorMap& tmB, const CUtensorMap* tmC, cudaStream_t stream) {
+  const GemmArgs a = make_args(L);
+  if (plan.pair) return launch_f16_gemm_pair(a, plan.bn, L.num_sms, tmA, tmB, tmC, stream);
+  switch (plan.bn) {
+    case 256: return launch_cfg<CfgF16_256>(tmA, tmB, tmA, tmC, a, L.num_sms, stream);
+    case 128: return launch_cfg<CfgF16_128>(tmA, tmB, tmA, tmC, a, L.num_sms, stream);
     default: return RB_E_SHAPE;
   }
 }

@@ -12,6 +12,13 @@
 
 namespace rb {
 
+// Weight kinds of the GEMM kernels: Q8_0 codes dequantised in shared memory
+// (kind::f16 UMMA), int8 codes by TMA (kind::i8, W8A8 epilogue), f16 values
+// by TMA (kind::f16, the reference's fp16-resident weights).
+constexpr int kKindQ8 = 0;
+constexpr int kKindI8 = 1;
+constexpr int kKindF16 = 2;
+
 constexpr int kEpiWarp0 = 2;      // first epilogue warp
 constexpr int kNumEpiWarps = 4;   // Q8_0 kernels: one warp per TMEM lane quarter
 constexpr int kNumEpiWarpsI8 = 8; // W8A8 kernels: two warps per lane quarter (column halves)

@@ -41,7 +41,7 @@ namespace rb {
 // ring of CSTAGES staged code/scale stages, refilled by its own producer warp
 // as soon as the dequant warps have read a stage (so dequantisation can run
 // ahead of the MMA by up to CSTAGES stages), and BSTAGES dequantised B stages.
-template <int BN_, int LSTAGES_, bool I8_, int CSTAGES_ = 1, int BSTAGES_ = 1, int DQ_WARPS_ = 8,
+template <int BN_, int LSTAGES_, int KIND_, int CSTAGES_ = 1, int BSTAGES_ = 1, int DQ_WARPS_ = 8,
           int DQ_GROUPS_ = 1>
 struct PairCfg {
   static constexpr int DQ_WARPS = DQ_WARPS_;         // Q8_0 dequant warps
@@ -50,8 +50,9 @@ struct PairCfg {
   static constexpr int BN = BN_;                    // UMMA N of the pair tile
   static constexpr int HB = BN / 2;                 // weight rows staged per CTA
   static constexpr int LSTAGES = LSTAGES_;
-  static constexpr bool I8 = I8_;
-  static constexpr bool Q8 = !I8_;
+  static constexpr bool I8 = KIND_ == kKindI8;
+  static constexpr bool Q8 = KIND_ == kKindQ8;
+  static constexpr bool TMAB = !Q8;                 // B halves loaded by TMA
   static constexpr int CSTAGES = Q8 ? CSTAGES_ : 1;
   static constexpr int BSTAGES = Q8 ? BSTAGES_ : 1;
   static constexpr int ELEM = I8 ? 1 : 2;
@@ -62,9 +63,9 @@ struct PairCfg {
   static constexpr int B_BYTES = HB * 128;          // this CTA's half of B (s8, or dequantised f16)
   static constexpr int CODE_BYTES = Q8 ? HB * 64 : 0;
   static constexpr int SC_BYTES = Q8 ? 2 * HB * 2 : 0;
-  static constexpr uint32_t PAIR_TX = I8 ? 2 * (A_BYTES + B_BYTES) : 2 * A_BYTES;
+  static constexpr uint32_t PAIR_TX = TMAB ? 2 * (A_BYTES + B_BYTES) : 2 * A_BYTES;
   static constexpr uint32_t CODE_TX = CODE_BYTES + SC_BYTES;
-  static constexpr int LSTAGE = round1k(A_BYTES + (I8 ? B_BYTES : 0));
+  static constexpr int LSTAGE = round1k(A_BYTES + (TMAB ? B_BYTES : 0));
   static constexpr int CSTAGE = Q8 ? round1k(CODE_BYTES + SC_BYTES) : 0;
   static constexpr int CODE_OFF = LSTAGES * LSTAGE;
   static constexpr int BRING_OFF = CODE_OFF + CSTAGES * CSTAGE;
@@ -177,7 +178,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           const uint32_t lf = mapa_shared(&ld_full[ls], 0);
           if (rank == 0) mbar_arrive_expect_tx(&ld_full[ls], Cfg::PAIR_TX);
           tma_load_2d_pair(st, &tmA, lf, kb * Cfg::BK, m0);
-          if constexpr (Cfg::I8) tma_load_2d_pair(st + Cfg::A_BYTES, &tmB, lf, kb * Cfg::BK, nb);
+          if constexpr (Cfg::TMAB) tma_load_2d_pair(st + Cfg::A_BYTES, &tmB, lf, kb * Cfg::BK, nb);
           if (++ls == LSTAGES) { ls = 0; lph ^= 1; }
         }
       }
@@ -356,10 +357,12 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 // --------------------------------------------------------------------------
 // Host-side launch.
 
-using PairQ8_256 = PairCfg<256, 5, false, 5, 5, 12, 3>;
-using PairQ8_128 = PairCfg<128, 7, false, 8, 6, 12, 3>;
-using PairI8_256 = PairCfg<256, 6, true>;
-using PairI8_128 = PairCfg<128, 8, true>;
+using PairQ8_256 = PairCfg<256, 5, kKindQ8, 5, 5, 12, 3>;
+using PairQ8_128 = PairCfg<128, 7, kKindQ8, 8, 6, 12, 3>;
+using PairI8_256 = PairCfg<256, 6, kKindI8>;
+using PairI8_128 = PairCfg<128, 8, kKindI8>;
+using PairF16_256 = PairCfg<256, 6, kKindF16>;
+using PairF16_128 = PairCfg<128, 8, kKindF16>;
 
 template <class Cfg>
 static int launch_pair_cfg(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmS,
@@ -408,6 +411,15 @@ int launch_q8_gemm_pair(const GemmArgs& a, int bn, int num_sms, const CUtensorMa
   switch (bn) {
     case 256: return launch_pair_cfg<PairQ8_256>(tmA, tmCodes, tmScales, tmC, a, num_sms, stream);
     case 128: return launch_pair_cfg<PairQ8_128>(tmA, tmCodes, tmScales, tmC, a, num_sms, stream);
+    default: return RB_E_SHAPE;
+  }
+}
+
+int launch_f16_gemm_pair(const GemmArgs& a, int bn, int num_sms, const CUtensorMap& tmA,
+                         const CUtensorMap& tmB, const CUtensorMap* tmC, cudaStream_t stream) {
+  switch (bn) {
+    case 256: return launch_pair_cfg<PairF16_256>(tmA, tmB, tmA, tmC, a, num_sms, stream);
+    case 128: return launch_pair_cfg<PairF16_128>(tmA, tmB, tmA, tmC, a, num_sms, stream);
     default: return RB_E_SHAPE;
   }
 }

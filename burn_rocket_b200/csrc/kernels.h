@@ -52,6 +52,10 @@ int launch_q8_gemm(const GemmLaunch& L, const GemmPlan& plan, const CUtensorMap&
 // codes [N, K] (box 128 x weight_rows()), both 128-B swizzled.
 int launch_w8a8_gemm(const GemmLaunch& L, const GemmPlan& plan, const CUtensorMap& tmA,
                      const CUtensorMap& tmB, const CUtensorMap* tmC, cudaStream_t stream);
+// f16 weights (the reference's fp16-resident pack): tmB = f16 weight [N, K]
+// (box 64 x weight_rows(), 128-B swizzle); same tile plans as W8A8.
+int launch_f16_gemm(const GemmLaunch& L, const GemmPlan& plan, const CUtensorMap& tmA,
+                    const CUtensorMap& tmB, const CUtensorMap* tmC, cudaStream_t stream);
 int launch_q8_dequant(const int8_t* codes, const void* scales, int N, int K, int pitch, void* out,
                       bool f16_out, cudaStream_t stream);
 

@@ -64,6 +64,7 @@ extern "C" {
 #define RB_WEIGHT_Q8_0 1 /* int8 codes + f16 scale per 32-wide K block           */
 #define RB_WEIGHT_W8A8 2 /* per-output-channel int8 codes + f32 scale (QAT form) */
 #define RB_WEIGHT_I8G 3  /* group-wise int8 codes + f32 scale per (row, K group)  */
+#define RB_WEIGHT_F16 4  /* f16 values [N, K] (the reference's fp16-resident pack) */
 
 /* Replaces burn_rocket::init(threads) (ext.rs:561-580): binds the calling
  * process to CUDA device `device_ordinal` and creates the engine. Later calls
@@ -111,6 +112,13 @@ RB_API int64_t rb_pack_w8a8(const int8_t* codes_host, const float* w_scale_host,
  * codes only). */
 RB_API int64_t rb_pack_f32_w8a8_device(const float* w_dev, int64_t n, int64_t k, float in_scale,
                                        float out_scale);
+
+/* fp16-resident weight (rocket_pack / pack2 / pack3, ext.rs:829-934): host parts
+ * [n_parts[i], k] of dtype src_dtype (RB_DTYPE_F32 / F16 / BF16) concatenated
+ * along N and rounded to f16 (RNE); rb_matmul is then f16 x f16 with f32
+ * accumulation. K % 8 == 0. */
+RB_API int64_t rb_pack_f16(const void* const* parts_host, const int64_t* n_parts, int num_parts, int64_t k,
+                           int src_dtype);
 
 /* Group-wise int8 weight from a host f32 [n, k] weight (rocket_pack_i8,
  * ext.rs:939-1029): per row and per `group`-wide K block, scale = max(max|w|/127,

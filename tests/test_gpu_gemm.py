@@ -47,7 +47,7 @@ def test_q8_0_device_encode_and_dequant_bit_exact(rb, orc, n, k):
     got16 = rb.q8_0_dequant(wid, "f16").cpu().numpy()
     assert np.array_equal(got16.view(np.uint16), orc.f32_to_f16_bits(deq))
     # device encoder (rb_pack_f32_q8_0) == reference encoder, bit for bit
-    wid2 = rb.pack(w)
+    wid2 = rb.pack_q8_0(w)
     got2 = rb.q8_0_dequant(wid2, "f32").cpu().numpy()
     assert np.array_equal(got2.view(np.uint32), deq.view(np.uint32))
     torch.cuda.synchronize()
@@ -250,3 +250,43 @@ def test_group_int8_rejects_bad_group(rb):
         rb.pack_i8(np.zeros((32, 96), np.float32), 64)   # 64 does not divide 96
     with pytest.raises(rbm.OpFailure):
         rb.pack_i8(np.zeros((32, 96), np.float32), 48)   # not a multiple of 32
+
+
+# ------------------------------------------------------------------ fp16-resident weights (a3-a5)
+@pytest.mark.parametrize("m,n,k", [(1, 32, 32), (77, 136, 160), (512, 3072, 1024), (2000, 1024, 2048)])
+def test_f16_weight_matmul(rb, orc, m, n, k):
+    """rocket_pack keeps the weight as f16 (ext.rs:829-850): f16 x f16 products
+    with f32 accumulation; only the summation order differs from the f64
+    product of the same f16 operands."""
+    import torch
+    rng = np.random.default_rng(m + n + k)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    wid = rb.pack(w)
+    for x_dt in (torch.float32, torch.float16):
+        y = rb.matmul(torch.from_numpy(a).cuda().to(x_dt), wid, out_dtype=torch.float32).cpu().numpy()
+        a16 = orc.f16_bits_to_f32(orc.f32_to_f16_bits(a))
+        w16 = orc.f16_bits_to_f32(orc.f32_to_f16_bits(w))
+        assert max_rel(y, orc.gemm_f64acc(a16, w16)) <= 1e-5
+    rb.check_device_errors()
+
+
+def test_f16_pack2_pack3_concatenate_and_policies(rb, orc, tile_policy):
+    import torch
+    rng = np.random.default_rng(3)
+    k = 256
+    parts = [(rng.standard_normal((n, k)) * 0.02).astype(np.float32) for n in (64, 96, 32)]
+    x = torch.from_numpy(rng.standard_normal((300, k)).astype(np.float32)).cuda()
+    full = rb.matmul(x, rb.pack(np.concatenate(parts, 0))).cpu().numpy()
+    for policy in ("single", "pair"):
+        tile_policy(policy)
+        y3 = rb.matmul(x, rb.pack3(*parts)).cpu().numpy()
+        assert np.array_equal(y3, full) or max_rel(y3, full) <= 1e-6
+    y2 = rb.matmul(x, rb.pack2(parts[0], parts[1])).cpu().numpy()
+    assert max_rel(y2, full[:, :160]) <= 1e-6
+    # bf16 host weights are rounded to f16 like the reference's pack
+    wb = torch.from_numpy(parts[0]).to(torch.bfloat16)
+    yb = rb.matmul(x, rb.pack(wb)).cpu().numpy()
+    wb16 = orc.f16_bits_to_f32(orc.f32_to_f16_bits(wb.float().numpy()))
+    a16 = orc.f16_bits_to_f32(orc.f32_to_f16_bits(x.cpu().numpy()))
+    assert max_rel(yb, orc.gemm_f64acc(a16, wb16)) <= 1e-5

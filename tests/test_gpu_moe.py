@@ -65,8 +65,8 @@ def test_dispatch_grouped_gemm_combine_matches_oracle(rb, orc):
     experts = [((rng.standard_normal((I, H)) * 0.02).astype(np.float32),
                 (rng.standard_normal((I, H)) * 0.02).astype(np.float32),
                 (rng.standard_normal((H, I)) * 0.02).astype(np.float32)) for _ in range(E)]
-    gu_id = rbm._pack_parts([m for g, u, _ in experts for m in (g, u)])
-    dn_id = rbm._pack_parts([d for _, _, d in experts])
+    gu_id = rbm._pack_parts_q8_0([m for g, u, _ in experts for m in (g, u)])
+    dn_id = rbm._pack_parts_q8_0([d for _, _, d in experts])
     rows = int(lib.rb_moe_max_rows(T, K, E))
     ws = torch.empty(int(lib.rb_moe_workspace_bytes(T, K, E)) // 4 + 1, dtype=torch.int32, device="cuda")
     xd = torch.from_numpy(x16).cuda()
