@@ -374,5 +374,17 @@ def set_tile_policy(policy: str) -> str:
     return names[old]
 
 
+def set_attention_split(policy: str) -> str:
+    """Attention work split for later calls: "auto", "never" (one CTA per
+    query-slot pair and KV head) or "always" (one CTA per SM over equal shares
+    of the key tiles). Returns the previous one."""
+    names = ["auto", "never", "always"]
+    if policy not in names:
+        raise ValueError(f"attention split policy must be one of {names}")
+    old = _lib.load().rb_set_attention_split(names.index(policy))
+    _check(old, "rb_set_attention_split")
+    return names[old]
+
+
 def launch_count(reset: bool = False) -> int:
     return int(_lib.load().rb_launch_count(1 if reset else 0))

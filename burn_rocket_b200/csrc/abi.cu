@@ -167,6 +167,8 @@ struct Engine {
   int device = -1;
   int num_sms = 0;
   uint32_t* err = nullptr;  // device error word
+  float* attn_rec = nullptr;  // attention split-mode records (kAttnRecBytes)
+  int* attn_cnt = nullptr;    // attention split-mode arrival counters (kAttnCntBytes)
   std::unordered_map<int64_t, Weight> weights;
   int64_t next_id = 1;
   Scratch act;       // activation staging (f16 or int8 codes)
@@ -489,7 +491,13 @@ static int attention_locked(Engine* e, const void* q, int64_t ldq, const void* k
   L.kv_start = kv_start;
   L.err = e->err;
   L.num_sms = e->num_sms;
-  if ((rc = launch_attention(tm, L, st)) != RB_OK) return fail(rc, "attention launch failed");
+  L.ws_rec = e->attn_rec;
+  L.ws_cnt = e->attn_cnt;
+  g_last_error.clear();
+  if ((rc = launch_attention(tm, L, st)) != RB_OK) {
+    const std::string why = g_last_error;
+    return fail(rc, "attention launch failed%s%s", why.empty() ? "" : ": ", why.c_str());
+  }
   g_launches++;
   if (dtype == RB_DTYPE_F32) {
     if ((rc = launch_cast(oh, RB_DTYPE_F16, out, RB_DTYPE_F32, batch * n_q * wq, st)) != RB_OK)
@@ -527,6 +535,16 @@ int rb_init(int device_ordinal) {
     return fail(RB_E_NOMEM, "cudaMalloc(error word) failed");
   }
   cudaMemset(e->err, 0, sizeof(uint32_t));
+  // Attention split-mode workspace; without it attention runs one CTA per unit.
+  if (cudaMalloc(&e->attn_rec, kAttnRecBytes) != cudaSuccess ||
+      cudaMalloc(&e->attn_cnt, kAttnCntBytes) != cudaSuccess ||
+      cudaMemset(e->attn_cnt, 0, kAttnCntBytes) != cudaSuccess) {
+    cudaGetLastError();
+    if (e->attn_rec) cudaFree(e->attn_rec);
+    if (e->attn_cnt) cudaFree(e->attn_cnt);
+    e->attn_rec = nullptr;
+    e->attn_cnt = nullptr;
+  }
   cudaStreamCreateWithFlags(&e->host_stream, cudaStreamNonBlocking);
   g_engine = e;
   return RB_OK;
@@ -550,6 +568,8 @@ int rb_check_device_errors(void) {
   RB_CUDA(cudaMemcpy(&word, e->err, sizeof(word), cudaMemcpyDeviceToHost), "read error word");
   if (word) {
     cudaMemset(e->err, 0, sizeof(uint32_t));
+    // An aborted attention launch can leave split-mode counters mid-count.
+    if (e->attn_cnt) cudaMemset(e->attn_cnt, 0, kAttnCntBytes);
     return fail(RB_E_DEVICE, "kernel error word 0x%x (%s%s%s)", word,
                 (word & kErrWaitTimeout) ? "wait-timeout " : "",
                 (word & kErrTmemAlloc) ? "tmem-alloc " : "",
@@ -1246,6 +1266,12 @@ int rb_moe_combine_rows(float* x, const void* y_f16, int64_t hidden, const int32
 int rb_set_tile_policy(int policy) {
   if (policy < RB_TILES_AUTO || policy > RB_TILES_PAIR) return fail(RB_E_SHAPE, "unknown tile policy %d", policy);
   return set_gemm_policy(policy);
+}
+
+int rb_set_attention_split(int policy) {
+  if (policy < RB_ATTN_SPLIT_AUTO || policy > RB_ATTN_SPLIT_ALWAYS)
+    return fail(RB_E_SHAPE, "unknown attention split policy %d", policy);
+  return set_attention_split(policy);
 }
 
 int64_t rb_launch_count(int reset) {

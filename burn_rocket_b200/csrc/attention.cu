@@ -40,6 +40,11 @@
 #include "sm100.cuh"
 #include "kernels.h"
 
+#include <algorithm>
+#include <atomic>
+#include <queue>
+#include <vector>
+
 namespace rb {
 
 namespace attn {
@@ -47,14 +52,21 @@ namespace attn {
 constexpr int BM = 128;      // query rows per slot
 constexpr int BN = 64;       // keys per tile
 constexpr int KV_STAGES = 4;
-constexpr int kSoftWarp0 = 4;
-constexpr int kThreads = 12 * 32;
+constexpr int kSoftWarp0 = 2;       // warps 2-5: slot 0, warps 6-9: slot 1
+constexpr int kThreads = 10 * 32;   // 3 warps on some SM sub-partitions: 168 registers a thread
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kClamp = -30000.0f;   // fa_score clamp (oneshot.rs PAD_KEY_SCORE)
 constexpr float kClamp2 = kClamp * kLog2e;
 constexpr float kRescaleThresh = 8.0f;  // log2 units
 constexpr float kFastMargin = 160.0f;   // exp2(-160) underflows f32 to 0
 constexpr int kNoBound = 1 << 30;
+constexpr int kMaxCtas = kAttnMaxCtas;  // split-mode grid bound (>= SM count)
+// Schedule cost model, in key tiles (one tile ~ 1.3 us of a CTA's time):
+constexpr int kItemCost = 6;   // split mode: per unit (Q load, pipeline refill, epilogue)
+constexpr int kMergeCost = 4;  // split mode: per CTA (partial records and the merge)
+constexpr int kCtaCost = 2;    // one CTA per unit: per CTA (prologue, epilogue)
+
+std::atomic<int> g_split_policy{RB_ATTN_SPLIT_AUTO};
 
 struct Params {
   void* out;
@@ -68,9 +80,25 @@ struct Params {
   int dlo, dhi;        // visible iff dlo <= (k_off + j) - (q_off + i) <= dhi
   int q_off, k_off;
   int d_out;           // output columns per head (<= D: the real head_dim)
-  // Sequences lie back to back: sequence b (blockIdx.y) owns query rows
-  // [b*n_q, (b+1)*n_q) and key rows [b*n_kv, (b+1)*n_kv) of the tensors.
+  // Sequences lie back to back: sequence b owns query rows [b*n_q, (b+1)*n_q)
+  // and key rows [b*n_kv, (b+1)*n_kv) of the tensors.
+  int batch;
+  int n_units;         // batch * pairs_per_group * n_kv_heads work units
+  // Split mode (split != 0): G CTAs share the W cost positions of all units
+  // evenly (SplitPlan gives each CTA's starting unit).
+  int split, W, G;
+  int item_cost;       // cost positions charged per unit on top of its key tiles
+  float* rec;          // [G][2 records][2 slots] partial (O, m, l)
+  int* cnt;            // [n_units][2 slots] parts arrived (self-resetting)
   uint32_t* err;
+};
+
+// Split mode: CTA c starts inside unit u0[c], whose first cost position is
+// pre0[c]. A separate grid-constant parameter, so that the per-tile reads of
+// Params stay plain constant-bank operands.
+struct SplitPlan {
+  int u0[kMaxCtas];
+  int pre0[kMaxCtas];
 };
 
 // A head row of D elements is staged as D/64 128-byte-swizzled atoms of 64
@@ -124,7 +152,10 @@ struct SlotInfo {
   int lo, hi; // key tile range (inclusive); empty when lo > hi
 };
 
-__device__ __forceinline__ SlotInfo slot_info(const Params& p, int g, int item) {
+__host__ __device__ __forceinline__ long lmax_(long a, long b) { return a > b ? a : b; }
+__host__ __device__ __forceinline__ long lmin_(long a, long b) { return a < b ? a : b; }
+
+__host__ __device__ inline SlotInfo slot_info(const Params& p, int g, int item) {
   SlotInfo s;
   const int total = p.group * p.q_tiles;
   if (item >= total) { s.head = 0; s.qt = 0; s.lo = 1; s.hi = 0; return s; }
@@ -132,12 +163,12 @@ __device__ __forceinline__ SlotInfo slot_info(const Params& p, int g, int item) 
   s.head = g * p.group + item % p.group;
   const int n_kv_tiles = (p.n_kv + BN - 1) / BN;
   const int qa0 = p.q_off + s.qt * BM;
-  const int qa1 = p.q_off + min(s.qt * BM + BM, p.n_q) - 1;
+  const int qa1 = p.q_off + static_cast<int>(lmin_(s.qt * BM + BM, p.n_q)) - 1;
   // Visible absolute keys of row qa: [qa + dlo, qa + dhi] ∩ [k_off, k_off + n_kv).
   const long klast = static_cast<long>(p.k_off) + p.n_kv - 1;
   auto row_empty = [&](int qa) {
-    const long lo = (p.dlo <= -kNoBound) ? p.k_off : max(static_cast<long>(p.k_off), static_cast<long>(qa) + p.dlo);
-    const long hi = (p.dhi >= kNoBound) ? klast : min(klast, static_cast<long>(qa) + p.dhi);
+    const long lo = (p.dlo <= -kNoBound) ? p.k_off : lmax_(static_cast<long>(p.k_off), static_cast<long>(qa) + p.dlo);
+    const long hi = (p.dhi >= kNoBound) ? klast : lmin_(klast, static_cast<long>(qa) + p.dhi);
     return lo > hi;
   };
   if (row_empty(qa0) || row_empty(qa1)) {
@@ -146,11 +177,141 @@ __device__ __forceinline__ SlotInfo slot_info(const Params& p, int g, int item) 
   }
   long jlo = (p.dlo <= -kNoBound) ? 0 : static_cast<long>(qa0) + p.dlo - p.k_off;
   long jhi = (p.dhi >= kNoBound) ? p.n_kv - 1 : static_cast<long>(qa1) + p.dhi - p.k_off;
-  jlo = max(jlo, 0L);
-  jhi = min(jhi, static_cast<long>(p.n_kv - 1));
+  jlo = lmax_(jlo, 0L);
+  jhi = lmin_(jhi, static_cast<long>(p.n_kv - 1));
   s.lo = static_cast<int>(jlo / BN);
   s.hi = static_cast<int>(jhi / BN);
   return s;
+}
+
+// A work unit: one KV head g of sequence b and one pair of query slots (two
+// heads of the group, or two query tiles of a one-head group). Its key tiles
+// are the union [J0, J1] of both slots'.
+struct Unit {
+  SlotInfo sl[2];
+  bool act1;
+  int b, g, J0, J1, len;
+};
+
+__host__ __device__ inline Unit unit_info(const Params& p, int u) {
+  Unit U;
+  U.g = u % p.n_kv_heads;
+  const int t = u / p.n_kv_heads;
+  U.b = t % p.batch;
+  // One-unit-per-CTA mode: heaviest first, for the hardware's greedy CTA
+  // scheduling. Split mode: heavy and light pairs alternate, so no CTA's
+  // range collects a long run of short units (each costs a Q load and an
+  // epilogue).
+  const int tb = t / p.batch;
+  const int pair = !p.split ? p.pairs_per_group - 1 - tb
+                            : ((tb & 1) ? tb / 2 : p.pairs_per_group - 1 - tb / 2);
+  U.sl[0] = slot_info(p, U.g, 2 * pair);
+  U.sl[1] = slot_info(p, U.g, 2 * pair + 1);
+  const bool act0 = U.sl[0].lo <= U.sl[0].hi;
+  U.act1 = U.sl[1].lo <= U.sl[1].hi;
+  if (!act0 && !U.act1) { U.J0 = 0; U.J1 = -1; }
+  else if (!U.act1) { U.J0 = U.sl[0].lo; U.J1 = U.sl[0].hi; }
+  else if (!act0) { U.J0 = U.sl[1].lo; U.J1 = U.sl[1].hi; }
+  else {
+    U.J0 = U.sl[0].lo < U.sl[1].lo ? U.sl[0].lo : U.sl[1].lo;
+    U.J1 = U.sl[0].hi > U.sl[1].hi ? U.sl[0].hi : U.sl[1].hi;
+  }
+  U.len = U.J1 - U.J0 + 1;
+  return U;
+}
+
+// Split mode works in "cost" positions: a unit with len > 0 key tiles costs
+// item_cost + len positions, the first item_cost standing for the per-item
+// overhead (Q load, pipeline refill, epilogue) and tile t at position
+// pre + item_cost + t. CTA c owns positions [c*W/G, (c+1)*W/G), so CTAs
+// that meet many short units get fewer tiles.
+__host__ __device__ __forceinline__ int split_begin(const Params& p, int c) {
+  return static_cast<int>(static_cast<long long>(c) * p.W / p.G);
+}
+__device__ __forceinline__ int split_cta(const Params& p, long long x) {
+  return static_cast<int>(((x + 1) * p.G - 1) / p.W);
+}
+
+// One CTA's walk over its items: a contiguous key-tile range [ja, jb] of one
+// unit. Every warp role walks the same sequence.
+struct Item {
+  Unit U;
+  int u, pre;    // unit index and its first cost position
+  int ja, jb;    // key tiles of this item
+  bool full;     // the item is the whole unit (no partial results)
+  bool first;    // first item of this CTA
+};
+
+struct Walk {
+  int u, pre, pos, end, k;
+  __device__ __forceinline__ void begin(const Params& p, const SplitPlan& plan) {
+    k = 0;
+    if (p.split) {
+      pos = split_begin(p, blockIdx.x);
+      end = split_begin(p, blockIdx.x + 1);
+      u = plan.u0[blockIdx.x];
+      pre = plan.pre0[blockIdx.x];
+    } else {
+      u = blockIdx.x;
+      pre = 0;
+      pos = 0;
+      end = -1;  // one whole unit
+    }
+  }
+  __device__ __forceinline__ bool next(const Params& p, Item& it) {
+    if (!p.split) {
+      if (end == 0 || u >= p.n_units) return false;
+      end = 0;
+      it.U = unit_info(p, u);
+      if (it.U.len <= 0) return false;
+      it.u = u;
+      it.pre = 0;
+      it.ja = it.U.J0;
+      it.jb = it.U.J1;
+      it.full = true;
+      it.first = true;
+      ++k;
+      return true;
+    }
+    for (;;) {
+      if (pos >= end || u >= p.n_units) return false;
+      it.U = unit_info(p, u);
+      if (it.U.len <= 0) {  // no keys: costs nothing
+        ++u;
+        continue;
+      }
+      const int base = pre + p.item_cost;  // cost position of tile 0
+      const int t0 = pos > base ? pos - base : 0;
+      const int t1 = (end - base < it.U.len) ? end - base : it.U.len;
+      const int cost = p.item_cost + it.U.len;
+      const int upre = pre, uu = u;
+      if (end >= pre + cost) {  // the unit ends inside this CTA's range
+        pos = pre + cost;
+        pre += cost;
+        ++u;
+      } else {
+        pos = end;
+      }
+      if (t1 <= t0) continue;  // only the unit's overhead positions fall here
+      it.u = uu;
+      it.pre = upre;
+      it.ja = it.U.J0 + t0;
+      it.jb = it.U.J0 + t1 - 1;
+      it.full = t0 == 0 && t1 == it.U.len;
+      it.first = k == 0;
+      ++k;
+      return true;
+    }
+  }
+};
+
+// Partial results of a split unit: per CTA two records (its first and its
+// last item), per slot the unnormalised O as [D/4][BM] float4 (a warp's 32
+// rows of one column quad are 512 contiguous bytes), then m[BM] and l[BM].
+template <int D>
+__device__ __forceinline__ float* record(const Params& p, int cta, int r, int s) {
+  constexpr int REC = BM * D + 2 * BM;
+  return p.rec + (static_cast<size_t>(cta) * 4 + r * 2 + s) * REC;
 }
 
 template <int D, bool BF16, bool SOFTCAP>
@@ -158,7 +319,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
             const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmQt,
             const __grid_constant__ CUtensorMap tmKt, const __grid_constant__ CUtensorMap tmVt,
-            Params p) {
+            Params p, const __grid_constant__ SplitPlan plan) {
   using L = Smem<D>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -173,26 +334,20 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   uint64_t* s_free = s_full + 4;                // [slot][buf]
   uint64_t* p_full = s_free + 4;                // [slot][buf]
   uint64_t* o_done = p_full + 4;                // [slot]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
+  uint64_t* q_empty = o_done + 2;               // [1]
+  uint64_t* o_free = q_empty + 1;               // [slot]
+  uint64_t* pub_bar = o_free + 2;               // [slot] a split part's record is written
+  uint64_t* dec_bar = pub_bar + 2;              // [slot] the last-arriver decision is made
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dec_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);  // [slot]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int q_row0 = blockIdx.y * p.n_q;    // this sequence's first query row
-  const int kv_row0 = blockIdx.y * p.n_kv;  // and first key row
-
-  // Work item: heavy (late) query tiles first so causal runs finish together.
-  const int g = blockIdx.x % p.n_kv_heads;
-  const int pair = p.pairs_per_group - 1 - blockIdx.x / p.n_kv_heads;
-  SlotInfo sl[2];
-  sl[0] = slot_info(p, g, 2 * pair);
-  sl[1] = slot_info(p, g, 2 * pair + 1);
-  const bool act1 = sl[1].lo <= sl[1].hi;
-  const int J0 = act1 ? min(sl[0].lo, sl[1].lo) : sl[0].lo;
-  const int J1 = act1 ? max(sl[0].hi, sl[1].hi) : sl[0].hi;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int i = 0; i < KV_STAGES; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
@@ -204,8 +359,12 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       mbar_init(&s_free[i], 1);
       mbar_init(&p_full[i], 4);
     }
-    mbar_init(&o_done[0], 1);
-    mbar_init(&o_done[1], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&o_done[i], 1);
+      mbar_init(&o_free[i], 4);
+      mbar_init(&pub_bar[i], 4);
+      mbar_init(&dec_bar[i], 1);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -217,6 +376,9 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  Walk w;
+  w.begin(p, plan);
+  Item item;
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA
@@ -224,35 +386,43 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
-      const int nslots = act1 ? 2 : 1;
-      mbar_arrive_expect_tx(q_full, nslots * L::Q_TILE);
-      for (int s = 0; s < nslots; ++s) {
-        for (int a = 0; a < L::ATOMS; ++a)
-          tma_load_2d(smem + L::Q_OFF + s * L::Q_TILE + a * L::Q_ATOM, &tmQ, q_full,
-                      sl[s].head * D + a * 64, q_row0 + sl[s].qt * BM);
-        if (L::TAIL)
-          tma_load_2d(smem + L::Q_OFF + s * L::Q_TILE + L::Q_TAIL_OFF, &tmQt, q_full,
-                      sl[s].head * D + L::ATOMS * 64, q_row0 + sl[s].qt * BM);
-      }
-      for (int j = J0; j <= J1; ++j) {
-        const int jl = j - J0, st = jl % KV_STAGES;
-        const uint32_t ph = ((jl / KV_STAGES) & 1) ^ 1;
-        if (!mbar_wait(&k_empty[st], ph, p.err, abort_flag)) break;
-        mbar_arrive_expect_tx(&k_full[st], L::KV_TILE);
-        for (int a = 0; a < L::ATOMS; ++a)
-          tma_load_2d(smem + L::K_OFF + st * L::KV_TILE + a * L::KV_ATOM, &tmK, &k_full[st],
-                      g * D + a * 64, kv_row0 + j * BN);
-        if (L::TAIL)
-          tma_load_2d(smem + L::K_OFF + st * L::KV_TILE + L::KV_TAIL_OFF, &tmKt, &k_full[st],
-                      g * D + L::ATOMS * 64, kv_row0 + j * BN);
-        if (!mbar_wait(&v_empty[st], ph, p.err, abort_flag)) break;
-        mbar_arrive_expect_tx(&v_full[st], L::KV_TILE);
-        for (int a = 0; a < L::ATOMS; ++a)
-          tma_load_2d(smem + L::V_OFF + st * L::KV_TILE + a * L::KV_ATOM, &tmV, &v_full[st],
-                      g * D + a * 64, kv_row0 + j * BN);
-        if (L::TAIL)
-          tma_load_2d(smem + L::V_OFF + st * L::KV_TILE + L::KV_TAIL_OFF, &tmVt, &v_full[st],
-                      g * D + L::ATOMS * 64, kv_row0 + j * BN);
+      int kv_it = 0;  // K/V ring position, continued across items
+      bool ok = true;
+      for (int k = 0; ok && w.next(p, item); ++k) {
+        const Unit& U = item.U;
+        const int q_row0 = U.b * p.n_q, kv_row0 = U.b * p.n_kv;
+        // The Q buffers are reused once every S of the previous item retired.
+        if (k > 0 && !mbar_wait(q_empty, (k - 1) & 1, p.err, abort_flag)) break;
+        const int nslots = U.act1 ? 2 : 1;
+        mbar_arrive_expect_tx(q_full, nslots * L::Q_TILE);
+        for (int s = 0; s < nslots; ++s) {
+          for (int a = 0; a < L::ATOMS; ++a)
+            tma_load_2d(smem + L::Q_OFF + s * L::Q_TILE + a * L::Q_ATOM, &tmQ, q_full,
+                        U.sl[s].head * D + a * 64, q_row0 + U.sl[s].qt * BM);
+          if (L::TAIL)
+            tma_load_2d(smem + L::Q_OFF + s * L::Q_TILE + L::Q_TAIL_OFF, &tmQt, q_full,
+                        U.sl[s].head * D + L::ATOMS * 64, q_row0 + U.sl[s].qt * BM);
+        }
+        for (int j = item.ja; j <= item.jb; ++j, ++kv_it) {
+          const int st = kv_it % KV_STAGES;
+          const uint32_t ph = ((kv_it / KV_STAGES) & 1) ^ 1;
+          if (!mbar_wait(&k_empty[st], ph, p.err, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&k_full[st], L::KV_TILE);
+          for (int a = 0; a < L::ATOMS; ++a)
+            tma_load_2d(smem + L::K_OFF + st * L::KV_TILE + a * L::KV_ATOM, &tmK, &k_full[st],
+                        U.g * D + a * 64, kv_row0 + j * BN);
+          if (L::TAIL)
+            tma_load_2d(smem + L::K_OFF + st * L::KV_TILE + L::KV_TAIL_OFF, &tmKt, &k_full[st],
+                        U.g * D + L::ATOMS * 64, kv_row0 + j * BN);
+          if (!mbar_wait(&v_empty[st], ph, p.err, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&v_full[st], L::KV_TILE);
+          for (int a = 0; a < L::ATOMS; ++a)
+            tma_load_2d(smem + L::V_OFF + st * L::KV_TILE + a * L::KV_ATOM, &tmV, &v_full[st],
+                        U.g * D + a * 64, kv_row0 + j * BN);
+          if (L::TAIL)
+            tma_load_2d(smem + L::V_OFF + st * L::KV_TILE + L::KV_TAIL_OFF, &tmVt, &v_full[st],
+                        U.g * D + L::ATOMS * 64, kv_row0 + j * BN);
+        }
       }
     }
   } else if (warp == 1) {
@@ -264,89 +434,116 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       const uint32_t q_addr = smem_u32(smem + L::Q_OFF);
       const uint32_t k_addr = smem_u32(smem + L::K_OFF);
       const uint32_t v_addr = smem_u32(smem + L::V_OFF);
-      int n_s[2] = {0, 0};   // S tiles issued per slot
-      int n_pv[2] = {0, 0};  // P·V issued per slot
-      bool ok = mbar_wait(q_full, 0, p.err, abort_flag);
-      // S = Q K_j^T for every slot that sees tile j, into its next S buffer.
-      auto issue_s = [&](int j) -> bool {
-        const int jl = j - J0, st = jl % KV_STAGES;
-        if (!mbar_wait(&k_full[st], (jl / KV_STAGES) & 1, p.err, abort_flag)) return false;
-        tc_fence_after();
+      int n_s[2] = {0, 0};    // S tiles issued per slot (all items)
+      int n_pv[2] = {0, 0};   // P·V issued per slot (all items)
+      int n_out[2] = {0, 0};  // items whose O the slot's softmax warps have taken out
+      int kv_base = 0;        // K/V ring position of the item's first tile
+      bool ok = true;
+      for (int k = 0; ok && w.next(p, item); ++k) {
+        int rlo[2], rhi[2];
         for (int s = 0; s < 2; ++s) {
-          if (!(sl[s].lo <= j && j <= sl[s].hi)) continue;
-          const int b = n_s[s] & 1;
-          if (n_s[s] >= 2) {  // the P·V that read this buffer two tiles ago has retired
-            if (!mbar_wait(&s_free[2 * s + b], ((n_s[s] >> 1) - 1) & 1, p.err, abort_flag)) return false;
-            tc_fence_after();
-          }
-          const uint32_t d_tmem = tmem_base + s * 256 + b * 64;
-#pragma unroll
-          for (int ks = 0; ks < L::ATOMS * 4; ++ks) {
-            const uint32_t qo = (ks >> 2) * L::Q_ATOM + (ks & 3) * 32;
-            const uint32_t ko = (ks >> 2) * L::KV_ATOM + (ks & 3) * 32;
-            umma_f16_ss(d_tmem, desc_kmajor_sw128(q_addr + s * L::Q_TILE + qo),
-                        desc_kmajor_sw128(k_addr + st * L::KV_TILE + ko), idesc_s, ks > 0);
-          }
-          if (L::TAIL) {  // the 16-column tail: one K step on 32-B-swizzled rows
-            umma_f16_ss(d_tmem, desc_kmajor_sw32(q_addr + s * L::Q_TILE + L::Q_TAIL_OFF),
-                        desc_kmajor_sw32(k_addr + st * L::KV_TILE + L::KV_TAIL_OFF), idesc_s, 1u);
-          }
-          umma_commit(&s_full[2 * s + b]);
-          ++n_s[s];
+          const bool act = s == 0 || item.U.act1;
+          rlo[s] = act ? max(item.ja, item.U.sl[s].lo) : 1;
+          rhi[s] = act ? min(item.jb, item.U.sl[s].hi) : 0;
         }
-        umma_commit(&k_empty[st]);
-        return true;
-      };
-      // O += P_j V_j for every slot that sees tile j.
-      auto issue_pv = [&](int j) -> bool {
-        const int jl = j - J0, st = jl % KV_STAGES;
-        if (!mbar_wait(&v_full[st], (jl / KV_STAGES) & 1, p.err, abort_flag)) return false;
-        tc_fence_after();
-        for (int s = 0; s < 2; ++s) {
-          if (!(sl[s].lo <= j && j <= sl[s].hi)) continue;
-          const int b = n_pv[s] & 1;
-          if (!mbar_wait(&p_full[2 * s + b], (n_pv[s] >> 1) & 1, p.err, abort_flag)) return false;
+        bool first_pv[2] = {true, true};
+        ok = mbar_wait(q_full, k & 1, p.err, abort_flag);
+        // S = Q K_j^T for every slot that sees tile j, into its next S buffer.
+        auto issue_s = [&](int j) -> bool {
+          const int jl = kv_base + j - item.ja, st = jl % KV_STAGES;
+          if (!mbar_wait(&k_full[st], (jl / KV_STAGES) & 1, p.err, abort_flag)) return false;
           tc_fence_after();
-          const uint32_t o_tmem = tmem_base + s * 256 + 128;
-          const uint32_t p_tmem = tmem_base + s * 256 + b * 64;
-#pragma unroll
-          for (int ks = 0; ks < BN / 16; ++ks) {
-            const uint32_t acc = (n_pv[s] > 0 || ks > 0) ? 1u : 0u;
-            const uint64_t vd = desc_mnmajor_sw128(v_addr + st * L::KV_TILE + ks * 2048, L::KV_ATOM, 1024);
-            umma_f16_ts(o_tmem, p_tmem + ks * 8, vd, idesc_o, acc);
-            if (L::TAIL) {  // O columns [64*ATOMS, D) from the tail atom (16 key rows = 512 B)
-              const uint64_t vt = desc_mnmajor_sw32(v_addr + st * L::KV_TILE + L::KV_TAIL_OFF + ks * 512);
-              umma_f16_ts(o_tmem + L::ATOMS * 64, p_tmem + ks * 8, vt, idesc_ot, acc);
+          for (int s = 0; s < 2; ++s) {
+            if (!(rlo[s] <= j && j <= rhi[s])) continue;
+            const int b = n_s[s] & 1;
+            if (n_s[s] >= 2) {  // the P·V that read this buffer two tiles ago has retired
+              if (!mbar_wait(&s_free[2 * s + b], ((n_s[s] >> 1) - 1) & 1, p.err, abort_flag)) return false;
+              tc_fence_after();
             }
+            const uint32_t d_tmem = tmem_base + s * 256 + b * 64;
+#pragma unroll
+            for (int ks = 0; ks < L::ATOMS * 4; ++ks) {
+              const uint32_t qo = (ks >> 2) * L::Q_ATOM + (ks & 3) * 32;
+              const uint32_t ko = (ks >> 2) * L::KV_ATOM + (ks & 3) * 32;
+              umma_f16_ss(d_tmem, desc_kmajor_sw128(q_addr + s * L::Q_TILE + qo),
+                          desc_kmajor_sw128(k_addr + st * L::KV_TILE + ko), idesc_s, ks > 0);
+            }
+            if (L::TAIL) {  // the 16-column tail: one K step on 32-B-swizzled rows
+              umma_f16_ss(d_tmem, desc_kmajor_sw32(q_addr + s * L::Q_TILE + L::Q_TAIL_OFF),
+                          desc_kmajor_sw32(k_addr + st * L::KV_TILE + L::KV_TAIL_OFF), idesc_s, 1u);
+            }
+            umma_commit(&s_full[2 * s + b]);
+            ++n_s[s];
           }
-          umma_commit(&s_free[2 * s + b]);
-          umma_commit(&o_done[s]);
-          ++n_pv[s];
+          umma_commit(&k_empty[st]);
+          if (j == item.jb) umma_commit(q_empty);  // every S of this item issued
+          return true;
+        };
+        // O += P_j V_j for every slot that sees tile j.
+        auto issue_pv = [&](int j) -> bool {
+          const int jl = kv_base + j - item.ja, st = jl % KV_STAGES;
+          if (!mbar_wait(&v_full[st], (jl / KV_STAGES) & 1, p.err, abort_flag)) return false;
+          tc_fence_after();
+          for (int s = 0; s < 2; ++s) {
+            if (!(rlo[s] <= j && j <= rhi[s])) continue;
+            if (first_pv[s] && n_out[s] > 0) {
+              // O is overwritten: the previous item's O must have been read out.
+              if (!mbar_wait(&o_free[s], (n_out[s] - 1) & 1, p.err, abort_flag)) return false;
+              tc_fence_after();
+            }
+            const int b = n_pv[s] & 1;
+            if (!mbar_wait(&p_full[2 * s + b], (n_pv[s] >> 1) & 1, p.err, abort_flag)) return false;
+            tc_fence_after();
+            const uint32_t o_tmem = tmem_base + s * 256 + 128;
+            const uint32_t p_tmem = tmem_base + s * 256 + b * 64;
+#pragma unroll
+            for (int ks = 0; ks < BN / 16; ++ks) {
+              const uint32_t acc = (!first_pv[s] || ks > 0) ? 1u : 0u;
+              const uint64_t vd = desc_mnmajor_sw128(v_addr + st * L::KV_TILE + ks * 2048, L::KV_ATOM, 1024);
+              umma_f16_ts(o_tmem, p_tmem + ks * 8, vd, idesc_o, acc);
+              if (L::TAIL) {  // O columns [64*ATOMS, D) from the tail atom (16 key rows = 512 B)
+                const uint64_t vt = desc_mnmajor_sw32(v_addr + st * L::KV_TILE + L::KV_TAIL_OFF + ks * 512);
+                umma_f16_ts(o_tmem + L::ATOMS * 64, p_tmem + ks * 8, vt, idesc_ot, acc);
+              }
+            }
+            umma_commit(&s_free[2 * s + b]);
+            umma_commit(&o_done[s]);
+            ++n_pv[s];
+            first_pv[s] = false;
+          }
+          umma_commit(&v_empty[st]);
+          return true;
+        };
+        if (ok) ok = issue_s(item.ja);
+        for (int j = item.ja; ok && j <= item.jb; ++j) {
+          if (j < item.jb) ok = issue_s(j + 1);
+          if (ok) ok = issue_pv(j);
         }
-        umma_commit(&v_empty[st]);
-        return true;
-      };
-      if (ok) ok = issue_s(J0);
-      for (int j = J0; ok && j <= J1; ++j) {
-        if (j < J1) ok = issue_s(j + 1);
-        if (ok) ok = issue_pv(j);
+        for (int s = 0; s < 2; ++s)
+          if (rlo[s] <= rhi[s]) ++n_out[s];
+        kv_base += item.jb - item.ja + 1;
       }
     }
   } else if (warp >= kSoftWarp0) {
     // ------------------------------------------------------------ softmax
     const int s = (warp - kSoftWarp0) >> 2;
-    const int quarter = warp & 3;
+    const int quarter = warp & 3;  // TMEM lanes 32*(warp % 4): each slot's four warps cover all 128
     const int row = quarter * 32 + lane;
-    const SlotInfo me = s == 0 ? sl[0] : sl[1];  // no runtime index into sl[]
-    if (me.lo <= me.hi) {
-      const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
-      const uint32_t o_col = s * 256 + 128;
+    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+    const uint32_t o_col = s * 256 + 128;
+    int it = 0;      // tiles this slot has processed (all items): S buffer / barrier phases
+    int n_part = 0;  // split parts this slot has published
+    bool ok = true;
+    while (ok && w.next(p, item)) {
+      const Unit& U = item.U;
+      if (s == 1 && !U.act1) continue;
+      const SlotInfo me = s == 0 ? U.sl[0] : U.sl[1];  // no runtime index into sl[]
+      const int lo = max(item.ja, me.lo), hi = min(item.jb, me.hi);
       const int qa = p.q_off + me.qt * BM + row;  // absolute query position
       const int qa_min = p.q_off + me.qt * BM, qa_max = qa_min + BM - 1;
       float m_used = -INFINITY, l = 0.0f;
-      int it = 0;
-      bool ok = true;
-      for (int j = me.lo; j <= me.hi; ++j, ++it) {
+      for (int j = lo; j <= hi; ++j, ++it) {
+        const bool first_tile = j == lo;
         const int b = it & 1;
         const uint32_t s_col = s * 256 + b * 64;
         if (!__all_sync(0xffffffffu, mbar_wait(&s_full[2 * s + b], (it >> 1) & 1, p.err, abort_flag))) {
@@ -356,15 +553,15 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         tc_fence_after();
         float x[BN];
         {
-          uint32_t r[32];
-          tmem_ld32(lane_base + s_col, r);
+          uint32_t r0[32], r1[32];
+          tmem_ld32(lane_base + s_col, r0);
+          tmem_ld32(lane_base + s_col + 32, r1);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) x[i] = __uint_as_float(r[i]);
-          tmem_ld32(lane_base + s_col + 32, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) x[32 + i] = __uint_as_float(r[i]);
+          for (int i = 0; i < 32; ++i) {
+            x[i] = __uint_as_float(r0[i]);
+            x[32 + i] = __uint_as_float(r1[i]);
+          }
         }
         if (SOFTCAP) {
           // s = softcap * tanh(s*scale / softcap), then back to "raw" units so
@@ -398,8 +595,17 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         // (masked real keys score exactly the clamp).
         float mraw = -INFINITY;
         if (interior) {
+          // eight independent chains, then a short tree (a single 32-deep
+          // max3 chain is latency-bound)
+          float m8[8];
 #pragma unroll
-          for (int i = 0; i < BN; i += 2) mraw = max3(mraw, x[i], x[i + 1]);
+          for (int q = 0; q < 8; ++q) m8[q] = fmaxf(x[q], x[q + 8]);
+#pragma unroll
+          for (int i = 16; i < BN; i += 16) {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) m8[q] = max3(m8[q], x[i + q], x[i + 8 + q]);
+          }
+          mraw = fmaxf(max3(m8[0], m8[1], m8[2]), max3(m8[3], m8[4], fmaxf(m8[5], max3(m8[6], m8[7], m8[0]))));
         } else {
 #pragma unroll
           for (int i = 0; i < BN; ++i) mraw = fmaxf(mraw, ((vis >> i) & 1) ? x[i] : -INFINITY);
@@ -409,7 +615,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         // Lazy rescale of the exponent base.
         float alpha = 1.0f;
         bool need = false;
-        if (it == 0) {
+        if (first_tile) {
           m_used = mt;
         } else if (mt > m_used + kRescaleThresh) {
           alpha = fast_exp2(m_used - mt);
@@ -418,7 +624,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         }
         const bool fast = __all_sync(0xffffffffu, m_used >= kClamp2 + kFastMargin);
         const float c = p.scale_log2, nm = -m_used;
-        float rowsum = 0.0f;
+        float rs[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};  // partial row sums
         uint32_t pk[BN / 2];
         if (fast) {
 #pragma unroll
@@ -429,7 +635,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
               p0 = ((vis >> i) & 1) ? p0 : 0.0f;
               p1 = ((vis >> (i + 1)) & 1) ? p1 : 0.0f;
             }
-            rowsum += p0 + p1;
+            rs[(i >> 1) & 7] += p0 + p1;
             pk[i / 2] = pack2<BF16>(p0, p1);
           }
         } else {
@@ -441,19 +647,20 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             if (!((vis >> i) & 1)) y0 = ((real >> i) & 1) ? kClamp2 : -INFINITY;
             if (!((vis >> (i + 1)) & 1)) y1 = ((real >> (i + 1)) & 1) ? kClamp2 : -INFINITY;
             const float p0 = fast_exp2(y0 + nm), p1 = fast_exp2(y1 + nm);
-            rowsum += p0 + p1;
+            rs[(i >> 1) & 7] += p0 + p1;
             pk[i / 2] = pack2<BF16>(p0, p1);
           }
         }
+        const float rowsum = ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
         l = l * alpha + rowsum;
         // O may only be rescaled once the previous P·V of this slot has
         // retired. The wait is unambiguous whenever it is taken: S(j) was
         // committed after P·V(j-2) was issued, so at this point P·V(j-2) has
         // completed and P·V(j) is not yet issued, i.e. o_done has completed
-        // exactly j-1 or j phases. On the slot's last tile the wait is always
+        // exactly it-1 or it phases. On the item's last tile the wait is always
         // taken so that the epilogue's wait for the final P·V is unambiguous too.
         const bool need_any = __any_sync(0xffffffffu, need);
-        if (it > 0 && (need_any || j == me.hi)) {
+        if (!first_tile && (need_any || j == hi)) {
           if (!__all_sync(0xffffffffu, mbar_wait(&o_done[s], (it - 1) & 1, p.err, abort_flag))) {
             ok = false;
             break;
@@ -488,31 +695,152 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[2 * s + b]);
       }
-      // Epilogue: wait for the last P·V, normalise, store.
-      if (ok && __all_sync(0xffffffffu, mbar_wait(&o_done[s], (it - 1) & 1, p.err, abort_flag))) {
+      if (!ok) break;
+      const bool has = lo <= hi;
+      // Wait for the item's last P·V.
+      if (has) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&o_done[s], (it - 1) & 1, p.err, abort_flag))) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
+      }
+      const int qrow = me.qt * BM + row;
+      uint16_t* out_row = reinterpret_cast<uint16_t*>(p.out) +
+                          static_cast<int64_t>(U.b * p.n_q + qrow) * p.ldo + me.head * p.d_out;
+      // Normalised store of one 32-column chunk.
+      auto store_chunk = [&](int c0, const float (&v)[32], float inv_l) {
+        if (qrow >= p.n_q) return;
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk[i] = pack2<BF16>(v[2 * i] * inv_l, v[2 * i + 1] * inv_l);
+        uint4* dst = reinterpret_cast<uint4*>(out_row + c0);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (c0 + 8 * i + 8 <= p.d_out)  // 8-column groups of the real head width
+            dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+      };
+      if (item.full) {
         const float inv_l = 1.0f / l;
-        const int qrow = me.qt * BM + row;
-        uint32_t r[32];
 #pragma unroll
         for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t r[32];
           tmem_ld32(lane_base + o_col + c0, r);
           tmem_wait_ld();
-          if (qrow < p.n_q) {
-            uint32_t pk[16];
+          float v[32];
 #pragma unroll
-            for (int i = 0; i < 16; ++i)
-              pk[i] = pack2<BF16>(__uint_as_float(r[2 * i]) * inv_l,
-                                  __uint_as_float(r[2 * i + 1]) * inv_l);
-            uint4* dst = reinterpret_cast<uint4*>(
-                reinterpret_cast<uint16_t*>(p.out) + static_cast<int64_t>(q_row0 + qrow) * p.ldo +
-                me.head * p.d_out + c0);
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+          store_chunk(c0, v, inv_l);
+        }
+      } else {
+        // Part of a unit split over CTAs c_first..c_last: publish (O, m, l);
+        // the last part to arrive merges every part's record in CTA order.
+        const long long tpos = static_cast<long long>(item.pre) + p.item_cost;  // tile 0's position
+        const int c_first = split_cta(p, tpos), c_last = split_cta(p, tpos + U.len - 1);
+        float* rec = record<D>(p, blockIdx.x, item.first ? 0 : 1, s);
+        if (has) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              if (c0 + 8 * i + 8 <= p.d_out)  // 8-column groups of the real head width
-                dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+          for (int c0 = 0; c0 < D; c0 += 32) {
+            uint32_t r[32];
+            tmem_ld32(lane_base + o_col + c0, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int q4 = c0 / 4 + i;
+              if (4 * q4 + 4 <= D)
+                __stcg(reinterpret_cast<float4*>(rec) + q4 * BM + row,
+                       make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                   __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3])));
+            }
           }
         }
+        __stcg(rec + BM * D + row, has ? m_used : -INFINITY);
+        __stcg(rec + BM * D + BM + row, has ? l : 0.0f);
+        __threadfence();
+        // The slot's four warps have published; one thread counts the part in.
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&pub_bar[s]);
+        if (row == 0) {
+          bool okp = mbar_wait(&pub_bar[s], n_part & 1, p.err, abort_flag);
+          int last = 0;
+          if (okp) {
+            int* cnt = p.cnt + 2 * item.u + s;
+            const int parts = c_last - c_first + 1;
+            const int old = atomicAdd(cnt, 1);
+            last = old == parts - 1;
+            if (last) atomicExch(cnt, 0);  // ready for the next launch
+          }
+          last_flag[s] = last;
+          mbar_arrive(&dec_bar[s]);
+        }
+        if (!__all_sync(0xffffffffu, mbar_wait(&dec_bar[s], n_part & 1, p.err, abort_flag))) {
+          ok = false;
+          break;
+        }
+        ++n_part;
+        if (last_flag[s]) {
+          __threadfence();
+          // One pass over the parts in CTA order with a running max (the
+          // result does not depend on which part arrived last), GC columns
+          // at a time.
+          constexpr int GC = (D % 64 == 0) ? 64 : 32;
+#pragma unroll 1
+          for (int g0 = 0; g0 < D; g0 += GC) {
+            float acc[GC];
+#pragma unroll
+            for (int i = 0; i < GC; ++i) acc[i] = 0.0f;
+            float M = -INFINITY, Lsum = 0.0f;
+            for (int cc = c_first; cc <= c_last; ++cc) {
+              // u is CTA cc's first item unless an earlier unit's tiles precede it there
+              const int rr = (cc == c_first && split_begin(p, cc) < item.pre) ? 1 : 0;
+              const float* rc = record<D>(p, cc, rr, s);
+              const float mc = __ldcg(rc + BM * D + row), lc = __ldcg(rc + BM * D + BM + row);
+              float v[GC];
+              if (cc == static_cast<int>(blockIdx.x)) {  // this CTA's part: still in TMEM
+                if (!has) continue;
+#pragma unroll
+                for (int h = 0; h < GC; h += 32) {
+                  uint32_t r[32];
+                  tmem_ld32(lane_base + o_col + g0 + h, r);
+                  tmem_wait_ld();
+#pragma unroll
+                  for (int i = 0; i < 32; ++i) v[h + i] = __uint_as_float(r[i]);
+                }
+              } else {
+                const float4* src = reinterpret_cast<const float4*>(rc) + (g0 / 4) * BM + row;
+#pragma unroll
+                for (int i = 0; i < GC / 4; ++i) {
+                  float4 v4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                  if (g0 + 4 * i + 4 <= D) v4 = __ldcg(src + i * BM);
+                  v[4 * i] = v4.x;
+                  v[4 * i + 1] = v4.y;
+                  v[4 * i + 2] = v4.z;
+                  v[4 * i + 3] = v4.w;
+                }
+              }
+              if (!(lc > 0.0f)) continue;  // a part without keys for this slot
+              const float Mn = fmaxf(M, mc);
+              const float a = fast_exp2(M - Mn), wc = fast_exp2(mc - Mn);
+#pragma unroll
+              for (int i = 0; i < GC; ++i) acc[i] = fmaf(wc, v[i], acc[i] * a);
+              Lsum = fmaf(wc, lc, Lsum * a);
+              M = Mn;
+            }
+            const float inv_l = 1.0f / Lsum;
+#pragma unroll
+            for (int h = 0; h < GC; h += 32) {
+              float o32[32];
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o32[i] = acc[h + i];
+              if (g0 + h < D) store_chunk(g0 + h, o32, inv_l);
+            }
+          }
+        }
+      }
+      if (has) {  // O has been read: the next item's first P·V may overwrite it
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&o_free[s]);
       }
     }
   }
@@ -527,7 +855,8 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
 }
 
 template <int D, bool BF16, bool SOFTCAP>
-static int launch_impl(const CUtensorMap* tm, const Params& p, dim3 grid, cudaStream_t stream) {
+static int launch_impl(const CUtensorMap* tm, const Params& p, const SplitPlan& plan, dim3 grid,
+                       cudaStream_t stream) {
   static uint64_t configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -538,20 +867,25 @@ static int launch_impl(const CUtensorMap* tm, const Params& p, dim3 grid, cudaSt
     configured |= 1ull << (dev & 63);
   }
   attn_kernel<D, BF16, SOFTCAP><<<grid, kThreads, Smem<D>::BYTES, stream>>>(tm[0], tm[1], tm[2], tm[3],
-                                                                          tm[4], tm[5], p);
-  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
+                                                                          tm[4], tm[5], p, plan);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return report_error(RB_E_DEVICE, cudaGetErrorString(e));
+  return RB_OK;
 }
 
 template <int D>
-static int launch_d(const CUtensorMap* tm, const Params& p, dim3 grid, bool bf16, cudaStream_t stream) {
+static int launch_d(const CUtensorMap* tm, const Params& p, const SplitPlan& plan, dim3 grid, bool bf16,
+                    cudaStream_t stream) {
   if (p.softcap != 0.0f)
-    return bf16 ? launch_impl<D, true, true>(tm, p, grid, stream)
-                : launch_impl<D, false, true>(tm, p, grid, stream);
-  return bf16 ? launch_impl<D, true, false>(tm, p, grid, stream)
-              : launch_impl<D, false, false>(tm, p, grid, stream);
+    return bf16 ? launch_impl<D, true, true>(tm, p, plan, grid, stream)
+                : launch_impl<D, false, true>(tm, p, plan, grid, stream);
+  return bf16 ? launch_impl<D, true, false>(tm, p, plan, grid, stream)
+              : launch_impl<D, false, false>(tm, p, plan, grid, stream);
 }
 
 }  // namespace attn
+
+int set_attention_split(int policy) { return attn::g_split_policy.exchange(policy); }
 
 int launch_attention(const CUtensorMap* tm, const AttnLaunch& L, cudaStream_t stream) {
   using namespace attn;
@@ -570,6 +904,7 @@ int launch_attention(const CUtensorMap* tm, const AttnLaunch& L, cudaStream_t st
   p.softcap = L.softcap;
   p.err = L.err;
   p.d_out = L.d_out;
+  p.batch = L.batch > 0 ? L.batch : 1;
   // Mask band in relative coordinates (key - query).
   auto clampw = [](int64_t w) { return static_cast<int>(w > (kNoBound / 2) ? (kNoBound / 2) : w); };
   p.dlo = -kNoBound;
@@ -606,11 +941,84 @@ int launch_attention(const CUtensorMap* tm, const AttnLaunch& L, cudaStream_t st
     default:
       return RB_E_SHAPE;
   }
-  const dim3 grid(p.pairs_per_group * L.n_kv_heads, L.batch > 0 ? L.batch : 1);
+  const long long units = static_cast<long long>(p.pairs_per_group) * L.n_kv_heads * p.batch;
+  if (units <= 0 || units > (1ll << 30)) return RB_E_SHAPE;
+  p.n_units = static_cast<int>(units);
+  p.split = 0;
+  // Split mode: the units' key tiles, concatenated, are cut into G equal
+  // ranges, one per SM, so the last wave does not leave SMs idle; a unit cut
+  // by a range boundary is finished by whichever of its parts arrives last.
+  // A unit's length depends only on its slot pair (not on KV head or
+  // sequence): units come in blocks of batch * n_kv_heads of one length.
+  SplitPlan plan{};
+  const int policy = g_split_policy.load();
+  if (policy != RB_ATTN_SPLIT_NEVER && L.ws_rec && L.ws_cnt && units <= kAttnMaxUnits && L.num_sms > 0) {
+    // A unit's length depends only on its slot pair (not on KV head or
+    // sequence): units come in blocks of batch * n_kv_heads of one pair.
+    const int blk = p.batch * L.n_kv_heads;
+    const int P = p.pairs_per_group;
+    std::vector<int> plen(P);  // key tiles of the units of slot pair `pair`
+    for (int pair = 0; pair < P; ++pair) {
+      p.split = 0;  // one-CTA-per-unit order: block t holds pair P-1-t
+      plen[pair] = std::max(0, unit_info(p, (P - 1 - pair) * blk).len);
+    }
+    p.split = 1;  // split-mode order (heavy and light pairs alternate)
+    std::vector<long long> bcost(P), bpre(P);
+    long long W = 0;
+    for (int t = 0; t < P; ++t) {
+      const int pair = (t & 1) ? t / 2 : P - 1 - t / 2;
+      bcost[t] = plen[pair] > 0 ? kItemCost + plen[pair] : 0;  // per unit of block t
+      bpre[t] = W;
+      W += blk * bcost[t];
+    }
+    const int G = static_cast<int>(std::min<long long>(W, std::min(L.num_sms, kMaxCtas)));
+    bool use = W > 0 && W < (1ll << 30);
+    if (use && policy == RB_ATTN_SPLIT_AUTO) {
+      // Estimated finish time, in key tiles, of the one-CTA-per-unit greedy
+      // schedule (heaviest first onto the first free SM) against the split.
+      const double split_t = static_cast<double>(W) / G + kMergeCost;
+      if (units <= 4 * 65536) {
+        std::priority_queue<long long, std::vector<long long>, std::greater<long long>> sm;
+        for (int i = 0; i < L.num_sms; ++i) sm.push(0);
+        for (int pair = P - 1; pair >= 0; --pair)
+          for (int i = 0; i < blk; ++i) {
+            const long long t0 = sm.top();
+            sm.pop();
+            sm.push(t0 + plen[pair] + kCtaCost);
+          }
+        long long greedy = 0;
+        while (!sm.empty()) {
+          greedy = std::max(greedy, sm.top());
+          sm.pop();
+        }
+        use = split_t < 0.97 * static_cast<double>(greedy);
+      } else {
+        use = false;  // many units: the greedy schedule's last wave is short
+      }
+    }
+    p.split = 0;
+    if (use) {
+      p.split = 1;
+      p.W = static_cast<int>(W);
+      p.G = G;
+      p.item_cost = kItemCost;
+      p.rec = L.ws_rec;
+      p.cnt = L.ws_cnt;
+      int t = 0;
+      for (int c = 0; c < G; ++c) {
+        const long long b0 = static_cast<long long>(c) * W / G;
+        while (t + 1 < P && bpre[t] + blk * bcost[t] <= b0) ++t;
+        const long long i = (b0 - bpre[t]) / bcost[t];  // bcost[t] > 0: position b0 lies in block t
+        plan.u0[c] = static_cast<int>(t * blk + i);
+        plan.pre0[c] = static_cast<int>(bpre[t] + i * bcost[t]);
+      }
+    }
+  }
+  const dim3 grid(p.split ? p.G : p.n_units);
   const bool bf16 = L.dtype == RB_DTYPE_BF16;
-  if (L.head_dim == 128) return launch_d<128>(tm, p, grid, bf16, stream);
-  if (L.head_dim == 64) return launch_d<64>(tm, p, grid, bf16, stream);
-  if (L.head_dim == 80) return launch_d<80>(tm, p, grid, bf16, stream);
+  if (L.head_dim == 128) return launch_d<128>(tm, p, plan, grid, bf16, stream);
+  if (L.head_dim == 64) return launch_d<64>(tm, p, plan, grid, bf16, stream);
+  if (L.head_dim == 80) return launch_d<80>(tm, p, plan, grid, bf16, stream);
   return RB_E_UNSUPPORTED;
 }
 

@@ -41,6 +41,7 @@ struct GemmPlan {
 GemmPlan gemm_plan(bool i8, int M, int N, int K, int num_sms);
 // Restricts gemm_plan to single-CTA or (preferably) pair tiles; returns the old policy.
 int set_gemm_policy(int policy);
+int set_attention_split(int policy);  // RB_ATTN_SPLIT_*; returns the previous one
 // Q8_0: tmA = f16 activations [M, K] (box 64 x a_rows(), 128-B swizzle);
 // tmCodes = codes [N, K] (box 64 x weight_rows()); tmScales = f16 scales
 // [K/32, N] (box weight_rows() x 2); tmC = output map (box 32 rows x 128 B,
@@ -99,6 +100,14 @@ int launch_q8_0_unpack_blocks(const uint8_t* blocks, int64_t n, int64_t k, int64
                               int8_t* codes, uint16_t* scales, cudaStream_t stream);
 
 // Attention (attention.cu).
+// Attention split-mode workspace bounds: partial-result records for up to
+// kAttnMaxCtas CTAs (head width <= 128) and arrival counters for up to
+// kAttnMaxUnits work units (query-slot pairs x KV heads x sequences).
+constexpr int kAttnMaxCtas = 160;
+constexpr int kAttnMaxUnits = 1 << 18;
+constexpr size_t kAttnRecBytes = static_cast<size_t>(kAttnMaxCtas) * 4 * (128 * 128 + 2 * 128) * sizeof(float);
+constexpr size_t kAttnCntBytes = static_cast<size_t>(kAttnMaxUnits) * 2 * sizeof(int);
+
 struct AttnLaunch {
   const void* q;
   const void* k;
@@ -115,6 +124,8 @@ struct AttnLaunch {
   int64_t window, q_start, kv_start;
   uint32_t* err;
   int num_sms;
+  float* ws_rec;  // split-mode workspace (kAttnRecBytes), or null: one CTA per unit
+  int* ws_cnt;    // kAttnCntBytes, zeroed once; counters reset themselves
 };
 // tm[0..2]: Q, K, V maps of the 64-column atoms (128-B swizzle); tm[3..5]: the
 // 16-column tail maps (32-B swizzle) used when head_dim == 80.

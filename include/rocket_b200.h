@@ -338,6 +338,18 @@ RB_API int64_t rb_launch_count(int reset);
 #define RB_TILES_PAIR 2
 RB_API int rb_set_tile_policy(int policy);
 
+/* Attention work split for later attention calls (process-wide; no
+ * counterpart in the reference): RB_ATTN_SPLIT_AUTO compares, per call, a
+ * greedy one-CTA-per-unit schedule (unit = a KV head's pair of 128-row query
+ * slots) against one CTA per SM over equal shares of all key tiles, with units
+ * cut at share boundaries and merged by their last finishing part;
+ * RB_ATTN_SPLIT_NEVER / RB_ATTN_SPLIT_ALWAYS force one of them. Results agree
+ * within f32 summation order. Returns the previous policy, or RB_E_SHAPE. */
+#define RB_ATTN_SPLIT_AUTO 0
+#define RB_ATTN_SPLIT_NEVER 1
+#define RB_ATTN_SPLIT_ALWAYS 2
+RB_API int rb_set_attention_split(int policy);
+
 #ifdef __cplusplus
 }
 #endif

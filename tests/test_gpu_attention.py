@@ -64,6 +64,10 @@ CASES = [
     (150, 500, 4, 2, 128, 6, -1, 300, 0),
     (150, 400, 4, 2, 64, 6, 90, 300, 100),
     (64, 300, 2, 1, 128, 1, -1, 0, 0),
+    # one or two long units: each is cut over many CTAs and merged by the last part
+    (64, 4096, 2, 1, 128, 1, -1, 0, 0),
+    (200, 6000, 2, 2, 128, 1, -1, 0, 0),
+    (256, 9000, 2, 1, 64, 6, -1, 8744, 0),
     # head_dim 72 (staged as 80 = 64-column atom + 16-column tail)
     (1, 1, 2, 2, 72, 0, -1, 0, 0),
     (300, 300, 16, 16, 72, 0, -1, 0, 0),
@@ -72,12 +76,44 @@ CASES = [
 ]
 
 
+@pytest.fixture(params=["never", "always"])
+def split(rb, request):
+    """Both work schedules: one CTA per query-slot pair and KV head, and one
+    CTA per SM over equal key-tile shares with split units merged."""
+    old = rb.set_attention_split(request.param)
+    yield request.param
+    rb.set_attention_split(old)
+
+
 @pytest.mark.parametrize("case", CASES)
-def test_attention_matches_oracle(rb, orc, case):
+def test_attention_matches_oracle(rb, orc, case, split):
     n_q, n_kv, h, hkv, d, mode, window, q0, k0 = case
     got, ref = run_case(rb, orc, n_q, n_kv, h, hkv, d, mode, window, q0, k0, seed=sum(case[:5]))
     assert cosine(got, ref) >= COS_MIN, cosine(got, ref)
     assert max_rel(got, ref) <= MAX_REL, max_rel(got, ref)
+
+
+def test_attention_split_policy_contract(rb):
+    import burn_rocket_b200._lib as L
+    assert L.load().rb_set_attention_split(7) != 0
+    with pytest.raises(ValueError):
+        rb.set_attention_split("sometimes")
+
+
+def test_attention_split_units_deterministic(rb, orc, split):
+    """Units cut over CTAs merge in CTA order whichever part arrives last, and
+    the arrival counters reset themselves: repeated calls agree bit for bit."""
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(3)
+    n_q, n_kv, h, hkv, d = 200, 7000, 4, 2, 128
+    q = torch.randn(n_q, h * d, device="cuda", generator=g).half()
+    k = torch.randn(n_kv, hkv * d, device="cuda", generator=g).half()
+    v = torch.randn(n_kv, hkv * d, device="cuda", generator=g).half()
+    outs = [rb.attention_raw(q, k, v, h, hkv, d, 1.0 / math.sqrt(d), 0.0, 1, -1, 0, 0).clone() for _ in range(4)]
+    torch.cuda.synchronize()
+    rb.check_device_errors()
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
 
 
 def test_attention_softcap(rb, orc):
@@ -116,7 +152,7 @@ def torch_ref(q, k, v, h, hkv, d, causal):
 
 @pytest.mark.parametrize("causal", [True, False])
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])
-def test_attention_config2_full_size(rb, causal, dtype):
+def test_attention_config2_full_size(rb, causal, dtype, split):
     """BASELINE config #2: 3633 tokens, 16/8 heads x 128, causal and bidirectional."""
     import torch
     g = torch.Generator(device="cuda").manual_seed(7)
@@ -174,8 +210,8 @@ def test_attention_contract_errors(rb):
 @pytest.mark.parametrize("window", [None, 300])
 def test_chunked_causal_attention_matches_dense(rb, orc, window):
     """causal_attention (src/util/causal.rs:103-163) with 512-row chunks equals
-    the dense causal(-window) op: bit for bit for pure causal (same key tiles),
-    within tolerance with a window (the band start shifts the key tiling)."""
+    the dense causal(-window) op within tolerance (the chunked calls tile and
+    split the key range differently, so the f32 sums round differently)."""
     import torch
     from burn_rocket_b200.causal import causal_attention
     S, H, KV, D = 1500, 8, 2, 128
@@ -187,8 +223,7 @@ def test_chunked_causal_attention_matches_dense(rb, orc, window):
     dense = causal_attention(q, k, v, H, KV, D, scale, window=window, chunk=0)
     chunked = causal_attention(q, k, v, H, KV, D, scale, window=window, chunk=512)
     torch.cuda.synchronize()
-    if window is None:
-        assert torch.equal(dense, chunked)
-    else:
-        assert cosine(dense.float().cpu().numpy(), chunked.float().cpu().numpy()) >= 0.99999
+    a, b = dense.float().cpu().numpy(), chunked.float().cpu().numpy()
+    assert cosine(a, b) >= 0.99999
+    assert max_rel(b, a) <= 2e-3
     rb.check_device_errors()
