@@ -331,8 +331,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   uint64_t* v_full = k_empty + KV_STAGES;       // [KV_STAGES]
   uint64_t* v_empty = v_full + KV_STAGES;       // [KV_STAGES]
   uint64_t* s_full = v_empty + KV_STAGES;       // [slot][buf]
-  uint64_t* s_free = s_full + 4;                // [slot][buf]
-  uint64_t* p_full = s_free + 4;                // [slot][buf]
+  uint64_t* p_full = s_full + 4;                // [slot][buf]
   uint64_t* o_done = p_full + 4;                // [slot]
   uint64_t* q_empty = o_done + 2;               // [1]
   uint64_t* o_free = q_empty + 1;               // [slot]
@@ -356,7 +355,6 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     }
     for (int i = 0; i < 4; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 1);
       mbar_init(&p_full[i], 4);
     }
     for (int i = 0; i < 2; ++i) {
@@ -435,6 +433,11 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       const uint32_t k_addr = smem_u32(smem + L::K_OFF);
       const uint32_t v_addr = smem_u32(smem + L::V_OFF);
       int n_s[2] = {0, 0};    // S tiles issued per slot (all items)
+      // Base descriptors; each UMMA advances them by a constant byte offset.
+      const uint64_t q_desc = desc_kmajor_sw128(q_addr), k_desc = desc_kmajor_sw128(k_addr);
+      const uint64_t v_desc = desc_mnmajor_sw128(v_addr, L::KV_ATOM, 1024);
+      const uint64_t qt_desc = desc_kmajor_sw32(q_addr), kt_desc = desc_kmajor_sw32(k_addr);
+      const uint64_t vt_desc = desc_mnmajor_sw32(v_addr);
       int n_pv[2] = {0, 0};   // P·V issued per slot (all items)
       int n_out[2] = {0, 0};  // items whose O the slot's softmax warps have taken out
       int kv_base = 0;        // K/V ring position of the item's first tile
@@ -448,77 +451,101 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         }
         bool first_pv[2] = {true, true};
         ok = mbar_wait(q_full, k & 1, p.err, abort_flag);
-        // S = Q K_j^T for every slot that sees tile j, into its next S buffer.
-        auto issue_s = [&](int j) -> bool {
-          const int jl = kv_base + j - item.ja, st = jl % KV_STAGES;
-          if (!mbar_wait(&k_full[st], (jl / KV_STAGES) & 1, p.err, abort_flag)) return false;
-          tc_fence_after();
-          for (int s = 0; s < 2; ++s) {
-            if (!(rlo[s] <= j && j <= rhi[s])) continue;
-            const int b = n_s[s] & 1;
-            if (n_s[s] >= 2) {  // the P·V that read this buffer two tiles ago has retired
-              if (!mbar_wait(&s_free[2 * s + b], ((n_s[s] >> 1) - 1) & 1, p.err, abort_flag)) return false;
-              tc_fence_after();
-            }
-            const uint32_t d_tmem = tmem_base + s * 256 + b * 64;
+        auto stage_of = [&](int j) { return (kv_base + j - item.ja) % KV_STAGES; };
+        auto phase_of = [&](int j) { return static_cast<uint32_t>(((kv_base + j - item.ja) / KV_STAGES) & 1); };
+        // S = Q K_j^T of slot s into its next S buffer. The buffer last held
+        // P(j-2), read by this slot's P·V(j-2), which this thread issued
+        // earlier: UMMAs issued by one thread execute in issue order, so the
+        // overwrite needs no wait.
+        auto issue_s = [&](int j, int s) {
+          const uint32_t st = stage_of(j);
+          const int b = n_s[s] & 1;
+          const uint32_t d_tmem = tmem_base + s * 256 + b * 64;
 #pragma unroll
-            for (int ks = 0; ks < L::ATOMS * 4; ++ks) {
-              const uint32_t qo = (ks >> 2) * L::Q_ATOM + (ks & 3) * 32;
-              const uint32_t ko = (ks >> 2) * L::KV_ATOM + (ks & 3) * 32;
-              umma_f16_ss(d_tmem, desc_kmajor_sw128(q_addr + s * L::Q_TILE + qo),
-                          desc_kmajor_sw128(k_addr + st * L::KV_TILE + ko), idesc_s, ks > 0);
-            }
-            if (L::TAIL) {  // the 16-column tail: one K step on 32-B-swizzled rows
-              umma_f16_ss(d_tmem, desc_kmajor_sw32(q_addr + s * L::Q_TILE + L::Q_TAIL_OFF),
-                          desc_kmajor_sw32(k_addr + st * L::KV_TILE + L::KV_TAIL_OFF), idesc_s, 1u);
-            }
-            umma_commit(&s_full[2 * s + b]);
-            ++n_s[s];
+          for (int ks = 0; ks < L::ATOMS * 4; ++ks) {
+            const uint32_t qo = (ks >> 2) * L::Q_ATOM + (ks & 3) * 32;
+            const uint32_t ko = (ks >> 2) * L::KV_ATOM + (ks & 3) * 32;
+            umma_f16_ss(d_tmem, desc_add(q_desc, s * L::Q_TILE + qo),
+                        desc_add(k_desc, st * L::KV_TILE + ko), idesc_s, ks > 0);
           }
-          umma_commit(&k_empty[st]);
-          if (j == item.jb) umma_commit(q_empty);  // every S of this item issued
+          if (L::TAIL) {  // the 16-column tail: one K step on 32-B-swizzled rows
+            umma_f16_ss(d_tmem, desc_add(qt_desc, s * L::Q_TILE + L::Q_TAIL_OFF),
+                        desc_add(kt_desc, st * L::KV_TILE + L::KV_TAIL_OFF), idesc_s, 1u);
+          }
+          umma_commit(&s_full[2 * s + b]);
+          ++n_s[s];
+        };
+        // After the last S that reads K tile j: release its stage (and Q after
+        // the item's last tile).
+        auto release_k = [&](int j) {
+          umma_commit(&k_empty[stage_of(j)]);
+          if (j == item.jb) umma_commit(q_empty);
+        };
+        // Both slots' S for tile j (the item's first two tiles).
+        auto issue_s_tile = [&](int j) -> bool {
+          if (!mbar_wait(&k_full[stage_of(j)], phase_of(j), p.err, abort_flag)) return false;
+          tc_fence_after();
+          for (int s = 0; s < 2; ++s)
+            if (rlo[s] <= j && j <= rhi[s]) issue_s(j, s);
+          release_k(j);
           return true;
         };
-        // O += P_j V_j for every slot that sees tile j.
-        auto issue_pv = [&](int j) -> bool {
-          const int jl = kv_base + j - item.ja, st = jl % KV_STAGES;
-          if (!mbar_wait(&v_full[st], (jl / KV_STAGES) & 1, p.err, abort_flag)) return false;
+        // Tile j: each slot's O += P_j V_j as soon as its P is ready, then the
+        // same slot's S for tile j + 2, so that one slot's late softmax does
+        // not hold back the other's next scores.
+        auto issue_tile = [&](int j) -> bool {
+          const uint32_t st = stage_of(j);
+          if (!mbar_wait(&v_full[st], phase_of(j), p.err, abort_flag)) return false;
           tc_fence_after();
+          const int j2 = j + 2;
+          bool k2_ready = false;
           for (int s = 0; s < 2; ++s) {
-            if (!(rlo[s] <= j && j <= rhi[s])) continue;
-            if (first_pv[s] && n_out[s] > 0) {
-              // O is overwritten: the previous item's O must have been read out.
-              if (!mbar_wait(&o_free[s], (n_out[s] - 1) & 1, p.err, abort_flag)) return false;
-              tc_fence_after();
-            }
-            const int b = n_pv[s] & 1;
-            if (!mbar_wait(&p_full[2 * s + b], (n_pv[s] >> 1) & 1, p.err, abort_flag)) return false;
-            tc_fence_after();
-            const uint32_t o_tmem = tmem_base + s * 256 + 128;
-            const uint32_t p_tmem = tmem_base + s * 256 + b * 64;
-#pragma unroll
-            for (int ks = 0; ks < BN / 16; ++ks) {
-              const uint32_t acc = (!first_pv[s] || ks > 0) ? 1u : 0u;
-              const uint64_t vd = desc_mnmajor_sw128(v_addr + st * L::KV_TILE + ks * 2048, L::KV_ATOM, 1024);
-              umma_f16_ts(o_tmem, p_tmem + ks * 8, vd, idesc_o, acc);
-              if (L::TAIL) {  // O columns [64*ATOMS, D) from the tail atom (16 key rows = 512 B)
-                const uint64_t vt = desc_mnmajor_sw32(v_addr + st * L::KV_TILE + L::KV_TAIL_OFF + ks * 512);
-                umma_f16_ts(o_tmem + L::ATOMS * 64, p_tmem + ks * 8, vt, idesc_ot, acc);
+            if (rlo[s] <= j && j <= rhi[s]) {
+              if (first_pv[s] && n_out[s] > 0) {
+                // O is overwritten: the previous item's O must have been read out.
+                if (!mbar_wait(&o_free[s], (n_out[s] - 1) & 1, p.err, abort_flag)) return false;
+                tc_fence_after();
               }
+              const int b = n_pv[s] & 1;
+              if (!mbar_wait(&p_full[2 * s + b], (n_pv[s] >> 1) & 1, p.err, abort_flag)) return false;
+              tc_fence_after();
+              const uint32_t o_tmem = tmem_base + s * 256 + 128;
+              const uint32_t p_tmem = tmem_base + s * 256 + b * 64;
+#pragma unroll
+              for (int ks = 0; ks < BN / 16; ++ks) {
+                const uint32_t acc = (!first_pv[s] || ks > 0) ? 1u : 0u;
+                const uint64_t vd = desc_add(v_desc, st * L::KV_TILE + ks * 2048);
+                umma_f16_ts(o_tmem, p_tmem + ks * 8, vd, idesc_o, acc);
+                if (L::TAIL) {  // O columns [64*ATOMS, D) from the tail atom (16 key rows = 512 B)
+                  const uint64_t vt = desc_add(vt_desc, st * L::KV_TILE + L::KV_TAIL_OFF + ks * 512);
+                  umma_f16_ts(o_tmem + L::ATOMS * 64, p_tmem + ks * 8, vt, idesc_ot, acc);
+                }
+              }
+              umma_commit(&o_done[s]);
+              ++n_pv[s];
+              first_pv[s] = false;
             }
-            umma_commit(&s_free[2 * s + b]);
-            umma_commit(&o_done[s]);
-            ++n_pv[s];
-            first_pv[s] = false;
+            if (j2 <= item.jb && rlo[s] <= j2 && j2 <= rhi[s]) {
+              if (!k2_ready) {
+                if (!mbar_wait(&k_full[stage_of(j2)], phase_of(j2), p.err, abort_flag)) return false;
+                tc_fence_after();
+                k2_ready = true;
+              }
+              issue_s(j2, s);
+            }
           }
           umma_commit(&v_empty[st]);
+          if (j2 <= item.jb) {
+            // A tile neither slot reads still has its load awaited before
+            // the stage is handed back.
+            if (!k2_ready && !mbar_wait(&k_full[stage_of(j2)], phase_of(j2), p.err, abort_flag)) return false;
+            release_k(j2);
+          }
           return true;
         };
-        if (ok) ok = issue_s(item.ja);
-        for (int j = item.ja; ok && j <= item.jb; ++j) {
-          if (j < item.jb) ok = issue_s(j + 1);
-          if (ok) ok = issue_pv(j);
-        }
+        if (ok) ok = issue_s_tile(item.ja);
+        if (ok && item.ja + 1 <= item.jb) ok = issue_s_tile(item.ja + 1);
+        for (int j = item.ja; ok && j <= item.jb; ++j) ok = issue_tile(j);
         for (int s = 0; s < 2; ++s)
           if (rlo[s] <= rhi[s]) ++n_out[s];
         kv_base += item.jb - item.ja + 1;
@@ -626,15 +653,23 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         const float c = p.scale_log2, nm = -m_used;
         float rs[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};  // partial row sums
         uint32_t pk[BN / 2];
-        if (fast) {
+        if (fast && interior) {  // the common case: no mask, no clamp
 #pragma unroll
           for (int i = 0; i < BN; i += 2) {
+            const float p0 = fast_exp2(fmaf(x[i], c, nm));
+            const float p1 = fast_exp2(fmaf(x[i + 1], c, nm));
+            rs[(i >> 1) & 7] += p0 + p1;
+            pk[i / 2] = pack2<BF16>(p0, p1);
+          }
+        } else if (fast) {
+          const uint32_t vlo = static_cast<uint32_t>(vis), vhi = static_cast<uint32_t>(vis >> 32);
+#pragma unroll
+          for (int i = 0; i < BN; i += 2) {
+            const uint32_t vw = i < 32 ? vlo : vhi;
             float p0 = fast_exp2(fmaf(x[i], c, nm));
             float p1 = fast_exp2(fmaf(x[i + 1], c, nm));
-            if (!interior) {
-              p0 = ((vis >> i) & 1) ? p0 : 0.0f;
-              p1 = ((vis >> (i + 1)) & 1) ? p1 : 0.0f;
-            }
+            p0 = ((vw >> (i & 31)) & 1) ? p0 : 0.0f;
+            p1 = ((vw >> ((i + 1) & 31)) & 1) ? p1 : 0.0f;
             rs[(i >> 1) & 7] += p0 + p1;
             pk[i / 2] = pack2<BF16>(p0, p1);
           }

@@ -420,6 +420,14 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes
   return d;
 }
 
+// A descriptor advanced by a 16-byte-aligned byte offset: the start address
+// sits in the low 14 bits of the low word (address >> 4), which stays in
+// range for any offset inside shared memory, so one 32-bit add suffices.
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t byte_off) {
+  const uint32_t lo = static_cast<uint32_t>(d) + (byte_off >> 4);
+  return (static_cast<uint64_t>(static_cast<uint32_t>(d >> 32)) << 32) | lo;
+}
+
 // K-major operand staged as 128-byte swizzled rows (TMA SWIZZLE_128B): rows are
 // 128 B apart, 8-row groups 1024 B apart. Advancing K inside the 128-byte atom
 // moves the start address by the K-step's byte width.
