@@ -622,17 +622,8 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         // (masked real keys score exactly the clamp).
         float mraw = -INFINITY;
         if (interior) {
-          // eight independent chains, then a short tree (a single 32-deep
-          // max3 chain is latency-bound)
-          float m8[8];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) m8[q] = fmaxf(x[q], x[q + 8]);
-#pragma unroll
-          for (int i = 16; i < BN; i += 16) {
-#pragma unroll
-            for (int q = 0; q < 8; ++q) m8[q] = max3(m8[q], x[i + q], x[i + 8 + q]);
-          }
-          mraw = fmaxf(max3(m8[0], m8[1], m8[2]), max3(m8[3], m8[4], fmaxf(m8[5], max3(m8[6], m8[7], m8[0]))));
+          for (int i = 0; i < BN; i += 2) mraw = max3(mraw, x[i], x[i + 1]);
         } else {
 #pragma unroll
           for (int i = 0; i < BN; ++i) mraw = fmaxf(mraw, ((vis >> i) & 1) ? x[i] : -INFINITY);
@@ -651,14 +642,14 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         }
         const bool fast = __all_sync(0xffffffffu, m_used >= kClamp2 + kFastMargin);
         const float c = p.scale_log2, nm = -m_used;
-        float rs[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};  // partial row sums
+        float rowsum = 0.0f;
         uint32_t pk[BN / 2];
         if (fast && interior) {  // the common case: no mask, no clamp
 #pragma unroll
           for (int i = 0; i < BN; i += 2) {
             const float p0 = fast_exp2(fmaf(x[i], c, nm));
             const float p1 = fast_exp2(fmaf(x[i + 1], c, nm));
-            rs[(i >> 1) & 7] += p0 + p1;
+            rowsum += p0 + p1;
             pk[i / 2] = pack2<BF16>(p0, p1);
           }
         } else if (fast) {
@@ -670,7 +661,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             float p1 = fast_exp2(fmaf(x[i + 1], c, nm));
             p0 = ((vw >> (i & 31)) & 1) ? p0 : 0.0f;
             p1 = ((vw >> ((i + 1) & 31)) & 1) ? p1 : 0.0f;
-            rs[(i >> 1) & 7] += p0 + p1;
+            rowsum += p0 + p1;
             pk[i / 2] = pack2<BF16>(p0, p1);
           }
         } else {
@@ -682,11 +673,10 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             if (!((vis >> i) & 1)) y0 = ((real >> i) & 1) ? kClamp2 : -INFINITY;
             if (!((vis >> (i + 1)) & 1)) y1 = ((real >> (i + 1)) & 1) ? kClamp2 : -INFINITY;
             const float p0 = fast_exp2(y0 + nm), p1 = fast_exp2(y1 + nm);
-            rs[(i >> 1) & 7] += p0 + p1;
+            rowsum += p0 + p1;
             pk[i / 2] = pack2<BF16>(p0, p1);
           }
         }
-        const float rowsum = ((rs[0] + rs[1]) + (rs[2] + rs[3])) + ((rs[4] + rs[5]) + (rs[6] + rs[7]));
         l = l * alpha + rowsum;
         // O may only be rescaled once the previous P·V of this slot has
         // retired. The wait is unambiguous whenever it is taken: S(j) was
