@@ -9,18 +9,22 @@
 // so a fully masked row averages the values of every key it iterates, as the
 // reference does.
 //
-// Design (one CTA = two 128-row query "slots" sharing one KV head):
+// Design (a work unit = two 128-row query "slots" sharing one KV head):
 //   * GQA: the two slots are two query heads of one KV group (or two query
 //     tiles of one head when the group has a single head), so every K/V tile
 //     is loaded by TMA once and consumed by both slots.
-//   * warp 0: TMA (Q once, then 4-stage K and V rings of 64-key tiles, 128-B
-//     swizzled); warp 1: UMMA issuer; warps 4-7 / 8-11: softmax of slot 0 /
-//     slot 1, one query row per thread (TMEM lane = row).
+//   * warp 0: TMA (Q per unit, then 4-stage K and V rings of 64-key tiles,
+//     128-B swizzled); warp 1: UMMA issuer; warps 2-5 / 6-9: softmax of slot 0
+//     / slot 1, one query row per thread (TMEM lane = row).
 //   * TMEM per slot (256 columns): two S buffers of 64 f32 columns and O in D
 //     columns. S(j+1) is computed into the other buffer while the softmax of
 //     tile j runs; P = exp2(S - m) is written back as packed f16/bf16 over the
 //     first 32 columns of its own S buffer and consumed by a TS-form UMMA
-//     (A from TMEM) O += P·V. The UMMA warp issues S(j+1) before P·V(j).
+//     (A from TMEM) O += P·V. Per slot the UMMA warp issues P·V(j) and then
+//     S(j+2) into the same buffer.
+//   * Schedules: one CTA per unit, or (split) one CTA per SM over an equal
+//     share of all units' key tiles, units cut at share boundaries being
+//     merged by whichever part finishes last (see launch_attention).
 //   * Online softmax in the log2 domain with a lazy rescale: the exponent base
 //     only moves (and O, l are rescaled) when a new row max exceeds it by more
 //     than 8 (a factor 256), so P stays within f16 range and O is rarely
@@ -244,9 +248,10 @@ struct Item {
 
 struct Walk {
   int u, pre, pos, end, k;
+  template <bool SPLIT>
   __device__ __forceinline__ void begin(const Params& p, const SplitPlan& plan) {
     k = 0;
-    if (p.split) {
+    if (SPLIT) {
       pos = split_begin(p, blockIdx.x);
       end = split_begin(p, blockIdx.x + 1);
       u = plan.u0[blockIdx.x];
@@ -258,8 +263,9 @@ struct Walk {
       end = -1;  // one whole unit
     }
   }
+  template <bool SPLIT>
   __device__ __forceinline__ bool next(const Params& p, Item& it) {
-    if (!p.split) {
+    if (!SPLIT) {
       if (end == 0 || u >= p.n_units) return false;
       end = 0;
       it.U = unit_info(p, u);
@@ -314,7 +320,9 @@ __device__ __forceinline__ float* record(const Params& p, int cta, int r, int s)
   return p.rec + (static_cast<size_t>(cta) * 4 + r * 2 + s) * REC;
 }
 
-template <int D, bool BF16, bool SOFTCAP>
+// SPLIT: the split schedule (Params::split != 0); the one-CTA-per-unit
+// instantiation compiles without the multi-item walk and partial records.
+template <int D, bool BF16, bool SOFTCAP, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
 attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
             const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmQt,
@@ -375,7 +383,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   Walk w;
-  w.begin(p, plan);
+  w.begin<SPLIT>(p, plan);
   Item item;
 
   if (warp == 0) {
@@ -386,7 +394,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       tma_prefetch_desc(&tmV);
       int kv_it = 0;  // K/V ring position, continued across items
       bool ok = true;
-      for (int k = 0; ok && w.next(p, item); ++k) {
+      for (int k = 0; ok && w.template next<SPLIT>(p, item); ++k) {
         const Unit& U = item.U;
         const int q_row0 = U.b * p.n_q, kv_row0 = U.b * p.n_kv;
         // The Q buffers are reused once every S of the previous item retired.
@@ -442,7 +450,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       int n_out[2] = {0, 0};  // items whose O the slot's softmax warps have taken out
       int kv_base = 0;        // K/V ring position of the item's first tile
       bool ok = true;
-      for (int k = 0; ok && w.next(p, item); ++k) {
+      for (int k = 0; ok && w.template next<SPLIT>(p, item); ++k) {
         int rlo[2], rhi[2];
         for (int s = 0; s < 2; ++s) {
           const bool act = s == 0 || item.U.act1;
@@ -561,7 +569,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     int it = 0;      // tiles this slot has processed (all items): S buffer / barrier phases
     int n_part = 0;  // split parts this slot has published
     bool ok = true;
-    while (ok && w.next(p, item)) {
+    while (ok && w.template next<SPLIT>(p, item)) {
       const Unit& U = item.U;
       if (s == 1 && !U.act1) continue;
       const SlotInfo me = s == 0 ? U.sl[0] : U.sl[1];  // no runtime index into sl[]
@@ -745,7 +753,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
           if (c0 + 8 * i + 8 <= p.d_out)  // 8-column groups of the real head width
             dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
       };
-      if (item.full) {
+      if (!SPLIT || item.full) {
         const float inv_l = 1.0f / l;
 #pragma unroll
         for (int c0 = 0; c0 < D; c0 += 32) {
@@ -879,33 +887,40 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   }
 }
 
-template <int D, bool BF16, bool SOFTCAP>
+template <int D, bool BF16, bool SOFTCAP, bool SPLIT>
 static int launch_impl(const CUtensorMap* tm, const Params& p, const SplitPlan& plan, dim3 grid,
                        cudaStream_t stream) {
   static uint64_t configured = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(configured & (1ull << (dev & 63)))) {
-    if (cudaFuncSetAttribute(attn_kernel<D, BF16, SOFTCAP>,
+    if (cudaFuncSetAttribute(attn_kernel<D, BF16, SOFTCAP, SPLIT>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, Smem<D>::BYTES) != cudaSuccess)
       return RB_E_DEVICE;
     configured |= 1ull << (dev & 63);
   }
-  attn_kernel<D, BF16, SOFTCAP><<<grid, kThreads, Smem<D>::BYTES, stream>>>(tm[0], tm[1], tm[2], tm[3],
+  attn_kernel<D, BF16, SOFTCAP, SPLIT><<<grid, kThreads, Smem<D>::BYTES, stream>>>(tm[0], tm[1], tm[2], tm[3],
                                                                           tm[4], tm[5], p, plan);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return report_error(RB_E_DEVICE, cudaGetErrorString(e));
   return RB_OK;
 }
 
+template <int D, bool SPLIT>
+static int launch_s(const CUtensorMap* tm, const Params& p, const SplitPlan& plan, dim3 grid, bool bf16,
+                    cudaStream_t stream) {
+  if (p.softcap != 0.0f)
+    return bf16 ? launch_impl<D, true, true, SPLIT>(tm, p, plan, grid, stream)
+                : launch_impl<D, false, true, SPLIT>(tm, p, plan, grid, stream);
+  return bf16 ? launch_impl<D, true, false, SPLIT>(tm, p, plan, grid, stream)
+              : launch_impl<D, false, false, SPLIT>(tm, p, plan, grid, stream);
+}
+
 template <int D>
 static int launch_d(const CUtensorMap* tm, const Params& p, const SplitPlan& plan, dim3 grid, bool bf16,
                     cudaStream_t stream) {
-  if (p.softcap != 0.0f)
-    return bf16 ? launch_impl<D, true, true>(tm, p, plan, grid, stream)
-                : launch_impl<D, false, true>(tm, p, plan, grid, stream);
-  return bf16 ? launch_impl<D, true, false>(tm, p, plan, grid, stream)
-              : launch_impl<D, false, false>(tm, p, plan, grid, stream);
+  return p.split ? launch_s<D, true>(tm, p, plan, grid, bf16, stream)
+                 : launch_s<D, false>(tm, p, plan, grid, bf16, stream);
 }
 
 }  // namespace attn
