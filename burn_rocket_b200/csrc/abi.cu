@@ -1268,6 +1268,29 @@ int rb_set_tile_policy(int policy) {
   return set_gemm_policy(policy);
 }
 
+int rb_selftest_wait_timeout(int64_t limit_ns, int64_t* waited_us) {
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    Engine* e;
+    int rc = ensure_engine(&e);
+    if (rc) return rc;
+    uint32_t* waited = nullptr;
+    RB_CUDA(cudaMalloc(&waited, sizeof(uint32_t)), "cudaMalloc(selftest)");
+    rc = launch_wait_timeout_probe(e->err, limit_ns, waited, nullptr);
+    uint32_t us = 0;
+    if (rc == RB_OK) {
+      if (cudaDeviceSynchronize() != cudaSuccess ||
+          cudaMemcpy(&us, waited, sizeof(us), cudaMemcpyDeviceToHost) != cudaSuccess)
+        rc = RB_E_DEVICE;
+    }
+    cudaFree(waited);
+    if (rc) return fail(rc, "wait-timeout probe launch failed (limit %lld ns)", (long long)limit_ns);
+    g_launches++;
+    if (waited_us) *waited_us = us;
+  }
+  return rb_check_device_errors();
+}
+
 int rb_set_attention_split(int policy) {
   if (policy < RB_ATTN_SPLIT_AUTO || policy > RB_ATTN_SPLIT_ALWAYS)
     return fail(RB_E_SHAPE, "unknown attention split policy %d", policy);

@@ -41,7 +41,9 @@ struct GemmPlan {
 GemmPlan gemm_plan(bool i8, int M, int N, int K, int num_sms);
 // Restricts gemm_plan to single-CTA or (preferably) pair tiles; returns the old policy.
 int set_gemm_policy(int policy);
-int set_attention_split(int policy);  // RB_ATTN_SPLIT_*; returns the previous one
+int set_attention_split(int policy);
+// selftest.cu: one bounded wait on an mbarrier nothing arrives on.
+int launch_wait_timeout_probe(uint32_t* err, int64_t limit_ns, uint32_t* waited_us, cudaStream_t st);  // RB_ATTN_SPLIT_*; returns the previous one
 // Q8_0: tmA = f16 activations [M, K] (box 64 x a_rows(), 128-B swizzle);
 // tmCodes = codes [N, K] (box 64 x weight_rows()); tmScales = f16 scales
 // [K/32, N] (box weight_rows() x 2); tmC = output map (box 32 rows x 128 B,

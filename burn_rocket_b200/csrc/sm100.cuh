@@ -82,23 +82,45 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete is
+// suspended until it completes or `ns` nanoseconds pass, instead of returning
+// at once and spinning (which takes issue slots from working warps).
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2, %3;\n\t"
+      "selp.b32 %0, 1, 0, P;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
+constexpr uint32_t kSuspendHintNs = 200000;  // 0.2 ms per suspended poll
+
 // Bounded wait for the phase with the given parity to complete. Returns false
 // (and flags the error word) when the wall-time limit runs out or another role
 // of the CTA has already given up (shared abort flag), so every role drains.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err,
-                                          volatile int* abort_flag) {
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, uint32_t* err,
+                                                volatile int* abort_flag, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 127u) == 0) {
+    if (mbar_try_wait_hint(bar, parity, kSuspendHintNs)) return true;
+    if ((i & 7u) == 0) {
       if (*abort_flag) return false;
-      if (global_timer_ns() - t0 > kWaitLimitNs) break;
+      if (global_timer_ns() - t0 > limit_ns) break;
     }
   }
   *abort_flag = 1;
   if (err) atomicOr(err, kErrWaitTimeout);
   return false;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err,
+                                          volatile int* abort_flag) {
+  return mbar_wait_limit(bar, parity, err, abort_flag, kWaitLimitNs);
 }
 
 // Same bounded wait, but backing off with nanosleep between polls: for waits

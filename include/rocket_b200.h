@@ -345,6 +345,16 @@ RB_API int rb_set_tile_policy(int policy);
  * cut at share boundaries and merged by their last finishing part;
  * RB_ATTN_SPLIT_NEVER / RB_ATTN_SPLIT_ALWAYS force one of them. Results agree
  * within f32 summation order. Returns the previous policy, or RB_E_SHAPE. */
+/* Failure-path self-test (no counterpart in the reference): one CTA waits,
+ * with the bounded mbarrier wait every pipeline uses, on a barrier nothing
+ * arrives on, for limit_ns (1 ns .. 1 s). The wait runs out, the kernel
+ * flags the engine's wait-timeout error bit and returns; this call then
+ * reads and clears the error word like rb_check_device_errors and returns its
+ * result (RB_E_DEVICE, last error naming "wait-timeout"). *waited_us receives
+ * how long the wait lasted. No GPU fault is involved and the context stays
+ * usable. */
+RB_API int rb_selftest_wait_timeout(int64_t limit_ns, int64_t* waited_us);
+
 #define RB_ATTN_SPLIT_AUTO 0
 #define RB_ATTN_SPLIT_NEVER 1
 #define RB_ATTN_SPLIT_ALWAYS 2
