@@ -126,8 +126,156 @@ __global__ void quantize_rows_kernel(const void* __restrict__ x, int64_t m, int6
   }
 }
 
+// Vectorised form for 16-bit activations with k % 16 == 0 and 16-byte
+// aligned rows: 16-byte loads (8 values) and 8-byte code stores, the row read
+// twice (the second pass hits L1/L2). Same arithmetic as quantize_rows_kernel,
+// so codes and scales are identical.
+template <int DT>
+__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (DT == RB_DTYPE_F16) {
+      const __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+      const float2 t = __half22float2(h);
+      f[2 * i] = t.x;
+      f[2 * i + 1] = t.y;
+    } else {
+      const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
+      const float2 t = __bfloat1622float2(h);
+      f[2 * i] = t.x;
+      f[2 * i + 1] = t.y;
+    }
+  }
+}
+
+// V = 16-byte vectors each lane keeps in registers: the row is read once
+// (k <= 2048).
+template <int DT, int V>
+__global__ void quantize_rows_vec_kernel(const uint4* __restrict__ x, int64_t m, int64_t k,
+                                         float in_scale, uint2* __restrict__ codes,
+                                         float* __restrict__ row_scale) {
+  const int lane = threadIdx.x & 31;
+  const int nv = static_cast<int>(k / 8);  // 16-byte vectors per row (<= 32 V)
+  const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
+       row < m; row += warps_total) {
+    const uint4* xr = x + row * nv;
+    uint4 v[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i)
+      if (lane + 32 * i < nv) v[i] = __ldg(xr + lane + 32 * i);
+    float s = in_scale;
+    if (in_scale == 0.0f) {
+      float amax = 0.0f;
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        if (lane + 32 * i < nv) {
+          float f[8];
+          unpack8<DT>(v[i], f);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) amax = fmaxf(amax, fabsf(f[q]));
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-12f);
+    }
+    const float inv = __fdiv_rn(1.0f, s);
+    uint2* q = codes + row * nv;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      if (lane + 32 * i < nv) {
+        float f[8];
+        unpack8<DT>(v[i], f);
+        uint32_t b[2] = {0u, 0u};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int c = static_cast<int>(fminf(fmaxf(rintf(__fmul_rn(f[e], inv)), -128.f), 127.f));
+          b[e >> 2] |= (static_cast<uint32_t>(c) & 0xFFu) << (8 * (e & 3));
+        }
+        q[lane + 32 * i] = make_uint2(b[0], b[1]);
+      }
+    }
+    if (lane == 0) row_scale[row] = s;
+  }
+}
+
+// Long rows (k > 2048): stream the row twice instead of holding it (the
+// second pass hits L1/L2), keeping registers low and many rows in flight.
+template <int DT>
+__global__ void quantize_rows_stream_kernel(const uint4* __restrict__ x, int64_t m, int64_t k,
+                                            float in_scale, uint2* __restrict__ codes,
+                                            float* __restrict__ row_scale) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nv = k / 8;
+  const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
+       row < m; row += warps_total) {
+    const uint4* xr = x + row * nv;
+    float s = in_scale;
+    if (in_scale == 0.0f) {
+      float amax = 0.0f;
+#pragma unroll 4
+      for (int64_t i = lane; i < nv; i += 32) {
+        float f[8];
+        unpack8<DT>(__ldg(xr + i), f);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) amax = fmaxf(amax, fabsf(f[q]));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-12f);
+    }
+    const float inv = __fdiv_rn(1.0f, s);
+    uint2* q = codes + row * nv;
+#pragma unroll 4
+    for (int64_t i = lane; i < nv; i += 32) {
+      float f[8];
+      unpack8<DT>(__ldg(xr + i), f);
+      uint32_t b[2] = {0u, 0u};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int c = static_cast<int>(fminf(fmaxf(rintf(__fmul_rn(f[e], inv)), -128.f), 127.f));
+        b[e >> 2] |= (static_cast<uint32_t>(c) & 0xFFu) << (8 * (e & 3));
+      }
+      q[i] = make_uint2(b[0], b[1]);
+    }
+    if (lane == 0) row_scale[row] = s;
+  }
+}
+
+template <int DT>
+static void launch_qrv(const void* x, int64_t m, int64_t k, float in_scale, int8_t* codes, float* row_scale,
+                       int blocks, cudaStream_t stream) {
+  const int nv = static_cast<int>(k / 8);
+  const uint4* xv = static_cast<const uint4*>(x);
+  uint2* cv = reinterpret_cast<uint2*>(codes);
+  if (nv <= 32 * 4) {
+    quantize_rows_vec_kernel<DT, 4><<<blocks, 256, 0, stream>>>(xv, m, k, in_scale, cv, row_scale);
+  } else if (nv <= 32 * 8) {
+    quantize_rows_vec_kernel<DT, 8><<<blocks, 256, 0, stream>>>(xv, m, k, in_scale, cv, row_scale);
+  } else {
+    const int sb = blocks < 148 * 8 ? blocks : 148 * 8;
+    quantize_rows_stream_kernel<DT><<<sb, 256, 0, stream>>>(xv, m, k, in_scale, cv, row_scale);
+  }
+}
+
 int launch_quantize_rows_i8(const void* x, int x_dtype, int64_t m, int64_t k, float in_scale,
                             int8_t* codes, float* row_scale, cudaStream_t stream) {
+  const bool vec = (x_dtype == RB_DTYPE_F16 || x_dtype == RB_DTYPE_BF16) && k % 8 == 0 &&
+                   (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(codes) & 7) == 0;
+  if (vec) {
+    // one warp per row; blocks of 8 rows, no grid-stride tail to balance
+    int64_t blocks = (m + 7) / 8;
+    if (blocks > (1 << 30)) blocks = 1 << 30;
+    if (blocks < 1) blocks = 1;
+    if (x_dtype == RB_DTYPE_F16)
+      launch_qrv<RB_DTYPE_F16>(x, m, k, in_scale, codes, row_scale, static_cast<int>(blocks), stream);
+    else
+      launch_qrv<RB_DTYPE_BF16>(x, m, k, in_scale, codes, row_scale, static_cast<int>(blocks), stream);
+    return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
+  }
   const int threads = 256;
   int64_t blocks = (m + 7) / 8;
   if (blocks > 148 * 16) blocks = 148 * 16;
