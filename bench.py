@@ -385,11 +385,12 @@ class Qwen3Workload:
         """Device time of the four Q8_0 GEMMs of one layer at the config shapes."""
         import torch
         m, L = self.model, self.model.layers[0]
-        calls = [(m.h, L["qkv"], m.qkv), (m.attn, L["o"], m.o), (m.h, L["gu"], m.gu), (m.act, L["down"], m.d)]
+        calls = [(m.h, L["qkv"], m.qkv), (m.attn, L["o"], m.o), (m.h, L["gu"], m.act), (m.act, L["down"], m.d)]
         flops = 0.0
         for x, w, y in calls:
             _, n, k = self.rb.weight_info(w)
-            flops += 2.0 * x.shape[0] * n * k
+            # a gated gate|up weight multiplies 2n rows for its n fused outputs
+            flops += 2.0 * x.shape[0] * n * k * (2 if w is L["gu"] else 1)
         for _ in range(2):
             for x, w, y in calls:
                 self.rb.matmul(x, w, out=y)
@@ -403,7 +404,7 @@ class Qwen3Workload:
         ev[1].record()
         torch.cuda.synchronize()
         ms = ev[0].elapsed_time(ev[1]) / reps
-        return "q8_0 gemm_kernel (qkv, o, gate|up, down of one layer)", flops / (ms / 1e3) / 1e12, ms
+        return "q8_0 gemm_kernel (qkv, o, gate|up with fused silu_mul, down of one layer)", flops / (ms / 1e3) / 1e12, ms
 
     @staticmethod
     def cpu_sample(orc, seed, timed_repeats=1):
@@ -583,7 +584,7 @@ class MoeWorkload:
 
         def run():
             lib.rb_matmul_grouped(lay["gu"].id, cfg.experts, m.xp.data_ptr(), m.max_rows, m.ws.data_ptr(), m.T,
-                                  cfg.top_k, m.gup.data_ptr(), L.DTYPE_F16, None)
+                                  cfg.top_k, (m.actp if m.gated else m.gup).data_ptr(), L.DTYPE_F16, None)
             lib.rb_matmul_grouped(lay["down"].id, cfg.experts, m.actp.data_ptr(), m.max_rows, m.ws.data_ptr(), m.T,
                                   cfg.top_k, m.yp.data_ptr(), L.DTYPE_F16, None)
         for _ in range(2):

@@ -165,6 +165,23 @@ def pack_q8_0(w) -> WeightId:
     return _pack_parts_q8_0([w])
 
 
+def pack_gated_q8_0(gate, up) -> WeightId:
+    """SwiGLU gate|up as one Q8_0 weight whose matmul returns the fused
+    f16 silu(x gate^T) * (x up^T) ([M, n_inter]; host.rs:31-38), i.e. the
+    pack2 gate|up matmul and silu_mul of a SwiGLU MLP in one kernel. gate and
+    up are [n_inter, K] float tensors (n_inter a multiple of 64); stacked
+    per-expert blocks give a gated grouped weight."""
+    import torch
+    lib = _lib.load()
+    g = gate.detach().to("cuda", torch.float32).contiguous()
+    u = up.detach().to("cuda", torch.float32).contiguous()
+    if g.shape != u.shape or g.dim() != 2:
+        raise OpFailure(Error("rocket_pack2", _lib.RB_E_SHAPE), 0, 0, 0, "gate and up must be equal [n, K]")
+    wid = lib.rb_pack_f32_q8_0_gated_device(g.data_ptr(), u.data_ptr(), g.shape[0], g.shape[1])
+    _check(wid, "rocket_pack2", 0, g.shape[1], 2 * g.shape[0])
+    return WeightId(int(wid))
+
+
 def pack2_q8_0(a, b) -> WeightId:
     return _pack_parts_q8_0([a, b])
 

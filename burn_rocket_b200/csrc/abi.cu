@@ -106,6 +106,7 @@ struct Weight {
   int64_t pitch = 0;         // Q8_0 scale row pitch: round_up(n, 8)
   float in_scale = 0.0f, out_scale = 0.0f;
   int64_t group = 0;         // RB_WEIGHT_I8G: K group width (scales f32 [n, k/group])
+  bool gated = false;        // gate|up interleaved in 32-row blocks: matmul gives silu(gate)*up, n/2 columns
   // TMA maps per staged weight-tile height ({256, 128, 96, 64}, see
   // bn_index; a CTA-pair tile stages half its N per CTA): the codes
   // (Q8_0: box 64 x bn; W8A8: box 128 x bn, 128-B swizzle) and the Q8_0
@@ -243,16 +244,20 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
   if (m <= 0) return fail(RB_E_SHAPE, "matmul needs M > 0 (M=%lld)", (long long)m);
   if (m > (int64_t(1) << 31) - 1) return fail(RB_E_SHAPE, "M=%lld too large", (long long)m);
   if (!dtype_bytes(x_dtype) || !dtype_bytes(y_dtype)) return fail(RB_E_SHAPE, "bad dtype");
-  if ((w.n * static_cast<int64_t>(dtype_bytes(y_dtype))) % 16 != 0 &&
+  const int64_t n_out = w.gated ? w.n / 2 : w.n;
+  if ((n_out * static_cast<int64_t>(dtype_bytes(y_dtype))) % 16 != 0 &&
       (reinterpret_cast<uintptr_t>(y) & 15) != 0)
     return fail(RB_E_SHAPE, "output buffer must be 16-byte aligned");
+  if (w.gated && (y_dtype != RB_DTYPE_F16 || (reinterpret_cast<uintptr_t>(y) & 15) != 0))
+    return fail(RB_E_SHAPE, "gated (SwiGLU) weight: the output must be a 16-byte aligned f16 buffer");
 
   GemmLaunch L{};
   L.M = static_cast<int>(m);
   L.N = static_cast<int>(w.n);
   L.K = static_cast<int>(w.k);
   L.out = y;
-  L.ldo = static_cast<int>(w.n);
+  L.ldo = static_cast<int>(n_out);
+  L.gated = w.gated ? 1 : 0;
   L.out_dtype = y_dtype;
   L.err = e->err;
   L.num_sms = e->num_sms;
@@ -287,10 +292,14 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
       g_launches++;
       a = e->act.ptr;
     }
-    const GemmPlan plan = gemm_plan(false, L.M, L.N, L.K, e->num_sms);
+    GemmPlan plan = gemm_plan(false, L.M, L.N, L.K, e->num_sms);
+    // The gated epilogue turns 128 accumulator columns into 64 outputs: tiles
+    // of 256 or 128 columns.
+    if (w.gated && plan.bn % 128 != 0) plan = GemmPlan{plan.pair ? 256 : 128, 1, plan.pair};
     CUtensorMap tmA, tmC;
     if ((rc = make_tmap_2d(&tmA, a, 2, m, k, k, 64, plan.a_rows(), 128)) != RB_OK) return rc;
-    const bool tstore = output_map(&tmC, y, y_dtype, m, w.n);
+    const bool tstore = output_map(&tmC, y, y_dtype, m, n_out);
+    if (w.gated && !tstore) return fail(RB_E_SHAPE, "gated weight: output tensor map unavailable");
     const int bi = bn_index(plan.weight_rows());
     if ((rc = launch_q8_gemm(L, plan, tmA, w.tm_codes[bi], w.tm_scales[bi], tstore ? &tmC : nullptr,
                              st)) != RB_OK)
@@ -677,6 +686,43 @@ int64_t rb_pack_f32_q8_0_device(const float* const* parts_dev, const int64_t* n_
   return pack_f32_q8_0_impl(parts_dev, n_parts, num_parts, k, cudaMemcpyDeviceToDevice);
 }
 
+int64_t rb_pack_f32_q8_0_gated_device(const float* gate_dev, const float* up_dev, int64_t n_inter, int64_t k) {
+  if (!gate_dev || !up_dev || n_inter <= 0 || n_inter % 64 != 0 || k <= 0)
+    return fail(RB_E_SHAPE, "gated pack: gate/up [%lld, %lld] need rows a positive multiple of 64",
+                (long long)n_inter, (long long)k);
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    Engine* e;
+    int rc = ensure_engine(&e);
+    if (rc) return rc;
+  }
+  // Interleave 32-row blocks: rows [64b, 64b+32) = gate block b, [64b+32, 64b+64) = up block b.
+  float* inter = nullptr;
+  const size_t blk = static_cast<size_t>(32) * k * sizeof(float);
+  if (cudaMalloc(&inter, 2 * static_cast<size_t>(n_inter) * k * sizeof(float)) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(RB_E_NOMEM, "gated pack: staging allocation failed");
+  }
+  const size_t nb = static_cast<size_t>(n_inter / 32);
+  if (cudaMemcpy2D(inter, 2 * blk, gate_dev, blk, blk, nb, cudaMemcpyDeviceToDevice) != cudaSuccess ||
+      cudaMemcpy2D(reinterpret_cast<uint8_t*>(inter) + blk, 2 * blk, up_dev, blk, blk, nb,
+                   cudaMemcpyDeviceToDevice) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(inter);
+    return fail(RB_E_DEVICE, "gated pack: interleave copy failed");
+  }
+  const float* parts[1] = {inter};
+  const int64_t ns[1] = {2 * n_inter};
+  const int64_t id = pack_f32_q8_0_impl(parts, ns, 1, k, cudaMemcpyDeviceToDevice);
+  cudaDeviceSynchronize();
+  cudaFree(inter);
+  if (id > 0) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    g_engine->weights[id].gated = true;
+  }
+  return id;
+}
+
 int64_t rb_pack_w8a8(const int8_t* codes_host, const float* w_scale_host, int64_t n, int64_t k,
                      float in_scale, float out_scale) {
   std::lock_guard<std::mutex> lk(g_mu);
@@ -855,7 +901,7 @@ int rb_weight_info(int64_t id, int* kind, int64_t* n, int64_t* k) {
   auto it = e->weights.find(id);
   if (it == e->weights.end()) return fail(RB_E_SHAPE, "weight id %lld is not packed", (long long)id);
   if (kind) *kind = it->second.kind;
-  if (n) *n = it->second.n;
+  if (n) *n = it->second.gated ? it->second.n / 2 : it->second.n;  // output columns
   if (k) *k = it->second.k;
   return RB_OK;
 }
@@ -879,7 +925,7 @@ int rb_matmul_host(int64_t id, const void* x_host, int x_dtype, int64_t m, int64
   if (!x_host || !y_host) return fail(RB_E_SHAPE, "null matmul buffer");
   auto it = e->weights.find(id);
   if (it == e->weights.end()) return fail(RB_E_SHAPE, "weight id %lld is not packed", (long long)id);
-  const int64_t n = it->second.n;
+  const int64_t n = it->second.gated ? it->second.n / 2 : it->second.n;  // output columns
   const size_t xb = static_cast<size_t>(m) * k * dtype_bytes(x_dtype);
   const size_t yb = static_cast<size_t>(m) * n * dtype_bytes(y_dtype);
   if (!xb || !yb) return fail(RB_E_SHAPE, "bad dtype or empty matmul");
@@ -1196,13 +1242,17 @@ int rb_matmul_grouped(int64_t id, int experts, const void* x_perm_f16, int64_t m
   if (max_rows != ml.max_rows) return fail(RB_E_SHAPE, "grouped matmul: max_rows must be rb_moe_max_rows()");
   if (!x_perm_f16 || !workspace || !y || (y_dtype != RB_DTYPE_F16 && y_dtype != RB_DTYPE_F32))
     return fail(RB_E_SHAPE, "grouped matmul: bad arguments");
-  const int64_t n = w.n / experts;
+  const int64_t n = w.n / experts;  // accumulator columns per expert
+  const int64_t n_out = w.gated ? n / 2 : n;
+  if (w.gated && (y_dtype != RB_DTYPE_F16 || n % 128 != 0))
+    return fail(RB_E_SHAPE, "grouped matmul: a gated weight needs f16 output and 64-aligned expert blocks");
   GemmLaunch L{};
   L.M = static_cast<int>(max_rows);
   L.N = static_cast<int>(n);
   L.K = static_cast<int>(w.k);
   L.out = y;
-  L.ldo = static_cast<int>(n);
+  L.ldo = static_cast<int>(n_out);
+  L.gated = w.gated ? 1 : 0;
   L.out_dtype = y_dtype;
   L.err = e->err;
   L.num_sms = e->num_sms;
@@ -1211,7 +1261,8 @@ int rb_matmul_grouped(int64_t id, int experts, const void* x_perm_f16, int64_t m
   const GemmPlan plan{n % 256 == 0 ? 256 : 128, 1, false};
   CUtensorMap tmA, tmC;
   if ((rc = make_tmap_2d(&tmA, x_perm_f16, 2, max_rows, w.k, w.k, 64, 128, 128)) != RB_OK) return rc;
-  const bool tstore = output_map(&tmC, y, y_dtype, max_rows, n);
+  const bool tstore = output_map(&tmC, y, y_dtype, max_rows, n_out);
+  if (w.gated && !tstore) return fail(RB_E_SHAPE, "grouped matmul: output tensor map unavailable");
   const int bi = bn_index(plan.weight_rows());
   if ((rc = launch_q8_gemm(L, plan, tmA, w.tm_codes[bi], w.tm_scales[bi], tstore ? &tmC : nullptr,
                            reinterpret_cast<cudaStream_t>(stream))) != RB_OK)

@@ -43,6 +43,9 @@ struct GemmArgs {
   // Grouped GEMM (MoE experts): per 128-row M tile, the expert whose weight
   // rows [e*N, (e+1)*N) it multiplies, or -1 to skip the tile; nullptr = plain.
   const int* tile_expert;
+  // Gated weight (gate and up rows interleaved in blocks of 32): the epilogue
+  // writes silu(gate) * up, N/2 f16 columns (kEpiSiluF16).
+  int gated;
   uint32_t* err;
 };
 
@@ -128,8 +131,15 @@ int epi_path_default();
 // W8A8 scaled forms (kEpiS8*; Q = onto the calibrated output grid).
 enum : int {
   kEpiRaw4 = 0, kEpiF16, kEpiBF16,
-  kEpiS8F32, kEpiS8F16, kEpiS8BF16, kEpiS8F32Q, kEpiS8F16Q, kEpiS8BF16Q
+  kEpiS8F32, kEpiS8F16, kEpiS8BF16, kEpiS8F32Q, kEpiS8F16Q, kEpiS8BF16Q,
+  kEpiSiluF16  // gated weight: f16 silu(gate) * up (SwiGLU, host.rs:31-38)
 };
+
+// silu on the epilogue path: two MUFU operations (ex2, rcp) per value, so the
+// fused epilogue keeps pace with the main loop; a few ulp of f32, far below
+// the f16 rounding of the output. Large negative g: exp overflows to +inf
+// and the quotient is -0.
+__device__ __forceinline__ float silu_acc(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
 __host__ __device__ __forceinline__ int epi_mode(bool i8, int out_dtype, float out_scale) {
   const int cast = out_dtype == RB_DTYPE_F16 ? 1 : out_dtype == RB_DTYPE_BF16 ? 2 : 0;
@@ -233,6 +243,48 @@ __device__ __forceinline__ void epi_block(uint32_t tmem_base, uint32_t acc_col, 
   // Raw int32 output (RB_DTYPE_I32) carries no scales.
   if (I8 && m < M && ep.out_dtype != RB_DTYPE_I32) rs = s_row[m];
   const bool rows_live = m0 + quarter * 32 < M;  // warp-uniform
+  if (mode == kEpiSiluF16) {
+    // Accumulator columns come in 64-wide groups: 32 gate columns, then the
+    // 32 up columns of the same intermediate units. Two groups (128
+    // accumulator columns) make one 64-column f16 output chunk at output
+    // column (n0 + c0) / 2. TMA-store path only (the host checks).
+    if (!rows_live) return;
+    for (int c0 = cbeg; c0 < cend && n0 + c0 < N; c0 += 128) {
+      if (lane == 0) bulk_wait_read<NBUF - 1>();
+      __syncwarp();
+      uint8_t* b = ebuf + buf * kEpiBufBytes + lane * 128;
+#pragma unroll 1
+      for (int hq = 0; hq < 4; ++hq) {  // 16 outputs at a time
+        const int cg = c0 + 64 * (hq >> 1) + 16 * (hq & 1);  // gate columns [cg, cg + 16), up at cg + 32
+        uint32_t gr[16], ur[16];
+        tmem_ld16(tmem_addr(tmem_base, quarter * 32, acc_col + cg), gr);
+        tmem_ld16(tmem_addr(tmem_base, quarter * 32, acc_col + cg + 32), ur);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          uint32_t pk[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int i = 8 * j + 2 * e;
+            const float v0 = silu_acc(__uint_as_float(gr[i])) * __uint_as_float(ur[i]);
+            const float v1 = silu_acc(__uint_as_float(gr[i + 1])) * __uint_as_float(ur[i + 1]);
+            __half2 h2 = __floats2half2_rn(v0, v1);
+            pk[e] = *reinterpret_cast<uint32_t*>(&h2);
+          }
+          const int q = 2 * hq + j;  // 16-byte unit of the 128-byte output row
+          *reinterpret_cast<uint4*>(b + ((q ^ (lane & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(tmC, ebuf + buf * kEpiBufBytes, (n0 + c0) / 2, m0 + quarter * 32);
+        bulk_commit();
+      }
+      if (NBUF == 2) buf ^= 1;
+    }
+    return;
+  }
   if (tma_store || vec_store) {
     if (rows_live) {
       for (int c0 = cbeg; c0 < cend && n0 + c0 < N; c0 += CW) {

@@ -24,6 +24,7 @@ struct GemmLaunch {
   int out_dtype;
   float out_scale;        // W8A8: 0 = unrounded output
   const int* tile_expert; // grouped GEMM table (single-CTA 128-row tiles), or nullptr
+  int gated;              // gate/up interleaved in 32-row blocks: out = silu(gate) * up, N/2 f16 columns
   uint32_t* err;
   int num_sms;
 };

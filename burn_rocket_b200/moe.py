@@ -14,8 +14,10 @@ torch spec `tools/clef_reference.py:179-246`): per layer
 then the final RMSNorm of every token. The experts run as grouped Q8_0 GEMMs
 over expert-contiguous, 128-row-aligned segments of a permuted activation
 buffer (`rb_moe_dispatch`, `rb_matmul_grouped`, `rb_moe_combine`): the
-experts' gate|up blocks are stacked in one Q8_0 weight ([E * 2 * inter,
-hidden]) and their down blocks in another ([E * hidden, inter]). Routing,
+experts' gate and up weights form one gated Q8_0 weight whose grouped matmul
+writes silu(gate·x)·(up·x) directly (`pack_gated_q8_0`; the unfused gate|up
+matmul + silu_mul when inter is not a multiple of 64), and their down blocks
+another ([E * hidden, inter]). Routing,
 dispatch and combine run on the device, so the whole forward is captured in
 one CUDA graph. The residual stream is f32; matmul operands are f16.
 """
@@ -28,7 +30,7 @@ from dataclasses import dataclass
 import numpy as np
 
 from . import _lib
-from . import _check, _dev_ptr, _stream_ptr, WeightId, matmul
+from . import _check, _dev_ptr, _stream_ptr, WeightId, matmul, pack_gated_q8_0
 from ._lib import DTYPE_F16, DTYPE_F32, MASK_CAUSAL
 from .qwen3 import rope_tables
 
@@ -85,6 +87,12 @@ class MoeModel:
         def ones(n):
             return torch.ones(n, device=dev)
 
+        self.gated = I % 64 == 0  # fused gate|up + silu_mul epilogue
+
+        def pack_gu(gate, up):
+            return pack_gated_q8_0(gate, up) if self.gated else pack_dev(
+                [m for e in range(E) for m in (gate[e * I:(e + 1) * I], up[e * I:(e + 1) * I])])
+
         self.layers = []
         for li in range(cfg.layers):
             if host_weights is not None:
@@ -93,17 +101,18 @@ class MoeModel:
                 qkv = pack_dev([t(W["wq"]), t(W["wk"]), t(W["wv"])])
                 o = pack_dev([t(W["wo"])])
                 router = pack_dev([t(W["router"])])
-                gu = pack_dev([t(m) for gate, up, _ in W["experts"] for m in (gate, up)])
+                gu = pack_gu(torch.cat([t(gate) for gate, _, _ in W["experts"]]),
+                             torch.cat([t(up) for _, up, _ in W["experts"]]))
                 down = pack_dev([t(dn) for _, _, dn in W["experts"]])
                 norms = {k: t(W[k]) for k in ("in_norm", "post_norm", "q_norm", "k_norm")}
             else:
                 qkv = pack_dev([randn(nh * d, h), randn(nkv * d, h), randn(nkv * d, h)])
                 o = pack_dev([randn(h, nh * d)])
                 router = pack_dev([randn(E, h)])
-                # experts: gate|up blocks stacked along N, then down blocks
-                big = randn(E * 2 * I, h)
-                gu = pack_dev([big])
-                del big
+                # experts: gate and up blocks stacked along N, then down blocks
+                gate, up = randn(E * I, h), randn(E * I, h)
+                gu = pack_gu(gate, up)
+                del gate, up
                 big = randn(E * h, I)
                 down = pack_dev([big])
                 del big
@@ -133,7 +142,7 @@ class MoeModel:
         self.wts = torch.empty(T, cfg.top_k, dtype=torch.float32, device=dev)
         self.ws = torch.empty((ws_bytes + 3) // 4, dtype=torch.int32, device=dev)
         self.xp = torch.empty(self.max_rows, h, dtype=f16, device=dev)
-        self.gup = torch.empty(self.max_rows, 2 * I, dtype=f16, device=dev)
+        self.gup = None if self.gated else torch.empty(self.max_rows, 2 * I, dtype=f16, device=dev)
         self.actp = torch.empty(self.max_rows, I, dtype=f16, device=dev)
         self.yp = torch.empty(self.max_rows, h, dtype=f16, device=dev)
         self.out = torch.empty(T, h, dtype=f16, device=dev)
@@ -172,10 +181,14 @@ class MoeModel:
                 self.routing.append((self.ids.clone(), self.wts.clone()))
             _check(lib.rb_moe_dispatch(_dev_ptr(self.ids), T, k, E, _dev_ptr(self.h), h, ws, _dev_ptr(self.xp), st),
                    "moe_dispatch")
-            _check(lib.rb_matmul_grouped(L["gu"].id, E, _dev_ptr(self.xp), self.max_rows, ws, T, k,
-                                         _dev_ptr(self.gup), DTYPE_F16, st), "matmul_grouped")
-            _check(lib.rb_silu_mul_halves(_dev_ptr(self.gup), self.max_rows, I, _dev_ptr(self.actp), st),
-                   "silu_mul")
+            if self.gated:  # silu(gate x) * (up x) straight from the grouped GEMM
+                _check(lib.rb_matmul_grouped(L["gu"].id, E, _dev_ptr(self.xp), self.max_rows, ws, T, k,
+                                             _dev_ptr(self.actp), DTYPE_F16, st), "matmul_grouped")
+            else:
+                _check(lib.rb_matmul_grouped(L["gu"].id, E, _dev_ptr(self.xp), self.max_rows, ws, T, k,
+                                             _dev_ptr(self.gup), DTYPE_F16, st), "matmul_grouped")
+                _check(lib.rb_silu_mul_halves(_dev_ptr(self.gup), self.max_rows, I, _dev_ptr(self.actp), st),
+                       "silu_mul")
             _check(lib.rb_matmul_grouped(L["down"].id, E, _dev_ptr(self.actp), self.max_rows, ws, T, k,
                                          _dev_ptr(self.yp), DTYPE_F16, st), "matmul_grouped")
             _check(lib.rb_moe_combine(xp, _dev_ptr(self.yp), h, _dev_ptr(self.ids), _dev_ptr(self.wts), ws, T, k, E,

@@ -30,7 +30,7 @@ import math
 import numpy as np
 
 from . import _lib
-from . import _check, _dev_ptr, WeightId, matmul
+from . import _check, _dev_ptr, WeightId, matmul, pack_gated_q8_0
 from ._lib import DTYPE_F16, MASK_CAUSAL, MASK_CAUSAL_BLOCK
 from .moe import MoeConfig
 from .qwen3 import rope_tables
@@ -109,6 +109,13 @@ class MoeEPModel:
             _check(wid, "rocket_pack", 0, parts[0].shape[1], sum(p.shape[0] for p in parts))
             return WeightId(int(wid))
 
+        self.gated = I % 64 == 0  # fused gate|up + silu_mul epilogue
+        epr = self.epr
+
+        def pack_gu(gate, up):
+            return pack_gated_q8_0(gate, up) if self.gated else pack_dev(
+                [m for e in range(epr) for m in (gate[e * I:(e + 1) * I], up[e * I:(e + 1) * I])])
+
         self.layers = []
         for li in range(cfg.layers):
             if host_weights is not None:
@@ -116,16 +123,17 @@ class MoeEPModel:
                 t = lambda a: torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(dev)
                 layer = {"qkv": pack_dev([t(W["wq"]), t(W["wk"]), t(W["wv"])]), "o": pack_dev([t(W["wo"])]),
                          "router": pack_dev([t(W["router"])]),
-                         "gu": pack_dev([t(m) for gate, up, _ in W["experts"][e0:e0 + self.epr] for m in (gate, up)]),
+                         "gu": pack_gu(torch.cat([t(gate) for gate, _, _ in W["experts"][e0:e0 + self.epr]]),
+                                       torch.cat([t(up) for _, up, _ in W["experts"][e0:e0 + self.epr]])),
                          "down": pack_dev([t(dn) for _, _, dn in W["experts"][e0:e0 + self.epr]])}
                 layer.update({kk: t(W[kk]) for kk in ("in_norm", "post_norm", "q_norm", "k_norm")})
             else:
                 layer = {"qkv": pack_dev([randn(g_dense, nh * d, h), randn(g_dense, nkv * d, h),
                                           randn(g_dense, nkv * d, h)]),
                          "o": pack_dev([randn(g_dense, h, nh * d)]), "router": pack_dev([randn(g_dense, E, h)])}
-                big = randn(g_exp, self.epr * 2 * I, h)
-                layer["gu"] = pack_dev([big])
-                del big
+                gate, up = randn(g_exp, self.epr * I, h), randn(g_exp, self.epr * I, h)
+                layer["gu"] = pack_gu(gate, up)
+                del gate, up
                 big = randn(g_exp, self.epr * h, I)
                 layer["down"] = pack_dev([big])
                 del big
@@ -170,7 +178,7 @@ class MoeEPModel:
         self.ws = torch.empty(int(lib.rb_moe_workspace_bytes(R, 1, self.epr)) // 4 + 1, dtype=torch.int32,
                               device=dev)
         self.xp = torch.empty(self.max_rows, h, dtype=f16, device=dev)
-        self.gup = torch.empty(self.max_rows, 2 * I, dtype=f16, device=dev)
+        self.gup = None if self.gated else torch.empty(self.max_rows, 2 * I, dtype=f16, device=dev)
         self.actp = torch.empty(self.max_rows, I, dtype=f16, device=dev)
         self.yp = torch.empty(self.max_rows, h, dtype=f16, device=dev)
         self.out = torch.empty(T, h, dtype=f16, device=dev)
@@ -245,9 +253,14 @@ class MoeEPModel:
                 ws = _dev_ptr(self.ws)
                 _check(lib.rb_moe_dispatch(_dev_ptr(self.recv_meta), R, 1, self.epr, _dev_ptr(self.recv_rows), h,
                                            ws, _dev_ptr(self.xp), None), "moe_dispatch")
-                _check(lib.rb_matmul_grouped(L["gu"].id, self.epr, _dev_ptr(self.xp), rows, ws, R, 1,
-                                             _dev_ptr(self.gup), DTYPE_F16, None), "matmul_grouped")
-                _check(lib.rb_silu_mul_halves(_dev_ptr(self.gup), rows, I, _dev_ptr(self.actp), None), "silu_mul")
+                if self.gated:  # silu(gate x) * (up x) straight from the grouped GEMM
+                    _check(lib.rb_matmul_grouped(L["gu"].id, self.epr, _dev_ptr(self.xp), rows, ws, R, 1,
+                                                 _dev_ptr(self.actp), DTYPE_F16, None), "matmul_grouped")
+                else:
+                    _check(lib.rb_matmul_grouped(L["gu"].id, self.epr, _dev_ptr(self.xp), rows, ws, R, 1,
+                                                 _dev_ptr(self.gup), DTYPE_F16, None), "matmul_grouped")
+                    _check(lib.rb_silu_mul_halves(_dev_ptr(self.gup), rows, I, _dev_ptr(self.actp), None),
+                           "silu_mul")
                 _check(lib.rb_matmul_grouped(L["down"].id, self.epr, _dev_ptr(self.actp), rows, ws, R, 1,
                                              _dev_ptr(self.yp), DTYPE_F16, None), "matmul_grouped")
                 # back to receive order: y_recv[i] = yp[row of received slot i]

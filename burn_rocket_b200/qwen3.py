@@ -29,7 +29,7 @@ from dataclasses import dataclass
 import numpy as np
 
 from . import _lib
-from . import _check, _dev_ptr, _stream_ptr, WeightId, matmul
+from . import _check, _dev_ptr, _stream_ptr, WeightId, matmul, pack_gated_q8_0
 from ._lib import DTYPE_F16, MASK_CAUSAL, MASK_NONE
 
 
@@ -107,7 +107,7 @@ class Qwen3Embedding:
             layer = {
                 "qkv": pack_dev([W["wq"], W["wk"], W["wv"]]),   # pack3
                 "o": pack_dev([W["wo"]]),
-                "gu": pack_dev([W["wg"], W["wu"]]),             # pack2
+                "gu": pack_gated_q8_0(W["wg"], W["wu"]),       # pack2 + fused silu_mul
                 "down": pack_dev([W["wd"]]),
                 "in_norm": W["in_norm"].float().contiguous(), "post_norm": W["post_norm"].float().contiguous(),
                 "q_norm": W["q_norm"].float().contiguous(), "k_norm": W["k_norm"].float().contiguous(),
@@ -132,7 +132,6 @@ class Qwen3Embedding:
         self.qkv = torch.empty(T, (nh + 2 * nkv) * hd, dtype=f16, device=dev)
         self.attn = torch.empty(T, nh * hd, dtype=f16, device=dev)
         self.o = torch.empty(T, h, dtype=f16, device=dev)
-        self.gu = torch.empty(T, 2 * inter, dtype=f16, device=dev)
         self.act = torch.empty(T, inter, dtype=f16, device=dev)
         self.d = torch.empty(T, h, dtype=f16, device=dev)
         self.out = torch.empty(batch, h, dtype=torch.float32, device=dev)
@@ -163,8 +162,7 @@ class Qwen3Embedding:
             matmul(self.attn, L["o"], out=self.o, stream=stream)
             _check(lib.rb_add_rms_norm(_dev_ptr(self.x), _dev_ptr(self.o), _dev_ptr(L["post_norm"]), cfg.eps,
                                        _dev_ptr(self.h), T, h, st), "add_rms_norm")
-            matmul(self.h, L["gu"], out=self.gu, stream=stream)
-            _check(lib.rb_silu_mul_halves(_dev_ptr(self.gu), T, inter, _dev_ptr(self.act), st), "silu_mul")
+            matmul(self.h, L["gu"], out=self.act, stream=stream)  # silu(h Wg^T) * (h Wu^T)
             matmul(self.act, L["down"], out=self.d, stream=stream)
             delta = _dev_ptr(self.d)
         # final residual, then the last token's norm + L2

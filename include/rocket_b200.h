@@ -117,6 +117,15 @@ RB_API int64_t rb_pack_f32_w8a8_device(const float* w_dev, int64_t n, int64_t k,
  * [n_parts[i], k] of dtype src_dtype (RB_DTYPE_F32 / F16 / BF16) concatenated
  * along N and rounded to f16 (RNE); rb_matmul is then f16 x f16 with f32
  * accumulation. K % 8 == 0. */
+/* Gated (SwiGLU) Q8_0 weight from device-resident f32 gate and up weights,
+ * each [n_inter, k] (n_inter a multiple of 64): rows are stored interleaved in
+ * blocks of 32 (gate block b, then up block b), and rb_matmul /
+ * rb_matmul_grouped on it write the fused f16 output silu(x gate^T) * (x up^T)
+ * of width n_inter (per expert for grouped weights, whose experts' gate and
+ * up blocks are stacked in order) — the gate|up matmul and silu_mul of a
+ * SwiGLU MLP in one kernel (host.rs:31-38). rb_weight_info reports n_inter. */
+RB_API int64_t rb_pack_f32_q8_0_gated_device(const float* gate_dev, const float* up_dev, int64_t n_inter, int64_t k);
+
 RB_API int64_t rb_pack_f16(const void* const* parts_host, const int64_t* n_parts, int num_parts, int64_t k,
                            int src_dtype);
 

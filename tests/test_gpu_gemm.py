@@ -290,3 +290,42 @@ def test_f16_pack2_pack3_concatenate_and_policies(rb, orc, tile_policy):
     wb16 = orc.f16_bits_to_f32(orc.f32_to_f16_bits(wb.float().numpy()))
     a16 = orc.f16_bits_to_f32(orc.f32_to_f16_bits(x.cpu().numpy()))
     assert max_rel(yb, orc.gemm_f64acc(a16, wb16)) <= 1e-5
+
+
+# ------------------------------------------------------------------ gated (SwiGLU) epilogue
+
+@pytest.mark.parametrize("policy", ["auto", "single", "pair"])
+@pytest.mark.parametrize("m,inter,k", [(1, 64, 64), (300, 768, 1024), (1000, 3072, 1024), (4096, 192, 256)])
+def test_gated_q8_0_matmul_is_silu_mul_of_gate_up(rb, orc, tile_policy, policy, m, inter, k):
+    """pack_gated_q8_0(gate, up) then matmul == silu(x gate^T) * (x up^T) of the
+    Q8_0-dequantised weights (host.rs:31-38), f16 output; cosine / max-rel bar."""
+    import torch
+    tile_policy(policy)
+    rng = np.random.default_rng(m + inter + k)
+    gate = (rng.standard_normal((inter, k)) * 0.02).astype(np.float32)
+    up = (rng.standard_normal((inter, k)) * 0.02).astype(np.float32)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    wid = rb.pack_gated_q8_0(torch.from_numpy(gate), torch.from_numpy(up))
+    assert rb.weight_info(wid)[1] == inter
+    xd = torch.from_numpy(x).cuda().half()
+    y = torch.empty(m, inter, dtype=torch.float16, device="cuda")
+    rb.matmul(xd, wid, out=y)
+    torch.cuda.synchronize()
+    rb.check_device_errors()
+    x16 = orc.f16_bits_to_f32(orc.f32_to_f16_bits(x)).astype(np.float64)
+    gd = orc.q8_0_dequant(*orc.q8_0_quantize(gate)).astype(np.float64)
+    ud = orc.q8_0_dequant(*orc.q8_0_quantize(up)).astype(np.float64)
+    g, u = x16 @ gd.T, x16 @ ud.T
+    ref = g / (1.0 + np.exp(-g)) * u
+    got = y.float().cpu().numpy()
+    assert cosine(got, ref) >= COS_MIN, cosine(got, ref)
+    assert max_rel(got, ref) <= MAX_REL, max_rel(got, ref)
+
+
+def test_gated_pack_contract(rb):
+    import torch
+    with pytest.raises(Exception):
+        rb.pack_gated_q8_0(torch.zeros(96, 64), torch.zeros(96, 64))  # rows not a multiple of 64
+    wid = rb.pack_gated_q8_0(torch.zeros(64, 64), torch.zeros(64, 64))
+    with pytest.raises(Exception):  # the fused output is f16 only
+        rb.matmul(torch.zeros(4, 64, device="cuda"), wid, out=torch.empty(4, 64, device="cuda"))
