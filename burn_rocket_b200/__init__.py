@@ -165,6 +165,15 @@ def pack_q8_0(w) -> WeightId:
     return _pack_parts_q8_0([w])
 
 
+def set_weight_activation(w: WeightId, act: str) -> None:
+    """Fuse an element-wise activation into later matmuls on weight `w`
+    ("gelu_tanh", host.rs:15-18, or "none"); the output must then be f16."""
+    names = {"none": 0, "gelu_tanh": 1}
+    if act not in names:
+        raise ValueError(f"activation must be one of {list(names)}")
+    _check(_lib.load().rb_set_weight_activation(w.id, names[act]), "rb_set_weight_activation")
+
+
 def pack_gated_q8_0(gate, up) -> WeightId:
     """SwiGLU gate|up as one Q8_0 weight whose matmul returns the fused
     f16 silu(x gate^T) * (x up^T) ([M, n_inter]; host.rs:31-38), i.e. the

@@ -107,6 +107,7 @@ struct Weight {
   float in_scale = 0.0f, out_scale = 0.0f;
   int64_t group = 0;         // RB_WEIGHT_I8G: K group width (scales f32 [n, k/group])
   bool gated = false;        // gate|up interleaved in 32-row blocks: matmul gives silu(gate)*up, n/2 columns
+  int act = RB_ACT_NONE;     // element-wise activation fused into the matmul epilogue
   // TMA maps per staged weight-tile height ({256, 128, 96, 64}, see
   // bn_index; a CTA-pair tile stages half its N per CTA): the codes
   // (Q8_0: box 64 x bn; W8A8: box 128 x bn, 128-B swizzle) and the Q8_0
@@ -217,6 +218,7 @@ int w8a8_view(int64_t id, W8A8View* v) {
   v->k = w.k;
   v->in_scale = w.in_scale;
   v->out_scale = w.out_scale;
+  v->act = w.act;
   for (int i = 0; i < 4; ++i) v->tm_codes[i] = w.tm_codes[i];
   v->err = e->err;
   v->num_sms = e->num_sms;
@@ -250,6 +252,8 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
     return fail(RB_E_SHAPE, "output buffer must be 16-byte aligned");
   if (w.gated && (y_dtype != RB_DTYPE_F16 || (reinterpret_cast<uintptr_t>(y) & 15) != 0))
     return fail(RB_E_SHAPE, "gated (SwiGLU) weight: the output must be a 16-byte aligned f16 buffer");
+  if (w.act != RB_ACT_NONE && y_dtype != RB_DTYPE_F16)
+    return fail(RB_E_SHAPE, "weight id %lld has a fused activation: the output must be f16", (long long)id);
 
   GemmLaunch L{};
   L.M = static_cast<int>(m);
@@ -258,6 +262,7 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
   L.out = y;
   L.ldo = static_cast<int>(n_out);
   L.gated = w.gated ? 1 : 0;
+  L.act = w.act;
   L.out_dtype = y_dtype;
   L.err = e->err;
   L.num_sms = e->num_sms;
@@ -1340,6 +1345,25 @@ int rb_selftest_wait_timeout(int64_t limit_ns, int64_t* waited_us) {
     if (waited_us) *waited_us = us;
   }
   return rb_check_device_errors();
+}
+
+int rb_set_weight_activation(int64_t id, int act) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Engine* e;
+  int rc = ensure_engine(&e);
+  if (rc) return rc;
+  auto it = e->weights.find(id);
+  if (it == e->weights.end()) return fail(RB_E_SHAPE, "weight id %lld is not packed", (long long)id);
+  Weight& w = it->second;
+  if (act != RB_ACT_NONE && act != RB_ACT_GELU_TANH) return fail(RB_E_SHAPE, "unknown activation %d", act);
+  if (act != RB_ACT_NONE) {
+    if (w.gated || w.kind == RB_WEIGHT_I8G)
+      return fail(RB_E_SHAPE, "weight id %lld: no fused activation on gated or group-wise weights", (long long)id);
+    if (w.kind == RB_WEIGHT_W8A8 && w.out_scale != 0.0f)
+      return fail(RB_E_SHAPE, "weight id %lld: no fused activation with a calibrated output grid", (long long)id);
+  }
+  w.act = act;
+  return RB_OK;
 }
 
 int rb_set_attention_split(int policy) {

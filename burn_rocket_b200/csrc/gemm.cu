@@ -224,7 +224,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     // columns and warps 6..9 the second (each quarter of TMEM lanes has two).
     constexpr int kColSplit = Cfg::EPI_WARPS / 4;
     const int cbeg = ((warp - kEpiWarp0) >> 2) * (BN / kColSplit), cend = cbeg + BN / kColSplit;
-    const int mode = args.gated ? kEpiSiluF16 : epi_mode(Cfg::I8, args.out_dtype, args.out_scale);
+    const int mode = args.gated ? kEpiSiluF16 : epi_mode(Cfg::I8, args.out_dtype, args.out_scale, args.act);
     int buf = 0;
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
@@ -405,6 +405,7 @@ static GemmArgs make_args(const GemmLaunch& L) {
   a.err = L.err;
   a.tile_expert = L.tile_expert;
   a.gated = L.gated;
+  a.act = L.act;
   return a;
 }
 

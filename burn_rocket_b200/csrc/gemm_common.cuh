@@ -46,6 +46,8 @@ struct GemmArgs {
   // Gated weight (gate and up rows interleaved in blocks of 32): the epilogue
   // writes silu(gate) * up, N/2 f16 columns (kEpiSiluF16).
   int gated;
+  // Element-wise activation applied before the f16 rounding (RB_ACT_*).
+  int act;
   uint32_t* err;
 };
 
@@ -132,8 +134,19 @@ int epi_path_default();
 enum : int {
   kEpiRaw4 = 0, kEpiF16, kEpiBF16,
   kEpiS8F32, kEpiS8F16, kEpiS8BF16, kEpiS8F32Q, kEpiS8F16Q, kEpiS8BF16Q,
-  kEpiSiluF16  // gated weight: f16 silu(gate) * up (SwiGLU, host.rs:31-38)
+  kEpiSiluF16,  // gated weight: f16 silu(gate) * up (SwiGLU, host.rs:31-38)
+  kEpiF16Gelu, kEpiS8F16Gelu  // f16 gelu_tanh(value) (host.rs:15-18)
 };
+
+// gelu_tanh(g) = 0.5 g (1 + tanh(sqrt(2/pi) (g + 0.044715 g^3))) with the
+// hardware tanh approximation (relative error ~2^-11, at the f16 output's
+// rounding level).
+__device__ __forceinline__ float gelu_acc(float g) {
+  const float inner = (g + g * g * g * 0.044715f) * 0.7978845608028654f;
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(inner));
+  return (g * (t + 1.0f)) * 0.5f;
+}
 
 // silu on the epilogue path: two MUFU operations (ex2, rcp) per value, so the
 // fused epilogue keeps pace with the main loop; a few ulp of f32, far below
@@ -141,7 +154,8 @@ enum : int {
 // and the quotient is -0.
 __device__ __forceinline__ float silu_acc(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
-__host__ __device__ __forceinline__ int epi_mode(bool i8, int out_dtype, float out_scale) {
+__host__ __device__ __forceinline__ int epi_mode(bool i8, int out_dtype, float out_scale, int act = 0) {
+  if (act == RB_ACT_GELU_TANH) return i8 ? kEpiS8F16Gelu : kEpiF16Gelu;  // f16, no output grid (host checks)
   const int cast = out_dtype == RB_DTYPE_F16 ? 1 : out_dtype == RB_DTYPE_BF16 ? 2 : 0;
   if (!i8 || out_dtype == RB_DTYPE_I32) return out_dtype == RB_DTYPE_I32 ? kEpiRaw4 : cast;
   return kEpiS8F32 + cast + (out_scale != 0.0f ? 3 : 0);
@@ -159,7 +173,7 @@ __host__ __device__ __forceinline__ int epi_mode(bool i8, int out_dtype, float o
 // in range, the rest clamp to the last valid one and are clipped by the TMA
 // store). OUT is the output element size in bytes' role: 4 (f32 / raw), 1 (f16),
 // 2 (bf16). QGRID rounds onto the static output grid (ext.rs:1236-1238).
-template <bool SCALE, int OUT, bool QGRID>
+template <bool SCALE, int OUT, bool QGRID, bool GELU = false>
 __device__ __forceinline__ void epi_chunk(uint8_t* b, uint4* g, bool live, int lane,
                                           const uint32_t (&ra)[32], const uint32_t (&rb)[32], float rs,
                                           const float* scp, int nvalid, const EpiParams& ep) {
@@ -179,7 +193,11 @@ __device__ __forceinline__ void epi_chunk(uint8_t* b, uint4* g, bool live, int l
   }
   auto value = [&](int i) -> float {
     const uint32_t r = i < 32 ? ra[i] : rb[i - 32];
-    if constexpr (!SCALE) {
+    if constexpr (GELU && SCALE) {
+      return gelu_acc(__fmul_rn(__int2float_rn(static_cast<int32_t>(r)), __fmul_rn(rs, sc[i])));
+    } else if constexpr (GELU) {
+      return gelu_acc(__uint_as_float(r));
+    } else if constexpr (!SCALE) {
       return __uint_as_float(r);
     } else {
       float y = __fmul_rn(__int2float_rn(static_cast<int32_t>(r)), __fmul_rn(rs, sc[i]));
@@ -237,7 +255,7 @@ __device__ __forceinline__ void epi_block(uint32_t tmem_base, uint32_t acc_col, 
   const bool tma_store = path == kEpiPathTma;
   const bool vec_store = path == kEpiPathVector;
   const int row = quarter * 32 + lane;
-  const int CW = (mode == kEpiRaw4 || mode == kEpiS8F32 || mode == kEpiS8F32Q) ? 32 : 64;
+  const int CW = (mode == kEpiRaw4 || mode == kEpiS8F32 || mode == kEpiS8F32Q) ? 32 : 64;  // GELU modes: f16
   const int m = m0 + row;
   float rs = 1.0f;
   // Raw int32 output (RB_DTYPE_I32) carries no scales.
@@ -310,6 +328,7 @@ __device__ __forceinline__ void epi_block(uint32_t tmem_base, uint32_t acc_col, 
           case kEpiRaw4: epi_chunk<false, 4, false>(b, g, m < M, lane, ra, rb, rs, scp, nvalid, ep); break;
           case kEpiF16: epi_chunk<false, 1, false>(b, g, m < M, lane, ra, rb, rs, scp, nvalid, ep); break;
           case kEpiBF16: epi_chunk<false, 2, false>(b, g, m < M, lane, ra, rb, rs, scp, nvalid, ep); break;
+          case kEpiF16Gelu: epi_chunk<false, 1, false, true>(b, g, m < M, lane, ra, rb, rs, scp, nvalid, ep); break;
           default:
             if constexpr (I8) {
               switch (mode) {
@@ -318,6 +337,9 @@ __device__ __forceinline__ void epi_block(uint32_t tmem_base, uint32_t acc_col, 
                 case kEpiS8BF16: epi_chunk<true, 2, false>(b, g, m < M, lane, ra, rb, rs, scp, nvalid, ep); break;
                 case kEpiS8F32Q: epi_chunk<true, 4, true>(b, g, m < M, lane, ra, rb, rs, scp, nvalid, ep); break;
                 case kEpiS8F16Q: epi_chunk<true, 1, true>(b, g, m < M, lane, ra, rb, rs, scp, nvalid, ep); break;
+                case kEpiS8F16Gelu:
+                  epi_chunk<true, 1, false, true>(b, g, m < M, lane, ra, rb, rs, scp, nvalid, ep);
+                  break;
                 default: epi_chunk<true, 2, true>(b, g, m < M, lane, ra, rb, rs, scp, nvalid, ep); break;
               }
             }

@@ -247,7 +247,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     uint8_t* ebuf = smem + Cfg::EPI_OFF + (warp - kEpiWarp0) * Cfg::EPI_BUFS * kEpiBufBytes;
     constexpr int kColSplit = Cfg::EPI_WARPS / 4;  // warps sharing a TMEM lane quarter
     const int cbeg = ((warp - kEpiWarp0) >> 2) * (BN / kColSplit), cend = cbeg + BN / kColSplit;
-    const int mode = args.gated ? kEpiSiluF16 : epi_mode(Cfg::I8, args.out_dtype, args.out_scale);
+    const int mode = args.gated ? kEpiSiluF16 : epi_mode(Cfg::I8, args.out_dtype, args.out_scale, args.act);
     int buf = 0;
     int local = 0;
     for (int t = pair; t < num_tiles; t += npairs, ++local) {

@@ -25,6 +25,7 @@ struct GemmLaunch {
   float out_scale;        // W8A8: 0 = unrounded output
   const int* tile_expert; // grouped GEMM table (single-CTA 128-row tiles), or nullptr
   int gated;              // gate/up interleaved in 32-row blocks: out = silu(gate) * up, N/2 f16 columns
+  int act;                // RB_ACT_*: element-wise activation before the f16 output rounding
   uint32_t* err;
   int num_sms;
 };
@@ -176,6 +177,7 @@ struct W8A8View {
   const float* w_scale;    // [n]
   int64_t n, k;
   float in_scale, out_scale;
+  int act;                  // RB_ACT_* fused into the epilogue
   CUtensorMap tm_codes[4];  // box heights 256 / 128 / 96 / 64 (bn_index)
   uint32_t* err;
   int num_sms;

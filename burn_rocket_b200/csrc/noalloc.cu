@@ -75,6 +75,8 @@ extern "C" int rb_matmul_w8a8_noalloc(int64_t id, const void* x, int x_dtype, in
   int rc = w8a8_view(id, &v);  // also makes the engine's device current
   if (rc != RB_OK) return rc;
   if (k != v.k) return report_error(RB_E_SHAPE, "activation K mismatch for the W8A8 weight");
+  if (v.act != RB_ACT_NONE && y_dtype != RB_DTYPE_F16)
+    return report_error(RB_E_SHAPE, "the W8A8 weight has a fused activation: the output must be f16");
   const size_t codes_bytes = (static_cast<size_t>(m) * static_cast<size_t>(k) + 255) & ~size_t(255);
   const size_t need = codes_bytes + static_cast<size_t>(m) * sizeof(float);
   if (m > (int64_t(1) << 30) || need > kNoAllocScratchBytes) {
@@ -106,6 +108,7 @@ extern "C" int rb_matmul_w8a8_noalloc(int64_t id, const void* x, int x_dtype, in
   L.ldo = static_cast<int>(v.n);
   L.out_dtype = y_dtype;
   L.out_scale = v.out_scale;
+  L.act = v.act;
   L.err = v.err;
   L.num_sms = v.num_sms;
   const bool tstore = make_output_map(&tmC, y, y_dtype, m, v.n);

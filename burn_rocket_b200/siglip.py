@@ -25,7 +25,7 @@ import math
 from dataclasses import dataclass
 
 from . import _lib
-from . import _check, _dev_ptr, _stream_ptr, matmul, pack_w8a8_float
+from . import _check, _dev_ptr, _stream_ptr, matmul, pack_w8a8_float, set_weight_activation
 from ._lib import DTYPE_F16, MASK_NONE
 
 
@@ -86,9 +86,11 @@ class SiglipTower:
                 W = {"wq": randn16(hq, h), "wk": randn16(hq, h), "wv": randn16(hq, h), "wo": randn16(h, hq),
                      "w1": randn16(inter, h), "w2": randn16(h, inter),
                      "ln1_g": g1, "ln1_b": b1, "ln2_g": g2, "ln2_b": b2}
+            fc1 = pack(W["w1"])
+            set_weight_activation(fc1, "gelu_tanh")  # gelu_tanh fused into the fc1 epilogue
             self.layers.append({
                 "qkv": pack(torch.cat([W["wq"], W["wk"], W["wv"]], 0)),
-                "o": pack(W["wo"]), "fc1": pack(W["w1"]), "fc2": pack(W["w2"]),
+                "o": pack(W["wo"]), "fc1": fc1, "fc2": pack(W["w2"]),
                 "ln1_g": W["ln1_g"].float().contiguous(), "ln1_b": W["ln1_b"].float().contiguous(),
                 "ln2_g": W["ln2_g"].float().contiguous(), "ln2_b": W["ln2_b"].float().contiguous(),
             })
@@ -139,8 +141,7 @@ class SiglipTower:
             matmul(self.attn, L["o"], out=self.o, stream=stream)
             _check(lib.rb_add_layer_norm(_dev_ptr(self.x), _dev_ptr(self.o), _dev_ptr(L["ln2_g"]), _dev_ptr(L["ln2_b"]),
                                          cfg.eps, _dev_ptr(self.h), T, h, st), "add_layer_norm")
-            matmul(self.h, L["fc1"], out=self.f, stream=stream)
-            _check(lib.rb_gelu(_dev_ptr(self.f), T * cfg.inter, st), "gelu")
+            matmul(self.h, L["fc1"], out=self.f, stream=stream)  # gelu_tanh(h W1^T), fused
             matmul(self.f, L["fc2"], out=self.d, stream=stream)
             delta = _dev_ptr(self.d)
         _check(lib.rb_add_layer_norm(_dev_ptr(self.x), delta, _dev_ptr(self.post_g), _dev_ptr(self.post_b), cfg.eps,

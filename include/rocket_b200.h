@@ -117,6 +117,15 @@ RB_API int64_t rb_pack_f32_w8a8_device(const float* w_dev, int64_t n, int64_t k,
  * [n_parts[i], k] of dtype src_dtype (RB_DTYPE_F32 / F16 / BF16) concatenated
  * along N and rounded to f16 (RNE); rb_matmul is then f16 x f16 with f32
  * accumulation. K % 8 == 0. */
+/* Element-wise activation fused into the matmul epilogue of weight `id`
+ * (no counterpart in the reference's trait; the GEMM-side form of its
+ * rocket_gelu glue, host.rs:15-18): later rb_matmul calls on this weight write
+ * act(x W^T) and need an f16 output (W8A8: without an output grid).
+ * RB_ACT_NONE restores the plain product. Returns RB_OK or RB_E_SHAPE. */
+#define RB_ACT_NONE 0
+#define RB_ACT_GELU_TANH 1
+RB_API int rb_set_weight_activation(int64_t id, int act);
+
 /* Gated (SwiGLU) Q8_0 weight from device-resident f32 gate and up weights,
  * each [n_inter, k] (n_inter a multiple of 64): rows are stored interleaved in
  * blocks of 32 (gate block b, then up block b), and rb_matmul /

@@ -329,3 +329,51 @@ def test_gated_pack_contract(rb):
     wid = rb.pack_gated_q8_0(torch.zeros(64, 64), torch.zeros(64, 64))
     with pytest.raises(Exception):  # the fused output is f16 only
         rb.matmul(torch.zeros(4, 64, device="cuda"), wid, out=torch.empty(4, 64, device="cuda"))
+
+
+# ------------------------------------------------------------------ fused activation (GELU-tanh)
+
+def _gelu_tanh(v):
+    return 0.5 * v * (1.0 + np.tanh(0.7978845608028654 * (v + 0.044715 * v ** 3)))
+
+
+@pytest.mark.parametrize("policy", ["auto", "single", "pair"])
+@pytest.mark.parametrize("m,n,k", [(1, 64, 64), (300, 4304, 1152), (2394, 1000, 256)])
+def test_w8a8_fused_gelu(rb, orc, tile_policy, policy, m, n, k):
+    """set_weight_activation(w, "gelu_tanh"): matmul == gelu_tanh(the W8A8
+    product) (host.rs:15-18) with f16 output."""
+    import torch
+    tile_policy(policy)
+    x, codes, ws, wid, xd = _w8a8_case(rb, orc, m, n, k, seed=m + n + 7 * k)
+    rb.set_weight_activation(wid, "gelu_tanh")
+    y = torch.empty(m, n, dtype=torch.float16, device="cuda")
+    rb.matmul(xd, wid, out=y)
+    torch.cuda.synchronize()
+    rb.check_device_errors()
+    ref = _gelu_tanh(orc.w8a8_matmul(x, codes, ws).astype(np.float64))
+    got = y.float().cpu().numpy()
+    assert cosine(got, ref) >= COS_MIN, cosine(got, ref)
+    assert max_rel(got, ref) <= MAX_REL, max_rel(got, ref)
+    rb.set_weight_activation(wid, "none")
+    with pytest.raises(ValueError):
+        rb.set_weight_activation(wid, "relu")
+
+
+def test_q8_0_fused_gelu_and_contract(rb, orc):
+    import torch
+    m, n, k = 200, 512, 256
+    w, codes, scales = q8_weight(orc, n, k, seed=5)
+    wid = rb.pack_q8_0(torch.from_numpy(w))
+    rb.set_weight_activation(wid, "gelu_tanh")
+    x = np.random.default_rng(1).standard_normal((m, k)).astype(np.float32)
+    y = torch.empty(m, n, dtype=torch.float16, device="cuda")
+    rb.matmul(torch.from_numpy(x).cuda().half(), wid, out=y)
+    torch.cuda.synchronize()
+    x16 = orc.f16_bits_to_f32(orc.f32_to_f16_bits(x)).astype(np.float64)
+    ref = _gelu_tanh(x16 @ orc.q8_0_dequant(codes, scales).astype(np.float64).T)
+    got = y.float().cpu().numpy()
+    assert cosine(got, ref) >= COS_MIN
+    assert max_rel(got, ref) <= MAX_REL
+    with pytest.raises(Exception):  # fused activations write f16 only
+        rb.matmul(torch.from_numpy(x).cuda(), wid, out=torch.empty(m, n, device="cuda"))
+    rb.check_device_errors()
