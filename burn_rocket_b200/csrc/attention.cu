@@ -65,10 +65,14 @@ constexpr float kRescaleThresh = 8.0f;  // log2 units
 constexpr float kFastMargin = 160.0f;   // exp2(-160) underflows f32 to 0
 constexpr int kNoBound = 1 << 30;
 constexpr int kMaxCtas = kAttnMaxCtas;  // split-mode grid bound (>= SM count)
-// Schedule cost model, in key tiles (one tile ~ 1.3 us of a CTA's time):
-constexpr int kItemCost = 6;   // split mode: per unit (Q load, pipeline refill, epilogue)
-constexpr int kMergeCost = 4;  // split mode: per CTA (partial records and the merge)
-constexpr int kCtaCost = 2;    // one CTA per unit: per CTA (prologue, epilogue)
+// Split-mode planning: each unit is charged kItemCost key tiles on top of
+// its own when the shares are cut (one tile ~ 1.25 us of a CTA's time).
+constexpr int kItemCost = 6;
+// Schedule choice, in key tiles, fitted to measured runs (config #2 both
+// masks, 64 x 512 and 4 x 2048 token batches, 16 x 2394 at head_dim 72):
+constexpr double kCtaTime = 5.0;    // one CTA per unit: a CTA's launch, prologue and epilogue
+constexpr double kItemTime = 3.0;   // split: one more item in a CTA's walk
+constexpr double kMergeTime = 10.0; // split: a CTA's partial records and merges
 
 std::atomic<int> g_split_policy{RB_ATTN_SPLIT_AUTO};
 
@@ -1016,7 +1020,13 @@ int launch_attention(const CUtensorMap* tm, const AttnLaunch& L, cudaStream_t st
     if (use && policy == RB_ATTN_SPLIT_AUTO) {
       // Estimated finish time, in key tiles, of the one-CTA-per-unit greedy
       // schedule (heaviest first onto the first free SM) against the split.
-      const double split_t = static_cast<double>(W) / G + kMergeCost;
+      long long tiles = 0;
+      bool equal = true;  // every unit has the same length (no causal / window mask)
+      for (int pair = 0; pair < P; ++pair) {
+        tiles += static_cast<long long>(blk) * plen[pair];
+        equal = equal && plen[pair] == plen[0];
+      }
+      const double split_t = (static_cast<double>(tiles) + kItemTime * static_cast<double>(units)) / G + kMergeTime;
       if (units <= 4 * 65536) {
         std::priority_queue<long long, std::vector<long long>, std::greater<long long>> sm;
         for (int i = 0; i < L.num_sms; ++i) sm.push(0);
@@ -1024,14 +1034,16 @@ int launch_attention(const CUtensorMap* tm, const AttnLaunch& L, cudaStream_t st
           for (int i = 0; i < blk; ++i) {
             const long long t0 = sm.top();
             sm.pop();
-            sm.push(t0 + plen[pair] + kCtaCost);
+            sm.push(t0 + plen[pair] + static_cast<long long>(kCtaTime));
           }
         long long greedy = 0;
         while (!sm.empty()) {
           greedy = std::max(greedy, sm.top());
           sm.pop();
         }
-        use = split_t < 0.97 * static_cast<double>(greedy);
+        // Units of unequal length leave the split's shares uneven in time
+        // (short items cost more than modelled): it must win clearly there.
+        use = split_t < (equal ? 0.97 : 0.75) * static_cast<double>(greedy);
       } else {
         use = false;  // many units: the greedy schedule's last wave is short
       }
