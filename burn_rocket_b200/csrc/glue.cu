@@ -272,40 +272,63 @@ __global__ void gelu_f16_kernel(__half* y, int64_t count8) {
 }
 
 // In place on qkv [T, ld] f16: heads [0, hq) of width 128 at column 0 (q) use
-// wq, heads [hq, hq+hk) (k) use wk. One warp per token: the RoPE row of the
-// token's position and both norm weights are loaded once, then every head is
-// normalised and rotated; lane l owns elements 2l, 2l+1 and 64+2l, 64+2l+1
-// (the rotate-half pairs).
+// wq, heads [hq, hq+hk) (k) use wk. Each half-warp takes one (token, head):
+// lane i of the 16 owns elements 4i..4i+3 and 64+4i..64+4i+3 (the rotate-half
+// pairs), read and written as 8-byte vectors; the head's sum of squares is
+// reduced over the 16 lanes.
 __global__ void qk_norm_rope_kernel(__half* qkv, int64_t ld, int64_t tokens, int hq, int hk,
                                     const float* wq, const float* wk, float eps,
                                     const float* cos_t, const float* sin_t, int seq) {
   const int lane = threadIdx.x & 31;
-  const float2 wq_a = *reinterpret_cast<const float2*>(wq + 2 * lane);
-  const float2 wq_b = *reinterpret_cast<const float2*>(wq + 64 + 2 * lane);
-  const float2 wk_a = *reinterpret_cast<const float2*>(wk + 2 * lane);
-  const float2 wk_b = *reinterpret_cast<const float2*>(wk + 64 + 2 * lane);
+  const int hl = lane & 15;  // lane within the half-warp
+  const int heads = hq + hk;
+  const int64_t tasks = tokens * heads;
   const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); t < tokens; t += nw) {
+  // Warp-uniform loop over task pairs (the shuffles below span the warp);
+  // a half-warp past the last task computes on zeros and stores nothing.
+  for (int64_t pr = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); 2 * pr < tasks;
+       pr += nw) {
+    const int64_t task = 2 * pr + (lane >> 4);
+    const bool live = task < tasks;
+    const int64_t t = live ? task / heads : 0;
+    const int hd = live ? static_cast<int>(task % heads) : 0;
     const int pos = static_cast<int>(t % seq);
-    const float2 cs = *reinterpret_cast<const float2*>(cos_t + pos * 64 + 2 * lane);
-    const float2 sn = *reinterpret_cast<const float2*>(sin_t + pos * 64 + 2 * lane);
-    __half* row = qkv + t * ld;
-#pragma unroll 4
-    for (int hd = 0; hd < hq + hk; ++hd) {
-      __half* p = row + static_cast<int64_t>(hd) * 128;
-      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(p + 2 * lane));
-      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(p + 64 + 2 * lane));
-      float ss = a.x * a.x + a.y * a.y + b.x * b.x + b.y * b.y;
-      ss = warp_sum(ss);
-      const float inv = 1.0f / sqrtf(ss / 128.0f + eps);
-      const float2 wa = hd < hq ? wq_a : wk_a;
-      const float2 wb = hd < hq ? wq_b : wk_b;
-      const float a0 = a.x * inv * wa.x, a1 = a.y * inv * wa.y;
-      const float b0 = b.x * inv * wb.x, b1 = b.y * inv * wb.y;
-      *reinterpret_cast<__half2*>(p + 2 * lane) =
-          __floats2half2_rn(a0 * cs.x - b0 * sn.x, a1 * cs.y - b1 * sn.y);
-      *reinterpret_cast<__half2*>(p + 64 + 2 * lane) =
-          __floats2half2_rn(b0 * cs.x + a0 * sn.x, b1 * cs.y + a1 * sn.y);
+    __half* p = qkv + t * ld + static_cast<int64_t>(hd) * 128;
+    const uint2 ua = live ? *reinterpret_cast<const uint2*>(p + 4 * hl) : make_uint2(0u, 0u);
+    const uint2 ub = live ? *reinterpret_cast<const uint2*>(p + 64 + 4 * hl) : make_uint2(0u, 0u);
+    const float2 a01 = __half22float2(*reinterpret_cast<const __half2*>(&ua.x));
+    const float2 a23 = __half22float2(*reinterpret_cast<const __half2*>(&ua.y));
+    const float2 b01 = __half22float2(*reinterpret_cast<const __half2*>(&ub.x));
+    const float2 b23 = __half22float2(*reinterpret_cast<const __half2*>(&ub.y));
+    const float a[4] = {a01.x, a01.y, a23.x, a23.y};
+    const float bb[4] = {b01.x, b01.y, b23.x, b23.y};
+    float ss = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ss += a[e] * a[e] + bb[e] * bb[e];
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = 1.0f / sqrtf(ss / 128.0f + eps);
+    const float* w = hd < hq ? wq : wk;
+    const float4 wa = *reinterpret_cast<const float4*>(w + 4 * hl);
+    const float4 wb = *reinterpret_cast<const float4*>(w + 64 + 4 * hl);
+    const float4 cs = *reinterpret_cast<const float4*>(cos_t + pos * 64 + 4 * hl);
+    const float4 sn = *reinterpret_cast<const float4*>(sin_t + pos * 64 + 4 * hl);
+    const float wa4[4] = {wa.x, wa.y, wa.z, wa.w}, wb4[4] = {wb.x, wb.y, wb.z, wb.w};
+    const float c4[4] = {cs.x, cs.y, cs.z, cs.w}, s4[4] = {sn.x, sn.y, sn.z, sn.w};
+    float oa[4], ob[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float a0 = a[e] * inv * wa4[e], b0 = bb[e] * inv * wb4[e];
+      oa[e] = a0 * c4[e] - b0 * s4[e];
+      ob[e] = b0 * c4[e] + a0 * s4[e];
+    }
+    const __half2 oa01 = __floats2half2_rn(oa[0], oa[1]), oa23 = __floats2half2_rn(oa[2], oa[3]);
+    const __half2 ob01 = __floats2half2_rn(ob[0], ob[1]), ob23 = __floats2half2_rn(ob[2], ob[3]);
+    if (live) {
+      *reinterpret_cast<uint2*>(p + 4 * hl) =
+          make_uint2(*reinterpret_cast<const uint32_t*>(&oa01), *reinterpret_cast<const uint32_t*>(&oa23));
+      *reinterpret_cast<uint2*>(p + 64 + 4 * hl) =
+          make_uint2(*reinterpret_cast<const uint32_t*>(&ob01), *reinterpret_cast<const uint32_t*>(&ob23));
     }
   }
 }
@@ -452,7 +475,11 @@ int launch_gelu_f16(void* y, int64_t count, cudaStream_t st) {
 int launch_qk_norm_rope(void* qkv, int64_t ld, int64_t tokens, int hq, int hk, const float* wq,
                         const float* wk, float eps, const float* cos_t, const float* sin_t, int seq,
                         cudaStream_t st) {
-  qk_norm_rope_kernel<<<grid_for_rows(tokens, 8), 256, 0, st>>>(
+  if ((ld % 4) != 0 || (reinterpret_cast<uintptr_t>(qkv) & 7) != 0) return RB_E_SHAPE;  // 8-byte vectors
+  int64_t blocks = (tokens * (hq + hk) + 15) / 16;  // two tasks per warp, 8 warps per block
+  if (blocks > 148 * 64) blocks = 148 * 64;
+  if (blocks < 1) blocks = 1;
+  qk_norm_rope_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(
       reinterpret_cast<__half*>(qkv), ld, tokens, hq, hk, wq, wk, eps, cos_t, sin_t, seq);
   return RB_LAUNCH_OK();
 }
