@@ -236,8 +236,10 @@ static size_t dtype_bytes(int dt) {
 }
 
 // ------------------------------------------------------------------ ops
+// pre_scale != null: x holds W8A8 activation codes int8 [m, k] with these
+// per-row scales (as rb_quantize_rows_i8 / rb_add_layer_norm_quant give).
 static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int64_t m,
-                         int64_t k, void* y, int y_dtype, cudaStream_t st) {
+                         int64_t k, void* y, int y_dtype, cudaStream_t st, const float* pre_scale = nullptr) {
   auto it = e->weights.find(id);
   if (it == e->weights.end()) return fail(RB_E_SHAPE, "weight id %lld is not packed", (long long)id);
   const Weight& w = it->second;
@@ -356,14 +358,22 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
     return RB_OK;
   }
   if (w.kind == RB_WEIGHT_W8A8) {
-    const size_t codes_bytes = (static_cast<size_t>(m) * k + 255) & ~size_t(255);
-    if ((rc = e->act.grow(codes_bytes, "w8a8 activation codes")) != RB_OK) return rc;
-    if ((rc = e->rowscale.grow(static_cast<size_t>(m) * 4, "w8a8 row scales")) != RB_OK) return rc;
-    int8_t* codes = reinterpret_cast<int8_t*>(e->act.ptr);
-    float* rs = reinterpret_cast<float*>(e->rowscale.ptr);
-    if ((rc = launch_quantize_rows_i8(x, x_dtype, m, k, w.in_scale, codes, rs, st)) != RB_OK)
-      return fail(rc, "row quantiser launch failed");
-    g_launches++;
+    const int8_t* codes = reinterpret_cast<const int8_t*>(x);
+    const float* rs = pre_scale;
+    if (!pre_scale) {
+      const size_t codes_bytes = (static_cast<size_t>(m) * k + 255) & ~size_t(255);
+      if ((rc = e->act.grow(codes_bytes, "w8a8 activation codes")) != RB_OK) return rc;
+      if ((rc = e->rowscale.grow(static_cast<size_t>(m) * 4, "w8a8 row scales")) != RB_OK) return rc;
+      int8_t* c8 = reinterpret_cast<int8_t*>(e->act.ptr);
+      float* r32 = reinterpret_cast<float*>(e->rowscale.ptr);
+      if ((rc = launch_quantize_rows_i8(x, x_dtype, m, k, w.in_scale, c8, r32, st)) != RB_OK)
+        return fail(rc, "row quantiser launch failed");
+      g_launches++;
+      codes = c8;
+      rs = r32;
+    } else if ((reinterpret_cast<uintptr_t>(x) & 15) != 0 || k % 16 != 0) {
+      return fail(RB_E_SHAPE, "w8a8 codes input: 16-byte aligned rows needed (k %% 16 == 0)");
+    }
     CUtensorMap tmA, tmC;
     if ((rc = make_tmap_2d(&tmA, codes, 1, m, k, k, 128, 128, 128)) != RB_OK) return rc;
     L.s_row = rs;
@@ -919,6 +929,29 @@ int rb_matmul(int64_t id, const void* x, int x_dtype, int64_t m, int64_t k, void
   if (rc) return rc;
   if (!x || !y) return fail(RB_E_SHAPE, "null matmul buffer");
   return matmul_locked(e, id, x, x_dtype, m, k, y, y_dtype, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int rb_matmul_w8a8_codes(int64_t id, const int8_t* codes, const float* row_scale, int64_t m, int64_t k, void* y,
+                         int y_dtype, void* stream) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Engine* e;
+  int rc = ensure_engine(&e);
+  if (rc) return rc;
+  if (!codes || !row_scale || !y) return fail(RB_E_SHAPE, "null matmul buffer");
+  auto it = e->weights.find(id);
+  if (it == e->weights.end() || it->second.kind != RB_WEIGHT_W8A8)
+    return fail(RB_E_SHAPE, "weight id %lld is not a W8A8 weight", (long long)id);
+  return matmul_locked(e, id, codes, RB_DTYPE_F16, m, k, y, y_dtype, reinterpret_cast<cudaStream_t>(stream),
+                       row_scale);
+}
+
+int rb_add_layer_norm_quant(float* x, const void* delta_f16, const float* g, const float* b, float eps,
+                            int8_t* codes, float* row_scale, int64_t rows, int64_t d, void* stream) {
+  if (!x || !g || !b || !codes || !row_scale || rows <= 0) return fail(RB_E_SHAPE, "add_layer_norm_quant: bad arguments");
+  const int rc = launch_add_layer_norm_quant(x, delta_f16, g, b, eps, codes, row_scale, rows, static_cast<int>(d),
+                                             reinterpret_cast<cudaStream_t>(stream));
+  g_launches++;
+  return rc == RB_OK ? RB_OK : fail(rc, "add_layer_norm_quant: unsupported width %lld", (long long)d);
 }
 
 int rb_matmul_host(int64_t id, const void* x_host, int x_dtype, int64_t m, int64_t k, void* y_host,

@@ -449,6 +449,88 @@ int launch_add_rms_norm(float* x, const void* delta, const float* w, float eps, 
   return RB_LAUNCH_OK();
 }
 
+// add_layer_norm_kernel followed by the W8A8 dynamic per-row activation
+// quantiser, without the f16 round trip through memory: the normalised row
+// is rounded to f16 (the value the separate quantiser would read), then
+// s = max(max|h| / 127, 1e-12) and code = clamp(rint(h * (1/s)), -128, 127)
+// exactly as quantize_rows_kernel (ext.rs:1236-1238, 1263-1279), so codes and
+// scales are bit-identical to layer norm + rb_quantize_rows_i8.
+template <int NV>
+__global__ void add_layer_norm_quant_kernel(float* x, const __half* delta, const float* g, const float* b,
+                                            float eps, int8_t* codes, float* row_scale, int64_t rows) {
+  constexpr int D = 128 * NV;
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += nw) {
+    float v[4 * NV];
+    float sum = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = j * 128 + lane * 4;
+      float4 xv = *reinterpret_cast<const float4*>(x + r * D + c);
+      if (delta) {
+        const uint2 d2 = *reinterpret_cast<const uint2*>(delta + r * D + c);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&d2.x));
+        const float2 bb = __half22float2(*reinterpret_cast<const __half2*>(&d2.y));
+        xv.x += a.x; xv.y += a.y; xv.z += bb.x; xv.w += bb.y;
+        *reinterpret_cast<float4*>(x + r * D + c) = xv;
+      }
+      v[4 * j] = xv.x; v[4 * j + 1] = xv.y; v[4 * j + 2] = xv.z; v[4 * j + 3] = xv.w;
+      sum += (xv.x + xv.y) + (xv.z + xv.w);
+    }
+    const float mean = warp_sum(sum) / static_cast<float>(D);
+    float var = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4 * NV; ++i) {
+      const float dv = v[i] - mean;
+      var = fmaf(dv, dv, var);
+    }
+    var = warp_sum(var) / static_cast<float>(D);
+    const float inv = 1.0f / sqrtf(var + eps);
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = j * 128 + lane * 4;
+      const float4 gv = *reinterpret_cast<const float4*>(g + c);
+      const float4 bv = *reinterpret_cast<const float4*>(b + c);
+      const float2 a = __half22float2(__floats2half2_rn((v[4 * j] - mean) * inv * gv.x + bv.x,
+                                                        (v[4 * j + 1] - mean) * inv * gv.y + bv.y));
+      const float2 bb = __half22float2(__floats2half2_rn((v[4 * j + 2] - mean) * inv * gv.z + bv.z,
+                                                         (v[4 * j + 3] - mean) * inv * gv.w + bv.w));
+      v[4 * j] = a.x; v[4 * j + 1] = a.y; v[4 * j + 2] = bb.x; v[4 * j + 3] = bb.y;
+      amax = fmaxf(fmaxf(amax, fmaxf(fabsf(a.x), fabsf(a.y))), fmaxf(fabsf(bb.x), fabsf(bb.y)));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float sc = fmaxf(__fdiv_rn(amax, 127.0f), 1e-12f);
+    const float qinv = __fdiv_rn(1.0f, sc);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = j * 128 + lane * 4;
+      char4 q;
+      q.x = static_cast<signed char>(fminf(fmaxf(rintf(__fmul_rn(v[4 * j], qinv)), -128.f), 127.f));
+      q.y = static_cast<signed char>(fminf(fmaxf(rintf(__fmul_rn(v[4 * j + 1], qinv)), -128.f), 127.f));
+      q.z = static_cast<signed char>(fminf(fmaxf(rintf(__fmul_rn(v[4 * j + 2], qinv)), -128.f), 127.f));
+      q.w = static_cast<signed char>(fminf(fmaxf(rintf(__fmul_rn(v[4 * j + 3], qinv)), -128.f), 127.f));
+      *reinterpret_cast<char4*>(codes + r * D + c) = q;
+    }
+    if (lane == 0) row_scale[r] = sc;
+  }
+}
+
+int launch_add_layer_norm_quant(float* x, const void* delta, const float* g, const float* b, float eps,
+                                int8_t* codes, float* row_scale, int64_t rows, int d, cudaStream_t st) {
+  const int grid = grid_for_rows(rows, 8);
+  const __half* dl = reinterpret_cast<const __half*>(delta);
+  switch (d) {
+    case 1152: add_layer_norm_quant_kernel<9><<<grid, 256, 0, st>>>(x, dl, g, b, eps, codes, row_scale, rows); break;
+    case 1024: add_layer_norm_quant_kernel<8><<<grid, 256, 0, st>>>(x, dl, g, b, eps, codes, row_scale, rows); break;
+    case 768: add_layer_norm_quant_kernel<6><<<grid, 256, 0, st>>>(x, dl, g, b, eps, codes, row_scale, rows); break;
+    default: return RB_E_UNSUPPORTED;
+  }
+  return RB_LAUNCH_OK();
+}
+
 int launch_add_layer_norm(float* x, const void* delta, const float* g, const float* b, float eps,
                           void* h, int64_t rows, int d, cudaStream_t st) {
   const int grid = grid_for_rows(rows, 8);

@@ -152,6 +152,8 @@ int launch_qk_norm_rope(void* qkv, int64_t ld, int64_t tokens, int hq, int hk, c
                         cudaStream_t st);
 // dst[r, h, 0:d] = src[r, h*d : h*d+d], dst[r, h, d:dp] = 0 (2-byte elements;
 // d and dp multiples of 8).
+int launch_add_layer_norm_quant(float* x, const void* delta, const float* g, const float* b, float eps,
+                                int8_t* codes, float* row_scale, int64_t rows, int d, cudaStream_t st);
 int launch_add_layer_norm(float* x, const void* delta, const float* g, const float* b, float eps,
                           void* h, int64_t rows, int d, cudaStream_t st);
 int launch_gelu_f16(void* y, int64_t count, cudaStream_t st);

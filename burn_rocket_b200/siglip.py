@@ -105,6 +105,9 @@ class SiglipTower:
         self.patches = torch.empty(T, h, dtype=torch.float32, device=dev)  # input patch embeddings
         self.x = torch.empty(T, h, dtype=torch.float32, device=dev)
         self.h = torch.empty(T, h, dtype=f16, device=dev)
+        # pre-LN rows quantised in the LayerNorm kernel for the W8A8 qkv / fc1 matmuls
+        self.hc = torch.empty(T, h, dtype=torch.int8, device=dev)
+        self.hs = torch.empty(T, dtype=torch.float32, device=dev)
         self.qkv = torch.empty(T, 3 * hq, dtype=f16, device=dev)
         self.attn = torch.empty(T, hq, dtype=f16, device=dev)
         self.o = torch.empty(T, h, dtype=f16, device=dev)
@@ -130,18 +133,23 @@ class SiglipTower:
         qkv_p = _dev_ptr(self.qkv)
         delta = None
         for L in self.layers:
-            _check(lib.rb_add_layer_norm(_dev_ptr(self.x), delta, _dev_ptr(L["ln1_g"]), _dev_ptr(L["ln1_b"]), cfg.eps,
-                                         _dev_ptr(self.h), T, h, st), "add_layer_norm")
-            matmul(self.h, L["qkv"], out=self.qkv, stream=stream)
+            _check(lib.rb_add_layer_norm_quant(_dev_ptr(self.x), delta, _dev_ptr(L["ln1_g"]), _dev_ptr(L["ln1_b"]),
+                                               cfg.eps, _dev_ptr(self.hc), _dev_ptr(self.hs), T, h, st),
+                   "add_layer_norm_quant")
+            _check(lib.rb_matmul_w8a8_codes(L["qkv"].id, _dev_ptr(self.hc), _dev_ptr(self.hs), T, h, qkv_p,
+                                            DTYPE_F16, st), "rocket_matmul", T, h, 3 * hq)
             _check(lib.rb_attention_batched(qkv_p, ld, qkv_p + hq * 2, ld, qkv_p + 2 * hq * 2, ld,
                                             _dev_ptr(self.attn), hq, DTYPE_F16, self.images, S, S,
                                             cfg.heads, cfg.heads, cfg.head_dim, 1.0 / math.sqrt(cfg.head_dim),
                                             0.0, MASK_NONE, -1, 0, 0, st),
                    "rocket_flash_attn", S, S, cfg.head_dim)
             matmul(self.attn, L["o"], out=self.o, stream=stream)
-            _check(lib.rb_add_layer_norm(_dev_ptr(self.x), _dev_ptr(self.o), _dev_ptr(L["ln2_g"]), _dev_ptr(L["ln2_b"]),
-                                         cfg.eps, _dev_ptr(self.h), T, h, st), "add_layer_norm")
-            matmul(self.h, L["fc1"], out=self.f, stream=stream)  # gelu_tanh(h W1^T), fused
+            _check(lib.rb_add_layer_norm_quant(_dev_ptr(self.x), _dev_ptr(self.o), _dev_ptr(L["ln2_g"]),
+                                               _dev_ptr(L["ln2_b"]), cfg.eps, _dev_ptr(self.hc), _dev_ptr(self.hs),
+                                               T, h, st), "add_layer_norm_quant")
+            _check(lib.rb_matmul_w8a8_codes(L["fc1"].id, _dev_ptr(self.hc), _dev_ptr(self.hs), T, h,
+                                            _dev_ptr(self.f), DTYPE_F16, st), "rocket_matmul", T, h, cfg.inter)
+            # (gelu_tanh(h W1^T) is fused into the fc1 epilogue)
             matmul(self.f, L["fc2"], out=self.d, stream=stream)
             delta = _dev_ptr(self.d)
         _check(lib.rb_add_layer_norm(_dev_ptr(self.x), delta, _dev_ptr(self.post_g), _dev_ptr(self.post_b), cfg.eps,

@@ -117,6 +117,19 @@ RB_API int64_t rb_pack_f32_w8a8_device(const float* w_dev, int64_t n, int64_t k,
  * [n_parts[i], k] of dtype src_dtype (RB_DTYPE_F32 / F16 / BF16) concatenated
  * along N and rounded to f16 (RNE); rb_matmul is then f16 x f16 with f32
  * accumulation. K % 8 == 0. */
+/* W8A8 matmul on activations already quantised per row (int8 codes [m, k],
+ * f32 scales [m], e.g. from rb_quantize_rows_i8 or rb_add_layer_norm_quant):
+ * the same product and epilogue as rb_matmul without the quantiser pass.
+ * codes must be 16-byte aligned with k % 16 == 0. */
+RB_API int rb_matmul_w8a8_codes(int64_t id, const int8_t* codes, const float* row_scale, int64_t m, int64_t k,
+                                void* y, int y_dtype, void* stream);
+/* rb_add_layer_norm with the W8A8 dynamic per-row quantiser fused in: writes
+ * int8 codes [rows, d] and f32 row scales [rows] of the f16-rounded normalised
+ * rows, bit-identical to rb_add_layer_norm then rb_quantize_rows_i8
+ * (ext.rs:1236-1238, 1263-1279), and no f16 rows. d in {768, 1024, 1152}. */
+RB_API int rb_add_layer_norm_quant(float* x, const void* delta_f16, const float* g, const float* b, float eps,
+                                   int8_t* codes, float* row_scale, int64_t rows, int64_t d, void* stream);
+
 /* Element-wise activation fused into the matmul epilogue of weight `id`
  * (no counterpart in the reference's trait; the GEMM-side form of its
  * rocket_gelu glue, host.rs:15-18): later rb_matmul calls on this weight write

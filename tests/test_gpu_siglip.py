@@ -58,6 +58,47 @@ def test_add_layer_norm(rb, d):
     rb.check_device_errors()
 
 
+@pytest.mark.parametrize("d", [768, 1024, 1152])
+def test_add_layer_norm_quant_matches_layer_norm_then_quantiser(rb, d):
+    """The fused LayerNorm + W8A8 row quantiser gives the codes and scales of
+    rb_add_layer_norm followed by rb_quantize_rows_i8, bit for bit, and the
+    code-input W8A8 matmul equals rb_matmul on the f16 rows bit for bit."""
+    import torch
+    import burn_rocket_b200._lib as L
+    lib = L.load()
+    rows = 333
+    g = torch.Generator(device="cuda").manual_seed(d)
+    x0 = torch.randn(rows, d, device="cuda", generator=g) * 3
+    delta = (torch.randn(rows, d, device="cuda", generator=g)).half()
+    gw = 1.0 + 0.1 * torch.randn(d, device="cuda", generator=g)
+    bw = 0.1 * torch.randn(d, device="cuda", generator=g)
+    xa, xb = x0.clone(), x0.clone()
+    h = torch.empty(rows, d, dtype=torch.float16, device="cuda")
+    assert lib.rb_add_layer_norm(xa.data_ptr(), delta.data_ptr(), gw.data_ptr(), bw.data_ptr(), 1e-6, h.data_ptr(),
+                                 rows, d, None) == 0
+    codes = torch.empty(rows, d, dtype=torch.int8, device="cuda")
+    scales = torch.empty(rows, dtype=torch.float32, device="cuda")
+    assert lib.rb_add_layer_norm_quant(xb.data_ptr(), delta.data_ptr(), gw.data_ptr(), bw.data_ptr(), 1e-6,
+                                       codes.data_ptr(), scales.data_ptr(), rows, d, None) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(xa, xb)  # the residual stream is updated alike
+    q, s = rb.quantize_rows_i8(h)
+    assert torch.equal(codes, q)
+    assert torch.equal(scales.view(torch.int32), s.view(torch.int32))
+    rng = np.random.default_rng(d)
+    n = 256
+    wid = rb.pack_qat(rng.integers(-127, 128, size=(n, d), dtype=np.int8), rng.random(n).astype(np.float32) * 1e-3,
+                      n, d)
+    y1 = torch.empty(rows, n, dtype=torch.float16, device="cuda")
+    y2 = torch.empty_like(y1)
+    rb.matmul(h, wid, out=y1)
+    assert lib.rb_matmul_w8a8_codes(wid.id, codes.data_ptr(), scales.data_ptr(), rows, d, y2.data_ptr(),
+                                    L.DTYPE_F16, None) == 0
+    torch.cuda.synchronize()
+    rb.check_device_errors()
+    assert torch.equal(y1, y2)
+
+
 def test_gelu_in_place(rb):
     import torch
     import burn_rocket_b200._lib as L
