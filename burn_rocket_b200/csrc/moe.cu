@@ -211,9 +211,11 @@ __global__ void moe_gather_kernel(const __half* __restrict__ x, int64_t hidden, 
     uint4* dst = reinterpret_cast<uint4*>(xp + r * hidden);
     if (real) {
       const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(token_of_row[r]) * hidden);
-      for (int64_t i = lane; i < v8; i += 32) dst[i] = src[i];
+#pragma unroll 8
+      for (int64_t i = lane; i < v8; i += 32) __stcs(dst + i, __ldg(src + i));  // loads in flight together
     } else {
-      for (int64_t i = lane; i < v8; i += 32) dst[i] = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll 8
+      for (int64_t i = lane; i < v8; i += 32) __stcs(dst + i, make_uint4(0u, 0u, 0u, 0u));
     }
   }
 }
@@ -243,6 +245,7 @@ int launch_moe_dispatch(const int32_t* ids, int64_t tokens, int top_k, int exper
 // ---------------------------------------------------------------- combine
 // One warp per token: x[t] (f32, in place) += w_j * y[row_j] over the
 // token's k slots in ascending expert id; each lane owns 8-column groups.
+template <int KMAX>
 __global__ void moe_combine_kernel(float* __restrict__ x, const __half* __restrict__ y, int64_t hidden,
                                    const int32_t* __restrict__ ids, const float* __restrict__ wts,
                                    const int32_t* __restrict__ row_of_slot, int64_t tokens, int k) {
@@ -263,10 +266,10 @@ __global__ void moe_combine_kernel(float* __restrict__ x, const __half* __restri
       if (ej < my_e || (ej == my_e && j < lane)) ++rank;
     }
     // order[r] = lane holding rank r
-    int ord_row[32];
-    float ord_w[32];
+    int ord_row[KMAX];
+    float ord_w[KMAX];
 #pragma unroll
-    for (int r = 0; r < 32; ++r) {
+    for (int r = 0; r < KMAX; ++r) {
       if (r >= k) break;
       const unsigned hit = __ballot_sync(0xffffffffu, lane < k && rank == r);
       const int src = __ffs(hit) - 1;
@@ -274,14 +277,19 @@ __global__ void moe_combine_kernel(float* __restrict__ x, const __half* __restri
       ord_w[r] = __shfl_sync(0xffffffffu, my_w, src);
     }
     float* xr = x + t * hidden;
+#pragma unroll 2
     for (int64_t c = lane * 8; c < hidden; c += 256) {
       float4 a0 = *reinterpret_cast<const float4*>(xr + c);
       float4 a1 = *reinterpret_cast<const float4*>(xr + c + 4);
       float acc[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      uint4 uv[KMAX];
 #pragma unroll
-      for (int r = 0; r < 32; ++r) {
+      for (int r = 0; r < KMAX; ++r)  // all of the token's rows in flight
+        if (r < k) uv[r] = __ldg(reinterpret_cast<const uint4*>(y + static_cast<int64_t>(ord_row[r]) * hidden + c));
+#pragma unroll
+      for (int r = 0; r < KMAX; ++r) {
         if (r >= k) break;
-        const uint4 u = *reinterpret_cast<const uint4*>(y + static_cast<int64_t>(ord_row[r]) * hidden + c);
+        const uint4 u = uv[r];
         const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -303,8 +311,12 @@ int launch_moe_combine(float* x, const void* y, int64_t hidden, const int32_t* i
   int64_t g = (tokens + 7) / 8;
   if (g > 148 * 16) g = 148 * 16;
   if (g < 1) g = 1;
-  moe_combine_kernel<<<static_cast<int>(g), 256, 0, st>>>(x, reinterpret_cast<const __half*>(y), hidden, ids, wts,
-                                                          ws + L.row_of_slot, tokens, top_k);
+  if (top_k <= 8)
+    moe_combine_kernel<8><<<static_cast<int>(g), 256, 0, st>>>(x, reinterpret_cast<const __half*>(y), hidden, ids,
+                                                              wts, ws + L.row_of_slot, tokens, top_k);
+  else
+    moe_combine_kernel<32><<<static_cast<int>(g), 256, 0, st>>>(x, reinterpret_cast<const __half*>(y), hidden, ids,
+                                                               wts, ws + L.row_of_slot, tokens, top_k);
   return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
 }
 
@@ -363,7 +375,8 @@ __global__ void gather_rows_kernel(const __half* __restrict__ in, const int32_t*
     const int64_t dst = inverse ? i : idx[i];
     const uint4* a = reinterpret_cast<const uint4*>(in + src * hidden);
     uint4* b = reinterpret_cast<uint4*>(out + dst * hidden);
-    for (int64_t c = lane; c < v8; c += 32) b[c] = a[c];
+#pragma unroll 8
+    for (int64_t c = lane; c < v8; c += 32) b[c] = __ldg(a + c);  // loads in flight together
   }
 }
 
@@ -404,8 +417,12 @@ int launch_moe_combine_rows(float* x, const void* y, int64_t hidden, const int32
   int64_t g = (tokens + 7) / 8;
   if (g > 148 * 16) g = 148 * 16;
   if (g < 1) g = 1;
-  moe_combine_kernel<<<static_cast<int>(g), 256, 0, st>>>(x, reinterpret_cast<const __half*>(y), hidden, ids, wts,
-                                                          row_of_slot, tokens, top_k);
+  if (top_k <= 8)
+    moe_combine_kernel<8><<<static_cast<int>(g), 256, 0, st>>>(x, reinterpret_cast<const __half*>(y), hidden, ids,
+                                                              wts, row_of_slot, tokens, top_k);
+  else
+    moe_combine_kernel<32><<<static_cast<int>(g), 256, 0, st>>>(x, reinterpret_cast<const __half*>(y), hidden, ids,
+                                                               wts, row_of_slot, tokens, top_k);
   return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
 }
 
