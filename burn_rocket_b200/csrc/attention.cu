@@ -511,39 +511,57 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
           tc_fence_after();
           const int j2 = j + 2;
           bool k2_ready = false;
-          for (int s = 0; s < 2; ++s) {
-            if (rlo[s] <= j && j <= rhi[s]) {
-              if (first_pv[s] && n_out[s] > 0) {
-                // O is overwritten: the previous item's O must have been read out.
-                if (!mbar_wait(&o_free[s], (n_out[s] - 1) & 1, p.err, abort_flag)) return false;
+          // Each slot's P·V(j), then its S(j + 2), in the order the two
+          // slots' P(j) become ready (polled), so a slot whose softmax ends
+          // first is not held behind the other.
+          bool pend[2] = {true, true};
+          const uint64_t t0 = global_timer_ns();
+          for (uint32_t spin = 1; pend[0] || pend[1]; ++spin) {
+            for (int s = 0; s < 2; ++s) {
+              if (!pend[s]) continue;
+              const bool has = rlo[s] <= j && j <= rhi[s];
+              if (has) {
+                if (!mbar_test(&p_full[2 * s + (n_pv[s] & 1)], (n_pv[s] >> 1) & 1)) continue;
                 tc_fence_after();
-              }
-              const int b = n_pv[s] & 1;
-              if (!mbar_wait(&p_full[2 * s + b], (n_pv[s] >> 1) & 1, p.err, abort_flag)) return false;
-              tc_fence_after();
-              const uint32_t o_tmem = tmem_base + s * 256 + 128;
-              const uint32_t p_tmem = tmem_base + s * 256 + b * 64;
-#pragma unroll
-              for (int ks = 0; ks < BN / 16; ++ks) {
-                const uint32_t acc = (!first_pv[s] || ks > 0) ? 1u : 0u;
-                const uint64_t vd = desc_add(v_desc, st * L::KV_TILE + ks * 2048);
-                umma_f16_ts(o_tmem, p_tmem + ks * 8, vd, idesc_o, acc);
-                if (L::TAIL) {  // O columns [64*ATOMS, D) from the tail atom (16 key rows = 512 B)
-                  const uint64_t vt = desc_add(vt_desc, st * L::KV_TILE + L::KV_TAIL_OFF + ks * 512);
-                  umma_f16_ts(o_tmem + L::ATOMS * 64, p_tmem + ks * 8, vt, idesc_ot, acc);
+                if (first_pv[s] && n_out[s] > 0) {
+                  // O is overwritten: the previous item's O must have been read out.
+                  if (!mbar_wait(&o_free[s], (n_out[s] - 1) & 1, p.err, abort_flag)) return false;
+                  tc_fence_after();
                 }
+                const int b = n_pv[s] & 1;
+                const uint32_t o_tmem = tmem_base + s * 256 + 128;
+                const uint32_t p_tmem = tmem_base + s * 256 + b * 64;
+#pragma unroll
+                for (int ks = 0; ks < BN / 16; ++ks) {
+                  const uint32_t acc = (!first_pv[s] || ks > 0) ? 1u : 0u;
+                  const uint64_t vd = desc_add(v_desc, st * L::KV_TILE + ks * 2048);
+                  umma_f16_ts(o_tmem, p_tmem + ks * 8, vd, idesc_o, acc);
+                  if (L::TAIL) {  // O columns [64*ATOMS, D) from the tail atom (16 key rows = 512 B)
+                    const uint64_t vt = desc_add(vt_desc, st * L::KV_TILE + L::KV_TAIL_OFF + ks * 512);
+                    umma_f16_ts(o_tmem + L::ATOMS * 64, p_tmem + ks * 8, vt, idesc_ot, acc);
+                  }
+                }
+                umma_commit(&o_done[s]);
+                ++n_pv[s];
+                first_pv[s] = false;
               }
-              umma_commit(&o_done[s]);
-              ++n_pv[s];
-              first_pv[s] = false;
+              if (j2 <= item.jb && rlo[s] <= j2 && j2 <= rhi[s]) {
+                if (!k2_ready) {
+                  if (!mbar_wait(&k_full[stage_of(j2)], phase_of(j2), p.err, abort_flag)) return false;
+                  tc_fence_after();
+                  k2_ready = true;
+                }
+                issue_s(j2, s);
+              }
+              pend[s] = false;
             }
-            if (j2 <= item.jb && rlo[s] <= j2 && j2 <= rhi[s]) {
-              if (!k2_ready) {
-                if (!mbar_wait(&k_full[stage_of(j2)], phase_of(j2), p.err, abort_flag)) return false;
-                tc_fence_after();
-                k2_ready = true;
+            if ((spin & 255u) == 0 && (pend[0] || pend[1])) {  // bounded like every other wait
+              if (*abort_flag) return false;
+              if (global_timer_ns() - t0 > kWaitLimitNs) {
+                *abort_flag = 1;
+                atomicOr(p.err, kErrWaitTimeout);
+                return false;
               }
-              issue_s(j2, s);
             }
           }
           umma_commit(&v_empty[st]);
