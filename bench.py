@@ -598,7 +598,7 @@ class MoeWorkload:
         ev[1].record()
         torch.cuda.synchronize()
         ms = ev[0].elapsed_time(ev[1]) / reps
-        return "grouped q8_0 gemm_kernel (experts gate|up + down of one layer)", ops / (ms / 1e3) / 1e12, ms
+        return "grouped q8_0 gemm_pair_kernel (experts gate|up + down of one layer)", ops / (ms / 1e3) / 1e12, ms
 
     @staticmethod
     def cpu_sample(orc, seed, timed_repeats=1):

@@ -1295,8 +1295,12 @@ int rb_matmul_grouped(int64_t id, int experts, const void* x_perm_f16, int64_t m
   L.err = e->err;
   L.num_sms = e->num_sms;
   L.tile_expert = reinterpret_cast<const int32_t*>(workspace) + ml.tile_expert;
-  // Grouped tiles are single-CTA with one 128-row M half (segments are 128-aligned).
-  const GemmPlan plan{n % 256 == 0 ? 256 : 128, 1, false};
+  // CTA-pair tiles (256 rows, one expert: segments are 256-row aligned) when
+  // the expert block is a multiple of 128 columns, else single-CTA 128-row
+  // tiles; RB_TILES_SINGLE forces the latter.
+  const bool pair = n % 128 == 0 && gemm_policy() != RB_TILES_SINGLE;
+  const GemmPlan plan = pair ? GemmPlan{n % 256 == 0 ? 256 : 128, 1, true}
+                             : GemmPlan{n % 256 == 0 ? 256 : 128, 1, false};
   CUtensorMap tmA, tmC;
   if ((rc = make_tmap_2d(&tmA, x_perm_f16, 2, max_rows, w.k, w.k, 64, 128, 128)) != RB_OK) return rc;
   const bool tstore = output_map(&tmC, y, y_dtype, max_rows, n_out);

@@ -354,6 +354,7 @@ int epi_path_default() {
 static std::atomic<int> g_policy{RB_TILES_AUTO};
 
 int set_gemm_policy(int policy) { return g_policy.exchange(policy); }
+int gemm_policy() { return g_policy.load(); }
 
 // Tile plan minimising the makespan of the persistent grid: rounds of tiles
 // per SM (per SM pair for the pair kernel) times the per-tile cost. A tile's

@@ -124,6 +124,16 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   const int num_kb = (K + Cfg::BK - 1) / Cfg::BK;
   const int pair = blockIdx.x >> 1;
   const int npairs = gridDim.x >> 1;
+  // Grouped GEMM (tile_expert != nullptr): the first weight row of tile t's
+  // expert block. Expert segments are 256-row aligned, so both 128-row
+  // halves of a pair tile share one expert (entries are per 128 rows); the
+  // tiles past the used segments (-1) form a suffix of the tile order, and
+  // every role stops at the first of them, so all roles see the same tiles.
+  auto expert_row0 = [&](int t) -> int {
+    if (!args.tile_expert) return 0;
+    const int e = __ldg(args.tile_expert + 2 * (t / tiles_n));
+    return e < 0 ? -1 : e * N;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < LSTAGES; ++s) {
@@ -170,8 +180,10 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       int ls = 0;
       uint32_t lph = 0;
       for (int t = pair; t < num_tiles; t += npairs) {
+        const int w0 = expert_row0(t);
+        if (w0 < 0) break;
         const int m0 = (t / tiles_n) * 256 + static_cast<int>(rank) * 128;
-        const int nb = (t % tiles_n) * BN + static_cast<int>(rank) * HB;
+        const int nb = w0 + (t % tiles_n) * BN + static_cast<int>(rank) * HB;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&ld_empty[ls], lph ^ 1, args.err, abort_flag)) goto producer_done;
           uint8_t* st = smem + ls * Cfg::LSTAGE;
@@ -194,6 +206,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       uint32_t lph = 0, bph = 0;
       int local = 0;
       for (int t = pair; t < num_tiles; t += npairs, ++local) {
+        if (expert_row0(t) < 0) break;
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait_cluster(&acc_empty[acc], acc_phase ^ 1, args.err, abort_flag)) goto mma_done;
@@ -232,6 +245,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       int bs = 0;
       uint32_t bph = 0;
       for (int t = pair; t < num_tiles; t += npairs) {
+        if (expert_row0(t) < 0) break;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&b_local[bs], bph, args.err, abort_flag)) goto fwd_b_done;
           mbar_arrive_cluster(mapa_shared(&b_full[bs], 0));
@@ -251,6 +265,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     int buf = 0;
     int local = 0;
     for (int t = pair; t < num_tiles; t += npairs, ++local) {
+      if (expert_row0(t) < 0) break;
       const int n0 = (t % tiles_n) * BN;
       const int m0 = (t / tiles_n) * 256 + static_cast<int>(rank) * 128;
       const int acc = local & 1;
@@ -271,7 +286,9 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       int cs = 0;
       uint32_t cph = 0;
       for (int t = pair; t < num_tiles; t += npairs) {
-        const int nb = (t % tiles_n) * BN + static_cast<int>(rank) * HB;
+        const int w0 = expert_row0(t);
+        if (w0 < 0) break;
+        const int nb = w0 + (t % tiles_n) * BN + static_cast<int>(rank) * HB;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&cd_empty[cs], cph ^ 1, args.err, abort_flag)) goto codes_done;
           uint8_t* st = smem + Cfg::CODE_OFF + cs * Cfg::CSTAGE;
@@ -289,6 +306,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     if (rank == 1 && elect_one_sync()) {
       int local = 0;
       for (int t = pair; t < num_tiles; t += npairs, ++local) {
+        if (expert_row0(t) < 0) break;
         const int acc = local & 1;
         if (!mbar_wait(&acc_local[acc], (local >> 1) & 1, args.err, abort_flag)) break;
         mbar_arrive_cluster(mapa_shared(&acc_empty[acc], 0));
@@ -311,6 +329,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     const int tid = threadIdx.x - (kDqWarp0 + grp * kGroupWarps) * 32;
     int q = 0;
     for (int t = pair; t < num_tiles; t += npairs) {
+      if (expert_row0(t) < 0) break;
       for (int kb = 0; kb < num_kb; ++kb, ++q) {
         if (q % Cfg::DQ_GROUPS != grp) continue;
         const int cs = q % Cfg::CSTAGES, bs = q % Cfg::BSTAGES;

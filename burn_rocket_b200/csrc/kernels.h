@@ -23,7 +23,7 @@ struct GemmLaunch {
   int ldo;
   int out_dtype;
   float out_scale;        // W8A8: 0 = unrounded output
-  const int* tile_expert; // grouped GEMM table (single-CTA 128-row tiles), or nullptr
+  const int* tile_expert; // grouped GEMM table (one expert id per 128 rows), or nullptr
   int gated;              // gate/up interleaved in 32-row blocks: out = silu(gate) * up, N/2 f16 columns
   int act;                // RB_ACT_*: element-wise activation before the f16 output rounding
   uint32_t* err;
@@ -43,6 +43,7 @@ struct GemmPlan {
 GemmPlan gemm_plan(bool i8, int M, int N, int K, int num_sms);
 // Restricts gemm_plan to single-CTA or (preferably) pair tiles; returns the old policy.
 int set_gemm_policy(int policy);
+int gemm_policy();
 int set_attention_split(int policy);
 // selftest.cu: one bounded wait on an mbarrier nothing arrives on.
 int launch_wait_timeout_probe(uint32_t* err, int64_t limit_ns, uint32_t* waited_us, cudaStream_t st);  // RB_ATTN_SPLIT_*; returns the previous one

@@ -7,9 +7,11 @@
 //   route     softmax over the E router logits of a token, top-k by
 //             probability (ties to the lower expert id), weights renormalised
 //             over the selected k (in selection order, f32);
-//   dispatch  per-expert row counts, 128-row-aligned expert segments in a
-//             permuted activation buffer, the M-tile -> expert table the
-//             grouped GEMM reads, and the gather of each routed token row;
+//   dispatch  per-expert row counts, 256-row-aligned expert segments in a
+//             permuted activation buffer (one CTA-pair tile of the grouped
+//             GEMM never spans two experts), the 128-row tile -> expert
+//             table the grouped GEMM reads, and the gather of each routed
+//             token row;
 //   combine   x[t] += w_j * y[row_j] over the token's k experts in ascending
 //             expert id (f32, product then sum, as the reference).
 //
@@ -30,13 +32,14 @@
 
 namespace rb {
 
-constexpr int kMoeSeg = 128;  // segment alignment = grouped-GEMM M tile
+constexpr int kMoeSeg = 256;   // expert segment alignment = grouped-GEMM CTA-pair M tile
+constexpr int kMoeTile = 128;  // rows per tile_expert entry = one CTA's M rows
 
 MoeLayout moe_layout(int64_t tokens, int top_k, int experts) {
   MoeLayout L{};
   L.max_rows = ((tokens * top_k + static_cast<int64_t>(experts) * (kMoeSeg - 1)) + kMoeSeg - 1) / kMoeSeg *
                kMoeSeg;
-  L.max_tiles = L.max_rows / kMoeSeg;
+  L.max_tiles = L.max_rows / kMoeTile;
   int64_t off = 0;
   L.counts = off; off += experts;
   L.seg_start = off; off += experts + 1;
@@ -132,29 +135,49 @@ int launch_moe_route(const float* logits, int64_t tokens, int experts, int top_k
 }
 
 // ---------------------------------------------------------------- dispatch
+// Count and scatter split the slots into one contiguous chunk per block and
+// aggregate in shared memory first: one global atomic per (block, expert)
+// instead of one per slot (the slots of a popular expert would otherwise
+// serialise on its counter).
+__device__ __forceinline__ void slot_chunk(int64_t slots, int64_t& s0, int64_t& s1) {
+  const int64_t chunk = (slots + gridDim.x - 1) / gridDim.x;
+  s0 = blockIdx.x * chunk;
+  s1 = s0 + chunk < slots ? s0 + chunk : slots;
+}
+
 __global__ void moe_count_kernel(const int32_t* __restrict__ ids, int64_t slots, int E, int32_t* counts,
                                  uint32_t* err) {
-  for (int64_t s = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; s < slots;
-       s += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+  __shared__ int32_t s_cnt[1024];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
+  __syncthreads();
+  int64_t s0, s1;
+  slot_chunk(slots, s0, s1);
+  for (int64_t s = s0 + threadIdx.x; s < s1; s += blockDim.x) {
     const int e = ids[s];
     if (e < 0 || e >= E) {
       atomicOr(err, kErrBadShape);
       continue;
     }
-    atomicAdd(&counts[e], 1);
+    atomicAdd(&s_cnt[e], 1);
   }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x)
+    if (s_cnt[e]) atomicAdd(&counts[e], s_cnt[e]);
 }
 
-// One block: exclusive scan of the 128-aligned segment sizes, the segment
-// starts, the insertion cursors and the M-tile -> expert table.
+// One block: exclusive scan of the 256-aligned segment sizes, the segment
+// starts, the insertion cursors and the 128-row tile -> expert table.
 __global__ void moe_offsets_kernel(const int32_t* __restrict__ counts, int E, int64_t max_tiles,
                                    int32_t* seg_start, int32_t* cursor, int32_t* tile_expert) {
   __shared__ int32_t s_start[1025];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) s_start[e] = (counts[e] + kMoeSeg - 1) / kMoeSeg * kMoeSeg;
+  __syncthreads();
   if (threadIdx.x == 0) {
     int32_t acc = 0;
     for (int e = 0; e < E; ++e) {
+      const int32_t sz = s_start[e];
       s_start[e] = acc;
-      acc += (counts[e] + kMoeSeg - 1) / kMoeSeg * kMoeSeg;
+      acc += sz;
     }
     s_start[E] = acc;
   }
@@ -163,13 +186,13 @@ __global__ void moe_offsets_kernel(const int32_t* __restrict__ counts, int E, in
     seg_start[e] = s_start[e];
     if (e < E) cursor[e] = s_start[e];
   }
-  const int64_t used = s_start[E] / kMoeSeg;
+  const int64_t used = s_start[E] / kMoeTile;
   for (int64_t mt = threadIdx.x; mt < max_tiles; mt += blockDim.x) {
     int32_t ex = -1;
     if (mt < used) {
       // expert whose segment holds tile mt (binary search over the starts)
       int lo = 0, hi = E - 1;
-      const int32_t row = static_cast<int32_t>(mt * kMoeSeg);
+      const int32_t row = static_cast<int32_t>(mt * kMoeTile);
       while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
         if (s_start[mid] <= row) lo = mid; else hi = mid - 1;
@@ -182,13 +205,30 @@ __global__ void moe_offsets_kernel(const int32_t* __restrict__ counts, int E, in
   }
 }
 
+// Pass 1 ranks each slot among its block's slots of the same expert (kept in
+// row_of_slot), one global atomic per expert then reserves the block's rows,
+// pass 2 turns ranks into rows. Each thread revisits only its own slots.
 __global__ void moe_scatter_kernel(const int32_t* __restrict__ ids, int64_t slots, int k, int E, int32_t* cursor,
                                    int32_t* row_of_slot, int32_t* token_of_row) {
-  for (int64_t s = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; s < slots;
-       s += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+  __shared__ int32_t s_cnt[1024];
+  __shared__ int32_t s_base[1024];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
+  __syncthreads();
+  int64_t s0, s1;
+  slot_chunk(slots, s0, s1);
+  for (int64_t s = s0 + threadIdx.x; s < s1; s += blockDim.x) {
     const int e = ids[s];
     if (e < 0 || e >= E) continue;
-    const int32_t row = atomicAdd(&cursor[e], 1);
+    row_of_slot[s] = atomicAdd(&s_cnt[e], 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x)
+    if (s_cnt[e]) s_base[e] = atomicAdd(&cursor[e], s_cnt[e]);
+  __syncthreads();
+  for (int64_t s = s0 + threadIdx.x; s < s1; s += blockDim.x) {
+    const int e = ids[s];
+    if (e < 0 || e >= E) continue;
+    const int32_t row = s_base[e] + row_of_slot[s];
     row_of_slot[s] = row;
     token_of_row[row] = static_cast<int32_t>(s / k);
   }
@@ -205,7 +245,7 @@ __global__ void moe_gather_kernel(const __half* __restrict__ x, int64_t hidden, 
   const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   const int64_t v8 = hidden / 8;
   for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); r < max_rows; r += nw) {
-    const int e = tile_expert[r / kMoeSeg];
+    const int e = tile_expert[r / kMoeTile];
     if (e < 0) continue;
     const bool real = (r - seg_start[e]) < counts[e];
     uint4* dst = reinterpret_cast<uint4*>(xp + r * hidden);
@@ -226,8 +266,8 @@ int launch_moe_dispatch(const int32_t* ids, int64_t tokens, int top_k, int exper
   const MoeLayout L = moe_layout(tokens, top_k, experts);
   const int64_t slots = tokens * top_k;
   if (cudaMemsetAsync(ws + L.counts, 0, sizeof(int32_t) * experts, st) != cudaSuccess) return RB_E_DEVICE;
-  int64_t g = (slots + 255) / 256;
-  if (g > 148 * 8) g = 148 * 8;
+  int64_t g = (slots + 2047) / 2048;  // ~8 slots a thread
+  if (g > 148) g = 148;
   if (g < 1) g = 1;
   moe_count_kernel<<<static_cast<int>(g), 256, 0, st>>>(ids, slots, experts, ws + L.counts, err);
   moe_offsets_kernel<<<1, 256, 0, st>>>(ws + L.counts, experts, L.max_tiles, ws + L.seg_start, ws + L.cursor,

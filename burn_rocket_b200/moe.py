@@ -12,7 +12,7 @@ torch spec `tools/clef_reference.py:179-246`): per layer
          w · down_e(silu(gate_e · n2) * (up_e · n2))                               (engine.rs:284-340)
 
 then the final RMSNorm of every token. The experts run as grouped Q8_0 GEMMs
-over expert-contiguous, 128-row-aligned segments of a permuted activation
+over expert-contiguous, 256-row-aligned segments of a permuted activation
 buffer (`rb_moe_dispatch`, `rb_matmul_grouped`, `rb_moe_combine`): the
 experts' gate and up weights form one gated Q8_0 weight whose grouped matmul
 writes silu(gate·x)·(up·x) directly (`pack_gated_q8_0`; the unfused gate|up

@@ -305,7 +305,8 @@ RB_API int rb_matmul_i8_acc(int64_t id, const int8_t* codes, int64_t m, int32_t*
  * route src/clef/model.rs:462-489, Buckets::build / combine
  * src/clef/engine.rs:284-340; device-side, so a layer stays graph-capturable). */
 /* Workspace bytes and permuted-row capacity for `tokens` x top_k routed slots
- * over `experts` (segments are 128-row aligned). */
+ * over `experts` (segments are 256-row aligned: one CTA-pair tile of the
+ * grouped GEMM never spans two experts). */
 RB_API int64_t rb_moe_workspace_bytes(int64_t tokens, int top_k, int experts);
 RB_API int64_t rb_moe_max_rows(int64_t tokens, int top_k, int experts);
 /* int32-word offset, inside the workspace, of the slot -> permuted-row map
