@@ -87,6 +87,31 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t ro
   return RB_OK;
 }
 
+// [rows, heads, d] view of head-strided f16 rows (dims: column in the head,
+// head, row): a box of box_d columns of one head reads the elements past d as
+// zeros, which stages a head narrower than the UMMA K granularity without a
+// padded copy.
+int make_tmap_heads(CUtensorMap* map, const void* base, uint64_t rows, uint64_t heads, uint64_t d,
+                    uint64_t row_stride_elems, uint32_t box_d, uint32_t box_rows, int swizzle_bytes) {
+  if (!load_encode_fn()) return fail(RB_E_DEVICE, "cuTensorMapEncodeTiled unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0)
+    return fail(RB_E_SHAPE, "tensor base %p is not 16-byte aligned", base);
+  if ((row_stride_elems * 2) % 16 != 0 || (d * 2) % 16 != 0)
+    return fail(RB_E_SHAPE, "head rows: strides must be multiples of 16 bytes");
+  cuuint64_t dims[3] = {d, heads, rows};
+  cuuint64_t strides[2] = {d * 2, row_stride_elems * 2};
+  cuuint32_t box[3] = {box_d, 1, box_rows};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_32B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(RB_E_DEVICE, "cuTensorMapEncodeTiled (heads) failed (%d) rows=%llu heads=%llu d=%llu", (int)r,
+                (unsigned long long)rows, (unsigned long long)heads, (unsigned long long)d);
+  return RB_OK;
+}
+
 int bn_index(int bn) {
   switch (bn) {
     case 256: return 0;
@@ -174,7 +199,6 @@ struct Engine {
   std::unordered_map<int64_t, Weight> weights;
   int64_t next_id = 1;
   Scratch act;       // activation staging (f16 or int8 codes)
-  Scratch pad;       // zero-padded attention heads (head_dim 72 -> 80)
   Scratch rowscale;  // per-row scales
   Scratch io_in, io_out, io_k, io_v;  // host-entry staging
   cudaStream_t host_stream = nullptr;
@@ -453,40 +477,28 @@ static int attention_locked(Engine* e, const void* q, int64_t ldq, const void* k
   } else if (dtype != RB_DTYPE_F16 && dtype != RB_DTYPE_BF16) {
     return fail(RB_E_SHAPE, "attention dtype %d", dtype);
   }
-  // head_dim 72 is staged as 80 (the UMMA K granularity): q/k/v are copied
-  // into zero-padded [rows, heads, 80] scratch and the output keeps 72 columns.
-  int d_stage = head_dim;
-  int64_t sq = ldq, sk = ldk, sv = ldv, cq = wq, ck = wk;
-  if (head_dim == 72) {
-    d_stage = 80;
-    const size_t pq = static_cast<size_t>(batch * n_q) * n_head * 80 * 2;
-    const size_t pk = static_cast<size_t>(batch * n_kv) * n_kv_heads * 80 * 2;
-    const size_t aq = (pq + 255) & ~size_t(255), ak = (pk + 255) & ~size_t(255);
-    if ((rc = e->pad.grow(aq + 2 * ak, "attention head padding")) != RB_OK) return rc;
-    uint8_t* base = reinterpret_cast<uint8_t*>(e->pad.ptr);
-    void* qp = base;
-    void* kp = base + aq;
-    void* vp = base + aq + ak;
-    if ((rc = launch_pad_heads(qh, ldq, batch * n_q, n_head, 72, qp, 80, st)) != RB_OK ||
-        (rc = launch_pad_heads(kh, ldk, batch * n_kv, n_kv_heads, 72, kp, 80, st)) != RB_OK ||
-        (rc = launch_pad_heads(vh, ldv, batch * n_kv, n_kv_heads, 72, vp, 80, st)) != RB_OK)
-      return fail(rc, "head_dim 72 staging: q/k/v need 16-byte-aligned rows (rc from the pad launch)");
-    g_launches += 3;
-    qh = qp; kh = kp; vh = vp;
-    cq = sq = static_cast<int64_t>(n_head) * 80;
-    ck = sk = sv = static_cast<int64_t>(n_kv_heads) * 80;
-  }
+  // head_dim 72 is staged as 80 (the UMMA K granularity) straight from the
+  // caller's rows: [rows, heads, 72] maps whose 16-column tail atom covers
+  // head columns 64..79, the last 8 past the head and so zero-filled by TMA.
+  // The output keeps 72 columns.
+  const int d_stage = head_dim == 72 ? 80 : head_dim;
+  const int64_t sq = ldq, sk = ldk, sv = ldv, cq = wq, ck = wk;
   CUtensorMap tm[6];
   // Q tiles are 128 query rows, K/V tiles 64 keys; 64-element (128-B) column
-  // atoms, plus 16-element (32-B) tail atoms for the padded 80-wide heads.
-  if ((rc = make_tmap_2d(&tm[0], qh, 2, batch * n_q, cq, sq, 64, 128, 128)) != RB_OK) return rc;
-  if ((rc = make_tmap_2d(&tm[1], kh, 2, batch * n_kv, ck, sk, 64, 64, 128)) != RB_OK) return rc;
-  if ((rc = make_tmap_2d(&tm[2], vh, 2, batch * n_kv, ck, sv, 64, 64, 128)) != RB_OK) return rc;
-  if (d_stage == 80) {
-    if ((rc = make_tmap_2d(&tm[3], qh, 2, batch * n_q, cq, sq, 16, 128, 32)) != RB_OK) return rc;
-    if ((rc = make_tmap_2d(&tm[4], kh, 2, batch * n_kv, ck, sk, 16, 64, 32)) != RB_OK) return rc;
-    if ((rc = make_tmap_2d(&tm[5], vh, 2, batch * n_kv, ck, sv, 16, 64, 32)) != RB_OK) return rc;
+  // atoms, plus 16-element (32-B) tail atoms for the 72-wide heads.
+  if (head_dim == 72) {
+    const uint64_t rq = batch * n_q, rk = batch * n_kv;
+    if ((rc = make_tmap_heads(&tm[0], qh, rq, n_head, 72, sq, 64, 128, 128)) != RB_OK ||
+        (rc = make_tmap_heads(&tm[1], kh, rk, n_kv_heads, 72, sk, 64, 64, 128)) != RB_OK ||
+        (rc = make_tmap_heads(&tm[2], vh, rk, n_kv_heads, 72, sv, 64, 64, 128)) != RB_OK ||
+        (rc = make_tmap_heads(&tm[3], qh, rq, n_head, 72, sq, 16, 128, 32)) != RB_OK ||
+        (rc = make_tmap_heads(&tm[4], kh, rk, n_kv_heads, 72, sk, 16, 64, 32)) != RB_OK ||
+        (rc = make_tmap_heads(&tm[5], vh, rk, n_kv_heads, 72, sv, 16, 64, 32)) != RB_OK)
+      return rc;
   } else {
+    if ((rc = make_tmap_2d(&tm[0], qh, 2, batch * n_q, cq, sq, 64, 128, 128)) != RB_OK) return rc;
+    if ((rc = make_tmap_2d(&tm[1], kh, 2, batch * n_kv, ck, sk, 64, 64, 128)) != RB_OK) return rc;
+    if ((rc = make_tmap_2d(&tm[2], vh, 2, batch * n_kv, ck, sv, 64, 64, 128)) != RB_OK) return rc;
     tm[3] = tm[0];
     tm[4] = tm[1];
     tm[5] = tm[2];
@@ -502,6 +514,7 @@ static int attention_locked(Engine* e, const void* q, int64_t ldq, const void* k
   L.n_head = n_head;
   L.n_kv_heads = n_kv_heads;
   L.head_dim = d_stage;
+  L.head_maps = head_dim == 72 ? 1 : 0;
   L.d_out = head_dim;
   L.ldq = static_cast<int>(sq);
   L.ldk = static_cast<int>(sk);
@@ -1217,7 +1230,7 @@ int rb_mem_stats(int64_t* weights_bytes, int64_t* scratch_bytes, int64_t* num_we
   for (auto& kv : e->weights) wb += static_cast<int64_t>(kv.second.bytes);
   if (weights_bytes) *weights_bytes = wb;
   if (scratch_bytes)
-    *scratch_bytes = static_cast<int64_t>(e->act.bytes + e->pad.bytes + e->rowscale.bytes + e->io_in.bytes +
+    *scratch_bytes = static_cast<int64_t>(e->act.bytes + e->rowscale.bytes + e->io_in.bytes +
                                           e->io_out.bytes + e->io_k.bytes + e->io_v.bytes);
   if (num_weights) *num_weights = static_cast<int64_t>(e->weights.size());
   return RB_OK;

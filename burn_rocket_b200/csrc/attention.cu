@@ -88,6 +88,7 @@ struct Params {
   int dlo, dhi;        // visible iff dlo <= (k_off + j) - (q_off + i) <= dhi
   int q_off, k_off;
   int d_out;           // output columns per head (<= D: the real head_dim)
+  int head3d;          // maps are [rows, heads, d_out] views: coordinates (column, head, row)
   // Sequences lie back to back: sequence b owns query rows [b*n_q, (b+1)*n_q)
   // and key rows [b*n_kv, (b+1)*n_kv) of the tensors.
   int batch;
@@ -396,6 +397,13 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
       tma_prefetch_desc(&tmV);
+      // Column `col` of head `head`, rows from `row`: a 2-D map over the
+      // rows' head-major columns, or a [rows, heads, d_out] view.
+      const bool h3 = p.head3d != 0;
+      auto load = [h3](void* dst, const CUtensorMap* map, uint64_t* bar, int head, int col, int row) {
+        if (h3) tma_load_3d(dst, map, bar, col, head, row);
+        else tma_load_2d(dst, map, bar, head * D + col, row);
+      };
       int kv_it = 0;  // K/V ring position, continued across items
       bool ok = true;
       for (int k = 0; ok && w.template next<SPLIT>(p, item); ++k) {
@@ -407,11 +415,11 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         mbar_arrive_expect_tx(q_full, nslots * L::Q_TILE);
         for (int s = 0; s < nslots; ++s) {
           for (int a = 0; a < L::ATOMS; ++a)
-            tma_load_2d(smem + L::Q_OFF + s * L::Q_TILE + a * L::Q_ATOM, &tmQ, q_full,
-                        U.sl[s].head * D + a * 64, q_row0 + U.sl[s].qt * BM);
+            load(smem + L::Q_OFF + s * L::Q_TILE + a * L::Q_ATOM, &tmQ, q_full, U.sl[s].head, a * 64,
+                 q_row0 + U.sl[s].qt * BM);
           if (L::TAIL)
-            tma_load_2d(smem + L::Q_OFF + s * L::Q_TILE + L::Q_TAIL_OFF, &tmQt, q_full,
-                        U.sl[s].head * D + L::ATOMS * 64, q_row0 + U.sl[s].qt * BM);
+            load(smem + L::Q_OFF + s * L::Q_TILE + L::Q_TAIL_OFF, &tmQt, q_full, U.sl[s].head, L::ATOMS * 64,
+                 q_row0 + U.sl[s].qt * BM);
         }
         for (int j = item.ja; j <= item.jb; ++j, ++kv_it) {
           const int st = kv_it % KV_STAGES;
@@ -419,19 +427,19 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
           if (!mbar_wait(&k_empty[st], ph, p.err, abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(&k_full[st], L::KV_TILE);
           for (int a = 0; a < L::ATOMS; ++a)
-            tma_load_2d(smem + L::K_OFF + st * L::KV_TILE + a * L::KV_ATOM, &tmK, &k_full[st],
-                        U.g * D + a * 64, kv_row0 + j * BN);
+            load(smem + L::K_OFF + st * L::KV_TILE + a * L::KV_ATOM, &tmK, &k_full[st], U.g, a * 64,
+                 kv_row0 + j * BN);
           if (L::TAIL)
-            tma_load_2d(smem + L::K_OFF + st * L::KV_TILE + L::KV_TAIL_OFF, &tmKt, &k_full[st],
-                        U.g * D + L::ATOMS * 64, kv_row0 + j * BN);
+            load(smem + L::K_OFF + st * L::KV_TILE + L::KV_TAIL_OFF, &tmKt, &k_full[st], U.g, L::ATOMS * 64,
+                 kv_row0 + j * BN);
           if (!mbar_wait(&v_empty[st], ph, p.err, abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(&v_full[st], L::KV_TILE);
           for (int a = 0; a < L::ATOMS; ++a)
-            tma_load_2d(smem + L::V_OFF + st * L::KV_TILE + a * L::KV_ATOM, &tmV, &v_full[st],
-                        U.g * D + a * 64, kv_row0 + j * BN);
+            load(smem + L::V_OFF + st * L::KV_TILE + a * L::KV_ATOM, &tmV, &v_full[st], U.g, a * 64,
+                 kv_row0 + j * BN);
           if (L::TAIL)
-            tma_load_2d(smem + L::V_OFF + st * L::KV_TILE + L::KV_TAIL_OFF, &tmVt, &v_full[st],
-                        U.g * D + L::ATOMS * 64, kv_row0 + j * BN);
+            load(smem + L::V_OFF + st * L::KV_TILE + L::KV_TAIL_OFF, &tmVt, &v_full[st], U.g, L::ATOMS * 64,
+                 kv_row0 + j * BN);
         }
       }
     }
@@ -966,6 +974,7 @@ int launch_attention(const CUtensorMap* tm, const AttnLaunch& L, cudaStream_t st
   p.softcap = L.softcap;
   p.err = L.err;
   p.d_out = L.d_out;
+  p.head3d = L.head_maps;
   p.batch = L.batch > 0 ? L.batch : 1;
   // Mask band in relative coordinates (key - query).
   auto clampw = [](int64_t w) { return static_cast<int>(w > (kNoBound / 2) ? (kNoBound / 2) : w); };

@@ -354,37 +354,7 @@ __global__ void last_token_l2_kernel(const float* x, int d, int seq, int batch, 
   for (int i = lane; i < d; i += 32) out[static_cast<int64_t>(b) * d + i] = row[i] * inv * w[i] * inv2;
 }
 
-// ---------------------------------------------------------------- head padding
-// One thread per 16-byte group (8 elements) of the padded output.
-__global__ void pad_heads_kernel(const uint16_t* __restrict__ src, int64_t ld_src, int64_t rows, int heads,
-                                 int d, uint16_t* __restrict__ dst, int dp) {
-  const int g_per_head = dp / 8, g_real = d / 8;
-  const int64_t total = rows * heads * g_per_head;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int gi = static_cast<int>(i % g_per_head);
-    const int64_t rh = i / g_per_head;
-    const int h = static_cast<int>(rh % heads);
-    const int64_t r = rh / heads;
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (gi < g_real) v = *reinterpret_cast<const uint4*>(src + r * ld_src + static_cast<int64_t>(h) * d + gi * 8);
-    *reinterpret_cast<uint4*>(dst + i * 8) = v;
-  }
-}
-
 // ---------------------------------------------------------------- launchers
-int launch_pad_heads(const void* src, int64_t ld_src, int64_t rows, int heads, int d, void* dst,
-                     int dp, cudaStream_t st) {
-  if (d % 8 || dp % 8 || dp < d || ld_src % 8) return RB_E_SHAPE;
-  if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) return RB_E_SHAPE;
-  int64_t g = (rows * heads * (dp / 8) + 255) / 256;
-  if (g > 148 * 32) g = 148 * 32;
-  if (g < 1) g = 1;
-  pad_heads_kernel<<<static_cast<int>(g), 256, 0, st>>>(reinterpret_cast<const uint16_t*>(src), ld_src, rows,
-                                                        heads, d, reinterpret_cast<uint16_t*>(dst), dp);
-  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
-}
-
 #define RB_LAUNCH_OK() (cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE)
 
 int launch_rms_norm(const void* x, int xdt, const float* w, float eps, void* y, int ydt, int64_t rows,

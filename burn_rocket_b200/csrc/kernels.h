@@ -123,6 +123,7 @@ struct AttnLaunch {
   int n_q, n_kv;  // per sequence
   int n_head, n_kv_heads, head_dim;  // head_dim: staged width (64, 80 or 128)
   int d_out;                          // output columns per head (real head_dim)
+  int head_maps;  // 1: the maps are [rows, heads, d_out] views (coordinates: column, head, row)
   int ldq, ldk, ldv, ldo;  // row strides in elements
   float scale, softcap;
   int mask_mode;
@@ -133,7 +134,8 @@ struct AttnLaunch {
   int* ws_cnt;    // kAttnCntBytes, zeroed once; counters reset themselves
 };
 // tm[0..2]: Q, K, V maps of the 64-column atoms (128-B swizzle); tm[3..5]: the
-// 16-column tail maps (32-B swizzle) used when head_dim == 80.
+// 16-column tail maps (32-B swizzle) used when head_dim == 80 (72-wide heads
+// staged as 80 through [rows, heads, 72] maps, head_maps = 1).
 int launch_attention(const CUtensorMap* tm, const AttnLaunch& L, cudaStream_t stream);
 
 // Glue (glue.cu).
@@ -158,8 +160,6 @@ int launch_add_layer_norm_quant(float* x, const void* delta, const float* g, con
 int launch_add_layer_norm(float* x, const void* delta, const float* g, const float* b, float eps,
                           void* h, int64_t rows, int d, cudaStream_t st);
 int launch_gelu_f16(void* y, int64_t count, cudaStream_t st);
-int launch_pad_heads(const void* src, int64_t ld_src, int64_t rows, int heads, int d, void* dst,
-                     int dp, cudaStream_t st);
 int launch_last_token_l2(const float* x, int d, int seq, int batch, const float* w, float eps,
                          float* out, cudaStream_t st);
 
