@@ -165,6 +165,31 @@ __global__ void embed_gather_kernel(const int32_t* ids, const __half* table, int
 
 // x [rows, D] f32 (+= delta f16 when non-null), then h = rms_norm(x, w) f16.
 // One warp per row; D = 32 * 4 * NV (D % 128 == 0), values kept in registers.
+// Row r of x (f32, D = 128 * NV; the lane owns the float4 groups at
+// j * 128 + 4 * lane) plus the f16 delta when non-null, the sum written back
+// to x. All of the row's loads are issued before its first store: the
+// compiler cannot prove x and delta distinct, and a store between two loads
+// would hold the later load back (one DRAM round trip per group).
+template <int NV>
+__device__ __forceinline__ void load_row_add(float* x, const __half* delta, int64_t r, int lane,
+                                             float4 (&xv)[NV]) {
+  constexpr int D = 128 * NV;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) xv[j] = *reinterpret_cast<const float4*>(x + r * D + j * 128 + lane * 4);
+  if (delta) {
+    uint2 d2[NV];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) d2[j] = *reinterpret_cast<const uint2*>(delta + r * D + j * 128 + lane * 4);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&d2[j].x));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&d2[j].y));
+      xv[j].x += a.x; xv[j].y += a.y; xv[j].z += b.x; xv[j].w += b.y;
+      *reinterpret_cast<float4*>(x + r * D + j * 128 + lane * 4) = xv[j];
+    }
+  }
+}
+
 template <int NV>
 __global__ void add_rms_norm_kernel(float* x, const __half* delta, const float* w, float eps,
                                     __half* h, int64_t rows) {
@@ -172,21 +197,14 @@ __global__ void add_rms_norm_kernel(float* x, const __half* delta, const float* 
   const int lane = threadIdx.x & 31;
   const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += nw) {
+    float4 xv[NV];
+    load_row_add<NV>(x, delta, r, lane, xv);
     float v[4 * NV];
     float ss = 0.0f;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
-      const int c = j * 128 + lane * 4;
-      float4 xv = *reinterpret_cast<const float4*>(x + r * D + c);
-      if (delta) {
-        const uint2 d2 = *reinterpret_cast<const uint2*>(delta + r * D + c);
-        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&d2.x));
-        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&d2.y));
-        xv.x += a.x; xv.y += a.y; xv.z += b.x; xv.w += b.y;
-        *reinterpret_cast<float4*>(x + r * D + c) = xv;
-      }
-      v[4 * j] = xv.x; v[4 * j + 1] = xv.y; v[4 * j + 2] = xv.z; v[4 * j + 3] = xv.w;
-      ss = fmaf(xv.x, xv.x, fmaf(xv.y, xv.y, fmaf(xv.z, xv.z, fmaf(xv.w, xv.w, ss))));
+      v[4 * j] = xv[j].x; v[4 * j + 1] = xv[j].y; v[4 * j + 2] = xv[j].z; v[4 * j + 3] = xv[j].w;
+      ss = fmaf(xv[j].x, xv[j].x, fmaf(xv[j].y, xv[j].y, fmaf(xv[j].z, xv[j].z, fmaf(xv[j].w, xv[j].w, ss))));
     }
     ss = warp_sum(ss);
     const float inv = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
@@ -214,21 +232,14 @@ __global__ void add_layer_norm_kernel(float* x, const __half* delta, const float
   const int lane = threadIdx.x & 31;
   const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += nw) {
+    float4 xv[NV];
+    load_row_add<NV>(x, delta, r, lane, xv);
     float v[4 * NV];
     float sum = 0.0f;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
-      const int c = j * 128 + lane * 4;
-      float4 xv = *reinterpret_cast<const float4*>(x + r * D + c);
-      if (delta) {
-        const uint2 d2 = *reinterpret_cast<const uint2*>(delta + r * D + c);
-        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&d2.x));
-        const float2 bb = __half22float2(*reinterpret_cast<const __half2*>(&d2.y));
-        xv.x += a.x; xv.y += a.y; xv.z += bb.x; xv.w += bb.y;
-        *reinterpret_cast<float4*>(x + r * D + c) = xv;
-      }
-      v[4 * j] = xv.x; v[4 * j + 1] = xv.y; v[4 * j + 2] = xv.z; v[4 * j + 3] = xv.w;
-      sum += (xv.x + xv.y) + (xv.z + xv.w);
+      v[4 * j] = xv[j].x; v[4 * j + 1] = xv[j].y; v[4 * j + 2] = xv[j].z; v[4 * j + 3] = xv[j].w;
+      sum += (xv[j].x + xv[j].y) + (xv[j].z + xv[j].w);
     }
     const float mean = warp_sum(sum) / static_cast<float>(D);
     float var = 0.0f;
@@ -432,21 +443,14 @@ __global__ void add_layer_norm_quant_kernel(float* x, const __half* delta, const
   const int lane = threadIdx.x & 31;
   const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += nw) {
+    float4 xv[NV];
+    load_row_add<NV>(x, delta, r, lane, xv);
     float v[4 * NV];
     float sum = 0.0f;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
-      const int c = j * 128 + lane * 4;
-      float4 xv = *reinterpret_cast<const float4*>(x + r * D + c);
-      if (delta) {
-        const uint2 d2 = *reinterpret_cast<const uint2*>(delta + r * D + c);
-        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&d2.x));
-        const float2 bb = __half22float2(*reinterpret_cast<const __half2*>(&d2.y));
-        xv.x += a.x; xv.y += a.y; xv.z += bb.x; xv.w += bb.y;
-        *reinterpret_cast<float4*>(x + r * D + c) = xv;
-      }
-      v[4 * j] = xv.x; v[4 * j + 1] = xv.y; v[4 * j + 2] = xv.z; v[4 * j + 3] = xv.w;
-      sum += (xv.x + xv.y) + (xv.z + xv.w);
+      v[4 * j] = xv[j].x; v[4 * j + 1] = xv[j].y; v[4 * j + 2] = xv[j].z; v[4 * j + 3] = xv[j].w;
+      sum += (xv[j].x + xv[j].y) + (xv[j].z + xv[j].w);
     }
     const float mean = warp_sum(sum) / static_cast<float>(D);
     float var = 0.0f;

@@ -236,7 +236,10 @@ __global__ void moe_scatter_kernel(const int32_t* __restrict__ ids, int64_t slot
 
 // One warp per permuted row: copy the routed token's f16 row, or zeros for
 // the padding rows of a segment. Rows of unused tiles are left alone (the
-// grouped GEMM skips those tiles).
+// grouped GEMM skips those tiles). The padding rows' outputs are never read,
+// but the grouped GEMMs measured 1.5-3% faster on zero padding rows than on
+// stale data (they run under the power cap), which more than repays the
+// zero writes.
 __global__ void moe_gather_kernel(const __half* __restrict__ x, int64_t hidden, int64_t max_rows,
                                   const int32_t* __restrict__ counts, const int32_t* __restrict__ seg_start,
                                   const int32_t* __restrict__ tile_expert, const int32_t* __restrict__ token_of_row,
@@ -247,16 +250,15 @@ __global__ void moe_gather_kernel(const __half* __restrict__ x, int64_t hidden, 
   for (int64_t r = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5); r < max_rows; r += nw) {
     const int e = tile_expert[r / kMoeTile];
     if (e < 0) continue;
-    const bool real = (r - seg_start[e]) < counts[e];
     uint4* dst = reinterpret_cast<uint4*>(xp + r * hidden);
-    if (real) {
-      const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(token_of_row[r]) * hidden);
-#pragma unroll 8
-      for (int64_t i = lane; i < v8; i += 32) __stcs(dst + i, __ldg(src + i));  // loads in flight together
-    } else {
+    if (r - seg_start[e] >= counts[e]) {  // segment padding
 #pragma unroll 8
       for (int64_t i = lane; i < v8; i += 32) __stcs(dst + i, make_uint4(0u, 0u, 0u, 0u));
+      continue;
     }
+    const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(token_of_row[r]) * hidden);
+#pragma unroll 8
+    for (int64_t i = lane; i < v8; i += 32) __stcs(dst + i, __ldg(src + i));  // loads in flight together
   }
 }
 

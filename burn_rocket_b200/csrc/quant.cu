@@ -201,7 +201,66 @@ __global__ void quantize_rows_vec_kernel(const uint4* __restrict__ x, int64_t m,
   }
 }
 
-// Long rows (k > 2048): stream the row twice instead of holding it (the
+// Rows of 2048 < k <= 1024 * V: one block of four warps per row holds the row
+// in registers (V 16-byte vectors a thread), so the row is read once. The
+// four warps' maxima meet in shared memory, double-buffered by row parity so
+// that one barrier per row suffices (a warp writes row i + 2's slot only
+// after every warp has passed row i + 1's barrier, i.e. has read row i's).
+template <int DT, int V>
+__global__ void __launch_bounds__(128) quantize_rows_block_kernel(const uint4* __restrict__ x, int64_t m,
+                                                                   int64_t k, float in_scale,
+                                                                   uint2* __restrict__ codes,
+                                                                   float* __restrict__ row_scale) {
+  __shared__ float s_max[2][4];
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int nv = static_cast<int>(k / 8);
+  int buf = 0;
+  for (int64_t row = blockIdx.x; row < m; row += gridDim.x, buf ^= 1) {
+    const uint4* xr = x + row * nv;
+    uint4 v[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i)
+      if (t + 128 * i < nv) v[i] = __ldg(xr + t + 128 * i);
+    float s = in_scale;
+    if (in_scale == 0.0f) {  // uniform over the grid
+      float amax = 0.0f;
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        if (t + 128 * i < nv) {
+          float f[8];
+          unpack8<DT>(v[i], f);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) amax = fmaxf(amax, fabsf(f[q]));
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      if (lane == 0) s_max[buf][warp] = amax;
+      __syncthreads();
+      amax = fmaxf(fmaxf(s_max[buf][0], s_max[buf][1]), fmaxf(s_max[buf][2], s_max[buf][3]));
+      s = fmaxf(__fdiv_rn(amax, 127.0f), 1e-12f);
+    }
+    const float inv = __fdiv_rn(1.0f, s);
+    uint2* q = codes + row * nv;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      if (t + 128 * i < nv) {
+        float f[8];
+        unpack8<DT>(v[i], f);
+        uint32_t b[2] = {0u, 0u};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int c = static_cast<int>(fminf(fmaxf(rintf(__fmul_rn(f[e], inv)), -128.f), 127.f));
+          b[e >> 2] |= (static_cast<uint32_t>(c) & 0xFFu) << (8 * (e & 3));
+        }
+        q[t + 128 * i] = make_uint2(b[0], b[1]);
+      }
+    }
+    if (t == 0) row_scale[row] = s;
+  }
+}
+
+// Longer rows (k > 8192): stream the row twice instead of holding it (the
 // second pass hits L1/L2), keeping registers low and many rows in flight.
 template <int DT>
 __global__ void quantize_rows_stream_kernel(const uint4* __restrict__ x, int64_t m, int64_t k,
@@ -255,6 +314,9 @@ static void launch_qrv(const void* x, int64_t m, int64_t k, float in_scale, int8
     quantize_rows_vec_kernel<DT, 4><<<blocks, 256, 0, stream>>>(xv, m, k, in_scale, cv, row_scale);
   } else if (nv <= 32 * 8) {
     quantize_rows_vec_kernel<DT, 8><<<blocks, 256, 0, stream>>>(xv, m, k, in_scale, cv, row_scale);
+  } else if (nv <= 128 * 8) {
+    const int64_t bb = m < 148 * 16 ? m : 148 * 16;
+    quantize_rows_block_kernel<DT, 8><<<static_cast<int>(bb), 128, 0, stream>>>(xv, m, k, in_scale, cv, row_scale);
   } else {
     const int sb = blocks < 148 * 8 ? blocks : 148 * 8;
     quantize_rows_stream_kernel<DT><<<sb, 256, 0, stream>>>(xv, m, k, in_scale, cv, row_scale);

@@ -233,8 +233,9 @@ RB_API int rb_attention_batched(const void* q, int64_t ldq, const void* k, int64
                                 int64_t q_start, int64_t kv_start, void* stream);
 
 /* head_dim 72 (the SigLIP-style config) is supported by every attention entry:
- * heads are staged zero-padded to 80 columns (the UMMA K granularity) in
- * engine scratch and the output keeps 72 columns. */
+ * heads are read in place and staged as 80 columns (the UMMA K granularity,
+ * the 8 columns past each head read as zeros) and the output keeps 72
+ * columns. */
 
 /* ---- glue ops of the RocketOps surface (ext.rs:70-83, 1054-1152; formulas
  * host.rs:15-72). Device buffers, any float dtype, asynchronous on `stream`. */
@@ -319,7 +320,7 @@ RB_API int rb_moe_route(const float* logits, int64_t tokens, int experts, int to
                         int32_t* ids, float* weights, void* stream);
 /* Buckets the routed slots per expert in `workspace` and gathers each slot's
  * f16 token row x[tokens, hidden] into x_perm[rb_moe_max_rows(), hidden]
- * (expert segments, padding rows zeroed). */
+ * (256-row-aligned expert segments, padding rows zeroed). */
 RB_API int rb_moe_dispatch(const int32_t* ids, int64_t tokens, int top_k, int experts, const void* x_f16,
                            int64_t hidden, void* workspace, void* x_perm_f16, void* stream);
 /* y_perm[r, :] = x_perm[r, :] · W_e^T for the expert e owning row r, where the
