@@ -286,7 +286,9 @@ __global__ void gelu_f16_kernel(__half* y, int64_t count8) {
 // wq, heads [hq, hq+hk) (k) use wk. Each half-warp takes one (token, head):
 // lane i of the 16 owns elements 4i..4i+3 and 64+4i..64+4i+3 (the rotate-half
 // pairs), read and written as 8-byte vectors; the head's sum of squares is
-// reduced over the 16 lanes.
+// reduced over the 16 lanes. Every operation is an explicitly rounded f32
+// intrinsic, so the GEMM epilogue that fuses this pass (kEpiQkRopeF16)
+// reproduces it bit for bit.
 __global__ void qk_norm_rope_kernel(__half* qkv, int64_t ld, int64_t tokens, int hq, int hk,
                                     const float* wq, const float* wk, float eps,
                                     const float* cos_t, const float* sin_t, int seq) {
@@ -315,10 +317,10 @@ __global__ void qk_norm_rope_kernel(__half* qkv, int64_t ld, int64_t tokens, int
     const float bb[4] = {b01.x, b01.y, b23.x, b23.y};
     float ss = 0.0f;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) ss += a[e] * a[e] + bb[e] * bb[e];
+    for (int e = 0; e < 4; ++e) ss = __fadd_rn(ss, __fadd_rn(__fmul_rn(a[e], a[e]), __fmul_rn(bb[e], bb[e])));
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float inv = 1.0f / sqrtf(ss / 128.0f + eps);
+    for (int o = 8; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(ss, 0.0078125f), eps)));
     const float* w = hd < hq ? wq : wk;
     const float4 wa = *reinterpret_cast<const float4*>(w + 4 * hl);
     const float4 wb = *reinterpret_cast<const float4*>(w + 64 + 4 * hl);
@@ -329,9 +331,9 @@ __global__ void qk_norm_rope_kernel(__half* qkv, int64_t ld, int64_t tokens, int
     float oa[4], ob[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const float a0 = a[e] * inv * wa4[e], b0 = bb[e] * inv * wb4[e];
-      oa[e] = a0 * c4[e] - b0 * s4[e];
-      ob[e] = b0 * c4[e] + a0 * s4[e];
+      const float a0 = __fmul_rn(__fmul_rn(a[e], inv), wa4[e]), b0 = __fmul_rn(__fmul_rn(bb[e], inv), wb4[e]);
+      oa[e] = __fsub_rn(__fmul_rn(a0, c4[e]), __fmul_rn(b0, s4[e]));
+      ob[e] = __fadd_rn(__fmul_rn(b0, c4[e]), __fmul_rn(a0, s4[e]));
     }
     const __half2 oa01 = __floats2half2_rn(oa[0], oa[1]), oa23 = __floats2half2_rn(oa[2], oa[3]);
     const __half2 ob01 = __floats2half2_rn(ob[0], ob[1]), ob23 = __floats2half2_rn(ob[2], ob[3]);

@@ -138,6 +138,18 @@ RB_API int rb_add_layer_norm_quant(float* x, const void* delta_f16, const float*
 #define RB_ACT_NONE 0
 #define RB_ACT_GELU_TANH 1
 RB_API int rb_set_weight_activation(int64_t id, int act);
+/* q/k RMSNorm + RoPE fused into later matmuls on Q8_0 weight `id`, whose
+ * output columns are [n_q_heads query heads | n_k_heads key heads | the rest]
+ * in heads of 128 (the fused q|k|v projection; the GEMM-epilogue form of the
+ * rb_qk_norm_rope glue, model.rs:369-376): each later rb_matmul writes the
+ * same f16 values rb_qk_norm_rope would give on the plain product, in the
+ * same pass. wq / wk [128], cos_t / sin_t [seq, 64] are f32 device arrays
+ * read by those later calls (they must stay allocated); a row's position is
+ * its index modulo seq. The output must be f16 and its column count a
+ * multiple of 128. n_q_heads = n_k_heads = 0 turns the fusion off. Returns
+ * RB_OK or RB_E_SHAPE. */
+RB_API int rb_set_weight_qk_norm_rope(int64_t id, int n_q_heads, int n_k_heads, const float* wq, const float* wk,
+                                      float eps, const float* cos_t, const float* sin_t, int seq);
 
 /* Gated (SwiGLU) Q8_0 weight from device-resident f32 gate and up weights,
  * each [n_inter, k] (n_inter a multiple of 64): rows are stored interleaved in
