@@ -61,6 +61,7 @@ PROFILES = {
     "w8a8": "gemm_pair_kernel_w8a8_8192x4304x1152_ncu.md",
     "qwen3": "gemm_pair_kernel_q8_0_8192x6144x1024_ncu.md",
     "siglip": "gemm_pair_kernel_w8a8_8192x4304x1152_ncu.md",
+    "moe": "gemm_pair_kernel_moe_grouped_ncu.md",
 }
 
 
@@ -526,13 +527,17 @@ class MoeWorkload:
     metric = "Qwen3-30B-A3B-style MoE prefill tok/s (config #5: 4 seq x 2048 tok, 48 layers, 128 experts top-8)"
     unit = "tok/s"
     BATCH, SEQ = 4, 2048
+    LAYERS = None  # --layers: fewer decoder layers, for small ncu captures of the same kernels
 
     def __init__(self, dev, seed, world=1, rank=0):
         import torch
+        from dataclasses import replace
         import burn_rocket_b200 as rb
         from burn_rocket_b200.moe import MoeConfig, MoeModel
         self.rb = rb
-        self.cfg = MoeConfig()
+        self.cfg = MoeConfig() if self.LAYERS is None else replace(MoeConfig(), layers=self.LAYERS)
+        if self.LAYERS is not None:
+            self.metric = self.metric + f" [profiling case: {self.LAYERS} layers, not config #5]"
         self.world = world
         g = torch.Generator(device="cpu").manual_seed(seed)
         ids = torch.randint(0, self.cfg.vocab, (self.BATCH * self.SEQ,), generator=g, dtype=torch.int32)
@@ -838,6 +843,9 @@ def main():
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying a CUDA graph")
     ap.add_argument("--tile-policy", default="auto", choices=["auto", "single", "pair"],
                     help="GEMM tile policy (rb_set_tile_policy)")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="moe: build only this many decoder layers (small ncu captures of the model's kernels; "
+                         "the line is then not config #5)")
     ap.add_argument("--gemm-shape", default=None,
                     help="q8gemm / w8a8: one M,N,K GEMM with f16 activations/outputs (profiling the model's shapes)")
     args = ap.parse_args()
@@ -853,6 +861,10 @@ def main():
         else:
             Q8GemmWorkload.M, Q8GemmWorkload.N, Q8GemmWorkload.K = m, n, k
             Q8GemmWorkload.X_DTYPE = "f16"
+    if args.layers is not None:
+        if args.workload != "moe" or args.layers < 1:
+            ap.error("--layers applies to --workload moe, with at least one layer")
+        MoeWorkload.LAYERS = args.layers
     if args.impl == "reference":
         run_reference(args)
     else:
