@@ -174,6 +174,9 @@ static bool output_map(CUtensorMap* map, void* y, int y_dtype, int64_t m, int64_
   return ok;
 }
 
+// Query-row chunks of the pipelined host-entry attention (rb_attention_host).
+constexpr int kHostAttnChunks = 4;
+
 struct Scratch {
   void* ptr = nullptr;
   size_t bytes = 0;
@@ -204,10 +207,31 @@ struct Engine {
   Scratch rowscale;  // per-row scales
   Scratch io_in, io_out, io_k, io_v;  // host-entry staging
   cudaStream_t host_stream = nullptr;
+  // Pipelined host-entry attention: copies in, kernels, copies out on three
+  // streams, ordered by events (created on first use).
+  cudaStream_t pipe_in = nullptr, pipe_out = nullptr;
+  cudaEvent_t pipe_ev[2 * kHostAttnChunks + 1] = {};
+  bool pipe_ready = false;
 };
 
 static std::mutex g_mu;
 static Engine* g_engine = nullptr;
+
+static int ensure_pipe(Engine* e) {
+  if (e->pipe_ready) return RB_OK;
+  if (cudaStreamCreateWithFlags(&e->pipe_in, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&e->pipe_out, cudaStreamNonBlocking) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(RB_E_DEVICE, "attention host pipeline: stream creation failed");
+  }
+  for (cudaEvent_t& ev : e->pipe_ev)
+    if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(RB_E_DEVICE, "attention host pipeline: event creation failed");
+    }
+  e->pipe_ready = true;
+  return RB_OK;
+}
 static std::atomic<int64_t> g_launches{0};
 
 static int ensure_engine(Engine** out) {
@@ -1030,11 +1054,59 @@ int rb_attention_host(const void* q, const void* k, const void* v, void* out, in
   if ((rc = e->io_in.grow(qb, "q staging")) || (rc = e->io_out.grow(qb, "out staging")) ||
       (rc = e->io_k.grow(kb, "k staging")) || (rc = e->io_v.grow(kb, "v staging")))
     return rc;
+  const int64_t wq = (int64_t)n_head * head_dim, wk = (int64_t)n_kv_heads * head_dim;
+  // Long full-sequence calls are pipelined: K and V go over first (every
+  // query reads all keys), then the query rows in chunks of whole 128-row
+  // tiles, each chunk's attention (the same mask as a block mode at the
+  // chunk's query offset) starting once its rows are on the device and its
+  // output going back while later chunks still copy in or compute. Each
+  // row's result is the unchunked call's up to f32 summation order.
+  const bool full_seq = mask_mode == RB_MASK_NONE || mask_mode == RB_MASK_CAUSAL ||
+                        mask_mode == RB_MASK_WINDOW || mask_mode == RB_MASK_CAUSAL_WINDOW;
+  if (full_seq && n_q == n_kv && n_q >= 2048 && dtype != RB_DTYPE_F32) {
+    if ((rc = ensure_pipe(e)) != RB_OK) return rc;
+    const int block_mode = mask_mode == RB_MASK_NONE     ? RB_MASK_NONE_BLOCK
+                           : mask_mode == RB_MASK_WINDOW ? RB_MASK_WINDOW_BLOCK
+                                                         : RB_MASK_CAUSAL_BLOCK;
+    const int64_t win = mask_mode == RB_MASK_CAUSAL ? -1 : window;
+    const int64_t rows = ((n_q + kHostAttnChunks - 1) / kHostAttnChunks + 127) / 128 * 128;
+    cudaStream_t s_in = e->pipe_in, s_cmp = e->host_stream, s_out = e->pipe_out;
+    cudaEvent_t* ev = e->pipe_ev;  // [0]: K and V in; [1 + c]: chunk c in; [1 + C + c]: chunk c done
+    const size_t row_b = static_cast<size_t>(wq) * eb;
+    RB_CUDA(cudaMemcpyAsync(e->io_k.ptr, k, kb, cudaMemcpyHostToDevice, s_in), "H2D k");
+    RB_CUDA(cudaMemcpyAsync(e->io_v.ptr, v, kb, cudaMemcpyHostToDevice, s_in), "H2D v");
+    RB_CUDA(cudaEventRecord(ev[0], s_in), "event");
+    RB_CUDA(cudaStreamWaitEvent(s_cmp, ev[0], 0), "event wait");
+    int c = 0;
+    for (int64_t r0 = 0; r0 < n_q; r0 += rows, ++c) {
+      const int64_t nr = n_q - r0 < rows ? n_q - r0 : rows;
+      uint8_t* qd = reinterpret_cast<uint8_t*>(e->io_in.ptr) + r0 * row_b;
+      uint8_t* od = reinterpret_cast<uint8_t*>(e->io_out.ptr) + r0 * row_b;
+      RB_CUDA(cudaMemcpyAsync(qd, reinterpret_cast<const uint8_t*>(q) + r0 * row_b, nr * row_b,
+                              cudaMemcpyHostToDevice, s_in), "H2D q chunk");
+      RB_CUDA(cudaEventRecord(ev[1 + c], s_in), "event");
+      RB_CUDA(cudaStreamWaitEvent(s_cmp, ev[1 + c], 0), "event wait");
+      if ((rc = attention_locked(e, qd, wq, e->io_k.ptr, wk, e->io_v.ptr, wk, od, wq, dtype, 1, nr, n_kv,
+                                 n_head, n_kv_heads, head_dim, scale, softcap, block_mode, win, r0, 0,
+                                 s_cmp)) != RB_OK) {
+        cudaStreamSynchronize(s_in);
+        cudaStreamSynchronize(s_cmp);
+        cudaStreamSynchronize(s_out);
+        return rc;
+      }
+      RB_CUDA(cudaEventRecord(ev[1 + kHostAttnChunks + c], s_cmp), "event");
+      RB_CUDA(cudaStreamWaitEvent(s_out, ev[1 + kHostAttnChunks + c], 0), "event wait");
+      RB_CUDA(cudaMemcpyAsync(reinterpret_cast<uint8_t*>(out) + r0 * row_b, od, nr * row_b,
+                              cudaMemcpyDeviceToHost, s_out), "D2H out chunk");
+    }
+    RB_CUDA(cudaStreamSynchronize(s_out), "attention sync");
+    RB_CUDA(cudaStreamSynchronize(s_cmp), "attention sync");
+    return RB_OK;
+  }
   cudaStream_t st = e->host_stream;
   RB_CUDA(cudaMemcpyAsync(e->io_in.ptr, q, qb, cudaMemcpyHostToDevice, st), "H2D q");
   RB_CUDA(cudaMemcpyAsync(e->io_k.ptr, k, kb, cudaMemcpyHostToDevice, st), "H2D k");
   RB_CUDA(cudaMemcpyAsync(e->io_v.ptr, v, kb, cudaMemcpyHostToDevice, st), "H2D v");
-  const int64_t wq = (int64_t)n_head * head_dim, wk = (int64_t)n_kv_heads * head_dim;
   if ((rc = attention_locked(e, e->io_in.ptr, wq, e->io_k.ptr, wk, e->io_v.ptr, wk, e->io_out.ptr, wq,
                              dtype, 1, n_q, n_kv, n_head, n_kv_heads, head_dim, scale, softcap,
                              mask_mode, window, q_start, kv_start, st)) != RB_OK)

@@ -188,6 +188,40 @@ def test_attention_host_entry(rb, orc):
     assert cosine(got, ref) >= COS_MIN and max_rel(got, ref) <= MAX_REL
 
 
+@pytest.mark.parametrize("mode,window,dim", [("causal", -1, 128), ("none", -1, 128), ("window", 300, 64),
+                                             ("causal_window", 500, 128), ("causal", -1, 72)])
+def test_attention_host_entry_pipelined(rb, mode, window, dim):
+    """Long full-sequence calls of rb_attention_host run in overlapped
+    query-row chunks (copy in, attention, copy out); the result equals the
+    device entry on the same inputs (up to f32 summation order), from pinned
+    and from pageable host buffers."""
+    import torch
+    import burn_rocket_b200._lib as L
+    modes = {"none": L.MASK_NONE, "causal": L.MASK_CAUSAL, "window": L.MASK_WINDOW,
+             "causal_window": L.MASK_CAUSAL_WINDOW}
+    n, h, hkv = 2500, 4, 2
+    g = torch.Generator().manual_seed(n + dim + window)
+    q = torch.randn(n, h * dim, generator=g).half()
+    k = torch.randn(n, hkv * dim, generator=g).half()
+    v = torch.randn(n, hkv * dim, generator=g).half()
+    scale = 1.0 / math.sqrt(dim)
+    ref = rb.attention_raw(q.cuda(), k.cuda(), v.cuda(), h, hkv, dim, scale, None, modes[mode], window)
+    torch.cuda.synchronize()
+    ref = ref.float().cpu()
+    for pinned in (True, False):
+        qh, kh, vh = (t.pin_memory() if pinned else t.clone() for t in (q, k, v))
+        out = torch.empty_like(qh).pin_memory() if pinned else torch.empty_like(qh)
+        rc = L.load().rb_attention_host(qh.data_ptr(), kh.data_ptr(), vh.data_ptr(), out.data_ptr(), L.DTYPE_F16,
+                                        n, n, h, hkv, dim, scale, 0.0, modes[mode], window, 0, 0)
+        assert rc == 0, L.last_error()
+        got = out.float()
+        cos = torch.nn.functional.cosine_similarity(got.flatten(), ref.flatten(), dim=0).item()
+        mr = ((got - ref).abs().max() / ref.abs().max()).item()
+        assert cos >= COS_MIN, cos
+        assert mr <= MAX_REL, mr
+    rb.check_device_errors()
+
+
 def test_attention_contract_errors(rb):
     import torch
     q = torch.zeros(8, 4 * 96, dtype=torch.float16, device="cuda")
