@@ -1014,6 +1014,40 @@ int rb_matmul_host(int64_t id, const void* x_host, int x_dtype, int64_t m, int64
   if (!xb || !yb) return fail(RB_E_SHAPE, "bad dtype or empty matmul");
   if ((rc = e->io_in.grow(xb, "matmul input staging")) != RB_OK) return rc;
   if ((rc = e->io_out.grow(yb, "matmul output staging")) != RB_OK) return rc;
+  // Larger calls are pipelined in row chunks (whole 256-row tiles): chunk
+  // c's rows go over, its matmul runs once they are on the device, and its
+  // output comes back while later chunks still copy in or compute. Every
+  // output row depends on its own input row only.
+  if (m >= 512 && it->second.kind != RB_WEIGHT_I8G) {
+    if ((rc = ensure_pipe(e)) != RB_OK) return rc;
+    const int64_t rows = ((m + kHostAttnChunks - 1) / kHostAttnChunks + 255) / 256 * 256;
+    cudaStream_t s_in = e->pipe_in, s_cmp = e->host_stream, s_out = e->pipe_out;
+    cudaEvent_t* ev = e->pipe_ev;  // [1 + c]: chunk c in; [1 + C + c]: chunk c done
+    const size_t xrow = static_cast<size_t>(k) * dtype_bytes(x_dtype), yrow = static_cast<size_t>(n) * dtype_bytes(y_dtype);
+    int c = 0;
+    for (int64_t r0 = 0; r0 < m; r0 += rows, ++c) {
+      const int64_t nr = m - r0 < rows ? m - r0 : rows;
+      uint8_t* xd = reinterpret_cast<uint8_t*>(e->io_in.ptr) + r0 * xrow;
+      uint8_t* yd = reinterpret_cast<uint8_t*>(e->io_out.ptr) + r0 * yrow;
+      RB_CUDA(cudaMemcpyAsync(xd, reinterpret_cast<const uint8_t*>(x_host) + r0 * xrow, nr * xrow,
+                              cudaMemcpyHostToDevice, s_in), "H2D chunk");
+      RB_CUDA(cudaEventRecord(ev[1 + c], s_in), "event");
+      RB_CUDA(cudaStreamWaitEvent(s_cmp, ev[1 + c], 0), "event wait");
+      if ((rc = matmul_locked(e, id, xd, x_dtype, nr, k, yd, y_dtype, s_cmp)) != RB_OK) {
+        cudaStreamSynchronize(s_in);
+        cudaStreamSynchronize(s_cmp);
+        cudaStreamSynchronize(s_out);
+        return rc;
+      }
+      RB_CUDA(cudaEventRecord(ev[1 + kHostAttnChunks + c], s_cmp), "event");
+      RB_CUDA(cudaStreamWaitEvent(s_out, ev[1 + kHostAttnChunks + c], 0), "event wait");
+      RB_CUDA(cudaMemcpyAsync(reinterpret_cast<uint8_t*>(y_host) + r0 * yrow, yd, nr * yrow,
+                              cudaMemcpyDeviceToHost, s_out), "D2H chunk");
+    }
+    RB_CUDA(cudaStreamSynchronize(s_out), "matmul sync");
+    RB_CUDA(cudaStreamSynchronize(s_cmp), "matmul sync");
+    return RB_OK;
+  }
   cudaStream_t st = e->host_stream;
   RB_CUDA(cudaMemcpyAsync(e->io_in.ptr, x_host, xb, cudaMemcpyHostToDevice, st), "H2D");
   if ((rc = matmul_locked(e, id, e->io_in.ptr, x_dtype, m, k, e->io_out.ptr, y_dtype, st)) != RB_OK)

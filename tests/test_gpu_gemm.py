@@ -110,6 +110,25 @@ def test_q8_0_gemm_host_entry_matches_device(rb, orc):
     assert np.array_equal(y_host, y_dev)
 
 
+@pytest.mark.parametrize("m", [512, 1100, 2394])
+def test_host_entry_pipelined_rows(rb, orc, m):
+    """Calls of rb_matmul_host with m >= 512 run in overlapped row chunks
+    (copy in, matmul, copy out); Q8_0 and W8A8 results equal the device entry
+    on the same inputs (W8A8 bit for bit; Q8_0 within f32 rounding)."""
+    import torch
+    rng = np.random.default_rng(m)
+    a = rng.standard_normal((m, 1152)).astype(np.float32)
+    w, codes, scales = q8_weight(orc, 640, 1152, m + 1)
+    wid = rb.pack_q8_0_blocks(orc.q8_0_to_blocks(codes, scales), 640, 1152)
+    y_host = rb.matmul_host(a, wid)
+    y_dev = rb.matmul(torch.from_numpy(a).cuda(), wid).cpu().numpy()
+    assert max_rel(y_host, y_dev) <= 1e-5
+    wq = rb.pack_w8a8_float(torch.from_numpy((rng.standard_normal((640, 1152)) * 0.02).astype(np.float32)).cuda())
+    y_host = rb.matmul_host(a, wq)
+    y_dev = rb.matmul(torch.from_numpy(a).cuda(), wq).cpu().numpy()
+    assert np.array_equal(y_host, y_dev)
+
+
 def test_q8_0_gemm_rejects_bad_k(rb, orc):
     import torch
     w, codes, scales = q8_weight(orc, 32, 64, 1)
