@@ -379,6 +379,8 @@ class Qwen3Workload:
         self.model.forward_device()
 
     def e2e_step(self):
+        if self.model.graph is None:  # the public host call replays the model's CUDA graph
+            self.model.capture()
         self.model.embed_host(self.hids, self.hout)
         return (self.hids.numel() * 4, self.hout.numel() * 4)
 
@@ -465,6 +467,8 @@ class SiglipWorkload:
         self.model.forward_device()
 
     def e2e_step(self):
+        if self.model.graph is None:  # the public host call replays the model's CUDA graph
+            self.model.capture()
         self.model.encode_host(self.hpatches, self.hout)
         return (self.hpatches.numel() * 4, self.hout.numel() * 2)
 
@@ -567,6 +571,8 @@ class MoeWorkload:
     def e2e_step(self):
         import torch
         if self.world == 1:
+            if self.model.graph is None:  # the public host call replays the model's CUDA graph
+                self.model.capture()
             self.model.prefill_host(self.hids, self.hout)
         else:
             self.model.ids_in.copy_(self.hids, non_blocking=True)
