@@ -117,43 +117,50 @@ class SiglipTower:
         self.graph = None
 
     # ------------------------------------------------------------------ forward
-    def forward_device(self, stream=None):
-        """One forward over self.patches (f32 [T, hidden]) into self.out (f16 [T, hidden])."""
+    def forward_device(self, stream=None, img0: int = 0, n_img: int | None = None):
+        """One forward over self.patches (f32 [T, hidden]) into self.out (f16 [T, hidden]);
+        img0 / n_img restrict it to the images [img0, img0 + n_img) (their rows
+        of every buffer; images are independent)."""
         import torch
-        cfg, lib, T = self.cfg, _lib.load(), self.T
+        cfg, lib = self.cfg, _lib.load()
         st = _stream_ptr(stream)
         h, hq, S = cfg.hidden, cfg.heads * cfg.head_dim, cfg.patches
         ld = 3 * hq
+        n_img = self.images - img0 if n_img is None else n_img
+        r0, T = img0 * S, n_img * S
+        rows = lambda t: t[r0:r0 + T]  # noqa: E731
+        x, hc, hs, qkv, attn, o, f, d, out = (rows(t) for t in (self.x, self.hc, self.hs, self.qkv, self.attn,
+                                                                 self.o, self.f, self.d, self.out))
         # the residual stream starts as the input (x is rewritten in place each layer)
         if stream is None:
-            self.x.copy_(self.patches)
+            x.copy_(rows(self.patches))
         else:
             with torch.cuda.stream(stream):
-                self.x.copy_(self.patches)
-        qkv_p = _dev_ptr(self.qkv)
+                x.copy_(rows(self.patches))
+        qkv_p = _dev_ptr(qkv)
         delta = None
         for L in self.layers:
-            _check(lib.rb_add_layer_norm_quant(_dev_ptr(self.x), delta, _dev_ptr(L["ln1_g"]), _dev_ptr(L["ln1_b"]),
-                                               cfg.eps, _dev_ptr(self.hc), _dev_ptr(self.hs), T, h, st),
+            _check(lib.rb_add_layer_norm_quant(_dev_ptr(x), delta, _dev_ptr(L["ln1_g"]), _dev_ptr(L["ln1_b"]),
+                                               cfg.eps, _dev_ptr(hc), _dev_ptr(hs), T, h, st),
                    "add_layer_norm_quant")
-            _check(lib.rb_matmul_w8a8_codes(L["qkv"].id, _dev_ptr(self.hc), _dev_ptr(self.hs), T, h, qkv_p,
+            _check(lib.rb_matmul_w8a8_codes(L["qkv"].id, _dev_ptr(hc), _dev_ptr(hs), T, h, qkv_p,
                                             DTYPE_F16, st), "rocket_matmul", T, h, 3 * hq)
             _check(lib.rb_attention_batched(qkv_p, ld, qkv_p + hq * 2, ld, qkv_p + 2 * hq * 2, ld,
-                                            _dev_ptr(self.attn), hq, DTYPE_F16, self.images, S, S,
+                                            _dev_ptr(attn), hq, DTYPE_F16, n_img, S, S,
                                             cfg.heads, cfg.heads, cfg.head_dim, 1.0 / math.sqrt(cfg.head_dim),
                                             0.0, MASK_NONE, -1, 0, 0, st),
                    "rocket_flash_attn", S, S, cfg.head_dim)
-            matmul(self.attn, L["o"], out=self.o, stream=stream)
-            _check(lib.rb_add_layer_norm_quant(_dev_ptr(self.x), _dev_ptr(self.o), _dev_ptr(L["ln2_g"]),
-                                               _dev_ptr(L["ln2_b"]), cfg.eps, _dev_ptr(self.hc), _dev_ptr(self.hs),
+            matmul(attn, L["o"], out=o, stream=stream)
+            _check(lib.rb_add_layer_norm_quant(_dev_ptr(x), _dev_ptr(o), _dev_ptr(L["ln2_g"]),
+                                               _dev_ptr(L["ln2_b"]), cfg.eps, _dev_ptr(hc), _dev_ptr(hs),
                                                T, h, st), "add_layer_norm_quant")
-            _check(lib.rb_matmul_w8a8_codes(L["fc1"].id, _dev_ptr(self.hc), _dev_ptr(self.hs), T, h,
-                                            _dev_ptr(self.f), DTYPE_F16, st), "rocket_matmul", T, h, cfg.inter)
+            _check(lib.rb_matmul_w8a8_codes(L["fc1"].id, _dev_ptr(hc), _dev_ptr(hs), T, h,
+                                            _dev_ptr(f), DTYPE_F16, st), "rocket_matmul", T, h, cfg.inter)
             # (gelu_tanh(h W1^T) is fused into the fc1 epilogue)
-            matmul(self.f, L["fc2"], out=self.d, stream=stream)
-            delta = _dev_ptr(self.d)
-        _check(lib.rb_add_layer_norm(_dev_ptr(self.x), delta, _dev_ptr(self.post_g), _dev_ptr(self.post_b), cfg.eps,
-                                     _dev_ptr(self.out), T, h, st), "add_layer_norm")
+            matmul(f, L["fc2"], out=d, stream=stream)
+            delta = _dev_ptr(d)
+        _check(lib.rb_add_layer_norm(_dev_ptr(x), delta, _dev_ptr(self.post_g), _dev_ptr(self.post_b), cfg.eps,
+                                     _dev_ptr(out), T, h, st), "add_layer_norm")
         return self.out
 
     def capture(self):
@@ -174,14 +181,52 @@ class SiglipTower:
             self.forward_device()
         return self.out
 
-    def encode_host(self, patches_host, out_host=None):
+    def encode_host(self, patches_host, out_host=None, overlap: bool = False):
         """End-to-end call: host patch embeddings [images*patches, hidden] f32 in,
-        host f16 patch states out."""
+        host f16 patch states out. overlap=True (two or more images, page-locked
+        host buffers) runs the tower as two halves of the images, each from its
+        own captured CUDA graph: the second half's input copies in while the
+        first half computes, and the first half's output copies out while the
+        second computes. Results then equal the whole-batch forward up to the
+        f32 summation order of attention."""
         import torch
-        self.patches.copy_(patches_host, non_blocking=True)
-        self.run()
         if out_host is None:
             out_host = torch.empty(self.T, self.cfg.hidden, dtype=torch.float16, pin_memory=True)
-        out_host.copy_(self.out, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
+        if not (overlap and self.images >= 2):
+            self.patches.copy_(patches_host, non_blocking=True)
+            self.run()
+            out_host.copy_(self.out, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            return out_host
+        half = self.images // 2
+        if getattr(self, "half_graphs", None) is None:
+            graphs = []
+            for i0, n in ((0, half), (half, self.images - half)):
+                self.forward_device(img0=i0, n_img=n)
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, capture_error_mode="thread_local"):
+                    self.forward_device(img0=i0, n_img=n)
+                graphs.append(g)
+            self.half_graphs = graphs
+            self.copy_in, self.copy_out = torch.cuda.Stream(), torch.cuda.Stream()
+        r = half * self.cfg.patches
+        cur = torch.cuda.current_stream()
+        self.copy_in.wait_stream(cur)
+        with torch.cuda.stream(self.copy_in):
+            self.patches[:r].copy_(patches_host[:r], non_blocking=True)
+            in_a = torch.cuda.current_stream().record_event()
+            self.patches[r:].copy_(patches_host[r:], non_blocking=True)
+            in_b = torch.cuda.current_stream().record_event()
+        cur.wait_event(in_a)
+        self.half_graphs[0].replay()
+        done_a = cur.record_event()
+        self.copy_out.wait_event(done_a)
+        with torch.cuda.stream(self.copy_out):
+            out_host[:r].copy_(self.out[:r], non_blocking=True)
+        cur.wait_event(in_b)
+        self.half_graphs[1].replay()
+        out_host[r:].copy_(self.out[r:], non_blocking=True)
+        cur.synchronize()
+        self.copy_out.synchronize()
         return out_host

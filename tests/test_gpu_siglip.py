@@ -205,3 +205,23 @@ def test_siglip_graph_replay_equals_eager(rb):
     out = tower.encode_host(tower.patches.cpu().pin_memory())
     assert torch.equal(out, eager.cpu())
     rb.check_device_errors()
+
+
+def test_siglip_encode_host_overlapped_halves(rb):
+    """encode_host(overlap=True) runs the images in two halves from their own
+    graphs, overlapping the copies with the other half's compute; twice in a
+    row, it matches the whole-batch forward (up to attention's f32 summation
+    order)."""
+    import torch
+    from burn_rocket_b200.siglip import SiglipConfig, SiglipTower
+    cfg = replace(SiglipConfig(), layers=2, patches=300)
+    tower = SiglipTower(cfg, 5, seed=4)
+    tower.patches.copy_(torch.randn(tower.T, cfg.hidden, device="cuda"))
+    ref = tower.forward_device().float().cpu()
+    hp = tower.patches.cpu().pin_memory()
+    for _ in range(2):
+        out = tower.encode_host(hp, overlap=True).float()
+        cos = torch.nn.functional.cosine_similarity(out.flatten(), ref.flatten(), dim=0).item()
+        assert cos >= 0.9999, cos
+        assert (out - ref).abs().max().item() <= 2e-2 * ref.abs().max().item()
+    rb.check_device_errors()
