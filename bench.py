@@ -1,30 +1,42 @@
 """bench.py — throughput of the offloaded ops on B200, one JSON line on rank 0.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload attn|q8gemm|w8a8|qwen3|siglip]
-                    [--impl b200|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W]
+                    [--workload qwen3|attn|q8gemm|w8a8|siglip|moe] [--impl b200|reference]
+
+BASELINE.json's metric has three items: "Q8_0/W8A8 GEMM TFLOP/s; GQA attn
+TFLOP/s; Qwen3-Emb-0.6B prefill tok/s". The default line is the model item,
+config #3, and at N = 1 it carries one sub-record per single-op item (key
+"sub"), each timed alone with its own ms_per_step, roofline and e2e.
 
 Workloads (synthetic seeded data of the named shapes):
+  qwen3   config #3 (default): Qwen3-Embedding-0.6B-architecture forward, 28
+          layers, 64 sequences x 512 tokens, bidirectional, random-init Q8_0
+          linears; data-parallel over sequences (64/N per GPU, global batch
+          fixed: strong scaling). Metric: tokens/s.
+  q8gemm  config #1: f32 [512, 1024] x Q8_0 [3072, 1024]^T -> f32 [512, 3072].
   attn    config #2: GQA attention, 3633 tokens, 16 q / 8 kv heads x 128, fp16,
           RoPE (theta 1e6) pre-applied; one step = one causal + one
           bidirectional call. Metric: attention TFLOP/s (algorithmic FLOPs:
           4*S*S*D*H bidirectional, 4*D*H*S(S+1)/2 causal).
-  q8gemm  config #1: f32 [512, 1024] x Q8_0 [3072, 1024]^T -> f32 [512, 3072].
   w8a8    config #4's four projection GEMMs (qkv 3456, o 1152, fc1 4304,
           fc2 1152 <- 4304) over one 16 x 2394-patch batch, W8A8, with the
           tower's fp16 activations in and out (dynamic per-token int8
           quantisation of the f16 input inside the step).
+  siglip  config #4: the SigLIP-style W8A8 tower, 16 images, DP over images.
+  moe     config #5: Qwen3-30B-A3B-style MoE prefill (EP over N GPUs).
 
 Timing: W untimed warm-up steps, then exactly K steps timed with CUDA events on
 the launching stream, an L2 flush (a 256 MiB write) between timed steps, a
-barrier + synchronize on both sides, max over ranks. With N > 1 each rank runs
-an independent replica (the single ops do not shard: replicas only) and
-`value` is the aggregate over ranks. The `e2e` figure goes through the public
-C-ABI host entry points (rb_*_host) with pinned host buffers, so host<->device
-copies are inside its timed region.
+barrier + synchronize on both sides, max over ranks. The single ops do not
+shard: with N > 1 each rank runs an independent replica and `value` is the
+aggregate over ranks. The `e2e` figure goes through the public host entry
+points (rb_*_host, the models' embed_host / encode_host / prefill_host) with
+pinned host buffers, so host<->device copies are inside its timed region.
 
 `--impl reference` times the reference algorithm on the host cores instead:
-the CPU restatement of the reference's `--device cpu` path (oracle/, all
-OpenMP threads), on a bounded sample of the same workload.
+the CPU restatement of the reference's `--device cpu` path (oracle/, OpenMP
+on every host core), on a bounded sample of the same workload; rank 0 alone
+runs under torchrun.
 """
 from __future__ import annotations
 
@@ -284,10 +296,10 @@ class Q8GemmWorkload:
 
 class W8A8Workload:
     name = "w8a8"
-    metric = "W8A8 GEMM TOP/s (config #4 projections, 16 x 2394 patches)"
+    metric = "W8A8 GEMM TOP/s (config #4 projections qkv/o/fc1/fc2 over 16 x 2394 patches, f16 in/out)"
     unit = "TOP/s"
-    M = 16 * 2394
-    SHAPES = [(3456, 1152), (1152, 1152), (4304, 1152), (1152, 4304)]  # (N, K)
+    M = M_CONFIG = 16 * 2394
+    SHAPES = SHAPES_CONFIG = [(3456, 1152), (1152, 1152), (4304, 1152), (1152, 4304)]  # (N, K)
     X_DTYPE = "f16"  # config #3's tower is fp16: f16 activations in, f16 out
 
     def __init__(self, dev, seed):
@@ -295,8 +307,8 @@ class W8A8Workload:
         import burn_rocket_b200 as rb
         self.rb = rb
         rng = np.random.default_rng(seed)
-        if self.X_DTYPE != "f32":
-            self.metric = "W8A8 GEMM TOP/s (" + ", ".join(f"[{self.M},{k}] f16 x s8 [{n},{k}]^T"
+        if (self.M, self.SHAPES) != (W8A8Workload.M_CONFIG, W8A8Workload.SHAPES_CONFIG):
+            self.metric = "W8A8 GEMM TOP/s (" + ", ".join(f"[{self.M},{k}] {self.X_DTYPE} x s8 [{n},{k}]^T"
                                                           for n, k in self.SHAPES) + ")"
         xdt = torch.float32 if self.X_DTYPE == "f32" else torch.float16
         self.ws, self.xs, self.ys = [], [], []
@@ -664,6 +676,142 @@ def dist_setup(n_gpus):
     return rank, world, local
 
 
+def config_dict(name, world):
+    """The `config` object of a workload's line; both arms print the same one."""
+    return {"workload": {"attn": "configs[1] GQA attention", "q8gemm": "configs[0] Q8_0 GEMM",
+                         "w8a8": "configs[3] W8A8 projections",
+                         "qwen3": "configs[2] Qwen3-Embedding-0.6B arch, 28 layers, 64x512 tokens",
+                         "siglip": "configs[3] SigLIP-style W8A8 tower, 27 layers, 16x2394 patches",
+                         "moe": "configs[4] Qwen3-30B-A3B-style MoE, 48 layers, 4x2048 tokens"}[name],
+            "l2": "flushed between timed steps (256 MiB write)",
+            "parallelism": (f"dp{world} over sequences" if name == "qwen3"
+                            else f"dp{world} over images" if name == "siglip"
+                            else ("single GPU, all 128 experts resident" if world == 1
+                                  else f"ep{world} (experts {128 // world}/rank, NCCL all-to-all), "
+                                       f"{'dp over sequences' if world <= 4 else 'half sequences'}")
+                            if name == "moe"
+                            else (f"replicas x{world}" if world > 1 else "single GPU"))}
+
+
+DTYPES = {"attn": "f16", "q8gemm": "f16xq8_0->f32", "w8a8": "s8", "qwen3": "f16xq8_0 (f32 residual)",
+          "siglip": "s8 linears, f16 attention (f32 residual)", "moe": "f16xq8_0 (f32 residual, f32 router)"}
+DEFAULT_STEPS = {"attn": 200, "q8gemm": 2000, "w8a8": 60, "qwen3": 20, "siglip": 5, "moe": 3}
+# configs[0], [1] and [3]'s projections: measured beside the default (config #3) line at N = 1
+SUB_WORKLOADS = ("q8gemm", "attn", "w8a8")
+
+
+def time_device(wl, steps, warmup, flush, stream, use_graph, barrier, local):
+    """W untimed warm-ups, then exactly `steps` steps timed with CUDA events on
+    the launching stream (an L2 flush between them, outside the events), with
+    NVML clock sampling during the timed region. One step = the workload's
+    C-ABI calls, captured once into a CUDA graph so host-side Python/ctypes
+    overhead stays out of the device timing. Returns (ms summed over the
+    steps, kernel launches in the timed region, graph used, clock summary)."""
+    import torch
+    import burn_rocket_b200 as rb
+    for _ in range(warmup):
+        wl.step()
+    torch.cuda.synchronize()
+    rb.check_device_errors()
+    graph = None
+    rb.launch_count(reset=True)
+    per_step = 0
+    if use_graph and getattr(wl, "graphable", True):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+            wl.step()
+        per_step = rb.launch_count(reset=True)
+        graph.replay()
+        torch.cuda.synchronize()
+        rb.check_device_errors()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    barrier()
+    with ClockSampler(local) as clocks:
+        for i in range(steps):
+            flush.zero_()
+            starts[i].record(stream)
+            if graph is not None:
+                graph.replay()
+            else:
+                wl.step()
+            ends[i].record(stream)
+        barrier()
+    launches = per_step * steps if graph is not None else rb.launch_count()
+    ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    rb.check_device_errors()
+    del graph
+    return ms, launches, per_step > 0, clocks.summary()
+
+
+def time_e2e(wl, steps, barrier):
+    """Seconds for `steps` end-to-end calls through the public host entry
+    points (pinned host buffers, copies inside), and their bytes per step."""
+    for _ in range(2):
+        wl.e2e_step()
+    barrier()
+    t0 = time.perf_counter()
+    h2d = d2h = 0
+    for _ in range(steps):
+        h2d, d2h = wl.e2e_step()
+    return time.perf_counter() - t0, h2d, d2h
+
+
+def roofline_of(wl, ms_per_step, peaks, peak_kind):
+    """Roofline of the workload's dominant kernel: the model workloads time
+    their dominant GEMMs alone (inside a long step they run at the sustained
+    clock, so against the sustained peak); the single ops use the whole step
+    against the burst peak."""
+    kr = wl.kernel_roofline() if hasattr(wl, "kernel_roofline") else None
+    int8 = wl.name in ("w8a8", "siglip")
+    if kr is not None:
+        kname, achieved, kms = kr
+        peak = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
+        peak_src = f"{peak_kind} MEASURED_PEAKS bf16_tflops_sustained"
+    else:
+        kname = "whole step"
+        achieved = wl.flops / (ms_per_step / 1e3) / 1e12
+        peak = float(peaks["bf16_tflops"])
+        peak_src = f"{peak_kind} MEASURED_PEAKS bf16_tflops (burst)"
+    if int8:
+        peak = 2.0 * peak  # dense int8 is twice the dense bf16 rate
+        peak_src += " x2 for int8"
+    return {"bound": "tensor", "kernel": kname, "achieved": round(achieved, 2), "peak": peak,
+            "unit": "TOP/s" if int8 else "TFLOP/s", "frac": round(achieved / peak, 4),
+            "traffic": profile_traffic(wl.name), "peak_source": peak_src}
+
+
+def cpu_baseline_of(W, orc):
+    v, sample = W.cpu_sample(orc, seed=1)
+    return {"value": round(v, 5), "unit": W.unit, "cores": orc.num_threads(), "kind": "port", "sample": sample}
+
+
+def measure_sub(name, dev, flush, stream, args, peaks, peak_kind, orc):
+    """One single-op sub-record (config #1 / #2 / #4 projections) at N = 1."""
+    import torch
+    W = WORKLOADS[name]
+    wl = W(dev, seed=0x5EED)
+    steps = DEFAULT_STEPS[name]
+    ms, launches, graphed, clocks = time_device(wl, steps, args.warmup, flush, stream, not args.no_graph,
+                                                torch.cuda.synchronize, dev.index)
+    ms_per_step = ms / steps
+    value = wl.flops / 1e12 / (ms_per_step / 1e3)
+    e2e_steps = 10
+    e2e_s, h2d, d2h = time_e2e(wl, e2e_steps, torch.cuda.synchronize)
+    rec = {"workload": config_dict(name, 1)["workload"], "metric": W.metric, "value": round(value, 3),
+           "unit": W.unit, "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
+           "dtype": DTYPES[name], "roofline": roofline_of(wl, ms_per_step, peaks, peak_kind),
+           "e2e": {"value": round(wl.flops / 1e12 * e2e_steps / e2e_s, 3), "unit": W.unit,
+                   "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
+           "gpu_launches": int(launches), "clocks": clocks,
+           "timing": "CUDA-graph replay of the step's C-ABI calls" if graphed else "eager launches"}
+    if orc is not None:
+        rec["cpu_baseline"] = cpu_baseline_of(W, orc)
+    del wl
+    torch.cuda.empty_cache()
+    return rec
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
@@ -681,44 +829,13 @@ def run_b200(args):
     stream = torch.cuda.current_stream()
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
 
-    for _ in range(args.warmup):
-        wl.step()
-    torch.cuda.synchronize()
-    rb.check_device_errors()
-
     def barrier():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
 
-    # One step = the workload's C-ABI calls, captured once into a CUDA graph so
-    # host-side Python/ctypes overhead stays out of the device timing.
-    graph = None
-    rb.launch_count(reset=True)
-    if not args.no_graph and getattr(wl, "graphable", True):
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, capture_error_mode="thread_local"):
-            wl.step()
-        per_step = rb.launch_count(reset=True)
-        graph.replay()
-        torch.cuda.synchronize()
-        rb.check_device_errors()
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    barrier()
-    with ClockSampler(local) as clocks:
-        for i in range(args.steps):
-            flush.zero_()  # L2 flush between timed steps (outside the events)
-            starts[i].record(stream)
-            if graph is not None:
-                graph.replay()
-            else:
-                wl.step()
-            ends[i].record(stream)
-        barrier()
-    launches = per_step * args.steps if graph is not None else rb.launch_count()
-    ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
-    rb.check_device_errors()
+    ms, launches, graphed, clocks = time_device(wl, args.steps, args.warmup, flush, stream, not args.no_graph,
+                                                barrier, local)
     t = torch.tensor([ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -729,78 +846,43 @@ def run_b200(args):
     value = per_step * world * args.steps / (ms_max / 1e3)
 
     # End-to-end through the host entry points (copies inside the timed region).
-    for _ in range(2):
-        wl.e2e_step()
-    barrier()
-    t0 = time.perf_counter()
     e2e_steps = max(3, min(args.steps, 10))
-    for _ in range(e2e_steps):
-        h2d, d2h = wl.e2e_step()
-    e2e_s = time.perf_counter() - t0
+    e2e_s, h2d, d2h = time_e2e(wl, e2e_steps, barrier)
     te = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_value = per_step * world * e2e_steps / float(te.item())
 
     peaks, peak_kind = load_peaks()
-    kr = wl.kernel_roofline() if hasattr(wl, "kernel_roofline") else None
-    if kr is not None:
-        # the dominant kernel measured on its own (inside a long step it runs
-        # at the sustained clock: compare with the sustained peak)
-        kname, achieved, kms = kr
-        peak = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
-        peak_src = f"{peak_kind} MEASURED_PEAKS bf16_tflops_sustained"
-        if wl.name == "siglip":
-            peak = 2.0 * peak  # dense int8 is twice the dense bf16 rate
-            peak_src += " x2 for int8"
-    else:
-        kname = "whole step"
-        achieved = wl.flops / (ms_per_step / 1e3) / 1e12  # per launch group, per GPU
-        peak = float(peaks["bf16_tflops"])
-        peak_src = f"{peak_kind} MEASURED_PEAKS bf16_tflops (burst)"
-        if wl.name == "w8a8":
-            peak = 2.0 * peak  # dense int8 is twice the dense bf16 rate
-            peak_src += " x2 for int8"
-    traffic = profile_traffic(wl.name)
     line = {
         "metric": wl.metric, "value": round(value, 3), "unit": wl.unit, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": True, "scaling": "strong" if wl.name in DP_WORKLOADS else "weak", "vs_baseline": None,
-        "dtype": {"attn": "f16", "q8gemm": "f16xq8_0->f32", "w8a8": "s8", "qwen3": "f16xq8_0 (f32 residual)",
-                  "siglip": "s8 linears, f16 attention (f32 residual)",
-                  "moe": "f16xq8_0 (f32 residual, f32 router)"}[wl.name],
+        "dtype": DTYPES[wl.name],
         "data": "synthetic (seeded, BASELINE.json shapes)",
-        "config": {"workload": {"attn": "configs[1] GQA attention", "q8gemm": "configs[0] Q8_0 GEMM",
-                                "w8a8": "configs[3] W8A8 projections",
-                                "qwen3": "configs[2] Qwen3-Embedding-0.6B arch, 28 layers, 64x512 tokens",
-                                "siglip": "configs[3] SigLIP-style W8A8 tower, 27 layers, 16x2394 patches",
-                                "moe": "configs[4] Qwen3-30B-A3B-style MoE, 48 layers, 4x2048 tokens"}[wl.name],
-                   "l2": "flushed between timed steps (256 MiB write)",
-                   "parallelism": (f"dp{world} over sequences" if wl.name == "qwen3"
-                                   else f"dp{world} over images" if wl.name == "siglip"
-                                   else ("single GPU, all 128 experts resident" if world == 1
-                                         else f"ep{world} (experts {128 // world}/rank, NCCL all-to-all), "
-                                              f"{'dp over sequences' if world <= 4 else 'half sequences'}")
-                                   if wl.name == "moe"
-                                   else (f"replicas x{world}" if world > 1 else "single GPU"))},
-        "roofline": {"bound": "tensor", "kernel": kname, "achieved": round(achieved, 2), "peak": peak,
-                     "unit": "TOP/s" if wl.name in ("w8a8", "siglip") else "TFLOP/s",
-                     "frac": round(achieved / peak, 4), "traffic": traffic, "peak_source": peak_src},
+        "config": config_dict(wl.name, world),
+        "roofline": roofline_of(wl, ms_per_step, peaks, peak_kind),
         "e2e": {"value": round(e2e_value, 3), "unit": wl.unit, "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h)},
         "gpu_launches": int(launches),
-        "timing": ("CUDA-graph replay of the step's C-ABI calls" if graph is not None
+        "timing": ("CUDA-graph replay of the step's C-ABI calls" if graphed
                    else "eager launches (per-layer host-sized all-to-all)" if wl.name == "moe" and world > 1
                    else "eager launches"),
-        "clocks": clocks.summary(),
+        "clocks": clocks,
     }
     if world > 1:
         dist.barrier()
+    orc = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import oracle as orc
-        v, sample = W.cpu_sample(orc, seed=1)
-        line["cpu_baseline"] = {"value": round(v, 5), "unit": wl.unit, "cores": orc.num_threads(),
-                                "kind": "port", "sample": sample}
+        orc.use_all_host_cores()
+        line["cpu_baseline"] = cpu_baseline_of(W, orc)
+    if world == 1 and args.workload == "qwen3" and not args.no_sub:
+        # the metric's other items, each timed alone on this GPU
+        del wl
+        torch.cuda.empty_cache()
+        line["sub"] = {name: measure_sub(name, dev, flush, stream, args, peaks, peak_kind, orc)
+                       for name in SUB_WORKLOADS}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -812,29 +894,46 @@ def run_reference(args):
     if rank != 0:
         return  # rank 0 alone runs the host-core reference
     from oracle import oracle as orc
+    # torchrun sets OMP_NUM_THREADS=1 in every rank: use all host cores anyway
+    orc.use_all_host_cores()
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+
+    def run(W, steps, warmup):
+        for _ in range(warmup):
+            W.cpu_sample(orc, seed=1)
+        vals, sample = [], ""
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            v, sample = W.cpu_sample(orc, seed=1)
+            vals.append(v)
+        return statistics.median(vals), sample, (time.perf_counter() - t0) / steps
+
     W = WORKLOADS[args.workload]
-    for _ in range(args.warmup):
-        W.cpu_sample(orc, seed=1)
-    vals = []
-    sample = ""
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        v, sample = W.cpu_sample(orc, seed=1)
-        vals.append(v)
-    wall = time.perf_counter() - t0
-    value = statistics.median(vals)
+    value, sample, s_per_step = run(W, args.steps, args.warmup)
+    note = ("CPU restatement of the reference's --device cpu algorithm (oracle/, OpenMP on all host cores); "
+            "the Rust reference cannot be built here (no cargo/rustc, no crate registry)")
     line = {
         "impl": "reference", "metric": W.metric, "value": round(value, 5), "unit": W.unit,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(wall / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(s_per_step * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong" if W.name in DP_WORKLOADS else "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE.json shapes)",
-        "config": {"workload": W.name},
+        "config": config_dict(W.name, world),
         "cpu_baseline": {"value": round(value, 5), "unit": W.unit, "cores": orc.num_threads(), "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(value, 5), "unit": W.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "note": "CPU restatement of the reference's --device cpu algorithm (oracle/, OpenMP); the Rust "
-                "reference cannot be built here (no cargo/rustc, no crate registry)",
+        "note": note,
     }
+    if args.workload == "qwen3" and not args.no_sub:
+        line["sub"] = {}
+        for name in SUB_WORKLOADS:
+            S = WORKLOADS[name]
+            v, smp, sps = run(S, 3, 1)
+            line["sub"][name] = {"workload": config_dict(name, 1)["workload"], "metric": S.metric,
+                                 "value": round(v, 5), "unit": S.unit, "steps": 3, "warmup": 1,
+                                 "ms_per_step": round(sps * 1e3, 3),
+                                 "cpu_baseline": {"value": round(v, 5), "unit": S.unit, "cores": orc.num_threads(),
+                                                  "kind": "port", "sample": smp}}
     print(json.dumps(line), flush=True)
 
 
@@ -843,7 +942,10 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None, help="timed steps (default: per workload, ~0.1-1 s)")
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="attn", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="qwen3", choices=sorted(WORKLOADS),
+                    help="default qwen3 (configs[2], the metric's model item) with sub-records for configs[0], "
+                         "[1] and [3]'s projections at N = 1")
+    ap.add_argument("--no-sub", action="store_true", help="qwen3: skip the single-op sub-records")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="launch eagerly instead of replaying a CUDA graph")
@@ -858,7 +960,7 @@ def main():
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.steps is None:
-        args.steps = {"attn": 200, "q8gemm": 2000, "w8a8": 60, "qwen3": 10, "siglip": 5, "moe": 3}.get(args.workload, 20)
+        args.steps = DEFAULT_STEPS.get(args.workload, 20)
     if args.gemm_shape:
         m, n, k = (int(v) for v in args.gemm_shape.split(","))
         if args.workload == "w8a8":

@@ -59,6 +59,7 @@ def lib() -> C.CDLL:
             "orc_flash_attn_ref": (None, [_p, _p, _p, _i64, _i64, _i, _i, _i, _f, _f, _i, _i64, _i64, _i64, _p]),
             "orc_attention_cpu": (None, [_p, _p, _p, _i64, _i64, _i, _i, _i, _f, _i, _p]),
             "orc_num_threads": (_i, []),
+            "orc_set_num_threads": (None, [_i]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -288,3 +289,19 @@ def attention_cpu(q, k, v, n_head, n_kv_heads, head_dim, scale, causal) -> np.nd
 
 def num_threads() -> int:
     return int(lib().orc_num_threads())
+
+
+def host_cores() -> int:
+    """Cores this process may run on (what `nproc` reports)."""
+    import os
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def use_all_host_cores() -> int:
+    """Run later oracle calls on every host core, whatever OMP_NUM_THREADS says;
+    returns the thread count now in effect."""
+    lib().orc_set_num_threads(host_cores())
+    return num_threads()

@@ -523,3 +523,13 @@ int orc_num_threads(void) {
   return 1;
 #endif
 }
+
+/* Thread count of the later parallel regions (a launcher such as torchrun sets
+ * OMP_NUM_THREADS=1 in every rank; the CPU baseline wants all host cores). */
+void orc_set_num_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}
