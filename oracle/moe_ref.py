@@ -117,9 +117,13 @@ def experts_combine(h, n2, ids, w, experts):
     return y
 
 
-def layer_forward(x, wts: dict, cfg: dict, lens=None):
+def layer_forward(x, wts: dict, cfg: dict, lens=None, force_ids=None):
     """One decoder layer over rows x [T, hidden] (records of `lens` rows, positions
-    restarting per record). Returns (y, ids, weights, margins)."""
+    restarting per record). Returns (y, ids, weights, margins): ids and margins
+    are this layer's own top-k selection, weights those the combine used.
+    force_ids [T, k] replaces the selection in the combine (e.g. by the
+    device's, to compare a layer across a near-tie): the weights are then this
+    layer's probabilities of those experts, renormalised over them."""
     nh, nkv, d, eps = cfg["heads"], cfg["kv_heads"], cfg["head_dim"], cfg["eps"]
     x = np.asarray(x, np.float64)
     t = x.shape[0]
@@ -141,7 +145,15 @@ def layer_forward(x, wts: dict, cfg: dict, lens=None):
     n2 = rms(hid, wts["post_norm"], eps)
     logits = n2 @ np.asarray(wts["router"], np.float64).T
     ids, w, margins = route(logits, cfg["top_k"], cfg.get("norm_topk", True))
-    y = experts_combine(hid, n2, ids, w, wts["experts"])
+    use = ids
+    if force_ids is not None:
+        use = np.asarray(force_ids, np.int64)
+        p = np.exp(logits - logits.max(-1, keepdims=True))
+        p /= p.sum(-1, keepdims=True)
+        w = np.take_along_axis(p, use, 1)
+        if cfg.get("norm_topk", True):
+            w = w / w.sum(-1, keepdims=True)
+    y = experts_combine(hid, n2, use, w, wts["experts"])
     return y, ids, w, margins
 
 
@@ -167,27 +179,54 @@ def make_host_weights(cfg, seed: int) -> dict:
     return {"layers": layers, "embed": randn(cfg.vocab, h), "final_norm": norm_w(h)}
 
 
-def forward(hw: dict, cfg, ids: np.ndarray, batch: int, seq: int):
-    """Final-normed hidden states [batch*seq, hidden] (f64) and per-layer
-    (ids, weights, margins), with every linear weight taken through the Q8_0
-    codec (oracle.q8_0_quantize / q8_0_dequant) and the embedding rounded to
-    f16, as the device model stores them."""
+class _LazyExperts:
+    """experts[e] -> (gate, up, down) f64, dequantised when used (a
+    full-width layer holds 128 x 3 expert matrices: too many to keep in f64)."""
+
+    def __init__(self, experts, deq):
+        self.experts, self.deq = experts, deq
+
+    def __len__(self):
+        return len(self.experts)
+
+    def __getitem__(self, e):
+        return tuple(self.deq(m) for m in self.experts[e])
+
+
+def dequantised_layer(L: dict, quant: bool = True) -> dict:
+    """A layer's weights as the device holds them: every linear through the
+    Q8_0 codec (oracle.q8_0_quantize / q8_0_dequant) when quant, f64."""
     from . import oracle as orc
 
     def deq(w):
+        if not quant:
+            return np.asarray(w, np.float64)
         codes, scales = orc.q8_0_quantize(np.asarray(w, np.float32))
         return orc.q8_0_dequant(codes, scales).astype(np.float64)
 
-    c = {"heads": cfg.heads, "kv_heads": cfg.kv_heads, "head_dim": cfg.head_dim, "eps": cfg.eps,
-         "theta": cfg.theta, "top_k": cfg.top_k, "norm_topk": True}
+    return {"in_norm": L["in_norm"], "post_norm": L["post_norm"], "q_norm": L["q_norm"], "k_norm": L["k_norm"],
+            "wq": deq(L["wq"]), "wk": deq(L["wk"]), "wv": deq(L["wv"]), "wo": deq(L["wo"]),
+            "router": deq(L["router"]), "experts": _LazyExperts(L["experts"], deq)}
+
+
+def layer_cfg(cfg) -> dict:
+    return {"heads": cfg.heads, "kv_heads": cfg.kv_heads, "head_dim": cfg.head_dim, "eps": cfg.eps,
+            "theta": cfg.theta, "top_k": cfg.top_k, "norm_topk": True}
+
+
+def forward(hw: dict, cfg, ids: np.ndarray, batch: int, seq: int, force_routing=None):
+    """Final-normed hidden states [batch*seq, hidden] (f64) and per-layer
+    (ids, weights, margins), with every linear weight taken through the Q8_0
+    codec (oracle.q8_0_quantize / q8_0_dequant) and the embedding rounded to
+    f16, as the device model stores them. force_routing: per layer, expert ids
+    [T, k] that replace this chain's own selection (layer_forward force_ids)."""
+    from . import oracle as orc
+    c = layer_cfg(cfg)
     emb = orc.f16_bits_to_f32(orc.f32_to_f16_bits(hw["embed"]))
     x = emb[np.asarray(ids).reshape(-1)].astype(np.float64)
     routing = []
-    for L in hw["layers"]:
-        w = {"in_norm": L["in_norm"], "post_norm": L["post_norm"], "q_norm": L["q_norm"], "k_norm": L["k_norm"],
-             "wq": deq(L["wq"]), "wk": deq(L["wk"]), "wv": deq(L["wv"]), "wo": deq(L["wo"]),
-             "router": deq(L["router"]),
-             "experts": [(deq(g), deq(u), deq(dn)) for g, u, dn in L["experts"]]}
-        x, rid, rw, mg = layer_forward(x, w, c, lens=[seq] * batch)
+    for li, L in enumerate(hw["layers"]):
+        force = None if force_routing is None else force_routing[li]
+        x, rid, rw, mg = layer_forward(x, dequantised_layer(L), c, lens=[seq] * batch, force_ids=force)
         routing.append((rid, rw, mg))
     return rms(x, hw["final_norm"], cfg.eps), routing

@@ -64,34 +64,56 @@ def rope_tables(seq: int, head_dim: int, theta: float):
     return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
 
 
-def forward(hw: dict, cfg, ids: np.ndarray, batch: int, seq: int, causal: bool = False) -> np.ndarray:
-    """Embeddings [batch, hidden] (L2-normalised last-token states)."""
+def layer(L: dict, cfg, x: np.ndarray, batch: int, seq: int, causal: bool = False, quant: bool = True):
+    """One decoder layer (model.rs:261-291) on the f64 residual stream x
+    [batch*seq, hidden]; returns the new residual stream. quant=False uses the
+    f32 weights as they are (the float skeleton, without the Q8_0 codec)."""
     h, hd, nh, nkv = cfg.hidden, cfg.head_dim, cfg.heads, cfg.kv_heads
     g = nh // nkv
-    emb = orc.f16_bits_to_f32(orc.f32_to_f16_bits(hw["embed"]))
-    x = emb[ids.reshape(batch, seq)].astype(np.float64)  # [B, S, h]
+    deq = _deq if quant else (lambda w: np.asarray(w, np.float64))
+    x = np.asarray(x, np.float64).reshape(batch, seq, h)
     cos, sin = rope_tables(seq, hd, cfg.theta)
     cos, sin = cos.astype(np.float64), sin.astype(np.float64)
-    for L in hw["layers"]:
-        wq, wk, wv, wo = _deq(L["wq"]), _deq(L["wk"]), _deq(L["wv"]), _deq(L["wo"])
-        wg, wu, wd = _deq(L["wg"]), _deq(L["wu"]), _deq(L["wd"])
-        hh = _rms(x, L["in_norm"].astype(np.float64), cfg.eps)
-        q = (hh @ wq.T).reshape(batch, seq, nh, hd)
-        k = (hh @ wk.T).reshape(batch, seq, nkv, hd)
-        v = (hh @ wv.T).reshape(batch, seq, nkv, hd)
-        q = _rope(_rms(q, L["q_norm"].astype(np.float64), cfg.eps), cos, sin)
-        k = _rope(_rms(k, L["k_norm"].astype(np.float64), cfg.eps), cos, sin)
-        att = np.empty((batch, seq, nh, hd))
-        for b in range(batch):
-            for hh_i in range(nh):
-                s = q[b, :, hh_i] @ k[b, :, hh_i // g].T / np.sqrt(hd)
-                if causal:
-                    s = np.where(np.tril(np.ones((seq, seq), bool)), s, -np.inf)
-                p = np.exp(s - s.max(-1, keepdims=True))
-                att[b, :, hh_i] = (p / p.sum(-1, keepdims=True)) @ v[b, :, hh_i // g]
-        x = x + att.reshape(batch, seq, nh * hd) @ wo.T
-        hh = _rms(x, L["post_norm"].astype(np.float64), cfg.eps)
-        gate, up = hh @ wg.T, hh @ wu.T
-        x = x + (gate / (1.0 + np.exp(-gate)) * up) @ wd.T
-    last = _rms(x[:, -1, :], hw["final_norm"].astype(np.float64), cfg.eps)
+    wq, wk, wv, wo = deq(L["wq"]), deq(L["wk"]), deq(L["wv"]), deq(L["wo"])
+    wg, wu, wd = deq(L["wg"]), deq(L["wu"]), deq(L["wd"])
+    hh = _rms(x, L["in_norm"].astype(np.float64), cfg.eps)
+    q = (hh @ wq.T).reshape(batch, seq, nh, hd)
+    k = (hh @ wk.T).reshape(batch, seq, nkv, hd)
+    v = (hh @ wv.T).reshape(batch, seq, nkv, hd)
+    q = _rope(_rms(q, L["q_norm"].astype(np.float64), cfg.eps), cos, sin)
+    k = _rope(_rms(k, L["k_norm"].astype(np.float64), cfg.eps), cos, sin)
+    att = np.empty((batch, seq, nh, hd))
+    for b in range(batch):
+        for hh_i in range(nh):
+            s = q[b, :, hh_i] @ k[b, :, hh_i // g].T / np.sqrt(hd)
+            if causal:
+                s = np.where(np.tril(np.ones((seq, seq), bool)), s, -np.inf)
+            p = np.exp(s - s.max(-1, keepdims=True))
+            att[b, :, hh_i] = (p / p.sum(-1, keepdims=True)) @ v[b, :, hh_i // g]
+    x = x + att.reshape(batch, seq, nh * hd) @ wo.T
+    hh = _rms(x, L["post_norm"].astype(np.float64), cfg.eps)
+    gate, up = hh @ wg.T, hh @ wu.T
+    x = x + (gate / (1.0 + np.exp(-gate)) * up) @ wd.T
+    return x.reshape(batch * seq, h)
+
+
+def embed(hw: dict, ids: np.ndarray, quant: bool = True) -> np.ndarray:
+    """Embedding rows of the token ids (f16-rounded table when quant), f64 [T, hidden]."""
+    emb = orc.f16_bits_to_f32(orc.f32_to_f16_bits(hw["embed"])) if quant else hw["embed"]
+    return emb[np.asarray(ids).reshape(-1)].astype(np.float64)
+
+
+def head(hw: dict, cfg, x: np.ndarray, batch: int, seq: int) -> np.ndarray:
+    """Final RMSNorm of each sequence's last token (model.rs:230-235), L2-normalised."""
+    last = _rms(np.asarray(x, np.float64).reshape(batch, seq, -1)[:, -1, :],
+                hw["final_norm"].astype(np.float64), cfg.eps)
     return last / np.maximum(np.linalg.norm(last, axis=-1, keepdims=True), 1e-12)
+
+
+def forward(hw: dict, cfg, ids: np.ndarray, batch: int, seq: int, causal: bool = False,
+            quant: bool = True) -> np.ndarray:
+    """Embeddings [batch, hidden] (L2-normalised last-token states)."""
+    x = embed(hw, ids, quant)
+    for L in hw["layers"]:
+        x = layer(L, cfg, x, batch, seq, causal, quant)
+    return head(hw, cfg, x, batch, seq)

@@ -260,6 +260,21 @@ void orc_quantize_rows_i8(const float* x, int64_t m, int64_t k, float in_scale, 
  * (RANGE) when an accumulator leaves int32. */
 int orc_gemm_i8(const int8_t* q, const int8_t* w, int64_t m, int64_t n, int64_t k, int32_t* acc) {
   int bad = 0;
+  if (k <= 131071) {
+    /* |q*w| <= 128*128 = 2^14, so any k below 2^17 sums exactly in int32
+     * (the same integers as the i64 form below, which checks the range). */
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < m; ++i) {
+      const int8_t* qr = q + i * k;
+      for (int64_t j = 0; j < n; ++j) {
+        const int8_t* wr = w + j * k;
+        int32_t s = 0;
+        for (int64_t p = 0; p < k; ++p) s += (int32_t)qr[p] * (int32_t)wr[p];
+        acc[i * n + j] = s;
+      }
+    }
+    return 0;
+  }
 #pragma omp parallel for schedule(static) reduction(| : bad)
   for (int64_t i = 0; i < m; ++i) {
     for (int64_t j = 0; j < n; ++j) {

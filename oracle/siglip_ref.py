@@ -57,7 +57,7 @@ def layer_norm(x, g, b, eps):
 
 def gelu_tanh(x):
     """host.rs:15-18: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))."""
-    return 0.5 * x * (1.0 + np.tanh(np.sqrt(2.0 / np.pi) * (x + 0.044715 * x ** 3)))
+    return 0.5 * x * (1.0 + np.tanh(np.sqrt(2.0 / np.pi) * (x + 0.044715 * (x * x * x))))
 
 
 def _w8a8(x16, w):
@@ -65,27 +65,58 @@ def _w8a8(x16, w):
     return orc.w8a8_matmul(np.asarray(x16, np.float32), codes, ws).astype(np.float64)
 
 
-def forward(hw: dict, cfg, patches: np.ndarray, images: int) -> np.ndarray:
-    """Final-LayerNorm patch states [images*patches, hidden] (f64)."""
+def attention(qkv, cfg, images: int, f16_inputs: bool = False) -> np.ndarray:
+    """Bidirectional softmax(q k^T / sqrt(D)) v per image and head over a fused
+    q|k|v [images*patches, 3*heads*D] buffer (f64). f16_inputs: the buffer
+    holds f16 values, so the C oracle's flash_attn_ref (attn/oneshot.rs:130-199,
+    f64 arithmetic, f16 result) computes it."""
     S, H, D = cfg.patches, cfg.heads, cfg.head_dim
     hq = H * D
-    x = np.asarray(patches, np.float64).reshape(images * S, cfg.hidden).copy()
-    for L in hw["layers"]:
-        wqkv = np.concatenate([L["wq"], L["wk"], L["wv"]], 0)
-        h16 = _f16(layer_norm(x, L["ln1_g"], L["ln1_b"], cfg.eps))
-        qkv = _f16(_w8a8(h16, wqkv))
-        att = np.empty((images * S, hq))
+    att = np.empty((images * S, hq))
+    if f16_inputs:
+        bits = orc.f32_to_f16_bits(np.asarray(qkv, np.float32))
         for im in range(images):
             rows = slice(im * S, (im + 1) * S)
-            for hh in range(H):
-                q = qkv[rows, hh * D:(hh + 1) * D]
-                k = qkv[rows, hq + hh * D:hq + (hh + 1) * D]
-                v = qkv[rows, 2 * hq + hh * D:2 * hq + (hh + 1) * D]
-                s = q @ k.T / np.sqrt(D)
-                p = np.exp(s - s.max(-1, keepdims=True))
-                att[rows, hh * D:(hh + 1) * D] = (p / p.sum(-1, keepdims=True)) @ v
-        x = x + _f16(_w8a8(_f16(att), L["wo"]))
-        h16 = _f16(layer_norm(x, L["ln2_g"], L["ln2_b"], cfg.eps))
-        f16 = _f16(gelu_tanh(_f16(_w8a8(h16, L["w1"]))))
-        x = x + _f16(_w8a8(f16, L["w2"]))
+            q, k, v = (np.ascontiguousarray(bits[rows, i * hq:(i + 1) * hq]) for i in range(3))
+            att[rows] = orc.f16_bits_to_f32(orc.flash_attn_ref(q, k, v, H, H, D, 1.0 / np.sqrt(D)))
+        return att
+    for im in range(images):
+        rows = slice(im * S, (im + 1) * S)
+        for hh in range(H):
+            q = qkv[rows, hh * D:(hh + 1) * D]
+            k = qkv[rows, hq + hh * D:hq + (hh + 1) * D]
+            v = qkv[rows, 2 * hq + hh * D:2 * hq + (hh + 1) * D]
+            s = q @ k.T / np.sqrt(D)
+            p = np.exp(s - s.max(-1, keepdims=True))
+            att[rows, hh * D:(hh + 1) * D] = (p / p.sum(-1, keepdims=True)) @ v
+    return att
+
+
+def layer(L: dict, cfg, x: np.ndarray, images: int, quant: bool = True) -> np.ndarray:
+    """One pre-LN encoder layer on the f64 residual stream x [images*patches,
+    hidden]; returns the new residual stream. quant=True follows the device's
+    W8A8 projections and f16 activations (GELU of the f32 fc1 product, then
+    the f16 store, as the fused fc1 epilogue does); quant=False is the float
+    skeleton (f64 throughout, no codes)."""
+    if quant:
+        f16, lin = _f16, _w8a8
+    else:
+        f16 = lambda a: np.asarray(a, np.float64)  # noqa: E731
+        lin = lambda a, w: np.asarray(a, np.float64) @ np.asarray(w, np.float64).T  # noqa: E731
+    x = np.asarray(x, np.float64)
+    wqkv = np.concatenate([L["wq"], L["wk"], L["wv"]], 0)
+    h16 = f16(layer_norm(x, L["ln1_g"], L["ln1_b"], cfg.eps))
+    qkv = f16(lin(h16, wqkv))
+    att = attention(qkv, cfg, images, f16_inputs=quant)
+    x = x + f16(lin(f16(att), L["wo"]))
+    h16 = f16(layer_norm(x, L["ln2_g"], L["ln2_b"], cfg.eps))
+    f = f16(gelu_tanh(lin(h16, L["w1"])))
+    return x + f16(lin(f, L["w2"]))
+
+
+def forward(hw: dict, cfg, patches: np.ndarray, images: int, quant: bool = True) -> np.ndarray:
+    """Final-LayerNorm patch states [images*patches, hidden] (f64)."""
+    x = np.asarray(patches, np.float64).reshape(images * cfg.patches, cfg.hidden).copy()
+    for L in hw["layers"]:
+        x = layer(L, cfg, x, images, quant)
     return layer_norm(x, hw["post_g"], hw["post_b"], cfg.eps)
