@@ -144,14 +144,15 @@ enum : int {
   kEpiF16Gelu, kEpiS8F16Gelu  // f16 gelu_tanh(value) (host.rs:15-18)
 };
 
-// gelu_tanh(g) = 0.5 g (1 + tanh(sqrt(2/pi) (g + 0.044715 g^3))) with the
-// hardware tanh approximation (relative error ~2^-11, at the f16 output's
-// rounding level).
+// gelu_tanh(g) = 0.5 g (1 + tanh(u)), u = sqrt(2/pi) (g + 0.044715 g^3),
+// evaluated through the identity 0.5 (1 + tanh(u)) = 1 / (1 + exp(-2u)):
+// one exp and one divide, relative error ~1e-6 over the whole range. (A
+// tanh approximation with ~2^-11 ABSOLUTE error turns into a large relative
+// error in the negative tail, where 1 + tanh(u) is small.) Large negative g:
+// exp overflows to +inf and the quotient is -0.
 __device__ __forceinline__ float gelu_acc(float g) {
-  const float inner = (g + g * g * g * 0.044715f) * 0.7978845608028654f;
-  float t;
-  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(inner));
-  return (g * (t + 1.0f)) * 0.5f;
+  const float u = (g + g * g * g * 0.044715f) * 0.7978845608028654f;
+  return __fdividef(g, 1.0f + __expf(-2.0f * u));
 }
 
 // silu on the epilogue path: two MUFU operations (ex2, rcp) per value, so the

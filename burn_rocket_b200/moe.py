@@ -159,54 +159,72 @@ class MoeModel:
         self.graph = None
 
     # ------------------------------------------------------------------ forward
-    def forward_device(self, stream=None, record_routing: bool = False):
-        """One forward over self.ids_in (int32 [T]) into self.out (f16, final-normed)."""
-        import torch
+    def _layer(self, L: dict, stream=None, record_routing: bool = False):
+        """One decoder layer on the residual stream self.x, in place (both
+        residual adds included)."""
         cfg, lib, T = self.cfg, _lib.load(), self.T
         st = _stream_ptr(stream)
         h, d, nh, nkv, E, I, k = cfg.hidden, cfg.head_dim, cfg.heads, cfg.kv_heads, cfg.experts, cfg.inter, cfg.top_k
         ld = (nh + 2 * nkv) * d
         qkv_p, xp, ws = _dev_ptr(self.qkv), _dev_ptr(self.x), _dev_ptr(self.ws)
-        _check(lib.rb_embed_gather(_dev_ptr(self.ids_in), T, _dev_ptr(self.embed), cfg.vocab, h, xp, st),
-               "embed_gather")
+        _check(lib.rb_add_rms_norm(xp, None, _dev_ptr(L["in_norm"]), cfg.eps, _dev_ptr(self.h), T, h, st),
+               "add_rms_norm")
+        matmul(self.h, L["qkv"], out=self.qkv, stream=stream)  # q/k norm + RoPE fused when fuse_qk_rope
+        if not self.fuse_qk_rope:
+            _check(lib.rb_qk_norm_rope(qkv_p, ld, T, nh, nkv, d, _dev_ptr(L["q_norm"]), _dev_ptr(L["k_norm"]),
+                                       cfg.eps, _dev_ptr(self.cos), _dev_ptr(self.sin), self.seq, st),
+                   "qk_norm_rope")
+        _check(lib.rb_attention_batched(qkv_p, ld, qkv_p + nh * d * 2, ld, qkv_p + (nh + nkv) * d * 2, ld,
+                                        _dev_ptr(self.attn), nh * d, DTYPE_F16, self.batch, self.seq, self.seq,
+                                        nh, nkv, d, 1.0 / math.sqrt(d), 0.0, MASK_CAUSAL, -1, 0, 0, st),
+               "rocket_flash_attn", self.seq, self.seq, d)
+        matmul(self.attn, L["o"], out=self.o, stream=stream)
+        _check(lib.rb_add_rms_norm(xp, _dev_ptr(self.o), _dev_ptr(L["post_norm"]), cfg.eps, _dev_ptr(self.h),
+                                   T, h, st), "add_rms_norm")
+        matmul(self.h, L["router"], out=self.logits, stream=stream)
+        _check(lib.rb_moe_route(_dev_ptr(self.logits), T, E, k, 1, _dev_ptr(self.ids), _dev_ptr(self.wts), st),
+               "moe_route")
+        if record_routing:
+            self.routing.append((self.ids.clone(), self.wts.clone()))
+        _check(lib.rb_moe_dispatch(_dev_ptr(self.ids), T, k, E, _dev_ptr(self.h), h, ws, _dev_ptr(self.xp), st),
+               "moe_dispatch")
+        if self.gated:  # silu(gate x) * (up x) straight from the grouped GEMM
+            _check(lib.rb_matmul_grouped(L["gu"].id, E, _dev_ptr(self.xp), self.max_rows, ws, T, k,
+                                         _dev_ptr(self.actp), DTYPE_F16, st), "matmul_grouped")
+        else:
+            _check(lib.rb_matmul_grouped(L["gu"].id, E, _dev_ptr(self.xp), self.max_rows, ws, T, k,
+                                         _dev_ptr(self.gup), DTYPE_F16, st), "matmul_grouped")
+            _check(lib.rb_silu_mul_halves(_dev_ptr(self.gup), self.max_rows, I, _dev_ptr(self.actp), st),
+                   "silu_mul")
+        _check(lib.rb_matmul_grouped(L["down"].id, E, _dev_ptr(self.actp), self.max_rows, ws, T, k,
+                                     _dev_ptr(self.yp), DTYPE_F16, st), "matmul_grouped")
+        _check(lib.rb_moe_combine(xp, _dev_ptr(self.yp), h, _dev_ptr(self.ids), _dev_ptr(self.wts), ws, T, k, E,
+                                  st), "moe_combine")
+
+    def embed_device(self, stream=None):
+        """self.x = the f32 embedding rows of self.ids_in (the residual stream's start)."""
+        cfg, lib = self.cfg, _lib.load()
+        _check(lib.rb_embed_gather(_dev_ptr(self.ids_in), self.T, _dev_ptr(self.embed), cfg.vocab, cfg.hidden,
+                                   _dev_ptr(self.x), _stream_ptr(stream)), "embed_gather")
+        return self.x
+
+    def forward_device(self, stream=None, record_routing: bool = False):
+        """One forward over self.ids_in (int32 [T]) into self.out (f16, final-normed)."""
+        cfg, lib = self.cfg, _lib.load()
+        self.embed_device(stream)
         self.routing = []
         for L in self.layers:
-            _check(lib.rb_add_rms_norm(xp, None, _dev_ptr(L["in_norm"]), cfg.eps, _dev_ptr(self.h), T, h, st),
-                   "add_rms_norm")
-            matmul(self.h, L["qkv"], out=self.qkv, stream=stream)  # q/k norm + RoPE fused when fuse_qk_rope
-            if not self.fuse_qk_rope:
-                _check(lib.rb_qk_norm_rope(qkv_p, ld, T, nh, nkv, d, _dev_ptr(L["q_norm"]), _dev_ptr(L["k_norm"]),
-                                           cfg.eps, _dev_ptr(self.cos), _dev_ptr(self.sin), self.seq, st),
-                       "qk_norm_rope")
-            _check(lib.rb_attention_batched(qkv_p, ld, qkv_p + nh * d * 2, ld, qkv_p + (nh + nkv) * d * 2, ld,
-                                            _dev_ptr(self.attn), nh * d, DTYPE_F16, self.batch, self.seq, self.seq,
-                                            nh, nkv, d, 1.0 / math.sqrt(d), 0.0, MASK_CAUSAL, -1, 0, 0, st),
-                   "rocket_flash_attn", self.seq, self.seq, d)
-            matmul(self.attn, L["o"], out=self.o, stream=stream)
-            _check(lib.rb_add_rms_norm(xp, _dev_ptr(self.o), _dev_ptr(L["post_norm"]), cfg.eps, _dev_ptr(self.h),
-                                       T, h, st), "add_rms_norm")
-            matmul(self.h, L["router"], out=self.logits, stream=stream)
-            _check(lib.rb_moe_route(_dev_ptr(self.logits), T, E, k, 1, _dev_ptr(self.ids), _dev_ptr(self.wts), st),
-                   "moe_route")
-            if record_routing:
-                self.routing.append((self.ids.clone(), self.wts.clone()))
-            _check(lib.rb_moe_dispatch(_dev_ptr(self.ids), T, k, E, _dev_ptr(self.h), h, ws, _dev_ptr(self.xp), st),
-                   "moe_dispatch")
-            if self.gated:  # silu(gate x) * (up x) straight from the grouped GEMM
-                _check(lib.rb_matmul_grouped(L["gu"].id, E, _dev_ptr(self.xp), self.max_rows, ws, T, k,
-                                             _dev_ptr(self.actp), DTYPE_F16, st), "matmul_grouped")
-            else:
-                _check(lib.rb_matmul_grouped(L["gu"].id, E, _dev_ptr(self.xp), self.max_rows, ws, T, k,
-                                             _dev_ptr(self.gup), DTYPE_F16, st), "matmul_grouped")
-                _check(lib.rb_silu_mul_halves(_dev_ptr(self.gup), self.max_rows, I, _dev_ptr(self.actp), st),
-                       "silu_mul")
-            _check(lib.rb_matmul_grouped(L["down"].id, E, _dev_ptr(self.actp), self.max_rows, ws, T, k,
-                                         _dev_ptr(self.yp), DTYPE_F16, st), "matmul_grouped")
-            _check(lib.rb_moe_combine(xp, _dev_ptr(self.yp), h, _dev_ptr(self.ids), _dev_ptr(self.wts), ws, T, k, E,
-                                      st), "moe_combine")
-        _check(lib.rb_add_rms_norm(xp, None, _dev_ptr(self.final_norm), cfg.eps, _dev_ptr(self.out), T, h, st),
-               "add_rms_norm")
+            self._layer(L, stream, record_routing)
+        _check(lib.rb_add_rms_norm(_dev_ptr(self.x), None, _dev_ptr(self.final_norm), cfg.eps, _dev_ptr(self.out),
+                                   self.T, cfg.hidden, _stream_ptr(stream)), "add_rms_norm")
         return self.out
+
+    def layer_step(self, li: int, stream=None):
+        """Layer li alone on self.x (its output residual stream left in self.x;
+        the layer's routing in self.ids / self.wts): a per-layer view of
+        forward_device for checking each layer from the device's own input."""
+        self._layer(self.layers[li], stream)
+        return self.x
 
     def capture(self):
         import torch

@@ -146,41 +146,67 @@ class Qwen3Embedding:
         self.graph = None
 
     # ------------------------------------------------------------------ forward
+    def _layer(self, L: dict, delta, stream=None):
+        """One decoder layer on the residual stream self.x: `delta` (a device
+        pointer or None) is the previous layer's pending MLP output, folded into
+        this layer's first residual-add + RMSNorm. Returns this layer's pending
+        MLP output pointer."""
+        cfg, lib, T = self.cfg, _lib.load(), self.T
+        st = _stream_ptr(stream)
+        h, hd, nh, nkv = cfg.hidden, cfg.head_dim, cfg.heads, cfg.kv_heads
+        ld = (nh + 2 * nkv) * hd
+        qkv_p = _dev_ptr(self.qkv)
+        _check(lib.rb_add_rms_norm(_dev_ptr(self.x), delta, _dev_ptr(L["in_norm"]), cfg.eps, _dev_ptr(self.h),
+                                   T, h, st), "add_rms_norm")
+        matmul(self.h, L["qkv"], out=self.qkv, stream=stream)  # q/k norm + RoPE fused when fuse_qk_rope
+        if not self.fuse_qk_rope:
+            _check(lib.rb_qk_norm_rope(qkv_p, ld, T, nh, nkv, hd, _dev_ptr(L["q_norm"]), _dev_ptr(L["k_norm"]),
+                                       cfg.eps, _dev_ptr(self.cos), _dev_ptr(self.sin), self.seq, st),
+                   "qk_norm_rope")
+        _check(lib.rb_attention_batched(qkv_p, ld, qkv_p + nh * hd * 2, ld, qkv_p + (nh + nkv) * hd * 2, ld,
+                                        _dev_ptr(self.attn), nh * hd, DTYPE_F16, self.batch, self.seq, self.seq,
+                                        nh, nkv, hd, 1.0 / math.sqrt(hd), 0.0,
+                                        MASK_CAUSAL if self.causal else MASK_NONE, -1, 0, 0, st),
+               "rocket_flash_attn", self.seq, self.seq, hd)
+        matmul(self.attn, L["o"], out=self.o, stream=stream)
+        _check(lib.rb_add_rms_norm(_dev_ptr(self.x), _dev_ptr(self.o), _dev_ptr(L["post_norm"]), cfg.eps,
+                                   _dev_ptr(self.h), T, h, st), "add_rms_norm")
+        matmul(self.h, L["gu"], out=self.act, stream=stream)  # silu(h Wg^T) * (h Wu^T)
+        matmul(self.act, L["down"], out=self.d, stream=stream)
+        return _dev_ptr(self.d)
+
     def forward_device(self, stream=None):
         """One forward over self.ids (device int32 [T]) into self.out [batch, hidden]."""
         cfg, lib, T = self.cfg, _lib.load(), self.T
         st = _stream_ptr(stream)
-        h, hd, nh, nkv, inter = cfg.hidden, cfg.head_dim, cfg.heads, cfg.kv_heads, cfg.inter
-        ld = (nh + 2 * nkv) * hd
-        _check(lib.rb_embed_gather(_dev_ptr(self.ids), T, _dev_ptr(self.embed), cfg.vocab, h, _dev_ptr(self.x), st),
-               "embed_gather")
-        qkv_p = _dev_ptr(self.qkv)
+        h = cfg.hidden
+        self.embed_device(stream)
         delta = None
         for L in self.layers:
-            _check(lib.rb_add_rms_norm(_dev_ptr(self.x), delta, _dev_ptr(L["in_norm"]), cfg.eps, _dev_ptr(self.h),
-                                       T, h, st), "add_rms_norm")
-            matmul(self.h, L["qkv"], out=self.qkv, stream=stream)  # q/k norm + RoPE fused when fuse_qk_rope
-            if not self.fuse_qk_rope:
-                _check(lib.rb_qk_norm_rope(qkv_p, ld, T, nh, nkv, hd, _dev_ptr(L["q_norm"]), _dev_ptr(L["k_norm"]),
-                                           cfg.eps, _dev_ptr(self.cos), _dev_ptr(self.sin), self.seq, st),
-                       "qk_norm_rope")
-            _check(lib.rb_attention_batched(qkv_p, ld, qkv_p + nh * hd * 2, ld, qkv_p + (nh + nkv) * hd * 2, ld,
-                                            _dev_ptr(self.attn), nh * hd, DTYPE_F16, self.batch, self.seq, self.seq,
-                                            nh, nkv, hd, 1.0 / math.sqrt(hd), 0.0,
-                                            MASK_CAUSAL if self.causal else MASK_NONE, -1, 0, 0, st),
-                   "rocket_flash_attn", self.seq, self.seq, hd)
-            matmul(self.attn, L["o"], out=self.o, stream=stream)
-            _check(lib.rb_add_rms_norm(_dev_ptr(self.x), _dev_ptr(self.o), _dev_ptr(L["post_norm"]), cfg.eps,
-                                       _dev_ptr(self.h), T, h, st), "add_rms_norm")
-            matmul(self.h, L["gu"], out=self.act, stream=stream)  # silu(h Wg^T) * (h Wu^T)
-            matmul(self.act, L["down"], out=self.d, stream=stream)
-            delta = _dev_ptr(self.d)
+            delta = self._layer(L, delta, stream)
         # final residual, then the last token's norm + L2
         _check(lib.rb_add_rms_norm(_dev_ptr(self.x), delta, _dev_ptr(self.final_norm), cfg.eps, _dev_ptr(self.h),
                                    T, h, st), "add_rms_norm")
         _check(lib.rb_last_token_l2(_dev_ptr(self.x), self.batch, self.seq, h, _dev_ptr(self.final_norm), cfg.eps,
                                     _dev_ptr(self.out), st), "last_token_l2")
         return self.out
+
+    def embed_device(self, stream=None):
+        """self.x = the f32 embedding rows of self.ids (the residual stream's start)."""
+        cfg, lib = self.cfg, _lib.load()
+        _check(lib.rb_embed_gather(_dev_ptr(self.ids), self.T, _dev_ptr(self.embed), cfg.vocab, cfg.hidden,
+                                   _dev_ptr(self.x), _stream_ptr(stream)), "embed_gather")
+        return self.x
+
+    def layer_step(self, li: int, stream=None):
+        """Layer li alone on self.x, leaving its output residual stream in self.x
+        (the pending MLP output folded in; self.h is scratch): a per-layer view
+        of forward_device for checking each layer from the device's own input."""
+        cfg, lib = self.cfg, _lib.load()
+        delta = self._layer(self.layers[li], None, stream)
+        _check(lib.rb_add_rms_norm(_dev_ptr(self.x), delta, _dev_ptr(self.final_norm), cfg.eps, _dev_ptr(self.h),
+                                   self.T, cfg.hidden, _stream_ptr(stream)), "add_rms_norm")
+        return self.x
 
     def capture(self):
         """Capture forward_device into a CUDA graph (after one eager warm-up)."""

@@ -117,6 +117,45 @@ class SiglipTower:
         self.graph = None
 
     # ------------------------------------------------------------------ forward
+    def _rows(self, img0: int, n_img: int | None):
+        S = self.cfg.patches
+        n_img = self.images - img0 if n_img is None else n_img
+        r0, T = img0 * S, n_img * S
+        return n_img, T, (lambda t: t[r0:r0 + T])
+
+    def _layer(self, L: dict, delta, stream=None, img0: int = 0, n_img: int | None = None):
+        """One encoder layer on the residual stream self.x (rows of images
+        [img0, img0 + n_img)): `delta` (a device pointer or None) is the previous
+        layer's pending MLP output, folded into this layer's first residual-add
+        + LayerNorm. Returns this layer's pending MLP output pointer."""
+        cfg, lib = self.cfg, _lib.load()
+        st = _stream_ptr(stream)
+        h, hq, S = cfg.hidden, cfg.heads * cfg.head_dim, cfg.patches
+        ld = 3 * hq
+        n_img, T, rows = self._rows(img0, n_img)
+        x, hc, hs, qkv, attn, o, f, d = (rows(t) for t in (self.x, self.hc, self.hs, self.qkv, self.attn,
+                                                            self.o, self.f, self.d))
+        qkv_p = _dev_ptr(qkv)
+        _check(lib.rb_add_layer_norm_quant(_dev_ptr(x), delta, _dev_ptr(L["ln1_g"]), _dev_ptr(L["ln1_b"]),
+                                           cfg.eps, _dev_ptr(hc), _dev_ptr(hs), T, h, st),
+               "add_layer_norm_quant")
+        _check(lib.rb_matmul_w8a8_codes(L["qkv"].id, _dev_ptr(hc), _dev_ptr(hs), T, h, qkv_p,
+                                        DTYPE_F16, st), "rocket_matmul", T, h, 3 * hq)
+        _check(lib.rb_attention_batched(qkv_p, ld, qkv_p + hq * 2, ld, qkv_p + 2 * hq * 2, ld,
+                                        _dev_ptr(attn), hq, DTYPE_F16, n_img, S, S,
+                                        cfg.heads, cfg.heads, cfg.head_dim, 1.0 / math.sqrt(cfg.head_dim),
+                                        0.0, MASK_NONE, -1, 0, 0, st),
+               "rocket_flash_attn", S, S, cfg.head_dim)
+        matmul(attn, L["o"], out=o, stream=stream)
+        _check(lib.rb_add_layer_norm_quant(_dev_ptr(x), _dev_ptr(o), _dev_ptr(L["ln2_g"]),
+                                           _dev_ptr(L["ln2_b"]), cfg.eps, _dev_ptr(hc), _dev_ptr(hs),
+                                           T, h, st), "add_layer_norm_quant")
+        _check(lib.rb_matmul_w8a8_codes(L["fc1"].id, _dev_ptr(hc), _dev_ptr(hs), T, h,
+                                        _dev_ptr(f), DTYPE_F16, st), "rocket_matmul", T, h, cfg.inter)
+        # (gelu_tanh(h W1^T) is fused into the fc1 epilogue)
+        matmul(f, L["fc2"], out=d, stream=stream)
+        return _dev_ptr(d)
+
     def forward_device(self, stream=None, img0: int = 0, n_img: int | None = None):
         """One forward over self.patches (f32 [T, hidden]) into self.out (f16 [T, hidden]);
         img0 / n_img restrict it to the images [img0, img0 + n_img) (their rows
@@ -124,44 +163,32 @@ class SiglipTower:
         import torch
         cfg, lib = self.cfg, _lib.load()
         st = _stream_ptr(stream)
-        h, hq, S = cfg.hidden, cfg.heads * cfg.head_dim, cfg.patches
-        ld = 3 * hq
-        n_img = self.images - img0 if n_img is None else n_img
-        r0, T = img0 * S, n_img * S
-        rows = lambda t: t[r0:r0 + T]  # noqa: E731
-        x, hc, hs, qkv, attn, o, f, d, out = (rows(t) for t in (self.x, self.hc, self.hs, self.qkv, self.attn,
-                                                                 self.o, self.f, self.d, self.out))
+        n_img, T, rows = self._rows(img0, n_img)
+        x, out = rows(self.x), rows(self.out)
         # the residual stream starts as the input (x is rewritten in place each layer)
         if stream is None:
             x.copy_(rows(self.patches))
         else:
             with torch.cuda.stream(stream):
                 x.copy_(rows(self.patches))
-        qkv_p = _dev_ptr(qkv)
         delta = None
         for L in self.layers:
-            _check(lib.rb_add_layer_norm_quant(_dev_ptr(x), delta, _dev_ptr(L["ln1_g"]), _dev_ptr(L["ln1_b"]),
-                                               cfg.eps, _dev_ptr(hc), _dev_ptr(hs), T, h, st),
-                   "add_layer_norm_quant")
-            _check(lib.rb_matmul_w8a8_codes(L["qkv"].id, _dev_ptr(hc), _dev_ptr(hs), T, h, qkv_p,
-                                            DTYPE_F16, st), "rocket_matmul", T, h, 3 * hq)
-            _check(lib.rb_attention_batched(qkv_p, ld, qkv_p + hq * 2, ld, qkv_p + 2 * hq * 2, ld,
-                                            _dev_ptr(attn), hq, DTYPE_F16, n_img, S, S,
-                                            cfg.heads, cfg.heads, cfg.head_dim, 1.0 / math.sqrt(cfg.head_dim),
-                                            0.0, MASK_NONE, -1, 0, 0, st),
-                   "rocket_flash_attn", S, S, cfg.head_dim)
-            matmul(attn, L["o"], out=o, stream=stream)
-            _check(lib.rb_add_layer_norm_quant(_dev_ptr(x), _dev_ptr(o), _dev_ptr(L["ln2_g"]),
-                                               _dev_ptr(L["ln2_b"]), cfg.eps, _dev_ptr(hc), _dev_ptr(hs),
-                                               T, h, st), "add_layer_norm_quant")
-            _check(lib.rb_matmul_w8a8_codes(L["fc1"].id, _dev_ptr(hc), _dev_ptr(hs), T, h,
-                                            _dev_ptr(f), DTYPE_F16, st), "rocket_matmul", T, h, cfg.inter)
-            # (gelu_tanh(h W1^T) is fused into the fc1 epilogue)
-            matmul(f, L["fc2"], out=d, stream=stream)
-            delta = _dev_ptr(d)
+            delta = self._layer(L, delta, stream, img0, n_img)
         _check(lib.rb_add_layer_norm(_dev_ptr(x), delta, _dev_ptr(self.post_g), _dev_ptr(self.post_b), cfg.eps,
-                                     _dev_ptr(out), T, h, st), "add_layer_norm")
+                                     _dev_ptr(out), T, cfg.hidden, st), "add_layer_norm")
         return self.out
+
+    def layer_step(self, li: int, stream=None):
+        """Layer li alone on self.x (all images), leaving its output residual
+        stream in self.x (the pending MLP output folded in; self.out is
+        scratch): a per-layer view of forward_device for checking each layer
+        from the device's own input."""
+        cfg, lib = self.cfg, _lib.load()
+        delta = self._layer(self.layers[li], None, stream)
+        _check(lib.rb_add_layer_norm(_dev_ptr(self.x), delta, _dev_ptr(self.post_g), _dev_ptr(self.post_b),
+                                     cfg.eps, _dev_ptr(self.out), self.T, cfg.hidden, _stream_ptr(stream)),
+               "add_layer_norm")
+        return self.x
 
     def capture(self):
         """Capture forward_device into a CUDA graph (after one eager warm-up)."""

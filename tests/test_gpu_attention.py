@@ -2,7 +2,8 @@
 
 Small and ragged cases compare against the CPU oracle (flash_attn_ref of
 attn/oneshot.rs:130-185 with the masks.rs predicates); the full BASELINE
-config #2 size compares against a plain torch fp32 reference of the same op.
+config #2 size compares against the oracle on one KV group and against a plain
+torch fp32 reference of the same op on all heads.
 Tolerance (north star): cosine >= 0.9999 and max |err| <= 1e-2 * max |ref|.
 """
 import math
@@ -170,6 +171,42 @@ def test_attention_config2_full_size(rb, causal, dtype, split):
     mr = ((got - ref).abs().max() / ref.abs().max()).item()
     assert cos >= COS_MIN, cos
     assert mr <= MAX_REL, mr
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_attention_config2_full_size_vs_oracle(rb, orc, causal):
+    """BASELINE config #2 at full size (3633 tokens, 16/8 heads x 128, RoPE
+    theta 1e6 pre-applied, fp16) against the oracle's flash_attn_ref
+    (attn/oneshot.rs:130-199, f64, the -30000 clamp) on one KV group: query
+    heads 10 and 11, which read KV head 5."""
+    import torch
+    n, h, hkv, d = 3633, 16, 8, 128
+    rng = np.random.default_rng(36)
+    half = d // 2
+    inv = np.array([1.0 / 1e6 ** (2.0 * i / d) for i in range(half)], np.float64).astype(np.float32)
+    ang = (np.arange(n, dtype=np.float32)[:, None] * inv[None, :]).astype(np.float32)
+    cos, sin = np.cos(ang)[:, None, :], np.sin(ang)[:, None, :]
+
+    def roped(heads):
+        x = rng.standard_normal((n, heads, d)).astype(np.float32)
+        x1, x2 = x[..., :half], x[..., half:]
+        return np.concatenate([x1 * cos - x2 * sin, x2 * cos + x1 * sin], -1).reshape(n, heads * d)
+
+    q = orc.f32_to_f16_bits(roped(h))
+    k = orc.f32_to_f16_bits(roped(hkv))
+    v = orc.f32_to_f16_bits(rng.standard_normal((n, hkv * d)).astype(np.float32))
+    tq, tk, tv = (torch.from_numpy(a.view(np.float16)).cuda() for a in (q, k, v))
+    out = rb.attention(tq, tk, tv, h, hkv, d, 1.0 / math.sqrt(d), None, causal)
+    torch.cuda.synchronize()
+    rb.check_device_errors()
+    got = out.float().cpu().numpy()[:, 10 * d:12 * d]
+    mode = orc.MASK_CAUSAL if causal else orc.MASK_NONE
+    ref = orc.f16_bits_to_f32(orc.flash_attn_ref(np.ascontiguousarray(q[:, 10 * d:12 * d]),
+                                                 np.ascontiguousarray(k[:, 5 * d:6 * d]),
+                                                 np.ascontiguousarray(v[:, 5 * d:6 * d]), 2, 1, d,
+                                                 1.0 / math.sqrt(d), 0.0, mode))
+    assert cosine(got, ref) >= COS_MIN, cosine(got, ref)
+    assert max_rel(got, ref) <= MAX_REL, max_rel(got, ref)
 
 
 def test_attention_host_entry(rb, orc):

@@ -16,6 +16,12 @@ import pytest
 pytestmark = pytest.mark.gpu
 
 
+def max_rel(got, want):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    return float(np.abs(got - want).max() / (np.abs(want).max() + 1e-30))
+
+
 def cosine(a, b):
     a, b = np.asarray(a, np.float64).ravel(), np.asarray(b, np.float64).ravel()
     return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b) + 1e-300))
@@ -91,7 +97,7 @@ def test_dispatch_grouped_gemm_combine_matches_oracle(rb, orc):
     want = moe_ref.experts_combine(np.zeros((T, H)), x16.astype(np.float64), ids_np, w_np,
                                    [(deq(g), deq(u), deq(d)) for g, u, d in experts])
     assert cosine(got, want) >= 0.9999, cosine(got, want)
-    assert np.abs(got - want).max() <= 2e-2 * np.abs(want).max()
+    assert max_rel(got, want) <= 1e-2, max_rel(got, want)
 
 
 SMALL = dict(layers=2, hidden=1024, heads=8, kv_heads=2, head_dim=128, experts=16, top_k=4, inter=256, vocab=512)
@@ -122,10 +128,15 @@ def test_moe_forward_matches_oracle(rb):
         # the combine sums in ascending expert id either way)
         assert np.array_equal(np.sort(dev_ids[stable], 1), np.sort(rid[stable], 1)), li
         stable_all &= stable
-    assert cosine(got[stable_all], want[stable_all]) >= 0.999, cosine(got[stable_all], want[stable_all])
+    # the whole forward, with the oracle chain following the device's routing
+    # (a near-tie flip changes which experts a token uses, which no tolerance
+    # on the outputs can absorb; the selection itself is checked above)
+    forced, _ = moe_ref.forward(hw, cfg, ids, batch, seq,
+                                force_routing=[r[0].cpu().numpy() for r in model.routing])
     for b in range(batch):
         rows = slice(b * seq, (b + 1) * seq)
-        assert cosine(got[rows], want[rows]) >= 0.99, (b, cosine(got[rows], want[rows]))
+        assert cosine(got[rows], forced[rows]) >= 0.9999, (b, cosine(got[rows], forced[rows]))
+    assert max_rel(got, forced) <= 1e-2, max_rel(got, forced)
 
 
 def test_moe_graph_replay_equals_eager(rb):
