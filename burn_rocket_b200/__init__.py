@@ -174,22 +174,6 @@ def set_weight_activation(w: WeightId, act: str) -> None:
     _check(_lib.load().rb_set_weight_activation(w.id, names[act]), "rb_set_weight_activation")
 
 
-def set_weight_qk_norm_rope(w: WeightId, n_q_heads: int, n_k_heads: int, wq, wk, eps: float, cos, sin,
-                            seq: int) -> None:
-    """Fuse the q/k RMSNorm + RoPE glue (rb_qk_norm_rope, model.rs:369-376)
-    into later matmuls on the fused q|k|v Q8_0 weight `w`: their f16 output
-    comes out with its first n_q_heads heads normalised by wq, the next
-    n_k_heads by wk, and both rotated at position row % seq. wq, wk ([128]),
-    cos and sin ([seq, 64]) are f32 CUDA tensors that must outlive those
-    calls. n_q_heads = n_k_heads = 0 turns it off."""
-    for t in (wq, wk, cos, sin):
-        if not (t.is_cuda and t.dtype.is_floating_point and t.element_size() == 4 and t.is_contiguous()):
-            raise ValueError("wq, wk, cos and sin must be contiguous f32 CUDA tensors")
-    _check(_lib.load().rb_set_weight_qk_norm_rope(w.id, n_q_heads, n_k_heads, wq.data_ptr(), wk.data_ptr(), eps,
-                                                  cos.data_ptr(), sin.data_ptr(), seq),
-           "rb_set_weight_qk_norm_rope")
-
-
 def pack_gated_q8_0(gate, up) -> WeightId:
     """SwiGLU gate|up as one Q8_0 weight whose matmul returns the fused
     f16 silu(x gate^T) * (x up^T) ([M, n_inter]; host.rs:31-38), i.e. the

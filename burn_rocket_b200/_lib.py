@@ -97,7 +97,6 @@ SIGNATURES = {
     "rb_matmul_w8a8_codes": (_i, [_i64, _p, _p, _i64, _i64, _p, _i, _p]),
     "rb_add_layer_norm_quant": (_i, [_p, _p, _p, _p, _f, _p, _p, _i64, _i64, _p]),
     "rb_set_weight_activation": (_i, [_i64, _i]),
-    "rb_set_weight_qk_norm_rope": (_i, [_i64, _i, _i, _p, _p, _f, _p, _p, _i]),
     "rb_pack_f32_q8_0_gated_device": (_i64, [_p, _p, _i64, _i64]),
     "rb_selftest_wait_timeout": (_i, [_i64, _p]),
     "rb_moe_workspace_bytes": (_i64, [_i64, _i, _i]),

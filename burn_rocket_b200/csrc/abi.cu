@@ -133,8 +133,6 @@ struct Weight {
   int64_t group = 0;         // RB_WEIGHT_I8G: K group width (scales f32 [n, k/group])
   bool gated = false;        // gate|up interleaved in 32-row blocks: matmul gives silu(gate)*up, n/2 columns
   int act = RB_ACT_NONE;     // element-wise activation fused into the matmul epilogue
-  QkRope rope{};             // q/k RMSNorm + RoPE fused into the matmul epilogue (rope.qk_cols != 0)
-  QkRope* rope_dev = nullptr;  // its device copy, read by the GEMM epilogue
   // TMA maps per staged weight-tile height ({256, 128, 96, 64}, see
   // bn_index; a CTA-pair tile stages half its N per CTA): the codes
   // (Q8_0: box 64 x bn; W8A8: box 128 x bn, 128-B swizzle) and the Q8_0
@@ -306,9 +304,6 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
     return fail(RB_E_SHAPE, "gated (SwiGLU) weight: the output must be a 16-byte aligned f16 buffer");
   if (w.act != RB_ACT_NONE && y_dtype != RB_DTYPE_F16)
     return fail(RB_E_SHAPE, "weight id %lld has a fused activation: the output must be f16", (long long)id);
-  if (w.rope.qk_cols && (y_dtype != RB_DTYPE_F16 || (reinterpret_cast<uintptr_t>(y) & 15) != 0))
-    return fail(RB_E_SHAPE, "weight id %lld has fused q/k norm + RoPE: the output must be a 16-byte aligned f16 buffer",
-                (long long)id);
 
   GemmLaunch L{};
   L.M = static_cast<int>(m);
@@ -318,7 +313,6 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
   L.ldo = static_cast<int>(n_out);
   L.gated = w.gated ? 1 : 0;
   L.act = w.act;
-  L.rope = w.rope.qk_cols ? w.rope_dev : nullptr;
   L.out_dtype = y_dtype;
   L.err = e->err;
   L.num_sms = e->num_sms;
@@ -354,15 +348,13 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
       a = e->act.ptr;
     }
     GemmPlan plan = gemm_plan(false, L.M, L.N, L.K, e->num_sms);
-    // The gated epilogue turns 128 accumulator columns into 64 outputs, the
-    // q/k norm + RoPE epilogue works on 128-column heads: tiles of 256 or 128
-    // columns.
-    if ((w.gated || w.rope.qk_cols) && plan.bn % 128 != 0) plan = GemmPlan{plan.pair ? 256 : 128, 1, plan.pair};
+    // The gated epilogue turns 128 accumulator columns into 64 outputs: tiles
+    // of 256 or 128 columns.
+    if (w.gated && plan.bn % 128 != 0) plan = GemmPlan{plan.pair ? 256 : 128, 1, plan.pair};
     CUtensorMap tmA, tmC;
     if ((rc = make_tmap_2d(&tmA, a, 2, m, k, k, 64, plan.a_rows(), 128)) != RB_OK) return rc;
     const bool tstore = output_map(&tmC, y, y_dtype, m, n_out);
-    if ((w.gated || w.rope.qk_cols) && !tstore)
-      return fail(RB_E_SHAPE, "gated / q/k-rope weight: output tensor map unavailable");
+    if (w.gated && !tstore) return fail(RB_E_SHAPE, "gated weight: output tensor map unavailable");
     const int bi = bn_index(plan.weight_rows());
     if ((rc = launch_q8_gemm(L, plan, tmA, w.tm_codes[bi], w.tm_scales[bi], tstore ? &tmC : nullptr,
                              st)) != RB_OK)
@@ -1402,7 +1394,6 @@ int rb_matmul_grouped(int64_t id, int experts, const void* x_perm_f16, int64_t m
   if (it == e->weights.end()) return fail(RB_E_SHAPE, "weight id %lld is not packed", (long long)id);
   const Weight& w = it->second;
   if (w.kind != RB_WEIGHT_Q8_0) return fail(RB_E_UNSUPPORTED, "grouped matmul: Q8_0 weights only");
-  if (w.rope.qk_cols) return fail(RB_E_UNSUPPORTED, "grouped matmul: no fused q/k norm + RoPE");
   if (experts <= 0 || w.n % experts) return fail(RB_E_SHAPE, "grouped matmul: weight rows not a multiple of experts");
   const MoeLayout ml = moe_layout(tokens, top_k, experts);
   if (max_rows != ml.max_rows) return fail(RB_E_SHAPE, "grouped matmul: max_rows must be rb_moe_max_rows()");
@@ -1522,48 +1513,12 @@ int rb_set_weight_activation(int64_t id, int act) {
   Weight& w = it->second;
   if (act != RB_ACT_NONE && act != RB_ACT_GELU_TANH) return fail(RB_E_SHAPE, "unknown activation %d", act);
   if (act != RB_ACT_NONE) {
-    if (w.rope.qk_cols)
-      return fail(RB_E_SHAPE, "weight id %lld: fused q/k norm + RoPE and an activation do not combine", (long long)id);
     if (w.gated || w.kind == RB_WEIGHT_I8G)
       return fail(RB_E_SHAPE, "weight id %lld: no fused activation on gated or group-wise weights", (long long)id);
     if (w.kind == RB_WEIGHT_W8A8 && w.out_scale != 0.0f)
       return fail(RB_E_SHAPE, "weight id %lld: no fused activation with a calibrated output grid", (long long)id);
   }
   w.act = act;
-  return RB_OK;
-}
-
-int rb_set_weight_qk_norm_rope(int64_t id, int n_q_heads, int n_k_heads, const float* wq, const float* wk,
-                               float eps, const float* cos_t, const float* sin_t, int seq) {
-  std::lock_guard<std::mutex> lk(g_mu);
-  Engine* e;
-  int rc = ensure_engine(&e);
-  if (rc) return rc;
-  auto it = e->weights.find(id);
-  if (it == e->weights.end()) return fail(RB_E_SHAPE, "weight id %lld is not packed", (long long)id);
-  Weight& w = it->second;
-  if (n_q_heads < 0 || n_k_heads < 0) return fail(RB_E_SHAPE, "qk rope: negative head counts");
-  if (n_q_heads == 0 && n_k_heads == 0) {
-    w.rope = QkRope{};
-    return RB_OK;
-  }
-  if (w.kind != RB_WEIGHT_Q8_0 || w.gated || w.act != RB_ACT_NONE)
-    return fail(RB_E_SHAPE, "weight id %lld: fused q/k norm + RoPE needs a plain Q8_0 weight", (long long)id);
-  if (w.n % 128 != 0 || (int64_t(n_q_heads) + n_k_heads) * 128 > w.n)
-    return fail(RB_E_SHAPE, "qk rope: %d + %d heads of 128 columns against %lld output columns (a multiple of 128)",
-                n_q_heads, n_k_heads, (long long)w.n);
-  if (!wq || !wk || !cos_t || !sin_t || seq <= 0 || !(eps >= 0.0f) ||
-      ((reinterpret_cast<uintptr_t>(wq) | reinterpret_cast<uintptr_t>(wk) | reinterpret_cast<uintptr_t>(cos_t) |
-        reinterpret_cast<uintptr_t>(sin_t)) & 15) != 0)
-    return fail(RB_E_SHAPE, "qk rope: norm weights and cos/sin tables must be 16-byte aligned device arrays, seq > 0");
-  const QkRope r{wq, wk, cos_t, sin_t, eps, seq, n_q_heads * 128, (n_q_heads + n_k_heads) * 128};
-  if (!w.rope_dev && cudaMalloc(&w.rope_dev, sizeof(QkRope)) != cudaSuccess) {
-    cudaGetLastError();
-    w.rope_dev = nullptr;
-    return fail(RB_E_NOMEM, "qk rope: device allocation failed");
-  }
-  RB_CUDA(cudaMemcpy(w.rope_dev, &r, sizeof(QkRope), cudaMemcpyHostToDevice), "qk rope parameters");
-  w.rope = r;
   return RB_OK;
 }
 

@@ -218,15 +218,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + Cfg::EPI_WARPS) {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    const EpiParams ep{args.s_col, args.out_dtype, args.out_scale, args.out_inv, args.rope};
+    const EpiParams ep{args.s_col, args.out_dtype, args.out_scale, args.out_inv};
     uint8_t* ebuf = smem + Cfg::EPI_OFF + (warp - kEpiWarp0) * Cfg::EPI_BUFS * kEpiBufBytes;
     // With eight epilogue warps, warps 2..5 take the first half of the tile's
     // columns and warps 6..9 the second (each quarter of TMEM lanes has two).
     constexpr int kColSplit = Cfg::EPI_WARPS / 4;
     const int cbeg = ((warp - kEpiWarp0) >> 2) * (BN / kColSplit), cend = cbeg + BN / kColSplit;
-    const int mode = args.gated           ? kEpiSiluF16
-                     : args.rope != nullptr ? kEpiQkRopeF16
-                                            : epi_mode(Cfg::I8, args.out_dtype, args.out_scale, args.act);
+    const int mode = args.gated ? kEpiSiluF16 : epi_mode(Cfg::I8, args.out_dtype, args.out_scale, args.act);
     int buf = 0;
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
@@ -409,7 +407,6 @@ static GemmArgs make_args(const GemmLaunch& L) {
   a.tile_expert = L.tile_expert;
   a.gated = L.gated;
   a.act = L.act;
-  a.rope = L.rope;
   return a;
 }
 

@@ -49,10 +49,6 @@ struct GemmArgs {
   // Element-wise activation applied before the f16 rounding (RB_ACT_*).
   int act;
   uint32_t* err;
-  // q/k RMSNorm + RoPE of the f16 output heads (kEpiQkRopeF16): a device
-  // struct, or nullptr. (A pointer: a larger by-value argument block made
-  // ptxas spill registers in the int8 pair kernel.)
-  const QkRope* rope;
 };
 
 // --------------------------------------------------------------------------
@@ -105,7 +101,6 @@ struct EpiParams {
   const float* s_col;
   int out_dtype;
   float out_scale, out_inv;
-  const QkRope* rope;
 };
 
 // Epilogue value for accumulator bits r at column n (row scale rs).
@@ -140,7 +135,6 @@ enum : int {
   kEpiRaw4 = 0, kEpiF16, kEpiBF16,
   kEpiS8F32, kEpiS8F16, kEpiS8BF16, kEpiS8F32Q, kEpiS8F16Q, kEpiS8BF16Q,
   kEpiSiluF16,  // gated weight: f16 silu(gate) * up (SwiGLU, host.rs:31-38)
-  kEpiQkRopeF16,  // f16 output with q/k RMSNorm + RoPE on the query and key heads
   kEpiF16Gelu, kEpiS8F16Gelu  // f16 gelu_tanh(value) (host.rs:15-18)
 };
 
@@ -309,109 +303,6 @@ __device__ __forceinline__ void epi_block(uint32_t tmem_base, uint32_t acc_col, 
       if (NBUF == 2) buf ^= 1;
     }
     return;
-  }
-  if constexpr (!I8) {  // Q8_0 / f16 weights only (not compiled into the int8 kernels)
-  if (mode == kEpiQkRopeF16) {
-    // Heads of 128 columns (the host makes N and the tile columns multiples
-    // of 128): a query or key head is RMS-normalised over its f16-rounded
-    // values and rotated (rotate-half RoPE at the row's position); value
-    // heads are plain f16. The arithmetic is qk_norm_rope_kernel's, in its
-    // order: the sum of squares is built as that kernel's 16 lane partials
-    // (elements 4i..4i+3 and 64+4i..64+4i+3) combined in its butterfly
-    // order, so the fused and the separate passes agree bit for bit. Four
-    // accumulator columns at a time keep the register count of the shared
-    // epilogue within the 640-thread kernels' budget. TMA-store path only
-    // (the host checks).
-    if (!rows_live) return;
-    const QkRope* R = ep.rope;
-    const int pos = (m < M ? m : 0) % R->seq;
-    const float* cs = R->cos_t + static_cast<int64_t>(pos) * 64;
-    const float* sn = R->sin_t + static_cast<int64_t>(pos) * 64;
-    auto f16r = [](uint32_t r) { return __half2float(__float2half_rn(__uint_as_float(r))); };
-    for (int c0 = cbeg; c0 < cend && n0 + c0 < N; c0 += 128) {
-      const int col = n0 + c0;
-      const uint32_t t0 = tmem_addr(tmem_base, quarter * 32, acc_col + c0);
-      const bool qk = col < R->qk_cols;
-      const float* w = col < R->q_cols ? R->wq : R->wk;
-      float inv = 0.0f;
-      if (qk) {
-        // partial i: columns 4i..4i+3 and 64+4i..64+4i+3; t8[i] = sp[i] + sp[i+8]
-        float sp[8], t8[8];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          uint32_t ra[4], rb[4];
-          tmem_ld4(t0 + 4 * i, ra);
-          tmem_ld4(t0 + 64 + 4 * i, rb);
-          tmem_wait_ld();
-          float s = 0.0f;
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float a = f16r(ra[e]), b = f16r(rb[e]);
-            s = __fadd_rn(s, __fadd_rn(__fmul_rn(a, a), __fmul_rn(b, b)));
-          }
-          if (i < 8) sp[i] = s;
-          else t8[i - 8] = __fadd_rn(sp[i - 8], s);
-        }
-        float u4[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) u4[i] = __fadd_rn(t8[i], t8[i + 4]);
-        const float ss = __fadd_rn(__fadd_rn(u4[0], u4[2]), __fadd_rn(u4[1], u4[3]));
-        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(ss, 0.0078125f), R->eps)));
-      }
-      for (int half = 0; half < 2; ++half) {  // output columns col + 64*half .. +63
-        if (lane == 0) bulk_wait_read<NBUF - 1>();
-        __syncwarp();
-        uint8_t* b = ebuf + buf * kEpiBufBytes + lane * 128;
-#pragma unroll 1
-        for (int g = 0; g < 8; ++g) {  // output columns 8g..8g+7 of this half: one 16-byte unit
-          uint32_t pk[4];
-#pragma unroll
-          for (int q4 = 0; q4 < 2; ++q4) {
-            const int i0 = 8 * g + 4 * q4;
-            uint32_t ra[4], rb[4];
-            float o[4];
-            if (qk) {
-              tmem_ld4(t0 + i0, ra);
-              tmem_ld4(t0 + 64 + i0, rb);
-              tmem_wait_ld();
-              const float4 c4 = __ldg(reinterpret_cast<const float4*>(cs + i0));
-              const float4 s4 = __ldg(reinterpret_cast<const float4*>(sn + i0));
-              const float4 wa4 = __ldg(reinterpret_cast<const float4*>(w + i0));
-              const float4 wb4 = __ldg(reinterpret_cast<const float4*>(w + 64 + i0));
-              const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
-              const float wa[4] = {wa4.x, wa4.y, wa4.z, wa4.w}, wb[4] = {wb4.x, wb4.y, wb4.z, wb4.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float a0 = __fmul_rn(__fmul_rn(f16r(ra[e]), inv), wa[e]);
-                const float b0 = __fmul_rn(__fmul_rn(f16r(rb[e]), inv), wb[e]);
-                o[e] = half == 0 ? __fsub_rn(__fmul_rn(a0, cc[e]), __fmul_rn(b0, sv[e]))
-                                 : __fadd_rn(__fmul_rn(b0, cc[e]), __fmul_rn(a0, sv[e]));
-              }
-            } else {
-              tmem_ld4(t0 + 64 * half + i0, ra);
-              tmem_wait_ld();
-#pragma unroll
-              for (int e = 0; e < 4; ++e) o[e] = __uint_as_float(ra[e]);
-            }
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              __half2 h2 = __floats2half2_rn(o[2 * e], o[2 * e + 1]);
-              pk[2 * q4 + e] = *reinterpret_cast<uint32_t*>(&h2);
-            }
-          }
-          *reinterpret_cast<uint4*>(b + ((g ^ (lane & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(tmC, ebuf + buf * kEpiBufBytes, col + 64 * half, m0 + quarter * 32);
-          bulk_commit();
-        }
-        if (NBUF == 2) buf ^= 1;
-      }
-    }
-    return;
-  }
   }
   if (tma_store || vec_store) {
     if (rows_live) {

@@ -257,13 +257,11 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   } else if (warp >= kEpiWarp0 && warp < kEpiWarp0 + Cfg::EPI_WARPS) {
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    const EpiParams ep{args.s_col, args.out_dtype, args.out_scale, args.out_inv, args.rope};
+    const EpiParams ep{args.s_col, args.out_dtype, args.out_scale, args.out_inv};
     uint8_t* ebuf = smem + Cfg::EPI_OFF + (warp - kEpiWarp0) * Cfg::EPI_BUFS * kEpiBufBytes;
     constexpr int kColSplit = Cfg::EPI_WARPS / 4;  // warps sharing a TMEM lane quarter
     const int cbeg = ((warp - kEpiWarp0) >> 2) * (BN / kColSplit), cend = cbeg + BN / kColSplit;
-    const int mode = args.gated           ? kEpiSiluF16
-                     : args.rope != nullptr ? kEpiQkRopeF16
-                                            : epi_mode(Cfg::I8, args.out_dtype, args.out_scale, args.act);
+    const int mode = args.gated ? kEpiSiluF16 : epi_mode(Cfg::I8, args.out_dtype, args.out_scale, args.act);
     int buf = 0;
     int local = 0;
     for (int t = pair; t < num_tiles; t += npairs, ++local) {

@@ -287,8 +287,7 @@ __global__ void gelu_f16_kernel(__half* y, int64_t count8) {
 // lane i of the 16 owns elements 4i..4i+3 and 64+4i..64+4i+3 (the rotate-half
 // pairs), read and written as 8-byte vectors; the head's sum of squares is
 // reduced over the 16 lanes. Every operation is an explicitly rounded f32
-// intrinsic, so the GEMM epilogue that fuses this pass (kEpiQkRopeF16)
-// reproduces it bit for bit.
+// intrinsic, so the result does not depend on the compiler's contraction.
 __global__ void qk_norm_rope_kernel(__half* qkv, int64_t ld, int64_t tokens, int hq, int hk,
                                     const float* wq, const float* wk, float eps,
                                     const float* cos_t, const float* sin_t, int seq) {

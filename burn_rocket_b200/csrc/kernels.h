@@ -13,20 +13,6 @@
 
 namespace rb {
 
-// q/k RMSNorm + RoPE applied to a matmul's f16 output, heads of 128 columns
-// (qk_norm_rope_kernel's operation): columns [0, q_cols) are query heads
-// normalised with wq, [q_cols, qk_cols) key heads with wk, the rest (value
-// heads) are left as they are; a row's position is its index modulo seq.
-struct QkRope {
-  const float* wq;
-  const float* wk;
-  const float* cos_t;  // [seq, 64]
-  const float* sin_t;  // [seq, 64]
-  float eps;
-  int seq;
-  int q_cols, qk_cols;
-};
-
 struct GemmLaunch {
   int M, N, K;
   const int8_t* w_codes;  // Q8_0 codes [N, K]
@@ -40,7 +26,6 @@ struct GemmLaunch {
   const int* tile_expert; // grouped GEMM table (one expert id per 128 rows), or nullptr
   int gated;              // gate/up interleaved in 32-row blocks: out = silu(gate) * up, N/2 f16 columns
   int act;                // RB_ACT_*: element-wise activation before the f16 output rounding
-  const QkRope* rope;     // device copy: q/k RMSNorm + RoPE of the f16 output, or nullptr
   uint32_t* err;
   int num_sms;
 };

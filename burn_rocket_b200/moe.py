@@ -30,7 +30,7 @@ from dataclasses import dataclass
 import numpy as np
 
 from . import _lib
-from . import _check, _dev_ptr, _stream_ptr, WeightId, matmul, pack_gated_q8_0, set_weight_qk_norm_rope
+from . import _check, _dev_ptr, _stream_ptr, WeightId, matmul, pack_gated_q8_0
 from ._lib import DTYPE_F16, DTYPE_F32, MASK_CAUSAL
 from .qwen3 import rope_tables
 
@@ -62,14 +62,9 @@ class MoeModel:
     """Resident random-init model (Q8_0 linears) + preallocated activations
     for `batch` sequences of `seq` tokens on the current CUDA device."""
 
-    def __init__(self, cfg: MoeConfig, batch: int, seq: int, seed: int = 0, host_weights: dict | None = None,
-                 fuse_qk_rope: bool = False):
+    def __init__(self, cfg: MoeConfig, batch: int, seq: int, seed: int = 0, host_weights: dict | None = None):
         import torch
         self.cfg, self.batch, self.seq = cfg, batch, seq
-        # fuse_qk_rope: q/k RMSNorm + RoPE in the qkv GEMM's epilogue
-        # (bit-identical to the separate rb_qk_norm_rope pass, but slower on
-        # B200 at these shapes, so off by default)
-        self.fuse_qk_rope = fuse_qk_rope
         dev = torch.device("cuda", torch.cuda.current_device())
         self.dev = dev
         T = batch * seq
@@ -132,10 +127,6 @@ class MoeModel:
         cos, sin = rope_tables(seq, d, cfg.theta)
         self.cos = torch.from_numpy(cos).to(dev)
         self.sin = torch.from_numpy(sin).to(dev)
-        if fuse_qk_rope:
-            for layer in self.layers:
-                set_weight_qk_norm_rope(layer["qkv"], cfg.heads, cfg.kv_heads, layer["q_norm"], layer["k_norm"],
-                                        cfg.eps, self.cos, self.sin, seq)
         torch.cuda.synchronize()
         f16 = torch.float16
         self.max_rows = int(lib.rb_moe_max_rows(T, cfg.top_k, E))
@@ -169,11 +160,10 @@ class MoeModel:
         qkv_p, xp, ws = _dev_ptr(self.qkv), _dev_ptr(self.x), _dev_ptr(self.ws)
         _check(lib.rb_add_rms_norm(xp, None, _dev_ptr(L["in_norm"]), cfg.eps, _dev_ptr(self.h), T, h, st),
                "add_rms_norm")
-        matmul(self.h, L["qkv"], out=self.qkv, stream=stream)  # q/k norm + RoPE fused when fuse_qk_rope
-        if not self.fuse_qk_rope:
-            _check(lib.rb_qk_norm_rope(qkv_p, ld, T, nh, nkv, d, _dev_ptr(L["q_norm"]), _dev_ptr(L["k_norm"]),
-                                       cfg.eps, _dev_ptr(self.cos), _dev_ptr(self.sin), self.seq, st),
-                   "qk_norm_rope")
+        matmul(self.h, L["qkv"], out=self.qkv, stream=stream)
+        _check(lib.rb_qk_norm_rope(qkv_p, ld, T, nh, nkv, d, _dev_ptr(L["q_norm"]), _dev_ptr(L["k_norm"]),
+                                   cfg.eps, _dev_ptr(self.cos), _dev_ptr(self.sin), self.seq, st),
+               "qk_norm_rope")
         _check(lib.rb_attention_batched(qkv_p, ld, qkv_p + nh * d * 2, ld, qkv_p + (nh + nkv) * d * 2, ld,
                                         _dev_ptr(self.attn), nh * d, DTYPE_F16, self.batch, self.seq, self.seq,
                                         nh, nkv, d, 1.0 / math.sqrt(d), 0.0, MASK_CAUSAL, -1, 0, 0, st),

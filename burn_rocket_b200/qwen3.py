@@ -29,7 +29,7 @@ from dataclasses import dataclass
 import numpy as np
 
 from . import _lib
-from . import _check, _dev_ptr, _stream_ptr, WeightId, matmul, pack_gated_q8_0, set_weight_qk_norm_rope
+from . import _check, _dev_ptr, _stream_ptr, WeightId, matmul, pack_gated_q8_0
 from ._lib import DTYPE_F16, MASK_CAUSAL, MASK_NONE
 
 
@@ -70,13 +70,9 @@ class Qwen3Embedding:
     `batch` sequences of `seq` tokens on the current CUDA device."""
 
     def __init__(self, cfg: Qwen3Config, batch: int, seq: int, seed: int = 0, causal: bool = False,
-                 host_weights: dict | None = None, norm_ones: bool = True, fuse_qk_rope: bool = False):
+                 host_weights: dict | None = None, norm_ones: bool = True):
         import torch
         self.cfg, self.batch, self.seq, self.causal = cfg, batch, seq, causal
-        # fuse_qk_rope: q/k RMSNorm + RoPE in the qkv GEMM's epilogue
-        # (bit-identical to the separate rb_qk_norm_rope pass, but slower on
-        # B200 at these shapes, so off by default)
-        self.fuse_qk_rope = fuse_qk_rope
         dev = torch.device("cuda", torch.cuda.current_device())
         self.dev = dev
         T = batch * seq
@@ -127,10 +123,6 @@ class Qwen3Embedding:
         cos, sin = rope_tables(seq, hd, cfg.theta)
         self.cos = torch.from_numpy(cos).to(dev)
         self.sin = torch.from_numpy(sin).to(dev)
-        if fuse_qk_rope:
-            for layer in self.layers:
-                set_weight_qk_norm_rope(layer["qkv"], nh, nkv, layer["q_norm"], layer["k_norm"], cfg.eps,
-                                        self.cos, self.sin, seq)
         torch.cuda.synchronize()
         # activations
         f16 = torch.float16
@@ -158,11 +150,10 @@ class Qwen3Embedding:
         qkv_p = _dev_ptr(self.qkv)
         _check(lib.rb_add_rms_norm(_dev_ptr(self.x), delta, _dev_ptr(L["in_norm"]), cfg.eps, _dev_ptr(self.h),
                                    T, h, st), "add_rms_norm")
-        matmul(self.h, L["qkv"], out=self.qkv, stream=stream)  # q/k norm + RoPE fused when fuse_qk_rope
-        if not self.fuse_qk_rope:
-            _check(lib.rb_qk_norm_rope(qkv_p, ld, T, nh, nkv, hd, _dev_ptr(L["q_norm"]), _dev_ptr(L["k_norm"]),
-                                       cfg.eps, _dev_ptr(self.cos), _dev_ptr(self.sin), self.seq, st),
-                   "qk_norm_rope")
+        matmul(self.h, L["qkv"], out=self.qkv, stream=stream)
+        _check(lib.rb_qk_norm_rope(qkv_p, ld, T, nh, nkv, hd, _dev_ptr(L["q_norm"]), _dev_ptr(L["k_norm"]),
+                                   cfg.eps, _dev_ptr(self.cos), _dev_ptr(self.sin), self.seq, st),
+               "qk_norm_rope")
         _check(lib.rb_attention_batched(qkv_p, ld, qkv_p + nh * hd * 2, ld, qkv_p + (nh + nkv) * hd * 2, ld,
                                         _dev_ptr(self.attn), nh * hd, DTYPE_F16, self.batch, self.seq, self.seq,
                                         nh, nkv, hd, 1.0 / math.sqrt(hd), 0.0,

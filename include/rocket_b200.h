@@ -113,10 +113,6 @@ RB_API int64_t rb_pack_w8a8(const int8_t* codes_host, const float* w_scale_host,
 RB_API int64_t rb_pack_f32_w8a8_device(const float* w_dev, int64_t n, int64_t k, float in_scale,
                                        float out_scale);
 
-/* fp16-resident weight (rocket_pack / pack2 / pack3, ext.rs:829-934): host parts
- * [n_parts[i], k] of dtype src_dtype (RB_DTYPE_F32 / F16 / BF16) concatenated
- * along N and rounded to f16 (RNE); rb_matmul is then f16 x f16 with f32
- * accumulation. K % 8 == 0. */
 /* W8A8 matmul on activations already quantised per row (int8 codes [m, k],
  * f32 scales [m], e.g. from rb_quantize_rows_i8 or rb_add_layer_norm_quant):
  * the same product and epilogue as rb_matmul without the quantiser pass.
@@ -138,18 +134,6 @@ RB_API int rb_add_layer_norm_quant(float* x, const void* delta_f16, const float*
 #define RB_ACT_NONE 0
 #define RB_ACT_GELU_TANH 1
 RB_API int rb_set_weight_activation(int64_t id, int act);
-/* q/k RMSNorm + RoPE fused into later matmuls on Q8_0 weight `id`, whose
- * output columns are [n_q_heads query heads | n_k_heads key heads | the rest]
- * in heads of 128 (the fused q|k|v projection; the GEMM-epilogue form of the
- * rb_qk_norm_rope glue, model.rs:369-376): each later rb_matmul writes the
- * same f16 values rb_qk_norm_rope would give on the plain product, in the
- * same pass. wq / wk [128], cos_t / sin_t [seq, 64] are f32 device arrays
- * read by those later calls (they must stay allocated); a row's position is
- * its index modulo seq. The output must be f16 and its column count a
- * multiple of 128. n_q_heads = n_k_heads = 0 turns the fusion off. Returns
- * RB_OK or RB_E_SHAPE. */
-RB_API int rb_set_weight_qk_norm_rope(int64_t id, int n_q_heads, int n_k_heads, const float* wq, const float* wk,
-                                      float eps, const float* cos_t, const float* sin_t, int seq);
 
 /* Gated (SwiGLU) Q8_0 weight from device-resident f32 gate and up weights,
  * each [n_inter, k] (n_inter a multiple of 64): rows are stored interleaved in
@@ -160,6 +144,10 @@ RB_API int rb_set_weight_qk_norm_rope(int64_t id, int n_q_heads, int n_k_heads, 
  * SwiGLU MLP in one kernel (host.rs:31-38). rb_weight_info reports n_inter. */
 RB_API int64_t rb_pack_f32_q8_0_gated_device(const float* gate_dev, const float* up_dev, int64_t n_inter, int64_t k);
 
+/* fp16-resident weight (rocket_pack / pack2 / pack3, ext.rs:829-934): host parts
+ * [n_parts[i], k] of dtype src_dtype (RB_DTYPE_F32 / F16 / BF16) concatenated
+ * along N and rounded to f16 (RNE); rb_matmul is then f16 x f16 with f32
+ * accumulation. K % 8 == 0. */
 RB_API int64_t rb_pack_f16(const void* const* parts_host, const int64_t* n_parts, int num_parts, int64_t k,
                            int src_dtype);
 

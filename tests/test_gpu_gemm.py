@@ -396,86 +396,3 @@ def test_q8_0_fused_gelu_and_contract(rb, orc):
     with pytest.raises(Exception):  # fused activations write f16 only
         rb.matmul(torch.from_numpy(x).cuda(), wid, out=torch.empty(m, n, device="cuda"))
     rb.check_device_errors()
-
-
-# ------------------------------------------------------------------ fused q/k RMSNorm + RoPE epilogue
-
-@pytest.mark.parametrize("policy", ["auto", "single", "pair"])
-@pytest.mark.parametrize("m,seq,hq,hk,k", [(1, 1, 2, 1, 64), (300, 100, 4, 2, 256), (1024, 512, 16, 8, 1024),
-                                          (513, 64, 2, 2, 128)])
-def test_qk_norm_rope_epilogue_bit_exact(rb, orc, tile_policy, policy, m, seq, hq, hk, k):
-    """A q|k|v Q8_0 matmul with set_weight_qk_norm_rope equals the plain matmul
-    followed by rb_qk_norm_rope (model.rs:369-376), bit for bit, on ragged M,
-    positions restarting every `seq` rows; both match a float64 restatement."""
-    import torch
-    import burn_rocket_b200._lib as L
-    from burn_rocket_b200.qwen3 import rope_tables
-    tile_policy(policy)
-    rng = np.random.default_rng(m + seq + hq + k)
-    n = (hq + 2 * hk) * 128
-    w = (rng.standard_normal((n, k)) * 0.05).astype(np.float32)
-    x = rng.standard_normal((m, k)).astype(np.float32)
-    wq = (1.0 + 0.1 * rng.standard_normal(128)).astype(np.float32)
-    wk = (1.0 + 0.1 * rng.standard_normal(128)).astype(np.float32)
-    cos, sin = rope_tables(seq, 128, 1e6)
-    eps = 1e-6
-    wid = rb.pack_q8_0(torch.from_numpy(w))
-    xd = torch.from_numpy(x).cuda().half()
-    wqd, wkd = torch.from_numpy(wq).cuda(), torch.from_numpy(wk).cuda()
-    cosd, sind = torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda()
-    lib = L.load()
-    # the plain matmul, then the separate pass in place
-    y_ref = torch.empty(m, n, dtype=torch.float16, device="cuda")
-    rb.matmul(xd, wid, out=y_ref)
-    assert lib.rb_qk_norm_rope(y_ref.data_ptr(), n, m, hq, hk, 128, wqd.data_ptr(), wkd.data_ptr(), eps,
-                               cosd.data_ptr(), sind.data_ptr(), seq, None) == 0, L.last_error()
-    # fused into the matmul epilogue
-    rb.set_weight_qk_norm_rope(wid, hq, hk, wqd, wkd, eps, cosd, sind, seq)
-    y = torch.empty(m, n, dtype=torch.float16, device="cuda")
-    rb.matmul(xd, wid, out=y)
-    torch.cuda.synchronize()
-    rb.check_device_errors()
-    assert torch.equal(y.view(torch.int16), y_ref.view(torch.int16))
-    # float64 restatement of the pass on the f16-rounded product
-    p = orc.f16_bits_to_f32(orc.f32_to_f16_bits(x)).astype(np.float64) @ \
-        orc.q8_0_dequant(*orc.q8_0_quantize(w)).astype(np.float64).T
-    p = orc.f16_bits_to_f32(orc.f32_to_f16_bits(p.astype(np.float32))).astype(np.float64)
-    want = p.copy()
-    pos = np.arange(m) % seq
-    c, s = cos[pos].astype(np.float64), sin[pos].astype(np.float64)
-    for h in range(hq + hk):
-        v = p[:, h * 128:(h + 1) * 128]
-        g = (wq if h < hq else wk).astype(np.float64)
-        v = v / np.sqrt((v * v).mean(axis=1, keepdims=True) + eps) * g
-        a, b = v[:, :64], v[:, 64:]
-        want[:, h * 128:h * 128 + 64] = a * c - b * s
-        want[:, h * 128 + 64:(h + 1) * 128] = b * c + a * s
-    got = y.float().cpu().numpy().astype(np.float64)
-    assert np.abs(got - want).max() <= 1e-2 * max(1.0, np.abs(want).max())
-    # off again: the plain product
-    rb.set_weight_qk_norm_rope(wid, 0, 0, wqd, wkd, eps, cosd, sind, seq)
-    y2 = torch.empty(m, n, dtype=torch.float16, device="cuda")
-    rb.matmul(xd, wid, out=y2)
-    y_plain = torch.empty(m, n, dtype=torch.float16, device="cuda")
-    rb.matmul(xd, wid, out=y_plain)
-    torch.cuda.synchronize()
-    assert torch.equal(y2.view(torch.int16), y_plain.view(torch.int16))
-    assert not torch.equal(y2.view(torch.int16), y.view(torch.int16))
-
-
-def test_qk_norm_rope_epilogue_contract(rb):
-    import torch
-    import burn_rocket_b200._lib as L
-    lib = L.load()
-    wq, cs = torch.ones(128, device="cuda"), torch.ones(8, 64, device="cuda")
-    wid = rb.pack_q8_0(torch.zeros(4 * 128, 64))
-    assert lib.rb_set_weight_qk_norm_rope(wid.id, 3, 2, wq.data_ptr(), wq.data_ptr(), 1e-6,
-                                          cs.data_ptr(), cs.data_ptr(), 8) != 0  # 5 heads > 4
-    assert lib.rb_set_weight_qk_norm_rope(wid.id, 2, 1, None, None, 1e-6, None, None, 8) != 0  # null tables
-    rb.set_weight_qk_norm_rope(wid, 2, 1, wq, wq, 1e-6, cs, cs, 8)
-    with pytest.raises(Exception):  # the fused output is f16 only
-        rb.matmul(torch.zeros(4, 64, device="cuda"), wid, out=torch.empty(4, 4 * 128, device="cuda"))
-    assert lib.rb_set_weight_activation(wid.id, 1) != 0  # no activation on top
-    gid = rb.pack_gated_q8_0(torch.zeros(128, 64), torch.zeros(128, 64))
-    assert lib.rb_set_weight_qk_norm_rope(gid.id, 1, 0, wq.data_ptr(), wq.data_ptr(), 1e-6, cs.data_ptr(),
-                                          cs.data_ptr(), 8) != 0  # not on a gated weight
