@@ -5,8 +5,11 @@
 
 BASELINE.json's metric has three items: "Q8_0/W8A8 GEMM TFLOP/s; GQA attn
 TFLOP/s; Qwen3-Emb-0.6B prefill tok/s". The default line is the model item,
-config #3, and at N = 1 it carries one sub-record per single-op item (key
-"sub"), each timed alone with its own ms_per_step, roofline and e2e.
+config #3, and it carries sub-records (key "sub"), each with its own
+ms_per_step, roofline and e2e: config #4's W8A8 tower data-parallel over the
+same N GPUs (every N), and at N = 1 one record per single-op item (config #1
+Q8_0 GEMM, config #2 attention, config #4's W8A8 projections), each timed
+alone.
 
 Workloads (synthetic seeded data of the named shapes):
   qwen3   config #3 (default): Qwen3-Embedding-0.6B-architecture forward, 28
@@ -812,6 +815,33 @@ def measure_sub(name, dev, flush, stream, args, peaks, peak_kind, orc):
     return rec
 
 
+def measure_dp_sub(name, dev, flush, stream, args, peaks, peak_kind, world, rank, barrier, reduce_max):
+    """A data-parallel model sub-record (config #4's tower over 16/N images per
+    rank), timed like the main line: max over ranks, aggregate value."""
+    import torch
+    W = WORKLOADS[name]
+    wl = W(dev, seed=0x5EED, world=world, rank=rank)
+    steps = DEFAULT_STEPS[name]
+    ms, launches, graphed, clocks = time_device(wl, steps, args.warmup, flush, stream, not args.no_graph,
+                                                barrier, dev.index)
+    ms_max = reduce_max(ms)
+    value = wl.units * world * steps / (ms_max / 1e3)
+    e2e_steps = 3
+    e2e_s, h2d, d2h = time_e2e(wl, e2e_steps, barrier)
+    e2e_value = wl.units * world * e2e_steps / reduce_max(e2e_s)
+    rec = {"workload": config_dict(name, world)["workload"], "metric": W.metric, "value": round(value, 3),
+           "unit": W.unit, "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms_max / steps, 4),
+           "scaling": "strong", "parallelism": config_dict(name, world)["parallelism"], "dtype": DTYPES[name],
+           "roofline": roofline_of(wl, ms_max / steps, peaks, peak_kind),
+           "e2e": {"value": round(e2e_value, 3), "unit": W.unit, "h2d_bytes_per_step": int(h2d),
+                   "d2h_bytes_per_step": int(d2h)},
+           "gpu_launches": int(launches), "clocks": clocks,
+           "timing": "CUDA-graph replay of the step's C-ABI calls" if graphed else "eager launches"}
+    del wl
+    torch.cuda.empty_cache()
+    return rec
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
@@ -877,12 +907,23 @@ def run_b200(args):
         from oracle import oracle as orc
         orc.use_all_host_cores()
         line["cpu_baseline"] = cpu_baseline_of(W, orc)
-    if world == 1 and args.workload == "qwen3" and not args.no_sub:
-        # the metric's other items, each timed alone on this GPU
+    if args.workload == "qwen3" and not args.no_sub:
         del wl
         torch.cuda.empty_cache()
-        line["sub"] = {name: measure_sub(name, dev, flush, stream, args, peaks, peak_kind, orc)
-                       for name in SUB_WORKLOADS}
+
+        def reduce_max(v):
+            t = torch.tensor([v], dtype=torch.float64, device=dev)
+            if world > 1:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+
+        # config #4's tower, data-parallel over images like the main line (every N)
+        line["sub"] = {"siglip": measure_dp_sub("siglip", dev, flush, stream, args, peaks, peak_kind, world, rank,
+                                                barrier, reduce_max)}
+        if world == 1:
+            # the metric's single-op items, each timed alone on this GPU
+            for name in SUB_WORKLOADS:
+                line["sub"][name] = measure_sub(name, dev, flush, stream, args, peaks, peak_kind, orc)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
