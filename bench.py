@@ -361,6 +361,48 @@ class W8A8Workload:
         return flops / t / 1e12, f"{rows} of {W8A8Workload.M} rows of each projection (quantise + int GEMM + epilogue)"
 
 
+class W8A8GroupWorkload(W8A8Workload):
+    """Config #4's projections with group-wise int8 weights and activations
+    (rocket_pack_i8 / matmul_i8, g = 128, the Clef experts' group): the group
+    quantiser and one GEMM with in-kernel group promotion per projection."""
+    name = "w8a8g"
+    GROUP = 128
+    metric = "group-wise int8 GEMM TOP/s (g128; config #4 projections over 16 x 2394 patches, f16 in/out)"
+
+    def __init__(self, dev, seed):
+        import torch
+        import burn_rocket_b200 as rb
+        self.rb = rb
+        rng = np.random.default_rng(seed)
+        self.ws, self.xs, self.ys = [], [], []
+        for n, k in self.SHAPES:
+            w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+            self.ws.append(rb.pack_i8(w, self.GROUP))
+            self.xs.append(torch.randn(self.M, k, device=dev).half())
+            self.ys.append(torch.empty(self.M, n, dtype=torch.float16, device=dev))
+        self.flops = sum(2.0 * self.M * n * k for n, k in self.SHAPES)
+        self.hx = [x.cpu().pin_memory() for x in self.xs]
+        self.hy = [y.cpu().pin_memory() for y in self.ys]
+
+    def kernel_launches(self):
+        return [(f"i8g gemm N={n} K={k} (+ group quantiser)", 2.0 * self.M * n * k) for n, k in self.SHAPES]
+
+    @staticmethod
+    def cpu_sample(orc, seed, timed_repeats=1):
+        rng = np.random.default_rng(seed)
+        rows, g = 256, W8A8GroupWorkload.GROUP
+        flops, t = 0.0, 0.0
+        for n, k in W8A8Workload.SHAPES:
+            x = rng.standard_normal((rows, k)).astype(np.float32)
+            wq, ws = orc.quantize_rows_groups((rng.standard_normal((n, k)) * 0.02).astype(np.float32), g)
+            t0 = time.perf_counter()
+            q, s = orc.quantize_rows_groups(x, g)
+            orc.matmul_gw(q, s, wq, ws, g)
+            t += time.perf_counter() - t0
+            flops += 2.0 * rows * n * k
+        return flops / t / 1e12, f"{rows} of {W8A8Workload.M} rows of each projection (group quantise + int GEMM + promotion)"
+
+
 class Qwen3Workload:
     """Config #3: Qwen3-Embedding-0.6B-architecture forward, 64 sequences x 512
     tokens bidirectional, data-parallel over sequences (64/N per GPU)."""
@@ -664,8 +706,8 @@ class MoeWorkload:
             "attention over 512 tokens; scaled to 48 layers and 2048-token sequences")
 
 
-WORKLOADS = {w.name: w for w in (AttnWorkload, Q8GemmWorkload, W8A8Workload, Qwen3Workload, SiglipWorkload,
-                                 MoeWorkload)}
+WORKLOADS = {w.name: w for w in (AttnWorkload, Q8GemmWorkload, W8A8Workload, W8A8GroupWorkload, Qwen3Workload,
+                                 SiglipWorkload, MoeWorkload)}
 DP_WORKLOADS = ("qwen3", "siglip", "moe")
 
 
@@ -683,6 +725,7 @@ def config_dict(name, world):
     """The `config` object of a workload's line; both arms print the same one."""
     return {"workload": {"attn": "configs[1] GQA attention", "q8gemm": "configs[0] Q8_0 GEMM",
                          "w8a8": "configs[3] W8A8 projections",
+                         "w8a8g": "configs[3] projections, group-wise int8 g128",
                          "qwen3": "configs[2] Qwen3-Embedding-0.6B arch, 28 layers, 64x512 tokens",
                          "siglip": "configs[3] SigLIP-style W8A8 tower, 27 layers, 16x2394 patches",
                          "moe": "configs[4] Qwen3-30B-A3B-style MoE, 48 layers, 4x2048 tokens"}[name],
@@ -696,11 +739,11 @@ def config_dict(name, world):
                             else (f"replicas x{world}" if world > 1 else "single GPU"))}
 
 
-DTYPES = {"attn": "f16", "q8gemm": "f16xq8_0->f32", "w8a8": "s8", "qwen3": "f16xq8_0 (f32 residual)",
+DTYPES = {"attn": "f16", "q8gemm": "f16xq8_0->f32", "w8a8": "s8", "w8a8g": "s8 (group-wise, g128)", "qwen3": "f16xq8_0 (f32 residual)",
           "siglip": "s8 linears, f16 attention (f32 residual)", "moe": "f16xq8_0 (f32 residual, f32 router)"}
-DEFAULT_STEPS = {"attn": 200, "q8gemm": 2000, "w8a8": 60, "qwen3": 20, "siglip": 5, "moe": 3}
+DEFAULT_STEPS = {"attn": 200, "q8gemm": 2000, "w8a8": 60, "w8a8g": 30, "qwen3": 20, "siglip": 5, "moe": 3}
 # configs[0], [1] and [3]'s projections: measured beside the default (config #3) line at N = 1
-SUB_WORKLOADS = ("q8gemm", "attn", "w8a8")
+SUB_WORKLOADS = ("q8gemm", "attn", "w8a8", "w8a8g")
 
 
 def time_device(wl, steps, warmup, flush, stream, use_graph, barrier, local):
@@ -766,7 +809,7 @@ def roofline_of(wl, ms_per_step, peaks, peak_kind):
     clock, so against the sustained peak); the single ops use the whole step
     against the burst peak."""
     kr = wl.kernel_roofline() if hasattr(wl, "kernel_roofline") else None
-    int8 = wl.name in ("w8a8", "siglip")
+    int8 = wl.name in ("w8a8", "w8a8g", "siglip")
     if kr is not None:
         kname, achieved, kms = kr
         peak = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))

@@ -131,6 +131,8 @@ struct Weight {
   int64_t pitch = 0;         // Q8_0 scale row pitch: round_up(n, 8)
   float in_scale = 0.0f, out_scale = 0.0f;
   int64_t group = 0;         // RB_WEIGHT_I8G: K group width (scales f32 [n, k/group])
+  float* scales_t = nullptr; // RB_WEIGHT_I8G: the scales group-major [k/group, ldb], zero past n
+  int64_t ldb = 0;           // RB_WEIGHT_I8G: round_up(n, 128)
   bool gated = false;        // gate|up interleaved in 32-row blocks: matmul gives silu(gate)*up, n/2 columns
   int act = RB_ACT_NONE;     // element-wise activation fused into the matmul epilogue
   // TMA maps per staged weight-tile height ({256, 128, 96, 64}, see
@@ -363,46 +365,27 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
     return RB_OK;
   }
   if (w.kind == RB_WEIGHT_I8G) {
-    // Group-wise int8: per group, the int8 GEMM of the K slice gives exact
-    // int32 partials, folded into the f32 result in group order.
+    // Group-wise int8: the activation group quantiser, then one GEMM whose
+    // fold warps promote each group's exact int32 partial into the f32 result
+    // in group order (no partial leaves the SM).
     const int64_t G = w.group, ng = k / G;
     const size_t codes_bytes = (static_cast<size_t>(m) * k + 255) & ~size_t(255);
-    const size_t part_bytes = (static_cast<size_t>(m) * w.n * 4 + 255) & ~size_t(255);
-    const size_t acc_bytes = y_dtype == RB_DTYPE_F32 ? 0 : static_cast<size_t>(m) * w.n * 4;
-    if ((rc = e->act.grow(codes_bytes + part_bytes + acc_bytes, "int8 group staging")) != RB_OK) return rc;
+    if ((rc = e->act.grow(codes_bytes, "int8 group activation codes")) != RB_OK) return rc;
     if ((rc = e->rowscale.grow(static_cast<size_t>(m) * ng * 4, "int8 group scales")) != RB_OK) return rc;
     int8_t* codes = reinterpret_cast<int8_t*>(e->act.ptr);
-    int32_t* part = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(e->act.ptr) + codes_bytes);
-    float* acc = y_dtype == RB_DTYPE_F32
-                     ? reinterpret_cast<float*>(y)
-                     : reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(e->act.ptr) + codes_bytes + part_bytes);
     float* a_s = reinterpret_cast<float*>(e->rowscale.ptr);
     if ((rc = launch_quantize_groups(x, x_dtype, m, k, static_cast<int>(G), codes, a_s, st)) != RB_OK)
       return fail(rc, "group quantiser launch failed");
     g_launches++;
-    L.K = static_cast<int>(G);
-    L.out = part;
-    L.out_dtype = RB_DTYPE_I32;
-    L.ldo = static_cast<int>(w.n);
-    const GemmPlan plan{w.n % 256 == 0 ? 256 : 128, 1, false};
-    CUtensorMap tmC;
-    const bool tstore = output_map(&tmC, part, RB_DTYPE_I32, m, w.n);
-    for (int64_t g = 0; g < ng; ++g) {
-      CUtensorMap tmA, tmB;  // the group's K slice of both operands
-      if ((rc = make_tmap_2d(&tmA, codes + g * G, 1, m, G, k, 128, 128, 128)) != RB_OK) return rc;
-      if ((rc = make_tmap_2d(&tmB, w.codes + g * G, 1, w.n, G, k, 128, plan.weight_rows(), 128)) != RB_OK)
-        return rc;
-      if ((rc = launch_w8a8_gemm(L, plan, tmA, tmB, tstore ? &tmC : nullptr, st)) != RB_OK)
-        return fail(rc, "int8 group gemm launch failed");
-      if ((rc = launch_group_fold(part, m, w.n, a_s, reinterpret_cast<const float*>(w.scales), ng, g, g == 0, acc,
-                                  st)) != RB_OK)
-        return fail(rc, "group fold launch failed");
-      g_launches += 2;
-    }
-    if (y_dtype != RB_DTYPE_F32) {
-      if ((rc = launch_cast(acc, RB_DTYPE_F32, y, y_dtype, m * w.n, st)) != RB_OK) return fail(rc, "output cast");
-      g_launches++;
-    }
+    CUtensorMap tmA, tmB, tmC;
+    if ((rc = make_tmap_2d(&tmA, codes, 1, m, k, k, 128, 128, 128)) != RB_OK) return rc;
+    if ((rc = make_tmap_2d(&tmB, w.codes, 1, w.n, k, k, 128, 128, 128)) != RB_OK) return rc;
+    const bool tstore = output_map(&tmC, y, y_dtype, m, w.n);
+    if ((rc = launch_i8g_gemm(static_cast<int>(m), static_cast<int>(w.n), static_cast<int>(k), static_cast<int>(G),
+                              a_s, w.scales_t, static_cast<int>(w.ldb), y, y_dtype, tmA, tmB,
+                              tstore ? &tmC : nullptr, e->err, e->num_sms, st)) != RB_OK)
+      return fail(rc, "int8 group gemm launch failed");
+    g_launches++;
     return RB_OK;
   }
   if (w.kind == RB_WEIGHT_W8A8) {
@@ -895,7 +878,23 @@ int64_t rb_pack_i8(const float* w_host, int64_t n, int64_t k, int64_t group) {
   const cudaError_t ce = cudaDeviceSynchronize();
   cudaFree(tmp);
   if (rc != RB_OK || ce != cudaSuccess) return fail(RB_E_DEVICE, "int8 group quantiser failed");
-  w.bytes = static_cast<size_t>(n) * k + static_cast<size_t>(n) * ng * 4;
+  // Group-major copy of the scales for the GEMM's fold warps (one 16-byte
+  // load gives four columns' scales of a group), zero-padded to whole tiles.
+  w.ldb = (n + 127) / 128 * 128;
+  {
+    std::vector<float> s(static_cast<size_t>(n) * ng), st(static_cast<size_t>(w.ldb) * ng, 0.0f);
+    RB_CUDA(cudaMemcpy(s.data(), w.scales, s.size() * 4, cudaMemcpyDeviceToHost), "int8 scales download");
+    for (int64_t r = 0; r < n; ++r)
+      for (size_t g = 0; g < ng; ++g) st[g * w.ldb + r] = s[r * ng + g];
+    if (cudaMalloc(&w.scales_t, st.size() * 4) != cudaSuccess) {
+      cudaGetLastError();
+      cudaFree(w.codes);
+      cudaFree(w.scales);
+      return fail(RB_E_NOMEM, "int8 pack: device allocation failed");
+    }
+    RB_CUDA(cudaMemcpy(w.scales_t, st.data(), st.size() * 4, cudaMemcpyHostToDevice), "int8 scales upload");
+  }
+  w.bytes = static_cast<size_t>(n) * k + static_cast<size_t>(n) * ng * 4 + static_cast<size_t>(w.ldb) * ng * 4;
   const int64_t id = e->next_id++;
   e->weights[id] = w;
   return id;

@@ -89,8 +89,11 @@ int launch_moe_combine_rows(float* x, const void* y, int64_t hidden, const int32
 // Elementwise / codec kernels (quant.cu).
 int launch_quantize_groups(const void* x, int x_dtype, int64_t m, int64_t k, int group, int8_t* codes,
                            float* scales, cudaStream_t st);
-int launch_group_fold(const int32_t* part, int64_t m, int64_t n, const float* a_s, const float* b_s, int64_t ng,
-                      int64_t g, int first, float* y, cudaStream_t st);
+// Group-wise int8 GEMM with in-kernel group promotion (gemm_group.cu): y =
+// sum over groups g of f32(a_s[m,g] * b_st[g,n]) * f32(int32 partial of group g).
+int launch_i8g_gemm(int M, int N, int K, int G, const float* a_s, const float* b_st, int ldb, void* out,
+                    int out_dtype, const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap* tmC,
+                    uint32_t* err, int num_sms, cudaStream_t stream);
 int launch_cast(const void* x, int x_dtype, void* y, int y_dtype, int64_t count,
                 cudaStream_t stream);
 int launch_quantize_rows_i8(const void* x, int x_dtype, int64_t m, int64_t k, float in_scale,

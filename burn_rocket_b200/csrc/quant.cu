@@ -445,31 +445,6 @@ int launch_quantize_groups(const void* x, int x_dtype, int64_t m, int64_t k, int
   return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
 }
 
-// y[m, n] (f32) = (first ? 0 : y) + f32(a_s[m, g] * b_s[n, g]) * f32(partial[m, n]):
-// one group's int32 partial promoted as the reference's readback does
-// (layout::detile_accum_i8_scaled, crates/rocket-npu/src/matmul/layout.rs:504-529).
-__global__ void group_fold_kernel(const int32_t* __restrict__ part, int64_t m, int64_t n,
-                                  const float* __restrict__ a_s, const float* __restrict__ b_s, int64_t ng,
-                                  int64_t g, int first, float* __restrict__ y) {
-  const int64_t total = m * n;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t r = i / n, c = i % n;
-    const float scale = __fmul_rn(a_s[r * ng + g], b_s[c * ng + g]);
-    const float t = __fmul_rn(scale, __int2float_rn(part[i]));
-    y[i] = first ? __fadd_rn(0.0f, t) : __fadd_rn(y[i], t);
-  }
-}
-
-int launch_group_fold(const int32_t* part, int64_t m, int64_t n, const float* a_s, const float* b_s, int64_t ng,
-                      int64_t g, int first, float* y, cudaStream_t st) {
-  int64_t blocks = (m * n + 255) / 256;
-  if (blocks > 148 * 32) blocks = 148 * 32;
-  if (blocks < 1) blocks = 1;
-  group_fold_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(part, m, n, a_s, b_s, ng, g, first, y);
-  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
-}
-
 // ---------------------------------------------------------------- casts
 template <int SRC, int DST>
 __global__ void cast_kernel(const void* __restrict__ x, void* __restrict__ y, int64_t count) {
