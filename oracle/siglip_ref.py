@@ -55,6 +55,16 @@ def layer_norm(x, g, b, eps):
     return (x - mu) / np.sqrt(var + eps) * g + b
 
 
+def layer_norm_f32(x, g, b, eps):
+    """The same LayerNorm evaluated in f32 (as an f32 CPU path computes it):
+    the chain's sensitivity to rounding-level differences."""
+    x = np.asarray(x, np.float32)
+    mu = x.mean(-1, keepdims=True, dtype=np.float32)
+    var = ((x - mu) ** 2).mean(-1, keepdims=True, dtype=np.float32)
+    y = (x - mu) / np.sqrt(var + np.float32(eps)) * np.asarray(g, np.float32) + np.asarray(b, np.float32)
+    return y.astype(np.float64)
+
+
 def gelu_tanh(x):
     """host.rs:15-18: 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))."""
     return 0.5 * x * (1.0 + np.tanh(np.sqrt(2.0 / np.pi) * (x + 0.044715 * (x * x * x))))
@@ -92,12 +102,13 @@ def attention(qkv, cfg, images: int, f16_inputs: bool = False) -> np.ndarray:
     return att
 
 
-def layer(L: dict, cfg, x: np.ndarray, images: int, quant: bool = True) -> np.ndarray:
+def layer(L: dict, cfg, x: np.ndarray, images: int, quant: bool = True, ln32: bool = False) -> np.ndarray:
     """One pre-LN encoder layer on the f64 residual stream x [images*patches,
     hidden]; returns the new residual stream. quant=True follows the device's
     W8A8 projections and f16 activations (GELU of the f32 fc1 product, then
     the f16 store, as the fused fc1 epilogue does); quant=False is the float
-    skeleton (f64 throughout, no codes)."""
+    skeleton (f64 throughout, no codes). ln32: the pre-norms in f32."""
+    norm = layer_norm_f32 if ln32 else layer_norm
     if quant:
         f16, lin = _f16, _w8a8
     else:
@@ -105,18 +116,18 @@ def layer(L: dict, cfg, x: np.ndarray, images: int, quant: bool = True) -> np.nd
         lin = lambda a, w: np.asarray(a, np.float64) @ np.asarray(w, np.float64).T  # noqa: E731
     x = np.asarray(x, np.float64)
     wqkv = np.concatenate([L["wq"], L["wk"], L["wv"]], 0)
-    h16 = f16(layer_norm(x, L["ln1_g"], L["ln1_b"], cfg.eps))
+    h16 = f16(norm(x, L["ln1_g"], L["ln1_b"], cfg.eps))
     qkv = f16(lin(h16, wqkv))
     att = attention(qkv, cfg, images, f16_inputs=quant)
     x = x + f16(lin(f16(att), L["wo"]))
-    h16 = f16(layer_norm(x, L["ln2_g"], L["ln2_b"], cfg.eps))
+    h16 = f16(norm(x, L["ln2_g"], L["ln2_b"], cfg.eps))
     f = f16(gelu_tanh(lin(h16, L["w1"])))
     return x + f16(lin(f, L["w2"]))
 
 
-def forward(hw: dict, cfg, patches: np.ndarray, images: int, quant: bool = True) -> np.ndarray:
+def forward(hw: dict, cfg, patches: np.ndarray, images: int, quant: bool = True, ln32: bool = False) -> np.ndarray:
     """Final-LayerNorm patch states [images*patches, hidden] (f64)."""
     x = np.asarray(patches, np.float64).reshape(images * cfg.patches, cfg.hidden).copy()
     for L in hw["layers"]:
-        x = layer(L, cfg, x, images, quant)
+        x = layer(L, cfg, x, images, quant, ln32)
     return layer_norm(x, hw["post_g"], hw["post_b"], cfg.eps)
