@@ -201,8 +201,6 @@ struct Engine {
   uint32_t* err = nullptr;  // device error word
   float* attn_rec = nullptr;  // attention split-mode records (kAttnRecBytes)
   int* attn_cnt = nullptr;    // attention split-mode arrival counters (kAttnCntBytes)
-  int* gemm_cnt = nullptr;    // split-K GEMM arrival counters (kGemmCntInts), nullptr = no split-K
-  Scratch gemm_ws;            // split-K GEMM partial accumulators
   std::unordered_map<int64_t, Weight> weights;
   int64_t next_id = 1;
   Scratch act;       // activation staging (f16 or int8 codes)
@@ -290,19 +288,6 @@ static size_t dtype_bytes(int dt) {
 // ------------------------------------------------------------------ ops
 // pre_scale != null: x holds W8A8 activation codes int8 [m, k] with these
 // per-row scales (as rb_quantize_rows_i8 / rb_add_layer_norm_quant give).
-// Split-K workspace of a plan: every part's 128-row accumulator blocks
-// (splits x tiles x 2 x 128 x bn words) and the engine's arrival counters.
-static int split_workspace(Engine* e, const GemmPlan& plan, int64_t m, int64_t n, GemmLaunch* L) {
-  if (plan.splits <= 1) return RB_OK;
-  const size_t tiles = static_cast<size_t>((m + 255) / 256) * static_cast<size_t>((n + plan.bn - 1) / plan.bn);
-  const int rc = e->gemm_ws.grow(static_cast<size_t>(plan.splits) * tiles * 2 * 128 * plan.bn * 4,
-                                 "split-K workspace");
-  if (rc != RB_OK) return rc;
-  L->split_ws = e->gemm_ws.ptr;
-  L->split_cnt = e->gemm_cnt;
-  return RB_OK;
-}
-
 static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int64_t m,
                          int64_t k, void* y, int y_dtype, cudaStream_t st, const float* pre_scale = nullptr) {
   auto it = e->weights.find(id);
@@ -364,11 +349,10 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
       g_launches++;
       a = e->act.ptr;
     }
-    GemmPlan plan = gemm_plan(false, L.M, L.N, L.K, e->num_sms, e->gemm_cnt != nullptr);
+    GemmPlan plan = gemm_plan(false, L.M, L.N, L.K, e->num_sms);
     // The gated epilogue turns 128 accumulator columns into 64 outputs: tiles
     // of 256 or 128 columns.
     if (w.gated && plan.bn % 128 != 0) plan = GemmPlan{plan.pair ? 256 : 128, 1, plan.pair};
-    if ((rc = split_workspace(e, plan, m, w.n, &L)) != RB_OK) return rc;
     CUtensorMap tmA, tmC;
     if ((rc = make_tmap_2d(&tmA, a, 2, m, k, k, 64, plan.a_rows(), 128)) != RB_OK) return rc;
     const bool tstore = output_map(&tmC, y, y_dtype, m, n_out);
@@ -427,8 +411,7 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
     L.s_col = reinterpret_cast<const float*>(w.scales);
     L.out_scale = w.out_scale;
     const bool tstore = output_map(&tmC, y, y_dtype, m, w.n);
-    const GemmPlan plan = gemm_plan(true, L.M, L.N, L.K, e->num_sms, e->gemm_cnt != nullptr);
-    if ((rc = split_workspace(e, plan, m, w.n, &L)) != RB_OK) return rc;
+    const GemmPlan plan = gemm_plan(true, L.M, L.N, L.K, e->num_sms);
     if ((rc = launch_w8a8_gemm(L, plan, tmA, w.tm_codes[bn_index(plan.weight_rows())], tstore ? &tmC : nullptr,
                                st)) != RB_OK)
       return fail(rc, "w8a8 gemm launch failed");
@@ -606,13 +589,6 @@ int rb_init(int device_ordinal) {
     e->attn_rec = nullptr;
     e->attn_cnt = nullptr;
   }
-  // Split-K counters (zero between launches); without them GEMMs do not split K.
-  if (cudaMalloc(&e->gemm_cnt, kGemmCntInts * sizeof(int)) != cudaSuccess ||
-      cudaMemset(e->gemm_cnt, 0, kGemmCntInts * sizeof(int)) != cudaSuccess) {
-    cudaGetLastError();
-    if (e->gemm_cnt) cudaFree(e->gemm_cnt);
-    e->gemm_cnt = nullptr;
-  }
   cudaStreamCreateWithFlags(&e->host_stream, cudaStreamNonBlocking);
   g_engine = e;
   return RB_OK;
@@ -638,7 +614,6 @@ int rb_check_device_errors(void) {
     cudaMemset(e->err, 0, sizeof(uint32_t));
     // An aborted attention launch can leave split-mode counters mid-count.
     if (e->attn_cnt) cudaMemset(e->attn_cnt, 0, kAttnCntBytes);
-    if (e->gemm_cnt) cudaMemset(e->gemm_cnt, 0, kGemmCntInts * sizeof(int));
     return fail(RB_E_DEVICE, "kernel error word 0x%x (%s%s%s)", word,
                 (word & kErrWaitTimeout) ? "wait-timeout " : "",
                 (word & kErrTmemAlloc) ? "tmem-alloc " : "",

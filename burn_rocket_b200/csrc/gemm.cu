@@ -367,7 +367,7 @@ int gemm_policy() { return g_policy.load(); }
 //   * Q8_0: pair tiles run ~40% faster than the best single-CTA tile (256 x
 //     128, two M halves sharing one dequantised B tile) at large M; at small
 //     M (a single round of tiles) the two are even.
-GemmPlan gemm_plan(bool i8, int M, int N, int K, int num_sms, bool allow_split) {
+GemmPlan gemm_plan(bool i8, int M, int N, int K, int num_sms) {
   const int policy = g_policy.load();
   struct Shape { int bn, mh; bool pair; double eff; };
   const bool long_k = K > 2048;
@@ -392,20 +392,6 @@ GemmPlan gemm_plan(bool i8, int M, int N, int K, int num_sms, bool allow_split) 
       best_cost = cost;
       best = GemmPlan{c[i].bn, c[i].mh, c[i].pair};
     }
-    // Split-K: a single round of 256-column pair tiles that leaves pairs idle
-    // can cut K into S parts (each part >= 4 k-blocks) so every pair works;
-    // a part costs 1/S of the tile's MMA columns plus the fixed overhead and
-    // the reduction (its rows through the workspace).
-    const int num_kb = K / (i8 ? 128 : 64);
-    if (allow_split && c[i].pair && c[i].bn == 256 && 2 * tiles <= units && tiles * 2 <= kGemmCntInts) {
-      for (int S = 2; S <= 4 && S * tiles <= units && num_kb >= 4 * S; ++S) {
-        const double cs = c[i].bn * c[i].eff / S + 32.0 + 24.0;
-        if (cs < best_cost) {
-          best_cost = cs;
-          best = GemmPlan{c[i].bn, 1, true, S};
-        }
-      }
-    }
   }
   return best;
 }
@@ -421,9 +407,6 @@ static GemmArgs make_args(const GemmLaunch& L) {
   a.tile_expert = L.tile_expert;
   a.gated = L.gated;
   a.act = L.act;
-  a.splits = 1;
-  a.split_ws = L.split_ws;
-  a.split_cnt = L.split_cnt;
   return a;
 }
 
@@ -436,12 +419,8 @@ int launch_w8a8_gemm_pair(const GemmArgs& a, int bn, int num_sms, const CUtensor
 int launch_q8_gemm(const GemmLaunch& L, const GemmPlan& plan, const CUtensorMap& tmA,
                    const CUtensorMap& tmCodes, const CUtensorMap& tmScales, const CUtensorMap* tmC,
                    cudaStream_t stream) {
-  GemmArgs a = make_args(L);
-  if (plan.pair) {
-    a.splits = plan.splits > 1 ? plan.splits : 1;
-    if (a.splits > 1 && (!a.split_ws || !a.split_cnt || a.tile_expert)) return RB_E_SHAPE;
-    return launch_q8_gemm_pair(a, plan.bn, L.num_sms, tmA, tmCodes, tmScales, tmC, stream);
-  }
+  const GemmArgs a = make_args(L);
+  if (plan.pair) return launch_q8_gemm_pair(a, plan.bn, L.num_sms, tmA, tmCodes, tmScales, tmC, stream);
   if (plan.mh == 2) {
     if (plan.bn != 128) return RB_E_SHAPE;
     return launch_cfg<CfgQ8_128x2>(tmA, tmCodes, tmScales, tmC, a, L.num_sms, stream);
@@ -460,12 +439,8 @@ int launch_f16_gemm_pair(const GemmArgs& a, int bn, int num_sms, const CUtensorM
 
 int launch_f16_gemm(const GemmLaunch& L, const GemmPlan& plan, const CUtensorMap& tmA,
                     const CUtensorMap& tmB, const CUtensorMap* tmC, cudaStream_t stream) {
-  GemmArgs a = make_args(L);
-  if (plan.pair) {
-    a.splits = plan.splits > 1 ? plan.splits : 1;
-    if (a.splits > 1 && (!a.split_ws || !a.split_cnt || a.tile_expert)) return RB_E_SHAPE;
-    return launch_f16_gemm_pair(a, plan.bn, L.num_sms, tmA, tmB, tmC, stream);
-  }
+  const GemmArgs a = make_args(L);
+  if (plan.pair) return launch_f16_gemm_pair(a, plan.bn, L.num_sms, tmA, tmB, tmC, stream);
   switch (plan.bn) {
     case 256: return launch_cfg<CfgF16_256>(tmA, tmB, tmA, tmC, a, L.num_sms, stream);
     case 128: return launch_cfg<CfgF16_128>(tmA, tmB, tmA, tmC, a, L.num_sms, stream);
@@ -475,12 +450,8 @@ int launch_f16_gemm(const GemmLaunch& L, const GemmPlan& plan, const CUtensorMap
 
 int launch_w8a8_gemm(const GemmLaunch& L, const GemmPlan& plan, const CUtensorMap& tmA,
                      const CUtensorMap& tmB, const CUtensorMap* tmC, cudaStream_t stream) {
-  GemmArgs a = make_args(L);
-  if (plan.pair) {
-    a.splits = plan.splits > 1 ? plan.splits : 1;
-    if (a.splits > 1 && (!a.split_ws || !a.split_cnt || a.tile_expert)) return RB_E_SHAPE;
-    return launch_w8a8_gemm_pair(a, plan.bn, L.num_sms, tmA, tmB, tmC, stream);
-  }
+  const GemmArgs a = make_args(L);
+  if (plan.pair) return launch_w8a8_gemm_pair(a, plan.bn, L.num_sms, tmA, tmB, tmC, stream);
   switch (plan.bn) {
     case 256: return launch_cfg<CfgI8_256>(tmA, tmB, tmA, tmC, a, L.num_sms, stream);
     case 128: return launch_cfg<CfgI8_128>(tmA, tmB, tmA, tmC, a, L.num_sms, stream);

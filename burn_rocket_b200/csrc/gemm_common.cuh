@@ -49,13 +49,6 @@ struct GemmArgs {
   // Element-wise activation applied before the f16 rounding (RB_ACT_*).
   int act;
   uint32_t* err;
-  // Split-K (CTA-pair kernel, plain GEMMs): each output tile's K range is cut
-  // into `splits` parts run by different pairs; every part stores its
-  // accumulator rows in split_ws and the last part to arrive (split_cnt, one
-  // self-resetting counter per 128-row half tile) adds them in split order.
-  int splits;
-  void* split_ws;
-  int* split_cnt;
 };
 
 // --------------------------------------------------------------------------

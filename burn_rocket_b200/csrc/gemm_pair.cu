@@ -11,14 +11,6 @@
 //     the leader's TMEM and rows 128..255 into the peer's;
 //   * each CTA's epilogue stores its own 128 rows.
 //
-// Split-K (args.splits > 1, plain GEMMs with fewer tiles than pairs): work
-// units are (tile, K split); each unit's pair accumulates its slice of the
-// k-blocks, each CTA stores its 128 accumulator rows in a workspace, and the
-// CTA that arrives last for its half tile (a self-resetting counter) adds the
-// parts in split order (f32 adds for Q8_0 / f16, exact int32 adds for W8A8),
-// writes the sum back to TMEM and runs the usual epilogue. No CTA waits for
-// another.
-//
 // Per SM this halves the B bytes loaded from L2 and read from shared memory
 // per FLOP compared with a 128 x BN tile on one SM, which is what bounds the
 // single-CTA kernel at large M (L2 -> SM traffic and shared-memory bandwidth),
@@ -50,9 +42,8 @@ namespace rb {
 // as soon as the dequant warps have read a stage (so dequantisation can run
 // ahead of the MMA by up to CSTAGES stages), and BSTAGES dequantised B stages.
 template <int BN_, int LSTAGES_, int KIND_, int CSTAGES_ = 1, int BSTAGES_ = 1, int DQ_WARPS_ = 8,
-          int DQ_GROUPS_ = 1, bool SPLIT_ = false>
+          int DQ_GROUPS_ = 1>
 struct PairCfg {
-  static constexpr bool SPLIT = SPLIT_;              // split-K variant (args.splits parts per tile)
   static constexpr int DQ_WARPS = DQ_WARPS_;         // Q8_0 dequant warps
   static constexpr int DQ_GROUPS = DQ_GROUPS_;       // stages dequantised concurrently
   static_assert(DQ_WARPS % DQ_GROUPS == 0, "equal dequant groups");
@@ -98,70 +89,6 @@ struct PairCfg {
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
 
-// Split-K step of one CTA's epilogue warps for its 128-row half of tile t:
-// store this part's accumulator rows [cbeg, cend) in the workspace; the part
-// that arrives last (counter cnt[2t + rank], reset by that part) then adds all
-// parts in split order (its own from TMEM) and writes the sum into TMEM for
-// the usual epilogue. Returns whether this CTA is that last part.
-// (Not inlined: its registers stay out of the pipeline roles' allocation.)
-template <class Cfg>
-__device__ __noinline__ bool split_reduce(uint32_t tmem_base, uint32_t acc_col, int quarter, int lane, int warp,
-                                          int cbeg, int cend, int t, int sp, int splits, uint32_t rank,
-                                          uint32_t* ws, int* cnt, volatile int* last_flag) {
-  constexpr int BN = Cfg::BN;
-  const int row = quarter * 32 + lane;
-  const size_t blk = static_cast<size_t>(t) * 2 + rank;
-  const size_t plane = static_cast<size_t>(128) * BN;  // one part's 128 x BN block (4-byte words)
-  uint32_t* mine = ws + (blk * splits + sp) * plane + static_cast<size_t>(row) * BN;
-  for (int c0 = cbeg; c0 < cend; c0 += 16) {
-    uint32_t r[16];
-    tmem_ld16(tmem_addr(tmem_base, quarter * 32, acc_col + c0), r);
-    tmem_wait_ld();
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      __stcg(reinterpret_cast<uint4*>(mine + c0) + i, make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]));
-  }
-  __threadfence();
-  named_bar_sync(1, Cfg::EPI_WARPS * 32);
-  if (warp == kEpiWarp0 && lane == 0) {
-    const int old = atomicAdd(cnt + blk, 1);
-    const int last = old == splits - 1;
-    if (last) atomicExch(cnt + blk, 0);  // ready for the next launch
-    *last_flag = last;
-  }
-  named_bar_sync(1, Cfg::EPI_WARPS * 32);
-  if (!*last_flag) return false;
-  __threadfence();
-  for (int c0 = cbeg; c0 < cend; c0 += 16) {
-    const uint32_t ta = tmem_addr(tmem_base, quarter * 32, acc_col + c0);
-    uint32_t sum[16];
-    for (int s = 0; s < splits; ++s) {
-      uint32_t v[16];
-      if (s == sp) {  // this part: still in TMEM
-        tmem_ld16(ta, v);
-        tmem_wait_ld();
-      } else {
-        const uint4* src = reinterpret_cast<const uint4*>(ws + (blk * splits + s) * plane +
-                                                          static_cast<size_t>(row) * BN + c0);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint4 q = __ldcg(src + i);
-          v[4 * i] = q.x; v[4 * i + 1] = q.y; v[4 * i + 2] = q.z; v[4 * i + 3] = q.w;
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        if (s == 0) sum[i] = v[i];
-        else if constexpr (Cfg::I8) sum[i] = sum[i] + v[i];  // exact int32 partial sums
-        else sum[i] = __float_as_uint(__fadd_rn(__uint_as_float(sum[i]), __uint_as_float(v[i])));
-      }
-    }
-    tmem_st16(ta, sum);
-  }
-  tmem_wait_st();
-  return true;
-}
-
 template <class Cfg>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Cfg::THREADS, 1)
 gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -186,7 +113,6 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   uint64_t* acc_local = acc_empty + 2;               // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_local + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);  // split-K: this CTA sums
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -198,10 +124,6 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   const int num_kb = (K + Cfg::BK - 1) / Cfg::BK;
   const int pair = blockIdx.x >> 1;
   const int npairs = gridDim.x >> 1;
-  const int splits = Cfg::SPLIT && args.splits > 1 ? args.splits : 1;
-  const int num_units = num_tiles * splits;  // (tile, K split) work units
-  auto kb_begin = [&](int u) { return (u % splits) * num_kb / splits; };
-  auto kb_end = [&](int u) { return (u % splits + 1) * num_kb / splits; };
   // Grouped GEMM (tile_expert != nullptr): the first weight row of tile t's
   // expert block. Expert segments are 256-row aligned, so both 128-row
   // halves of a pair tile share one expert (entries are per 128 rows); the
@@ -257,13 +179,12 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     if (elect_one_sync()) {
       int ls = 0;
       uint32_t lph = 0;
-      for (int u = pair; u < num_units; u += npairs) {
-        const int t = u / splits;
+      for (int t = pair; t < num_tiles; t += npairs) {
         const int w0 = expert_row0(t);
         if (w0 < 0) break;
         const int m0 = (t / tiles_n) * 256 + static_cast<int>(rank) * 128;
         const int nb = w0 + (t % tiles_n) * BN + static_cast<int>(rank) * HB;
-        for (int kb = kb_begin(u); kb < kb_end(u); ++kb) {
+        for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&ld_empty[ls], lph ^ 1, args.err, abort_flag)) goto producer_done;
           uint8_t* st = smem + ls * Cfg::LSTAGE;
           const uint32_t lf = mapa_shared(&ld_full[ls], 0);
@@ -284,15 +205,14 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       int ls = 0, bs = 0;
       uint32_t lph = 0, bph = 0;
       int local = 0;
-      for (int u = pair; u < num_units; u += npairs, ++local) {
-        if (expert_row0(u / splits) < 0) break;
+      for (int t = pair; t < num_tiles; t += npairs, ++local) {
+        if (expert_row0(t) < 0) break;
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait_cluster(&acc_empty[acc], acc_phase ^ 1, args.err, abort_flag)) goto mma_done;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        const int kb0 = kb_begin(u);
-        for (int kb = kb0; kb < kb_end(u); ++kb) {
+        for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait_cluster(&ld_full[ls], lph, args.err, abort_flag)) goto mma_done;
           if constexpr (Cfg::Q8) {
             if (!mbar_wait(&b_local[bs], bph, args.err, abort_flag)) goto mma_done;
@@ -306,7 +226,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           for (int ks = 0; ks < Cfg::KSTEPS; ++ks) {
             const uint64_t da = desc_kmajor_sw128(a_addr + ks * 32);
             const uint64_t db = desc_kmajor_sw128(b_addr + ks * 32);
-            const uint32_t accum = (kb > kb0 || ks > 0) ? 1u : 0u;
+            const uint32_t accum = (kb > 0 || ks > 0) ? 1u : 0u;
             if constexpr (Cfg::I8) umma_i8_pair(d_tmem, da, db, idesc, accum);
             else umma_f16_pair(d_tmem, da, db, idesc, accum);
           }
@@ -324,9 +244,9 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       // Peer: forward "my half of B stage bs is ready" to the leader, once.
       int bs = 0;
       uint32_t bph = 0;
-      for (int u = pair; u < num_units; u += npairs) {
-        if (expert_row0(u / splits) < 0) break;
-        for (int kb = kb_begin(u); kb < kb_end(u); ++kb) {
+      for (int t = pair; t < num_tiles; t += npairs) {
+        if (expert_row0(t) < 0) break;
+        for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&b_local[bs], bph, args.err, abort_flag)) goto fwd_b_done;
           mbar_arrive_cluster(mapa_shared(&b_full[bs], 0));
           if (++bs == Cfg::BSTAGES) { bs = 0; bph ^= 1; }
@@ -344,8 +264,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     const int mode = args.gated ? kEpiSiluF16 : epi_mode(Cfg::I8, args.out_dtype, args.out_scale, args.act);
     int buf = 0;
     int local = 0;
-    for (int u = pair; u < num_units; u += npairs, ++local) {
-      const int t = u / splits;
+    for (int t = pair; t < num_tiles; t += npairs, ++local) {
       if (expert_row0(t) < 0) break;
       const int n0 = (t % tiles_n) * BN;
       const int m0 = (t / tiles_n) * 256 + static_cast<int>(rank) * 128;
@@ -353,15 +272,6 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!warp_wait(&acc_full[acc], acc_phase, args.err, abort_flag)) break;
       tc_fence_after();
-      if (Cfg::SPLIT && splits > 1 && !split_reduce<Cfg>(tmem_base, acc * BN, quarter, lane, warp, cbeg, cend, t, u % splits,
-                                           splits, rank, reinterpret_cast<uint32_t*>(args.split_ws),
-                                           args.split_cnt, last_flag)) {
-        // another part of this half tile sums it: release the accumulator
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(rank == 0 ? &acc_empty[acc] : &acc_local[acc]);
-        continue;
-      }
       epi_block<BN, Cfg::I8, Cfg::EPI_BUFS>(tmem_base, acc * BN, quarter, lane, m0, n0, cbeg, cend, M, N,
                                             args.s_row, args.out, args.ldo, mode, ep, args.epi_path,
                                             &tmC, ebuf, buf);
@@ -375,12 +285,11 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     if (elect_one_sync()) {
       int cs = 0;
       uint32_t cph = 0;
-      for (int u = pair; u < num_units; u += npairs) {
-        const int t = u / splits;
+      for (int t = pair; t < num_tiles; t += npairs) {
         const int w0 = expert_row0(t);
         if (w0 < 0) break;
         const int nb = w0 + (t % tiles_n) * BN + static_cast<int>(rank) * HB;
-        for (int kb = kb_begin(u); kb < kb_end(u); ++kb) {
+        for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&cd_empty[cs], cph ^ 1, args.err, abort_flag)) goto codes_done;
           uint8_t* st = smem + Cfg::CODE_OFF + cs * Cfg::CSTAGE;
           mbar_arrive_expect_tx(&cd_full[cs], Cfg::CODE_TX);
@@ -396,8 +305,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     // Forward "my accumulator rows are drained" to the leader, once per tile.
     if (rank == 1 && elect_one_sync()) {
       int local = 0;
-      for (int u = pair; u < num_units; u += npairs, ++local) {
-        if (expert_row0(u / splits) < 0) break;
+      for (int t = pair; t < num_tiles; t += npairs, ++local) {
+        if (expert_row0(t) < 0) break;
         const int acc = local & 1;
         if (!mbar_wait(&acc_local[acc], (local >> 1) & 1, args.err, abort_flag)) break;
         mbar_arrive_cluster(mapa_shared(&acc_empty[acc], 0));
@@ -419,9 +328,9 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     const int grp = (warp - kDqWarp0) / kGroupWarps;
     const int tid = threadIdx.x - (kDqWarp0 + grp * kGroupWarps) * 32;
     int q = 0;
-    for (int u = pair; u < num_units; u += npairs) {
-      if (expert_row0(u / splits) < 0) break;
-      for (int kb = kb_begin(u); kb < kb_end(u); ++kb, ++q) {
+    for (int t = pair; t < num_tiles; t += npairs) {
+      if (expert_row0(t) < 0) break;
+      for (int kb = 0; kb < num_kb; ++kb, ++q) {
         if (q % Cfg::DQ_GROUPS != grp) continue;
         const int cs = q % Cfg::CSTAGES, bs = q % Cfg::BSTAGES;
         const uint32_t cph = (q / Cfg::CSTAGES) & 1, bph = (q / Cfg::BSTAGES) & 1;
@@ -468,10 +377,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 // Host-side launch.
 
 using PairQ8_256 = PairCfg<256, 5, kKindQ8, 5, 5, 12, 3>;
-using PairQ8_256S = PairCfg<256, 5, kKindQ8, 5, 5, 12, 3, true>;  // split-K
 using PairQ8_128 = PairCfg<128, 7, kKindQ8, 8, 6, 12, 3>;
 using PairI8_256 = PairCfg<256, 6, kKindI8>;
-using PairI8_256S = PairCfg<256, 6, kKindI8, 1, 1, 8, 1, true>;  // split-K
 using PairI8_128 = PairCfg<128, 8, kKindI8>;
 using PairF16_256 = PairCfg<256, 6, kKindF16>;
 using PairF16_128 = PairCfg<128, 8, kKindF16>;
@@ -480,7 +387,7 @@ template <class Cfg>
 static int launch_pair_cfg(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmS,
                            const CUtensorMap* tmC, const GemmArgs& a, int num_sms,
                            cudaStream_t stream) {
-  const int tiles = ((a.M + 255) / 256) * ((a.N + Cfg::BN - 1) / Cfg::BN) * (a.splits > 1 ? a.splits : 1);
+  const int tiles = ((a.M + 255) / 256) * ((a.N + Cfg::BN - 1) / Cfg::BN);
   static uint64_t configured = 0;  // one bit per device ordinal
   static int max_pairs[64] = {};
   int dev = 0;
@@ -520,8 +427,6 @@ static int launch_pair_cfg(const CUtensorMap& tmA, const CUtensorMap& tmB, const
 int launch_q8_gemm_pair(const GemmArgs& a, int bn, int num_sms, const CUtensorMap& tmA,
                         const CUtensorMap& tmCodes, const CUtensorMap& tmScales,
                         const CUtensorMap* tmC, cudaStream_t stream) {
-  if (a.splits > 1)
-    return bn == 256 ? launch_pair_cfg<PairQ8_256S>(tmA, tmCodes, tmScales, tmC, a, num_sms, stream) : RB_E_SHAPE;
   switch (bn) {
     case 256: return launch_pair_cfg<PairQ8_256>(tmA, tmCodes, tmScales, tmC, a, num_sms, stream);
     case 128: return launch_pair_cfg<PairQ8_128>(tmA, tmCodes, tmScales, tmC, a, num_sms, stream);
@@ -531,7 +436,6 @@ int launch_q8_gemm_pair(const GemmArgs& a, int bn, int num_sms, const CUtensorMa
 
 int launch_f16_gemm_pair(const GemmArgs& a, int bn, int num_sms, const CUtensorMap& tmA,
                          const CUtensorMap& tmB, const CUtensorMap* tmC, cudaStream_t stream) {
-  if (a.splits > 1) return RB_E_SHAPE;
   switch (bn) {
     case 256: return launch_pair_cfg<PairF16_256>(tmA, tmB, tmA, tmC, a, num_sms, stream);
     case 128: return launch_pair_cfg<PairF16_128>(tmA, tmB, tmA, tmC, a, num_sms, stream);
@@ -541,8 +445,6 @@ int launch_f16_gemm_pair(const GemmArgs& a, int bn, int num_sms, const CUtensorM
 
 int launch_w8a8_gemm_pair(const GemmArgs& a, int bn, int num_sms, const CUtensorMap& tmA,
                           const CUtensorMap& tmB, const CUtensorMap* tmC, cudaStream_t stream) {
-  if (a.splits > 1)
-    return bn == 256 ? launch_pair_cfg<PairI8_256S>(tmA, tmB, tmA, tmC, a, num_sms, stream) : RB_E_SHAPE;
   switch (bn) {
     case 256: return launch_pair_cfg<PairI8_256>(tmA, tmB, tmA, tmC, a, num_sms, stream);
     case 128: return launch_pair_cfg<PairI8_128>(tmA, tmB, tmA, tmC, a, num_sms, stream);

@@ -26,8 +26,6 @@ struct GemmLaunch {
   const int* tile_expert; // grouped GEMM table (one expert id per 128 rows), or nullptr
   int gated;              // gate/up interleaved in 32-row blocks: out = silu(gate) * up, N/2 f16 columns
   int act;                // RB_ACT_*: element-wise activation before the f16 output rounding
-  void* split_ws;         // split-K partial accumulators (plan.splits > 1)
-  int* split_cnt;         // split-K arrival counters, zero between launches
   uint32_t* err;
   int num_sms;
 };
@@ -39,14 +37,10 @@ struct GemmPlan {
   int bn;
   int mh;
   bool pair;
-  int splits = 1;  // pair tiles only: K splits per output tile
   int weight_rows() const { return pair ? bn / 2 : bn; }  // weight map box height
   int a_rows() const { return pair ? 128 : 128 * mh; }     // activation map box height
 };
-// allow_split: the caller provides split-K workspace (pair tiles may then cut
-// K into 2..4 parts when the tiles alone leave SM pairs idle).
-GemmPlan gemm_plan(bool i8, int M, int N, int K, int num_sms, bool allow_split = false);
-constexpr int kGemmCntInts = 1024;  // split-K arrival counters (two per tile; tiles <= SM pairs)
+GemmPlan gemm_plan(bool i8, int M, int N, int K, int num_sms);
 // Restricts gemm_plan to single-CTA or (preferably) pair tiles; returns the old policy.
 int set_gemm_policy(int policy);
 int gemm_policy();

@@ -181,11 +181,6 @@ __device__ __forceinline__ void drain_after_abort() {
   __syncthreads();
 }
 
-// Named barrier `id` (1..15) over `threads` threads of the CTA (a multiple of 32).
-__device__ __forceinline__ void named_bar_sync(int id, int threads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -84,35 +84,6 @@ def test_q8_0_gemm_config1_parity(rb, orc):
     assert max_rel(got, ref16) <= 1e-5
 
 
-def test_split_k_plans(rb, orc, tile_policy):
-    """Plans that cut K into parts (CTA-pair 256-column tiles, too few tiles
-    for the SM pairs; the last part of each half tile adds the parts in split
-    order): config #1's Q8_0 GEMM equals the single-CTA plan within f32
-    summation order, and a long-K W8A8 GEMM stays bit-exact (int32 parts add
-    exactly); each twice in a row (the arrival counters reset themselves)."""
-    import torch
-    m, n, k = 512, 3072, 1024
-    w, codes, scales = q8_weight(orc, n, k, seed=91)
-    wid = rb.pack_q8_0(torch.from_numpy(w))
-    a = np.random.default_rng(92).standard_normal((m, k)).astype(np.float32)
-    ad = torch.from_numpy(a).cuda()
-    tile_policy("single")
-    base = rb.matmul(ad, wid).cpu().numpy()
-    tile_policy("auto")
-    for _ in range(2):
-        got = rb.matmul(ad, wid).cpu().numpy()
-        assert max_rel(got, base) <= 1e-5
-    a16 = orc.f16_bits_to_f32(orc.f32_to_f16_bits(a))
-    ref16 = orc.gemm_f64acc(a16, orc.f16_bits_to_f32(orc.f32_to_f16_bits(orc.q8_0_dequant(codes, scales))))
-    assert max_rel(got, ref16) <= 1e-5
-    x, wc, ws, w8, xd = _w8a8_case(rb, orc, 512, 3072, 4096, seed=93)
-    want = orc.w8a8_matmul(x, wc, ws)
-    for _ in range(2):
-        y = rb.matmul(xd, w8).cpu().numpy()
-        assert np.array_equal(y.view(np.uint32), want.view(np.uint32))
-    rb.check_device_errors()
-
-
 @pytest.mark.parametrize("m,n,k", [(1, 32, 32), (3, 96, 96), (129, 200, 1024), (300, 3072, 64),
                                    (77, 136, 160), (1000, 1024, 1024), (128, 6144, 1024)])
 def test_q8_0_gemm_ragged_shapes(rb, orc, m, n, k):
