@@ -17,15 +17,18 @@
 //   warps 2..9  fold: as soon as a group's partial lands, each warp loads its
 //               32 rows x 64 columns of it, releases the buffer, and adds
 //               f32(a_s * b_s) * f32(partial) into f32 registers — the
-//               reference's order, every operation individually rounded, so
-//               the result is bit-identical. The MMA of the next groups runs
+//               reference's order, every operation individually rounded (the
+//               multiplies two columns per packed f32x2 instruction, each
+//               lane IEEE-rounded on its own; the accumulating adds scalar,
+//               never contracted with a multiply), so the result is
+//               bit-identical. The MMA of the next groups runs
 //               while the fold works. At the end of the tile the f32 sums go
 //               to a fourth TMEM buffer and leave through the shared GEMM
 //               epilogue (swizzled staging + TMA store; f16 / bf16 casts).
 // No partial ever goes through global memory: per call there are two
 // launches, the activation group quantiser and this kernel.
 //
-// f32(partial): |P_g| <= 127 * 128 * G, below 2^22 for G <= 256, where the
+// f32(partial): |P_g| <= 127 * 127 * G, below 2^22 for G <= 256, where the
 // int32 -> f32 conversion is exact and is done on the FP32 pipe (adding the
 // integer to the bits of 1.5 * 2^23 and subtracting 1.5 * 2^23); larger
 // groups use the conversion instruction (rounding to nearest even either way,
@@ -62,12 +65,43 @@ struct GroupArgs {
   uint32_t* err;
 };
 
-__device__ __forceinline__ float group_part_f32(uint32_t p, bool small) {
-  // exact for |p| < 2^22: 1.5 * 2^23 + p is representable with ulp 1
-  return small ? __fsub_rn(__int_as_float(static_cast<int>(p) + 0x4B400000), 12582912.0f)
-               : __int2float_rn(static_cast<int>(p));
+// Packed pairs of f32: two independent IEEE-rounded multiplies per
+// instruction. (The accumulating adds stay scalar add.rn, which is never
+// contracted with a multiply into a single rounding.)
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
 }
 
+// f32 of two int32 partials. SMALL (|p| < 2^22): 1.5 * 2^23 + p is exact with
+// ulp 1, so adding the integer to the bits of 1.5 * 2^23 and subtracting
+// 1.5 * 2^23 is the exact conversion; otherwise the conversion instruction.
+template <bool SMALL>
+__device__ __forceinline__ uint64_t group_part_f32x2(uint32_t p0, uint32_t p1) {
+  if constexpr (SMALL) {
+    const uint64_t m = f2_pack(__int_as_float(static_cast<int>(p0) + 0x4B400000),
+                               __int_as_float(static_cast<int>(p1) + 0x4B400000));
+    return f2_add(m, f2_pack(-12582912.0f, -12582912.0f));  // exact: no rounding involved
+  } else {
+    return f2_pack(__int2float_rn(static_cast<int>(p0)), __int2float_rn(static_cast<int>(p1)));
+  }
+}
+
+template <bool SMALL>
 __global__ void __launch_bounds__(kGThreads, 1)
 gemm_i8g_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmC, GroupArgs args) {
@@ -179,7 +213,6 @@ gemm_i8g_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     const EpiParams ep{nullptr, args.out_dtype, 0.0f, 0.0f};
     const int mode = epi_mode(false, args.out_dtype, 0.0f);
     uint8_t* ebuf = smem + kGEpiOff + (warp - kEpiWarp0) * kEpiBufBytes;
-    const bool small = G <= 256;
     int buf = 0;
     int q = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
@@ -197,23 +230,29 @@ gemm_i8g_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         const uint32_t taddr = tmem_addr(tmem_base, quarter * 32, pb * kGBN + cbeg);
         tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&p[0]));
         tmem_ld32(taddr + 32, *reinterpret_cast<uint32_t(*)[32]>(&p[32]));
+        const float a = __ldg(asr + g);  // scale loads in flight with the TMEM loads
+        const float4* bs = reinterpret_cast<const float4*>(args.b_st + static_cast<int64_t>(g) * args.ldb + n0 +
+                                                           cbeg);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&part_empty[pb]);  // the MMA may refill this buffer
-        const float a = __ldg(asr + g);
-        const float4* bs = reinterpret_cast<const float4*>(args.b_st + static_cast<int64_t>(g) * args.ldb + n0 +
-                                                           cbeg);
+        const uint64_t aa = f2_pack(a, a);
 #pragma unroll
         for (int c4 = 0; c4 < kGHalf / 4; ++c4) {
           const float4 b4 = __ldg(bs + c4);
-          const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int c = 4 * c4 + e;
-            const float s = __fmul_rn(a, bv[e]);
-            acc[c] = __fadd_rn(acc[c], __fmul_rn(s, group_part_f32(p[c], small)));
-          }
+          // f32(a_s * b_s), then f32(that * f32(partial)), two columns per instruction
+          const uint64_t t01 = f2_mul(f2_mul(aa, f2_pack(b4.x, b4.y)),
+                                      group_part_f32x2<SMALL>(p[4 * c4], p[4 * c4 + 1]));
+          const uint64_t t23 = f2_mul(f2_mul(aa, f2_pack(b4.z, b4.w)),
+                                      group_part_f32x2<SMALL>(p[4 * c4 + 2], p[4 * c4 + 3]));
+          float t0, t1, t2, t3;
+          f2_unpack(t01, t0, t1);
+          f2_unpack(t23, t2, t3);
+          acc[4 * c4] = __fadd_rn(acc[4 * c4], t0);
+          acc[4 * c4 + 1] = __fadd_rn(acc[4 * c4 + 1], t1);
+          acc[4 * c4 + 2] = __fadd_rn(acc[4 * c4 + 2], t2);
+          acc[4 * c4 + 3] = __fadd_rn(acc[4 * c4 + 3], t3);
         }
       }
       {
@@ -255,7 +294,10 @@ int launch_i8g_gemm(int M, int N, int K, int G, const float* a_s, const float* b
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(configured & (1ull << (dev & 63)))) {
-    if (cudaFuncSetAttribute(gemm_i8g_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmem) != cudaSuccess)
+    if (cudaFuncSetAttribute(gemm_i8g_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmem) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(gemm_i8g_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmem) !=
+            cudaSuccess)
       return RB_E_DEVICE;
     configured |= 1ull << (dev & 63);
   }
@@ -266,7 +308,10 @@ int launch_i8g_gemm(int M, int N, int K, int G, const float* a_s, const float* b
   a.epi_path = tmC == nullptr ? kEpiPathScalar : epi_path_default();
   const int tiles = ((M + 127) / 128) * ((N + kGBN - 1) / kGBN);
   const int grid = tiles < num_sms ? tiles : num_sms;
-  gemm_i8g_kernel<<<grid, kGThreads, kGSmem, stream>>>(tmA, tmB, tmC ? *tmC : tmA, a);
+  if (G <= 256)
+    gemm_i8g_kernel<true><<<grid, kGThreads, kGSmem, stream>>>(tmA, tmB, tmC ? *tmC : tmA, a);
+  else
+    gemm_i8g_kernel<false><<<grid, kGThreads, kGSmem, stream>>>(tmA, tmB, tmC ? *tmC : tmA, a);
   return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
 }
 

@@ -234,7 +234,8 @@ def test_tile_policy_rejects_unknown(rb):
 # ------------------------------------------------------------------ group-wise int8 (a7)
 @pytest.mark.parametrize("m,n,k,group", [(1, 32, 32, 32), (50, 96, 256, 32), (300, 1024, 1024, 128),
                                          (129, 3072, 1024, 64), (257, 200, 384, 128), (70, 130, 1024, 512),
-                                         (2394, 4304, 1152, 128), (1000, 1152, 4096, 32)])
+                                         (2394, 4304, 1152, 128), (1000, 1152, 4096, 32),
+                                         (100, 200, 4096, 2048)])
 def test_group_int8_matmul_bit_exact(rb, orc, m, n, k, group):
     """rocket_pack_i8 + matmul_i8 (ext.rs:939-1029, 1505-1554): codes and group
     scales of both operands, and the f32 sum of promoted int32 group partials,
