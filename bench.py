@@ -7,9 +7,10 @@ BASELINE.json's metric has three items: "Q8_0/W8A8 GEMM TFLOP/s; GQA attn
 TFLOP/s; Qwen3-Emb-0.6B prefill tok/s". The default line is the model item,
 config #3, and it carries sub-records (key "sub"), each with its own
 ms_per_step, roofline and e2e: config #4's W8A8 tower data-parallel over the
-same N GPUs (every N), and at N = 1 one record per single-op item (config #1
-Q8_0 GEMM, config #2 attention, config #4's W8A8 projections), each timed
-alone.
+same N GPUs (every N), config #5's MoE expert-parallel over them (N >= 2,
+with its all-to-all time and share), and at N = 1 one record per single-op
+item (config #1 Q8_0 GEMM, config #2 attention, config #4's W8A8
+projections, group-wise int8), each timed alone.
 
 Workloads (synthetic seeded data of the named shapes):
   qwen3   config #3 (default): Qwen3-Embedding-0.6B-architecture forward, 28
@@ -615,10 +616,10 @@ class MoeWorkload:
             from burn_rocket_b200.moe_ep import MoeEPModel, ep_plan
             pairs = ([dist.new_group([2 * i, 2 * i + 1]) for i in range(world // 2)]
                      if world > self.BATCH else None)
+            # fixed-capacity all-to-alls: no host reads, the whole forward replays from a CUDA graph
             self.model = MoeEPModel(self.cfg, self.BATCH, self.SEQ, rank, world, seed=0, pair_groups=pairs)
             mine = torch.cat([ids[s * self.SEQ + r0: s * self.SEQ + r0 + n]
                               for s, r0, n in ep_plan(world, self.BATCH, self.SEQ)[rank]])
-            self.graphable = False  # the all-to-all splits are read on the host every layer
         self.model.ids_in.copy_(mine.to(dev))
         self.hids = mine.pin_memory()
         self.hout = torch.empty(self.model.T, self.cfg.hidden, dtype=torch.float16).pin_memory()
@@ -629,17 +630,39 @@ class MoeWorkload:
         self.model.forward_device()
 
     def e2e_step(self):
-        import torch
-        if self.world == 1:
-            if self.model.graph is None:  # the public host call replays the model's CUDA graph
-                self.model.capture()
-            self.model.prefill_host(self.hids, self.hout)
-        else:
-            self.model.ids_in.copy_(self.hids, non_blocking=True)
-            self.model.forward_device()
-            self.hout.copy_(self.model.out, non_blocking=True)
-            torch.cuda.current_stream().synchronize()
+        if self.model.graph is None:  # the public host call replays the model's CUDA graph
+            self.model.capture()
+        self.model.prefill_host(self.hids, self.hout)
         return (self.hids.numel() * 4, self.hout.numel() * 2)
+
+    def exchange_ms(self, barrier):
+        """Expert parallelism: device time (max over ranks) of one step's
+        all-to-alls alone — per layer the rows and expert ids out and the
+        outputs back, on the model's own fixed-capacity buffers."""
+        if self.world == 1:
+            return None
+        import torch
+        import torch.distributed as dist
+        from burn_rocket_b200.moe_ep import exchange
+        m = self.model
+
+        def step():
+            for _ in range(self.cfg.layers):
+                exchange(m.recv_rows, m.send_rows, None, None, m.group)
+                exchange(m.recv_meta, m.send_meta, None, None, m.group)
+                exchange(m.y_back, m.y_recv, None, None, m.group)
+        step()
+        barrier()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        reps = 3
+        ev[0].record()
+        for _ in range(reps):
+            step()
+        ev[1].record()
+        barrier()
+        t = torch.tensor([ev[0].elapsed_time(ev[1]) / reps], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
 
     def kernel_roofline(self):
         """Device time of one layer's grouped expert GEMMs (gate|up and down);
@@ -883,6 +906,14 @@ def measure_dp_sub(name, dev, flush, stream, args, peaks, peak_kind, world, rank
                    "d2h_bytes_per_step": int(d2h)},
            "gpu_launches": int(launches), "clocks": clocks,
            "timing": "CUDA-graph replay of the step's C-ABI calls" if graphed else "eager launches"}
+    if hasattr(wl, "exchange_ms"):
+        a2a = wl.exchange_ms(barrier)
+        if a2a is not None:
+            rec["alltoall"] = {"ms_per_step": round(a2a, 4), "share_of_step": round(a2a / (ms_max / steps), 4),
+                               "what": "per layer: token rows + expert ids out, expert outputs back "
+                                       f"(NCCL all_to_all_single, fixed capacity {wl.model.capacity} rows "
+                                       "per destination), timed alone"}
+    wl.model.graph = None  # release the graph (NCCL calls inside) before the process group
     del wl
     torch.cuda.empty_cache()
     return rec
@@ -966,6 +997,10 @@ def run_b200(args):
         # config #4's tower, data-parallel over images like the main line (every N)
         line["sub"] = {"siglip": measure_dp_sub("siglip", dev, flush, stream, args, peaks, peak_kind, world, rank,
                                                 barrier, reduce_max)}
+        if world > 1:
+            # config #5's MoE, its experts spread over the N GPUs (expert parallelism)
+            line["sub"]["moe_ep"] = measure_dp_sub("moe", dev, flush, stream, args, peaks, peak_kind, world, rank,
+                                                   barrier, reduce_max)
         if world == 1:
             # the metric's single-op items, each timed alone on this GPU
             for name in SUB_WORKLOADS:

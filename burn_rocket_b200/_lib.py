@@ -107,6 +107,7 @@ SIGNATURES = {
     "rb_matmul_grouped": (_i, [_i64, _i, _p, _i64, _p, _i64, _i, _p, _i, _p]),
     "rb_moe_combine": (_i, [_p, _p, _i64, _p, _p, _p, _i64, _i, _i, _p]),
     "rb_ep_build_send": (_i, [_p, _i64, _i, _i, _i, _p, _i64, _p, _p, _p, _p, _p, _p]),
+    "rb_ep_build_send_capacity": (_i, [_p, _i64, _i, _i, _i, _i64, _p, _i64, _p, _p, _p, _p, _p, _p]),
     "rb_gather_rows": (_i, [_p, _p, _i64, _i64, _p, _p]),
     "rb_moe_combine_rows": (_i, [_p, _p, _i64, _p, _p, _p, _i64, _i, _p]),
 }

@@ -614,10 +614,11 @@ int rb_check_device_errors(void) {
     cudaMemset(e->err, 0, sizeof(uint32_t));
     // An aborted attention launch can leave split-mode counters mid-count.
     if (e->attn_cnt) cudaMemset(e->attn_cnt, 0, kAttnCntBytes);
-    return fail(RB_E_DEVICE, "kernel error word 0x%x (%s%s%s)", word,
+    return fail(RB_E_DEVICE, "kernel error word 0x%x (%s%s%s%s)", word,
                 (word & kErrWaitTimeout) ? "wait-timeout " : "",
                 (word & kErrTmemAlloc) ? "tmem-alloc " : "",
-                (word & kErrBadShape) ? "bad-shape" : "");
+                (word & kErrBadShape) ? "bad-shape " : "",
+                (word & kErrOverflow) ? "exchange-capacity-overflow" : "");
   }
   return RB_OK;
 }
@@ -1454,6 +1455,24 @@ int rb_ep_build_send(const int32_t* ids, int64_t tokens, int top_k, int experts,
                             slot_pos, send_rows_f16, e->err, reinterpret_cast<cudaStream_t>(stream));
   g_launches += 4;
   return rc == RB_OK ? RB_OK : fail(rc, "ep_build_send: experts must divide over ranks, hidden % 8 == 0");
+}
+
+int rb_ep_build_send_capacity(const int32_t* ids, int64_t tokens, int top_k, int experts, int ranks,
+                              int64_t capacity, const void* x_f16, int64_t hidden, int32_t* dest_counts,
+                              int32_t* dest_cursor, int32_t* send_meta, int32_t* slot_pos, void* send_rows_f16,
+                              void* stream) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Engine* e;
+  int rc = ensure_engine(&e);
+  if (rc) return rc;
+  if (!ids || !x_f16 || !dest_counts || !dest_cursor || !send_meta || !slot_pos || !send_rows_f16 || tokens <= 0 ||
+      capacity < 1 || capacity > (1 << 30) / (ranks > 0 ? ranks : 1))
+    return fail(RB_E_SHAPE, "ep_build_send_capacity: bad arguments");
+  rc = launch_ep_build_send_fixed(ids, tokens, top_k, experts, ranks, static_cast<int>(capacity), x_f16, hidden,
+                                  dest_counts, dest_cursor, send_meta, slot_pos, send_rows_f16, e->err,
+                                  reinterpret_cast<cudaStream_t>(stream));
+  g_launches += 4;
+  return rc == RB_OK ? RB_OK : fail(rc, "ep_build_send_capacity: experts must divide over ranks, hidden % 8 == 0");
 }
 
 int rb_gather_rows(const void* in_f16, const int32_t* idx, int64_t n, int64_t hidden, void* out_f16, void* stream) {

@@ -83,6 +83,10 @@ int launch_ep_build_send(const int32_t* ids, int64_t tokens, int top_k, int expe
                          int64_t hidden, int32_t* dest_counts, int32_t* dest_cursor, int32_t* send_meta,
                          int32_t* slot_pos, void* send_rows, uint32_t* err, cudaStream_t st);
 int launch_gather_rows(const void* in, const int32_t* idx, int64_t n, int64_t hidden, void* out, cudaStream_t st);
+int launch_ep_build_send_fixed(const int32_t* ids, int64_t tokens, int top_k, int experts, int ranks, int cap,
+                               const void* x, int64_t hidden, int32_t* dest_counts, int32_t* dest_cursor,
+                               int32_t* send_meta, int32_t* slot_pos, void* send_rows, uint32_t* err,
+                               cudaStream_t st);
 int launch_moe_combine_rows(float* x, const void* y, int64_t hidden, const int32_t* ids, const float* wts,
                             const int32_t* row_of_slot, int64_t tokens, int top_k, cudaStream_t st);
 

@@ -154,6 +154,7 @@ __global__ void moe_count_kernel(const int32_t* __restrict__ ids, int64_t slots,
   slot_chunk(slots, s0, s1);
   for (int64_t s = s0 + threadIdx.x; s < s1; s += blockDim.x) {
     const int e = ids[s];
+    if (e == -1) continue;  // no expert: a padding row of a fixed-capacity exchange
     if (e < 0 || e >= E) {
       atomicOr(err, kErrBadShape);
       continue;
@@ -227,7 +228,10 @@ __global__ void moe_scatter_kernel(const int32_t* __restrict__ ids, int64_t slot
   __syncthreads();
   for (int64_t s = s0 + threadIdx.x; s < s1; s += blockDim.x) {
     const int e = ids[s];
-    if (e < 0 || e >= E) continue;
+    if (e < 0 || e >= E) {
+      row_of_slot[s] = -1;  // no row (a padding slot): gathers and combines skip it
+      continue;
+    }
     const int32_t row = s_base[e] + row_of_slot[s];
     row_of_slot[s] = row;
     token_of_row[row] = static_cast<int32_t>(s / k);
@@ -327,10 +331,12 @@ __global__ void moe_combine_kernel(float* __restrict__ x, const __half* __restri
       uint4 uv[KMAX];
 #pragma unroll
       for (int r = 0; r < KMAX; ++r)  // all of the token's rows in flight
-        if (r < k) uv[r] = __ldg(reinterpret_cast<const uint4*>(y + static_cast<int64_t>(ord_row[r]) * hidden + c));
+        if (r < k && ord_row[r] >= 0)
+          uv[r] = __ldg(reinterpret_cast<const uint4*>(y + static_cast<int64_t>(ord_row[r]) * hidden + c));
 #pragma unroll
       for (int r = 0; r < KMAX; ++r) {
         if (r >= k) break;
+        if (ord_row[r] < 0) continue;  // a slot that overflowed its exchange buffer (flagged)
         const uint4 u = uv[r];
         const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
@@ -415,6 +421,7 @@ __global__ void gather_rows_kernel(const __half* __restrict__ in, const int32_t*
     // inverse: out[i] = in[idx[i]] (gather).
     const int64_t src = inverse ? idx[i] : i / div;
     const int64_t dst = inverse ? i : idx[i];
+    if (src < 0 || dst < 0) continue;  // a padding or overflowed slot: nothing to move
     const uint4* a = reinterpret_cast<const uint4*>(in + src * hidden);
     uint4* b = reinterpret_cast<uint4*>(out + dst * hidden);
 #pragma unroll 8
@@ -436,6 +443,58 @@ int launch_ep_build_send(const int32_t* ids, int64_t tokens, int top_k, int expe
   ep_offsets_kernel<<<1, 32, 0, st>>>(dest_counts, ranks, dest_cursor);
   ep_scatter_kernel<<<static_cast<int>(g), 256, 0, st>>>(ids, slots, top_k, per_rank, dest_cursor, send_meta,
                                                          slot_pos);
+  int64_t gr = (slots + 7) / 8;
+  if (gr > 148 * 16) gr = 148 * 16;
+  gather_rows_kernel<<<static_cast<int>(gr), 256, 0, st>>>(reinterpret_cast<const __half*>(x), slot_pos, top_k,
+                                                           slots, hidden, reinterpret_cast<__half*>(send_rows), 0);
+  return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
+}
+
+// Fixed-capacity form: destination q owns send positions [q*cap, (q+1)*cap),
+// so every all-to-all split is `cap` rows and no count has to reach the host.
+// A slot beyond its destination's capacity is not sent (slot_pos = -1) and
+// flags kErrOverflow; unused positions keep send_meta = -1 (no expert).
+__global__ void ep_offsets_fixed_kernel(const int32_t* __restrict__ dest_counts, int ranks, int cap,
+                                        int32_t* dest_cursor, uint32_t* err) {
+  for (int q = threadIdx.x; q < ranks; q += blockDim.x) {
+    dest_cursor[q] = q * cap;
+    if (dest_counts[q] > cap) atomicOr(err, kErrOverflow);
+  }
+}
+
+__global__ void ep_scatter_fixed_kernel(const int32_t* __restrict__ ids, int64_t slots, int per_rank, int cap,
+                                        int32_t* dest_cursor, int32_t* send_meta, int32_t* slot_pos) {
+  for (int64_t s = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; s < slots;
+       s += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int e = ids[s];
+    const int q = e / per_rank;
+    const int32_t pos = atomicAdd(&dest_cursor[q], 1);
+    if (pos >= (q + 1) * cap) {
+      slot_pos[s] = -1;
+      continue;
+    }
+    send_meta[pos] = e - q * per_rank;
+    slot_pos[s] = pos;
+  }
+}
+
+int launch_ep_build_send_fixed(const int32_t* ids, int64_t tokens, int top_k, int experts, int ranks, int cap,
+                               const void* x, int64_t hidden, int32_t* dest_counts, int32_t* dest_cursor,
+                               int32_t* send_meta, int32_t* slot_pos, void* send_rows, uint32_t* err,
+                               cudaStream_t st) {
+  if (ranks < 1 || experts % ranks || hidden % 8 || cap < 1) return RB_E_SHAPE;
+  const int per_rank = experts / ranks;
+  const int64_t slots = tokens * top_k;
+  if (cudaMemsetAsync(dest_counts, 0, sizeof(int32_t) * ranks, st) != cudaSuccess ||
+      cudaMemsetAsync(send_meta, 0xFF, sizeof(int32_t) * static_cast<size_t>(ranks) * cap, st) != cudaSuccess)
+    return RB_E_DEVICE;
+  int64_t g = (slots + 255) / 256;
+  if (g > 148 * 8) g = 148 * 8;
+  if (g < 1) g = 1;
+  ep_count_kernel<<<static_cast<int>(g), 256, 0, st>>>(ids, slots, per_rank, ranks, dest_counts, err);
+  ep_offsets_fixed_kernel<<<1, 256, 0, st>>>(dest_counts, ranks, cap, dest_cursor, err);
+  ep_scatter_fixed_kernel<<<static_cast<int>(g), 256, 0, st>>>(ids, slots, per_rank, cap, dest_cursor, send_meta,
+                                                               slot_pos);
   int64_t gr = (slots + 7) / 8;
   if (gr > 148 * 16) gr = 148 * 16;
   gather_rows_kernel<<<static_cast<int>(gr), 256, 0, st>>>(reinterpret_cast<const __half*>(x), slot_pos, top_k,

@@ -20,6 +20,7 @@ enum : uint32_t {
   kErrWaitTimeout = 1u << 0,   // an mbarrier wait ran out of iterations
   kErrTmemAlloc   = 1u << 1,   // tcgen05.alloc returned an unusable address
   kErrBadShape    = 1u << 2,   // a device-side shape guard tripped
+  kErrOverflow    = 1u << 3,   // more rows than a fixed-capacity exchange buffer holds
 };
 
 // A wait is declared hung after this much wall time (nanoseconds of the

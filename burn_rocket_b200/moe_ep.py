@@ -10,14 +10,23 @@ blocks (rank r owns experts [r*E/world, (r+1)*E/world)); the dense part
     its k|v columns and the second half runs a causal block mask with query
     offset seq/2 (`attention_causal_block`).
 
-Per layer the routed slots travel to their experts' ranks and back with two
-NCCL all-to-alls of f16 token rows (plus one of the local expert ids and one
-of the per-destination counts, read on the host to size the exchange):
+Per layer the routed slots travel to their experts' ranks and back with NCCL
+all-to-alls of f16 token rows (plus one of the local expert ids):
 
-    route -> rb_ep_build_send -> all_to_all(counts) -> all_to_all(rows, meta)
+    route -> rb_ep_build_send_capacity -> all_to_all(rows, meta)
       -> local grouped expert GEMMs -> all_to_all(outputs back)
       -> rb_moe_combine_rows (ascending expert id per token, as
          src/clef/engine.rs:317-340)
+
+The exchange has a fixed capacity per destination (capacity_factor x the even
+share of the rank's routed slots, default 1.25): every split is `capacity`
+rows, padding rows carry expert id -1 and are skipped, so no count is read on
+the host and the whole forward is captured into one CUDA graph. A routing so
+skewed that a destination receives more than its capacity sets the
+exchange-overflow bit of the device error word (rb_check_device_errors); a
+caller then reruns the step with capacity_factor=None, the exact form that
+reads the per-destination counts on the host every layer and sizes each
+all-to-all to them.
 
 The reference runs every expert on one board (experts streamed from NVMe,
 src/clef/engine.rs:7-19); expert parallelism is new here.
@@ -50,10 +59,13 @@ def ep_plan(world: int, batch: int, seq: int):
 
 
 def exchange(out, inp, out_splits, in_splits, group=None):
-    """all_to_all_single with uneven splits along dim 0 (NCCL for CUDA
-    tensors, gloo for CPU tensors)."""
+    """all_to_all_single along dim 0 (NCCL for CUDA tensors, gloo for CPU
+    tensors): uneven splits, or equal ones when the splits are None."""
     import torch.distributed as dist
-    dist.all_to_all_single(out, inp, list(map(int, out_splits)), list(map(int, in_splits)), group=group)
+    if out_splits is None:
+        dist.all_to_all_single(out, inp, group=group)
+    else:
+        dist.all_to_all_single(out, inp, list(map(int, out_splits)), list(map(int, in_splits)), group=group)
     return out
 
 
@@ -73,12 +85,35 @@ def build_send_np(ids: np.ndarray, experts: int, ranks: int):
     return counts, meta, slot_pos
 
 
+def build_send_fixed_np(ids: np.ndarray, experts: int, ranks: int, capacity: int):
+    """numpy restatement of rb_ep_build_send_capacity with a stable (slot-order)
+    layout: counts [ranks], meta [ranks*capacity] (local expert id, -1 where
+    unused), slot_pos [slots] (send position, -1 for a slot past its
+    destination's capacity) and whether any destination overflowed."""
+    per = experts // ranks
+    flat = ids.reshape(-1)
+    dest = flat // per
+    counts = np.bincount(dest, minlength=ranks).astype(np.int64)
+    meta = np.full(ranks * capacity, -1, np.int64)
+    slot_pos = np.full(flat.size, -1, np.int64)
+    fill = np.zeros(ranks, np.int64)
+    for s in range(flat.size):
+        q = dest[s]
+        if fill[q] < capacity:
+            pos = q * capacity + fill[q]
+            meta[pos] = flat[s] - q * per
+            slot_pos[s] = pos
+        fill[q] += 1
+    return counts, meta, slot_pos, bool((counts > capacity).any())
+
+
 class MoeEPModel:
     """Expert-parallel MoE decoder: this rank's token blocks, all dense
     weights, and its own block of experts (Q8_0)."""
 
     def __init__(self, cfg: MoeConfig, batch: int, seq: int, rank: int, world: int, seed: int = 0,
-                 host_weights: dict | None = None, group=None, pair_groups=None):
+                 host_weights: dict | None = None, group=None, pair_groups=None,
+                 capacity_factor: float | None = 1.25):
         import torch
         self.cfg, self.batch, self.seq, self.rank, self.world = cfg, batch, seq, rank, world
         self.group = group
@@ -152,7 +187,13 @@ class MoeEPModel:
         torch.cuda.synchronize()
         f16 = torch.float16
         S = T * k                      # slots sent by this rank
-        R = batch * seq * k            # upper bound on rows received
+        if capacity_factor is None:    # exact splits, sized on the host every layer
+            self.capacity = None
+            R = batch * seq * k        # upper bound on rows received
+            S_buf = S
+        else:                          # fixed capacity per destination
+            self.capacity = max(8, int(math.ceil(capacity_factor * S / world / 8.0)) * 8)
+            R = S_buf = world * self.capacity
         self.R_cap = R
         self.ids_in = torch.zeros(T, dtype=torch.int32, device=dev)
         self.x = torch.empty(T, h, dtype=torch.float32, device=dev)
@@ -167,13 +208,13 @@ class MoeEPModel:
         self.dest_counts = torch.empty(world, dtype=torch.int32, device=dev)
         self.recv_counts = torch.empty(world, dtype=torch.int32, device=dev)
         self.dest_cursor = torch.empty(world, dtype=torch.int32, device=dev)
-        self.send_meta = torch.empty(S, dtype=torch.int32, device=dev)
+        self.send_meta = torch.empty(S_buf, dtype=torch.int32, device=dev)
         self.slot_pos = torch.empty(S, dtype=torch.int32, device=dev)
-        self.send_rows = torch.empty(S, h, dtype=f16, device=dev)
+        self.send_rows = torch.empty(S_buf, h, dtype=f16, device=dev)
         self.recv_meta = torch.empty(R, dtype=torch.int32, device=dev)
         self.recv_rows = torch.empty(R, h, dtype=f16, device=dev)
         self.y_recv = torch.empty(R, h, dtype=f16, device=dev)
-        self.y_back = torch.empty(S, h, dtype=f16, device=dev)
+        self.y_back = torch.empty(S_buf, h, dtype=f16, device=dev)
         self.max_rows = int(lib.rb_moe_max_rows(R, 1, self.epr))
         self.ws = torch.empty(int(lib.rb_moe_workspace_bytes(R, 1, self.epr)) // 4 + 1, dtype=torch.int32,
                               device=dev)
@@ -183,15 +224,16 @@ class MoeEPModel:
         self.yp = torch.empty(self.max_rows, h, dtype=f16, device=dev)
         self.out = torch.empty(T, h, dtype=f16, device=dev)
         self.exchanged_rows = 0
+        self.graph = None
 
-    def _attention(self, L, lib, qkv_p, ld):
+    def _attention(self, L, lib, qkv_p, ld, st):
         cfg, d, nh, nkv = self.cfg, self.cfg.head_dim, self.cfg.heads, self.cfg.kv_heads
         scale = 1.0 / math.sqrt(d)
         if not self.split:
             b = len(self.blocks)
             _check(lib.rb_attention_batched(qkv_p, ld, qkv_p + nh * d * 2, ld, qkv_p + (nh + nkv) * d * 2, ld,
                                             _dev_ptr(self.attn), nh * d, DTYPE_F16, b, self.seq, self.seq,
-                                            nh, nkv, d, scale, 0.0, MASK_CAUSAL, -1, 0, 0, None),
+                                            nh, nkv, d, scale, 0.0, MASK_CAUSAL, -1, 0, 0, st),
                    "rocket_flash_attn", self.seq, self.seq, d)
             return
         import torch.distributed as dist
@@ -205,15 +247,40 @@ class MoeEPModel:
         n_kv = q_start + half
         _check(lib.rb_attention_batched(qkv_p, ld, kvp, ldkv, kvp + nkv * d * 2, ldkv, _dev_ptr(self.attn), nh * d,
                                         DTYPE_F16, 1, half, n_kv, nh, nkv, d, scale, 0.0, MASK_CAUSAL_BLOCK, -1,
-                                        q_start, 0, None),
+                                        q_start, 0, st),
                "rocket_flash_attn", half, n_kv, d)
 
+    def _experts(self, L, lib, R, st):
+        """Grouped expert GEMMs over R received rows (recv_meta, recv_rows) into
+        y_recv in receive order."""
+        cfg = self.cfg
+        h, I = cfg.hidden, cfg.inter
+        rows = int(lib.rb_moe_max_rows(R, 1, self.epr))
+        ws = _dev_ptr(self.ws)
+        _check(lib.rb_moe_dispatch(_dev_ptr(self.recv_meta), R, 1, self.epr, _dev_ptr(self.recv_rows), h,
+                                   ws, _dev_ptr(self.xp), st), "moe_dispatch")
+        if self.gated:  # silu(gate x) * (up x) straight from the grouped GEMM
+            _check(lib.rb_matmul_grouped(L["gu"].id, self.epr, _dev_ptr(self.xp), rows, ws, R, 1,
+                                         _dev_ptr(self.actp), DTYPE_F16, st), "matmul_grouped")
+        else:
+            _check(lib.rb_matmul_grouped(L["gu"].id, self.epr, _dev_ptr(self.xp), rows, ws, R, 1,
+                                         _dev_ptr(self.gup), DTYPE_F16, st), "matmul_grouped")
+            _check(lib.rb_silu_mul_halves(_dev_ptr(self.gup), rows, I, _dev_ptr(self.actp), st), "silu_mul")
+        _check(lib.rb_matmul_grouped(L["down"].id, self.epr, _dev_ptr(self.actp), rows, ws, R, 1,
+                                     _dev_ptr(self.yp), DTYPE_F16, st), "matmul_grouped")
+        # back to receive order: y_recv[i] = yp[row of received slot i] (padding slots: none)
+        off = int(lib.rb_moe_slot_rows_offset(R, 1, self.epr))
+        _check(lib.rb_gather_rows(_dev_ptr(self.yp), ws + 4 * off, R, h, _dev_ptr(self.y_recv), st),
+               "gather_rows")
+
     def forward_device(self):
-        """One forward over self.ids_in (this rank's tokens) into self.out."""
-        import torch
+        """One forward over self.ids_in (this rank's tokens) into self.out, on
+        the current CUDA stream."""
+        from . import _stream_ptr
         cfg, lib, T = self.cfg, _lib.load(), self.T
-        h, d, nh, nkv, E, I, k = cfg.hidden, cfg.head_dim, cfg.heads, cfg.kv_heads, cfg.experts, cfg.inter, cfg.top_k
+        h, d, nh, nkv, E, k = cfg.hidden, cfg.head_dim, cfg.heads, cfg.kv_heads, cfg.experts, cfg.top_k
         W = self.world
+        st = _stream_ptr(None)
         ld = (nh + 2 * nkv) * d
         qkv_p, xp = _dev_ptr(self.qkv), _dev_ptr(self.x)
         # rope positions of this rank's first row (tables offset by the row within the sequence)
@@ -221,55 +288,83 @@ class MoeEPModel:
         cos_p = _dev_ptr(self.cos) + pos0 * (d // 2) * 4
         sin_p = _dev_ptr(self.sin) + pos0 * (d // 2) * 4
         rope_seq = self.blocks[0][2]
-        _check(lib.rb_embed_gather(_dev_ptr(self.ids_in), T, _dev_ptr(self.embed), cfg.vocab, h, xp, None),
+        _check(lib.rb_embed_gather(_dev_ptr(self.ids_in), T, _dev_ptr(self.embed), cfg.vocab, h, xp, st),
                "embed_gather")
         self.exchanged_rows = 0
         for L in self.layers:
-            _check(lib.rb_add_rms_norm(xp, None, _dev_ptr(L["in_norm"]), cfg.eps, _dev_ptr(self.h), T, h, None),
+            _check(lib.rb_add_rms_norm(xp, None, _dev_ptr(L["in_norm"]), cfg.eps, _dev_ptr(self.h), T, h, st),
                    "add_rms_norm")
             matmul(self.h, L["qkv"], out=self.qkv)
             _check(lib.rb_qk_norm_rope(qkv_p, ld, T, nh, nkv, d, _dev_ptr(L["q_norm"]), _dev_ptr(L["k_norm"]),
-                                       cfg.eps, cos_p, sin_p, rope_seq, None), "qk_norm_rope")
-            self._attention(L, lib, qkv_p, ld)
+                                       cfg.eps, cos_p, sin_p, rope_seq, st), "qk_norm_rope")
+            self._attention(L, lib, qkv_p, ld, st)
             matmul(self.attn, L["o"], out=self.o)
             _check(lib.rb_add_rms_norm(xp, _dev_ptr(self.o), _dev_ptr(L["post_norm"]), cfg.eps, _dev_ptr(self.h),
-                                       T, h, None), "add_rms_norm")
+                                       T, h, st), "add_rms_norm")
             matmul(self.h, L["router"], out=self.logits)
-            _check(lib.rb_moe_route(_dev_ptr(self.logits), T, E, k, 1, _dev_ptr(self.ids), _dev_ptr(self.wts), None),
+            _check(lib.rb_moe_route(_dev_ptr(self.logits), T, E, k, 1, _dev_ptr(self.ids), _dev_ptr(self.wts), st),
                    "moe_route")
-            _check(lib.rb_ep_build_send(_dev_ptr(self.ids), T, k, E, W, _dev_ptr(self.h), h,
-                                        _dev_ptr(self.dest_counts), _dev_ptr(self.dest_cursor),
-                                        _dev_ptr(self.send_meta), _dev_ptr(self.slot_pos),
-                                        _dev_ptr(self.send_rows), None), "ep_build_send")
-            exchange(self.recv_counts, self.dest_counts, [1] * W, [1] * W, self.group)
-            send_splits = self.dest_counts.cpu().tolist()
-            recv_splits = self.recv_counts.cpu().tolist()
-            R = int(sum(recv_splits))
-            self.exchanged_rows += int(sum(send_splits))
-            exchange(self.recv_rows[:R], self.send_rows, recv_splits, send_splits, self.group)
-            exchange(self.recv_meta[:R], self.send_meta, recv_splits, send_splits, self.group)
-            if R > 0:
-                rows = int(lib.rb_moe_max_rows(R, 1, self.epr))
-                ws = _dev_ptr(self.ws)
-                _check(lib.rb_moe_dispatch(_dev_ptr(self.recv_meta), R, 1, self.epr, _dev_ptr(self.recv_rows), h,
-                                           ws, _dev_ptr(self.xp), None), "moe_dispatch")
-                if self.gated:  # silu(gate x) * (up x) straight from the grouped GEMM
-                    _check(lib.rb_matmul_grouped(L["gu"].id, self.epr, _dev_ptr(self.xp), rows, ws, R, 1,
-                                                 _dev_ptr(self.actp), DTYPE_F16, None), "matmul_grouped")
-                else:
-                    _check(lib.rb_matmul_grouped(L["gu"].id, self.epr, _dev_ptr(self.xp), rows, ws, R, 1,
-                                                 _dev_ptr(self.gup), DTYPE_F16, None), "matmul_grouped")
-                    _check(lib.rb_silu_mul_halves(_dev_ptr(self.gup), rows, I, _dev_ptr(self.actp), None),
-                           "silu_mul")
-                _check(lib.rb_matmul_grouped(L["down"].id, self.epr, _dev_ptr(self.actp), rows, ws, R, 1,
-                                             _dev_ptr(self.yp), DTYPE_F16, None), "matmul_grouped")
-                # back to receive order: y_recv[i] = yp[row of received slot i]
-                off = int(lib.rb_moe_slot_rows_offset(R, 1, self.epr))
-                _check(lib.rb_gather_rows(_dev_ptr(self.yp), ws + 4 * off, R, h, _dev_ptr(self.y_recv), None),
-                       "gather_rows")
-            exchange(self.y_back, self.y_recv[:R], send_splits, recv_splits, self.group)
+            if self.capacity is not None:
+                # fixed-capacity exchange: equal splits, nothing read on the host
+                _check(lib.rb_ep_build_send_capacity(_dev_ptr(self.ids), T, k, E, W, self.capacity,
+                                                     _dev_ptr(self.h), h, _dev_ptr(self.dest_counts),
+                                                     _dev_ptr(self.dest_cursor), _dev_ptr(self.send_meta),
+                                                     _dev_ptr(self.slot_pos), _dev_ptr(self.send_rows), st),
+                       "ep_build_send_capacity")
+                exchange(self.recv_rows, self.send_rows, None, None, self.group)
+                exchange(self.recv_meta, self.send_meta, None, None, self.group)
+                self._experts(L, lib, self.R_cap, st)
+                exchange(self.y_back, self.y_recv, None, None, self.group)
+            else:
+                # exact splits: the per-destination counts are read on the host
+                _check(lib.rb_ep_build_send(_dev_ptr(self.ids), T, k, E, W, _dev_ptr(self.h), h,
+                                            _dev_ptr(self.dest_counts), _dev_ptr(self.dest_cursor),
+                                            _dev_ptr(self.send_meta), _dev_ptr(self.slot_pos),
+                                            _dev_ptr(self.send_rows), st), "ep_build_send")
+                exchange(self.recv_counts, self.dest_counts, [1] * W, [1] * W, self.group)
+                send_splits = self.dest_counts.cpu().tolist()
+                recv_splits = self.recv_counts.cpu().tolist()
+                R = int(sum(recv_splits))
+                self.exchanged_rows += int(sum(send_splits))
+                exchange(self.recv_rows[:R], self.send_rows, recv_splits, send_splits, self.group)
+                exchange(self.recv_meta[:R], self.send_meta, recv_splits, send_splits, self.group)
+                if R > 0:
+                    self._experts(L, lib, R, st)
+                exchange(self.y_back, self.y_recv[:R], send_splits, recv_splits, self.group)
             _check(lib.rb_moe_combine_rows(xp, _dev_ptr(self.y_back), h, _dev_ptr(self.ids), _dev_ptr(self.wts),
-                                           _dev_ptr(self.slot_pos), T, k, None), "moe_combine")
-        _check(lib.rb_add_rms_norm(xp, None, _dev_ptr(self.final_norm), cfg.eps, _dev_ptr(self.out), T, h, None),
+                                           _dev_ptr(self.slot_pos), T, k, st), "moe_combine")
+        _check(lib.rb_add_rms_norm(xp, None, _dev_ptr(self.final_norm), cfg.eps, _dev_ptr(self.out), T, h, st),
                "add_rms_norm")
         return self.out
+
+    def capture(self):
+        """Capture forward_device (fixed-capacity exchange) into a CUDA graph,
+        NCCL all-to-alls included, after one eager warm-up."""
+        import torch
+        if self.capacity is None:
+            raise RuntimeError("only the fixed-capacity exchange is graph-capturable")
+        self.forward_device()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, capture_error_mode="thread_local"):
+            self.forward_device()
+        self.graph = g
+        return g
+
+    def run(self):
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self.forward_device()
+        return self.out
+
+    def prefill_host(self, ids_host, out_host=None):
+        """End-to-end call: this rank's host token ids in, its final-normed f16 hidden states out."""
+        import torch
+        self.ids_in.copy_(ids_host, non_blocking=True)
+        self.run()
+        if out_host is None:
+            out_host = torch.empty(self.T, self.cfg.hidden, dtype=torch.float16, pin_memory=True)
+        out_host.copy_(self.out, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        return out_host

@@ -320,7 +320,9 @@ RB_API int rb_moe_route(const float* logits, int64_t tokens, int experts, int to
                         int32_t* ids, float* weights, void* stream);
 /* Buckets the routed slots per expert in `workspace` and gathers each slot's
  * f16 token row x[tokens, hidden] into x_perm[rb_moe_max_rows(), hidden]
- * (256-row-aligned expert segments, padding rows zeroed). */
+ * (256-row-aligned expert segments, padding rows zeroed). An id of -1 means
+ * "no expert" (the padding rows of a fixed-capacity exchange): the slot gets
+ * no row and its slot -> row entry is -1. */
 RB_API int rb_moe_dispatch(const int32_t* ids, int64_t tokens, int top_k, int experts, const void* x_f16,
                            int64_t hidden, void* workspace, void* x_perm_f16, void* stream);
 /* y_perm[r, :] = x_perm[r, :] · W_e^T for the expert e owning row r, where the
@@ -345,7 +347,20 @@ RB_API int rb_moe_combine(float* x, const void* y_perm_f16, int64_t hidden, cons
 RB_API int rb_ep_build_send(const int32_t* ids, int64_t tokens, int top_k, int experts, int ranks,
                             const void* x_f16, int64_t hidden, int32_t* dest_counts, int32_t* dest_cursor,
                             int32_t* send_meta, int32_t* slot_pos, void* send_rows_f16, void* stream);
-/* out[i, :] = in[idx[i], :] for f16 rows. */
+/* rb_ep_build_send with a fixed capacity per destination, so the exchange
+ * needs no counts on the host (equal all-to-all splits of `capacity` rows; a
+ * layer stays graph-capturable): destination q owns send positions
+ * [q*capacity, (q+1)*capacity) of send_rows [ranks*capacity, hidden] and
+ * send_meta [ranks*capacity]; unused positions hold send_meta = -1 (no expert:
+ * rb_moe_dispatch skips such rows, rb_gather_rows skips index -1). A slot past
+ * its destination's capacity is not sent (slot_pos = -1, rb_moe_combine_rows
+ * skips it) and sets the exchange-overflow bit that rb_check_device_errors
+ * reports. dest_counts[ranks] still receives the true rows per destination. */
+RB_API int rb_ep_build_send_capacity(const int32_t* ids, int64_t tokens, int top_k, int experts, int ranks,
+                                     int64_t capacity, const void* x_f16, int64_t hidden, int32_t* dest_counts,
+                                     int32_t* dest_cursor, int32_t* send_meta, int32_t* slot_pos,
+                                     void* send_rows_f16, void* stream);
+/* out[i, :] = in[idx[i], :] for f16 rows (rows with idx[i] < 0 are left as they are). */
 RB_API int rb_gather_rows(const void* in_f16, const int32_t* idx, int64_t n, int64_t hidden, void* out_f16,
                           void* stream);
 /* rb_moe_combine with an explicit slot -> row map (e.g. slot_pos after the

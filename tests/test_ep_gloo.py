@@ -10,7 +10,7 @@ import socket
 import numpy as np
 import pytest
 
-from burn_rocket_b200.moe_ep import build_send_np, ep_plan, exchange
+from burn_rocket_b200.moe_ep import build_send_fixed_np, build_send_np, ep_plan, exchange
 
 E, K, H = 8, 3, 16
 
@@ -106,3 +106,60 @@ def test_build_send_groups_slots_by_destination():
     dest = ids.reshape(-1) // 4
     assert (dest[np.argsort(pos)] == np.sort(dest, kind="stable")).all()
     assert (meta[pos] == ids.reshape(-1) % 4).all()
+
+
+def worker_fixed(rank, world, port, tokens, capacity, q):
+    """The fixed-capacity exchange: equal all-to-all splits of `capacity` rows,
+    padding rows (meta -1) skipped by the experts, slots past the capacity
+    dropped and flagged."""
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        ids, w, x = rank_inputs(rank, tokens[rank])
+        _, meta, slot_pos, overflow = build_send_fixed_np(ids, E, world, capacity)
+        send_rows = np.zeros((world * capacity, H), np.float32)
+        sent = slot_pos >= 0
+        send_rows[slot_pos[sent]] = np.repeat(x, K, axis=0)[sent]
+        recv_rows = torch.empty(world * capacity, H)
+        recv_meta = torch.empty(world * capacity, dtype=torch.int64)
+        exchange(recv_rows, torch.from_numpy(send_rows), None, None)
+        exchange(recv_meta, torch.from_numpy(meta), None, None)
+        rm = recv_meta.numpy()
+        y_recv = np.zeros((world * capacity, H), np.float32)
+        real = rm >= 0
+        y_recv[real] = expert_fn(recv_rows.numpy()[real], rm[real] + rank * (E // world))
+        y_back = torch.empty(world * capacity, H)
+        exchange(y_back, torch.from_numpy(y_recv), None, None)
+        outs_by_slot = np.zeros((ids.size, H), np.float32)
+        outs_by_slot[sent] = y_back.numpy()[slot_pos[sent]]
+        q.put((rank, combine(x, ids, w, outs_by_slot), overflow))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("tokens,capacity", [((37, 29), 64), ((5, 0), 8), ((37, 29), 4)])
+def test_ep_fixed_capacity_exchange(tokens, capacity):
+    """Equal splits of a fixed capacity reproduce the single-process result
+    whenever no destination overflows; an overflow is reported."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=worker_fixed, args=(r, 2, port, tokens, capacity, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict((r, (y, of)) for r, y, of in (q.get(timeout=120) for _ in procs))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in range(2):
+        ids, w, x = rank_inputs(r, tokens[r])
+        y, overflow = got[r]
+        counts = np.bincount(ids.reshape(-1) // (E // 2), minlength=2)
+        assert overflow == bool((counts > capacity).any())
+        if not overflow:
+            want = combine(x, ids, w, expert_fn(np.repeat(x, K, axis=0), ids.reshape(-1).astype(np.float32)))
+            np.testing.assert_allclose(y, want, rtol=1e-6, atol=1e-6)
