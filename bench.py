@@ -621,6 +621,9 @@ class MoeWorkload:
             mine = torch.cat([ids[s * self.SEQ + r0: s * self.SEQ + r0 + n]
                               for s, r0, n in ep_plan(world, self.BATCH, self.SEQ)[rank]])
         self.model.ids_in.copy_(mine.to(dev))
+        if world > 1:
+            # exchange capacity from one exact forward over these inputs (outside any timing)
+            self.model.calibrate_capacity()
         self.hids = mine.pin_memory()
         self.hout = torch.empty(self.model.T, self.cfg.hidden, dtype=torch.float16).pin_memory()
         self.units = self.model.T  # tokens per step on this rank
@@ -646,11 +649,13 @@ class MoeWorkload:
         from burn_rocket_b200.moe_ep import exchange
         m = self.model
 
+        n = self.world * m.capacity
+
         def step():
             for _ in range(self.cfg.layers):
-                exchange(m.recv_rows, m.send_rows, None, None, m.group)
-                exchange(m.recv_meta, m.send_meta, None, None, m.group)
-                exchange(m.y_back, m.y_recv, None, None, m.group)
+                exchange(m.recv_rows[:n], m.send_rows[:n], None, None, m.group)
+                exchange(m.recv_meta[:n], m.send_meta[:n], None, None, m.group)
+                exchange(m.y_back[:n], m.y_recv[:n], None, None, m.group)
         step()
         barrier()
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
@@ -912,7 +917,8 @@ def measure_dp_sub(name, dev, flush, stream, args, peaks, peak_kind, world, rank
             rec["alltoall"] = {"ms_per_step": round(a2a, 4), "share_of_step": round(a2a / (ms_max / steps), 4),
                                "what": "per layer: token rows + expert ids out, expert outputs back "
                                        f"(NCCL all_to_all_single, fixed capacity {wl.model.capacity} rows "
-                                       "per destination), timed alone"}
+                                       f"per destination of the rank's {wl.model.S} routed slots, calibrated "
+                                       "from an exact forward over the inputs), timed alone"}
     wl.model.graph = None  # release the graph (NCCL calls inside) before the process group
     del wl
     torch.cuda.empty_cache()

@@ -19,14 +19,16 @@ all-to-alls of f16 token rows (plus one of the local expert ids):
          src/clef/engine.rs:317-340)
 
 The exchange has a fixed capacity per destination (capacity_factor x the even
-share of the rank's routed slots, default 1.25): every split is `capacity`
-rows, padding rows carry expert id -1 and are skipped, so no count is read on
-the host and the whole forward is captured into one CUDA graph. A routing so
+share of the rank's routed slots, default 1.25, or calibrate_capacity() from
+an exact forward over the actual inputs): every split is `capacity` rows,
+padding rows carry expert id -1 and are skipped, so no count is read on the
+host and the whole forward is captured into one CUDA graph. A routing so
 skewed that a destination receives more than its capacity sets the
 exchange-overflow bit of the device error word (rb_check_device_errors); a
-caller then reruns the step with capacity_factor=None, the exact form that
+caller then reruns the step with capacity_factor=None (the exact form, which
 reads the per-destination counts on the host every layer and sizes each
-all-to-all to them.
+all-to-all to them) or recalibrates. The buffers are sized for the worst case
+(every slot to one destination), so the capacity can change freely.
 
 The reference runs every expert on one board (experts streamed from NVMe,
 src/clef/engine.rs:7-19); expert parallelism is new here.
@@ -187,14 +189,14 @@ class MoeEPModel:
         torch.cuda.synchronize()
         f16 = torch.float16
         S = T * k                      # slots sent by this rank
-        if capacity_factor is None:    # exact splits, sized on the host every layer
-            self.capacity = None
-            R = batch * seq * k        # upper bound on rows received
-            S_buf = S
-        else:                          # fixed capacity per destination
-            self.capacity = max(8, int(math.ceil(capacity_factor * S / world / 8.0)) * 8)
-            R = S_buf = world * self.capacity
+        self.S = S
+        # exchange buffers for the worst case: every slot of every rank to one
+        # destination (world * S rows), whatever the capacity
+        R = S_buf = world * S
+        self.capacity = None if capacity_factor is None else min(
+            S, max(8, int(math.ceil(capacity_factor * S / world / 8.0)) * 8))
         self.R_cap = R
+        self.max_dest = 0  # largest per-destination row count seen by an exact forward
         self.ids_in = torch.zeros(T, dtype=torch.int32, device=dev)
         self.x = torch.empty(T, h, dtype=torch.float32, device=dev)
         self.h = torch.empty(T, h, dtype=f16, device=dev)
@@ -273,10 +275,12 @@ class MoeEPModel:
         _check(lib.rb_gather_rows(_dev_ptr(self.yp), ws + 4 * off, R, h, _dev_ptr(self.y_recv), st),
                "gather_rows")
 
-    def forward_device(self):
+    def forward_device(self, exact: bool = False):
         """One forward over self.ids_in (this rank's tokens) into self.out, on
-        the current CUDA stream."""
+        the current CUDA stream; exact=True (or no capacity set) sizes every
+        all-to-all to the per-destination counts, read on the host."""
         from . import _stream_ptr
+        cap = None if exact else self.capacity
         cfg, lib, T = self.cfg, _lib.load(), self.T
         h, d, nh, nkv, E, k = cfg.hidden, cfg.head_dim, cfg.heads, cfg.kv_heads, cfg.experts, cfg.top_k
         W = self.world
@@ -304,17 +308,18 @@ class MoeEPModel:
             matmul(self.h, L["router"], out=self.logits)
             _check(lib.rb_moe_route(_dev_ptr(self.logits), T, E, k, 1, _dev_ptr(self.ids), _dev_ptr(self.wts), st),
                    "moe_route")
-            if self.capacity is not None:
+            if cap is not None:
                 # fixed-capacity exchange: equal splits, nothing read on the host
-                _check(lib.rb_ep_build_send_capacity(_dev_ptr(self.ids), T, k, E, W, self.capacity,
+                _check(lib.rb_ep_build_send_capacity(_dev_ptr(self.ids), T, k, E, W, cap,
                                                      _dev_ptr(self.h), h, _dev_ptr(self.dest_counts),
                                                      _dev_ptr(self.dest_cursor), _dev_ptr(self.send_meta),
                                                      _dev_ptr(self.slot_pos), _dev_ptr(self.send_rows), st),
                        "ep_build_send_capacity")
-                exchange(self.recv_rows, self.send_rows, None, None, self.group)
-                exchange(self.recv_meta, self.send_meta, None, None, self.group)
-                self._experts(L, lib, self.R_cap, st)
-                exchange(self.y_back, self.y_recv, None, None, self.group)
+                n = W * cap
+                exchange(self.recv_rows[:n], self.send_rows[:n], None, None, self.group)
+                exchange(self.recv_meta[:n], self.send_meta[:n], None, None, self.group)
+                self._experts(L, lib, n, st)
+                exchange(self.y_back[:n], self.y_recv[:n], None, None, self.group)
             else:
                 # exact splits: the per-destination counts are read on the host
                 _check(lib.rb_ep_build_send(_dev_ptr(self.ids), T, k, E, W, _dev_ptr(self.h), h,
@@ -326,16 +331,33 @@ class MoeEPModel:
                 recv_splits = self.recv_counts.cpu().tolist()
                 R = int(sum(recv_splits))
                 self.exchanged_rows += int(sum(send_splits))
-                exchange(self.recv_rows[:R], self.send_rows, recv_splits, send_splits, self.group)
-                exchange(self.recv_meta[:R], self.send_meta, recv_splits, send_splits, self.group)
+                self.max_dest = max(self.max_dest, max(send_splits))
+                S = self.S
+                exchange(self.recv_rows[:R], self.send_rows[:S], recv_splits, send_splits, self.group)
+                exchange(self.recv_meta[:R], self.send_meta[:S], recv_splits, send_splits, self.group)
                 if R > 0:
                     self._experts(L, lib, R, st)
-                exchange(self.y_back, self.y_recv[:R], send_splits, recv_splits, self.group)
+                exchange(self.y_back[:S], self.y_recv[:R], send_splits, recv_splits, self.group)
             _check(lib.rb_moe_combine_rows(xp, _dev_ptr(self.y_back), h, _dev_ptr(self.ids), _dev_ptr(self.wts),
                                            _dev_ptr(self.slot_pos), T, k, st), "moe_combine")
         _check(lib.rb_add_rms_norm(xp, None, _dev_ptr(self.final_norm), cfg.eps, _dev_ptr(self.out), T, h, st),
                "add_rms_norm")
         return self.out
+
+    def calibrate_capacity(self, margin: float = 1.05) -> int:
+        """Set the exchange capacity from an exact forward over the current
+        inputs: the largest per-destination row count over every layer and
+        rank, times `margin`, rounded up to 8 (at most every slot). All ranks
+        call it together and agree on the result."""
+        import torch
+        import torch.distributed as dist
+        self.max_dest = 0
+        self.forward_device(exact=True)
+        t = torch.tensor([self.max_dest], dtype=torch.int64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+        self.capacity = min(self.S, max(8, int(math.ceil(int(t.item()) * margin / 8.0)) * 8))
+        self.graph = None
+        return self.capacity
 
     def capture(self):
         """Capture forward_device (fixed-capacity exchange) into a CUDA graph,

@@ -43,9 +43,12 @@ def main():
     mine = np.concatenate([ids[s * seq + r0: s * seq + r0 + n] for s, r0, n in ep_plan(world, batch, seq)[rank]])
     outs = {}
     # fixed-capacity exchange (no host reads; captured into a CUDA graph) and the exact host-sized splits
-    for mode, factor in (("capacity", 1.25), ("exact", None)):
+    for mode, factor in (("capacity", 1.25), ("exact", None), ("calibrated", 1.25)):
         model = MoeEPModel(cfg, batch, seq, rank, world, host_weights=hw, pair_groups=pairs, capacity_factor=factor)
         model.ids_in.copy_(torch.from_numpy(mine))
+        if mode == "calibrated":
+            cap = model.calibrate_capacity()
+            print(f"rank {rank}: calibrated capacity {cap} of {model.S} slots", flush=True)
         out = model.forward_device().float().clone()
         rb.check_device_errors()
         if factor is not None:
@@ -87,8 +90,9 @@ def main():
                 cos = float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b)))
                 worst = min(worst, cos)
                 print(f"{m} exchange, rank {r}: cosine vs single-GPU {cos:.7f}", flush=True)
-        same = all(torch.equal(gathered["capacity"][r], gathered["exact"][r]) for r in range(world))
-        print(f"capacity == exact exchange: {same}; overflow flagged: {overflow_flagged}", flush=True)
+        same = all(torch.equal(gathered[m][r], gathered["exact"][r]) for m in ("capacity", "calibrated")
+                   for r in range(world))
+        print(f"capacity, calibrated == exact exchange: {same}; overflow flagged: {overflow_flagged}", flush=True)
         status[0] = status[0] * (1.0 if worst >= 0.9999 and same else 0.0)
     dist.all_reduce(status, op=dist.ReduceOp.MIN)
     ok = bool(status.item() == 1.0)
