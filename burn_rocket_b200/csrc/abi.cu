@@ -491,21 +491,22 @@ static int attention_locked(Engine* e, const void* q, int64_t ldq, const void* k
   const int d_stage = head_dim == 72 ? 80 : head_dim;
   const int64_t sq = ldq, sk = ldk, sv = ldv, cq = wq, ck = wk;
   CUtensorMap tm[6];
-  // Q tiles are 128 query rows, K/V tiles 64 keys; 64-element (128-B) column
-  // atoms, plus 16-element (32-B) tail atoms for the 72-wide heads.
+  // Q tiles are 128 query rows, K/V tiles kAttnKeyTile keys; 64-element
+  // (128-B) column atoms, plus 16-element (32-B) tail atoms for the 72-wide heads.
+  constexpr uint32_t kt = kAttnKeyTile;
   if (head_dim == 72) {
     const uint64_t rq = batch * n_q, rk = batch * n_kv;
     if ((rc = make_tmap_heads(&tm[0], qh, rq, n_head, 72, sq, 64, 128, 128)) != RB_OK ||
-        (rc = make_tmap_heads(&tm[1], kh, rk, n_kv_heads, 72, sk, 64, 64, 128)) != RB_OK ||
-        (rc = make_tmap_heads(&tm[2], vh, rk, n_kv_heads, 72, sv, 64, 64, 128)) != RB_OK ||
+        (rc = make_tmap_heads(&tm[1], kh, rk, n_kv_heads, 72, sk, 64, kt, 128)) != RB_OK ||
+        (rc = make_tmap_heads(&tm[2], vh, rk, n_kv_heads, 72, sv, 64, kt, 128)) != RB_OK ||
         (rc = make_tmap_heads(&tm[3], qh, rq, n_head, 72, sq, 16, 128, 32)) != RB_OK ||
-        (rc = make_tmap_heads(&tm[4], kh, rk, n_kv_heads, 72, sk, 16, 64, 32)) != RB_OK ||
-        (rc = make_tmap_heads(&tm[5], vh, rk, n_kv_heads, 72, sv, 16, 64, 32)) != RB_OK)
+        (rc = make_tmap_heads(&tm[4], kh, rk, n_kv_heads, 72, sk, 16, kt, 32)) != RB_OK ||
+        (rc = make_tmap_heads(&tm[5], vh, rk, n_kv_heads, 72, sv, 16, kt, 32)) != RB_OK)
       return rc;
   } else {
     if ((rc = make_tmap_2d(&tm[0], qh, 2, batch * n_q, cq, sq, 64, 128, 128)) != RB_OK) return rc;
-    if ((rc = make_tmap_2d(&tm[1], kh, 2, batch * n_kv, ck, sk, 64, 64, 128)) != RB_OK) return rc;
-    if ((rc = make_tmap_2d(&tm[2], vh, 2, batch * n_kv, ck, sv, 64, 64, 128)) != RB_OK) return rc;
+    if ((rc = make_tmap_2d(&tm[1], kh, 2, batch * n_kv, ck, sk, 64, kt, 128)) != RB_OK) return rc;
+    if ((rc = make_tmap_2d(&tm[2], vh, 2, batch * n_kv, ck, sv, 64, kt, 128)) != RB_OK) return rc;
     tm[3] = tm[0];
     tm[4] = tm[1];
     tm[5] = tm[2];

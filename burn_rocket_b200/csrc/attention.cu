@@ -13,15 +13,19 @@
 //   * GQA: the two slots are two query heads of one KV group (or two query
 //     tiles of one head when the group has a single head), so every K/V tile
 //     is loaded by TMA once and consumed by both slots.
-//   * warp 0: TMA (Q per unit, then 4-stage K and V rings of 64-key tiles,
-//     128-B swizzled); warp 1: UMMA issuer; warps 2-5 / 6-9: softmax of slot 0
-//     / slot 1, one query row per thread (TMEM lane = row).
-//   * TMEM per slot (256 columns): two S buffers of 64 f32 columns and O in D
-//     columns. S(j+1) is computed into the other buffer while the softmax of
-//     tile j runs; P = exp2(S - m) is written back as packed f16/bf16 over the
-//     first 32 columns of its own S buffer and consumed by a TS-form UMMA
-//     (A from TMEM) O += P·V. Per slot the UMMA warp issues P·V(j) and then
-//     S(j+2) into the same buffer.
+//   * warp 0: TMA (Q per unit, then K and V rings of 128-key tiles, 128-B
+//     swizzled); warp 1: UMMA issuer; warps 2-5 / 6-9: softmax of slot 0 /
+//     slot 1, one query row per thread (TMEM lane = row).
+//   * TMEM per slot (256 columns): S, a 128 x 128 f32 score tile (M=128,
+//     N=128 UMMAs: the shape that runs the tensor pipe at its full rate from
+//     shared-memory operands), and O in D columns. P = exp2(S - m) is written
+//     back as packed f16/bf16 over the first 64 columns of S and consumed by a
+//     TS-form UMMA (A from TMEM) O += P·V.
+//   * One S buffer per slot, the two slots in ping-pong: per key tile the
+//     UMMA warp issues slot 0's P·V(j) and S(j+1), then slot 1's, so the
+//     tensor pipe works on one slot while the other slot's softmax runs. A
+//     slot's S(j+1) is issued behind its own P·V(j), so its commit also
+//     retires P·V(j): the softmax may rescale O without a separate wait.
 //   * Schedules: one CTA per unit, or (split) one CTA per SM over an equal
 //     share of all units' key tiles, units cut at share boundaries being
 //     merged by whichever part finishes last (see launch_attention).
@@ -33,9 +37,10 @@
 //     clamp (any row with a visible key scoring above ~-29900), every clamped
 //     or masked key underflows to 0 either way, and the warp takes the fast
 //     path (one FFMA + one MUFU ex2 per score).
-//   * Causal / window / block masks: key tiles wholly outside a slot's visible
-//     band are skipped; tiles wholly inside skip the predicate; a slot that
-//     may contain a fully masked row iterates every key tile.
+//   * Causal / window / block masks: the visible keys of a row form one
+//     interval; key tiles wholly outside a slot's visible band are skipped,
+//     tiles wholly inside skip the predicate, and a slot that may contain a
+//     fully masked row iterates every key tile.
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -54,8 +59,10 @@ namespace rb {
 namespace attn {
 
 constexpr int BM = 128;      // query rows per slot
-constexpr int BN = 64;       // keys per tile
-constexpr int KV_STAGES = 4;
+constexpr int BN = kAttnKeyTile;    // keys per tile (128)
+#ifndef RB_ATTN_POLY_EVERY
+#define RB_ATTN_POLY_EVERY 4  // every 4th pair of scores: exp2 by polynomial
+#endif
 constexpr int kSoftWarp0 = 2;       // warps 2-5: slot 0, warps 6-9: slot 1
 constexpr int kThreads = 10 * 32;   // 3 warps on some SM sub-partitions: 168 registers a thread
 constexpr float kLog2e = 1.4426950408889634f;
@@ -66,13 +73,13 @@ constexpr float kFastMargin = 160.0f;   // exp2(-160) underflows f32 to 0
 constexpr int kNoBound = 1 << 30;
 constexpr int kMaxCtas = kAttnMaxCtas;  // split-mode grid bound (>= SM count)
 // Split-mode planning: each unit is charged kItemCost key tiles on top of
-// its own when the shares are cut (one tile ~ 1.25 us of a CTA's time).
-constexpr int kItemCost = 6;
+// its own when the shares are cut (one 128-key tile ~ 1.2 us of a CTA's time).
+constexpr int kItemCost = 3;
 // Schedule choice, in key tiles, fitted to measured runs (config #2 both
 // masks, 64 x 512 and 4 x 2048 token batches, 16 x 2394 at head_dim 72):
-constexpr double kCtaTime = 5.0;    // one CTA per unit: a CTA's launch, prologue and epilogue
-constexpr double kItemTime = 3.0;   // split: one more item in a CTA's walk
-constexpr double kMergeTime = 10.0; // split: a CTA's partial records and merges
+constexpr double kCtaTime = 2.5;    // one CTA per unit: a CTA's launch, prologue and epilogue
+constexpr double kItemTime = 1.5;   // split: one more item in a CTA's walk
+constexpr double kMergeTime = 5.0;  // split: a CTA's partial records and merges
 
 std::atomic<int> g_split_policy{RB_ATTN_SPLIT_AUTO};
 
@@ -119,23 +126,60 @@ struct Smem {
   static constexpr int TAIL = D % 64;               // 0 or 16 columns (32-B rows)
   static_assert(TAIL == 0 || TAIL == 16, "head width must be 64k or 64k+16");
   static constexpr int Q_ATOM = BM * 128;           // 16 KB
-  static constexpr int KV_ATOM = BN * 128;          // 8 KB
+  static constexpr int KV_ATOM = BN * 128;          // 16 KB
   static constexpr int Q_TAIL_OFF = ATOMS * Q_ATOM;
   static constexpr int KV_TAIL_OFF = ATOMS * KV_ATOM;
   static constexpr int Q_TILE = ATOMS * Q_ATOM + BM * TAIL * 2;
   static constexpr int KV_TILE = ATOMS * KV_ATOM + BN * TAIL * 2;
   static_assert(Q_TILE % 1024 == 0 && KV_TILE % 1024 == 0, "tiles keep 1024-B alignment");
+  // K and V rings fill what the two Q tiles leave of the 227 KB (D = 128:
+  // 3 K + 2 V stages; narrower heads: 4 + 4).
+  static constexpr int FREE = 232448 - 512 - 1024 - 2 * Q_TILE;
+  static constexpr int NKV = FREE / KV_TILE;
+  static constexpr int V_STAGES = NKV / 2 > 4 ? 4 : NKV / 2;
+  static constexpr int K_STAGES = NKV - V_STAGES > 4 ? 4 : NKV - V_STAGES;
+  static_assert(K_STAGES >= 2 && V_STAGES >= 2, "K/V double buffering");
   static constexpr int Q_OFF = 0;                   // 2 slots
   static constexpr int K_OFF = 2 * Q_TILE;
-  static constexpr int V_OFF = K_OFF + KV_STAGES * KV_TILE;
-  static constexpr int BAR_OFF = V_OFF + KV_STAGES * KV_TILE;
+  static constexpr int V_OFF = K_OFF + K_STAGES * KV_TILE;
+  static constexpr int BAR_OFF = V_OFF + V_STAGES * KV_TILE;
   static constexpr int BYTES = BAR_OFF + 512 + 1024;
+  static_assert(BYTES <= 232448, "shared memory budget");
 };
 
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// exp2 of a pair of scores on the FMA/ALU pipes, used for every
+// kPolyEvery-th pair of the unmasked fast path so that the MUFU pipe (one
+// ex2 per score otherwise, 16 a clock per SM: as many cycles per key tile as
+// the tile's UMMAs at head_dim 128) does not bound the softmax. Range
+// reduction y = j + f with j = floor(y): 1.5 * 2^23 + y rounded toward -inf
+// is exact and holds j in its low mantissa bits, whose shift by 23 adds j to
+// the exponent field. 2^f on [0, 1) is a degree-3 polynomial fitted for the
+// least maximum relative error (Lawson's iteratively reweighted least
+// squares): 7.5e-5 relative, below half an ulp of the f16 P it becomes. y is
+// clamped at -126: smaller scores round to 0 in an f16/bf16 P either way.
+constexpr int kPolyEvery = RB_ATTN_POLY_EVERY;
+constexpr float kPolyC0 = 0.9999251365661621f, kPolyC1 = 0.6958339810371399f,
+                kPolyC2 = 0.22606706619262695f, kPolyC3 = 0.07802402973175049f;
+
+__device__ __forceinline__ void exp2_poly2(float y0, float y1, float& p0, float& p1) {
+  const uint64_t y = f2_pack(fmaxf(y0, -126.0f), fmaxf(y1, -126.0f));
+  const uint64_t t = f2_add_rm(y, f2_pack(12582912.0f, 12582912.0f));
+  const uint64_t j = f2_add(t, f2_pack(-12582912.0f, -12582912.0f));  // floor(y), exact
+  const uint64_t f = f2_fma(j, f2_pack(-1.0f, -1.0f), y);              // y - floor(y), exact
+  uint64_t q = f2_fma(f2_pack(kPolyC3, kPolyC3), f, f2_pack(kPolyC2, kPolyC2));
+  q = f2_fma(q, f, f2_pack(kPolyC1, kPolyC1));
+  q = f2_fma(q, f, f2_pack(kPolyC0, kPolyC0));
+  float q0, q1, t0, t1;
+  f2_unpack(q, q0, q1);
+  f2_unpack(t, t0, t1);
+  p0 = __uint_as_float(__float_as_uint(q0) + (__float_as_uint(t0) << 23));
+  p1 = __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23));
 }
 
 __device__ __forceinline__ float max3(float a, float b, float c) {
@@ -334,20 +378,21 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             const __grid_constant__ CUtensorMap tmKt, const __grid_constant__ CUtensorMap tmVt,
             Params p, const __grid_constant__ SplitPlan plan) {
   using L = Smem<D>;
+  constexpr int KS = L::K_STAGES, VS = L::V_STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::BAR_OFF);
   uint64_t* q_full = bars;                      // [1]
-  uint64_t* k_full = bars + 1;                  // [KV_STAGES]
-  uint64_t* k_empty = k_full + KV_STAGES;       // [KV_STAGES]
-  uint64_t* v_full = k_empty + KV_STAGES;       // [KV_STAGES]
-  uint64_t* v_empty = v_full + KV_STAGES;       // [KV_STAGES]
-  uint64_t* s_full = v_empty + KV_STAGES;       // [slot][buf]
-  uint64_t* p_full = s_full + 4;                // [slot][buf]
-  uint64_t* o_done = p_full + 4;                // [slot]
-  uint64_t* q_empty = o_done + 2;               // [1]
-  uint64_t* o_free = q_empty + 1;               // [slot]
+  uint64_t* q_empty = q_full + 1;               // [1]
+  uint64_t* k_full = q_empty + 1;               // [KS]
+  uint64_t* k_empty = k_full + KS;              // [KS]
+  uint64_t* v_full = k_empty + KS;              // [VS]
+  uint64_t* v_empty = v_full + VS;              // [VS]
+  uint64_t* s_full = v_empty + VS;              // [slot] S of the slot's next tile is in TMEM
+  uint64_t* p_full = s_full + 2;                // [slot] P is in TMEM (4 softmax warps)
+  uint64_t* o_done = p_full + 2;                // [slot] a P·V retired
+  uint64_t* o_free = o_done + 2;                // [slot] the item's O was read out
   uint64_t* pub_bar = o_free + 2;               // [slot] a split part's record is written
   uint64_t* dec_bar = pub_bar + 2;              // [slot] the last-arriver decision is made
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dec_bar + 2);
@@ -360,17 +405,17 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     mbar_init(q_empty, 1);
-    for (int i = 0; i < KV_STAGES; ++i) {
+    for (int i = 0; i < KS; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < VS; ++i) {
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
     }
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);
-    }
-    for (int i = 0; i < 2; ++i) {
       mbar_init(&o_done[i], 1);
       mbar_init(&o_free[i], 4);
       mbar_init(&pub_bar[i], 4);
@@ -404,7 +449,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         if (h3) tma_load_3d(dst, map, bar, col, head, row);
         else tma_load_2d(dst, map, bar, head * D + col, row);
       };
-      int kv_it = 0;  // K/V ring position, continued across items
+      int kv_base = 0;  // ring position of the item's first tile, continued across items
       bool ok = true;
       for (int k = 0; ok && w.template next<SPLIT>(p, item); ++k) {
         const Unit& U = item.U;
@@ -421,26 +466,33 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             load(smem + L::Q_OFF + s * L::Q_TILE + L::Q_TAIL_OFF, &tmQt, q_full, U.sl[s].head, L::ATOMS * 64,
                  q_row0 + U.sl[s].qt * BM);
         }
-        for (int j = item.ja; j <= item.jb; ++j, ++kv_it) {
-          const int st = kv_it % KV_STAGES;
-          const uint32_t ph = ((kv_it / KV_STAGES) & 1) ^ 1;
-          if (!mbar_wait(&k_empty[st], ph, p.err, abort_flag)) { ok = false; break; }
-          mbar_arrive_expect_tx(&k_full[st], L::KV_TILE);
+        // K tile j at ring position kv_base + j - ja of the K ring, V tile j
+        // at the same position of the V ring.
+        auto load_kv = [&](bool is_k, int j) -> bool {
+          const int pos = kv_base + j - item.ja;
+          const int nst = is_k ? KS : VS;
+          const int st = pos % nst;
+          const uint32_t ph = ((pos / nst) & 1) ^ 1;
+          uint64_t* empty = is_k ? &k_empty[st] : &v_empty[st];
+          uint64_t* full = is_k ? &k_full[st] : &v_full[st];
+          if (!mbar_wait(empty, ph, p.err, abort_flag)) return false;
+          mbar_arrive_expect_tx(full, L::KV_TILE);
+          uint8_t* dst = smem + (is_k ? L::K_OFF : L::V_OFF) + st * L::KV_TILE;
+          const CUtensorMap* map = is_k ? &tmK : &tmV;
           for (int a = 0; a < L::ATOMS; ++a)
-            load(smem + L::K_OFF + st * L::KV_TILE + a * L::KV_ATOM, &tmK, &k_full[st], U.g, a * 64,
-                 kv_row0 + j * BN);
+            load(dst + a * L::KV_ATOM, map, full, U.g, a * 64, kv_row0 + j * BN);
           if (L::TAIL)
-            load(smem + L::K_OFF + st * L::KV_TILE + L::KV_TAIL_OFF, &tmKt, &k_full[st], U.g, L::ATOMS * 64,
-                 kv_row0 + j * BN);
-          if (!mbar_wait(&v_empty[st], ph, p.err, abort_flag)) { ok = false; break; }
-          mbar_arrive_expect_tx(&v_full[st], L::KV_TILE);
-          for (int a = 0; a < L::ATOMS; ++a)
-            load(smem + L::V_OFF + st * L::KV_TILE + a * L::KV_ATOM, &tmV, &v_full[st], U.g, a * 64,
-                 kv_row0 + j * BN);
-          if (L::TAIL)
-            load(smem + L::V_OFF + st * L::KV_TILE + L::KV_TAIL_OFF, &tmVt, &v_full[st], U.g, L::ATOMS * 64,
-                 kv_row0 + j * BN);
+            load(dst + L::KV_TAIL_OFF, is_k ? &tmKt : &tmVt, full, U.g, L::ATOMS * 64, kv_row0 + j * BN);
+          return true;
+        };
+        // K runs one tile ahead of V: the UMMA warp issues S(j+1) right
+        // behind P·V(j).
+        ok = load_kv(true, item.ja);
+        for (int j = item.ja; ok && j <= item.jb; ++j) {
+          if (j + 1 <= item.jb && !(ok = load_kv(true, j + 1))) break;
+          ok = load_kv(false, j);
         }
+        kv_base += item.jb - item.ja + 1;
       }
     }
   } else if (warp == 1) {
@@ -452,7 +504,6 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       const uint32_t q_addr = smem_u32(smem + L::Q_OFF);
       const uint32_t k_addr = smem_u32(smem + L::K_OFF);
       const uint32_t v_addr = smem_u32(smem + L::V_OFF);
-      int n_s[2] = {0, 0};    // S tiles issued per slot (all items)
       // Base descriptors; each UMMA advances them by a constant byte offset.
       const uint64_t q_desc = desc_kmajor_sw128(q_addr), k_desc = desc_kmajor_sw128(k_addr);
       const uint64_t v_desc = desc_mnmajor_sw128(v_addr, L::KV_ATOM, 1024);
@@ -460,7 +511,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       const uint64_t vt_desc = desc_mnmajor_sw32(v_addr);
       int n_pv[2] = {0, 0};   // P·V issued per slot (all items)
       int n_out[2] = {0, 0};  // items whose O the slot's softmax warps have taken out
-      int kv_base = 0;        // K/V ring position of the item's first tile
+      int kv_base = 0;        // ring position of the item's first tile
       bool ok = true;
       for (int k = 0; ok && w.template next<SPLIT>(p, item); ++k) {
         int rlo[2], rhi[2];
@@ -471,16 +522,14 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         }
         bool first_pv[2] = {true, true};
         ok = mbar_wait(q_full, k & 1, p.err, abort_flag);
-        auto stage_of = [&](int j) { return (kv_base + j - item.ja) % KV_STAGES; };
-        auto phase_of = [&](int j) { return static_cast<uint32_t>(((kv_base + j - item.ja) / KV_STAGES) & 1); };
-        // S = Q K_j^T of slot s into its next S buffer. The buffer last held
-        // P(j-2), read by this slot's P·V(j-2), which this thread issued
+        auto pos_of = [&](int j) { return kv_base + j - item.ja; };
+        // S = Q K_j^T of slot s into the slot's S columns. They last held
+        // P(j-1), read by this slot's P·V(j-1), which this thread issued
         // earlier: UMMAs issued by one thread execute in issue order, so the
         // overwrite needs no wait.
         auto issue_s = [&](int j, int s) {
-          const uint32_t st = stage_of(j);
-          const int b = n_s[s] & 1;
-          const uint32_t d_tmem = tmem_base + s * 256 + b * 64;
+          const uint32_t st = pos_of(j) % KS;
+          const uint32_t d_tmem = tmem_base + s * 256;
 #pragma unroll
           for (int ks = 0; ks < L::ATOMS * 4; ++ks) {
             const uint32_t qo = (ks >> 2) * L::Q_ATOM + (ks & 3) * 32;
@@ -492,98 +541,68 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             umma_f16_ss(d_tmem, desc_add(qt_desc, s * L::Q_TILE + L::Q_TAIL_OFF),
                         desc_add(kt_desc, st * L::KV_TILE + L::KV_TAIL_OFF), idesc_s, 1u);
           }
-          umma_commit(&s_full[2 * s + b]);
-          ++n_s[s];
+          umma_commit(&s_full[s]);
         };
-        // After the last S that reads K tile j: release its stage (and Q after
-        // the item's last tile).
-        auto release_k = [&](int j) {
-          umma_commit(&k_empty[stage_of(j)]);
+        int k_ready = item.ja - 1;  // last key tile whose K load has been awaited
+        auto wait_k = [&](int j) -> bool {
+          if (j <= k_ready) return true;
+          if (!mbar_wait(&k_full[pos_of(j) % KS], (pos_of(j) / KS) & 1, p.err, abort_flag)) return false;
+          tc_fence_after();
+          k_ready = j;
+          return true;
+        };
+        for (int j = item.ja; ok && j <= item.jb; ++j) {
+          // S(j) of the slots whose range starts at tile j (the others' S(j)
+          // went out behind their P·V(j-1)).
+          for (int s = 0; ok && s < 2; ++s)
+            if (rlo[s] <= rhi[s] && rlo[s] == j && (ok = wait_k(j))) issue_s(j, s);
+          // Every S that reads K tile j is issued: hand its stage back (the
+          // load is awaited first even when no slot reads the tile), and Q
+          // after the item's last tile.
+          if (!ok || !(ok = wait_k(j))) break;
+          umma_commit(&k_empty[pos_of(j) % KS]);
           if (j == item.jb) umma_commit(q_empty);
-        };
-        // Both slots' S for tile j (the item's first two tiles).
-        auto issue_s_tile = [&](int j) -> bool {
-          if (!mbar_wait(&k_full[stage_of(j)], phase_of(j), p.err, abort_flag)) return false;
-          tc_fence_after();
-          for (int s = 0; s < 2; ++s)
-            if (rlo[s] <= j && j <= rhi[s]) issue_s(j, s);
-          release_k(j);
-          return true;
-        };
-        // Tile j: each slot's O += P_j V_j as soon as its P is ready, then the
-        // same slot's S for tile j + 2, so that one slot's late softmax does
-        // not hold back the other's next scores.
-        auto issue_tile = [&](int j) -> bool {
-          const uint32_t st = stage_of(j);
-          if (!mbar_wait(&v_full[st], phase_of(j), p.err, abort_flag)) return false;
-          tc_fence_after();
-          const int j2 = j + 2;
-          bool k2_ready = false;
-          // Each slot's P·V(j), then its S(j + 2), in the order the two
-          // slots' P(j) become ready (polled), so a slot whose softmax ends
-          // first is not held behind the other.
-          bool pend[2] = {true, true};
-          const uint64_t t0 = global_timer_ns();
-          for (uint32_t spin = 1; pend[0] || pend[1]; ++spin) {
-            for (int s = 0; s < 2; ++s) {
-              if (!pend[s]) continue;
-              const bool has = rlo[s] <= j && j <= rhi[s];
-              if (has) {
-                if (!mbar_test(&p_full[2 * s + (n_pv[s] & 1)], (n_pv[s] >> 1) & 1)) continue;
-                tc_fence_after();
-                if (first_pv[s] && n_out[s] > 0) {
-                  // O is overwritten: the previous item's O must have been read out.
-                  if (!mbar_wait(&o_free[s], (n_out[s] - 1) & 1, p.err, abort_flag)) return false;
-                  tc_fence_after();
-                }
-                const int b = n_pv[s] & 1;
-                const uint32_t o_tmem = tmem_base + s * 256 + 128;
-                const uint32_t p_tmem = tmem_base + s * 256 + b * 64;
+          // Per slot, in ping-pong order: O += P_j V_j as soon as the slot's
+          // P is in TMEM, then the slot's S(j+1).
+          const uint32_t vs = pos_of(j) % VS;
+          bool v_ready = false;
+          for (int s = 0; ok && s < 2; ++s) {
+            if (!(rlo[s] <= j && j <= rhi[s])) continue;
+            if (!(ok = mbar_wait(&p_full[s], n_pv[s] & 1, p.err, abort_flag))) break;
+            tc_fence_after();
+            if (first_pv[s] && n_out[s] > 0) {
+              // O is overwritten: the previous item's O must have been read out.
+              if (!(ok = mbar_wait(&o_free[s], (n_out[s] - 1) & 1, p.err, abort_flag))) break;
+              tc_fence_after();
+            }
+            if (!v_ready) {
+              if (!(ok = mbar_wait(&v_full[vs], (pos_of(j) / VS) & 1, p.err, abort_flag))) break;
+              tc_fence_after();
+              v_ready = true;
+            }
+            const uint32_t o_tmem = tmem_base + s * 256 + 128;
+            const uint32_t p_tmem = tmem_base + s * 256;
 #pragma unroll
-                for (int ks = 0; ks < BN / 16; ++ks) {
-                  const uint32_t acc = (!first_pv[s] || ks > 0) ? 1u : 0u;
-                  const uint64_t vd = desc_add(v_desc, st * L::KV_TILE + ks * 2048);
-                  umma_f16_ts(o_tmem, p_tmem + ks * 8, vd, idesc_o, acc);
-                  if (L::TAIL) {  // O columns [64*ATOMS, D) from the tail atom (16 key rows = 512 B)
-                    const uint64_t vt = desc_add(vt_desc, st * L::KV_TILE + L::KV_TAIL_OFF + ks * 512);
-                    umma_f16_ts(o_tmem + L::ATOMS * 64, p_tmem + ks * 8, vt, idesc_ot, acc);
-                  }
-                }
-                umma_commit(&o_done[s]);
-                ++n_pv[s];
-                first_pv[s] = false;
-              }
-              if (j2 <= item.jb && rlo[s] <= j2 && j2 <= rhi[s]) {
-                if (!k2_ready) {
-                  if (!mbar_wait(&k_full[stage_of(j2)], phase_of(j2), p.err, abort_flag)) return false;
-                  tc_fence_after();
-                  k2_ready = true;
-                }
-                issue_s(j2, s);
-              }
-              pend[s] = false;
-            }
-            if ((spin & 255u) == 0 && (pend[0] || pend[1])) {  // bounded like every other wait
-              if (*abort_flag) return false;
-              if (global_timer_ns() - t0 > kWaitLimitNs) {
-                *abort_flag = 1;
-                atomicOr(p.err, kErrWaitTimeout);
-                return false;
+            for (int ks = 0; ks < BN / 16; ++ks) {
+              const uint32_t acc = (!first_pv[s] || ks > 0) ? 1u : 0u;
+              const uint64_t vd = desc_add(v_desc, vs * L::KV_TILE + ks * 2048);
+              umma_f16_ts(o_tmem, p_tmem + ks * 8, vd, idesc_o, acc);
+              if (L::TAIL) {  // O columns [64*ATOMS, D) from the tail atom (16 key rows = 512 B)
+                const uint64_t vt = desc_add(vt_desc, vs * L::KV_TILE + L::KV_TAIL_OFF + ks * 512);
+                umma_f16_ts(o_tmem + L::ATOMS * 64, p_tmem + ks * 8, vt, idesc_ot, acc);
               }
             }
+            umma_commit(&o_done[s]);
+            ++n_pv[s];
+            first_pv[s] = false;
+            if (j + 1 <= rhi[s] && (ok = wait_k(j + 1))) issue_s(j + 1, s);
           }
-          umma_commit(&v_empty[st]);
-          if (j2 <= item.jb) {
-            // A tile neither slot reads still has its load awaited before
-            // the stage is handed back.
-            if (!k2_ready && !mbar_wait(&k_full[stage_of(j2)], phase_of(j2), p.err, abort_flag)) return false;
-            release_k(j2);
-          }
-          return true;
-        };
-        if (ok) ok = issue_s_tile(item.ja);
-        if (ok && item.ja + 1 <= item.jb) ok = issue_s_tile(item.ja + 1);
-        for (int j = item.ja; ok && j <= item.jb; ++j) ok = issue_tile(j);
+          if (!ok) break;
+          // A tile neither slot reads still has its load awaited before the
+          // stage is handed back.
+          if (!v_ready && !(ok = mbar_wait(&v_full[vs], (pos_of(j) / VS) & 1, p.err, abort_flag))) break;
+          umma_commit(&v_empty[vs]);
+        }
         for (int s = 0; s < 2; ++s)
           if (rlo[s] <= rhi[s]) ++n_out[s];
         kv_base += item.jb - item.ja + 1;
@@ -595,8 +614,9 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
     const int quarter = warp & 3;  // TMEM lanes 32*(warp % 4): each slot's four warps cover all 128
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+    const uint32_t s_col = s * 256;
     const uint32_t o_col = s * 256 + 128;
-    int it = 0;      // tiles this slot has processed (all items): S buffer / barrier phases
+    int it = 0;      // tiles this slot has processed (all items): barrier phases
     int n_part = 0;  // split parts this slot has published
     bool ok = true;
     while (ok && w.template next<SPLIT>(p, item)) {
@@ -609,23 +629,25 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
       float m_used = -INFINITY, l = 0.0f;
       for (int j = lo; j <= hi; ++j, ++it) {
         const bool first_tile = j == lo;
-        const int b = it & 1;
-        const uint32_t s_col = s * 256 + b * 64;
-        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[2 * s + b], (it >> 1) & 1, p.err, abort_flag))) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&s_full[s], it & 1, p.err, abort_flag))) {
           ok = false;
           break;
         }
         tc_fence_after();
         float x[BN];
         {
-          uint32_t r0[32], r1[32];
+          uint32_t r0[32], r1[32], r2[32], r3[32];
           tmem_ld32(lane_base + s_col, r0);
           tmem_ld32(lane_base + s_col + 32, r1);
+          tmem_ld32(lane_base + s_col + 64, r2);
+          tmem_ld32(lane_base + s_col + 96, r3);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             x[i] = __uint_as_float(r0[i]);
             x[32 + i] = __uint_as_float(r1[i]);
+            x[64 + i] = __uint_as_float(r2[i]);
+            x[96 + i] = __uint_as_float(r3[i]);
           }
         }
         if (SOFTCAP) {
@@ -642,32 +664,34 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         const bool interior = (kvalid >= BN) &&
             (p.dlo <= -kNoBound || ka0 - qa_max >= p.dlo) &&
             (p.dhi >= kNoBound || ka0 + BN - 1 - qa_min <= p.dhi);
-        // Visibility bitmask of this row's 64 keys (all ones on interior tiles).
-        uint64_t vis = ~0ull, real = ~0ull;
+        // This row's visible keys in the tile: the band's interval [vlo, vhi]
+        // cut to the real keys [0, rlast] (everything on interior tiles).
+        const int rlast = (kvalid < BN ? kvalid : BN) - 1;
+        int vlo = 0, vhi = BN - 1;
         if (!interior) {
-          vis = 0;
-          real = 0;
-#pragma unroll
-          for (int i = 0; i < BN; ++i) {
-            const int d = ka0 + i - qa;
-            const bool r_ = i < kvalid;
-            const bool v_ = r_ && (p.dlo <= -kNoBound || d >= p.dlo) && (p.dhi >= kNoBound || d <= p.dhi);
-            vis |= static_cast<uint64_t>(v_) << i;
-            real |= static_cast<uint64_t>(r_) << i;
-          }
+          const long a = static_cast<long>(qa) + p.dlo - ka0, b = static_cast<long>(qa) + p.dhi - ka0;
+          vlo = p.dlo <= -kNoBound ? 0 : static_cast<int>(a < 0 ? 0 : (a > BN ? BN : a));
+          vhi = p.dhi >= kNoBound ? rlast : static_cast<int>(b > rlast ? rlast : (b < -1 ? -1 : b));
         }
         // Tile max in log2 units: max over visible of s*c, floored at the clamp
         // (masked real keys score exactly the clamp).
-        float mraw = -INFINITY;
+        float mraw;
         if (interior) {
+          float m0 = -INFINITY, m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
 #pragma unroll
-          for (int i = 0; i < BN; i += 2) mraw = max3(mraw, x[i], x[i + 1]);
+          for (int i = 0; i < BN; i += 8) {
+            m0 = max3(m0, x[i], x[i + 1]);
+            m1 = max3(m1, x[i + 2], x[i + 3]);
+            m2 = max3(m2, x[i + 4], x[i + 5]);
+            m3 = max3(m3, x[i + 6], x[i + 7]);
+          }
+          mraw = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
         } else {
+          mraw = -INFINITY;
 #pragma unroll
-          for (int i = 0; i < BN; ++i) mraw = fmaxf(mraw, ((vis >> i) & 1) ? x[i] : -INFINITY);
+          for (int i = 0; i < BN; ++i) mraw = fmaxf(mraw, (i >= vlo && i <= vhi) ? x[i] : -INFINITY);
         }
-        float mt = mraw * p.scale_log2;
-        if (real != vis || mt < kClamp2) mt = fmaxf(mt, kClamp2);
+        const float mt = fmaxf(mraw * p.scale_log2, kClamp2);
         // Lazy rescale of the exponent base.
         float alpha = 1.0f;
         bool need = false;
@@ -680,57 +704,60 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
         }
         const bool fast = __all_sync(0xffffffffu, m_used >= kClamp2 + kFastMargin);
         const float c = p.scale_log2, nm = -m_used;
-        float rowsum = 0.0f;
-        uint32_t pk[BN / 2];
-        if (fast && interior) {  // the common case: no mask, no clamp
+        uint64_t rs[2] = {0ull, 0ull};  // packed row-sum partials (+0.0f pairs)
+        // P over the first BN/2 columns of S, 32 keys (16 columns) at a time.
 #pragma unroll
-          for (int i = 0; i < BN; i += 2) {
-            const float p0 = fast_exp2(fmaf(x[i], c, nm));
-            const float p1 = fast_exp2(fmaf(x[i + 1], c, nm));
-            rowsum += p0 + p1;
-            pk[i / 2] = pack2<BF16>(p0, p1);
-          }
-        } else if (fast) {
-          const uint32_t vlo = static_cast<uint32_t>(vis), vhi = static_cast<uint32_t>(vis >> 32);
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint32_t pk[16];
+          if (fast && interior) {  // the common case: no mask, no clamp
+            const uint64_t c2 = f2_pack(c, c), nm2 = f2_pack(nm, nm);
 #pragma unroll
-          for (int i = 0; i < BN; i += 2) {
-            const uint32_t vw = i < 32 ? vlo : vhi;
-            float p0 = fast_exp2(fmaf(x[i], c, nm));
-            float p1 = fast_exp2(fmaf(x[i + 1], c, nm));
-            p0 = ((vw >> (i & 31)) & 1) ? p0 : 0.0f;
-            p1 = ((vw >> ((i + 1) & 31)) & 1) ? p1 : 0.0f;
-            rowsum += p0 + p1;
-            pk[i / 2] = pack2<BF16>(p0, p1);
-          }
-        } else {
-          // Exact path near the clamp: y = visible ? max(s*c, clamp) :
-          // (real key ? clamp : -inf).
+            for (int i = 0; i < 32; i += 2) {
+              float y0, y1, p0, p1;
+              f2_unpack(f2_fma(f2_pack(x[c0 + i], x[c0 + i + 1]), c2, nm2), y0, y1);
+              if (kPolyEvery > 0 && (i / 2) % kPolyEvery == kPolyEvery - 1) {
+                exp2_poly2(y0, y1, p0, p1);
+              } else {
+                p0 = fast_exp2(y0);
+                p1 = fast_exp2(y1);
+              }
+              rs[(i / 2) & 1] = f2_add(rs[(i / 2) & 1], f2_pack(p0, p1));
+              pk[i / 2] = pack2<BF16>(p0, p1);
+            }
+          } else if (fast) {
 #pragma unroll
-          for (int i = 0; i < BN; i += 2) {
-            float y0 = fmaxf(x[i] * c, kClamp2), y1 = fmaxf(x[i + 1] * c, kClamp2);
-            if (!((vis >> i) & 1)) y0 = ((real >> i) & 1) ? kClamp2 : -INFINITY;
-            if (!((vis >> (i + 1)) & 1)) y1 = ((real >> (i + 1)) & 1) ? kClamp2 : -INFINITY;
-            const float p0 = fast_exp2(y0 + nm), p1 = fast_exp2(y1 + nm);
-            rowsum += p0 + p1;
-            pk[i / 2] = pack2<BF16>(p0, p1);
+            for (int i = 0; i < 32; i += 2) {
+              const int k0 = c0 + i;
+              float p0 = fast_exp2(fmaf(x[k0], c, nm));
+              float p1 = fast_exp2(fmaf(x[k0 + 1], c, nm));
+              p0 = (k0 >= vlo && k0 <= vhi) ? p0 : 0.0f;
+              p1 = (k0 + 1 >= vlo && k0 + 1 <= vhi) ? p1 : 0.0f;
+              rs[(i / 2) & 1] = f2_add(rs[(i / 2) & 1], f2_pack(p0, p1));
+              pk[i / 2] = pack2<BF16>(p0, p1);
+            }
+          } else {
+            // Exact path near the clamp: y = visible ? max(s*c, clamp) :
+            // (real key ? clamp : -inf).
+#pragma unroll
+            for (int i = 0; i < 32; i += 2) {
+              const int k0 = c0 + i;
+              float y0 = fmaxf(x[k0] * c, kClamp2), y1 = fmaxf(x[k0 + 1] * c, kClamp2);
+              if (!(k0 >= vlo && k0 <= vhi)) y0 = k0 <= rlast ? kClamp2 : -INFINITY;
+              if (!(k0 + 1 >= vlo && k0 + 1 <= vhi)) y1 = k0 + 1 <= rlast ? kClamp2 : -INFINITY;
+              const float p0 = fast_exp2(y0 + nm), p1 = fast_exp2(y1 + nm);
+              rs[(i / 2) & 1] = f2_add(rs[(i / 2) & 1], f2_pack(p0, p1));
+              pk[i / 2] = pack2<BF16>(p0, p1);
+            }
           }
+          tmem_st16(lane_base + s_col + c0 / 2, pk);
         }
-        l = l * alpha + rowsum;
-        // O may only be rescaled once the previous P·V of this slot has
-        // retired. The wait is unambiguous whenever it is taken: S(j) was
-        // committed after P·V(j-2) was issued, so at this point P·V(j-2) has
-        // completed and P·V(j) is not yet issued, i.e. o_done has completed
-        // exactly it-1 or it phases. On the item's last tile the wait is always
-        // taken so that the epilogue's wait for the final P·V is unambiguous too.
-        const bool need_any = __any_sync(0xffffffffu, need);
-        if (!first_tile && (need_any || j == hi)) {
-          if (!__all_sync(0xffffffffu, mbar_wait(&o_done[s], (it - 1) & 1, p.err, abort_flag))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-        }
-        if (need_any) {
+        float rs0, rs1, rs2, rs3;
+        f2_unpack(rs[0], rs0, rs1);
+        f2_unpack(rs[1], rs2, rs3);
+        l = l * alpha + ((rs0 + rs1) + (rs2 + rs3));
+        // O is idle here: this slot's S(j) was issued behind its P·V(j-1),
+        // so S(j)'s commit retired it, and P·V(j) waits for p_full.
+        if (__any_sync(0xffffffffu, need)) {
           uint32_t r[32];
 #pragma unroll
           for (int c0 = 0; c0 < D; c0 += 32) {
@@ -746,17 +773,10 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             tmem_st16(lane_base + o_col + c0 + 16, hi16);
           }
         }
-        {
-          uint32_t a16[16], b16[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) { a16[i] = pk[i]; b16[i] = pk[16 + i]; }
-          tmem_st16(lane_base + s_col, a16);
-          tmem_st16(lane_base + s_col + 16, b16);
-        }
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[2 * s + b]);
+        if (lane == 0) mbar_arrive(&p_full[s]);
       }
       if (!ok) break;
       const bool has = lo <= hi;

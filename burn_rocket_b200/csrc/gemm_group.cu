@@ -65,27 +65,8 @@ struct GroupArgs {
   uint32_t* err;
 };
 
-// Packed pairs of f32: two independent IEEE-rounded multiplies per
-// instruction. (The accumulating adds stay scalar add.rn, which is never
-// contracted with a multiply into a single rounding.)
-__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-  return r;
-}
-__device__ __forceinline__ void f2_unpack(uint64_t r, float& a, float& b) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
-}
-__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
+// (Packed f32x2 helpers: sm100.cuh. The accumulating adds below stay scalar
+// add.rn, which is never contracted with a multiply into a single rounding.)
 
 // f32 of two int32 partials. SMALL (|p| < 2^22): 1.5 * 2^23 + p is exact with
 // ulp 1, so adding the integer to the bits of 1.5 * 2^23 and subtracting

@@ -112,6 +112,9 @@ int launch_q8_0_unpack_blocks(const uint8_t* blocks, int64_t n, int64_t k, int64
                               int8_t* codes, uint16_t* scales, cudaStream_t stream);
 
 // Attention (attention.cu).
+// Query tiles are 128 rows, key/value tiles kAttnKeyTile rows (the TMA box
+// height of the K and V maps).
+constexpr int kAttnKeyTile = 128;
 // Attention split-mode workspace bounds: partial-result records for up to
 // kAttnMaxCtas CTAs (head width <= 128) and arrival counters for up to
 // kAttnMaxUnits work units (query-slot pairs x KV heads x sequences).
