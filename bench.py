@@ -216,6 +216,43 @@ class AttnWorkload:
     def kernel_launches(self):
         return [("attn_kernel causal", self.flops_c), ("attn_kernel bidirectional", self.flops_b)]
 
+    def beside(self, stream, peak):
+        """Reported beside config #2: config #4's head_dim-72 attention (16
+        images x 2394 patches, 16 heads x 72, bidirectional; q/k/v strided
+        inside the tower's [rows, 3 x 1152] qkv buffer, 265 MB: larger than
+        L2), one rb_attention_batched call per step, 20 steps back to back."""
+        import torch
+        import burn_rocket_b200._lib as L
+        n_img, T, h, hd = 16, 2394, 16, 72
+        hq = h * hd
+        g = torch.Generator(device="cpu").manual_seed(7)
+        qkv = torch.randn(n_img * T, 3 * hq, generator=g).half().to(self.q.device)
+        att = torch.empty(n_img * T, hq, dtype=torch.half, device=self.q.device)
+        p0, lib = qkv.data_ptr(), L.load()
+
+        def call():
+            rc = lib.rb_attention_batched(p0, 3 * hq, p0 + hq * 2, 3 * hq, p0 + 2 * hq * 2, 3 * hq, att.data_ptr(), hq,
+                                          L.DTYPE_F16, n_img, T, T, h, h, hd, 1.0 / math.sqrt(hd), 0.0,
+                                          L.MASK_NONE, -1, 0, 0, stream.cuda_stream)
+            if rc != 0:
+                raise RuntimeError(L.last_error())
+        for _ in range(3):
+            call()
+        torch.cuda.synchronize()
+        steps = 20
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(2_000_000)
+        a.record(stream)
+        for _ in range(steps):
+            call()
+        b.record(stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / steps
+        tflops = 4.0 * T * T * hd * h * n_img / (ms / 1e3) / 1e12
+        return {"siglip_hd72": {"what": "config #4 tower attention, 16 x 2394 patches, 16 heads x 72, bidirectional",
+                                "ms_per_call": round(ms, 4), "tflops": round(tflops, 1),
+                                "frac_of_burst": round(tflops / peak, 4)}}
+
     def e2e_step(self):
         import burn_rocket_b200._lib as L
         lib = L.load()
@@ -760,7 +797,7 @@ def config_dict(name, world):
                          "qwen3": "configs[2] Qwen3-Embedding-0.6B arch, 28 layers, 64x512 tokens",
                          "siglip": "configs[3] SigLIP-style W8A8 tower, 27 layers, 16x2394 patches",
                          "moe": "configs[4] Qwen3-30B-A3B-style MoE, 48 layers, 4x2048 tokens"}[name],
-            "l2": "flushed between timed steps (256 MiB write)",
+            "l2": L2_NOTE.get(name, "flushed between timed steps (256 MiB write)"),
             "parallelism": (f"dp{world} over sequences" if name == "qwen3"
                             else f"dp{world} over images" if name == "siglip"
                             else ("single GPU, all 128 experts resident" if world == 1
@@ -773,6 +810,15 @@ def config_dict(name, world):
 DTYPES = {"attn": "f16", "q8gemm": "f16xq8_0->f32", "w8a8": "s8", "w8a8g": "s8 (group-wise, g128)", "qwen3": "f16xq8_0 (f32 residual)",
           "siglip": "s8 linears, f16 attention (f32 residual)", "moe": "f16xq8_0 (f32 residual, f32 router)"}
 DEFAULT_STEPS = {"attn": 200, "q8gemm": 2000, "w8a8": 60, "w8a8g": 30, "qwen3": 20, "siglip": 5, "moe": 3}
+# Single ops: steps run back to back, cycling over COPIES independent input
+# sets (weights included) whose bytes together exceed the 126 MB L2, so no
+# step finds its inputs in L2 and no flush or per-step event pair sits
+# between them; w8a8 / w8a8g touch over 1 GB per step already.
+COPIES = {"q8gemm": 20, "attn": 4, "w8a8": 1, "w8a8g": 1}
+L2_NOTE = {"q8gemm": "inputs larger than L2: steps back to back over 20 input/weight copies (234 MB)",
+           "attn": "inputs larger than L2: steps back to back over 4 q/k/v/out copies (238 MB)",
+           "w8a8": "inputs larger than L2: > 1 GB of activations and outputs per step, steps back to back",
+           "w8a8g": "inputs larger than L2: > 1 GB of activations and outputs per step, steps back to back"}
 # configs[0], [1] and [3]'s projections: measured beside the default (config #3) line at N = 1
 SUB_WORKLOADS = ("q8gemm", "attn", "w8a8", "w8a8g")
 
@@ -821,6 +867,55 @@ def time_device(wl, steps, warmup, flush, stream, use_graph, barrier, local):
     return ms, launches, per_step > 0, clocks.summary()
 
 
+def time_single(wls, steps, warmup, stream, use_graph, local):
+    """Single-op timing: W untimed warm-up steps, then exactly `steps` steps
+    back to back between one pair of CUDA events on the launching stream,
+    step i running on input copy i % len(wls) (see COPIES). The steps are
+    captured as one CUDA graph over all copies, replayed steps / copies times;
+    a short device-side sleep ahead of the first replay lets the host queue
+    the replays before the timed region starts. Returns (ms summed over the
+    steps, kernel launches in the timed region, graph used, clock summary)."""
+    import torch
+    import burn_rocket_b200 as rb
+    C = len(wls)
+    if steps % C:
+        raise ValueError(f"steps ({steps}) must be a multiple of the {C} input copies")
+    for i in range(max(warmup, C)):
+        wls[i % C].step()
+    torch.cuda.synchronize()
+    rb.check_device_errors()
+    rb.launch_count(reset=True)
+    graph = None
+    if use_graph and all(getattr(w, "graphable", True) for w in wls):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+            for w in wls:
+                w.step()
+        per_replay = rb.launch_count(reset=True)
+        graph.replay()
+        torch.cuda.synchronize()
+        rb.check_device_errors()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        torch.cuda._sleep(2_000_000)  # ~1 ms: the replays are queued behind it
+        start.record(stream)
+        if graph is not None:
+            for _ in range(steps // C):
+                graph.replay()
+        else:
+            for i in range(steps):
+                wls[i % C].step()
+        end.record(stream)
+        torch.cuda.synchronize()
+    graphed = graph is not None
+    launches = per_replay * (steps // C) if graphed else rb.launch_count()
+    ms = start.elapsed_time(end)
+    rb.check_device_errors()
+    del graph
+    return ms, launches, graphed, clocks.summary()
+
+
 def time_e2e(wl, steps, barrier):
     """Seconds for `steps` end-to-end calls through the public host entry
     points (pinned host buffers, copies inside), and their bytes per step."""
@@ -863,14 +958,15 @@ def cpu_baseline_of(W, orc):
     return {"value": round(v, 5), "unit": W.unit, "cores": orc.num_threads(), "kind": "port", "sample": sample}
 
 
-def measure_sub(name, dev, flush, stream, args, peaks, peak_kind, orc):
-    """One single-op sub-record (config #1 / #2 / #4 projections) at N = 1."""
+def measure_sub(name, dev, flush, stream, args, peaks, peak_kind):
+    """One single-op sub-record (config #1 / #2 / #4 projections) at N = 1
+    (its cpu_baseline is added after every GPU measurement of the run)."""
     import torch
     W = WORKLOADS[name]
-    wl = W(dev, seed=0x5EED)
+    wls = [W(dev, seed=0x5EED + i) for i in range(COPIES[name])]
+    wl = wls[0]
     steps = DEFAULT_STEPS[name]
-    ms, launches, graphed, clocks = time_device(wl, steps, args.warmup, flush, stream, not args.no_graph,
-                                                torch.cuda.synchronize, dev.index)
+    ms, launches, graphed, clocks = time_single(wls, steps, args.warmup, stream, not args.no_graph, dev.index)
     ms_per_step = ms / steps
     value = wl.flops / 1e12 / (ms_per_step / 1e3)
     e2e_steps = 10
@@ -880,11 +976,12 @@ def measure_sub(name, dev, flush, stream, args, peaks, peak_kind, orc):
            "dtype": DTYPES[name], "roofline": roofline_of(wl, ms_per_step, peaks, peak_kind),
            "e2e": {"value": round(wl.flops / 1e12 * e2e_steps / e2e_s, 3), "unit": W.unit,
                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
-           "gpu_launches": int(launches), "clocks": clocks,
-           "timing": "CUDA-graph replay of the step's C-ABI calls" if graphed else "eager launches"}
-    if orc is not None:
-        rec["cpu_baseline"] = cpu_baseline_of(W, orc)
-    del wl
+           "gpu_launches": int(launches), "clocks": clocks, "l2": L2_NOTE[name],
+           "timing": ("CUDA-graph replay of the steps' C-ABI calls, back to back" if graphed
+                      else "eager launches, back to back")}
+    if hasattr(wl, "beside"):
+        rec.update(wl.beside(stream, float(peaks["bf16_tflops"])))
+    del wl, wls
     torch.cuda.empty_cache()
     return rec
 
@@ -947,8 +1044,18 @@ def run_b200(args):
             dist.barrier()
         torch.cuda.synchronize()
 
-    ms, launches, graphed, clocks = time_device(wl, args.steps, args.warmup, flush, stream, not args.no_graph,
-                                                barrier, local)
+    if wl.name in COPIES:
+        barrier()
+        wls = [wl] + [W(dev, seed=0x5EED + rank + 1000 * i) for i in range(1, COPIES[wl.name])]
+        steps = -(-args.steps // len(wls)) * len(wls)
+        if steps != args.steps:
+            raise SystemExit(f"--steps must be a multiple of {len(wls)} for {wl.name}")
+        ms, launches, graphed, clocks = time_single(wls, args.steps, args.warmup, stream, not args.no_graph, local)
+        barrier()
+        del wls
+    else:
+        ms, launches, graphed, clocks = time_device(wl, args.steps, args.warmup, flush, stream, not args.no_graph,
+                                                    barrier, local)
     t = torch.tensor([ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -985,11 +1092,6 @@ def run_b200(args):
     }
     if world > 1:
         dist.barrier()
-    orc = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        from oracle import oracle as orc
-        orc.use_all_host_cores()
-        line["cpu_baseline"] = cpu_baseline_of(W, orc)
     if args.workload == "qwen3" and not args.no_sub:
         del wl
         torch.cuda.empty_cache()
@@ -1010,7 +1112,16 @@ def run_b200(args):
         if world == 1:
             # the metric's single-op items, each timed alone on this GPU
             for name in SUB_WORKLOADS:
-                line["sub"][name] = measure_sub(name, dev, flush, stream, args, peaks, peak_kind, orc)
+                line["sub"][name] = measure_sub(name, dev, flush, stream, args, peaks, peak_kind)
+    # The host-core baselines run after every GPU measurement, so that their
+    # OpenMP threads share no time with a timed region.
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as orc
+        orc.use_all_host_cores()
+        line["cpu_baseline"] = cpu_baseline_of(W, orc)
+        for name, rec in line.get("sub", {}).items():
+            if name in SUB_WORKLOADS:
+                rec["cpu_baseline"] = cpu_baseline_of(WORKLOADS[name], orc)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

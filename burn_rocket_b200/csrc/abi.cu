@@ -329,6 +329,7 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
         return fail(rc, "activation cast launch failed");
       g_launches++;
       a = e->act.ptr;
+      L.pdl = 1;  // the GEMM's prologue (and Q8_0 weight staging) overlaps the cast
     }
     const GemmPlan plan = gemm_plan(true, L.M, L.N, L.K, e->num_sms);
     CUtensorMap tmA, tmC;
@@ -348,6 +349,7 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
         return fail(rc, "activation cast launch failed");
       g_launches++;
       a = e->act.ptr;
+      L.pdl = 1;  // the GEMM's prologue (and Q8_0 weight staging) overlaps the cast
     }
     GemmPlan plan = gemm_plan(false, L.M, L.N, L.K, e->num_sms);
     // The gated epilogue turns 128 accumulator columns into 64 outputs: tiles
@@ -402,6 +404,7 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
       g_launches++;
       codes = c8;
       rs = r32;
+      L.pdl = 1;  // the GEMM's prologue overlaps the quantiser
     } else if ((reinterpret_cast<uintptr_t>(x) & 15) != 0 || k % 16 != 0) {
       return fail(RB_E_SHAPE, "w8a8 codes input: 16-byte aligned rows needed (k %% 16 == 0)");
     }

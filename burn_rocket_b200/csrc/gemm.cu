@@ -138,6 +138,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();  // A, row scales and expert tables come from the previous kernel
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -336,8 +337,10 @@ static int launch_cfg(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUte
   // means the output rows are 16-byte aligned.
   args.epi_path = (tmC == nullptr || (Cfg::BN % (128 / out_bytes)) != 0) ? kEpiPathScalar
                   : epi_path_default();
-  gemm_kernel<Cfg><<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(tmA, tmB, tmS,
-                                                                     tmC ? *tmC : tmA, args);
+  const CUtensorMap& tc = tmC ? *tmC : tmA;
+  if (launch_kernel(gemm_kernel<Cfg>, dim3(grid), dim3(Cfg::THREADS), Cfg::SMEM_BYTES, stream, a.pdl != 0,
+                    tmA, tmB, tmS, tc, args) != cudaSuccess)
+    return RB_E_DEVICE;
   return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
 }
 
@@ -407,6 +410,7 @@ static GemmArgs make_args(const GemmLaunch& L) {
   a.tile_expert = L.tile_expert;
   a.gated = L.gated;
   a.act = L.act;
+  a.pdl = L.pdl;
   return a;
 }
 

@@ -49,7 +49,27 @@ struct GemmArgs {
   // Element-wise activation applied before the f16 rounding (RB_ACT_*).
   int act;
   uint32_t* err;
+  int pdl;  // host side: launched with programmatic stream serialization
 };
+
+// Kernel launch, with programmatic stream serialization when `pdl` is set.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                 cudaStream_t stream, bool pdl, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (pdl) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // --------------------------------------------------------------------------
 // Q8_0 dequantisation of 8 consecutive codes of one weight row:

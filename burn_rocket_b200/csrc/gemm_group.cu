@@ -130,6 +130,7 @@ gemm_i8g_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  griddep_wait();  // the activation codes and group scales come from the quantiser
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -289,10 +290,14 @@ int launch_i8g_gemm(int M, int N, int K, int G, const float* a_s, const float* b
   a.epi_path = tmC == nullptr ? kEpiPathScalar : epi_path_default();
   const int tiles = ((M + 127) / 128) * ((N + kGBN - 1) / kGBN);
   const int grid = tiles < num_sms ? tiles : num_sms;
+  // A programmatic dependent of the group quantiser launched just before it.
+  const CUtensorMap& tc = tmC ? *tmC : tmA;
+  cudaError_t e;
   if (G <= 256)
-    gemm_i8g_kernel<true><<<grid, kGThreads, kGSmem, stream>>>(tmA, tmB, tmC ? *tmC : tmA, a);
+    e = launch_kernel(gemm_i8g_kernel<true>, dim3(grid), dim3(kGThreads), kGSmem, stream, true, tmA, tmB, tc, a);
   else
-    gemm_i8g_kernel<false><<<grid, kGThreads, kGSmem, stream>>>(tmA, tmB, tmC ? *tmC : tmA, a);
+    e = launch_kernel(gemm_i8g_kernel<false>, dim3(grid), dim3(kGThreads), kGSmem, stream, true, tmA, tmB, tc, a);
+  if (e != cudaSuccess) return RB_E_DEVICE;
   return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
 }
 

@@ -173,6 +173,10 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // A, row scales and expert tables come from the previous kernel; the Q8_0
+  // weight path (codes producer and dequant warps) reads only the resident
+  // weight, and starts on it at once unless it needs the expert table.
+  if (!(Cfg::Q8 && args.tile_expert == nullptr && warp >= kDqWarp0)) griddep_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer (both CTAs)
@@ -419,8 +423,10 @@ static int launch_pair_cfg(const CUtensorMap& tmA, const CUtensorMap& tmB, const
   // means the output rows are 16-byte aligned.
   args.epi_path = (tmC == nullptr || (Cfg::BN % (128 / out_bytes)) != 0) ? kEpiPathScalar
                   : epi_path_default();
-  gemm_pair_kernel<Cfg><<<2 * pairs, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(
-      tmA, tmB, tmS, tmC ? *tmC : tmA, args);
+  const CUtensorMap& tc = tmC ? *tmC : tmA;
+  if (launch_kernel(gemm_pair_kernel<Cfg>, dim3(2 * pairs), dim3(Cfg::THREADS), Cfg::SMEM_BYTES, stream,
+                    a.pdl != 0, tmA, tmB, tmS, tc, args) != cudaSuccess)
+    return RB_E_DEVICE;
   return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
 }
 

@@ -28,6 +28,10 @@ struct GemmLaunch {
   int act;                // RB_ACT_*: element-wise activation before the f16 output rounding
   uint32_t* err;
   int num_sms;
+  // Launch with programmatic stream serialization: the previous kernel of the
+  // stream (a cast or quantiser producing A) lets this GEMM start early; the
+  // GEMM waits for it before reading anything it wrote.
+  int pdl;
 };
 
 // Tile plan of one matmul. Single CTA: a (128*mh) x bn output tile per CTA.

@@ -111,6 +111,7 @@ extern "C" int rb_matmul_w8a8_noalloc(int64_t id, const void* x, int x_dtype, in
   L.act = v.act;
   L.err = v.err;
   L.num_sms = v.num_sms;
+  L.pdl = 1;  // the GEMM's prologue overlaps the quantiser launched just before it
   const bool tstore = make_output_map(&tmC, y, y_dtype, m, v.n);
   const GemmPlan plan = gemm_plan(true, L.M, L.N, L.K, v.num_sms);
   if ((rc = launch_w8a8_gemm(L, plan, tmA, v.tm_codes[bn_index(plan.weight_rows())],

@@ -14,6 +14,7 @@
 #include <cuda_bf16.h>
 
 #include "kernels.h"
+#include "sm100.cuh"
 
 namespace rb {
 
@@ -93,6 +94,7 @@ template <int DT>
 __global__ void quantize_rows_kernel(const void* __restrict__ x, int64_t m, int64_t k,
                                      float in_scale, int8_t* __restrict__ codes,
                                      float* __restrict__ row_scale) {
+  griddep_launch_dependents();  // the GEMM reading our output may start its prologue
   const int lane = threadIdx.x & 31;
   const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   for (int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -155,6 +157,7 @@ template <int DT, int V>
 __global__ void quantize_rows_vec_kernel(const uint4* __restrict__ x, int64_t m, int64_t k,
                                          float in_scale, uint2* __restrict__ codes,
                                          float* __restrict__ row_scale) {
+  griddep_launch_dependents();  // the GEMM reading our output may start its prologue
   const int lane = threadIdx.x & 31;
   const int nv = static_cast<int>(k / 8);  // 16-byte vectors per row (<= 32 V)
   const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
@@ -211,6 +214,7 @@ __global__ void __launch_bounds__(128) quantize_rows_block_kernel(const uint4* _
                                                                    int64_t k, float in_scale,
                                                                    uint2* __restrict__ codes,
                                                                    float* __restrict__ row_scale) {
+  griddep_launch_dependents();  // the GEMM reading our output may start its prologue
   __shared__ float s_max[2][4];
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int nv = static_cast<int>(k / 8);
@@ -266,6 +270,7 @@ template <int DT>
 __global__ void quantize_rows_stream_kernel(const uint4* __restrict__ x, int64_t m, int64_t k,
                                             float in_scale, uint2* __restrict__ codes,
                                             float* __restrict__ row_scale) {
+  griddep_launch_dependents();  // the GEMM reading our output may start its prologue
   const int lane = threadIdx.x & 31;
   const int64_t nv = k / 8;
   const int64_t warps_total = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
@@ -401,6 +406,7 @@ int launch_w8a8_weight_quant(const float* w, int64_t n, int64_t k, int8_t* codes
 template <int DT>
 __global__ void quantize_groups_kernel(const void* __restrict__ x, int64_t m, int64_t k, int group,
                                        int8_t* __restrict__ codes, float* __restrict__ scales) {
+  griddep_launch_dependents();  // the GEMM reading our output may start its prologue
   const int lane = threadIdx.x & 31;
   const int64_t ng = k / group;
   const int64_t nw = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
@@ -460,6 +466,7 @@ __global__ void cast_kernel(const void* __restrict__ x, void* __restrict__ y, in
 // f32 -> f16, 8 elements per thread (the hot cast on the Q8_0 matmul path).
 __global__ void cast_f32_f16_vec_kernel(const float4* __restrict__ x, uint4* __restrict__ y,
                                         int64_t count8) {
+  griddep_launch_dependents();  // the GEMM reading our output may start its prologue
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < count8;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const float4 a = x[2 * i], b = x[2 * i + 1];

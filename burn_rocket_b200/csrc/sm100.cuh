@@ -27,6 +27,17 @@ enum : uint32_t {
 // %globaltimer clock); a healthy pipeline completes each wait in microseconds.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
+// Programmatic dependent launch. A kernel launched with programmatic stream
+// serialization may start while the previous kernel of its stream still
+// runs: griddep_wait() returns once that kernel has completed and its writes
+// are visible (at once for a kernel launched without the attribute), and a
+// producer kernel calls griddep_launch_dependents() so that the next kernel's
+// prologue can start early.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Packed pairs of f32 (sm_100 f32x2 instructions): two independent
 // IEEE-rounded operations per instruction, one per 32-bit half.
 __device__ __forceinline__ uint64_t f2_pack(float a, float b) {
