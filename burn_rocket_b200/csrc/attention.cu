@@ -804,16 +804,19 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
       };
       if (!SPLIT || item.full) {
+        // All of O's columns in one batch of TMEM loads (one load latency).
         const float inv_l = 1.0f / l;
+        constexpr int NCH = (D + 31) / 32;
+        uint32_t r[NCH][32];
 #pragma unroll
-        for (int c0 = 0; c0 < D; c0 += 32) {
-          uint32_t r[32];
-          tmem_ld32(lane_base + o_col + c0, r);
-          tmem_wait_ld();
+        for (int c = 0; c < NCH; ++c) tmem_ld32(lane_base + o_col + c * 32, r[c]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < NCH; ++c) {
           float v[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-          store_chunk(c0, v, inv_l);
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[c][i]);
+          store_chunk(c * 32, v, inv_l);
         }
       } else {
         // Part of a unit split over CTAs c_first..c_last: publish (O, m, l);

@@ -77,6 +77,10 @@ extern "C" int rb_matmul_w8a8_noalloc(int64_t id, const void* x, int x_dtype, in
   if (k != v.k) return report_error(RB_E_SHAPE, "activation K mismatch for the W8A8 weight");
   if (v.act != RB_ACT_NONE && y_dtype != RB_DTYPE_F16)
     return report_error(RB_E_SHAPE, "the W8A8 weight has a fused activation: the output must be f16");
+  // The same output contract as rb_matmul.
+  const int64_t y_bytes = y_dtype == RB_DTYPE_F32 ? 4 : 2;
+  if ((v.n * y_bytes) % 16 != 0 && (reinterpret_cast<uintptr_t>(y) & 15) != 0)
+    return report_error(RB_E_SHAPE, "output buffer must be 16-byte aligned");
   const size_t codes_bytes = (static_cast<size_t>(m) * static_cast<size_t>(k) + 255) & ~size_t(255);
   const size_t need = codes_bytes + static_cast<size_t>(m) * sizeof(float);
   if (m > (int64_t(1) << 30) || need > kNoAllocScratchBytes) {
