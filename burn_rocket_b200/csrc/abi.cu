@@ -360,6 +360,10 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
     const bool tstore = output_map(&tmC, y, y_dtype, m, n_out);
     if (w.gated && !tstore) return fail(RB_E_SHAPE, "gated weight: output tensor map unavailable");
     const int bi = bn_index(plan.weight_rows());
+    L.w_codes = w.codes;
+    L.w_scales = w.scales;
+    L.w_pitch = w.pitch;
+    L.w_rows = w.n;
     if ((rc = launch_q8_gemm(L, plan, tmA, w.tm_codes[bi], w.tm_scales[bi], tstore ? &tmC : nullptr,
                              st)) != RB_OK)
       return fail(rc, "q8_0 gemm launch failed");
@@ -1429,6 +1433,10 @@ int rb_matmul_grouped(int64_t id, int experts, const void* x_perm_f16, int64_t m
   const bool tstore = output_map(&tmC, y, y_dtype, max_rows, n_out);
   if (w.gated && !tstore) return fail(RB_E_SHAPE, "grouped matmul: output tensor map unavailable");
   const int bi = bn_index(plan.weight_rows());
+  L.w_codes = w.codes;
+  L.w_scales = w.scales;
+  L.w_pitch = w.pitch;
+  L.w_rows = w.n;
   if ((rc = launch_q8_gemm(L, plan, tmA, w.tm_codes[bi], w.tm_scales[bi], tstore ? &tmC : nullptr,
                            reinterpret_cast<cudaStream_t>(stream))) != RB_OK)
     return fail(rc, "grouped q8_0 gemm launch failed");

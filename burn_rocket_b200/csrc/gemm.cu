@@ -411,6 +411,10 @@ static GemmArgs make_args(const GemmLaunch& L) {
   a.gated = L.gated;
   a.act = L.act;
   a.pdl = L.pdl;
+  a.w_codes = L.w_codes;
+  a.w_scales = reinterpret_cast<const __half*>(L.w_scales);
+  a.w_pitch = L.w_pitch;
+  a.w_rows = L.w_rows;
   return a;
 }
 

@@ -50,6 +50,12 @@ struct GemmArgs {
   int act;
   uint32_t* err;
   int pdl;  // host side: launched with programmatic stream serialization
+  // Q8_0 weight in global memory (the CTA-pair kernel's dequant warps read it
+  // directly): codes int8 [w_rows, K], scales f16 [K/32, w_pitch].
+  const int8_t* w_codes;
+  const __half* w_scales;
+  long long w_pitch;
+  long long w_rows;
 };
 
 // Kernel launch, with programmatic stream serialization when `pdl` is set.

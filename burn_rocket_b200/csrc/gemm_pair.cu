@@ -21,8 +21,6 @@
 //                (cta_group::2 loads complete on the leader's barrier); the
 //                leader's producer arms it with both CTAs' byte count.
 //   ld_empty[s]  each CTA: the leader's UMMA commit (multicast to both CTAs).
-//   cd_full[c]   Q8_0, each CTA: its own codes + scales bytes (codes producer).
-//   cd_empty[c]  Q8_0, each CTA: its own dequant warps have read the stage.
 //   b_local[b]   each CTA: its own dequant warps (local arrive).
 //   b_full[b]    leader: the peer's half is dequantised — one remote arrive
 //                per stage by the peer's forwarding thread (warp 1), which
@@ -37,12 +35,11 @@
 
 namespace rb {
 
-// LSTAGES: A stages (W8A8: A + this CTA's B half). Q8_0 also has a separate
-// ring of CSTAGES staged code/scale stages, refilled by its own producer warp
-// as soon as the dequant warps have read a stage (so dequantisation can run
-// ahead of the MMA by up to CSTAGES stages), and BSTAGES dequantised B stages.
-template <int BN_, int LSTAGES_, int KIND_, int CSTAGES_ = 1, int BSTAGES_ = 1, int DQ_WARPS_ = 8,
-          int DQ_GROUPS_ = 1>
+// LSTAGES: A stages (W8A8: A + this CTA's B half). Q8_0 also has BSTAGES
+// dequantised B stages; its dequant warps read the weight codes and scales
+// straight from global memory into registers (one stage ahead), so the codes
+// never pass through shared memory, whose bandwidth bounds this kernel.
+template <int BN_, int LSTAGES_, int KIND_, int BSTAGES_ = 1, int DQ_WARPS_ = 8, int DQ_GROUPS_ = 1>
 struct PairCfg {
   static constexpr int DQ_WARPS = DQ_WARPS_;         // Q8_0 dequant warps
   static constexpr int DQ_GROUPS = DQ_GROUPS_;       // stages dequantised concurrently
@@ -53,7 +50,6 @@ struct PairCfg {
   static constexpr bool I8 = KIND_ == kKindI8;
   static constexpr bool Q8 = KIND_ == kKindQ8;
   static constexpr bool TMAB = !Q8;                 // B halves loaded by TMA
-  static constexpr int CSTAGES = Q8 ? CSTAGES_ : 1;
   static constexpr int BSTAGES = Q8 ? BSTAGES_ : 1;
   static constexpr int ELEM = I8 ? 1 : 2;
   static constexpr int BK = 128 / ELEM;             // K elements per stage (one 128-B atom)
@@ -61,14 +57,9 @@ struct PairCfg {
   static constexpr int KSTEPS = BK / UMMA_K;        // 4
   static constexpr int A_BYTES = 128 * 128;         // this CTA's 128 rows of A
   static constexpr int B_BYTES = HB * 128;          // this CTA's half of B (s8, or dequantised f16)
-  static constexpr int CODE_BYTES = Q8 ? HB * 64 : 0;
-  static constexpr int SC_BYTES = Q8 ? 2 * HB * 2 : 0;
   static constexpr uint32_t PAIR_TX = TMAB ? 2 * (A_BYTES + B_BYTES) : 2 * A_BYTES;
-  static constexpr uint32_t CODE_TX = CODE_BYTES + SC_BYTES;
   static constexpr int LSTAGE = round1k(A_BYTES + (TMAB ? B_BYTES : 0));
-  static constexpr int CSTAGE = Q8 ? round1k(CODE_BYTES + SC_BYTES) : 0;
-  static constexpr int CODE_OFF = LSTAGES * LSTAGE;
-  static constexpr int BRING_OFF = CODE_OFF + CSTAGES * CSTAGE;
+  static constexpr int BRING_OFF = LSTAGES * LSTAGE;
   static constexpr int BRING = Q8 ? BSTAGES * B_BYTES : 0;
   static constexpr int EPI_OFF = BRING_OFF + BRING;
   static constexpr int EPI_WARPS = I8 ? kNumEpiWarpsI8 : kNumEpiWarps;
@@ -77,10 +68,9 @@ struct PairCfg {
   static constexpr int BAR_OFF = EPI_OFF + EPI_BYTES;
   static constexpr int SMEM_BYTES = BAR_OFF + 512 + 1024;
   // After the role warps: the peer's accumulator-release forwarder (idle in
-  // the leader) and, for Q8_0, the codes producer.
+  // the leader).
   static constexpr int FWD_WARP = Q8 ? (kDqWarp0 + DQ_WARPS) : kEpiWarp0 + EPI_WARPS;
-  static constexpr int CP_WARP = FWD_WARP + 1;
-  static constexpr int NUM_WARPS = Q8 ? CP_WARP + 1 : FWD_WARP + 1;
+  static constexpr int NUM_WARPS = FWD_WARP + 1;
   static constexpr int THREADS = NUM_WARPS * 32;
   static constexpr uint32_t TMEM_COLS = 2 * BN <= 256 ? 256 : 512;  // two accumulators
   static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "pair UMMA N");
@@ -103,9 +93,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::BAR_OFF);
   uint64_t* ld_full = bars;                          // [LSTAGES]
   uint64_t* ld_empty = ld_full + LSTAGES;            // [LSTAGES]
-  uint64_t* cd_full = ld_empty + LSTAGES;            // [CSTAGES]
-  uint64_t* cd_empty = cd_full + Cfg::CSTAGES;       // [CSTAGES]
-  uint64_t* b_full = cd_empty + Cfg::CSTAGES;        // [BSTAGES]
+  uint64_t* b_full = ld_empty + LSTAGES;             // [BSTAGES]
   uint64_t* b_empty = b_full + Cfg::BSTAGES;         // [BSTAGES]
   uint64_t* b_local = b_empty + Cfg::BSTAGES;        // [BSTAGES]
   uint64_t* acc_full = b_local + Cfg::BSTAGES;       // [2]
@@ -140,10 +128,6 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       mbar_init(&ld_full[s], 1);
       mbar_init(&ld_empty[s], 1);
     }
-    for (int s = 0; s < Cfg::CSTAGES; ++s) {
-      mbar_init(&cd_full[s], 1);
-      mbar_init(&cd_empty[s], Cfg::DQ_WARPS / Cfg::DQ_GROUPS);
-    }
     for (int i = 0; i < Cfg::BSTAGES; ++i) {
       mbar_init(&b_full[i], 1);
       mbar_init(&b_empty[i], 1);
@@ -164,7 +148,6 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    if (Cfg::Q8) tma_prefetch_desc(&tmS);
     if (args.epi_path == kEpiPathTma) tma_prefetch_desc(&tmC);
   }
   // Both CTAs' barriers are initialised (and visible cluster-wide) before any
@@ -174,8 +157,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   // A, row scales and expert tables come from the previous kernel; the Q8_0
-  // weight path (codes producer and dequant warps) reads only the resident
-  // weight, and starts on it at once unless it needs the expert table.
+  // dequant warps read only the resident weight, and start on it at once
+  // unless they need the expert table.
   if (!(Cfg::Q8 && args.tile_expert == nullptr && warp >= kDqWarp0)) griddep_wait();
 
   if (warp == 0) {
@@ -284,26 +267,6 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       if (lane == 0) mbar_arrive(rank == 0 ? &acc_empty[acc] : &acc_local[acc]);
     }
     if (args.epi_path == kEpiPathTma && lane == 0) bulk_wait_all<0>();  // stores complete before exit
-  } else if (Cfg::Q8 && warp == Cfg::CP_WARP) {
-    // ------------------------------------------------------------ codes producer (Q8_0, both CTAs)
-    if (elect_one_sync()) {
-      int cs = 0;
-      uint32_t cph = 0;
-      for (int t = pair; t < num_tiles; t += npairs) {
-        const int w0 = expert_row0(t);
-        if (w0 < 0) break;
-        const int nb = w0 + (t % tiles_n) * BN + static_cast<int>(rank) * HB;
-        for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(&cd_empty[cs], cph ^ 1, args.err, abort_flag)) goto codes_done;
-          uint8_t* st = smem + Cfg::CODE_OFF + cs * Cfg::CSTAGE;
-          mbar_arrive_expect_tx(&cd_full[cs], Cfg::CODE_TX);
-          tma_load_2d(st, &tmB, &cd_full[cs], kb * 64, nb);
-          tma_load_2d(st + Cfg::CODE_BYTES, &tmS, &cd_full[cs], nb, kb * 2);
-          if (++cs == Cfg::CSTAGES) { cs = 0; cph ^= 1; }
-        }
-      }
-    codes_done:;
-    }
   } else if (warp == Cfg::FWD_WARP) {
     // ------------------------------------------------------------ peer: accumulator release
     // Forward "my accumulator rows are drained" to the leader, once per tile.
@@ -320,47 +283,71 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     // ------------------------------------------------------------ Q8_0 dequant (both CTAs)
     // The dequant warps form DQ_GROUPS groups; group g dequantises stages
     // q = g, g + DQ_GROUPS, ... of the (tile, k-block) sequence, so several
-    // stages are in flight at once and each stage's fixed wait / fence /
-    // arrive latency overlaps the others'. Within a stage, chunk (row, c) —
-    // 8 codes of one of this CTA's HB weight rows — is read from the staged
-    // codes at row*64 + c*8 and written as 8 f16 in the 128-byte swizzled
-    // K-major layout the UMMA descriptor reads.
+    // stages are in flight at once. Thread `tid` of a group owns the chunks
+    // (row r0 + j * kRowStep, column c): 8 codes of one of this CTA's HB
+    // weight rows and their block's f16 scale. It loads them for the group's
+    // next stage from global memory (read-only path; L2 after the first M
+    // tile) before it writes the current stage as 8 f16 values per chunk in
+    // the 128-byte swizzled K-major layout the UMMA descriptor reads. Rows
+    // past the weight and columns past K read as zero (the TMA fill).
     constexpr int kGroupWarps = Cfg::DQ_WARPS / Cfg::DQ_GROUPS;
-    constexpr int kChunks = HB * 8;
     constexpr int kThreads = kGroupWarps * 32;
-    constexpr int kPer = (kChunks + kThreads - 1) / kThreads;
+    constexpr int kRowStep = kThreads / 8;
+    constexpr int kPer = HB / kRowStep;
+    static_assert(HB % kRowStep == 0, "whole chunks per thread");
     const int grp = (warp - kDqWarp0) / kGroupWarps;
     const int tid = threadIdx.x - (kDqWarp0 + grp * kGroupWarps) * 32;
-    int q = 0;
-    for (int t = pair; t < num_tiles; t += npairs) {
-      if (expert_row0(t) < 0) break;
-      for (int kb = 0; kb < num_kb; ++kb, ++q) {
-        if (q % Cfg::DQ_GROUPS != grp) continue;
-        const int cs = q % Cfg::CSTAGES, bs = q % Cfg::BSTAGES;
-        const uint32_t cph = (q / Cfg::CSTAGES) & 1, bph = (q / Cfg::BSTAGES) & 1;
-        if (!warp_wait(&cd_full[cs], cph, args.err, abort_flag)) goto dq_done;
-        if (!warp_wait(&b_empty[bs], bph ^ 1, args.err, abort_flag)) goto dq_done;
-        const uint8_t* codes = smem + Cfg::CODE_OFF + cs * Cfg::CSTAGE;
-        const __half* sc = reinterpret_cast<const __half*>(codes + Cfg::CODE_BYTES);
-        uint8_t* sb = smem + Cfg::BRING_OFF + bs * Cfg::B_BYTES;
+    const int c = tid & 7, r0 = tid >> 3;
+    const int8_t* __restrict__ wc = args.w_codes;
+    const __half* __restrict__ ws = args.w_scales;
+    struct Staged {
+      uint2 q[kPer];
+      __half d[kPer];
+    };
+    // Stage q of the sequence is k-block q % num_kb of this pair's tile
+    // number q / num_kb; false past the last tile.
+    auto fetch = [&](int q, Staged& st) -> bool {
+      const int t = pair + (q / num_kb) * npairs;
+      if (t >= num_tiles) return false;
+      const int w0 = expert_row0(t);
+      if (w0 < 0) return false;
+      const int kb = q % num_kb;
+      const long long row0 = static_cast<long long>(w0) + (t % tiles_n) * BN + static_cast<int>(rank) * HB + r0;
+      const int col = kb * 64 + c * 8;
 #pragma unroll
-        for (int j = 0; j < kPer; ++j) {
-          const int i = tid + j * kThreads;
-          if (kChunks % kThreads == 0 || i < kChunks) {
-            const int rowi = i >> 3, c = i & 7;
-            const uint2 qc = *reinterpret_cast<const uint2*>(codes + rowi * 64 + c * 8);
-            const __half d = sc[(c >> 2) * HB + rowi];
-            *reinterpret_cast<uint4*>(sb + rowi * 128 + ((c ^ (rowi & 7)) << 4)) =
-                q8_dequant8_f16(qc, d);
-          }
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&b_local[bs]);    // this CTA's half of B stage bs is written
-          mbar_arrive(&cd_empty[cs]);   // staged codes consumed
+      for (int j = 0; j < kPer; ++j) {
+        const long long row = row0 + j * kRowStep;
+        if (row < args.w_rows && col < K) {
+          st.q[j] = __ldg(reinterpret_cast<const uint2*>(wc + row * K + col));
+          st.d[j] = ws[static_cast<long long>(col >> 5) * args.w_pitch + row];
+        } else {
+          st.q[j] = make_uint2(0u, 0u);
+          st.d[j] = __ushort_as_half(0);
         }
       }
+      return true;
+    };
+    Staged cur, nxt;
+    int q = grp;
+    bool have = fetch(q, cur);
+    while (have) {
+      const int qn = q + Cfg::DQ_GROUPS;
+      const bool have_n = fetch(qn, nxt);  // in flight while this stage is written
+      const int bs = q % Cfg::BSTAGES;
+      const uint32_t bph = (q / Cfg::BSTAGES) & 1;
+      if (!warp_wait(&b_empty[bs], bph ^ 1, args.err, abort_flag)) goto dq_done;
+      uint8_t* sb = smem + Cfg::BRING_OFF + bs * Cfg::B_BYTES;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int rowi = r0 + j * kRowStep;
+        *reinterpret_cast<uint4*>(sb + rowi * 128 + ((c ^ (rowi & 7)) << 4)) = q8_dequant8_f16(cur.q[j], cur.d[j]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&b_local[bs]);  // this CTA's half of B stage bs is written
+      cur = nxt;
+      q = qn;
+      have = have_n;
     }
   dq_done:;
   }
@@ -380,8 +367,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 // --------------------------------------------------------------------------
 // Host-side launch.
 
-using PairQ8_256 = PairCfg<256, 5, kKindQ8, 5, 5, 12, 3>;
-using PairQ8_128 = PairCfg<128, 7, kKindQ8, 8, 6, 12, 3>;
+using PairQ8_256 = PairCfg<256, 7, kKindQ8, 6, 12, 3>;
+using PairQ8_128 = PairCfg<128, 9, kKindQ8, 8, 12, 3>;
 using PairI8_256 = PairCfg<256, 6, kKindI8>;
 using PairI8_128 = PairCfg<128, 8, kKindI8>;
 using PairF16_256 = PairCfg<256, 6, kKindF16>;

@@ -15,8 +15,10 @@ namespace rb {
 
 struct GemmLaunch {
   int M, N, K;
-  const int8_t* w_codes;  // Q8_0 codes [N, K]
-  const void* w_scales;   // Q8_0 f16 scales [K/32, N]
+  const int8_t* w_codes;  // Q8_0 codes [w_rows, K] (all experts of a grouped weight)
+  const void* w_scales;   // Q8_0 f16 scales [K/32, w_pitch]
+  int64_t w_pitch;        // Q8_0 scale row pitch
+  int64_t w_rows;         // Q8_0 weight rows in memory
   const float* s_row;     // W8A8 per-row activation scale [M]
   const float* s_col;     // W8A8 per-channel weight scale [N]
   void* out;
