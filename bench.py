@@ -75,6 +75,7 @@ PROFILES = {
     "attn": "attn_kernel_gqa_s3633_ncu.md",
     "q8gemm": "gemm_pair_kernel_q8_0_config1_ncu.md",
     "w8a8": "gemm_pair_kernel_w8a8_8192x4304x1152_ncu.md",
+    "w8a8g": "gemm_i8g_kernel_g128_config4_ncu.md",
     "qwen3": "gemm_pair_kernel_q8_0_8192x6144x1024_ncu.md",
     "siglip": "gemm_pair_kernel_w8a8_8192x4304x1152_ncu.md",
     "moe": "gemm_pair_kernel_moe_grouped_ncu.md",
@@ -302,6 +303,7 @@ class Q8GemmWorkload:
         self.x = torch.from_numpy(a).to(dev).to(xdt)
         self.y = torch.empty(self.M, self.N, dtype=xdt, device=dev)
         self.flops = 2.0 * self.M * self.N * self.K
+        self.weight_bytes = self.N * self.K * (1 + 2 / 32)  # Q8_0 codes + f16 block scales
         self.hx = self.x.cpu().pin_memory()
         self.hy = torch.empty(self.M, self.N, dtype=xdt).pin_memory()
 
@@ -360,6 +362,7 @@ class W8A8Workload:
             self.xs.append(torch.randn(self.M, k, device=dev).to(xdt))
             self.ys.append(torch.empty(self.M, n, dtype=xdt, device=dev))
         self.flops = sum(2.0 * self.M * n * k for n, k in self.SHAPES)
+        self.weight_bytes = sum(n * k + 4 * n for n, k in self.SHAPES)
         self.hx = [x.cpu().pin_memory() for x in self.xs]
         self.hy = [y.cpu().pin_memory() for y in self.ys]
 
@@ -422,6 +425,7 @@ class W8A8GroupWorkload(W8A8Workload):
             self.xs.append(torch.randn(self.M, k, device=dev).half())
             self.ys.append(torch.empty(self.M, n, dtype=torch.float16, device=dev))
         self.flops = sum(2.0 * self.M * n * k for n, k in self.SHAPES)
+        self.weight_bytes = sum(n * k + 4 * n for n, k in self.SHAPES)
         self.hx = [x.cpu().pin_memory() for x in self.xs]
         self.hy = [y.cpu().pin_memory() for y in self.ys]
 
@@ -797,7 +801,8 @@ def config_dict(name, world):
                          "qwen3": "configs[2] Qwen3-Embedding-0.6B arch, 28 layers, 64x512 tokens",
                          "siglip": "configs[3] SigLIP-style W8A8 tower, 27 layers, 16x2394 patches",
                          "moe": "configs[4] Qwen3-30B-A3B-style MoE, 48 layers, 4x2048 tokens"}[name],
-            "l2": L2_NOTE.get(name, "flushed between timed steps (256 MiB write)"),
+            "l2": L2_NOTE.get(name, "flushed between timed steps (256 MiB write)") if name not in SINGLE_OPS
+                  else "inputs larger than L2: steps back to back over input/weight copies exceeding 2 x L2",
             "parallelism": (f"dp{world} over sequences" if name == "qwen3"
                             else f"dp{world} over images" if name == "siglip"
                             else ("single GPU, all 128 experts resident" if world == 1
@@ -810,15 +815,36 @@ def config_dict(name, world):
 DTYPES = {"attn": "f16", "q8gemm": "f16xq8_0->f32", "w8a8": "s8", "w8a8g": "s8 (group-wise, g128)", "qwen3": "f16xq8_0 (f32 residual)",
           "siglip": "s8 linears, f16 attention (f32 residual)", "moe": "f16xq8_0 (f32 residual, f32 router)"}
 DEFAULT_STEPS = {"attn": 200, "q8gemm": 2000, "w8a8": 60, "w8a8g": 30, "qwen3": 20, "siglip": 5, "moe": 3}
-# Single ops: steps run back to back, cycling over COPIES independent input
-# sets (weights included) whose bytes together exceed the 126 MB L2, so no
+# Single ops: steps run back to back, cycling over independent input sets
+# (weights included) whose bytes together exceed twice the 126 MB L2, so no
 # step finds its inputs in L2 and no flush or per-step event pair sits
-# between them; w8a8 / w8a8g touch over 1 GB per step already.
-COPIES = {"q8gemm": 20, "attn": 4, "w8a8": 1, "w8a8g": 1}
-L2_NOTE = {"q8gemm": "inputs larger than L2: steps back to back over 20 input/weight copies (234 MB)",
-           "attn": "inputs larger than L2: steps back to back over 4 q/k/v/out copies (238 MB)",
-           "w8a8": "inputs larger than L2: > 1 GB of activations and outputs per step, steps back to back",
-           "w8a8g": "inputs larger than L2: > 1 GB of activations and outputs per step, steps back to back"}
+# between them (w8a8 / w8a8g touch over 1 GB per step: one set).
+SINGLE_OPS = ("q8gemm", "attn", "w8a8", "w8a8g")
+L2_BYTES = 126e6
+L2_NOTE = {}  # workload -> the `l2` note of its last single-op measurement
+
+
+def footprint_bytes(wl):
+    """Device bytes one step of a single-op workload touches: its CUDA
+    tensors plus the resident weights it names in `weight_bytes`."""
+    import torch
+    tot = float(getattr(wl, "weight_bytes", 0))
+    for v in vars(wl).values():
+        for t in (v if isinstance(v, (list, tuple)) else [v]):
+            if isinstance(t, torch.Tensor) and t.is_cuda:
+                tot += t.numel() * t.element_size()
+    return tot
+
+
+def input_copies(wl):
+    """Independent input sets so that their bytes exceed 2 x L2 (at most 32)."""
+    return int(min(32, max(1, math.ceil(2 * L2_BYTES / max(footprint_bytes(wl), 1.0)))))
+
+
+def l2_note(C, fp):
+    if C == 1:
+        return f"inputs larger than L2: {fp / 1e6:.0f} MB per step, steps back to back"
+    return f"inputs larger than L2: steps back to back over {C} input/weight copies ({C * fp / 1e6:.0f} MB)"
 # configs[0], [1] and [3]'s projections: measured beside the default (config #3) line at N = 1
 SUB_WORKLOADS = ("q8gemm", "attn", "w8a8", "w8a8g")
 
@@ -870,16 +896,14 @@ def time_device(wl, steps, warmup, flush, stream, use_graph, barrier, local):
 def time_single(wls, steps, warmup, stream, use_graph, local):
     """Single-op timing: W untimed warm-up steps, then exactly `steps` steps
     back to back between one pair of CUDA events on the launching stream,
-    step i running on input copy i % len(wls) (see COPIES). The steps are
-    captured as one CUDA graph over all copies, replayed steps / copies times;
-    a short device-side sleep ahead of the first replay lets the host queue
-    the replays before the timed region starts. Returns (ms summed over the
-    steps, kernel launches in the timed region, graph used, clock summary)."""
+    step i running on input set i % len(wls). The `steps` steps are captured
+    as one CUDA graph (replayed once untimed, then timed), queued behind a
+    short device-side sleep so that the host's launch is off the device
+    timeline. Returns (ms summed over the steps, kernel launches in the timed
+    region, graph used, clock summary)."""
     import torch
     import burn_rocket_b200 as rb
     C = len(wls)
-    if steps % C:
-        raise ValueError(f"steps ({steps}) must be a multiple of the {C} input copies")
     for i in range(max(warmup, C)):
         wls[i % C].step()
     torch.cuda.synchronize()
@@ -889,8 +913,8 @@ def time_single(wls, steps, warmup, stream, use_graph, local):
     if use_graph and all(getattr(w, "graphable", True) for w in wls):
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, capture_error_mode="thread_local"):
-            for w in wls:
-                w.step()
+            for i in range(steps):
+                wls[i % C].step()
         per_replay = rb.launch_count(reset=True)
         graph.replay()
         torch.cuda.synchronize()
@@ -898,18 +922,17 @@ def time_single(wls, steps, warmup, stream, use_graph, local):
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
-        torch.cuda._sleep(2_000_000)  # ~1 ms: the replays are queued behind it
+        torch.cuda._sleep(2_000_000)  # ~1 ms
         start.record(stream)
         if graph is not None:
-            for _ in range(steps // C):
-                graph.replay()
+            graph.replay()
         else:
             for i in range(steps):
                 wls[i % C].step()
         end.record(stream)
         torch.cuda.synchronize()
     graphed = graph is not None
-    launches = per_replay * (steps // C) if graphed else rb.launch_count()
+    launches = per_replay if graphed else rb.launch_count()
     ms = start.elapsed_time(end)
     rb.check_device_errors()
     del graph
@@ -963,8 +986,10 @@ def measure_sub(name, dev, flush, stream, args, peaks, peak_kind):
     (its cpu_baseline is added after every GPU measurement of the run)."""
     import torch
     W = WORKLOADS[name]
-    wls = [W(dev, seed=0x5EED + i) for i in range(COPIES[name])]
-    wl = wls[0]
+    wl = W(dev, seed=0x5EED)
+    C, fp = input_copies(wl), footprint_bytes(wl)
+    wls = [wl] + [W(dev, seed=0x5EED + i) for i in range(1, C)]
+    L2_NOTE[name] = l2_note(C, fp)
     steps = DEFAULT_STEPS[name]
     ms, launches, graphed, clocks = time_single(wls, steps, args.warmup, stream, not args.no_graph, dev.index)
     ms_per_step = ms / steps
@@ -977,7 +1002,7 @@ def measure_sub(name, dev, flush, stream, args, peaks, peak_kind):
            "e2e": {"value": round(wl.flops / 1e12 * e2e_steps / e2e_s, 3), "unit": W.unit,
                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
            "gpu_launches": int(launches), "clocks": clocks, "l2": L2_NOTE[name],
-           "timing": ("CUDA-graph replay of the steps' C-ABI calls, back to back" if graphed
+           "timing": ("one CUDA graph over the steps' C-ABI calls, back to back" if graphed
                       else "eager launches, back to back")}
     if hasattr(wl, "beside"):
         rec.update(wl.beside(stream, float(peaks["bf16_tflops"])))
@@ -1044,12 +1069,11 @@ def run_b200(args):
             dist.barrier()
         torch.cuda.synchronize()
 
-    if wl.name in COPIES:
+    if wl.name in SINGLE_OPS:
         barrier()
-        wls = [wl] + [W(dev, seed=0x5EED + rank + 1000 * i) for i in range(1, COPIES[wl.name])]
-        steps = -(-args.steps // len(wls)) * len(wls)
-        if steps != args.steps:
-            raise SystemExit(f"--steps must be a multiple of {len(wls)} for {wl.name}")
+        C, fp = input_copies(wl), footprint_bytes(wl)
+        L2_NOTE[wl.name] = l2_note(C, fp)
+        wls = [wl] + [W(dev, seed=0x5EED + rank + 1000 * i) for i in range(1, C)]
         ms, launches, graphed, clocks = time_single(wls, args.steps, args.warmup, stream, not args.no_graph, local)
         barrier()
         del wls
@@ -1085,7 +1109,9 @@ def run_b200(args):
         "e2e": {"value": round(e2e_value, 3), "unit": wl.unit, "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h)},
         "gpu_launches": int(launches),
-        "timing": ("CUDA-graph replay of the step's C-ABI calls" if graphed
+        **({"l2": L2_NOTE[wl.name]} if wl.name in L2_NOTE else {}),
+        "timing": ("one CUDA graph over the steps' C-ABI calls, back to back" if graphed and wl.name in SINGLE_OPS
+                   else "CUDA-graph replay of the step's C-ABI calls" if graphed
                    else "eager launches (per-layer host-sized all-to-all)" if wl.name == "moe" and world > 1
                    else "eager launches"),
         "clocks": clocks,
