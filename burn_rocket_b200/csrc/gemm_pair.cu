@@ -123,6 +123,18 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     return e < 0 ? -1 : e * N;
   };
 
+  // Q8_0 pairs with exactly one tile (small M, e.g. a 512-row call): once
+  // that tile's main loop is done the dequant warps have nothing left to do,
+  // so they drain the accumulator beside the epilogue warps, each warp of a
+  // TMEM lane quarter taking a column slice (the B ring, read by no UMMA any
+  // more, serves as their staging). Not for the gated epilogue, whose chunks
+  // span 128 accumulator columns.
+  const int epi_mode_k = args.gated ? kEpiSiluF16 : epi_mode(Cfg::I8, args.out_dtype, args.out_scale, args.act);
+  const int epi_cw = (epi_mode_k == kEpiRaw4) ? 32 : 64;  // columns per epilogue chunk (Q8_0 modes)
+  const int help_slices = BN / epi_cw < 4 ? BN / epi_cw : 4;
+  const bool one_tile = Cfg::Q8 && Cfg::DQ_WARPS == 12 && !args.gated && args.tile_expert == nullptr &&
+                        num_tiles <= npairs && pair < num_tiles && help_slices > 1;
+
   if (threadIdx.x == 0) {
     for (int s = 0; s < LSTAGES; ++s) {
       mbar_init(&ld_full[s], 1);
@@ -247,8 +259,12 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     const EpiParams ep{args.s_col, args.out_dtype, args.out_scale, args.out_inv};
     uint8_t* ebuf = smem + Cfg::EPI_OFF + (warp - kEpiWarp0) * Cfg::EPI_BUFS * kEpiBufBytes;
     constexpr int kColSplit = Cfg::EPI_WARPS / 4;  // warps sharing a TMEM lane quarter
-    const int cbeg = ((warp - kEpiWarp0) >> 2) * (BN / kColSplit), cend = cbeg + BN / kColSplit;
-    const int mode = args.gated ? kEpiSiluF16 : epi_mode(Cfg::I8, args.out_dtype, args.out_scale, args.act);
+    int cbeg = ((warp - kEpiWarp0) >> 2) * (BN / kColSplit), cend = cbeg + BN / kColSplit;
+    if (one_tile) {  // slice 0 of the quarter's columns; dequant warps take the others
+      cbeg = 0;
+      cend = BN / help_slices;
+    }
+    const int mode = epi_mode_k;
     int buf = 0;
     int local = 0;
     for (int t = pair; t < num_tiles; t += npairs, ++local) {
@@ -348,6 +364,21 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       cur = nxt;
       q = qn;
       have = have_n;
+    }
+    // Single-tile pair: help drain the accumulator (slices 1.. of this warp's
+    // lane quarter; three dequant warps per quarter).
+    if (one_tile && (warp - kDqWarp0) / 4 + 1 < help_slices) {
+      const int slice = (warp - kDqWarp0) / 4 + 1;
+      if (!warp_wait(&acc_full[0], 0, args.err, abort_flag)) goto dq_done;
+      tc_fence_after();
+      const EpiParams ep{args.s_col, args.out_dtype, args.out_scale, args.out_inv};
+      uint8_t* ebuf = smem + Cfg::BRING_OFF + (warp - kDqWarp0) * kEpiBufBytes;
+      int buf = 0;
+      const int w = BN / help_slices;
+      epi_block<BN, false, 1>(tmem_base, 0, warp & 3, lane, (pair / tiles_n) * 256 + static_cast<int>(rank) * 128,
+                              (pair % tiles_n) * BN, slice * w, (slice + 1) * w, M, N, args.s_row, args.out,
+                              args.ldo, epi_mode_k, ep, args.epi_path, &tmC, ebuf, buf);
+      if (args.epi_path == kEpiPathTma && lane == 0) bulk_wait_all<0>();  // stores complete before exit
     }
   dq_done:;
   }

@@ -225,6 +225,28 @@ def test_q8_0_gemm_each_tile_policy(rb, orc, tile_policy, policy, m, n, k):
     assert max_rel(got, orc.gemm_f64acc(a16, w16)) <= 1e-5
 
 
+@pytest.mark.parametrize("policy", ["auto", "pair"])
+@pytest.mark.parametrize("m,n,k", [(512, 3072, 1024), (300, 1000, 256), (600, 6144, 1024), (5000, 1024, 512)])
+def test_q8_0_gemm_f16_out_is_rounded_f32_out(rb, orc, tile_policy, policy, m, n, k):
+    """The f16 output is the f32 result rounded once (same accumulators),
+    including single-tile pair launches, whose dequant warps help the
+    epilogue warps drain the accumulator (and a multi-tile shape, where they
+    do not)."""
+    import torch
+    tile_policy(policy)
+    rng = np.random.default_rng(m + 2 * n + 3 * k)
+    w, codes, scales = q8_weight(orc, n, k, seed=m + k)
+    wid = rb.pack_q8_0_blocks(orc.q8_0_to_blocks(codes, scales), n, k)
+    x = torch.from_numpy(rng.standard_normal((m, k)).astype(np.float32)).to("cuda", torch.float16)
+    y32 = rb.matmul(x, wid, out_dtype=torch.float32)
+    y16 = rb.matmul(x, wid, out_dtype=torch.float16)
+    torch.cuda.synchronize()
+    rb.check_device_errors()
+    assert torch.equal(y16.view(torch.int16), y32.half().view(torch.int16))
+    ref = orc.gemm_f64acc(x.float().cpu().numpy(), orc.q8_0_dequant(codes, scales))
+    assert cosine(y32.cpu().numpy(), ref) >= COS_MIN
+
+
 def test_tile_policy_rejects_unknown(rb):
     import burn_rocket_b200._lib as L
     assert L.load().rb_set_tile_policy(7) != 0
