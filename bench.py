@@ -897,9 +897,8 @@ def time_single(wls, steps, warmup, stream, use_graph, local):
     """Single-op timing: W untimed warm-up steps, then exactly `steps` steps
     back to back between one pair of CUDA events on the launching stream,
     step i running on input set i % len(wls). The `steps` steps are captured
-    as one CUDA graph (replayed once untimed, then timed), queued behind a
-    short device-side sleep so that the host's launch is off the device
-    timeline. Returns (ms summed over the steps, kernel launches in the timed
+    as one CUDA graph, replayed once behind a short device-side sleep so that
+    the host's launch is off the device timeline. Returns (ms summed over the steps, kernel launches in the timed
     region, graph used, clock summary)."""
     import torch
     import burn_rocket_b200 as rb
@@ -916,9 +915,6 @@ def time_single(wls, steps, warmup, stream, use_graph, local):
             for i in range(steps):
                 wls[i % C].step()
         per_replay = rb.launch_count(reset=True)
-        graph.replay()
-        torch.cuda.synchronize()
-        rb.check_device_errors()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     with ClockSampler(local) as clocks:
