@@ -164,6 +164,12 @@ __device__ __forceinline__ float fast_exp2(float x) {
 // squares): 7.5e-5 relative, below half an ulp of the f16 P it becomes. y is
 // clamped at -126: smaller scores round to 0 in an f16/bf16 P either way.
 constexpr int kPolyEvery = RB_ATTN_POLY_EVERY;
+// Only at head_dim 128, where the exponentials cost as many MUFU cycles as
+// the tile's UMMAs: at the narrower widths (64, 72 staged as 80) the
+// polynomial measured slower than MUFU alone (config #4's attention 902
+// against 866 us).
+template <int D>
+constexpr int poly_every() { return D >= 128 ? kPolyEvery : 0; }
 constexpr float kPolyC0 = 0.9999251365661621f, kPolyC1 = 0.6958339810371399f,
                 kPolyC2 = 0.22606706619262695f, kPolyC3 = 0.07802402973175049f;
 
@@ -715,7 +721,7 @@ attn_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUt
             for (int i = 0; i < 32; i += 2) {
               float y0, y1, p0, p1;
               f2_unpack(f2_fma(f2_pack(x[c0 + i], x[c0 + i + 1]), c2, nm2), y0, y1);
-              if (kPolyEvery > 0 && (i / 2) % kPolyEvery == kPolyEvery - 1) {
+              if (poly_every<D>() > 0 && (i / 2) % poly_every<D>() == poly_every<D>() - 1) {
                 exp2_poly2(y0, y1, p0, p1);
               } else {
                 p0 = fast_exp2(y0);
