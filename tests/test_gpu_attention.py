@@ -69,11 +69,17 @@ CASES = [
     (64, 4096, 2, 1, 128, 1, -1, 0, 0),
     (200, 6000, 2, 2, 128, 1, -1, 0, 0),
     (256, 9000, 2, 1, 64, 6, -1, 8744, 0),
+    # bands that start or end one key either side of a 128-key tile edge
+    (256, 256, 4, 2, 128, 4, 127, 0, 0),
+    (256, 384, 4, 2, 128, 5, 128, 129, 1),
+    (129, 257, 2, 1, 128, 6, 129, 128, 0),
+    (257, 257, 2, 2, 64, 3, 129, 0, 0),
     # head_dim 72 (staged as 80 = 64-column atom + 16-column tail)
     (1, 1, 2, 2, 72, 0, -1, 0, 0),
     (300, 300, 16, 16, 72, 0, -1, 0, 0),
     (257, 257, 4, 2, 72, 2, -1, 0, 0),
     (150, 400, 4, 2, 72, 5, 60, 200, 150),
+    (255, 255, 2, 2, 72, 3, 128, 0, 0),
 ]
 
 
