@@ -139,11 +139,21 @@ def test_siglip_layer_stages(rb, orc):
         c2, s2 = orc.quantize_weight_per_channel(Lh["w2"])
         d = rb.matmul(f, Ld["fc2"])
         assert np.array_equal(d.float().cpu().numpy(), f16r(orc, orc.w8a8_matmul(fn, c2, s2))), li
-        # --- the whole layer (the model's own launch sequence) against the oracle layer
+        # --- the whole layer (the model's own launch sequence) against the oracle layer.
+        # Its output (the new residual stream) is held to the north-star bar. Its update
+        # alone re-quantises three activations (LayerNorm rows, attention output, GELU
+        # output): a rounding-level difference ahead of a quantiser moves that element a
+        # whole int8 step, which the oracle shows against itself (its LayerNorms in f32
+        # instead of f64 move the update by ~8e-3 of its max). So the update's max error
+        # may reach twice the oracle's own f32-LayerNorm distance; its cosine stays >= 0.9999.
         tower.x.copy_(x_in)
         got = tower.layer_step(li).cpu().numpy().astype(np.float64)
         want = siglip_ref.layer(Lh, cfg, xin, 1)
-        assert_close(got - xin, want - xin, f"layer {li} update")
+        alt = siglip_ref.layer(Lh, cfg, xin, 1, ln32=True)
+        assert_close(got, want, f"layer {li} output")
+        r_alt = max_rel(alt - xin, want - xin)
+        print(f"layer {li} oracle f32-LayerNorm update vs f64: max rel {r_alt:.2e}")
+        assert_close(got - xin, want - xin, f"layer {li} update", rel=max(MAX_REL, 2.0 * r_alt))
     rb.check_device_errors()
 
 
