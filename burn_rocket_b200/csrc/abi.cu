@@ -1252,6 +1252,8 @@ int rb_qk_norm_rope(void* qkv_f16, int64_t ld, int64_t tokens, int n_q_heads, in
   if (!qkv_f16 || !q_norm_w || !k_norm_w || !cos_t || !sin_t || tokens <= 0 || seq <= 0)
     return fail(RB_E_SHAPE, "qk_norm_rope: bad arguments");
   if (head_dim != 128) return fail(RB_E_UNSUPPORTED, "qk_norm_rope: head_dim %d (supported: 128)", head_dim);
+  if (n_q_heads <= 0 || n_kv_heads < 0 || ld < static_cast<int64_t>(n_q_heads + n_kv_heads) * 128)
+    return fail(RB_E_SHAPE, "qk_norm_rope: row stride %lld below the q and k columns", static_cast<long long>(ld));
   const int rc = launch_qk_norm_rope(qkv_f16, ld, tokens, n_q_heads, n_kv_heads, q_norm_w, k_norm_w, eps,
                                      cos_t, sin_t, static_cast<int>(seq),
                                      reinterpret_cast<cudaStream_t>(stream));

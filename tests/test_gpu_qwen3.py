@@ -53,7 +53,7 @@ def test_rms_norm_and_gated_glue(rb):
     np.testing.assert_allclose(o.cpu().numpy(), gel, rtol=1e-5, atol=1e-5)
 
 
-def test_rope_and_qk_norm_rope(rb):
+def test_rope(rb):
     import torch
     import burn_rocket_b200._lib as L
     from oracle.qwen3_ref import rope_tables
@@ -71,25 +71,60 @@ def test_rope_and_qk_norm_rope(rb):
     want = np.concatenate([x[..., :half] * c - x[..., half:] * s, x[..., half:] * c + x[..., :half] * s], -1)
     torch.cuda.synchronize()
     np.testing.assert_allclose(y.cpu().numpy(), want, rtol=1e-5, atol=1e-5)
-    # fused per-head norm + rope on a q|k|v buffer
-    ld = (HQ + 2 * HK) * D
-    qkv = (rng.standard_normal((B * S, ld)) * 3).astype(np.float16)
+
+
+@pytest.mark.parametrize("hq,hk", [(4, 2), (16, 8), (32, 4), (36, 4)])
+def test_qk_norm_rope(rb, hq, hk):
+    """Per-head RMSNorm + RoPE in place on a fused q|k|v buffer against the f64
+    formula, through both device forms: one warp per token with 16-byte
+    accesses (row stride a multiple of 8 halves, at most 36 q+k heads) and the
+    half-warp-per-head form (any other stride, more heads). The two differ
+    only in the order of each head's sum of squares, so they agree within one
+    f16 step; v columns and the padding columns stay untouched."""
+    import torch
+    import burn_rocket_b200._lib as L
+    from oracle.qwen3_ref import rope_tables
+    lib = L.load()
+    rng = np.random.default_rng(hq * 100 + hk)
+    B, S, D = 2, 40, 128
+    half = D // 2
+    cos, sin = rope_tables(S, D, 1e6)
+    cd, sd = torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda()
+    c, s = cos[None, :, None, :], sin[None, :, None, :]
+    width = (hq + 2 * hk) * D
+    src16 = (rng.standard_normal((B * S, width)) * 3).astype(np.float16)
     wq = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32)
     wk = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32)
-    t = torch.from_numpy(qkv.copy()).cuda()
-    assert lib.rb_qk_norm_rope(t.data_ptr(), ld, B * S, HQ, HK, D, torch.from_numpy(wq).cuda().data_ptr(),
-                               torch.from_numpy(wk).cuda().data_ptr(), 1e-6, cd.data_ptr(), sd.data_ptr(), S,
-                               None) == 0
-    torch.cuda.synchronize()
-    got = t.cpu().numpy().astype(np.float64)
-    src = qkv.astype(np.float64).reshape(B, S, HQ + 2 * HK, D)
-    heads = src[:, :, :HQ + HK]
-    wts = np.concatenate([np.tile(wq, (HQ, 1)), np.tile(wk, (HK, 1))])[None, None]
+    wqd, wkd = torch.from_numpy(wq).cuda(), torch.from_numpy(wk).cuda()
+    src = src16.astype(np.float64).reshape(B, S, hq + 2 * hk, D)
+    heads = src[:, :, :hq + hk]
+    wts = np.concatenate([np.tile(wq, (hq, 1)), np.tile(wk, (hk, 1))])[None, None]
     nrm = heads / np.sqrt((heads ** 2).mean(-1, keepdims=True) + 1e-6) * wts
     rot = np.concatenate([nrm[..., :half] * c - nrm[..., half:] * s, nrm[..., half:] * c + nrm[..., :half] * s], -1)
-    got = got.reshape(B, S, HQ + 2 * HK, D)
-    assert np.abs(got[:, :, :HQ + HK] - rot).max() < 2e-2 * np.abs(rot).max()
-    assert np.array_equal(got[:, :, HQ + HK:], src[:, :, HQ + HK:])  # v untouched
+    outs = []
+    for pad in (0, 4):  # pad 0: the 16-byte form when hq + hk <= 36; pad 4: the half-warp form
+        ld = width + pad
+        buf = np.full((B * S, ld), 7.0, np.float16)
+        buf[:, :width] = src16
+        t = torch.from_numpy(buf).cuda()
+        assert lib.rb_qk_norm_rope(t.data_ptr(), ld, B * S, hq, hk, D, wqd.data_ptr(), wkd.data_ptr(), 1e-6,
+                                   cd.data_ptr(), sd.data_ptr(), S, None) == 0
+        torch.cuda.synchronize()
+        got16 = t.cpu().numpy()
+        assert np.all(got16[:, width:] == 7.0)
+        got = got16[:, :width].astype(np.float64).reshape(B, S, hq + 2 * hk, D)
+        assert np.array_equal(got[:, :, hq + hk:], src[:, :, hq + hk:])  # v untouched
+        err = np.abs(got[:, :, :hq + hk] - rot)
+        # f16 output: within 1e-3 of the row's scale (two f16 steps at |x| ~ 4)
+        assert err.max() < 1e-3 * np.abs(rot).max(), (pad, err.max())
+        outs.append(got16[:, :width])
+    a = outs[0].astype(np.float16).view(np.int16).astype(np.int64)
+    b = outs[1].astype(np.float16).view(np.int16).astype(np.int64)
+    assert np.abs(a - b).max() <= 1
+    # a row stride that does not cover the q and k columns is rejected
+    t = torch.from_numpy(src16.copy()).cuda()
+    assert lib.rb_qk_norm_rope(t.data_ptr(), (hq + hk) * D - 8, B * S, hq, hk, D, wqd.data_ptr(), wkd.data_ptr(),
+                               1e-6, cd.data_ptr(), sd.data_ptr(), S, None) == L.RB_E_SHAPE
 
 
 def test_batched_attention_equals_per_sequence(rb):
