@@ -351,7 +351,9 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
       a = e->act.ptr;
       L.pdl = 1;  // the GEMM's prologue (and Q8_0 weight staging) overlaps the cast
     }
-    GemmPlan plan = gemm_plan(false, L.M, L.N, L.K, e->num_sms);
+    // 96-column CTA-pair tiles only where the epilogue stores whole 32-column
+    // f32 chunks (2-byte outputs take 64-column chunks).
+    GemmPlan plan = gemm_plan(false, L.M, L.N, L.K, e->num_sms, y_dtype == RB_DTYPE_F32 && !w.gated);
     // The gated epilogue turns 128 accumulator columns into 64 outputs: tiles
     // of 256 or 128 columns.
     if (w.gated && plan.bn % 128 != 0) plan = GemmPlan{plan.pair ? 256 : 128, 1, plan.pair};
@@ -359,7 +361,9 @@ static int matmul_locked(Engine* e, int64_t id, const void* x, int x_dtype, int6
     if ((rc = make_tmap_2d(&tmA, a, 2, m, k, k, 64, plan.a_rows(), 128)) != RB_OK) return rc;
     const bool tstore = output_map(&tmC, y, y_dtype, m, n_out);
     if (w.gated && !tstore) return fail(RB_E_SHAPE, "gated weight: output tensor map unavailable");
-    const int bi = bn_index(plan.weight_rows());
+    // The pair kernel reads Q8_0 codes and scales from global memory, not
+    // through these maps (a 96-column pair tile has no map of its own).
+    const int bi = bn_index(plan.weight_rows()) < 0 ? 0 : bn_index(plan.weight_rows());
     L.w_codes = w.codes;
     L.w_scales = w.scales;
     L.w_pitch = w.pitch;

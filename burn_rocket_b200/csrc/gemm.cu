@@ -247,7 +247,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[acc]);
     }
-    if (args.epi_path == kEpiPathTma && lane == 0) bulk_wait_all<0>();  // stores complete before exit
+    if (args.epi_path == kEpiPathTma && lane == 0) bulk_wait_read<0>();  // sources read: the CTA may leave (stores complete with the grid)
   } else if (Cfg::Q8 && warp >= kDqWarp0) {
     // ------------------------------------------------------------ Q8_0 dequant
     // Chunk (row, c) — 8 codes of one weight row — is read from the staged
@@ -370,17 +370,21 @@ int gemm_policy() { return g_policy.load(); }
 //   * Q8_0: pair tiles run ~40% faster than the best single-CTA tile (256 x
 //     128, two M halves sharing one dequantised B tile) at large M; at small
 //     M (a single round of tiles) the two are even.
-GemmPlan gemm_plan(bool i8, int M, int N, int K, int num_sms) {
+GemmPlan gemm_plan(bool i8, int M, int N, int K, int num_sms, bool pair96) {
   const int policy = g_policy.load();
   struct Shape { int bn, mh; bool pair; double eff; };
   const bool long_k = K > 2048;
+  // 96-column pair tiles: per SM and k-block ~11% less shared-memory traffic
+  // than 128-column ones (A 32 KB + B 18 KB against 32 + 24), which bounds
+  // these tiles; they fill 64 SM pairs where 128-column tiles fill 48 at
+  // config #1's 512 x 3072.
   const Shape q8c[] = {{256, 1, false, 2.0}, {128, 1, false, 2.0}, {96, 1, false, 2.0},
                        {64, 1, false, 2.0},  {128, 2, false, 1.5}, {256, 1, true, 1.03},
-                       {128, 1, true, 1.2}};
+                       {128, 1, true, 1.2},  {96, 1, true, 1.4}};
   const Shape i8c[] = {{256, 1, false, long_k ? 1.13 : 1.04}, {128, 1, false, long_k ? 1.25 : 1.15},
                        {256, 1, true, 1.0}, {128, 1, true, 1.12}};
   const Shape* c = i8 ? i8c : q8c;
-  const int nc = i8 ? 4 : 7;
+  const int nc = i8 ? 4 : (pair96 ? 8 : 7);
   GemmPlan best{c[0].bn, c[0].mh, false};
   double best_cost = -1.0;
   for (int i = 0; i < nc; ++i) {

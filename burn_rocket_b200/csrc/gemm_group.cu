@@ -253,7 +253,7 @@ gemm_i8g_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
       }
     }
   fold_done:
-    if (args.epi_path == kEpiPathTma && lane == 0) bulk_wait_all<0>();  // stores complete before exit
+    if (args.epi_path == kEpiPathTma && lane == 0) bulk_wait_read<0>();  // sources read: the CTA may leave (stores complete with the grid)
   }
 
   tc_fence_before();

@@ -46,7 +46,8 @@ struct GemmPlan {
   int weight_rows() const { return pair ? bn / 2 : bn; }  // weight map box height
   int a_rows() const { return pair ? 128 : 128 * mh; }     // activation map box height
 };
-GemmPlan gemm_plan(bool i8, int M, int N, int K, int num_sms);
+// pair96: also consider 96-column Q8_0 CTA-pair tiles (f32 output only).
+GemmPlan gemm_plan(bool i8, int M, int N, int K, int num_sms, bool pair96 = false);
 // Restricts gemm_plan to single-CTA or (preferably) pair tiles; returns the old policy.
 int set_gemm_policy(int policy);
 int gemm_policy();

@@ -432,6 +432,15 @@ __device__ __forceinline__ void cluster_sync_all() {
                    : "memory");
 }
 
+// The same barrier for warps with nothing to publish to the cluster: a
+// relaxed arrive does not wait for the warp's earlier memory accesses (e.g.
+// loads still in flight) to complete; the wait still acquires what the other
+// warps released.
+__device__ __forceinline__ void cluster_sync_relaxed_arrive() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
 // TMA tile load into this CTA's shared memory whose completion bytes are
 // counted on an mbarrier of either CTA of the pair (cluster address; here the
 // leader's). No multicast.

@@ -84,8 +84,12 @@ def test_q8_0_gemm_config1_parity(rb, orc):
     assert max_rel(got, ref16) <= 1e-5
 
 
+# (1000, 1000, 512): 96-column CTA-pair tiles, one per pair, a 40-column last
+# tile; (2560, 1920, 512): 96-column pair tiles, three per pair (both
+# accumulator buffers in turn).
 @pytest.mark.parametrize("m,n,k", [(1, 32, 32), (3, 96, 96), (129, 200, 1024), (300, 3072, 64),
-                                   (77, 136, 160), (1000, 1024, 1024), (128, 6144, 1024)])
+                                   (77, 136, 160), (1000, 1024, 1024), (128, 6144, 1024),
+                                   (1000, 1000, 512), (2560, 1920, 512)])
 def test_q8_0_gemm_ragged_shapes(rb, orc, m, n, k):
     got, ref, _, _ = _q8_gemm_case(rb, orc, m, n, k, seed=m + n + k)
     assert cosine(got, ref) >= COS_MIN
