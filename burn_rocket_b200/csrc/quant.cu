@@ -480,12 +480,54 @@ __global__ void cast_f32_f16_vec_kernel(const float4* __restrict__ x, uint4* __r
   }
 }
 
+// The same cast for small inputs (up to 148 x 128 x 4 groups of 8), shaped
+// to sit beside the GEMM that consumes it: at most one 128-thread CTA per SM
+// and at most 56 registers a thread (__launch_bounds__(128, 9)), so an SM
+// running one still has the registers for a CTA-pair GEMM CTA (19 warps x 96),
+// which under programmatic dependent launch then sets up and stages its
+// weights meanwhile. Each thread converts up to four groups, every load
+// issued before the first store.
+__global__ void __launch_bounds__(128, 9)
+cast_f32_f16_x4_kernel(const float4* __restrict__ x, uint4* __restrict__ y, int64_t count8) {
+  griddep_launch_dependents();
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t i0 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  float4 a[4], b[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int64_t i = i0 + j * stride;
+    if (i < count8) {
+      a[j] = x[2 * i];
+      b[j] = x[2 * i + 1];
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int64_t i = i0 + j * stride;
+    if (i < count8) {
+      uint4 o;
+      __half2* h = reinterpret_cast<__half2*>(&o);
+      h[0] = __floats2half2_rn(a[j].x, a[j].y);
+      h[1] = __floats2half2_rn(a[j].z, a[j].w);
+      h[2] = __floats2half2_rn(b[j].x, b[j].y);
+      h[3] = __floats2half2_rn(b[j].z, b[j].w);
+      y[i] = o;
+    }
+  }
+}
+
 int launch_cast(const void* x, int x_dtype, void* y, int y_dtype, int64_t count,
                 cudaStream_t stream) {
   const int threads = 256;
   if (x_dtype == RB_DTYPE_F32 && y_dtype == RB_DTYPE_F16 && (count & 7) == 0 &&
       (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
     const int64_t c8 = count / 8;
+    if (c8 <= 148 * 128 * 4) {
+      const int64_t blocks = (c8 + 128 * 4 - 1) / (128 * 4);
+      cast_f32_f16_x4_kernel<<<static_cast<int>(blocks), 128, 0, stream>>>(
+          reinterpret_cast<const float4*>(x), reinterpret_cast<uint4*>(y), c8);
+      return cudaGetLastError() == cudaSuccess ? RB_OK : RB_E_DEVICE;
+    }
     int64_t blocks = (c8 + threads - 1) / threads;
     if (blocks > 148 * 8) blocks = 148 * 8;
     if (blocks < 1) blocks = 1;
