@@ -31,6 +31,11 @@
 //   b_local[s]   peer, Q8_0: its dequant group's warps (local arrive), which
 //                the forwarding thread waits on. (Cluster-scope arrives are
 //                costly: one per stage instead of one per dequant warp.)
+// Q8_0 256-column tiles (Cfg::SPLIT) keep the dequantised B halves in a ring
+// of their own, so A can run more stages ahead than 32 KB unified stages
+// would allow; there the leader's dequant group and the peer's forward arrive
+// on b_full[b] instead of ld_full, and the issuer's commit also releases
+// b_empty[b] (two waits and two commits per k-block).
 //   acc_full[a]  each CTA: the leader's UMMA commit (multicast).
 //   acc_local[a] peer: its own epilogue warps (local arrive).
 //   acc_empty[a] leader: its own epilogue warps (local arrive) + one remote
