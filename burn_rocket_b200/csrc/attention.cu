@@ -1099,11 +1099,12 @@ int launch_attention(const CUtensorMap* tm, const AttnLaunch& L, cudaStream_t st
         }
         // Units of unequal length leave the split's shares uneven in time
         // (short items cost more than modelled): it must win clearly there.
-        // Equal units: measured on config #4's tower (2560 units of 19 key
-        // tiles, head_dim 72), the split estimated at 0.93 of the greedy
+        // Equal units: measured on config #4's tower (2560 units of 38 key
+        // tiles, head_dim 72), the split estimated at 0.94 of the greedy
         // finish ran 2.5-5% slower, its records and merges costing more than
-        // modelled; at 0.84 (config #2) and 0.89 (config #3) it is as fast or
-        // faster. So it must beat the greedy estimate by 10%.
+        // modelled; config #3's forward (2048 units of 8 key tiles, 0.93) ran
+        // as fast either way; config #2's bidirectional call (0.81) gains from
+        // it. So it must beat the greedy estimate by 10%.
         use = split_t < (equal ? 0.90 : 0.75) * static_cast<double>(greedy);
       } else {
         use = false;  // many units: the greedy schedule's last wave is short
